@@ -1,0 +1,518 @@
+// Split-K flash-decoding for the Qwen3.5 gated full-attention core (sm_100a).
+//
+// Replaces, for one decode token per sequence:
+//   forward_full_attn_from_proj  models/llm/qwen3_5.cpp:944-1002
+//     (QK RMSNorm 952-959, RoPE 961-971, ring append 973-986, gqa_attention
+//      988-991, sigmoid gate 993-1000), and
+//   gqa_attention                core/cpu_ops.cpp:148-204.
+//
+// Work decomposition: one CTA per (batch row, split of the ring's logical
+// range, kv head).  A CTA
+//   1. rebuilds the group's G query heads from the projection row (RMSNorm,
+//      RoPE, 1/sqrt(d)), and the new token's k/v; split 0 appends k/v to the
+//      ring slot (fp16);
+//   2. streams its range of K and V rows (64-token tiles, 16-byte cp.async into
+//      XOR-swizzled shared memory, 3-stage pipeline) -- each KV byte is read
+//      from HBM once and serves all G query heads;
+//   3. computes Q K^T and P V on the tensor cores with fp32 accumulation.  The
+//      fp32 queries and probabilities are split into fp16 hi + lo halves that
+//      sit side by side in the 8 columns of an m16n8k16 MMA (G <= 4), so the
+//      products carry ~22 significant bits while K/V stay in their fp16
+//      storage format;
+//   4. keeps an online softmax (running max / sum per head) across tiles and
+//      writes an unnormalised partial (O, m, l).
+// The last CTA of a (row, kv head) -- found with an atomic counter, no waiting
+// -- merges the partials, applies the sigmoid gate and writes the output; the
+// last of those updates the ring's len/start.
+//
+// New-token handling: the slot being written is never one of the old tokens the
+// other CTAs read (it is either empty or the evicted oldest slot), so the
+// append and the reads of the same launch do not race.  The CTA whose tile
+// holds the new token patches that row in shared memory with the fp16 k/v.
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace anelm {
+
+namespace {
+
+constexpr int kTile = 64;      // tokens per pipeline tile
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kStages = 3;
+constexpr int kGP = 4;         // padded query heads per kv head (hi+lo fill n=8)
+constexpr int kPRow = kTile + 8;  // halves per P row (padding breaks bank conflicts)
+
+template <int D>
+struct Smem {
+    static constexpr size_t tiles = 0;
+    static constexpr size_t tile_bytes = size_t(kTile) * D * 2;
+    static constexpr size_t q = tiles + kStages * tile_bytes;     // float [kGP][D]
+    static constexpr size_t kf = q + size_t(kGP) * D * 4;          // float [D]
+    static constexpr size_t vf = kf + size_t(D) * 4;               // float [D]
+    static constexpr size_t kh = vf + size_t(D) * 4;               // half  [D]
+    static constexpr size_t vh = kh + size_t(D) * 2;               // half  [D]
+    static constexpr size_t sc = vh + size_t(D) * 2;               // float [kGP][kTile]
+    static constexpr size_t P = sc + size_t(kGP) * kTile * 4;      // half  [2*kGP][kPRow]
+    static constexpr size_t misc = P + size_t(2 * kGP) * kPRow * 2;  // float [32]
+    static constexpr size_t total = misc + 32 * 4;
+};
+
+__device__ __forceinline__ void rope_cs(const FaDecodeParams& p, int pos, int j, float& c, float& s) {
+    const int half = p.rot_dim >> 1;
+    if (pos >= 0 && pos < p.rope_len && p.rope_cos) {
+        c = p.rope_cos[(long long)pos * half + j];
+        s = p.rope_sin[(long long)pos * half + j];
+    } else {  // core/cpu_ops.cpp:51-56
+        float freq = 1.0f / powf(p.rope_theta, (float)(2 * j) / (float)p.rot_dim);
+        float angle = (float)pos * freq;
+        c = cosf(angle);
+        s = sinf(angle);
+    }
+}
+
+__device__ __forceinline__ void set_err(int* err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodeParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    using S = Smem<D>;
+    constexpr int CPR = D / 8;             // 16-byte chunks per row
+    constexpr int DW = D / kWarps;         // d columns per warp in P V
+    constexpr int MT = DW / 16;            // m16 tiles per warp in P V
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int blk = blockIdx.x, kvh = blockIdx.y;
+    const int b = p.blk_b[blk], split = p.blk_split[blk];
+    const int Hkv = p.Hkv;
+    const int G = p.Hq / Hkv;
+    const int seq = p.seq_ids ? p.seq_ids[b] : 0;
+
+    // ---- ring metadata (models/llm/qwen3_5.cpp:973-983) ----
+    int cap, len0, start0;
+    long long base;
+    if (p.kv_len) {
+        cap = p.kv_cap[seq];
+        len0 = p.kv_len[seq];
+        start0 = p.kv_start[seq];
+        base = p.kv_base[seq];
+    } else {
+        cap = p.cap_s;
+        len0 = p.len_s;
+        start0 = p.start_s;
+        base = 0;
+    }
+    const int pos = p.pos_arr ? p.pos_arr[b] : p.pos_scalar;
+    int len1 = len0, start1 = start0, slot = -1;
+    if (p.append) {
+        if (p.kv_mode == ANELM_KV_LINEAR) {  // scripts/serve_hybrid.py:105-108
+            if (pos < 0 || pos >= cap) {
+                set_err(p.err, ANELM_ERR_CAPACITY);
+                return;  // uniform for every CTA of this row: counters stay untouched
+            }
+            slot = pos;
+            len1 = pos + 1;
+            start1 = 0;
+        } else if (len0 < cap) {
+            slot = start0 + len0;
+            if (slot >= cap) slot -= cap;
+            len1 = len0 + 1;
+        } else {
+            slot = start0;
+            start1 = start0 + 1;
+            if (start1 >= cap) start1 = 0;
+        }
+    }
+    const int n_old = p.append ? len1 - 1 : len1;  // tokens read from the ring
+    const int t_begin = split * p.CH;
+    const int t_end = min(t_begin + p.CH, len1);
+    const int n_tok = max(0, t_end - t_begin);
+    const int n_tiles = (n_tok + kTile - 1) / kTile;
+
+    float* q_s = reinterpret_cast<float*>(smem + S::q);
+    float* kf_s = reinterpret_cast<float*>(smem + S::kf);
+    float* vf_s = reinterpret_cast<float*>(smem + S::vf);
+    __half* kh_s = reinterpret_cast<__half*>(smem + S::kh);
+    __half* vh_s = reinterpret_cast<__half*>(smem + S::vh);
+    float* sc_s = reinterpret_cast<float*>(smem + S::sc);
+    __half* P_s = reinterpret_cast<__half*>(smem + S::P);
+    float* misc = reinterpret_cast<float*>(smem + S::misc);
+    // misc: [0..3] m_run, [4..7] l_run, [8..11] alpha, [12..15] score scale
+    const char* proj_row = reinterpret_cast<const char*>(p.proj) +
+                           (long long)b * p.proj_stride * dtype_bytes(p.proj_dtype);
+
+    float acc[MT][4];
+#pragma unroll
+    for (int i = 0; i < MT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+    if (n_tok > 0) {
+        // ---- 1. prologue: queries, new k/v ----
+        for (int idx = tid; idx < kGP * D; idx += kThreads) {
+            int g = idx / D, i = idx - g * D;
+            q_s[idx] = (g < G) ? load_as_float(proj_row, p.proj_dtype,
+                                               (long long)(kvh * G + g) * p.q_head_stride + i)
+                               : 0.f;
+        }
+        if (p.append) {
+            for (int i = tid; i < D; i += kThreads) {
+                kf_s[i] = load_as_float(proj_row, p.proj_dtype, p.k_off + (long long)kvh * D + i);
+                vf_s[i] = load_as_float(proj_row, p.proj_dtype, p.v_off + (long long)kvh * D + i);
+            }
+        }
+        __syncthreads();
+        const int nvec = G + (p.append ? 1 : 0);
+        if (p.qk_norm) {  // rmsnorm, core/cpu_ops.cpp:24-30
+            for (int vec = warp; vec < nvec; vec += kWarps) {
+                float* x = vec < G ? q_s + vec * D : kf_s;
+                const float* w = vec < G ? p.q_norm : p.k_norm;
+                float ss = 0.f;
+                for (int i = lane; i < D; i += 32) ss += x[i] * x[i];
+                ss = warp_sum(ss);
+                const float r = 1.0f / sqrtf(ss / (float)D + p.rms_eps);
+                for (int i = lane; i < D; i += 32) x[i] = __fmul_rn(__fmul_rn(x[i], r), w[i]);
+            }
+            __syncthreads();
+        }
+        if (p.rot_dim > 0) {  // apply_rope_cached, core/cpu_ops.cpp:40-63 (or rotate-half)
+            const int half = p.rot_dim >> 1;
+            for (int idx = tid; idx < nvec * half; idx += kThreads) {
+                int vec = idx / half, j = idx - vec * half;
+                float* x = vec < G ? q_s + vec * D : kf_s;
+                float c, s;
+                rope_cs(p, pos, j, c, s);
+                int i0, i1;
+                if (p.rope_mode == ANELM_ROPE_INTERLEAVED) {
+                    i0 = 2 * j;
+                    i1 = 2 * j + 1;
+                } else {
+                    i0 = j;
+                    i1 = j + half;
+                }
+                float v0 = x[i0], v1 = x[i1];
+                if (p.rope_mode == ANELM_ROPE_INTERLEAVED) {
+                    x[i0] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+                    x[i1] = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+                } else {  // serve_hybrid.py:98-99: q1*cos - q2*sin, q2*cos + q1*sin
+                    x[i0] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+                    x[i1] = __fadd_rn(__fmul_rn(v1, c), __fmul_rn(v0, s));
+                }
+            }
+            __syncthreads();
+        }
+        if (p.append) {
+            for (int i = tid; i < D; i += kThreads) {
+                kh_s[i] = __float2half_rn(kf_s[i]);
+                vh_s[i] = __float2half_rn(vf_s[i]);
+            }
+        }
+        // per-head power-of-two prescale so the fp16 hi/lo split keeps full range
+        if (warp < kGP) {
+            float mx = 0.f;
+            for (int i = lane; i < D; i += 32) mx = fmaxf(mx, fabsf(q_s[warp * D + i]));
+            mx = warp_max(mx);
+            int e = 0;
+            if (mx > 0.f) frexpf(mx, &e);
+            const int sh = 10 - e;  // max |q| * 2^sh in [2^9, 2^10)
+            if (lane == 0) {
+                misc[12 + warp] = ldexpf(p.scale, -sh);
+                misc[16 + warp] = ldexpf(1.0f, sh);
+            }
+        }
+        __syncthreads();
+        if (p.append && split == 0 && slot >= 0) {  // ring append, qwen3_5.cpp:984-986
+            const long long row = ((base + slot) * Hkv + kvh) * (long long)D;
+            for (int ch = tid; ch < CPR; ch += kThreads) {
+                reinterpret_cast<uint4*>(p.k_pool + row)[ch] = reinterpret_cast<const uint4*>(kh_s)[ch];
+                reinterpret_cast<uint4*>(p.v_pool + row)[ch] = reinterpret_cast<const uint4*>(vh_s)[ch];
+            }
+        }
+    }
+
+    if (n_tok > 0) {
+        // B fragments of Q (k = d, n = [4 hi heads | 4 lo heads]) kept in registers.
+        uint32_t qb[D / 16][2];
+        {
+            const int n = lane >> 2, c = lane & 3, h = n & 3;
+            const bool lo = n >= 4;
+            const float up = misc[16 + h];
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ks++) {
+#pragma unroll
+                for (int part = 0; part < 2; part++) {
+                    const int i = 16 * ks + 8 * part + 2 * c;
+                    float x0 = q_s[h * D + i] * up, x1 = q_s[h * D + i + 1] * up;
+                    __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+                    if (lo) {
+                        h0 = __float2half_rn(x0 - __half2float(h0));
+                        h1 = __float2half_rn(x1 - __half2float(h1));
+                    }
+                    qb[ks][part] = pack_half2(h0, h1);
+                }
+            }
+        }
+        if (tid < kGP) {
+            misc[tid] = -INFINITY;
+            misc[4 + tid] = 0.f;
+            misc[8 + tid] = 1.f;
+        }
+        for (int idx = tid; idx < 2 * kGP * kPRow; idx += kThreads) P_s[idx] = __float2half_rn(0.f);
+
+        const int t_new = p.append ? len1 - 1 : -1;  // logical index of the new token
+        const __half* kpool = p.k_pool;
+        const __half* vpool = p.v_pool;
+        auto issue = [&](int j) {
+            const int stage = j % kStages;
+            const int tile = j >> 1;
+            const __half* pool = (j & 1) ? vpool : kpool;
+            const uint32_t sbase = smem_u32(smem + S::tiles + stage * S::tile_bytes);
+            for (int idx = tid; idx < kTile * CPR; idx += kThreads) {
+                const int r = idx / CPR, ch = idx - r * CPR;
+                const int t = t_begin + tile * kTile + r;
+                const bool valid = (t < t_end) && (t < n_old);
+                int s = start1 + t;
+                if (s >= cap) s -= cap;
+                const __half* src = pool + ((base + (valid ? s : 0)) * Hkv + kvh) * (long long)D + ch * 8;
+                const uint32_t dst = sbase + (uint32_t)(r * D + ((ch ^ (r & 7)) * 8)) * 2u;
+                cp_async_16(dst, src, valid ? 16 : 0);
+            }
+        };
+
+        const int n_jobs = 2 * n_tiles;
+#pragma unroll
+        for (int j = 0; j < kStages - 1; j++) {
+            if (j < n_jobs) issue(j);
+            cp_async_commit();
+        }
+        for (int j = 0; j < n_jobs; j++) {
+            cp_async_wait<kStages - 2>();
+            __syncthreads();
+            if (j + kStages - 1 < n_jobs) issue(j + kStages - 1);
+            cp_async_commit();
+            const int stage = j % kStages;
+            const int tile = j >> 1;
+            const bool isV = j & 1;
+            uint8_t* tbuf = smem + S::tiles + stage * S::tile_bytes;
+            const int tile_t0 = t_begin + tile * kTile;
+            if (t_new >= tile_t0 && t_new < tile_t0 + kTile && t_new < t_end) {
+                const int r = t_new - tile_t0;
+                const __half* src = isV ? vh_s : kh_s;
+                for (int ch = tid; ch < CPR; ch += kThreads)
+                    *reinterpret_cast<uint4*>(tbuf + (r * D + ((ch ^ (r & 7)) * 8)) * 2) =
+                        reinterpret_cast<const uint4*>(src)[ch];
+                __syncthreads();
+            }
+            const uint32_t tb = smem_u32(tbuf);
+            if (!isV) {
+                // ---- scores for tokens [16*warp, 16*warp+16) of this tile ----
+                float c4[4] = {0.f, 0.f, 0.f, 0.f};
+                const int r = 16 * warp + (lane & 7) + (((lane >> 3) & 1) << 3);
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ks++) {
+                    const int ch = 2 * ks + (lane >> 4);
+                    uint32_t a0, a1, a2, a3;
+                    ldmatrix_x4(tb + (uint32_t)(r * D + ((ch ^ (r & 7)) * 8)) * 2u, a0, a1, a2, a3);
+                    mma_16816(c4, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+                }
+                float o0 = __shfl_xor_sync(0xffffffffu, c4[0], 2);
+                float o1 = __shfl_xor_sync(0xffffffffu, c4[1], 2);
+                float o2 = __shfl_xor_sync(0xffffffffu, c4[2], 2);
+                float o3 = __shfl_xor_sync(0xffffffffu, c4[3], 2);
+                if ((lane & 3) < 2) {
+                    const int h0 = 2 * (lane & 3), h1 = h0 + 1;
+                    const int tl = 16 * warp + (lane >> 2);
+                    const bool v0 = tile_t0 + tl < t_end, v1 = tile_t0 + tl + 8 < t_end;
+                    sc_s[h0 * kTile + tl] = v0 ? (c4[0] + o0) * misc[12 + h0] : -INFINITY;
+                    sc_s[h1 * kTile + tl] = v0 ? (c4[1] + o1) * misc[12 + h1] : -INFINITY;
+                    sc_s[h0 * kTile + tl + 8] = v1 ? (c4[2] + o2) * misc[12 + h0] : -INFINITY;
+                    sc_s[h1 * kTile + tl + 8] = v1 ? (c4[3] + o3) * misc[12 + h1] : -INFINITY;
+                }
+                __syncthreads();
+                // ---- online softmax update, one warp per query head ----
+                if (warp < G) {
+                    const int h = warp;
+                    const float s0 = sc_s[h * kTile + lane], s1 = sc_s[h * kTile + lane + 32];
+                    const float m_old = misc[h];
+                    const float m_new = fmaxf(m_old, warp_max(fmaxf(s0, s1)));
+                    float alpha = 1.f, p0 = 0.f, p1 = 0.f;
+                    if (m_new != -INFINITY) {
+                        alpha = expf(m_old - m_new);
+                        p0 = expf(s0 - m_new);
+                        p1 = expf(s1 - m_new);
+                    }
+                    const float ps = warp_sum(p0 + p1);
+                    const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
+                    P_s[h * kPRow + lane] = h0;
+                    P_s[h * kPRow + lane + 32] = h1;
+                    P_s[(kGP + h) * kPRow + lane] = __float2half_rn(p0 - __half2float(h0));
+                    P_s[(kGP + h) * kPRow + lane + 32] = __float2half_rn(p1 - __half2float(h1));
+                    if (lane == 0) {
+                        misc[h] = m_new;
+                        misc[4 + h] = misc[4 + h] * alpha + ps;
+                        misc[8 + h] = alpha;
+                    }
+                }
+            } else {
+                // ---- O^T[d][n] += V^T P^T for d in this warp's columns ----
+                const int c = lane & 3;
+                const float al0 = misc[8 + ((2 * c) & 3)], al1 = misc[8 + ((2 * c + 1) & 3)];
+#pragma unroll
+                for (int mt = 0; mt < MT; mt++) {
+                    acc[mt][0] *= al0;
+                    acc[mt][1] *= al1;
+                    acc[mt][2] *= al0;
+                    acc[mt][3] *= al1;
+                }
+                const int n = lane >> 2;
+                const int jm = lane >> 3;
+#pragma unroll
+                for (int kk = 0; kk < kTile / 16; kk++) {
+                    const int tl = 16 * kk + 2 * c;
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(P_s + n * kPRow + tl);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(P_s + n * kPRow + tl + 8);
+                    const int r = 16 * kk + (lane & 7) + ((jm >> 1) << 3);
+#pragma unroll
+                    for (int mt = 0; mt < MT; mt++) {
+                        const int ch = ((warp * DW + 16 * mt) >> 3) + (jm & 1);
+                        uint32_t a0, a1, a2, a3;
+                        ldmatrix_x4_trans(tb + (uint32_t)(r * D + ((ch ^ (r & 7)) * 8)) * 2u, a0, a1, a2, a3);
+                        mma_16816(acc[mt], a0, a1, a2, a3, b0, b1);
+                    }
+                }
+            }
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+    }
+
+    // ---- 4. partial (O unnormalised, m, l) ----
+    const long long pidx = (p.part_off[b] + split) * Hkv + kvh;
+    float* po = p.part_o + pidx * kGP * D;
+    {
+        const int c = lane & 3;
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++) {
+            float o0 = __shfl_xor_sync(0xffffffffu, acc[mt][0], 2);
+            float o1 = __shfl_xor_sync(0xffffffffu, acc[mt][1], 2);
+            float o2 = __shfl_xor_sync(0xffffffffu, acc[mt][2], 2);
+            float o3 = __shfl_xor_sync(0xffffffffu, acc[mt][3], 2);
+            if (c < 2) {
+                const int d0 = warp * DW + 16 * mt + (lane >> 2);
+                const int h0 = 2 * c, h1 = h0 + 1;
+                po[h0 * D + d0] = acc[mt][0] + o0;
+                po[h1 * D + d0] = acc[mt][1] + o1;
+                po[h0 * D + d0 + 8] = acc[mt][2] + o2;
+                po[h1 * D + d0 + 8] = acc[mt][3] + o3;
+            }
+        }
+        if (tid < kGP) {
+            p.part_ml[pidx * kGP * 2 + 2 * tid] = (n_tok > 0) ? misc[tid] : -INFINITY;
+            p.part_ml[pidx * kGP * 2 + 2 * tid + 1] = (n_tok > 0) ? misc[4 + tid] : 0.f;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (tid == 0) {
+        const int prev = atomicAdd(&p.cnt_head[b * Hkv + kvh], 1);
+        s_last = (prev == p.nsplit[b] - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    // ---- 5. merge splits, gate, write (last CTA of this row / kv head) ----
+    const int ns = p.nsplit[b];
+    const long long p0 = p.part_off[b];
+    float* wts = reinterpret_cast<float*>(smem + S::tiles);  // [ns][kGP] (tiles are free now)
+    __shared__ float s_L[kGP];
+    if (warp < G) {
+        const int h = warp;
+        float M = -INFINITY;
+        for (int s = lane; s < ns; s += 32)
+            M = fmaxf(M, ld_cg(p.part_ml + ((p0 + s) * Hkv + kvh) * kGP * 2 + 2 * h));
+        M = warp_max(M);
+        float L = 0.f;
+        for (int s = lane; s < ns; s += 32) {
+            const float* ml = p.part_ml + ((p0 + s) * Hkv + kvh) * kGP * 2 + 2 * h;
+            const float m = ld_cg(ml);
+            const float w = (m == -INFINITY) ? 0.f : expf(m - M);
+            wts[s * kGP + h] = w;
+            L += w * ld_cg(ml + 1);
+        }
+        L = warp_sum(L);
+        if (lane == 0) s_L[h] = L;
+    }
+    __syncthreads();
+    for (int idx4 = tid; idx4 < (G * D) / 4; idx4 += kThreads) {
+        const int g = (idx4 * 4) / D, i = idx4 * 4 - g * D;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int s = 0; s < ns; s++) {
+            const float w = wts[s * kGP + g];
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(
+                p.part_o + ((p0 + s) * Hkv + kvh) * kGP * D + g * D + i));
+            o.x += w * v.x;
+            o.y += w * v.y;
+            o.z += w * v.z;
+            o.w += w * v.w;
+        }
+        const float L = s_L[g];
+        float ov[4] = {o.x, o.y, o.z, o.w};
+        const int h = kvh * G + g;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            float O = (L > 0.f) ? ov[e] / L : 0.f;
+            if (p.gate) {  // mul_sigmoid_inplace, core/cpu_ops.cpp:15-22
+                const float z = load_as_float(proj_row, p.proj_dtype,
+                                              p.gate_off + (long long)h * p.q_head_stride + i + e);
+                O = O / (1.0f + expf(-z));
+            }
+            store_from_float(p.out, p.out_dtype, (long long)b * p.out_stride + (long long)h * D + i + e, O);
+        }
+    }
+    if (tid == 0) {
+        p.cnt_head[b * Hkv + kvh] = 0;
+        __threadfence();
+        const int prev = atomicAdd(&p.cnt_seq[b], 1);
+        if (prev == Hkv - 1) {
+            if (p.append && p.kv_len) {
+                p.kv_len[seq] = len1;
+                p.kv_start[seq] = start1;
+            }
+            p.cnt_seq[b] = 0;
+        }
+    }
+}
+
+}  // namespace
+
+int fa_decode_max_splits(int head_dim) {
+    const size_t tiles = size_t(kStages) * kTile * head_dim * 2;
+    return (int)(tiles / (kGP * sizeof(float)));
+}
+
+size_t fa_decode_smem_bytes(int head_dim) {
+    return head_dim == 256 ? Smem<256>::total : Smem<128>::total;
+}
+
+int launch_fa_decode(const FaDecodeParams& p, int head_dim, int n_blocks, cudaStream_t stream) {
+    dim3 grid(n_blocks, p.Hkv);
+    if (head_dim == 256) {
+        const size_t sm = Smem<256>::total;
+        cudaFuncSetAttribute(fa_decode_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        fa_decode_kernel<256><<<grid, kThreads, sm, stream>>>(p);
+    } else if (head_dim == 128) {
+        const size_t sm = Smem<128>::total;
+        cudaFuncSetAttribute(fa_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        fa_decode_kernel<128><<<grid, kThreads, sm, stream>>>(p);
+    } else {
+        return ANELM_ERR_UNSUPPORTED;
+    }
+    return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
+}
+
+}  // namespace anelm

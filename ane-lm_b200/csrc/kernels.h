@@ -1,0 +1,86 @@
+// Kernel parameter blocks and launchers shared between the host ABI (anelm_abi.cu)
+// and the kernel translation units.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace anelm {
+
+// Split-K flash-decoding over slot-major fp16 KV rings [slots][Hkv][D].
+// One CTA per (batch row b, ring split, kv head).
+struct FaDecodeParams {
+    int Hq, Hkv, rot_dim;
+    float rope_theta, rms_eps, scale;
+    int gate, qk_norm, rope_mode, kv_mode, append;
+    const float* q_norm;
+    const float* k_norm;
+    const float* rope_cos;
+    const float* rope_sin;
+    int rope_len;
+    // KV pool of this layer
+    __half* k_pool;
+    __half* v_pool;
+    const long long* kv_base;  // [seq] first slot of the sequence's ring in the pool
+    const int* kv_cap;         // [seq]
+    int* kv_len;               // [seq] (this layer); nullptr => scalar metadata below
+    int* kv_start;             // [seq]
+    int cap_s, len_s, start_s;
+    // batch
+    const int* seq_ids;        // [n] or nullptr (=> seq 0)
+    const int* pos_arr;        // [n] device positions or nullptr
+    int pos_scalar;
+    const void* proj;          // [n][proj_stride] elements of proj_dtype
+    int proj_dtype;
+    long long proj_stride;
+    int q_head_stride;         // elements between q heads inside a proj row (2*D in the glue)
+    long long k_off, v_off;    // element offsets of the new k / v inside a proj row
+    long long gate_off;        // element offset of head 0's gate inside a proj row (q_head_stride apart)
+    void* out;
+    int out_dtype;
+    long long out_stride;
+    // split plan
+    const int* blk_b;
+    const int* blk_split;
+    const int* nsplit;         // [n]
+    const long long* part_off; // [n] first split index of row b in the partial arrays
+    int CH;                    // tokens per split (multiple of 64)
+    float* part_o;             // [total_splits][Hkv][4][D]
+    float* part_ml;            // [total_splits][Hkv][4][2]
+    int* cnt_head;             // [n][Hkv] zero between launches
+    int* cnt_seq;              // [n]      zero between launches
+    int* err;                  // device error word (first error code wins), may be nullptr
+};
+
+// Gated DeltaNet decode step; a cluster of NSPLIT CTAs per (batch row, value head),
+// each CTA owning dv/NSPLIT columns of the fp32 state.
+struct GdnDecodeParams {
+    int Hk, Hv, C;
+    float l2_eps;
+    int delta_mode;
+    const float* conv_w;   // [C][4]
+    const float* A;        // [Hv] = exp(A_log)
+    const float* dt_bias;  // [Hv]
+    const float* norm_w;   // [dv]
+    float* ssm;            // [seqs][Hv][128][128]
+    float* conv4;          // [seqs][C][4] ring of the last 4 inputs
+    int* conv_cnt;         // [seqs] tokens seen (ring index = cnt mod 4)
+    const int* seq_ids;    // [n] or nullptr
+    int seq_scalar;
+    const void* proj;
+    int proj_dtype;
+    long long proj_stride;
+    void* out;
+    int out_dtype;
+    long long out_stride;
+    int* cnt_seq;          // [n] zero between launches
+};
+
+int launch_fa_decode(const FaDecodeParams& p, int head_dim, int n_blocks, cudaStream_t stream);
+size_t fa_decode_smem_bytes(int head_dim);
+// Largest split count one row may use: the merge keeps [splits][4] weights in the tile buffers.
+int fa_decode_max_splits(int head_dim);
+int launch_gdn_decode(const GdnDecodeParams& p, int n_rows, int key_dim, int val_dim, cudaStream_t stream);
+
+}  // namespace anelm

@@ -10,7 +10,9 @@ Fixtures written (seeded, numpy default_rng):
 
 * ``cpu_ops_ref.npz``      -- each core/cpu_ops.h entry point on small inputs;
 * ``full_attn_ref.npz``    -- forward_full_attn_from_proj (qwen3_5.cpp:944-1002) over
-  40 tokens of a 32-slot ring (so the ring wraps), 8 q / 2 kv heads, d=256;
+  40 tokens of a 32-slot ring (so the ring wraps), 8 q / 2 kv heads, d=256; once with
+  the reference's fp32 cache and once with K/V rounded to fp16 as they are written
+  (``*_f16kv``: the storage format of the GPU ring);
 * ``deltanet_ref.npz``     -- forward_deltanet_from_proj (qwen3_5.cpp:849-910) over
   16 tokens, 4 value / 2 key heads, dk=dv=128, random initial state;
 * ``serve_hybrid_ref.npz`` -- scripts/serve_hybrid.py:85-132 ``cpu_attention`` run from
@@ -115,10 +117,15 @@ def gen_full_attn(rng):
     ring = po.KVRing.empty(cap, 2, d_)
     start_pos = 4070  # crosses the 4096-row table edge -> on-the-fly RoPE branch too
     out = po.full_attn_tokens("ref", shape, var, q_norm, k_norm, ring, proj, start_pos, (cos, sin))
+    # same run with the K/V written to the cache rounded to fp16 (the GPU's storage format)
+    ring16 = po.KVRing.empty(cap, 2, d_)
+    out16 = po.full_attn_tokens("ref", shape, po.make_variant(kv_round_f16=1), q_norm, k_norm, ring16, proj,
+                                start_pos, (cos, sin))
     np.savez_compressed(os.path.join(OUT, "full_attn_ref.npz"), proj=proj.astype(np.float16),
                         q_norm=q_norm, k_norm=k_norm, start_pos=np.int32(start_pos), cap=np.int32(cap),
                         out=out, k_cache=ring.k, v_cache=ring.v, len=np.int32(ring.len),
-                        start=np.int32(ring.start))
+                        start=np.int32(ring.start), out_f16kv=out16, k_cache_f16kv=ring16.k,
+                        v_cache_f16kv=ring16.v)
 
 
 def gen_deltanet(rng):
