@@ -85,7 +85,6 @@ struct anelm_plan {
     float* part_ml = nullptr;
     int* cnt_head = nullptr;
     int* cnt_seq = nullptr;
-    int* cnt_gdn = nullptr;
     std::vector<void*> allocs;
 };
 
@@ -106,8 +105,8 @@ struct anelm_ctx {
     std::vector<__half*> k_pool, v_pool;
     std::vector<float*> q_norm, k_norm;
     std::vector<char> fa_w_set;
-    std::vector<float*> ssm, conv4;
-    int* conv_cnt = nullptr;  // [n_gdn][max_seqs]
+    std::vector<float*> ssm, conv;
+    int* conv_pos = nullptr;  // [n_gdn][max_seqs][Hk]
     std::vector<float*> conv_w, A, dt_bias, norm_w;
     std::vector<char> gdn_w_set;
     float* rope_cos = nullptr;
@@ -207,7 +206,6 @@ int build_plan(anelm_ctx* ctx, int n, const int* seqs, anelm_plan** out) {
         if ((rc = dev_alloc(p->allocs, &(ptr), (count)))) return cleanup(rc); \
     } while (0)
     PALLOC(p->seq_d, n);
-    PALLOC(p->cnt_gdn, n);
     if (cudaMemcpy(p->seq_d, seqs, n * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
         return cleanup(fail(ANELM_ERR_CUDA, "plan upload failed"));
     if (ctx->n_fa > 0) {
@@ -323,8 +321,8 @@ GdnDecodeParams gdn_params(anelm_ctx* ctx, int layer, const anelm_plan* plan, co
     p.dt_bias = ctx->dt_bias[gi];
     p.norm_w = ctx->norm_w[gi];
     p.ssm = ctx->ssm[gi];
-    p.conv4 = ctx->conv4[gi];
-    p.conv_cnt = ctx->conv_cnt + (long long)gi * c.max_seqs;
+    p.conv = ctx->conv[gi];
+    p.conv_pos = ctx->conv_pos + (long long)gi * c.max_seqs * c.lin_num_key_heads;
     p.seq_ids = plan->seq_d;
     p.proj = proj;
     p.proj_dtype = proj_dtype;
@@ -332,7 +330,6 @@ GdnDecodeParams gdn_params(anelm_ctx* ctx, int layer, const anelm_plan* plan, co
     p.out = out;
     p.out_dtype = out_dtype;
     p.out_stride = (long long)c.lin_num_val_heads * c.lin_val_dim;
-    p.cnt_seq = plan->cnt_gdn;
     return p;
 }
 
@@ -527,9 +524,9 @@ ANELM_API int anelm_create(const anelm_config* cfg, int device, anelm_ctx** out)
         CALLOC(ctx->py_out, (size_t)c.num_q_heads * c.head_dim);
     }
     if (ctx->n_gdn > 0) {
-        CALLOC(ctx->conv_cnt, (size_t)ctx->n_gdn * c.max_seqs);
+        CALLOC(ctx->conv_pos, (size_t)ctx->n_gdn * c.max_seqs * c.lin_num_key_heads);
         ctx->ssm.resize(ctx->n_gdn);
-        ctx->conv4.resize(ctx->n_gdn);
+        ctx->conv.resize(ctx->n_gdn);
         ctx->conv_w.resize(ctx->n_gdn);
         ctx->A.resize(ctx->n_gdn);
         ctx->dt_bias.resize(ctx->n_gdn);
@@ -537,7 +534,7 @@ ANELM_API int anelm_create(const anelm_config* cfg, int device, anelm_ctx** out)
         ctx->gdn_w_set.assign(ctx->n_gdn, 0);
         for (int g = 0; g < ctx->n_gdn; g++) {
             CALLOC(ctx->ssm[g], (size_t)c.max_seqs * Hv * dk * dv);
-            CALLOC(ctx->conv4[g], (size_t)c.max_seqs * ctx->C * 4);
+            CALLOC(ctx->conv[g], (size_t)c.max_seqs * ctx->C * 3);
             CALLOC(ctx->conv_w[g], (size_t)ctx->C * 4);
             CALLOC(ctx->A[g], Hv);
             CALLOC(ctx->dt_bias[g], Hv);
@@ -603,8 +600,9 @@ ANELM_API int anelm_reset(anelm_ctx* ctx, int seq) {
     const size_t st = (size_t)c.lin_num_val_heads * c.lin_key_dim * c.lin_val_dim;
     for (int g = 0; g < ctx->n_gdn; g++) {
         CUDA_TRY(cudaMemset(ctx->ssm[g] + s0 * st, 0, (s1 - s0) * st * 4));
-        CUDA_TRY(cudaMemset(ctx->conv4[g] + (size_t)s0 * ctx->C * 4, 0, (size_t)(s1 - s0) * ctx->C * 16));
-        CUDA_TRY(cudaMemset(ctx->conv_cnt + (size_t)g * c.max_seqs + s0, 0, (s1 - s0) * 4));
+        CUDA_TRY(cudaMemset(ctx->conv[g] + (size_t)s0 * ctx->C * 3, 0, (size_t)(s1 - s0) * ctx->C * 12));
+        const size_t hk = c.lin_num_key_heads;
+        CUDA_TRY(cudaMemset(ctx->conv_pos + ((size_t)g * c.max_seqs + s0) * hk, 0, (s1 - s0) * hk * 4));
     }
     CUDA_TRY(cudaDeviceSynchronize());
     return ANELM_OK;
@@ -702,17 +700,17 @@ ANELM_API int anelm_deltanet_state_export(anelm_ctx* ctx, int layer, int seq, fl
     const size_t st = (size_t)c.lin_num_val_heads * c.lin_key_dim * c.lin_val_dim;
     CUDA_TRY(cudaDeviceSynchronize());
     if (ssm_host) CUDA_TRY(cudaMemcpy(ssm_host, ctx->ssm[g] + seq * st, st * 4, cudaMemcpyDeviceToHost));
-    int n = 0;
-    CUDA_TRY(cudaMemcpy(&n, ctx->conv_cnt + (size_t)g * c.max_seqs + seq, 4, cudaMemcpyDeviceToHost));
-    if (conv_host) {
-        // 4-slot ring (x_t in slot t mod 4) -> reference ring [C][3] with conv_pos = n mod 3
-        std::vector<float> r4((size_t)ctx->C * 4);
-        CUDA_TRY(cudaMemcpy(r4.data(), ctx->conv4[g] + (size_t)seq * ctx->C * 4, r4.size() * 4, cudaMemcpyDeviceToHost));
-        const int p3 = n % 3;
-        for (int ch = 0; ch < ctx->C; ch++)
-            for (int j = 0; j < 3; j++) conv_host[ch * 3 + (p3 + j) % 3] = r4[(size_t)ch * 4 + ((n + 1 + j) & 3)];
-    }
-    if (conv_pos) *conv_pos = n % 3;
+    // the ring is kept in the reference layout [C][3]; every key-head copy of the position is equal
+    const size_t hk = c.lin_num_key_heads;
+    std::vector<int> pos(hk);
+    CUDA_TRY(cudaMemcpy(pos.data(), ctx->conv_pos + ((size_t)g * c.max_seqs + seq) * hk, hk * 4,
+                        cudaMemcpyDeviceToHost));
+    for (size_t i = 1; i < hk; i++)
+        if (pos[i] != pos[0]) return fail(ANELM_ERR_STATE, "conv ring positions disagree across key heads");
+    if (conv_host)
+        CUDA_TRY(cudaMemcpy(conv_host, ctx->conv[g] + (size_t)seq * ctx->C * 3, (size_t)ctx->C * 12,
+                            cudaMemcpyDeviceToHost));
+    if (conv_pos) *conv_pos = pos[0];
     return ANELM_OK;
 }
 
@@ -727,14 +725,13 @@ ANELM_API int anelm_deltanet_state_import(anelm_ctx* ctx, int layer, int seq, co
     const size_t st = (size_t)c.lin_num_val_heads * c.lin_key_dim * c.lin_val_dim;
     CUDA_TRY(cudaDeviceSynchronize());
     if (ssm_host) CUDA_TRY(cudaMemcpy(ctx->ssm[g] + seq * st, ssm_host, st * 4, cudaMemcpyHostToDevice));
-    const int n = conv_pos;  // n mod 3 == conv_pos, n mod 4 == conv_pos
-    if (conv_host) {
-        std::vector<float> r4((size_t)ctx->C * 4, 0.f);
-        for (int ch = 0; ch < ctx->C; ch++)
-            for (int j = 0; j < 3; j++) r4[(size_t)ch * 4 + ((n + 1 + j) & 3)] = conv_host[ch * 3 + (conv_pos + j) % 3];
-        CUDA_TRY(cudaMemcpy(ctx->conv4[g] + (size_t)seq * ctx->C * 4, r4.data(), r4.size() * 4, cudaMemcpyHostToDevice));
-    }
-    CUDA_TRY(cudaMemcpy(ctx->conv_cnt + (size_t)g * c.max_seqs + seq, &n, 4, cudaMemcpyHostToDevice));
+    if (conv_host)
+        CUDA_TRY(cudaMemcpy(ctx->conv[g] + (size_t)seq * ctx->C * 3, conv_host, (size_t)ctx->C * 12,
+                            cudaMemcpyHostToDevice));
+    const size_t hk = c.lin_num_key_heads;
+    std::vector<int> pos(hk, conv_pos);
+    CUDA_TRY(cudaMemcpy(ctx->conv_pos + ((size_t)g * c.max_seqs + seq) * hk, pos.data(), hk * 4,
+                        cudaMemcpyHostToDevice));
     return ANELM_OK;
 }
 

@@ -53,8 +53,8 @@ struct FaDecodeParams {
     int* err;                  // device error word (first error code wins), may be nullptr
 };
 
-// Gated DeltaNet decode step; a cluster of NSPLIT CTAs per (batch row, value head),
-// each CTA owning dv/NSPLIT columns of the fp32 state.
+// Gated DeltaNet decode step; one cluster per (batch row, key head): the value heads
+// sharing that key head times column blocks of their fp32 state.
 struct GdnDecodeParams {
     int Hk, Hv, C;
     float l2_eps;
@@ -64,8 +64,8 @@ struct GdnDecodeParams {
     const float* dt_bias;  // [Hv]
     const float* norm_w;   // [dv]
     float* ssm;            // [seqs][Hv][128][128]
-    float* conv4;          // [seqs][C][4] ring of the last 4 inputs
-    int* conv_cnt;         // [seqs] tokens seen (ring index = cnt mod 4)
+    float* conv;           // [seqs][C][3] ring of the last 3 inputs (reference layout)
+    int* conv_pos;         // [seqs][Hk] ring position, one copy per key-head cluster
     const int* seq_ids;    // [n] or nullptr
     int seq_scalar;
     const void* proj;
@@ -74,7 +74,6 @@ struct GdnDecodeParams {
     void* out;
     int out_dtype;
     long long out_stride;
-    int* cnt_seq;          // [n] zero between launches
 };
 
 int launch_fa_decode(const FaDecodeParams& p, int head_dim, int n_blocks, cudaStream_t stream);

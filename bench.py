@@ -1,0 +1,564 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 attention core (one JSON line on rank 0).
+
+Default workload: batched serving decode of a Qwen3.5-4B
+shaped 32-layer stack (24 Gated DeltaNet + 8 gated full-attention layers, 3:1),
+256 concurrent sequences per GPU with ragged KV lengths ~ U[512, 32768] (fp16
+N(0,1)) and per-sequence fp32 DeltaNet state N(0, 0.1).  One step = one decode
+token for every sequence through all 32 layers' attention cores, each layer one
+call of the C ABI (anelm_full_attn_decode / anelm_deltanet_decode) on the
+layer's synthetic projection rows.  Sequences are independent: under torchrun
+each rank owns its own 256 sequences (weak scaling, no data-path collective).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py --workload fa_b1|gdn_b1      # BASELINE configs 1 / 2 (single sequence)
+
+The reference arm (--impl reference) times the reference's own CPU attention
+core (core/cpu_ops.cpp compiled unmodified + the qwen3_5.cpp glue, oracle/_ref)
+on the host cores over a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "ane-lm_b200"))
+
+PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
+FALLBACK_HBM = 6650.0
+
+# Qwen3.5-4B attention-core shape (serve_hybrid.py:32-47)
+HQ, HKV, HD, ROT = 16, 4, 256, 64
+HK, HV, DK, DV = 16, 32, 128, 128
+N_LAYERS = 32
+LAYER_TYPES = [1 if (l + 1) % 4 == 0 else 0 for l in range(N_LAYERS)]  # every 4th layer full attention
+C_CONV = 2 * HK * DK + HV * DV
+FA_PROJ = HQ * 2 * HD + 2 * HKV * HD
+GDN_PROJ = C_CONV + HV * DV + 2 * HV
+FA_OUT = HQ * HD
+GDN_OUT = HV * DV
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def peaks():
+    try:
+        d = json.load(open(PEAKS))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+def kv_lengths(n, seed=0):
+    return np.random.default_rng(seed).integers(512, 32768, size=n, endpoint=True).astype(np.int64)
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (median SM clock + throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = [l.split(",") for l in open(self.path).read().strip().splitlines() if l.count(",") >= 8]
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if "Active" in val and "Not" not in val:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip().replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def setup_serving(torch, n_seqs, lengths, slack, seed, device):
+    import anelm_b200 as ab
+    from anelm_b200.core import Context
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    caps = [int(L) + slack for L in lengths]
+    ctx = Context(device=device.index or 0, layer_types=LAYER_TYPES, num_q_heads=HQ, num_kv_heads=HKV, head_dim=HD,
+                  rot_dim=ROT, rope_theta=1e7, lin_num_key_heads=HK, lin_num_val_heads=HV,
+                  seq_kv_capacity=caps, rope_table_len=4096)
+    rng = np.random.default_rng(seed)
+    # weights: QK-norm N(1, 0.02); conv fp16 N(0, 0.5); A = 1, dt_bias = 0; norm 1 + N(0, 0.1)
+    for l, t in enumerate(LAYER_TYPES):
+        if t == ab.LAYER_FULL_ATTN:
+            ctx.set_full_attn_weights(l, (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32),
+                                      (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32))
+        else:
+            cw = (0.5 * rng.standard_normal((C_CONV, 4))).astype(np.float16).astype(np.float32)
+            ctx.set_deltanet_weights(l, cw, np.ones(HV, np.float32), np.zeros(HV, np.float32),
+                                     (1 + 0.1 * rng.standard_normal(DV)).astype(np.float32))
+    # KV: fp16 N(0,1) rows drawn from one random pool at rotating offsets (values are
+    # N(0,1) everywhere; only their position in the pool repeats).
+    row = HKV * HD
+    pool_rows = 1 << 18
+    src = torch.randn(pool_rows + 32768, row, generator=g, device=device, dtype=torch.float16)
+    off = 0
+    for l, t in enumerate(LAYER_TYPES):
+        if t != ab.LAYER_FULL_ATTN:
+            continue
+        for s, L in enumerate(lengths):
+            L = int(L)
+            o1 = off % pool_rows
+            o2 = (off * 7 + 12345) % pool_rows
+            ctx.kv_write(l, s, 0, src[o1:o1 + L], src[o2:o2 + L])
+            ctx.kv_set_meta(l, s, L, 0)
+            off += 104729
+    del src
+    st = (0.1 * torch.randn(16, HV, DK, DV, generator=g, device=device, dtype=torch.float32)).contiguous()
+    for l, t in enumerate(LAYER_TYPES):
+        if t != ab.LAYER_LINEAR_ATTN:
+            continue
+        for s in range(n_seqs):
+            ctx.deltanet_state_write(l, s, st[(s + l) % 16])
+    torch.cuda.synchronize(device)
+    del st
+    plan = ctx.plan(list(range(n_seqs)))
+    projs = []
+    for t in LAYER_TYPES:
+        w = FA_PROJ if t == ab.LAYER_FULL_ATTN else GDN_PROJ
+        projs.append(torch.randn(n_seqs, w, generator=g, device=device, dtype=torch.float16))
+    outs = [torch.empty(n_seqs, FA_OUT if t == ab.LAYER_FULL_ATTN else GDN_OUT, device=device,
+                        dtype=torch.float16) for t in LAYER_TYPES]
+    return ctx, plan, projs, outs
+
+
+def step_bytes(lengths, step_offset):
+    """Algorithmic HBM bytes of ONE full-attention layer launch and ONE DeltaNet layer
+    launch over all sequences at `step_offset` tokens past the initial lengths."""
+    n = len(lengths)
+    Lcur = lengths + step_offset
+    fa = 0
+    fa += int((2 * Lcur * HKV * HD * 2).sum())          # K and V rows read (old tokens)
+    fa += n * (FA_PROJ * 2 + FA_OUT * 2 + 2 * HKV * HD * 2)  # projection in, output, appended k/v
+    gdn = n * (2 * HV * DK * DV * 4                      # state read + write
+               + C_CONV * 16                             # conv ring: 3 old inputs read + 1 written
+               + GDN_PROJ * 2 + GDN_OUT * 2) + C_CONV * 16  # projection in, output; conv weights
+    return fa, gdn
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = env_rank()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    hbm_peak, peak_kind = peaks()
+
+    if args.workload != "serve":
+        return run_gpu_single(args, torch, device, hbm_peak, peak_kind)
+
+    n = args.seqs
+    lengths = kv_lengths(n, 0)
+    slack = args.warmup + args.steps + 16
+    ctx, plan, projs, outs = setup_serving(torch, n, lengths, slack, 1000 + rank, device)
+    import anelm_b200 as ab
+
+    pos = [torch.tensor(lengths + k, dtype=torch.int32, device=device) for k in range(args.warmup + args.steps + 1)]
+    fa_layers = [l for l, t in enumerate(LAYER_TYPES) if t == ab.LAYER_FULL_ATTN]
+    stream = torch.cuda.current_stream(device)
+
+    def step(k, ev=None):
+        for l, t in enumerate(LAYER_TYPES):
+            if t == ab.LAYER_FULL_ATTN:
+                if ev is not None:
+                    ev[l][0].record(stream)
+                ctx.full_attn_decode(plan, l, projs[l], pos[k], outs[l])
+                if ev is not None:
+                    ev[l][1].record(stream)
+            else:
+                if ev is not None:
+                    ev[l][0].record(stream)
+                ctx.deltanet_decode(plan, l, projs[l], outs[l])
+                if ev is not None:
+                    ev[l][1].record(stream)
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    ev_steps = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in LAYER_TYPES]
+                for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    t0.record(stream)
+    for k in range(args.steps):
+        step(args.warmup + k, ev_steps[k])
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    ck = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+        dist.barrier()
+    err = ctx.device_error()
+    assert err == 0, f"device reported status {err}"
+
+    # per-kernel times (events on the launching stream)
+    fa_ms = [ev_steps[k][l][0].elapsed_time(ev_steps[k][l][1]) for k in range(args.steps) for l in fa_layers]
+    gdn_ms = [ev_steps[k][l][0].elapsed_time(ev_steps[k][l][1]) for k in range(args.steps)
+              for l, t in enumerate(LAYER_TYPES) if t == 0]
+    n_fa = len(fa_layers)
+    n_gdn = N_LAYERS - n_fa
+    fa_b = gdn_b = 0  # per-launch bytes summed over the timed steps
+    for k in range(args.steps):
+        a, b = step_bytes(lengths, args.warmup + k)
+        fa_b += a
+        gdn_b += b
+    fa_per_launch = fa_b / args.steps
+    gdn_per_launch = gdn_b / args.steps
+    fa_gbs = fa_per_launch / (statistics.mean(fa_ms) * 1e-3) / 1e9
+    gdn_gbs = gdn_per_launch / (statistics.mean(gdn_ms) * 1e-3) / 1e9
+    ms_step = ms / args.steps
+    tok_s = n * world / (ms_step * 1e-3)
+    step_gb = (n_fa * fa_per_launch + n_gdn * gdn_per_launch) / 1e9
+
+    # e2e: same step through the C ABI with host (pinned) buffers, copies inside the timed region
+    e2e = run_e2e(args, torch, ctx, plan, projs, outs, pos, device, world)
+
+    result = {
+        "metric": "decode attn-core tok/s (batched serving decode, 32-layer 3:1 DeltaNet:attention stack)",
+        "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "BASELINE cfg5: batched serving decode, Qwen3.5-4B-shaped 32 layers (24 GDN + 8 FA)",
+                   "seqs_per_gpu": n, "global_batch": n * world, "kv_len": "U[512,32768] seed 0",
+                   "kv_storage": "fp16 ring [slots][4][256]", "state": "fp32 [32][128][128] per seq per GDN layer",
+                   "proj_io": "fp16", "Hq": HQ, "Hkv": HKV, "head_dim": HD, "rot_dim": ROT, "Hv": HV, "Hk": HK,
+                   "parallelism": f"sequence-sharded x{world}, no collective",
+                   "l2": f"inputs {step_gb:.1f} GB/step > 126 MB L2 (no flush needed)"},
+        "hbm_gbs_step": round(step_gb / (ms_step * 1e-3), 1),
+        "roofline": {"bound": "hbm", "kernel": "fa_decode_kernel<256>", "achieved": round(fa_gbs, 1),
+                     "peak": hbm_peak, "unit": "GB/s", "frac": round(fa_gbs / hbm_peak, 4),
+                     "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": int(fa_per_launch)},
+        "roofline_gdn": {"bound": "hbm", "kernel": "gdn_decode_kernel<4>", "achieved": round(gdn_gbs, 1),
+                         "peak": hbm_peak, "unit": "GB/s", "frac": round(gdn_gbs / hbm_peak, 4),
+                         "algorithmic_bytes_per_launch": int(gdn_per_launch)},
+        "e2e": e2e,
+        "kernel_ms_per_step": {"fa_decode": round(n_fa * statistics.mean(fa_ms), 3),
+                               "gdn_decode": round(n_gdn * statistics.mean(gdn_ms), 3)},
+        "gpu_launches": args.steps * N_LAYERS,
+        "clocks": ck,
+    }
+    if args.traffic_json and os.path.exists(args.traffic_json):
+        tr = json.load(open(args.traffic_json))
+        result["roofline"]["traffic"] = tr.get("fa_decode_bytes_per_launch")
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_reference_serving(args.cpu_seconds, threads=None, kind="reference")
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    plan.close()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, torch, ctx, plan, projs, outs, pos, device, world):
+    """The step with projections coming from pinned HOST memory and outputs going back
+    to the host every step (copies on a side stream, overlapped with earlier layers)."""
+    import anelm_b200 as ab
+    import torch.distributed as dist
+
+    host_in = [p.cpu().pin_memory() for p in projs]
+    host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    comp = torch.cuda.current_stream(device)
+    copy = torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in LAYER_TYPES]
+    ev_out = [torch.cuda.Event() for _ in LAYER_TYPES]
+    h2d = sum(h.numel() * h.element_size() for h in host_in)
+    d2h = sum(h.numel() * h.element_size() for h in host_out)
+    base = args.warmup + args.steps  # positions continue after the device-resident run
+    # each e2e step appends one more token; capacity slack covers warmup + steps + 16
+
+    def step(k):
+        with torch.cuda.stream(copy):
+            for l in range(N_LAYERS):
+                projs[l].copy_(host_in[l], non_blocking=True)
+                ev_in[l].record(copy)
+        for l, t in enumerate(LAYER_TYPES):
+            comp.wait_event(ev_in[l])
+            if t == ab.LAYER_FULL_ATTN:
+                ctx.full_attn_decode(plan, l, projs[l], pos[min(k, len(pos) - 1)], outs[l])
+            else:
+                ctx.deltanet_decode(plan, l, projs[l], outs[l])
+            ev_out[l].record(comp)
+            with torch.cuda.stream(copy):
+                copy.wait_event(ev_out[l])
+                host_out[l].copy_(outs[l], non_blocking=True)
+        copy.synchronize()
+
+    n_steps = max(1, min(args.steps, 8))
+    step(base)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    t = time.perf_counter()
+    for k in range(n_steps):
+        step(base)
+    torch.cuda.synchronize(device)
+    dt = (time.perf_counter() - t) / n_steps
+    if world > 1:
+        tt = torch.tensor([dt], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dt = float(tt.item())
+    n = plan.n
+    return {"value": round(n * world / dt, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "steps": n_steps,
+            "note": "host pinned projections in / outputs out each step, timed on the host clock"}
+
+
+def run_gpu_single(args, torch, device, hbm_peak, peak_kind):
+    """BASELINE configs 1 and 2: one sequence, one layer call per step, replayed from a CUDA graph."""
+    import anelm_b200 as ab
+    from anelm_b200.core import Context
+
+    rng = np.random.default_rng(0)
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    if args.workload == "fa_b1":
+        ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_FULL_ATTN], max_seqs=1, kv_capacity=2048)
+        ctx.set_full_attn_weights(0, (1 + 0.02 * rng.standard_normal(256)).astype(np.float32),
+                                  (1 + 0.02 * rng.standard_normal(256)).astype(np.float32))
+        kv = torch.randn(2048, 2, 256, generator=g, device=device, dtype=torch.float16)
+        ctx.kv_write(0, 0, 0, kv, kv.flip(0).contiguous())
+        ctx.kv_set_meta(0, 0, 2048, 0)
+        proj = torch.randn(ctx.fa_proj_dim, generator=g, device=device, dtype=torch.float16)
+        out = torch.empty(ctx.fa_out_dim, device=device, dtype=torch.float16)
+        call = lambda: ctx.full_attn_from_proj(0, 0, proj, 5000, out)  # noqa: E731
+        nbytes = 2 * 2048 * 2 * 256 * 2 + ctx.fa_proj_dim * 2 + ctx.fa_out_dim * 2 + 2 * 2 * 256 * 2
+        metric, kname = "FA decode step tok/s (cfg1, 0.8B shape, KV 2048 fp16)", "fa_decode_kernel<256>"
+    else:
+        ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_LINEAR_ATTN], max_seqs=1)
+        C = ctx.conv_channels
+        ctx.set_deltanet_weights(0, (0.5 * rng.standard_normal((C, 4))).astype(np.float16).astype(np.float32),
+                                 np.ones(16, np.float32), np.zeros(16, np.float32), np.ones(128, np.float32))
+        st = (0.1 * torch.randn(16, 128, 128, generator=g, device=device)).contiguous()
+        ctx.deltanet_state_write(0, 0, st)
+        proj = torch.randn(ctx.gdn_proj_dim, generator=g, device=device, dtype=torch.float16)
+        out = torch.empty(ctx.gdn_out_dim, device=device, dtype=torch.float16)
+        call = lambda: ctx.deltanet_from_proj(0, 0, proj, out)  # noqa: E731
+        nbytes = 2 * 16 * 128 * 128 * 4 + C * 16 + C * 16 + ctx.gdn_proj_dim * 2 + ctx.gdn_out_dim * 2
+        metric, kname = "GDN decode step tok/s (cfg2, 16 heads, fp32 state)", "gdn_decode_kernel<8>"
+    for _ in range(max(3, args.warmup)):
+        call()
+    torch.cuda.synchronize(device)
+    reps = 64
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            for _ in range(reps):
+                call()
+    torch.cuda.synchronize(device)
+    graph.replay()
+    torch.cuda.synchronize(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    t1.record()
+    torch.cuda.synchronize(device)
+    us = t0.elapsed_time(t1) * 1e3 / (args.steps * reps)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    print(json.dumps({"metric": metric, "value": round(1e6 / us, 1), "unit": "tok/s", "n_gpus": 1,
+                      "steps": args.steps * reps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 6),
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                      "data": "synthetic", "config": {"workload": args.workload, "graph_replay": reps},
+                      "roofline": {"bound": "hbm", "kernel": kname, "achieved": round(gbs, 1), "peak": hbm_peak,
+                                   "unit": "GB/s", "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                                   "traffic": None, "algorithmic_bytes_per_launch": nbytes},
+                      "gpu_launches": args.steps * reps}), flush=True)
+    ctx.close()
+
+
+# ------------------------------------------------------------------ CPU reference arm
+
+def cpu_reference_serving(seconds: float, threads=None, kind="reference"):
+    """The reference CPU attention core (oracle/_ref/libref_core_fast.so: core/cpu_ops.cpp,
+    unmodified, + the qwen3_5.cpp glue restated) on a bounded sample of the serving
+    workload: `threads` sequences, each decoded token by token through all 32 layers
+    (fp32 KV ring of its length, fp32 DeltaNet state), one host thread per sequence.
+    Returns tokens/s over the sample."""
+    from oracle import pyoracle as po
+
+    lib_kind = "ref_fast" if po.available("ref_fast") else "oracle"
+    threads = threads or max(1, min(os.cpu_count() or 1, 32))
+    shape = po.make_shape(num_q_heads=HQ, num_kv_heads=HKV, head_dim=HD, rot_dim=ROT, rope_theta=1e7,
+                          lin_num_key_heads=HK, lin_num_val_heads=HV)
+    var = po.make_variant()
+    lengths = kv_lengths(256, 0)[:threads]
+    rng = np.random.default_rng(0)
+    qn = (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32)
+    cw = (0.5 * rng.standard_normal((C_CONV, 4))).astype(np.float16).astype(np.float32)
+    A, dtb = np.ones(HV, np.float32), np.zeros(HV, np.float32)
+    nw = np.ones(DV, np.float32)
+    rope = po.rope_table(4096, ROT, 1e7)
+    block = rng.standard_normal((4096, HKV, HD)).astype(np.float32)
+    fa_proj = rng.standard_normal(FA_PROJ).astype(np.float32)
+    gdn_proj = rng.standard_normal(GDN_PROJ).astype(np.float32)
+    fa = po.fn(lib_kind, "full_attn_from_proj")
+    gdn = po.fn(lib_kind, "deltanet_from_proj")
+    P = po.P
+
+    def worker(i):
+        L = int(lengths[i])
+        cap = L + 64
+        rings = []
+        for _ in range(8):
+            k = np.empty((cap, HKV, HD), np.float32)
+            v = np.empty((cap, HKV, HD), np.float32)
+            for o in range(0, cap, 4096):
+                m = min(4096, cap - o)
+                k[o:o + m] = block[:m]
+                v[o:o + m] = block[::-1][:m]
+            rings.append([k, v, ctypes.c_int(L), ctypes.c_int(0)])
+        states = [po.DeltaState.zeros(shape) for _ in range(24)]
+        for s in states:
+            s.ssm[:] = 0.01
+        out_fa = np.zeros(FA_OUT, np.float32)
+        out_g = np.zeros(GDN_OUT, np.float32)
+        tmp = np.zeros(HD, np.float32)
+        scratch = np.zeros(2 * C_CONV + GDN_OUT, np.float32)
+        pbuf = np.empty(FA_PROJ, np.float32)
+        tokens = 0
+        t_end = time.perf_counter() + seconds
+        t0 = time.perf_counter()
+        while True:
+            fi = gi = 0
+            for t in LAYER_TYPES:
+                if t == 1:
+                    k, v, ln, st = rings[fi]
+                    pbuf[:] = fa_proj
+                    fa(ctypes.byref(shape), ctypes.byref(var), P(qn), P(qn), P(k), P(v), ctypes.byref(ln),
+                       ctypes.byref(st), cap, P(rope[0]), P(rope[1]), 4096, P(pbuf), L + tokens, P(out_fa), P(tmp))
+                    fi += 1
+                else:
+                    s = states[gi]
+                    cp = ctypes.c_int(s.conv_pos)
+                    gdn(ctypes.byref(shape), ctypes.byref(var), P(cw), P(A), P(dtb), P(nw), P(s.ssm), P(s.conv),
+                        ctypes.byref(cp), P(gdn_proj), P(out_g), P(scratch))
+                    s.conv_pos = cp.value
+                    gi += 1
+            tokens += 1
+            if time.perf_counter() >= t_end or tokens >= 60:
+                break
+        return tokens, time.perf_counter() - t0
+
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        res = list(ex.map(worker, range(threads)))
+    toks = sum(r[0] for r in res)
+    wall = max(r[1] for r in res)
+    cpu_model = ""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                cpu_model = line.split(":", 1)[1].strip()
+                break
+    except Exception:
+        pass
+    return {"value": round(toks / wall, 3), "unit": "tok/s", "cores": threads, "kind": kind,
+            "sample": (f"{threads} sequences (KV lengths = the first {threads} of the workload's U[512,32768] draw), "
+                       f"{toks} tokens through all 32 layers, fp32 KV/state, {wall:.1f} s wall; "
+                       f"lib={os.path.basename(po.LIBS[lib_kind])}; cpu={cpu_model}; nproc={os.cpu_count()}")}
+
+
+def run_reference(args):
+    rank, world, local = env_rank()
+    if rank != 0:
+        return
+    cb = cpu_reference_serving(args.cpu_seconds, threads=None, kind="reference")
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "decode attn-core tok/s (batched serving decode, 32-layer 3:1 DeltaNet:attention stack)",
+        "value": cb["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "BASELINE cfg5: batched serving decode, Qwen3.5-4B-shaped 32 layers (24 GDN + 8 FA)",
+                   "seqs_per_gpu": args.seqs, "kv_len": "U[512,32768] seed 0"},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="anelm", choices=["anelm", "reference"])
+    ap.add_argument("--workload", default="serve", choices=["serve", "fa_b1", "gdn_b1"])
+    ap.add_argument("--seqs", type=int, default=256)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--traffic-json", default=os.path.join(REPO, "profiles", "traffic.json"))
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -65,14 +65,16 @@ def test_conv_ssm_ops(golden):
     ys = []
     for t in range(g["conv_x"].shape[0]):
         y = torch.empty(C, device="cuda")
-        check(L.anelm_conv1d_update(P(y), P(st), ctypes.byref(pos), P(D(g["conv_x"][t])), P(w), C, 4, None), "conv")
-        ys.append(y)
+        x = D(g["conv_x"][t])  # keep a reference: the kernel runs asynchronously
+        check(L.anelm_conv1d_update(P(y), P(st), ctypes.byref(pos), P(x), P(w), C, 4, None), "conv")
+        ys.append((y, x))
+    ys = [y for y, _ in ys]
     assert_close(torch.stack(ys).cpu(), g["conv_y"], atol=1e-6, rtol=1e-6, what="conv y")
     np.testing.assert_array_equal(st.cpu().numpy(), g["conv_state"])
     assert pos.value == int(g["conv_pos"][0])
     S, y = D(g["ssm_S0"]), torch.empty(128, device="cuda")
-    check(L.anelm_ssm_step(P(y), P(S), P(D(g["ssm_q"])), P(D(g["ssm_k"])), P(D(g["ssm_v"])), 0.9, 0.3, 128, 128,
-                           None), "ssm_step")
+    q, k, v = D(g["ssm_q"]), D(g["ssm_k"]), D(g["ssm_v"])
+    check(L.anelm_ssm_step(P(y), P(S), P(q), P(k), P(v), 0.9, 0.3, 128, 128, None), "ssm_step")
     assert_close(y.cpu(), g["ssm_y"], atol=1e-5, rtol=1e-4, what="ssm y")
     assert_close(S.cpu(), g["ssm_S"], atol=1e-6, rtol=1e-5, what="ssm S")
 
@@ -101,7 +103,7 @@ def test_gqa_attention_op_long_fp16():
     want = np.zeros((Hq, d), np.float32)
     po.lib("oracle").orc_gqa_attention(po.P(want), po.P(q), po.P(kc), po.P(vc), Hq, Hkv, d, 2 * d, 12345, 29999, cap)
     o = torch.empty((Hq, d), device="cuda")
-    check(lib().anelm_gqa_attention(P(o), P(D(q)), P(torch.from_numpy(kc).half().cuda()),
-                                    P(torch.from_numpy(vc).half().cuda()), ab.F16, Hq, Hkv, d, 2 * d, 12345, 29999,
-                                    cap, None), "gqa long")
+    qd, kd, vd = D(q), torch.from_numpy(kc).half().cuda(), torch.from_numpy(vc).half().cuda()
+    check(lib().anelm_gqa_attention(P(o), P(qd), P(kd), P(vd), ab.F16, Hq, Hkv, d, 2 * d, 12345, 29999, cap, None),
+          "gqa long")
     assert_close(o.cpu(), want, what="long wrapped ring")
