@@ -80,6 +80,7 @@ SIGNATURES = {
     "anelm_deltanet_decode": [_vp, _vp, _i, _vp, _i, _vp, _i, _vp],
     "anelm_py_cpu_attention": [_vp, _i, _i, _u16p, _u16p, _u16p, _i, _u16p, _vp],
     "anelm_gqa_attention": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
+    "anelm_gqa_attention_noalloc": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],
     "anelm_ssm_step": [_vp, _vp, _vp, _vp, _vp, _f, _f, _i, _i, _vp],
     "anelm_conv1d_update": [_vp, _vp, _ip, _vp, _vp, _i, _i, _vp],
     "anelm_rmsnorm": [_vp, _vp, _vp, _i, _f, _i, _vp],

@@ -70,6 +70,10 @@ int launch_status(int rc, const char* what) {
 
 }  // namespace
 
+namespace anelm {
+void set_last_error(const char* msg) { g_err = msg; }
+}  // namespace anelm
+
 struct anelm_plan {
     anelm_ctx* ctx = nullptr;
     int n = 0;

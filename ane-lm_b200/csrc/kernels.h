@@ -80,6 +80,9 @@ int launch_fa_decode(const FaDecodeParams& p, int head_dim, int n_blocks, cudaSt
 size_t fa_decode_smem_bytes(int head_dim);
 // Largest split count one row may use: the merge keeps [splits][4] weights in the tile buffers.
 int fa_decode_max_splits(int head_dim);
+// Sets the message anelm_last_error() returns on the calling thread.
+void set_last_error(const char* msg);
+
 int launch_gdn_decode(const GdnDecodeParams& p, int n_rows, int key_dim, int val_dim, cudaStream_t stream);
 
 }  // namespace anelm

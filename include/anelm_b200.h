@@ -227,6 +227,29 @@ ANELM_API int anelm_gqa_attention(float* out, const float* q, const void* k_cach
                                   int head_dim, int q_head_stride, int cache_start, int cache_len,
                                   int cache_capacity, void* stream);
 
+/* Allocation-free variant of anelm_gqa_attention for fp16 caches.  No
+ * counterpart in the reference.  For callers that cannot allocate device memory
+ * where attention runs: a server whose own pool already holds all free HBM (a
+ * cudaMalloc / cudaMallocAsync there would fail or fragment it) or a plugin host
+ * that owns the allocator.  anelm_gqa_attention draws its split-K scratch from
+ * the stream-ordered pool on each call; this one uses a fixed device array of
+ * ANELM_GQA_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads
+ * the library holds until the process exits.  It calls no cudaMalloc / cudaFree
+ * and no allocating library routine.  Arguments as anelm_gqa_attention with
+ * kv_dtype = ANELM_F16 implied.  Limit: the scratch holds partial results of
+ * (ANELM_GQA_NOALLOC_SCRATCH_BYTES - 16 KiB) / (n_kv_heads * (4*head_dim + 8) * 4)
+ * splits; longer caches get longer splits, and a configuration whose single
+ * split does not fit is rejected with ANELM_ERR_CAPACITY.  All calls on a device
+ * share the array and it keeps the last call's contents (the call clears what
+ * must start at zero): calls whose executions overlap on the GPU race on it.
+ * The first call on each device looks the array's device address up
+ * (cudaGetSymbolAddress, with that device current); make it before any stream
+ * capture. */
+#define ANELM_GQA_NOALLOC_SCRATCH_BYTES (4u << 20)
+ANELM_API int anelm_gqa_attention_noalloc(float* out, const float* q, const void* k_cache, const void* v_cache,
+                                          int n_heads, int n_kv_heads, int head_dim, int q_head_stride,
+                                          int cache_start, int cache_len, int cache_capacity, void* stream);
+
 /* ssm_step (core/cpu_ops.cpp:131-146): state [key_dim][value_dim] updated in place. */
 ANELM_API int anelm_ssm_step(float* y, float* state, const float* q, const float* k, const float* v,
                              float decay, float beta, int key_dim, int value_dim, void* stream);
