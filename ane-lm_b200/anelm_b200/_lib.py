@@ -78,6 +78,7 @@ SIGNATURES = {
     "anelm_plan_info": [_vp, _ip, _ip],
     "anelm_full_attn_decode": [_vp, _vp, _i, _vp, _i, _vp, _vp, _i, _vp],
     "anelm_deltanet_decode": [_vp, _vp, _i, _vp, _i, _vp, _i, _vp],
+    "anelm_full_attn_prefill": [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _vp],
     "anelm_py_cpu_attention": [_vp, _i, _i, _u16p, _u16p, _u16p, _i, _u16p, _vp],
     "anelm_gqa_attention": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "anelm_gqa_attention_noalloc": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],

@@ -232,6 +232,20 @@ class Context:
               "anelm_full_attn_decode")
         return out
 
+    def full_attn_prefill(self, plan: Plan, layer: int, proj: torch.Tensor, start_pos: int = 0, out=None,
+                          out_dtype=torch.float32):
+        """Causal prefill of fresh rings: proj [B][n][fa_proj_dim] for the plan's B sequences;
+        returns out [B][n][Hq*d].  Leaves each ring holding the n tokens (len n, start 0)."""
+        assert proj.is_cuda and proj.is_contiguous() and proj.dim() == 3 and proj.shape[0] == plan.n
+        assert proj.shape[2] == self.fa_proj_dim
+        n = proj.shape[1]
+        if out is None:
+            out = torch.empty((plan.n, n, self.fa_out_dim), dtype=out_dtype, device=proj.device)
+        check(lib().anelm_full_attn_prefill(self.handle, plan.handle, layer, n, ctypes.c_void_p(proj.data_ptr()),
+                                            _dtype_code(proj), start_pos, ctypes.c_void_p(out.data_ptr()),
+                                            _dtype_code(out), _stream(proj.device)), "anelm_full_attn_prefill")
+        return out
+
     def deltanet_decode(self, plan: Plan, layer: int, proj: torch.Tensor, out=None, out_dtype=torch.float32):
         assert proj.is_cuda and proj.is_contiguous() and proj.shape == (plan.n, self.gdn_proj_dim)
         if out is None:

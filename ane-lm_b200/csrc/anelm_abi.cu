@@ -116,6 +116,9 @@ struct anelm_ctx {
     float* rope_cos = nullptr;
     float* rope_sin = nullptr;
     int* err = nullptr;
+    std::vector<char> fresh;    // [n_fa][max_seqs]: ring known to be empty (prefill may start it)
+    void* prefill_ws = nullptr;  // prefill staging (Q, K, V, V^T), grown on demand
+    size_t prefill_ws_bytes = 0;
     __half* py_proj = nullptr;  // staging for anelm_py_cpu_attention
     __half* py_out = nullptr;
     std::vector<void*> allocs;
@@ -491,6 +494,7 @@ ANELM_API int anelm_create(const anelm_config* cfg, int device, anelm_ctx** out)
         cudaMemcpy(ctx->kv_cap, ctx->cap_h.data(), c.max_seqs * sizeof(int), cudaMemcpyHostToDevice))
         return bail(fail(ANELM_ERR_CUDA, "metadata upload failed"));
     if (ctx->n_fa > 0) {
+        ctx->fresh.assign((size_t)ctx->n_fa * c.max_seqs, 1);
         CALLOC(ctx->kv_len, (size_t)ctx->n_fa * c.max_seqs);
         CALLOC(ctx->kv_start, (size_t)ctx->n_fa * c.max_seqs);
         const size_t row = (size_t)c.num_kv_heads * c.head_dim;
@@ -555,6 +559,7 @@ ANELM_API int anelm_destroy(anelm_ctx* ctx) {
     DeviceGuard dg(ctx->device);
     cudaDeviceSynchronize();
     for (auto& kv : ctx->single) free_plan(kv.second);
+    if (ctx->prefill_ws) cudaFree(ctx->prefill_ws);
     for (void* a : ctx->allocs) cudaFree(a);
     delete ctx;
     return ANELM_OK;
@@ -600,6 +605,7 @@ ANELM_API int anelm_reset(anelm_ctx* ctx, int seq) {
         CUDA_TRY(cudaMemset(ctx->v_pool[f] + a * row, 0, (e - a) * row * 2));
         CUDA_TRY(cudaMemset(ctx->kv_len + (size_t)f * c.max_seqs + s0, 0, (s1 - s0) * 4));
         CUDA_TRY(cudaMemset(ctx->kv_start + (size_t)f * c.max_seqs + s0, 0, (s1 - s0) * 4));
+        for (int s = s0; s < s1; s++) ctx->fresh[(size_t)f * c.max_seqs + s] = 1;
     }
     const size_t st = (size_t)c.lin_num_val_heads * c.lin_key_dim * c.lin_val_dim;
     for (int g = 0; g < ctx->n_gdn; g++) {
@@ -660,6 +666,7 @@ ANELM_API int anelm_kv_import(anelm_ctx* ctx, int layer, int seq, const float* k
     }
     CUDA_TRY(cudaMemcpy(ctx->kv_len + (size_t)f * c.max_seqs + seq, &len, 4, cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(ctx->kv_start + (size_t)f * c.max_seqs + seq, &start, 4, cudaMemcpyHostToDevice));
+    ctx->fresh[(size_t)f * c.max_seqs + seq] = (len == 0);
     return ANELM_OK;
 }
 
@@ -691,6 +698,7 @@ ANELM_API int anelm_kv_set_meta(anelm_ctx* ctx, int layer, int seq, int len, int
     const int f = ctx->fa_idx[layer];
     CUDA_TRY(cudaMemcpy(ctx->kv_len + (size_t)f * ctx->cfg.max_seqs + seq, &len, 4, cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(ctx->kv_start + (size_t)f * ctx->cfg.max_seqs + seq, &start, 4, cudaMemcpyHostToDevice));
+    ctx->fresh[(size_t)f * ctx->cfg.max_seqs + seq] = (len == 0);
     return ANELM_OK;
 }
 
@@ -791,6 +799,7 @@ static int fa_launch(anelm_ctx* ctx, const anelm_plan* plan, int layer, const vo
     if (ctx->cfg.qk_norm_in_core && !ctx->fa_w_set[ctx->fa_idx[layer]])
         return fail(ANELM_ERR_STATE, "full-attention weights of layer %d not set", layer);
     DeviceGuard dg(ctx->device);
+    for (int s : plan->seq_h) ctx->fresh[(size_t)ctx->fa_idx[layer] * ctx->cfg.max_seqs + s] = 0;
     FaDecodeParams p = fa_params(ctx, layer, plan, proj, proj_dtype, pos_arr, pos_scalar, out, out_dtype);
     return launch_status(launch_fa_decode(p, ctx->cfg.head_dim, plan->n_blocks, static_cast<cudaStream_t>(stream)),
                          "fa_decode");
@@ -850,6 +859,80 @@ ANELM_API int anelm_deltanet_from_proj(anelm_ctx* ctx, int layer, int seq, const
 ANELM_API int anelm_deltanet_decode(anelm_ctx* ctx, const anelm_plan* plan, int layer, const void* proj,
                                     int proj_dtype, void* out, int out_dtype, void* stream) {
     return gdn_launch(ctx, plan, layer, proj, proj_dtype, out, out_dtype, stream);
+}
+
+ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,
+                                      const void* proj, int proj_dtype, int start_pos, void* out, int out_dtype,
+                                      void* stream) {
+    if (int rc = check_layer(ctx, layer, ANELM_LAYER_FULL_ATTN)) return rc;
+    if (!plan || plan->ctx != ctx) return fail(ANELM_ERR_INVALID_ARG, "plan belongs to another context");
+    if (!proj || !out || n_tokens <= 0) return fail(ANELM_ERR_INVALID_ARG, "null tensor or no tokens");
+    if (int rc = check_dtype(proj_dtype)) return rc;
+    if (int rc = check_dtype(out_dtype)) return rc;
+    const anelm_config& c = ctx->cfg;
+    if (c.head_dim != 256) return fail(ANELM_ERR_UNSUPPORTED, "prefill kernel is built for head_dim 256");
+    if (c.kv_mode == ANELM_KV_LINEAR && start_pos != 0)
+        return fail(ANELM_ERR_UNSUPPORTED, "linear-cache prefill starts at position 0");
+    if (c.qk_norm_in_core && !ctx->fa_w_set[ctx->fa_idx[layer]])
+        return fail(ANELM_ERR_STATE, "full-attention weights of layer %d not set", layer);
+    const int f = ctx->fa_idx[layer];
+    for (int s : plan->seq_h) {
+        if (!ctx->fresh[(size_t)f * c.max_seqs + s])
+            return fail(ANELM_ERR_STATE, "prefill needs an empty ring (sequence %d, layer %d): reset it first", s, layer);
+        if (n_tokens > ctx->cap_h[s])
+            return fail(ANELM_ERR_CAPACITY, "%d prompt tokens exceed the ring capacity %d of sequence %d", n_tokens,
+                        ctx->cap_h[s], s);
+    }
+    DeviceGuard dg(ctx->device);
+    const size_t need = fa_prefill_workspace_bytes(plan->n, n_tokens, c.num_q_heads, c.num_kv_heads, c.head_dim);
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        if (need > ctx->prefill_ws_bytes) {
+            if (ctx->prefill_ws) cudaFree(ctx->prefill_ws);
+            ctx->prefill_ws = nullptr;
+            ctx->prefill_ws_bytes = 0;
+            cudaError_t e = cudaMalloc(&ctx->prefill_ws, need);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return fail(ANELM_ERR_NOMEM, "prefill workspace of %zu bytes: %s", need, cudaGetErrorString(e));
+            }
+            ctx->prefill_ws_bytes = need;
+        }
+    }
+    FaPrefillParams p{};
+    p.B = plan->n;
+    p.n = n_tokens;
+    p.Hq = c.num_q_heads;
+    p.Hkv = c.num_kv_heads;
+    p.rot_dim = c.rot_dim;
+    p.rope_theta = c.rope_theta;
+    p.rms_eps = c.rms_eps;
+    p.qk_norm = c.qk_norm_in_core;
+    p.rope_mode = c.rope_mode;
+    p.gate = c.attn_output_gate;
+    p.start_pos = start_pos;
+    p.q_norm = ctx->q_norm[f];
+    p.k_norm = ctx->k_norm[f];
+    p.rope_cos = ctx->rope_cos;
+    p.rope_sin = ctx->rope_sin;
+    p.rope_len = c.rope_table_len;
+    p.proj = proj;
+    p.proj_dtype = proj_dtype;
+    p.proj_stride = ctx->fa_proj;
+    p.k_pool = ctx->k_pool[f];
+    p.v_pool = ctx->v_pool[f];
+    p.kv_base = ctx->kv_base;
+    p.seq_ids = plan->seq_d;
+    p.kv_len = ctx->kv_len + (size_t)f * c.max_seqs;
+    p.kv_start = ctx->kv_start + (size_t)f * c.max_seqs;
+    p.out = out;
+    p.out_dtype = out_dtype;
+    p.out_stride = (long long)c.num_q_heads * c.head_dim;
+    p.err = ctx->err;
+    const int rc = launch_fa_prefill(p, ctx->prefill_ws, c.head_dim, static_cast<cudaStream_t>(stream));
+    if (rc) return launch_status(rc, "fa_prefill");
+    for (int s : plan->seq_h) ctx->fresh[(size_t)f * c.max_seqs + s] = 0;
+    return ANELM_OK;
 }
 
 ANELM_API int anelm_py_cpu_attention(anelm_ctx* ctx, int layer, int seq, const uint16_t* q_gate, const uint16_t* k,

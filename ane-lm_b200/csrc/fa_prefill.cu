@@ -1,0 +1,435 @@
+// Causal prefill for the Qwen3.5 gated full-attention core (sm_100a, tcgen05 + TMA).
+//
+// Replaces the per-token prefill loop of the reference (qwen3_5.cpp:1205-1217,
+// serve_hybrid.py:368-370), which runs forward_full_attn_from_proj
+// (qwen3_5.cpp:944-1002) once per prompt token: for each token t, QK RMSNorm,
+// RoPE at position start_pos + t, ring append at slot t, softmax attention over
+// tokens [0, t], sigmoid gate.  The result is the same set of outputs, computed
+// as one causal attention.
+//
+// Three launches:
+//   fa_prefill_prep_kernel  per token: RMSNorm + RoPE of the q heads and k heads
+//                           (same arithmetic as the decode prologue), fp16
+//                           Q [B][Hq][n_pad][D], K [B][Hkv][n_pad][D] and V, and
+//                           the ring append (slot t, len = n, start = 0);
+//   transpose_v_kernel      V -> V^T [B][Hkv][D][n_pad] so both MMA operands of
+//                           P V are K-major;
+//   fa_prefill_kernel       one CTA per (128-row query tile, q head, sequence):
+//     warp 4  TMA producer: Q tile once, K / V^T tiles of 64 keys into a 2-stage
+//             ring of 128B-swizzled shared-memory buffers;
+//     warp 5  MMA issuer (one thread): S = Q K^T  (M=128, N=64, K=256) into one of
+//             two TMEM S buffers, O += P V^T (M=128, N=256, K=64) into TMEM;
+//     warps 0-3  softmax, one query row per thread: tcgen05.ld of its S row,
+//             causal mask, running max with lazy rescaling of O (only when the max
+//             grows by more than 2^8), P (fp16) into swizzled shared memory; at the
+//             end O / l, the sigmoid gate, and the store.
+//   All MMAs are kind::f16 (fp16 operands, fp32 accumulation in TMEM).  Every
+//   mbarrier wait is bounded and records ANELM_ERR_TIMEOUT instead of hanging.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc100.cuh"
+
+namespace anelm {
+
+namespace {
+
+constexpr int kBM = 128;   // query rows per CTA
+constexpr int kBN = 64;    // keys per tile
+constexpr int kD = 256;    // head dim of this kernel
+constexpr int kQBytes = kBM * kD * 2;        // 64 KB (4 boxes of 128 x 64)
+constexpr int kKBytes = kBN * kD * 2;        // 32 KB (4 boxes of 64 x 64)
+constexpr int kVBytes = kD * kBN * 2;        // 32 KB (1 box of 256 x 64, V^T)
+constexpr int kPBytes = kBM * kBN * 2;       // 16 KB
+constexpr int kSmemTiles = kQBytes + 2 * kKBytes + 2 * kVBytes + kPBytes;
+constexpr int kSmemBytes = kSmemTiles + 256 + 1024;  // barriers + alignment slack
+constexpr uint32_t kTmemCols = 512;          // S0 [0,64), S1 [64,128), O [128,384)
+
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, S_EMPTY = 11, P_FULL = 13,
+           PV_DONE = 14, N_BARS = 15 };
+
+__device__ __forceinline__ void rope_cs_pf(const FaPrefillParams& p, int pos, int j, float& c, float& s) {
+    const int half = p.rot_dim >> 1;
+    if (pos >= 0 && pos < p.rope_len && p.rope_cos) {
+        c = p.rope_cos[(long long)pos * half + j];
+        s = p.rope_sin[(long long)pos * half + j];
+    } else {  // core/cpu_ops.cpp:51-56
+        const float freq = 1.0f / powf(p.rope_theta, (float)(2 * j) / (float)p.rot_dim);
+        const float angle = (float)pos * freq;
+        c = cosf(angle);
+        s = sinf(angle);
+    }
+}
+
+// One token of one sequence per CTA (256 threads).
+__global__ void __launch_bounds__(256) fa_prefill_prep_kernel(const FaPrefillParams p) {
+    extern __shared__ float xs[];  // [(Hq + Hkv) vectors][kD], then v [Hkv][kD]
+    const int t = blockIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int Hq = p.Hq, Hkv = p.Hkv;
+    const int nvec = Hq + Hkv;
+    const long long qrow = ((long long)b * Hq) * p.n_pad + t;
+    const long long krow = ((long long)b * Hkv) * p.n_pad + t;
+    if (t >= p.n) {  // padding rows: finite zeros
+        for (int idx = tid; idx < Hq * kD; idx += 256)
+            p.Qh[(qrow + (long long)(idx / kD) * p.n_pad) * kD + idx % kD] = __float2half_rn(0.f);
+        for (int idx = tid; idx < Hkv * kD; idx += 256) {
+            const long long o = (krow + (long long)(idx / kD) * p.n_pad) * kD + idx % kD;
+            p.Kh[o] = __float2half_rn(0.f);
+            p.Vh[o] = __float2half_rn(0.f);
+        }
+        return;
+    }
+    const char* row = reinterpret_cast<const char*>(p.proj) +
+                      ((long long)b * p.n + t) * p.proj_stride * dtype_bytes(p.proj_dtype);
+    float* vs = xs + nvec * kD;
+    for (int idx = tid; idx < nvec * kD; idx += 256) {
+        const int v = idx / kD, i = idx % kD;
+        const long long off = v < Hq ? (long long)v * 2 * kD + i : (long long)Hq * 2 * kD + (long long)(v - Hq) * kD + i;
+        xs[idx] = load_as_float(row, p.proj_dtype, off);
+    }
+    for (int idx = tid; idx < Hkv * kD; idx += 256)
+        vs[idx] = load_as_float(row, p.proj_dtype, (long long)Hq * 2 * kD + (long long)Hkv * kD + idx);
+    __syncthreads();
+    if (p.qk_norm) {  // rmsnorm, cpu_ops.cpp:24-30 (qwen3_5.cpp:952-959)
+        for (int v = warp; v < nvec; v += 8) {
+            float* x = xs + v * kD;
+            const float* w = v < Hq ? p.q_norm : p.k_norm;
+            float ss = 0.f;
+            for (int i = lane; i < kD; i += 32) ss += x[i] * x[i];
+            ss = warp_sum(ss);
+            const float r = 1.0f / sqrtf(ss / (float)kD + p.rms_eps);
+            for (int i = lane; i < kD; i += 32) x[i] = __fmul_rn(__fmul_rn(x[i], r), w[i]);
+        }
+        __syncthreads();
+    }
+    const int pos = p.start_pos + t;
+    if (p.rot_dim > 0) {  // apply_rope_cached, cpu_ops.cpp:40-63 (or rotate-half)
+        const int half = p.rot_dim >> 1;
+        for (int idx = tid; idx < nvec * half; idx += 256) {
+            const int v = idx / half, j = idx % half;
+            float* x = xs + v * kD;
+            float c, s;
+            rope_cs_pf(p, pos, j, c, s);
+            const int i0 = p.rope_mode == ANELM_ROPE_INTERLEAVED ? 2 * j : j;
+            const int i1 = p.rope_mode == ANELM_ROPE_INTERLEAVED ? 2 * j + 1 : j + half;
+            const float v0 = x[i0], v1 = x[i1];
+            x[i0] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+            x[i1] = p.rope_mode == ANELM_ROPE_INTERLEAVED ? __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c))
+                                                          : __fadd_rn(__fmul_rn(v1, c), __fmul_rn(v0, s));
+        }
+        __syncthreads();
+    }
+    const int seq = p.seq_ids ? p.seq_ids[b] : 0;
+    const long long slot_row = p.kv_base ? (p.kv_base[seq] + t) * Hkv : 0;
+    for (int idx = tid; idx < Hq * kD; idx += 256)
+        p.Qh[(qrow + (long long)(idx / kD) * p.n_pad) * kD + idx % kD] = __float2half_rn(xs[idx]);
+    for (int idx = tid; idx < Hkv * kD; idx += 256) {
+        const int v = idx / kD, i = idx % kD;
+        const __half kh = __float2half_rn(xs[(Hq + v) * kD + i]);
+        const __half vh = __float2half_rn(vs[idx]);
+        const long long o = (krow + (long long)v * p.n_pad) * kD + i;
+        p.Kh[o] = kh;
+        p.Vh[o] = vh;
+        if (p.k_pool) {  // ring append at slot t (qwen3_5.cpp:984-986)
+            p.k_pool[(slot_row + v) * kD + i] = kh;
+            p.v_pool[(slot_row + v) * kD + i] = vh;
+        }
+    }
+    if (t == 0 && tid == 0 && p.kv_len) {
+        p.kv_len[seq] = p.n;
+        p.kv_start[seq] = 0;
+    }
+}
+
+// V [BH][n_pad][kD] -> V^T [BH][kD][n_pad], 32 x 32 tiles.
+__global__ void transpose_v_kernel(const __half* __restrict__ v, __half* __restrict__ vt, int n_pad) {
+    __shared__ __half tile[32][33];
+    const int bh = blockIdx.z;
+    const int t0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+    const __half* src = v + (long long)bh * n_pad * kD;
+    __half* dst = vt + (long long)bh * kD * n_pad;
+    for (int r = threadIdx.y; r < 32; r += 8) tile[r][threadIdx.x] = src[(long long)(t0 + r) * kD + d0 + threadIdx.x];
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += 8) dst[(long long)(d0 + r) * n_pad + t0 + threadIdx.x] = tile[threadIdx.x][r];
+}
+
+__global__ void __launch_bounds__(192, 1)
+    fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const FaPrefillParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + kQBytes;
+    uint8_t* sV = sK + 2 * kKBytes;
+    uint8_t* sP = sV + 2 * kVBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n_qt = p.n_pad / kBM;
+    const int qt = n_qt - 1 - (int)blockIdx.x;  // longest (causal) tiles first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int G = p.Hq / p.Hkv;
+    const int kvh = h / G;
+    const int q0 = qt * kBM;
+    const int kv_end = min(q0 + kBM, p.n);
+    const int nT = (kv_end + kBN - 1) / kBN;
+
+    if (tid == 0) {
+        *abort = 0;
+        tc::mbar_init(&bars[Q_FULL], 1);
+        for (int s = 0; s < 2; s++) {
+            tc::mbar_init(&bars[K_FULL + s], 1);
+            tc::mbar_init(&bars[K_EMPTY + s], 1);
+            tc::mbar_init(&bars[V_FULL + s], 1);
+            tc::mbar_init(&bars[V_EMPTY + s], 1);
+            tc::mbar_init(&bars[S_FULL + s], 1);
+            tc::mbar_init(&bars[S_EMPTY + s], kBM);
+        }
+        tc::mbar_init(&bars[P_FULL], kBM);
+        tc::mbar_init(&bars[PV_DONE], 1);
+        tc::fence_barrier_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0 && nT > 0) {
+            tc::prefetch_tmap(&tmQ);
+            tc::prefetch_tmap(&tmK);
+            tc::prefetch_tmap(&tmV);
+            const int qrow0 = (b * p.Hq + h) * p.n_pad + q0;
+            const int krow0 = (b * p.Hkv + kvh) * p.n_pad;
+            const int vrow0 = (b * p.Hkv + kvh) * kD;
+            tc::mbar_arrive_expect_tx(&bars[Q_FULL], kQBytes);
+            for (int kb = 0; kb < 4; kb++) tc::tma_load_2d(sQ + kb * (kBM * 128), &tmQ, &bars[Q_FULL], kb * 64, qrow0);
+            for (int j = 0; j < nT; j++) {
+                const int s = j & 1, u = j >> 1;
+                if (j >= 2) tc::mbar_wait(&bars[K_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                tc::mbar_arrive_expect_tx(&bars[K_FULL + s], kKBytes);
+                for (int kb = 0; kb < 4; kb++)
+                    tc::tma_load_2d(sK + s * kKBytes + kb * (kBN * 128), &tmK, &bars[K_FULL + s], kb * 64,
+                                    krow0 + j * kBN);
+                if (j >= 2) tc::mbar_wait(&bars[V_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                tc::mbar_arrive_expect_tx(&bars[V_FULL + s], kVBytes);
+                tc::tma_load_2d(sV + s * kVBytes, &tmV, &bars[V_FULL + s], j * kBN, vrow0);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0 && nT > 0) {
+            constexpr uint32_t id_qk = tc::idesc_f16_f32(kBM, kBN);
+            constexpr uint32_t id_pv = tc::idesc_f16_f32(kBM, kD);
+            const uint32_t aQ = (uint32_t)__cvta_generic_to_shared(sQ);
+            const uint32_t aK = (uint32_t)__cvta_generic_to_shared(sK);
+            const uint32_t aV = (uint32_t)__cvta_generic_to_shared(sV);
+            const uint32_t aP = (uint32_t)__cvta_generic_to_shared(sP);
+            tc::mbar_wait(&bars[Q_FULL], 0, p.err, ANELM_ERR_TIMEOUT, abort);
+            auto qk = [&](int j) {
+                const int s = j & 1, u = j >> 1;
+                tc::mbar_wait(&bars[K_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                if (j >= 2) tc::mbar_wait(&bars[S_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                tc::tc_fence_after();
+#pragma unroll
+                for (int kb = 0; kb < 4; kb++)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ks++)
+                        tc::mma_f16_ss(tmem + s * kBN, tc::desc_kmajor_sw128(aQ + kb * (kBM * 128) + ks * 32),
+                                       tc::desc_kmajor_sw128(aK + s * kKBytes + kb * (kBN * 128) + ks * 32), id_qk,
+                                       (kb | ks) != 0);
+                tc::mma_commit(&bars[S_FULL + s]);
+                tc::mma_commit(&bars[K_EMPTY + s]);
+            };
+            auto pv = [&](int j) {
+                const int s = j & 1, u = j >> 1;
+                tc::mbar_wait(&bars[P_FULL], j & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                tc::mbar_wait(&bars[V_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                tc::tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < 4; ks++)
+                    tc::mma_f16_ss(tmem + 2 * kBN, tc::desc_kmajor_sw128(aP + ks * 32),
+                                   tc::desc_kmajor_sw128(aV + s * kVBytes + ks * 32), id_pv, (j > 0) || (ks > 0));
+                tc::mma_commit(&bars[PV_DONE]);
+                tc::mma_commit(&bars[V_EMPTY + s]);
+            };
+            qk(0);
+            for (int j = 0; j < nT; j++) {
+                if (j + 1 < nT) qk(j + 1);
+                pv(j);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- softmax: thread r owns query row q0 + r ----------------
+        const int r = tid;  // 0..127 == TMEM lane
+        const int qpos = q0 + r;
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        const float sl2 = 1.4426950408889634f / sqrtf((float)kD);
+        float m_used = -INFINITY, l = 0.f;
+        float x[64];
+        for (int j = 0; j < nT; j++) {
+            const int s = j & 1, u = j >> 1;
+            tc::mbar_wait(&bars[S_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+            tc::tc_fence_after();
+            tc::tmem_ld64(trow + s * kBN, x);
+            tc::tmem_ld_wait();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bars[S_EMPTY + s]);
+            const int k0 = j * kBN;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 64; c++) {
+                const int kv = k0 + c;
+                x[c] = (kv <= qpos && kv < p.n) ? x[c] * sl2 : -INFINITY;
+                mx = fmaxf(mx, x[c]);
+            }
+            const float m_new = fmaxf(m_used, mx);
+            const bool grow = (m_used == -INFINITY) || (m_new > m_used + 8.0f);
+            if (j > 0) {
+                // O and the P buffer are free once P V of the previous tile completed
+                tc::mbar_wait(&bars[PV_DONE], (j - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                tc::tc_fence_after();
+                if (__any_sync(0xffffffffu, grow)) {
+                    const float alpha = grow ? exp2f(m_used - m_new) : 1.0f;
+                    float o[64];
+#pragma unroll
+                    for (int ch = 0; ch < 4; ch++) {
+                        tc::tmem_ld64(trow + 2 * kBN + ch * 64, o);
+                        tc::tmem_ld_wait();
+#pragma unroll
+                        for (int c = 0; c < 64; c++) o[c] *= alpha;
+                        tc::tmem_st64(trow + 2 * kBN + ch * 64, o);
+                    }
+                    tc::tmem_st_wait();
+                    l *= alpha;
+                }
+            }
+            if (grow) m_used = m_new;
+            // P row (fp16) into the 128B-swizzled K-major tile: chunk c of row r at (c ^ (r & 7))
+            float sum = 0.f;
+            uint8_t* prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+            for (int ch = 0; ch < 8; ch++) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const __half lo = __float2half_rn(exp2f(x[ch * 8 + 2 * e] - m_used));
+                    const __half hi = __float2half_rn(exp2f(x[ch * 8 + 2 * e + 1] - m_used));
+                    sum += __half2float(lo) + __half2float(hi);
+                    w[e] = pack_half2(lo, hi);
+                }
+                *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            l += sum;
+            tc::fence_proxy_async_smem();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bars[P_FULL]);
+        }
+        // ---------------- epilogue ----------------
+        if (nT > 0) {
+            tc::mbar_wait(&bars[PV_DONE], (nT - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+            tc::tc_fence_after();
+            const float inv = (l > 0.f) ? 1.0f / l : 0.f;
+            const bool valid = qpos < p.n;
+            const char* prow = reinterpret_cast<const char*>(p.proj) +
+                               ((long long)b * p.n + (valid ? qpos : 0)) * p.proj_stride * dtype_bytes(p.proj_dtype);
+            const long long orow = ((long long)b * p.n + qpos) * p.out_stride + (long long)h * kD;
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ch++) {
+                float o[64];
+                tc::tmem_ld64(trow + 2 * kBN + ch * 64, o);
+                tc::tmem_ld_wait();
+                if (valid) {
+#pragma unroll
+                    for (int c = 0; c < 64; c++) {
+                        float v = o[c] * inv;
+                        if (p.gate) {  // mul_sigmoid_inplace, cpu_ops.cpp:15-22
+                            const float z = load_as_float(prow, p.proj_dtype, (long long)h * 2 * kD + kD + ch * 64 + c);
+                            v = v / (1.0f + expf(-z));
+                        }
+                        store_from_float(p.out, p.out_dtype, orow + ch * 64 + c, v);
+                    }
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
+
+// 2D fp16 tensor map, inner dimension `cols` (contiguous), 128B swizzle, box {64, box_rows}.
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t fa_prefill_workspace_bytes(int B, int n, int Hq, int Hkv, int head_dim) {
+    const long long n_pad = (n + kBM - 1) / kBM * kBM;
+    return (size_t)B * n_pad * head_dim * 2 * (Hq + 3 * (size_t)Hkv);
+}
+
+int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream) {
+    if (head_dim != kD) return ANELM_ERR_UNSUPPORTED;
+    p.n_pad = (p.n + kBM - 1) / kBM * kBM;
+    const long long nq = (long long)p.B * p.Hq * p.n_pad * kD, nk = (long long)p.B * p.Hkv * p.n_pad * kD;
+    __half* ws = static_cast<__half*>(workspace);
+    p.Qh = ws;
+    p.Kh = ws + nq;
+    p.Vh = p.Kh + nk;
+    p.Vt = p.Vh + nk;
+    CUtensorMap mQ, mK, mV;
+    if (!make_map(&mQ, p.Qh, (uint64_t)p.B * p.Hq * p.n_pad, kD, kBM) ||
+        !make_map(&mK, p.Kh, (uint64_t)p.B * p.Hkv * p.n_pad, kD, kBN) ||
+        !make_map(&mV, p.Vt, (uint64_t)p.B * p.Hkv * kD, p.n_pad, kD))
+        return ANELM_ERR_CUDA;
+    const size_t prep_smem = (size_t)(p.Hq + 2 * p.Hkv) * kD * sizeof(float);
+    if (prep_smem > 48 * 1024)
+        cudaFuncSetAttribute(fa_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
+    fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
+    transpose_v_kernel<<<dim3(p.n_pad / 32, kD / 32, p.B * p.Hkv), dim3(32, 8), 0, stream>>>(p.Vh, p.Vt, p.n_pad);
+    cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), 192, kSmemBytes, stream>>>(mQ, mK, mV, p);
+    return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
+}
+
+}  // namespace anelm

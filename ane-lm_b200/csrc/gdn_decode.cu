@@ -22,7 +22,9 @@
 // its W columns).  So the reference's own ring layout [C][K-1] is updated in
 // place without races, and the ring position is kept per (sequence, key head):
 // every CTA of the cluster reads it before the first cluster barrier and rank 0
-// advances it after that barrier.  No atomics, no memory fences.
+// advances it after the last one.  No atomics, no memory fences.  All global
+// stores (state write-back, ring inputs, position) come after the last cluster
+// barrier, whose release would otherwise wait for them to be acknowledged.
 //
 // Exchanges (distributed shared memory, push style).  Each CTA convolves its
 // slice of the q/k channels and stores the SiLU outputs straight into every
@@ -68,7 +70,7 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
     __shared__ __align__(16) float z_s[W];
     __shared__ __align__(16) float y_s[W];
     __shared__ __align__(16) float w_s[W];
-    __shared__ __align__(16) float red[NW][W];
+    __shared__ __align__(16) float red[2][NW][W];
     __shared__ float ss_s[NSPLIT];
     __shared__ float scal[4];
 
@@ -104,32 +106,41 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
     if (p2 == 3) p2 = 0;
     float* ring = p.conv + (long long)seq * C * 3;
 
-    // conv1d_update (cpu_ops.cpp:95-110) + SiLU (cpu_ops.cpp:6-13) of one channel; stores x in the ring
-    auto conv_ch = [&](int c) -> float {
+    // conv1d_update (cpu_ops.cpp:95-110) + SiLU (cpu_ops.cpp:6-13) of one channel.  The new input x
+    // goes into ring slot n only after the last cluster barrier (a barrier's release would
+    // otherwise wait for that global store to be acknowledged).
+    auto conv_ch = [&](int c, float& x) -> float {
         const float4 w = *reinterpret_cast<const float4*>(p.conv_w + (long long)c * 4);
         const float s0 = ring[c * 3 + n], s1 = ring[c * 3 + p1], s2 = ring[c * 3 + p2];
-        const float x = load_as_float(proj_row, p.proj_dtype, c);
+        x = load_as_float(proj_row, p.proj_dtype, c);
         const float y = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(s0, w.x), __fmul_rn(s1, w.y)), __fmul_rn(s2, w.z)),
                                   __fmul_rn(x, w.w));
-        ring[c * 3 + n] = x;
         return y / (1.0f + expf(-y));
     };
 
     // ---- 2. this CTA's v / z columns and its slice of the q/k channels ----
-    for (int i = tid; i < W; i += THREADS) {
-        v_s[i] = conv_ch(2 * key_total + h * kDv + j0 + i);
-        z_s[i] = load_as_float(proj_row, p.proj_dtype, C + (long long)h * kDv + j0 + i);
-        w_s[i] = p.norm_w[j0 + i];
+    constexpr int NV = (W + THREADS - 1) / THREADS;
+    float xv[NV], xqk[NU];
+#pragma unroll
+    for (int u = 0; u < NV; u++) {
+        const int i = tid + u * THREADS;
+        xv[u] = 0.f;
+        if (i < W) {
+            v_s[i] = conv_ch(2 * key_total + h * kDv + j0 + i, xv[u]);
+            z_s[i] = load_as_float(proj_row, p.proj_dtype, C + (long long)h * kDv + j0 + i);
+            w_s[i] = p.norm_w[j0 + i];
+        }
     }
     float qk_mine[NU];
 #pragma unroll
     for (int u = 0; u < NU; u++) {
         const int i = tid + u * THREADS;
         qk_mine[u] = 0.f;
+        xqk[u] = 0.f;
         if (i < QKP) {
             const int ci = rank * QKP + i;  // 0..255 within (q | k) of key head kh
             const int c = (ci < kDk) ? kh * kDk + ci : key_total + kh * kDk + (ci - kDk);
-            qk_mine[u] = conv_ch(c);
+            qk_mine[u] = conv_ch(c, xqk[u]);
         }
     }
     if (tid == 0) {
@@ -148,7 +159,6 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
         }
     }
     cluster.sync();  // q/k published; every CTA has read the ring position
-    if (rank == 0 && tid == 0) *pos_ptr = p1;  // cpu_ops.cpp:126-128
 
     // ---- 3. L2-normalise q and k (cpu_ops.cpp:82-87), q *= 1/sqrt(dk) (qwen3_5.cpp:879-887) ----
     if (warp < 2) {
@@ -168,7 +178,8 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
     const float beta = scal[0], decay = scal[1];
 
     // column sums over the 128 key rows: shuffles across row groups, then across warps
-    auto colsum = [&](float4 v) -> float4 {
+    // (each of the two uses has its own buffer, so one barrier per reduction suffices)
+    auto colsum = [&](float4 v, int buf) -> float4 {
 #pragma unroll
         for (int o = QPR; o < 32; o <<= 1) {
             v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
@@ -176,15 +187,14 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
             v.z += __shfl_xor_sync(0xffffffffu, v.z, o);
             v.w += __shfl_xor_sync(0xffffffffu, v.w, o);
         }
-        if (lane < QPR) *reinterpret_cast<float4*>(&red[warp][4 * lane]) = v;
+        if (lane < QPR) *reinterpret_cast<float4*>(&red[buf][warp][4 * lane]) = v;
         __syncthreads();
-        float4 t = *reinterpret_cast<const float4*>(&red[0][4 * cq]);
+        float4 t = *reinterpret_cast<const float4*>(&red[buf][0][4 * cq]);
 #pragma unroll
         for (int w = 1; w < NW; w++) {
-            const float4 u = *reinterpret_cast<const float4*>(&red[w][4 * cq]);
+            const float4 u = *reinterpret_cast<const float4*>(&red[buf][w][4 * cq]);
             t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
         }
-        __syncthreads();
         return t;
     };
 
@@ -199,7 +209,7 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
             const float kr = k_s[rg + RPP * i];
             sk.x += S[i].x * kr; sk.y += S[i].y * kr; sk.z += S[i].z * kr; sk.w += S[i].w * kr;
         }
-        sk = colsum(sk);
+        sk = colsum(sk, 0);
         const float4 d = make_float4(v_s[4 * cq] - sk.x, v_s[4 * cq + 1] - sk.y, v_s[4 * cq + 2] - sk.z,
                                      v_s[4 * cq + 3] - sk.w);
 #pragma unroll
@@ -219,7 +229,7 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
             const float kr = k_s[rg + RPP * i];
             sk.x += S[i].x * kr; sk.y += S[i].y * kr; sk.z += S[i].z * kr; sk.w += S[i].w * kr;
         }
-        sk = colsum(sk);
+        sk = colsum(sk, 0);
         const float4 d = make_float4((v_s[4 * cq] - sk.x) * beta, (v_s[4 * cq + 1] - sk.y) * beta,
                                      (v_s[4 * cq + 2] - sk.z) * beta, (v_s[4 * cq + 3] - sk.w) * beta);
 #pragma unroll
@@ -231,15 +241,14 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
             S[i].w = __fadd_rn(S[i].w, __fmul_rn(kr, d.w));
         }
     }
-    // y = S^T q (cpu_ops.cpp:144-145); S written back
+    // y = S^T q (cpu_ops.cpp:144-145)
     float4 yv = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < NR; i++) {
         const float qr = q_s[rg + RPP * i];
         yv.x += S[i].x * qr; yv.y += S[i].y * qr; yv.z += S[i].z * qr; yv.w += S[i].w * qr;
-        __stcs(reinterpret_cast<float4*>(Sbase + (long long)(rg + RPP * i) * kDv), S[i]);
     }
-    yv = colsum(yv);
+    yv = colsum(yv, 1);
     if (rg == 0) *reinterpret_cast<float4*>(&y_s[4 * cq]) = yv;
     __syncthreads();
 
@@ -251,6 +260,24 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
         if (lane < NSPLIT) *cluster.map_shared_rank(&ss_s[cb], hl * NSPLIT + lane) = ss;
     }
     cluster.sync();  // partial sums published; no DSMEM access after this point
+    // global stores only now: the state block, and the new inputs into ring slot n (cpu_ops.cpp:109)
+#pragma unroll
+    for (int i = 0; i < NR; i++) __stcs(reinterpret_cast<float4*>(Sbase + (long long)(rg + RPP * i) * kDv), S[i]);
+#pragma unroll
+    for (int u = 0; u < NV; u++) {
+        const int i = tid + u * THREADS;
+        if (i < W) ring[(2 * key_total + h * kDv + j0 + i) * 3 + n] = xv[u];
+    }
+#pragma unroll
+    for (int u = 0; u < NU; u++) {
+        const int i = tid + u * THREADS;
+        if (i < QKP) {
+            const int ci = rank * QKP + i;
+            const int c = (ci < kDk) ? kh * kDk + ci : key_total + kh * kDk + (ci - kDk);
+            ring[c * 3 + n] = xqk[u];
+        }
+    }
+    if (rank == 0 && tid == 0) *pos_ptr = p1;  // cpu_ops.cpp:126-128
     float tot = 0.f;
 #pragma unroll
     for (int q = 0; q < NSPLIT; q++) tot += ss_s[q];

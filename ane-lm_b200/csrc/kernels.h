@@ -76,6 +76,38 @@ struct GdnDecodeParams {
     long long out_stride;
 };
 
+// Causal prefill of a fresh ring: B sequences of n tokens each.
+struct FaPrefillParams {
+    int B, n, n_pad, Hq, Hkv, rot_dim;
+    float rope_theta, rms_eps;
+    int qk_norm, rope_mode, gate, start_pos;
+    const float* q_norm;
+    const float* k_norm;
+    const float* rope_cos;
+    const float* rope_sin;
+    int rope_len;
+    const void* proj;      // [B][n][proj_stride] elements of proj_dtype
+    int proj_dtype;
+    long long proj_stride;
+    __half* Qh;            // [B][Hq][n_pad][D]   (workspace)
+    __half* Kh;            // [B][Hkv][n_pad][D]
+    __half* Vh;            // [B][Hkv][n_pad][D]
+    __half* Vt;            // [B][Hkv][D][n_pad]
+    __half* k_pool;        // ring pools of the layer (nullptr: no append)
+    __half* v_pool;
+    const long long* kv_base;
+    const int* seq_ids;    // [B]
+    int* kv_len;
+    int* kv_start;
+    void* out;             // [B][n][out_stride]
+    int out_dtype;
+    long long out_stride;
+    int* err;
+};
+
+size_t fa_prefill_workspace_bytes(int B, int n, int Hq, int Hkv, int head_dim);
+int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream);
+
 int launch_fa_decode(const FaDecodeParams& p, int head_dim, int n_blocks, cudaStream_t stream);
 size_t fa_decode_smem_bytes(int head_dim);
 // Largest split count one row may use: the merge keeps [splits][4] weights in the tile buffers.

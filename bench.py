@@ -12,6 +12,7 @@ each rank owns its own 256 sequences (weak scaling, no data-path collective).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
     python bench.py --workload fa_b1|gdn_b1      # BASELINE configs 1 / 2 (single sequence)
+    python bench.py --workload fa_prefill [--prefill-batch 8]
 
 The reference arm (--impl reference) times the reference's own CPU attention
 core (core/cpu_ops.cpp compiled unmodified + the qwen3_5.cpp glue, oracle/_ref)
@@ -198,6 +199,8 @@ def run_gpu(args):
     device = torch.device("cuda", local)
     hbm_peak, peak_kind = peaks()
 
+    if args.workload == "fa_prefill":
+        return run_prefill(args, torch, device)
     if args.workload != "serve":
         return run_gpu_single(args, torch, device, hbm_peak, peak_kind)
 
@@ -365,6 +368,62 @@ def run_e2e(args, torch, ctx, plan, projs, outs, pos, device, world):
     return {"value": round(n * world / dt, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "steps": n_steps,
             "note": "host pinned projections in / outputs out each step, timed on the host clock"}
+
+
+def run_prefill(args, torch, device):
+    """causal full-attention prefill, Qwen3.5-4B shape, 4096 tokens, bf16 inputs."""
+    import anelm_b200 as ab
+    from anelm_b200.core import Context
+
+    try:
+        peak = float(json.load(open(PEAKS))["bf16_tflops"])
+        peak_kind = "measured"
+    except Exception:
+        peak, peak_kind = 1590.0, "fallback"
+    rng = np.random.default_rng(0)
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    B, n = args.prefill_batch, args.prefill_len
+    ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_FULL_ATTN], num_q_heads=HQ, num_kv_heads=HKV,
+                  head_dim=HD, rot_dim=ROT, rope_theta=1e7, max_seqs=B, kv_capacity=n)
+    ctx.set_full_attn_weights(0, (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32),
+                              (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32))
+    plan = ctx.plan(list(range(B)))
+    proj = torch.randn(B, n, FA_PROJ, generator=g, device=device).to(torch.bfloat16)
+    out = torch.empty(B, n, FA_OUT, device=device, dtype=torch.bfloat16)
+
+    def call():
+        ctx.reset(-1)
+        ctx.full_attn_prefill(plan, 0, proj, 0, out)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(device)
+    times = []
+    for _ in range(args.steps):
+        ctx.reset(-1)  # synchronous; outside the timed region
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        ctx.full_attn_prefill(plan, 0, proj, 0, out)
+        t1.record()
+        torch.cuda.synchronize(device)
+        times.append(t0.elapsed_time(t1))
+    ms = statistics.median(times)
+    flops = 4.0 * n * n * HD * HQ / 2 * B  # causal: half of the S x S score / PV work
+    tf = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "causal prefill attention TFLOP/s (cfg3, Qwen3.5-4B shape)", "value": round(tf, 1),
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": f"BASELINE cfg3 prefill B={B} S={n}", "Hq": HQ, "Hkv": HKV, "head_dim": HD,
+                   "proj": "bf16 N(0,1)", "timed": "whole call: prep (norm, RoPE, ring append) + V^T + attention"},
+        "roofline": {"bound": "tensor", "kernel": "fa_prefill_kernel", "achieved": round(tf, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(tf / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_flops_per_launch": flops},
+        "gpu_launches": 3 * args.steps}), flush=True)
+    plan.close()
+    ctx.close()
 
 
 def run_gpu_single(args, torch, device, hbm_peak, peak_kind):
@@ -547,7 +606,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="anelm", choices=["anelm", "reference"])
-    ap.add_argument("--workload", default="serve", choices=["serve", "fa_b1", "gdn_b1"])
+    ap.add_argument("--workload", default="serve", choices=["serve", "fa_b1", "gdn_b1", "fa_prefill"])
+    ap.add_argument("--prefill-batch", type=int, default=1)
+    ap.add_argument("--prefill-len", type=int, default=4096)
     ap.add_argument("--seqs", type=int, default=256)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

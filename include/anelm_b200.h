@@ -205,6 +205,22 @@ ANELM_API int anelm_deltanet_decode(anelm_ctx* ctx, const anelm_plan* plan, int 
                                     const void* proj, int proj_dtype, void* out, int out_dtype,
                                     void* stream);
 
+/* ---- prefill ---- */
+
+/* Causal prefill of the plan's sequences, each of n_tokens prompt tokens, into
+ * EMPTY rings (fresh context or after anelm_reset).  Equivalent to n_tokens
+ * successive forward_full_attn_from_proj calls at positions start_pos,
+ * start_pos+1, ... (the per-token loop of qwen3_5.cpp:1205-1217 /
+ * serve_hybrid.py:368-370), computed as one causal attention on the tcgen05
+ * tensor cores.  proj: [n_seqs][n_tokens][proj_dim] of proj_dtype; out:
+ * [n_seqs][n_tokens][Hq*d].  Afterwards each ring holds the n_tokens keys and
+ * values (len = n_tokens, start = 0) and decode continues from there.
+ * head_dim 256 only; n_tokens <= each ring's capacity.  Uses a context-owned
+ * staging buffer: prefill calls on one context must not overlap on the GPU. */
+ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,
+                                      const void* proj, int proj_dtype, int start_pos, void* out, int out_dtype,
+                                      void* stream);
+
 /* ---- Python route: scripts/serve_hybrid.py cpu_attention ---- */
 
 /* Drop-in for cpu_attention(q_gate_fp16, k_fp16, v_fp16, pos, kv_caches, layer_idx)
