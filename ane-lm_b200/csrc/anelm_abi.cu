@@ -337,6 +337,7 @@ GdnDecodeParams gdn_params(anelm_ctx* ctx, int layer, const anelm_plan* plan, co
     p.out = out;
     p.out_dtype = out_dtype;
     p.out_stride = (long long)c.lin_num_val_heads * c.lin_val_dim;
+    p.err = ctx->err;
     return p;
 }
 

@@ -15,14 +15,17 @@
 //   transpose_v_kernel      V -> V^T [B][Hkv][D][n_pad] so both MMA operands of
 //                           P V are K-major;
 //   fa_prefill_kernel       one CTA per (128-row query tile, q head, sequence):
-//     warp 4  TMA producer: Q tile once, K / V^T tiles of 64 keys into a 2-stage
-//             ring of 128B-swizzled shared-memory buffers;
+//     warps 4, 6  TMA producers (K; Q and V^T): tiles of 64 keys into 2-stage
+//             rings of 128B-swizzled shared-memory buffers, each ring refilled as
+//             soon as its own slot frees;
 //     warp 5  MMA issuer (one thread): S = Q K^T  (M=128, N=64, K=256) into one of
 //             two TMEM S buffers, O += P V^T (M=128, N=256, K=64) into TMEM;
 //     warps 0-3  softmax, one query row per thread: tcgen05.ld of its S row,
 //             causal mask, running max with lazy rescaling of O (only when the max
-//             grows by more than 2^8), P (fp16) into swizzled shared memory; at the
-//             end O / l, the sigmoid gate, and the store.
+//             grows by more than 2^8), P (fp16) into one of two swizzled shared-memory
+//             buffers, so the softmax of tile j+1 overlaps P V of tile j; at the end
+//             O / l is staged row by row in shared memory and each warp applies the
+//             sigmoid gate and stores whole rows (coalesced).
 //   All MMAs are kind::f16 (fp16 operands, fp32 accumulation in TMEM).  Every
 //   mbarrier wait is bounded and records ANELM_ERR_TIMEOUT instead of hanging.
 #include <cuda.h>
@@ -45,12 +48,16 @@ constexpr int kQBytes = kBM * kD * 2;        // 64 KB (4 boxes of 128 x 64)
 constexpr int kKBytes = kBN * kD * 2;        // 32 KB (4 boxes of 64 x 64)
 constexpr int kVBytes = kD * kBN * 2;        // 32 KB (1 box of 256 x 64, V^T)
 constexpr int kPBytes = kBM * kBN * 2;       // 16 KB
-constexpr int kSmemTiles = kQBytes + 2 * kKBytes + 2 * kVBytes + kPBytes;
+constexpr int kSmemTiles = kQBytes + 2 * kKBytes + 2 * kVBytes + 2 * kPBytes;
 constexpr int kSmemBytes = kSmemTiles + 256 + 1024;  // barriers + alignment slack
 constexpr uint32_t kTmemCols = 512;          // S0 [0,64), S1 [64,128), O [128,384)
+constexpr int kORow = kD + 4;                // fp32 words per staged output row (padding: no bank conflicts)
+static_assert(kBM * kORow * 4 <= 2 * kKBytes + 2 * kVBytes + 2 * kPBytes, "output staging fits the K/V/P buffers");
 
+// Every ring buffer has its own pair of barriers, so no barrier ever runs more than
+// one phase ahead of a waiter (a parity wait cannot tell phases k and k+2 apart).
 enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, S_EMPTY = 11, P_FULL = 13,
-           PV_DONE = 14, N_BARS = 15 };
+           PV_DONE = 15, N_BARS = 17 };
 
 __device__ __forceinline__ void rope_cs_pf(const FaPrefillParams& p, int pos, int j, float& c, float& s) {
     const int half = p.rot_dim >> 1;
@@ -158,7 +165,7 @@ __global__ void transpose_v_kernel(const __half* __restrict__ v, __half* __restr
     for (int r = threadIdx.y; r < 32; r += 8) dst[(long long)(d0 + r) * n_pad + t0 + threadIdx.x] = tile[threadIdx.x][r];
 }
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(224, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const FaPrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -167,8 +174,8 @@ __global__ void __launch_bounds__(192, 1)
     uint8_t* sK = sQ + kQBytes;
     uint8_t* sV = sK + 2 * kKBytes;
     uint8_t* sP = sV + 2 * kVBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -191,9 +198,9 @@ __global__ void __launch_bounds__(192, 1)
             tc::mbar_init(&bars[V_EMPTY + s], 1);
             tc::mbar_init(&bars[S_FULL + s], 1);
             tc::mbar_init(&bars[S_EMPTY + s], kBM);
+            tc::mbar_init(&bars[P_FULL + s], kBM);
+            tc::mbar_init(&bars[PV_DONE + s], 1);
         }
-        tc::mbar_init(&bars[P_FULL], kBM);
-        tc::mbar_init(&bars[PV_DONE], 1);
         tc::fence_barrier_init();
     }
     if (warp == 0) {
@@ -205,27 +212,35 @@ __global__ void __launch_bounds__(192, 1)
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
-        // ---------------- TMA producer ----------------
+    if (warp == 4 || warp == 6) {
+        // ---------------- TMA producers: warp 4 streams K, warp 6 streams Q and V ----------------
+        // (separate so a K tile never waits behind the V slot, which frees later)
         if (lane == 0 && nT > 0) {
-            tc::prefetch_tmap(&tmQ);
-            tc::prefetch_tmap(&tmK);
-            tc::prefetch_tmap(&tmV);
-            const int qrow0 = (b * p.Hq + h) * p.n_pad + q0;
             const int krow0 = (b * p.Hkv + kvh) * p.n_pad;
             const int vrow0 = (b * p.Hkv + kvh) * kD;
-            tc::mbar_arrive_expect_tx(&bars[Q_FULL], kQBytes);
-            for (int kb = 0; kb < 4; kb++) tc::tma_load_2d(sQ + kb * (kBM * 128), &tmQ, &bars[Q_FULL], kb * 64, qrow0);
-            for (int j = 0; j < nT; j++) {
-                const int s = j & 1, u = j >> 1;
-                if (j >= 2) tc::mbar_wait(&bars[K_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                tc::mbar_arrive_expect_tx(&bars[K_FULL + s], kKBytes);
+            if (warp == 4) {
+                tc::prefetch_tmap(&tmK);
+                for (int j = 0; j < nT; j++) {
+                    const int s = j & 1, u = j >> 1;
+                    if (j >= 2) tc::mbar_wait(&bars[K_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                    tc::mbar_arrive_expect_tx(&bars[K_FULL + s], kKBytes);
+                    for (int kb = 0; kb < 4; kb++)
+                        tc::tma_load_2d(sK + s * kKBytes + kb * (kBN * 128), &tmK, &bars[K_FULL + s], kb * 64,
+                                        krow0 + j * kBN);
+                }
+            } else {
+                tc::prefetch_tmap(&tmQ);
+                tc::prefetch_tmap(&tmV);
+                const int qrow0 = (b * p.Hq + h) * p.n_pad + q0;
+                tc::mbar_arrive_expect_tx(&bars[Q_FULL], kQBytes);
                 for (int kb = 0; kb < 4; kb++)
-                    tc::tma_load_2d(sK + s * kKBytes + kb * (kBN * 128), &tmK, &bars[K_FULL + s], kb * 64,
-                                    krow0 + j * kBN);
-                if (j >= 2) tc::mbar_wait(&bars[V_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                tc::mbar_arrive_expect_tx(&bars[V_FULL + s], kVBytes);
-                tc::tma_load_2d(sV + s * kVBytes, &tmV, &bars[V_FULL + s], j * kBN, vrow0);
+                    tc::tma_load_2d(sQ + kb * (kBM * 128), &tmQ, &bars[Q_FULL], kb * 64, qrow0);
+                for (int j = 0; j < nT; j++) {
+                    const int s = j & 1, u = j >> 1;
+                    if (j >= 2) tc::mbar_wait(&bars[V_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                    tc::mbar_arrive_expect_tx(&bars[V_FULL + s], kVBytes);
+                    tc::tma_load_2d(sV + s * kVBytes, &tmV, &bars[V_FULL + s], j * kBN, vrow0);
+                }
             }
         }
         __syncwarp();
@@ -256,14 +271,14 @@ __global__ void __launch_bounds__(192, 1)
             };
             auto pv = [&](int j) {
                 const int s = j & 1, u = j >> 1;
-                tc::mbar_wait(&bars[P_FULL], j & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                tc::mbar_wait(&bars[P_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::mbar_wait(&bars[V_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 4; ks++)
-                    tc::mma_f16_ss(tmem + 2 * kBN, tc::desc_kmajor_sw128(aP + ks * 32),
+                    tc::mma_f16_ss(tmem + 2 * kBN, tc::desc_kmajor_sw128(aP + s * kPBytes + ks * 32),
                                    tc::desc_kmajor_sw128(aV + s * kVBytes + ks * 32), id_pv, (j > 0) || (ks > 0));
-                tc::mma_commit(&bars[PV_DONE]);
+                tc::mma_commit(&bars[PV_DONE + s]);
                 tc::mma_commit(&bars[V_EMPTY + s]);
             };
             qk(0);
@@ -278,7 +293,7 @@ __global__ void __launch_bounds__(192, 1)
         const int r = tid;  // 0..127 == TMEM lane
         const int qpos = q0 + r;
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-        const float sl2 = 1.4426950408889634f / sqrtf((float)kD);
+        const float sl2 = 1.4426950408889634f / sqrtf((float)kD);  // log2(e) / sqrt(d)
         float m_used = -INFINITY, l = 0.f;
         float x[64];
         for (int j = 0; j < nT; j++) {
@@ -290,80 +305,99 @@ __global__ void __launch_bounds__(192, 1)
             tc::tc_fence_before();
             tc::mbar_arrive(&bars[S_EMPTY + s]);
             const int k0 = j * kBN;
-            float mx = -INFINITY;
+            if (k0 + kBN - 1 > q0 || k0 + kBN > p.n) {  // diagonal or ragged tile: causal / length mask
 #pragma unroll
-            for (int c = 0; c < 64; c++) {
-                const int kv = k0 + c;
-                x[c] = (kv <= qpos && kv < p.n) ? x[c] * sl2 : -INFINITY;
-                mx = fmaxf(mx, x[c]);
-            }
-            const float m_new = fmaxf(m_used, mx);
-            const bool grow = (m_used == -INFINITY) || (m_new > m_used + 8.0f);
-            if (j > 0) {
-                // O and the P buffer are free once P V of the previous tile completed
-                tc::mbar_wait(&bars[PV_DONE], (j - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                tc::tc_fence_after();
-                if (__any_sync(0xffffffffu, grow)) {
-                    const float alpha = grow ? exp2f(m_used - m_new) : 1.0f;
-                    float o[64];
-#pragma unroll
-                    for (int ch = 0; ch < 4; ch++) {
-                        tc::tmem_ld64(trow + 2 * kBN + ch * 64, o);
-                        tc::tmem_ld_wait();
-#pragma unroll
-                        for (int c = 0; c < 64; c++) o[c] *= alpha;
-                        tc::tmem_st64(trow + 2 * kBN + ch * 64, o);
-                    }
-                    tc::tmem_st_wait();
-                    l *= alpha;
+                for (int c = 0; c < 64; c++) {
+                    const int kv = k0 + c;
+                    if (kv > qpos || kv >= p.n) x[c] = -INFINITY;
                 }
+            }
+            float mx = x[0];
+#pragma unroll
+            for (int c = 1; c < 64; c++) mx = fmaxf(mx, x[c]);
+            const float m_new = fmaxf(m_used, mx);
+            // lazy rescaling: keep the old max unless it grew by more than 2^8 in probability units
+            const bool grow = (m_used == -INFINITY) || ((m_new - m_used) * sl2 > 8.0f);
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                // O is stable once P V of the previous tile completed
+                tc::mbar_wait(&bars[PV_DONE + ((j - 1) & 1)], ((j - 1) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                tc::tc_fence_after();
+                const float alpha = grow ? exp2f((m_used - m_new) * sl2) : 1.0f;
+                float o[64];
+#pragma unroll
+                for (int ch = 0; ch < 4; ch++) {
+                    tc::tmem_ld64(trow + 2 * kBN + ch * 64, o);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int c = 0; c < 64; c++) o[c] *= alpha;
+                    tc::tmem_st64(trow + 2 * kBN + ch * 64, o);
+                }
+                tc::tmem_st_wait();
+                l *= alpha;
             }
             if (grow) m_used = m_new;
-            // P row (fp16) into the 128B-swizzled K-major tile: chunk c of row r at (c ^ (r & 7))
+            const float nm = -m_used * sl2;
+            uint32_t w[32];
             float sum = 0.f;
-            uint8_t* prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-            for (int ch = 0; ch < 8; ch++) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const __half lo = __float2half_rn(exp2f(x[ch * 8 + 2 * e] - m_used));
-                    const __half hi = __float2half_rn(exp2f(x[ch * 8 + 2 * e + 1] - m_used));
-                    sum += __half2float(lo) + __half2float(hi);
-                    w[e] = pack_half2(lo, hi);
-                }
-                *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int e = 0; e < 32; e++) {
+                const float a = exp2f(fmaf(x[2 * e], sl2, nm));
+                const float b2 = exp2f(fmaf(x[2 * e + 1], sl2, nm));
+                sum += a + b2;
+                const __half2 hp = __floats2half2_rn(a, b2);
+                w[e] = *reinterpret_cast<const uint32_t*>(&hp);
             }
             l += sum;
+            // P buffer s is free once P V of tile j-2 completed
+            if (j >= 2) tc::mbar_wait(&bars[PV_DONE + s], ((j - 2) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+            // P row (fp16) into the 128B-swizzled K-major tile: chunk c of row r at (c ^ (r & 7))
+            uint8_t* prow = sP + s * kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+            for (int ch = 0; ch < 8; ch++)
+                *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
+                    make_uint4(w[4 * ch], w[4 * ch + 1], w[4 * ch + 2], w[4 * ch + 3]);
             tc::fence_proxy_async_smem();
             tc::tc_fence_before();
-            tc::mbar_arrive(&bars[P_FULL]);
+            tc::mbar_arrive(&bars[P_FULL + s]);
         }
-        // ---------------- epilogue ----------------
+        // ---------------- epilogue part 1: O / l into shared memory ----------------
+        // (the K / V / P buffers are idle once the last P V completed)
         if (nT > 0) {
-            tc::mbar_wait(&bars[PV_DONE], (nT - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+            tc::mbar_wait(&bars[PV_DONE + ((nT - 1) & 1)], ((nT - 1) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
             tc::tc_fence_after();
             const float inv = (l > 0.f) ? 1.0f / l : 0.f;
-            const bool valid = qpos < p.n;
-            const char* prow = reinterpret_cast<const char*>(p.proj) +
-                               ((long long)b * p.n + (valid ? qpos : 0)) * p.proj_stride * dtype_bytes(p.proj_dtype);
-            const long long orow = ((long long)b * p.n + qpos) * p.out_stride + (long long)h * kD;
+            float* orow = reinterpret_cast<float*>(sK) + r * kORow;
 #pragma unroll 1
             for (int ch = 0; ch < 4; ch++) {
                 float o[64];
                 tc::tmem_ld64(trow + 2 * kBN + ch * 64, o);
                 tc::tmem_ld_wait();
-                if (valid) {
 #pragma unroll
-                    for (int c = 0; c < 64; c++) {
-                        float v = o[c] * inv;
-                        if (p.gate) {  // mul_sigmoid_inplace, cpu_ops.cpp:15-22
-                            const float z = load_as_float(prow, p.proj_dtype, (long long)h * 2 * kD + kD + ch * 64 + c);
-                            v = v / (1.0f + expf(-z));
-                        }
-                        store_from_float(p.out, p.out_dtype, orow + ch * 64 + c, v);
-                    }
+                for (int c = 0; c < 64; c += 4)
+                    *reinterpret_cast<float4*>(orow + ch * 64 + c) =
+                        make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+            }
+        }
+    }
+    // ---------------- epilogue part 2: gate and store, one warp per row ----------------
+    __syncthreads();
+    if (warp < 4 && nT > 0) {
+        for (int rr = warp; rr < kBM; rr += 4) {
+            const int qpos = q0 + rr;
+            if (qpos >= p.n) break;
+            const float* orow = reinterpret_cast<const float*>(sK) + rr * kORow;
+            const char* prow = reinterpret_cast<const char*>(p.proj) +
+                               ((long long)b * p.n + qpos) * p.proj_stride * dtype_bytes(p.proj_dtype);
+            const long long obase = ((long long)b * p.n + qpos) * p.out_stride + (long long)h * kD;
+#pragma unroll
+            for (int e = 0; e < kD / 32; e++) {
+                const int c = e * 32 + lane;
+                float v = orow[c];
+                if (p.gate) {  // mul_sigmoid_inplace, cpu_ops.cpp:15-22
+                    const float z = load_as_float(prow, p.proj_dtype, (long long)h * 2 * kD + kD + c);
+                    v = v / (1.0f + expf(-z));
                 }
+                store_from_float(p.out, p.out_dtype, obase + c, v);
             }
         }
     }
@@ -428,7 +462,7 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
     fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
     transpose_v_kernel<<<dim3(p.n_pad / 32, kD / 32, p.B * p.Hkv), dim3(32, 8), 0, stream>>>(p.Vh, p.Vt, p.n_pad);
     cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), 192, kSmemBytes, stream>>>(mQ, mK, mV, p);
+    fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), 224, kSmemBytes, stream>>>(mQ, mK, mV, p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 

@@ -22,18 +22,20 @@
 // its W columns).  So the reference's own ring layout [C][K-1] is updated in
 // place without races, and the ring position is kept per (sequence, key head):
 // every CTA of the cluster reads it before the first cluster barrier and rank 0
-// advances it after the last one.  No atomics, no memory fences.  All global
-// stores (state write-back, ring inputs, position) come after the last cluster
-// barrier, whose release would otherwise wait for them to be acknowledged.
+// advances it once the whole cluster's q/k slices (pushed after each CTA read
+// the position) have arrived.  No atomics, no memory fences.
 //
-// Exchanges (distributed shared memory, push style).  Each CTA convolves its
-// slice of the q/k channels and stores the SiLU outputs straight into every
-// peer's q/k buffer; one cluster barrier publishes them.  The gated RMSNorm
-// needs sum(y^2) over the head's 128 columns: each CTA pushes its partial into
-// the peers of the same head; a second barrier publishes it.  After that no CTA
-// touches another's shared memory, so CTAs exit without a further barrier.
+// Exchanges (distributed shared memory, no cluster barriers).  Each CTA convolves
+// its slice of the q/k channels and pushes the SiLU outputs into every peer's q/k
+// buffer with st.async, whose arrival is counted in bytes on the peer's
+// mbarrier; the gated RMSNorm's sum(y^2) partials travel the same way to the
+// CTAs of the same head.  Each CTA waits only on its own barriers, so no
+// cluster-wide release has to wait for the state loads or stores in flight.  A
+// single relaxed cluster arrive/wait publishes the barrier initialisation.
 #include <cooperative_groups.h>
 #include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -51,6 +53,46 @@ __device__ __forceinline__ void cluster_arrive_relaxed() {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory"); }
+
+// Shared-memory address of `p` inside CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_rank(const void* p, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+
+// Asynchronous 4-byte store into another CTA's shared memory; its arrival is
+// counted (as 4 transaction bytes) on that CTA's mbarrier `bar`.
+__device__ __forceinline__ void st_async_f32(uint32_t dst, float v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];\n" ::"r"(dst),
+                 "r"(__float_as_uint(v)), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_init1(uint64_t* bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(bar)));
+}
+__device__ __forceinline__ void mbar_expect(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}\n" ::"r"(
+                     smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+// Bounded wait for phase 0 of a single-use barrier; false (and *err set) if it never completes.
+__device__ __forceinline__ bool mbar_wait0(uint64_t* bar, int* err) {
+    for (uint32_t i = 0; i < (1u << 22); i++) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok)
+            : "r"(smem_u32(bar))
+            : "memory");
+        if (ok) return true;
+    }
+    if (err) atomicCAS(err, 0, ANELM_ERR_TIMEOUT);
+    return false;
+}
 
 template <int RATIO, int NSPLIT, int THREADS>
 __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodeParams p) {
@@ -71,11 +113,21 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
     __shared__ __align__(16) float y_s[W];
     __shared__ __align__(16) float w_s[W];
     __shared__ __align__(16) float red[2][NW][W];
-    __shared__ float ss_s[NSPLIT];
+    __shared__ __align__(16) float ss_s[NSPLIT];
     __shared__ float scal[4];
+    __shared__ __align__(8) uint64_t bar_qk, bar_ss;
 
     cg::cluster_group cluster = cg::this_cluster();
-    cluster_arrive_relaxed();  // matched below, before the first DSMEM store
+    if (threadIdx.x == 0) {
+        mbar_init1(&bar_qk);
+        mbar_init1(&bar_ss);
+        // expected bytes are posted before this CTA arrives on the cluster barrier, so no
+        // peer can deliver before the expectation exists
+        mbar_expect(&bar_qk, 2 * kDk * 4);   // the whole q | k vector arrives from the cluster
+        mbar_expect(&bar_ss, NSPLIT * 4);    // one partial sum of y^2 per column block of this head
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    cluster_arrive_relaxed();  // matched below, before the first store into a peer
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rank = (int)cluster.block_rank();
@@ -149,16 +201,20 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
         scal[0] = sigmoid_ref(bb);                                     // qwen3_5.cpp:897
         scal[1] = expf(-p.A[h] * softplus_ref(a + p.dt_bias[h]));      // qwen3_5.cpp:898
     }
-    cluster_wait();  // every CTA of the cluster has started: DSMEM is addressable
+    cluster_wait();  // every CTA of the cluster has initialised its barriers
 #pragma unroll
     for (int u = 0; u < NU; u++) {
         const int i = tid + u * THREADS;
         if (i < QKP) {
 #pragma unroll
-            for (int q = 0; q < CS; q++) *cluster.map_shared_rank(&qk_s[rank * QKP + i], q) = qk_mine[u];
+            for (int q = 0; q < CS; q++)
+                st_async_f32(map_rank(&qk_s[rank * QKP + i], q), qk_mine[u], map_rank(&bar_qk, q));
         }
     }
-    cluster.sync();  // q/k published; every CTA has read the ring position
+    // q | k of this key head complete.  Every CTA of the cluster read the ring position before
+    // pushing its slice, so once rank 0 has every slice the position may advance.
+    mbar_wait0(&bar_qk, p.err);
+    if (rank == 0 && tid == 0) *pos_ptr = p1;  // cpu_ops.cpp:126-128
 
     // ---- 3. L2-normalise q and k (cpu_ops.cpp:82-87), q *= 1/sqrt(dk) (qwen3_5.cpp:879-887) ----
     if (warp < 2) {
@@ -257,10 +313,9 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
         float ss = 0.f;
         for (int i = lane; i < W; i += 32) ss += y_s[i] * y_s[i];
         ss = warp_sum(ss);
-        if (lane < NSPLIT) *cluster.map_shared_rank(&ss_s[cb], hl * NSPLIT + lane) = ss;
+        if (lane < NSPLIT) st_async_f32(map_rank(&ss_s[cb], hl * NSPLIT + lane), ss, map_rank(&bar_ss, hl * NSPLIT + lane));
     }
-    cluster.sync();  // partial sums published; no DSMEM access after this point
-    // global stores only now: the state block, and the new inputs into ring slot n (cpu_ops.cpp:109)
+    // global stores: the state block and the new inputs into ring slot n (cpu_ops.cpp:109)
 #pragma unroll
     for (int i = 0; i < NR; i++) __stcs(reinterpret_cast<float4*>(Sbase + (long long)(rg + RPP * i) * kDv), S[i]);
 #pragma unroll
@@ -277,7 +332,7 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
             ring[c * 3 + n] = xqk[u];
         }
     }
-    if (rank == 0 && tid == 0) *pos_ptr = p1;  // cpu_ops.cpp:126-128
+    mbar_wait0(&bar_ss, p.err);  // the head's partial sums have arrived
     float tot = 0.f;
 #pragma unroll
     for (int q = 0; q < NSPLIT; q++) tot += ss_s[q];
@@ -316,14 +371,26 @@ int launch_cfg(const GdnDecodeParams& p, int n_rows, cudaStream_t stream) {
 int launch_gdn_decode(const GdnDecodeParams& p, int n_rows, int key_dim, int val_dim, cudaStream_t stream) {
     if (key_dim != kDk || val_dim != kDv) return ANELM_ERR_UNSUPPORTED;
     const int ratio = p.Hv / p.Hk;
-    // Few rows: more column blocks per head to spread the state over more SMs.
-    const bool small = (long long)n_rows * p.Hv * 4 < 2 * 148;
-    switch (ratio) {
-        case 1: return small ? launch_cfg<1, 8, 128>(p, n_rows, stream) : launch_cfg<1, 4, 128>(p, n_rows, stream);
-        case 2: return launch_cfg<2, 4, 128>(p, n_rows, stream);
-        case 4: return launch_cfg<4, 2, 128>(p, n_rows, stream);
-        default: return ANELM_ERR_UNSUPPORTED;
+    // Column blocks per value head and threads per CTA.  Few rows: narrow blocks to spread
+    // the state over more SMs; many rows: wide blocks so each CTA's serial chain (conv,
+    // norms, two reductions, two cluster barriers) covers more bytes.
+    int nsplit = 0, threads = 0;
+    if (const char* e = getenv("ANELM_GDN_SPLIT")) {  // tuning override "nsplit,threads"
+        if (sscanf(e, "%d,%d", &nsplit, &threads) != 2) nsplit = threads = 0;
     }
+    const bool small = (long long)n_rows * p.Hv * 4 < 2 * 148;
+    if (!nsplit) {  // measured on B200: 2 x 128 is fastest for 256 rows (60% of HBM peak vs 52% for 2 x 256)
+        nsplit = small ? (ratio == 1 ? 8 : 4) : 2;
+        threads = 128;
+        if (ratio == 4) nsplit = 2;
+    }
+#define GDN_CASE(R, NS, T) \
+    if (ratio == R && nsplit == NS && threads == T) return launch_cfg<R, NS, T>(p, n_rows, stream);
+    GDN_CASE(1, 8, 128) GDN_CASE(1, 4, 128) GDN_CASE(1, 4, 256) GDN_CASE(1, 2, 256) GDN_CASE(1, 2, 128)
+    GDN_CASE(2, 4, 128) GDN_CASE(2, 4, 256) GDN_CASE(2, 2, 128) GDN_CASE(2, 2, 256)
+    GDN_CASE(4, 2, 128) GDN_CASE(4, 2, 256)
+#undef GDN_CASE
+    return ANELM_ERR_UNSUPPORTED;
 }
 
 }  // namespace anelm

@@ -74,6 +74,7 @@ struct GdnDecodeParams {
     void* out;
     int out_dtype;
     long long out_stride;
+    int* err;              // device error word (first error code wins), may be nullptr
 };
 
 // Causal prefill of a fresh ring: B sequences of n tokens each.
