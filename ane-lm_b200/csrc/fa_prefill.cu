@@ -48,16 +48,19 @@ constexpr int kQBytes = kBM * kD * 2;        // 64 KB (4 boxes of 128 x 64)
 constexpr int kKBytes = kBN * kD * 2;        // 32 KB (4 boxes of 64 x 64)
 constexpr int kVBytes = kD * kBN * 2;        // 32 KB (1 box of 256 x 64, V^T)
 constexpr int kPBytes = kBM * kBN * 2;       // 16 KB
-constexpr int kSmemTiles = kQBytes + 2 * kKBytes + 2 * kVBytes + 2 * kPBytes;
+constexpr int kKStages = 3;                 // K tiles run further ahead: their slot frees after Q K^T
+constexpr int kVStages = 2;
+constexpr int kSmemTiles = kQBytes + kKStages * kKBytes + kVStages * kVBytes;
 constexpr int kSmemBytes = kSmemTiles + 256 + 1024;  // barriers + alignment slack
-constexpr uint32_t kTmemCols = 512;          // S0 [0,64), S1 [64,128), O [128,384)
+constexpr uint32_t kTmemCols = 512;          // S0 [0,64), S1 [64,128) (P over its first 32), O [128,384)
 constexpr int kORow = kD + 4;                // fp32 words per staged output row (padding: no bank conflicts)
-static_assert(kBM * kORow * 4 <= 2 * kKBytes + 2 * kVBytes + 2 * kPBytes, "output staging fits the K/V/P buffers");
+static_assert(kBM * kORow * 4 <= kKStages * kKBytes + kVStages * kVBytes, "output staging fits the K/V buffers");
 
 // Every ring buffer has its own pair of barriers, so no barrier ever runs more than
 // one phase ahead of a waiter (a parity wait cannot tell phases k and k+2 apart).
-enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, S_EMPTY = 11, P_FULL = 13,
-           PV_DONE = 15, N_BARS = 17 };
+// PV_DONE[s] also frees TMEM buffer s (S of tile j and the P written over it).
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 4, V_FULL = 7, V_EMPTY = 9, S_FULL = 11, P_FULL = 13, PV_DONE = 15,
+           N_BARS = 17 };
 
 __device__ __forceinline__ void rope_cs_pf(const FaPrefillParams& p, int pos, int j, float& c, float& s) {
     const int half = p.rot_dim >> 1;
@@ -172,9 +175,8 @@ __global__ void __launch_bounds__(224, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + kQBytes;
-    uint8_t* sV = sK + 2 * kKBytes;
-    uint8_t* sP = sV + 2 * kVBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+    uint8_t* sV = sK + kKStages * kKBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVStages * kVBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -191,13 +193,14 @@ __global__ void __launch_bounds__(224, 1)
     if (tid == 0) {
         *abort = 0;
         tc::mbar_init(&bars[Q_FULL], 1);
-        for (int s = 0; s < 2; s++) {
+        for (int s = 0; s < kKStages; s++) {
             tc::mbar_init(&bars[K_FULL + s], 1);
             tc::mbar_init(&bars[K_EMPTY + s], 1);
+        }
+        for (int s = 0; s < 2; s++) {
             tc::mbar_init(&bars[V_FULL + s], 1);
             tc::mbar_init(&bars[V_EMPTY + s], 1);
             tc::mbar_init(&bars[S_FULL + s], 1);
-            tc::mbar_init(&bars[S_EMPTY + s], kBM);
             tc::mbar_init(&bars[P_FULL + s], kBM);
             tc::mbar_init(&bars[PV_DONE + s], 1);
         }
@@ -221,8 +224,9 @@ __global__ void __launch_bounds__(224, 1)
             if (warp == 4) {
                 tc::prefetch_tmap(&tmK);
                 for (int j = 0; j < nT; j++) {
-                    const int s = j & 1, u = j >> 1;
-                    if (j >= 2) tc::mbar_wait(&bars[K_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                    const int s = j % kKStages, u = j / kKStages;
+                    if (j >= kKStages)
+                        tc::mbar_wait(&bars[K_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                     tc::mbar_arrive_expect_tx(&bars[K_FULL + s], kKBytes);
                     for (int kb = 0; kb < 4; kb++)
                         tc::tma_load_2d(sK + s * kKBytes + kb * (kBN * 128), &tmK, &bars[K_FULL + s], kb * 64,
@@ -252,22 +256,23 @@ __global__ void __launch_bounds__(224, 1)
             const uint32_t aQ = (uint32_t)__cvta_generic_to_shared(sQ);
             const uint32_t aK = (uint32_t)__cvta_generic_to_shared(sK);
             const uint32_t aV = (uint32_t)__cvta_generic_to_shared(sV);
-            const uint32_t aP = (uint32_t)__cvta_generic_to_shared(sP);
             tc::mbar_wait(&bars[Q_FULL], 0, p.err, ANELM_ERR_TIMEOUT, abort);
             auto qk = [&](int j) {
-                const int s = j & 1, u = j >> 1;
-                tc::mbar_wait(&bars[K_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                if (j >= 2) tc::mbar_wait(&bars[S_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                const int ks_ = j % kKStages, uk = j / kKStages;  // K stage
+                const int s = j & 1, u = j >> 1;                  // TMEM S / P buffer
+                tc::mbar_wait(&bars[K_FULL + ks_], uk & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                // buffer s is free once P V of tile j-2 (which read P from it) completed
+                if (j >= 2) tc::mbar_wait(&bars[PV_DONE + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::tc_fence_after();
 #pragma unroll
                 for (int kb = 0; kb < 4; kb++)
 #pragma unroll
                     for (int ks = 0; ks < 4; ks++)
                         tc::mma_f16_ss(tmem + s * kBN, tc::desc_kmajor_sw128(aQ + kb * (kBM * 128) + ks * 32),
-                                       tc::desc_kmajor_sw128(aK + s * kKBytes + kb * (kBN * 128) + ks * 32), id_qk,
+                                       tc::desc_kmajor_sw128(aK + ks_ * kKBytes + kb * (kBN * 128) + ks * 32), id_qk,
                                        (kb | ks) != 0);
                 tc::mma_commit(&bars[S_FULL + s]);
-                tc::mma_commit(&bars[K_EMPTY + s]);
+                tc::mma_commit(&bars[K_EMPTY + ks_]);
             };
             auto pv = [&](int j) {
                 const int s = j & 1, u = j >> 1;
@@ -275,8 +280,8 @@ __global__ void __launch_bounds__(224, 1)
                 tc::mbar_wait(&bars[V_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::tc_fence_after();
 #pragma unroll
-                for (int ks = 0; ks < 4; ks++)
-                    tc::mma_f16_ss(tmem + 2 * kBN, tc::desc_kmajor_sw128(aP + s * kPBytes + ks * 32),
+                for (int ks = 0; ks < 4; ks++)  // A = P from TMEM: 16 keys = 8 columns per step
+                    tc::mma_f16_ts(tmem + 2 * kBN, tmem + s * kBN + ks * 8,
                                    tc::desc_kmajor_sw128(aV + s * kVBytes + ks * 32), id_pv, (j > 0) || (ks > 0));
                 tc::mma_commit(&bars[PV_DONE + s]);
                 tc::mma_commit(&bars[V_EMPTY + s]);
@@ -302,8 +307,6 @@ __global__ void __launch_bounds__(224, 1)
             tc::tc_fence_after();
             tc::tmem_ld64(trow + s * kBN, x);
             tc::tmem_ld_wait();
-            tc::tc_fence_before();
-            tc::mbar_arrive(&bars[S_EMPTY + s]);
             const int k0 = j * kBN;
             if (k0 + kBN - 1 > q0 || k0 + kBN > p.n) {  // diagonal or ragged tile: causal / length mask
 #pragma unroll
@@ -348,15 +351,9 @@ __global__ void __launch_bounds__(224, 1)
                 w[e] = *reinterpret_cast<const uint32_t*>(&hp);
             }
             l += sum;
-            // P buffer s is free once P V of tile j-2 completed
-            if (j >= 2) tc::mbar_wait(&bars[PV_DONE + s], ((j - 2) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-            // P row (fp16) into the 128B-swizzled K-major tile: chunk c of row r at (c ^ (r & 7))
-            uint8_t* prow = sP + s * kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-            for (int ch = 0; ch < 8; ch++)
-                *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
-                    make_uint4(w[4 * ch], w[4 * ch + 1], w[4 * ch + 2], w[4 * ch + 3]);
-            tc::fence_proxy_async_smem();
+            // P (fp16 pairs) over the first 32 columns of this tile's S buffer: the A operand of P V
+            tc::tmem_st32(trow + s * kBN, w);
+            tc::tmem_st_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars[P_FULL + s]);
         }
@@ -382,22 +379,33 @@ __global__ void __launch_bounds__(224, 1)
     // ---------------- epilogue part 2: gate and store, one warp per row ----------------
     __syncthreads();
     if (warp < 4 && nT > 0) {
-        for (int rr = warp; rr < kBM; rr += 4) {
-            const int qpos = q0 + rr;
-            if (qpos >= p.n) break;
-            const float* orow = reinterpret_cast<const float*>(sK) + rr * kORow;
-            const char* prow = reinterpret_cast<const char*>(p.proj) +
-                               ((long long)b * p.n + qpos) * p.proj_stride * dtype_bytes(p.proj_dtype);
-            const long long obase = ((long long)b * p.n + qpos) * p.out_stride + (long long)h * kD;
+        // four rows per pass: all gate loads of the pass are issued before any store
+        for (int r0 = warp * 4; r0 < kBM; r0 += 16) {
+            float z[4][kD / 32];
 #pragma unroll
-            for (int e = 0; e < kD / 32; e++) {
-                const int c = e * 32 + lane;
-                float v = orow[c];
-                if (p.gate) {  // mul_sigmoid_inplace, cpu_ops.cpp:15-22
-                    const float z = load_as_float(prow, p.proj_dtype, (long long)h * 2 * kD + kD + c);
-                    v = v / (1.0f + expf(-z));
+            for (int i = 0; i < 4; i++) {
+                const int qpos = min(q0 + r0 + i, p.n - 1);
+                const char* prow = reinterpret_cast<const char*>(p.proj) +
+                                   ((long long)b * p.n + qpos) * p.proj_stride * dtype_bytes(p.proj_dtype);
+#pragma unroll
+                for (int e = 0; e < kD / 32; e++)
+                    z[i][e] = p.gate ? load_as_float(prow, p.proj_dtype, (long long)h * 2 * kD + kD + e * 32 + lane)
+                                     : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int rr = r0 + i;
+                const int qpos = q0 + rr;
+                if (qpos >= p.n) break;
+                const float* orow = reinterpret_cast<const float*>(sK) + rr * kORow;
+                const long long obase = ((long long)b * p.n + qpos) * p.out_stride + (long long)h * kD;
+#pragma unroll
+                for (int e = 0; e < kD / 32; e++) {
+                    const int c = e * 32 + lane;
+                    float v = orow[c];
+                    if (p.gate) v = v / (1.0f + expf(-z[i][e]));  // mul_sigmoid_inplace, cpu_ops.cpp:15-22
+                    store_from_float(p.out, p.out_dtype, obase + c, v);
                 }
-                store_from_float(p.out, p.out_dtype, obase + c, v);
             }
         }
     }
