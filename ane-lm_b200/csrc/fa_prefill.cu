@@ -15,11 +15,14 @@
 //   transpose_v_kernel      V -> V^T [B][Hkv][D][n_pad] so both MMA operands of
 //                           P V are K-major;
 //   fa_prefill_kernel       one CTA per (128-row query tile, q head, sequence):
-//     warps 4, 6  TMA producers (K; Q and V^T): tiles of 64 keys into 2-stage
+//     warps 4, 6  TMA producers (K; V^T): tiles of 64 keys into 3-stage
 //             rings of 128B-swizzled shared-memory buffers, each ring refilled as
 //             soon as its own slot frees;
 //     warp 5  MMA issuer (one thread): S = Q K^T  (M=128, N=64, K=256) into one of
-//             two TMEM S buffers, O += P V^T (M=128, N=256, K=64) into TMEM;
+//             two TMEM S buffers, O += P V^T (M=128, N=256, K=64) into TMEM.  Q is the
+//             TMEM (A) operand of Q K^T (each softmax thread stores its row once), which
+//             leaves shared memory to the K / V rings and two P buffers, so Q K^T of
+//             tile j+2 queues behind P V of tile j without waiting for it;
 //     warps 0-3  softmax, one query row per thread: tcgen05.ld of its S row,
 //             causal mask, running max with lazy rescaling of O (only when the max
 //             grows by more than 2^8), P (fp16) into one of two swizzled shared-memory
@@ -42,25 +45,25 @@ namespace anelm {
 namespace {
 
 constexpr int kBM = 128;   // query rows per CTA
-constexpr int kBN = 64;    // keys per tile
+constexpr int kBN = 128;   // keys per tile (Q K^T at N = 128: a tcgen05.mma costs ~100 cycles even at
+                           // N = 64, so narrower tiles leave the tensor core two-thirds idle)
 constexpr int kD = 256;    // head dim of this kernel
-constexpr int kQBytes = kBM * kD * 2;        // 64 KB (4 boxes of 128 x 64)
-constexpr int kKBytes = kBN * kD * 2;        // 32 KB (4 boxes of 64 x 64)
-constexpr int kVBytes = kD * kBN * 2;        // 32 KB (1 box of 256 x 64, V^T)
-constexpr int kPBytes = kBM * kBN * 2;       // 16 KB
-constexpr int kKStages = 3;                 // K tiles run further ahead: their slot frees after Q K^T
-constexpr int kVStages = 2;
-constexpr int kSmemTiles = kQBytes + kKStages * kKBytes + kVStages * kVBytes;
+constexpr int kQBytes = kBM * kD * 2;        // 64 KB: 4 boxes of 128 rows x 64 d
+constexpr int kKBytes = kBN * kD * 2;        // 64 KB: 4 boxes of 128 keys x 64 d
+constexpr int kVBytes = kD * kBN * 2;        // 64 KB: V^T, 2 boxes of 256 d x 64 keys
+constexpr int kSmemTiles = kQBytes + kKBytes + kVBytes;
 constexpr int kSmemBytes = kSmemTiles + 256 + 1024;  // barriers + alignment slack
-constexpr uint32_t kTmemCols = 512;          // S0 [0,64), S1 [64,128) (P over its first 32), O [128,384)
+constexpr uint32_t kTmemCols = 512;          // S0 [0,128), S1 [128,256) (P over the first 64 of each), O [256,512)
+constexpr uint32_t kOCol = 2 * kBN;
 constexpr int kORow = kD + 4;                // fp32 words per staged output row (padding: no bank conflicts)
-static_assert(kBM * kORow * 4 <= kKStages * kKBytes + kVStages * kVBytes, "output staging fits the K/V buffers");
+static_assert(kBM * kORow * 4 <= kSmemTiles, "output staging fits the Q/K/V buffers");
 
-// Every ring buffer has its own pair of barriers, so no barrier ever runs more than
-// one phase ahead of a waiter (a parity wait cannot tell phases k and k+2 apart).
-// PV_DONE[s] also frees TMEM buffer s (S of tile j and the P written over it).
-enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 4, V_FULL = 7, V_EMPTY = 9, S_FULL = 11, P_FULL = 13, PV_DONE = 15,
-           N_BARS = 17 };
+// Single-stage K and V buffers: a 64 KB load (~0.4 us) hides behind the other operand's
+// MMAs (~1.4 us per tile).  Each barrier is used once per tile (K, V) or once per use of
+// a TMEM buffer (S_FULL, P_FULL, PV_DONE), so no barrier runs two phases ahead of a waiter.
+// PV_DONE[s] frees TMEM buffer s (its P was read) and says O is stable for rescaling.
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 2, V_FULL = 3, V_EMPTY = 4, S_FULL = 5, P_FULL = 7, PV_DONE = 9,
+           N_BARS = 11 };
 
 __device__ __forceinline__ void rope_cs_pf(const FaPrefillParams& p, int pos, int j, float& c, float& s) {
     const int half = p.rot_dim >> 1;
@@ -175,9 +178,9 @@ __global__ void __launch_bounds__(224, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + kQBytes;
-    uint8_t* sV = sK + kKStages * kKBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVStages * kVBytes);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+    uint8_t* sV = sK + kKBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVBytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -192,18 +195,7 @@ __global__ void __launch_bounds__(224, 1)
 
     if (tid == 0) {
         *abort = 0;
-        tc::mbar_init(&bars[Q_FULL], 1);
-        for (int s = 0; s < kKStages; s++) {
-            tc::mbar_init(&bars[K_FULL + s], 1);
-            tc::mbar_init(&bars[K_EMPTY + s], 1);
-        }
-        for (int s = 0; s < 2; s++) {
-            tc::mbar_init(&bars[V_FULL + s], 1);
-            tc::mbar_init(&bars[V_EMPTY + s], 1);
-            tc::mbar_init(&bars[S_FULL + s], 1);
-            tc::mbar_init(&bars[P_FULL + s], kBM);
-            tc::mbar_init(&bars[PV_DONE + s], 1);
-        }
+        for (int i = 0; i < N_BARS; i++) tc::mbar_init(&bars[i], (i == P_FULL || i == P_FULL + 1) ? kBM : 1);
         tc::fence_barrier_init();
     }
     if (warp == 0) {
@@ -216,34 +208,29 @@ __global__ void __launch_bounds__(224, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 4 || warp == 6) {
-        // ---------------- TMA producers: warp 4 streams K, warp 6 streams Q and V ----------------
-        // (separate so a K tile never waits behind the V slot, which frees later)
+        // ---------------- TMA producers: warp 4 streams Q then K, warp 6 streams V ----------------
         if (lane == 0 && nT > 0) {
             const int krow0 = (b * p.Hkv + kvh) * p.n_pad;
             const int vrow0 = (b * p.Hkv + kvh) * kD;
             if (warp == 4) {
-                tc::prefetch_tmap(&tmK);
-                for (int j = 0; j < nT; j++) {
-                    const int s = j % kKStages, u = j / kKStages;
-                    if (j >= kKStages)
-                        tc::mbar_wait(&bars[K_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                    tc::mbar_arrive_expect_tx(&bars[K_FULL + s], kKBytes);
-                    for (int kb = 0; kb < 4; kb++)
-                        tc::tma_load_2d(sK + s * kKBytes + kb * (kBN * 128), &tmK, &bars[K_FULL + s], kb * 64,
-                                        krow0 + j * kBN);
-                }
-            } else {
                 tc::prefetch_tmap(&tmQ);
-                tc::prefetch_tmap(&tmV);
+                tc::prefetch_tmap(&tmK);
                 const int qrow0 = (b * p.Hq + h) * p.n_pad + q0;
                 tc::mbar_arrive_expect_tx(&bars[Q_FULL], kQBytes);
-                for (int kb = 0; kb < 4; kb++)
-                    tc::tma_load_2d(sQ + kb * (kBM * 128), &tmQ, &bars[Q_FULL], kb * 64, qrow0);
+                for (int kb = 0; kb < 4; kb++) tc::tma_load_2d(sQ + kb * (kBM * 128), &tmQ, &bars[Q_FULL], kb * 64, qrow0);
                 for (int j = 0; j < nT; j++) {
-                    const int s = j & 1, u = j >> 1;
-                    if (j >= 2) tc::mbar_wait(&bars[V_EMPTY + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                    tc::mbar_arrive_expect_tx(&bars[V_FULL + s], kVBytes);
-                    tc::tma_load_2d(sV + s * kVBytes, &tmV, &bars[V_FULL + s], j * kBN, vrow0);
+                    if (j >= 1) tc::mbar_wait(&bars[K_EMPTY], (j - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                    tc::mbar_arrive_expect_tx(&bars[K_FULL], kKBytes);
+                    for (int kb = 0; kb < 4; kb++)
+                        tc::tma_load_2d(sK + kb * (kBN * 128), &tmK, &bars[K_FULL], kb * 64, krow0 + j * kBN);
+                }
+            } else {
+                tc::prefetch_tmap(&tmV);
+                for (int j = 0; j < nT; j++) {
+                    if (j >= 1) tc::mbar_wait(&bars[V_EMPTY], (j - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                    tc::mbar_arrive_expect_tx(&bars[V_FULL], kVBytes);
+                    for (int kb = 0; kb < 2; kb++)
+                        tc::tma_load_2d(sV + kb * (kD * 128), &tmV, &bars[V_FULL], j * kBN + kb * 64, vrow0);
                 }
             }
         }
@@ -258,10 +245,9 @@ __global__ void __launch_bounds__(224, 1)
             const uint32_t aV = (uint32_t)__cvta_generic_to_shared(sV);
             tc::mbar_wait(&bars[Q_FULL], 0, p.err, ANELM_ERR_TIMEOUT, abort);
             auto qk = [&](int j) {
-                const int ks_ = j % kKStages, uk = j / kKStages;  // K stage
-                const int s = j & 1, u = j >> 1;                  // TMEM S / P buffer
-                tc::mbar_wait(&bars[K_FULL + ks_], uk & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                // buffer s is free once P V of tile j-2 (which read P from it) completed
+                const int s = j & 1, u = j >> 1;
+                tc::mbar_wait(&bars[K_FULL], j & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                // TMEM buffer s is free once P V of tile j-2 (which read P from it) completed
                 if (j >= 2) tc::mbar_wait(&bars[PV_DONE + s], (u - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::tc_fence_after();
 #pragma unroll
@@ -269,22 +255,22 @@ __global__ void __launch_bounds__(224, 1)
 #pragma unroll
                     for (int ks = 0; ks < 4; ks++)
                         tc::mma_f16_ss(tmem + s * kBN, tc::desc_kmajor_sw128(aQ + kb * (kBM * 128) + ks * 32),
-                                       tc::desc_kmajor_sw128(aK + ks_ * kKBytes + kb * (kBN * 128) + ks * 32), id_qk,
-                                       (kb | ks) != 0);
+                                       tc::desc_kmajor_sw128(aK + kb * (kBN * 128) + ks * 32), id_qk, (kb | ks) != 0);
                 tc::mma_commit(&bars[S_FULL + s]);
-                tc::mma_commit(&bars[K_EMPTY + ks_]);
+                tc::mma_commit(&bars[K_EMPTY]);
             };
             auto pv = [&](int j) {
                 const int s = j & 1, u = j >> 1;
                 tc::mbar_wait(&bars[P_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                tc::mbar_wait(&bars[V_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                tc::mbar_wait(&bars[V_FULL], j & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::tc_fence_after();
 #pragma unroll
-                for (int ks = 0; ks < 4; ks++)  // A = P from TMEM: 16 keys = 8 columns per step
-                    tc::mma_f16_ts(tmem + 2 * kBN, tmem + s * kBN + ks * 8,
-                                   tc::desc_kmajor_sw128(aV + s * kVBytes + ks * 32), id_pv, (j > 0) || (ks > 0));
+                for (int ks = 0; ks < kBN / 16; ks++)  // A = P from TMEM: 16 keys = 8 columns per step
+                    tc::mma_f16_ts(tmem + kOCol, tmem + s * kBN + ks * 8,
+                                   tc::desc_kmajor_sw128(aV + (ks >> 2) * (kD * 128) + (ks & 3) * 32), id_pv,
+                                   (j > 0) || (ks > 0));
                 tc::mma_commit(&bars[PV_DONE + s]);
-                tc::mma_commit(&bars[V_EMPTY + s]);
+                tc::mma_commit(&bars[V_EMPTY]);
             };
             qk(0);
             for (int j = 0; j < nT; j++) {
@@ -305,19 +291,24 @@ __global__ void __launch_bounds__(224, 1)
             const int s = j & 1, u = j >> 1;
             tc::mbar_wait(&bars[S_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
             tc::tc_fence_after();
-            tc::tmem_ld64(trow + s * kBN, x);
-            tc::tmem_ld_wait();
             const int k0 = j * kBN;
-            if (k0 + kBN - 1 > q0 || k0 + kBN > p.n) {  // diagonal or ragged tile: causal / length mask
+            const bool need_mask = (k0 + kBN - 1 > q0) || (k0 + kBN > p.n);  // diagonal or ragged tile
+            // pass 1: row max over the two 64-key halves of S
+            float mx = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < 64; c++) {
-                    const int kv = k0 + c;
-                    if (kv > qpos || kv >= p.n) x[c] = -INFINITY;
+            for (int half = 0; half < 2; half++) {
+                tc::tmem_ld64(trow + s * kBN + half * 64, x);
+                tc::tmem_ld_wait();
+                if (need_mask) {
+#pragma unroll
+                    for (int c = 0; c < 64; c++) {
+                        const int kv = k0 + half * 64 + c;
+                        if (kv > qpos || kv >= p.n) x[c] = -INFINITY;
+                    }
                 }
-            }
-            float mx = x[0];
 #pragma unroll
-            for (int c = 1; c < 64; c++) mx = fmaxf(mx, x[c]);
+                for (int c = 0; c < 64; c++) mx = fmaxf(mx, x[c]);
+            }
             const float m_new = fmaxf(m_used, mx);
             // lazy rescaling: keep the old max unless it grew by more than 2^8 in probability units
             const bool grow = (m_used == -INFINITY) || ((m_new - m_used) * sl2 > 8.0f);
@@ -329,45 +320,58 @@ __global__ void __launch_bounds__(224, 1)
                 float o[64];
 #pragma unroll
                 for (int ch = 0; ch < 4; ch++) {
-                    tc::tmem_ld64(trow + 2 * kBN + ch * 64, o);
+                    tc::tmem_ld64(trow + kOCol + ch * 64, o);
                     tc::tmem_ld_wait();
 #pragma unroll
                     for (int c = 0; c < 64; c++) o[c] *= alpha;
-                    tc::tmem_st64(trow + 2 * kBN + ch * 64, o);
+                    tc::tmem_st64(trow + kOCol + ch * 64, o);
                 }
                 tc::tmem_st_wait();
                 l *= alpha;
             }
             if (grow) m_used = m_new;
             const float nm = -m_used * sl2;
-            uint32_t w[32];
+            // pass 2: P = exp2((s - m) * log2(e)/sqrt(d)) as fp16 pairs over the first 64 columns of S
+            // (half h of S has been read before P half h is written over columns [32h, 32h + 32))
             float sum = 0.f;
 #pragma unroll
-            for (int e = 0; e < 32; e++) {
-                const float a = exp2f(fmaf(x[2 * e], sl2, nm));
-                const float b2 = exp2f(fmaf(x[2 * e + 1], sl2, nm));
-                sum += a + b2;
-                const __half2 hp = __floats2half2_rn(a, b2);
-                w[e] = *reinterpret_cast<const uint32_t*>(&hp);
+            for (int half = 0; half < 2; half++) {
+                tc::tmem_ld64(trow + s * kBN + half * 64, x);
+                tc::tmem_ld_wait();
+                if (need_mask) {  // masked scores become -inf, so exp2 gives exactly 0 without a branch
+#pragma unroll
+                    for (int c = 0; c < 64; c++) {
+                        const int kv = k0 + half * 64 + c;
+                        if (kv > qpos || kv >= p.n) x[c] = -INFINITY;
+                    }
+                }
+                uint32_t w[32];
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    const float a = exp2f(fmaf(x[2 * e], sl2, nm));
+                    const float b2 = exp2f(fmaf(x[2 * e + 1], sl2, nm));
+                    sum += a + b2;
+                    const __half2 hp = __floats2half2_rn(a, b2);
+                    w[e] = *reinterpret_cast<const uint32_t*>(&hp);
+                }
+                tc::tmem_st32(trow + s * kBN + half * 32, w);
             }
             l += sum;
-            // P (fp16 pairs) over the first 32 columns of this tile's S buffer: the A operand of P V
-            tc::tmem_st32(trow + s * kBN, w);
             tc::tmem_st_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars[P_FULL + s]);
         }
         // ---------------- epilogue part 1: O / l into shared memory ----------------
-        // (the K / V / P buffers are idle once the last P V completed)
+        // (Q / K / V buffers are idle once the last P V completed)
         if (nT > 0) {
             tc::mbar_wait(&bars[PV_DONE + ((nT - 1) & 1)], ((nT - 1) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
             tc::tc_fence_after();
             const float inv = (l > 0.f) ? 1.0f / l : 0.f;
-            float* orow = reinterpret_cast<float*>(sK) + r * kORow;
+            float* orow = reinterpret_cast<float*>(sQ) + r * kORow;
 #pragma unroll 1
             for (int ch = 0; ch < 4; ch++) {
                 float o[64];
-                tc::tmem_ld64(trow + 2 * kBN + ch * 64, o);
+                tc::tmem_ld64(trow + kOCol + ch * 64, o);
                 tc::tmem_ld_wait();
 #pragma unroll
                 for (int c = 0; c < 64; c += 4)
@@ -397,7 +401,7 @@ __global__ void __launch_bounds__(224, 1)
                 const int rr = r0 + i;
                 const int qpos = q0 + rr;
                 if (qpos >= p.n) break;
-                const float* orow = reinterpret_cast<const float*>(sK) + rr * kORow;
+                const float* orow = reinterpret_cast<const float*>(sQ) + rr * kORow;
                 const long long obase = ((long long)b * p.n + qpos) * p.out_stride + (long long)h * kD;
 #pragma unroll
                 for (int e = 0; e < kD / 32; e++) {
