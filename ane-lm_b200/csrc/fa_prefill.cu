@@ -58,12 +58,39 @@ constexpr uint32_t kOCol = 2 * kBN;
 constexpr int kORow = kD + 4;                // fp32 words per staged output row (padding: no bank conflicts)
 static_assert(kBM * kORow * 4 <= kSmemTiles, "output staging fits the Q/K/V buffers");
 
+// 8 consecutive 16-bit values (bf16 or fp16) <-> fp32
+__device__ __forceinline__ void unpack8(const uint4 v, bool bf, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        float2 t;
+        if (bf) t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        else t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8], bool bf) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        if (bf) {
+            const __nv_bfloat162 t = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&t);
+        } else {
+            const __half2 t = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&t);
+        }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // Single-stage K and V buffers: a 64 KB load (~0.4 us) hides behind the other operand's
 // MMAs (~1.4 us per tile).  Each barrier is used once per tile (K, V) or once per use of
 // a TMEM buffer (S_FULL, P_FULL, PV_DONE), so no barrier runs two phases ahead of a waiter.
 // PV_DONE[s] frees TMEM buffer s (its P was read) and says O is stable for rescaling.
 enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 2, V_FULL = 3, V_EMPTY = 4, S_FULL = 5, P_FULL = 7, PV_DONE = 9,
-           N_BARS = 11 };
+           G_FULL = 11, N_BARS = 12 };
 
 __device__ __forceinline__ void rope_cs_pf(const FaPrefillParams& p, int pos, int j, float& c, float& s) {
     const int half = p.rot_dim >> 1;
@@ -173,7 +200,8 @@ __global__ void transpose_v_kernel(const __half* __restrict__ v, __half* __restr
 
 __global__ void __launch_bounds__(224, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                      const __grid_constant__ CUtensorMap tmV, const FaPrefillParams p) {
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG,
+                      const __grid_constant__ CUtensorMap tmO, const FaPrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
@@ -223,6 +251,15 @@ __global__ void __launch_bounds__(224, 1)
                     tc::mbar_arrive_expect_tx(&bars[K_FULL], kKBytes);
                     for (int kb = 0; kb < 4; kb++)
                         tc::tma_load_2d(sK + kb * (kBN * 128), &tmK, &bars[K_FULL], kb * 64, krow0 + j * kBN);
+                }
+                if (p.tma_epilogue && p.gate) {
+                    // the gate columns of this tile's 128 rows into the K buffer once the last Q K^T has
+                    // read it (rows past the sequence end are zero-filled), hidden behind the last tiles
+                    tc::prefetch_tmap(&tmG);
+                    tc::mbar_wait(&bars[K_EMPTY], (nT - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+                    tc::mbar_arrive_expect_tx(&bars[G_FULL], kBM * kD * 2);
+                    for (int kb = 0; kb < 4; kb++)
+                        tc::tma_load_3d(sK + kb * (kBM * 128), &tmG, &bars[G_FULL], h * 2 * kD + kD + kb * 64, q0, b);
                 }
             } else {
                 tc::prefetch_tmap(&tmV);
@@ -361,9 +398,47 @@ __global__ void __launch_bounds__(224, 1)
             tc::tc_fence_before();
             tc::mbar_arrive(&bars[P_FULL + s]);
         }
-        // ---------------- epilogue part 1: O / l into shared memory ----------------
-        // (Q / K / V buffers are idle once the last P V completed)
-        if (nT > 0) {
+        if (p.tma_epilogue) {
+            // ---------------- epilogue: O / l * sigmoid(gate) -> swizzled tiles -> TMA store ----------------
+            // Thread r reads its O row from TMEM and its gate row from the K buffer (128B-swizzled boxes of
+            // 64 columns, the TMA layout) and writes the 16-bit output row into the Q buffer in the same
+            // layout; one thread then stores the four boxes (rows past the sequence end are clipped).
+            tc::mbar_wait(&bars[PV_DONE + ((nT - 1) & 1)], ((nT - 1) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
+            tc::tc_fence_after();
+            if (p.gate) tc::mbar_wait(&bars[G_FULL], 0, p.err, ANELM_ERR_TIMEOUT, abort);
+            const float inv = (l > 0.f) ? 1.0f / l : 0.f;
+            const bool out_bf = p.out_dtype == ANELM_BF16, gate_bf = p.proj_dtype == ANELM_BF16;
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ch++) {
+                float o[64];
+                tc::tmem_ld64(trow + kOCol + ch * 64, o);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int off = ch * (kBM * 128) + r * 128 + ((u ^ (r & 7)) << 4);
+                    float v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] = o[u * 8 + e] * inv;
+                    if (p.gate) {
+                        float g[8];
+                        unpack8(*reinterpret_cast<const uint4*>(sK + off), gate_bf, g);
+#pragma unroll
+                        for (int e = 0; e < 8; e++) v[e] = v[e] / (1.0f + expf(-g[e]));  // cpu_ops.cpp:15-22
+                    }
+                    *reinterpret_cast<uint4*>(sQ + off) = pack8(v, out_bf);
+                }
+            }
+            tc::fence_proxy_async_smem();
+            tc::named_bar_sync(1, kBM);
+            if (tid == 0) {
+                tc::prefetch_tmap(&tmO);
+                for (int ch = 0; ch < 4; ch++) tc::tma_store_3d(&tmO, sQ + ch * (kBM * 128), h * kD + ch * 64, q0, b);
+                tc::bulk_commit_group();
+                tc::bulk_wait_group_read0();
+            }
+        } else if (nT > 0) {
+            // ---------------- epilogue part 1: O / l into shared memory ----------------
+            // (Q / K / V buffers are idle once the last P V completed)
             tc::mbar_wait(&bars[PV_DONE + ((nT - 1) & 1)], ((nT - 1) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
             tc::tc_fence_after();
             const float inv = (l > 0.f) ? 1.0f / l : 0.f;
@@ -381,8 +456,8 @@ __global__ void __launch_bounds__(224, 1)
         }
     }
     // ---------------- epilogue part 2: gate and store, one warp per row ----------------
-    __syncthreads();
-    if (warp < 4 && nT > 0) {
+    if (!p.tma_epilogue) __syncthreads();
+    if (!p.tma_epilogue && warp < 4 && nT > 0) {
         // four rows per pass: all gate loads of the pass are issued before any store
         for (int r0 = warp * 4; r0 < kBM; r0 += 16) {
             float z[4][kD / 32];
@@ -447,6 +522,22 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
     return r == CUDA_SUCCESS;
 }
 
+// 3D map over a [B][n][row_stride] tensor of a 16-bit type, inner extent `cols`, box {64, 128, 1}, 128B
+// swizzle: rows past n fall outside the map (loads zero-fill them, stores skip them).
+bool make_map_rows(CUtensorMap* m, int dtype, const void* base, uint64_t cols, uint64_t n, uint64_t B,
+                   uint64_t row_stride) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {cols, n, B};
+    cuuint64_t strides[2] = {row_stride * 2, n * row_stride * 2};
+    cuuint32_t box[3] = {64, kBM, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, dtype == ANELM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 size_t fa_prefill_workspace_bytes(int B, int n, int Hq, int Hkv, int head_dim) {
@@ -468,13 +559,21 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
         !make_map(&mK, p.Kh, (uint64_t)p.B * p.Hkv * p.n_pad, kD, kBN) ||
         !make_map(&mV, p.Vt, (uint64_t)p.B * p.Hkv * kD, p.n_pad, kD))
         return ANELM_ERR_CUDA;
+    // TMA epilogue: 16-bit proj and out, 16-byte aligned bases and row strides
+    auto b16 = [](int dt) { return dt == ANELM_BF16 || dt == ANELM_F16; };
+    CUtensorMap mG = mQ, mO = mQ;
+    p.tma_epilogue = b16(p.proj_dtype) && b16(p.out_dtype) && ((uintptr_t)p.proj % 16 == 0) &&
+                     ((uintptr_t)p.out % 16 == 0) && (p.proj_stride % 8 == 0) && (p.out_stride % 8 == 0) &&
+                     make_map_rows(&mO, p.out_dtype, p.out, (uint64_t)p.Hq * kD, p.n, p.B, p.out_stride) &&
+                     (!p.gate || make_map_rows(&mG, p.proj_dtype, p.proj, (uint64_t)p.Hq * 2 * kD, p.n, p.B,
+                                               p.proj_stride));
     const size_t prep_smem = (size_t)(p.Hq + 2 * p.Hkv) * kD * sizeof(float);
     if (prep_smem > 48 * 1024)
         cudaFuncSetAttribute(fa_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
     fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
     transpose_v_kernel<<<dim3(p.n_pad / 32, kD / 32, p.B * p.Hkv), dim3(32, 8), 0, stream>>>(p.Vh, p.Vt, p.n_pad);
     cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), 224, kSmemBytes, stream>>>(mQ, mK, mV, p);
+    fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), 224, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 

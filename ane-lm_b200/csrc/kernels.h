@@ -104,6 +104,7 @@ struct FaPrefillParams {
     int out_dtype;
     long long out_stride;
     int* err;
+    int tma_epilogue;      // set by launch_fa_prefill: gate tile loaded and output stored by TMA
 };
 
 size_t fa_prefill_workspace_bytes(int B, int n, int Hq, int Hkv, int head_dim);

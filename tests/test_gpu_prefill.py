@@ -72,7 +72,10 @@ def torch_reference(proj, qn, kn, start_pos, rope):
     return out.reshape(B, n, HQ * D)
 
 
-def test_prefill_matches_oracle_with_padding_and_decode_after():
+@pytest.mark.parametrize("out_dtype", ["float32", "bfloat16", "float16"])
+def test_prefill_matches_oracle_with_padding_and_decode_after(out_dtype):
+    """fp32 output takes the row-store epilogue; 16-bit outputs take the TMA tile store, whose rows past
+    each sequence's end (200 of a 256-row tile) must not spill into the next sequence's rows."""
     rng = np.random.default_rng(5)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(5)
@@ -84,7 +87,8 @@ def test_prefill_matches_oracle_with_padding_and_decode_after():
     with ctx_for(B, cap) as ctx:
         ctx.set_full_attn_weights(0, qn, kn)
         plan = ctx.plan([1, 0])
-        out = ctx.full_attn_prefill(plan, 0, proj, start_pos=0).cpu().numpy()
+        out = ctx.full_attn_prefill(plan, 0, proj, start_pos=0, out_dtype=getattr(torch, out_dtype))
+        out = out.float().cpu().numpy()
         # one more decode token for sequence 1 (row 0 of the plan)
         nxt = torch.randn(PROJ, generator=gen, device="cuda").to(torch.bfloat16)
         dec = ctx.full_attn_from_proj(0, 1, nxt, n).cpu().numpy()
@@ -105,8 +109,8 @@ def test_prefill_matches_oracle_with_padding_and_decode_after():
         assert_close(k[:ring.len], ring.k[:ring.len], atol=2e-3, rtol=2e-3, what="K ring after prefill")
 
 
-@pytest.mark.parametrize("B", [1, 8])
-def test_prefill_config3_full_size(B):
+@pytest.mark.parametrize("B,out_dtype", [(1, "float32"), (8, "bfloat16")])
+def test_prefill_config3_full_size(B, out_dtype):
     """Qwen3.5-4B shape, seq 4096, bf16 inputs N(0,1)."""
     rng = np.random.default_rng(3)
     gen = torch.Generator(device="cuda")
@@ -118,13 +122,13 @@ def test_prefill_config3_full_size(B):
     with ctx_for(B, n) as ctx:
         ctx.set_full_attn_weights(0, qn, kn)
         plan = ctx.plan(list(range(B)))
-        out = ctx.full_attn_prefill(plan, 0, proj, start_pos=0)
+        out = ctx.full_attn_prefill(plan, 0, proj, start_pos=0, out_dtype=getattr(torch, out_dtype))
         torch.cuda.synchronize()
         assert ctx.device_error() == 0
         plan.close()
     check = [0, B - 1] if B > 1 else [0]
     want = torch_reference(proj[check], qn, kn, 0, rope)
-    assert_close(out[check].cpu().numpy(), want.cpu().numpy(), what=f"config-3 prefill B={B}")
+    assert_close(out[check].float().cpu().numpy(), want.cpu().numpy(), what=f"config-3 prefill B={B}")
 
 
 def test_prefill_state_errors():
