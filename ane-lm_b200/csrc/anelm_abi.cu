@@ -117,7 +117,7 @@ struct anelm_ctx {
     float* rope_sin = nullptr;
     int* err = nullptr;
     std::vector<char> fresh;    // [n_fa][max_seqs]: ring known to be empty (prefill may start it)
-    void* prefill_ws = nullptr;  // prefill staging (Q, K, V, V^T), grown on demand
+    void* prefill_ws = nullptr;  // prefill staging (Q, K, V, V^T, sigmoid(gate)), grown on demand
     size_t prefill_ws_bytes = 0;
     __half* py_proj = nullptr;  // staging for anelm_py_cpu_attention
     __half* py_out = nullptr;

@@ -180,6 +180,13 @@ __global__ void __launch_bounds__(256) fa_prefill_prep_kernel(const FaPrefillPar
             p.v_pool[(slot_row + v) * kD + i] = vh;
         }
     }
+    if (p.SG) {  // sigmoid of the gate columns for the TMA epilogue (mul_sigmoid_inplace, cpu_ops.cpp:15-22)
+        __half* sg = p.SG + ((long long)b * p.n + t) * Hq * kD;
+        for (int idx = tid; idx < Hq * kD; idx += 256) {
+            const float g = load_as_float(row, p.proj_dtype, (long long)(idx / kD) * 2 * kD + kD + idx % kD);
+            sg[idx] = __float2half_rn(1.0f / (1.0f + expf(-g)));
+        }
+    }
     if (t == 0 && tid == 0 && p.kv_len) {
         p.kv_len[seq] = p.n;
         p.kv_start[seq] = 0;
@@ -253,13 +260,13 @@ __global__ void __launch_bounds__(224, 1)
                         tc::tma_load_2d(sK + kb * (kBN * 128), &tmK, &bars[K_FULL], kb * 64, krow0 + j * kBN);
                 }
                 if (p.tma_epilogue && p.gate) {
-                    // the gate columns of this tile's 128 rows into the K buffer once the last Q K^T has
+                    // sigmoid(gate) of this tile's 128 rows into the K buffer once the last Q K^T has
                     // read it (rows past the sequence end are zero-filled), hidden behind the last tiles
                     tc::prefetch_tmap(&tmG);
                     tc::mbar_wait(&bars[K_EMPTY], (nT - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                     tc::mbar_arrive_expect_tx(&bars[G_FULL], kBM * kD * 2);
                     for (int kb = 0; kb < 4; kb++)
-                        tc::tma_load_3d(sK + kb * (kBM * 128), &tmG, &bars[G_FULL], h * 2 * kD + kD + kb * 64, q0, b);
+                        tc::tma_load_3d(sK + kb * (kBM * 128), &tmG, &bars[G_FULL], h * kD + kb * 64, q0, b);
                 }
             } else {
                 tc::prefetch_tmap(&tmV);
@@ -407,7 +414,7 @@ __global__ void __launch_bounds__(224, 1)
             tc::tc_fence_after();
             if (p.gate) tc::mbar_wait(&bars[G_FULL], 0, p.err, ANELM_ERR_TIMEOUT, abort);
             const float inv = (l > 0.f) ? 1.0f / l : 0.f;
-            const bool out_bf = p.out_dtype == ANELM_BF16, gate_bf = p.proj_dtype == ANELM_BF16;
+            const bool out_bf = p.out_dtype == ANELM_BF16;
 #pragma unroll 1
             for (int ch = 0; ch < 4; ch++) {
                 float o[64];
@@ -419,11 +426,11 @@ __global__ void __launch_bounds__(224, 1)
                     float v[8];
 #pragma unroll
                     for (int e = 0; e < 8; e++) v[e] = o[u * 8 + e] * inv;
-                    if (p.gate) {
+                    if (p.gate) {  // sigmoid(gate) was computed by the prep kernel
                         float g[8];
-                        unpack8(*reinterpret_cast<const uint4*>(sK + off), gate_bf, g);
+                        unpack8(*reinterpret_cast<const uint4*>(sK + off), false, g);
 #pragma unroll
-                        for (int e = 0; e < 8; e++) v[e] = v[e] / (1.0f + expf(-g[e]));  // cpu_ops.cpp:15-22
+                        for (int e = 0; e < 8; e++) v[e] *= g[e];
                     }
                     *reinterpret_cast<uint4*>(sQ + off) = pack8(v, out_bf);
                 }
@@ -542,7 +549,8 @@ bool make_map_rows(CUtensorMap* m, int dtype, const void* base, uint64_t cols, u
 
 size_t fa_prefill_workspace_bytes(int B, int n, int Hq, int Hkv, int head_dim) {
     const long long n_pad = (n + kBM - 1) / kBM * kBM;
-    return (size_t)B * n_pad * head_dim * 2 * (Hq + 3 * (size_t)Hkv);
+    // fp16 Q, K, V, V^T and sigmoid(gate) [B][n][Hq][D]
+    return (size_t)B * n_pad * head_dim * 2 * (2 * (size_t)Hq + 3 * (size_t)Hkv);
 }
 
 int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream) {
@@ -554,19 +562,22 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
     p.Kh = ws + nq;
     p.Vh = p.Kh + nk;
     p.Vt = p.Vh + nk;
+    p.SG = nullptr;
     CUtensorMap mQ, mK, mV;
     if (!make_map(&mQ, p.Qh, (uint64_t)p.B * p.Hq * p.n_pad, kD, kBM) ||
         !make_map(&mK, p.Kh, (uint64_t)p.B * p.Hkv * p.n_pad, kD, kBN) ||
         !make_map(&mV, p.Vt, (uint64_t)p.B * p.Hkv * kD, p.n_pad, kD))
         return ANELM_ERR_CUDA;
-    // TMA epilogue: 16-bit proj and out, 16-byte aligned bases and row strides
-    auto b16 = [](int dt) { return dt == ANELM_BF16 || dt == ANELM_F16; };
+    // TMA epilogue: 16-bit output with a 16-byte aligned base and row stride; sigmoid(gate) as fp16
+    // [B][n][Hq * D] after V^T in the workspace
     CUtensorMap mG = mQ, mO = mQ;
-    p.tma_epilogue = b16(p.proj_dtype) && b16(p.out_dtype) && ((uintptr_t)p.proj % 16 == 0) &&
-                     ((uintptr_t)p.out % 16 == 0) && (p.proj_stride % 8 == 0) && (p.out_stride % 8 == 0) &&
+    __half* sg = p.Vt + nk;
+    p.tma_epilogue = (p.out_dtype == ANELM_BF16 || p.out_dtype == ANELM_F16) && ((uintptr_t)p.out % 16 == 0) &&
+                     (p.out_stride % 8 == 0) &&
                      make_map_rows(&mO, p.out_dtype, p.out, (uint64_t)p.Hq * kD, p.n, p.B, p.out_stride) &&
-                     (!p.gate || make_map_rows(&mG, p.proj_dtype, p.proj, (uint64_t)p.Hq * 2 * kD, p.n, p.B,
-                                               p.proj_stride));
+                     (!p.gate || make_map_rows(&mG, ANELM_F16, sg, (uint64_t)p.Hq * kD, p.n, p.B,
+                                               (uint64_t)p.Hq * kD));
+    if (p.tma_epilogue && p.gate) p.SG = sg;
     const size_t prep_smem = (size_t)(p.Hq + 2 * p.Hkv) * kD * sizeof(float);
     if (prep_smem > 48 * 1024)
         cudaFuncSetAttribute(fa_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
