@@ -52,11 +52,21 @@ constexpr int kQBytes = kBM * kD * 2;        // 64 KB: 4 boxes of 128 rows x 64 
 constexpr int kKBytes = kBN * kD * 2;        // 64 KB: 4 boxes of 128 keys x 64 d
 constexpr int kVBytes = kD * kBN * 2;        // 64 KB: V^T, 2 boxes of 256 d x 64 keys
 constexpr int kSmemTiles = kQBytes + kKBytes + kVBytes;
-constexpr int kSmemBytes = kSmemTiles + 256 + 1024;  // barriers + alignment slack
+constexpr int kSmemBytes = kSmemTiles + 256 + 6 * 128 * 4 + 1024;  // barriers, softmax exchange, alignment
+constexpr int kSoftmaxWarps = 8;             // two per TMEM lane quadrant, 64 keys of each tile each
+constexpr int kWarpK = kSoftmaxWarps, kWarpMma = kSoftmaxWarps + 1, kWarpV = kSoftmaxWarps + 2;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 3);
 constexpr uint32_t kTmemCols = 512;          // S0 [0,128), S1 [128,256) (P over the first 64 of each), O [256,512)
 constexpr uint32_t kOCol = 2 * kBN;
 constexpr int kORow = kD + 4;                // fp32 words per staged output row (padding: no bank conflicts)
 static_assert(kBM * kORow * 4 <= kSmemTiles, "output staging fits the Q/K/V buffers");
+
+// 2^x by the hardware approximation (PTX ex2.approx.ftz: relative error ~2^-22, -inf -> +0)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // 8 consecutive 16-bit values (bf16 or fp16) <-> fp32
 __device__ __forceinline__ void unpack8(const uint4 v, bool bf, float (&f)[8]) {
@@ -205,7 +215,7 @@ __global__ void transpose_v_kernel(const __half* __restrict__ v, __half* __restr
     for (int r = threadIdx.y; r < 32; r += 8) dst[(long long)(d0 + r) * n_pad + t0 + threadIdx.x] = tile[threadIdx.x][r];
 }
 
-__global__ void __launch_bounds__(224, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG,
                       const __grid_constant__ CUtensorMap tmO, const FaPrefillParams p) {
@@ -217,6 +227,7 @@ __global__ void __launch_bounds__(224, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* red = reinterpret_cast<float*>(sV + kVBytes + 256);  // [6][128]: row max (2 tiles x 2 halves), row sum
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n_qt = p.n_pad / kBM;
@@ -230,7 +241,7 @@ __global__ void __launch_bounds__(224, 1)
 
     if (tid == 0) {
         *abort = 0;
-        for (int i = 0; i < N_BARS; i++) tc::mbar_init(&bars[i], (i == P_FULL || i == P_FULL + 1) ? kBM : 1);
+        for (int i = 0; i < N_BARS; i++) tc::mbar_init(&bars[i], (i == P_FULL || i == P_FULL + 1) ? 2 * kBM : 1);
         tc::fence_barrier_init();
     }
     if (warp == 0) {
@@ -242,12 +253,12 @@ __global__ void __launch_bounds__(224, 1)
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4 || warp == 6) {
-        // ---------------- TMA producers: warp 4 streams Q then K, warp 6 streams V ----------------
+    if (warp == kWarpK || warp == kWarpV) {
+        // ---------------- TMA producers: one warp streams Q then K (then the gate tile), one streams V^T ----------------
         if (lane == 0 && nT > 0) {
             const int krow0 = (b * p.Hkv + kvh) * p.n_pad;
             const int vrow0 = (b * p.Hkv + kvh) * kD;
-            if (warp == 4) {
+            if (warp == kWarpK) {
                 tc::prefetch_tmap(&tmQ);
                 tc::prefetch_tmap(&tmK);
                 const int qrow0 = (b * p.Hq + h) * p.n_pad + q0;
@@ -279,7 +290,7 @@ __global__ void __launch_bounds__(224, 1)
             }
         }
         __syncwarp();
-    } else if (warp == 5) {
+    } else if (warp == kWarpMma) {
         // ---------------- MMA issuer ----------------
         if (lane == 0 && nT > 0) {
             constexpr uint32_t id_qk = tc::idesc_f16_f32(kBM, kBN);
@@ -324,10 +335,11 @@ __global__ void __launch_bounds__(224, 1)
         }
         __syncwarp();
     } else {
-        // ---------------- softmax: thread r owns query row q0 + r ----------------
-        const int r = tid;  // 0..127 == TMEM lane
+        // ---------------- softmax: thread (r, hf) owns keys [64 hf, 64 hf + 64) of query row q0 + r ----------------
+        const int r = tid & (kBM - 1), hf = tid >> 7;  // TMEM lane; key half of each S tile
         const int qpos = q0 + r;
-        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const uint32_t pair_bar = 1 + (warp & 3);  // warps w and w + 4 share TMEM lanes [32w, 32w + 32)
         const float sl2 = 1.4426950408889634f / sqrtf((float)kD);  // log2(e) / sqrt(d)
         float m_used = -INFINITY, l = 0.f;
         float x[64];
@@ -335,88 +347,82 @@ __global__ void __launch_bounds__(224, 1)
             const int s = j & 1, u = j >> 1;
             tc::mbar_wait(&bars[S_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
             tc::tc_fence_after();
-            const int k0 = j * kBN;
-            const bool need_mask = (k0 + kBN - 1 > q0) || (k0 + kBN > p.n);  // diagonal or ragged tile
-            // pass 1: row max over the two 64-key halves of S
-            float mx = -INFINITY;
+            const int k0 = j * kBN + hf * 64;
+            tc::tmem_ld64(trow + s * kBN + hf * 64, x);
+            tc::tmem_ld_wait();
+            if ((k0 + 63 > q0) || (k0 + 64 > p.n)) {  // diagonal or ragged: masked scores become -inf (exp2 -> 0)
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
-                tc::tmem_ld64(trow + s * kBN + half * 64, x);
-                tc::tmem_ld_wait();
-                if (need_mask) {
-#pragma unroll
-                    for (int c = 0; c < 64; c++) {
-                        const int kv = k0 + half * 64 + c;
-                        if (kv > qpos || kv >= p.n) x[c] = -INFINITY;
-                    }
-                }
-#pragma unroll
-                for (int c = 0; c < 64; c++) mx = fmaxf(mx, x[c]);
+                for (int c = 0; c < 64; c++)
+                    if (k0 + c > qpos || k0 + c >= p.n) x[c] = -INFINITY;
             }
+            float m4[4] = {x[0], x[1], x[2], x[3]};
+#pragma unroll
+            for (int c = 4; c < 64; c++) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+            float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+            // row max over both halves; the exchange slots alternate by tile so a slot is only
+            // rewritten after the partner has passed the next pair barrier (and so read it)
+            red[((j & 1) * 2 + hf) * kBM + r] = mx;
+            tc::named_bar_sync(pair_bar, 64);
+            mx = fmaxf(mx, red[((j & 1) * 2 + (hf ^ 1)) * kBM + r]);
             const float m_new = fmaxf(m_used, mx);
             // lazy rescaling: keep the old max unless it grew by more than 2^8 in probability units
+            // (both halves see the same maxima, so they take the same branch)
             const bool grow = (m_used == -INFINITY) || ((m_new - m_used) * sl2 > 8.0f);
             if (j > 0 && __any_sync(0xffffffffu, grow)) {
-                // O is stable once P V of the previous tile completed
+                // O is stable once P V of the previous tile completed; this half rescales O columns
+                // [128 hf, 128 hf + 128)
                 tc::mbar_wait(&bars[PV_DONE + ((j - 1) & 1)], ((j - 1) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::tc_fence_after();
                 const float alpha = grow ? exp2f((m_used - m_new) * sl2) : 1.0f;
-                float o[64];
-#pragma unroll
-                for (int ch = 0; ch < 4; ch++) {
-                    tc::tmem_ld64(trow + kOCol + ch * 64, o);
+#pragma unroll 1
+                for (int ch = 0; ch < 4; ch++) {  // 32 columns at a time: the S row stays in registers
+                    uint32_t o[32];
+                    tc::tmem_ld32(trow + kOCol + hf * 128 + ch * 32, o);
                     tc::tmem_ld_wait();
 #pragma unroll
-                    for (int c = 0; c < 64; c++) o[c] *= alpha;
-                    tc::tmem_st64(trow + kOCol + ch * 64, o);
+                    for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                    tc::tmem_st32(trow + kOCol + hf * 128 + ch * 32, o);
                 }
                 tc::tmem_st_wait();
                 l *= alpha;
             }
             if (grow) m_used = m_new;
             const float nm = -m_used * sl2;
-            // pass 2: P = exp2((s - m) * log2(e)/sqrt(d)) as fp16 pairs over the first 64 columns of S
-            // (half h of S has been read before P half h is written over columns [32h, 32h + 32))
-            float sum = 0.f;
+            // P = exp2((s - m) * log2(e)/sqrt(d)) as fp16 pairs: half hf fills columns [32 hf, 32 hf + 32) of
+            // the S buffer (both halves read their S columns before the pair barrier above)
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t w[32];
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
-                tc::tmem_ld64(trow + s * kBN + half * 64, x);
-                tc::tmem_ld_wait();
-                if (need_mask) {  // masked scores become -inf, so exp2 gives exactly 0 without a branch
-#pragma unroll
-                    for (int c = 0; c < 64; c++) {
-                        const int kv = k0 + half * 64 + c;
-                        if (kv > qpos || kv >= p.n) x[c] = -INFINITY;
-                    }
-                }
-                uint32_t w[32];
-#pragma unroll
-                for (int e = 0; e < 32; e++) {
-                    const float a = exp2f(fmaf(x[2 * e], sl2, nm));
-                    const float b2 = exp2f(fmaf(x[2 * e + 1], sl2, nm));
-                    sum += a + b2;
-                    const __half2 hp = __floats2half2_rn(a, b2);
-                    w[e] = *reinterpret_cast<const uint32_t*>(&hp);
-                }
-                tc::tmem_st32(trow + s * kBN + half * 32, w);
+            for (int e = 0; e < 32; e++) {
+                const float a = ex2_approx(fmaf(x[2 * e], sl2, nm));
+                const float b2 = ex2_approx(fmaf(x[2 * e + 1], sl2, nm));
+                s4[e & 3] += a + b2;
+                const __half2 hp = __floats2half2_rn(a, b2);
+                w[e] = *reinterpret_cast<const uint32_t*>(&hp);
             }
-            l += sum;
+            tc::tmem_st32(trow + s * kBN + hf * 32, w);
+            l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
             tc::tmem_st_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars[P_FULL + s]);
         }
+        // row sum over both halves (own slots: the max exchange slots may still be read)
+        red[4 * kBM + hf * kBM + r] = l;
+        tc::named_bar_sync(pair_bar, 64);
+        l += red[4 * kBM + (hf ^ 1) * kBM + r];
         if (p.tma_epilogue) {
             // ---------------- epilogue: O / l * sigmoid(gate) -> swizzled tiles -> TMA store ----------------
-            // Thread r reads its O row from TMEM and its gate row from the K buffer (128B-swizzled boxes of
-            // 64 columns, the TMA layout) and writes the 16-bit output row into the Q buffer in the same
-            // layout; one thread then stores the four boxes (rows past the sequence end are clipped).
+            // Thread (r, hf) reads O row r, columns [128 hf, 128 hf + 128), from TMEM and the matching gate
+            // values from the K buffer (128B-swizzled boxes of 64 columns, the TMA layout) and writes the
+            // 16-bit output into the Q buffer in the same layout; one thread then stores the four boxes
+            // (rows past the sequence end are clipped).
             tc::mbar_wait(&bars[PV_DONE + ((nT - 1) & 1)], ((nT - 1) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
             tc::tc_fence_after();
             if (p.gate) tc::mbar_wait(&bars[G_FULL], 0, p.err, ANELM_ERR_TIMEOUT, abort);
             const float inv = (l > 0.f) ? 1.0f / l : 0.f;
             const bool out_bf = p.out_dtype == ANELM_BF16;
 #pragma unroll 1
-            for (int ch = 0; ch < 4; ch++) {
+            for (int ch = 2 * hf; ch < 2 * hf + 2; ch++) {
                 float o[64];
                 tc::tmem_ld64(trow + kOCol + ch * 64, o);
                 tc::tmem_ld_wait();
@@ -436,7 +442,7 @@ __global__ void __launch_bounds__(224, 1)
                 }
             }
             tc::fence_proxy_async_smem();
-            tc::named_bar_sync(1, kBM);
+            tc::named_bar_sync(5, 2 * kBM);
             if (tid == 0) {
                 tc::prefetch_tmap(&tmO);
                 for (int ch = 0; ch < 4; ch++) tc::tma_store_3d(&tmO, sQ + ch * (kBM * 128), h * kD + ch * 64, q0, b);
@@ -451,7 +457,7 @@ __global__ void __launch_bounds__(224, 1)
             const float inv = (l > 0.f) ? 1.0f / l : 0.f;
             float* orow = reinterpret_cast<float*>(sQ) + r * kORow;
 #pragma unroll 1
-            for (int ch = 0; ch < 4; ch++) {
+            for (int ch = 2 * hf; ch < 2 * hf + 2; ch++) {
                 float o[64];
                 tc::tmem_ld64(trow + kOCol + ch * 64, o);
                 tc::tmem_ld_wait();
@@ -464,9 +470,9 @@ __global__ void __launch_bounds__(224, 1)
     }
     // ---------------- epilogue part 2: gate and store, one warp per row ----------------
     if (!p.tma_epilogue) __syncthreads();
-    if (!p.tma_epilogue && warp < 4 && nT > 0) {
+    if (!p.tma_epilogue && warp < kSoftmaxWarps && nT > 0) {
         // four rows per pass: all gate loads of the pass are issued before any store
-        for (int r0 = warp * 4; r0 < kBM; r0 += 16) {
+        for (int r0 = warp * 4; r0 < kBM; r0 += 4 * kSoftmaxWarps) {
             float z[4][kD / 32];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
@@ -584,7 +590,7 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
     fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
     transpose_v_kernel<<<dim3(p.n_pad / 32, kD / 32, p.B * p.Hkv), dim3(32, 8), 0, stream>>>(p.Vh, p.Vt, p.n_pad);
     cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), 224, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
+    fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 
