@@ -68,6 +68,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// 1/x by the hardware approximation (PTX rcp.approx.ftz: relative error ~2^-23, 1/inf -> 0)
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // 8 consecutive 16-bit values (bf16 or fp16) <-> fp32
 __device__ __forceinline__ void unpack8(const uint4 v, bool bf, float (&f)[8]) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -198,6 +205,129 @@ __global__ void __launch_bounds__(256) fa_prefill_prep_kernel(const FaPrefillPar
         }
     }
     if (t == 0 && tid == 0 && p.kv_len) {
+        p.kv_len[seq] = p.n;
+        p.kv_start[seq] = 0;
+    }
+}
+
+// Same work as fa_prefill_prep_kernel, organised for bandwidth: one CTA per token, each warp owns
+// whole 256-element segments of the token's projection row (segment s = q head s/2 or its gate for
+// s < 2 Hq, then the k heads, then the v heads; it starts at element 256 s), one 16-byte vector of
+// 8 elements per lane.  A warp issues the loads of up to four segments before using any, RMSNorm is a
+// warp reduction and rotate-half RoPE pairs lanes by shuffle, so no shared memory or block barrier is
+// involved.  Needs a 16-byte aligned projection row and rot_dim % 16 == 0.
+constexpr int kPrepBatch = 4;  // segments whose loads a warp issues together (more registers per thread
+                               // cost occupancy: 5 at 3 CTAs per SM ran slower than 4 at 4)
+__device__ __forceinline__ void load8(const char* row, int dtype, long long e0, float (&x)[8]) {
+    if (dtype == ANELM_F32) {
+        const float4 a = *reinterpret_cast<const float4*>(row + e0 * 4);
+        const float4 c = *reinterpret_cast<const float4*>(row + e0 * 4 + 16);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+    } else {
+        unpack8(*reinterpret_cast<const uint4*>(row + e0 * 2), dtype == ANELM_BF16, x);
+    }
+}
+__device__ __forceinline__ uint4 half8(const float (&x)[8]) { return pack8(x, false); }
+
+__global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPrefillParams p) {
+    const int t = blockIdx.x, b = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int Hq = p.Hq, Hkv = p.Hkv;
+    const int nseg = 2 * Hq + 2 * Hkv;
+    const int e0 = 8 * lane;  // this lane's first element within a 256-element segment
+    if (t >= p.n) {  // padding rows: finite zeros in Q, K, V
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        for (int h = warp; h < Hq; h += 8)
+            *reinterpret_cast<uint4*>(p.Qh + (((long long)b * Hq + h) * p.n_pad + t) * kD + e0) = z;
+        for (int h = warp; h < Hkv; h += 8) {
+            const long long o = (((long long)b * Hkv + h) * p.n_pad + t) * kD + e0;
+            *reinterpret_cast<uint4*>(p.Kh + o) = z;
+            *reinterpret_cast<uint4*>(p.Vh + o) = z;
+        }
+        return;
+    }
+    const char* row = reinterpret_cast<const char*>(p.proj) +
+                      ((long long)b * p.n + t) * p.proj_stride * dtype_bytes(p.proj_dtype);
+    const int pos = p.start_pos + t;
+    const int seq = p.seq_ids ? p.seq_ids[b] : 0;
+    const long long slot_row = p.kv_base ? (p.kv_base[seq] + t) * Hkv : 0;
+    const int half = p.rot_dim >> 1;
+    for (int s0 = warp; s0 < nseg; s0 += 8 * kPrepBatch) {
+        float x[kPrepBatch][8];
+#pragma unroll
+        for (int i = 0; i < kPrepBatch; i++)
+            if (s0 + 8 * i < nseg) load8(row, p.proj_dtype, (long long)(s0 + 8 * i) * kD + e0, x[i]);
+#pragma unroll
+        for (int i = 0; i < kPrepBatch; i++) {
+            const int s = s0 + 8 * i;
+            if (s >= nseg) break;
+            const bool is_q = s < 2 * Hq && !(s & 1), is_gate = s < 2 * Hq && (s & 1);
+            const bool is_k = s >= 2 * Hq && s < 2 * Hq + Hkv;
+            float* v = x[i];
+            if (is_q || is_k) {
+                if (p.qk_norm) {  // rmsnorm, cpu_ops.cpp:24-30 (qwen3_5.cpp:952-959)
+                    float ss = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 8; e++) ss += v[e] * v[e];
+                    ss = warp_sum(ss);
+                    const float r = 1.0f / sqrtf(ss / (float)kD + p.rms_eps);
+                    const float* w = (is_q ? p.q_norm : p.k_norm) + e0;
+#pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fmul_rn(v[e], r), w[e]);
+                }
+                if (p.rot_dim > 0) {  // apply_rope_cached, cpu_ops.cpp:40-63 (or rotate-half)
+                    if (p.rope_mode == ANELM_ROPE_INTERLEAVED) {
+                        if (e0 < p.rot_dim) {
+#pragma unroll
+                            for (int e = 0; e < 8; e += 2) {
+                                float c, sn;
+                                rope_cs_pf(p, pos, (e0 + e) >> 1, c, sn);
+                                const float v0 = v[e], v1 = v[e + 1];
+                                v[e] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, sn));
+                                v[e + 1] = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, c));
+                            }
+                        }
+                    } else {
+                        const int hl = half >> 3;  // lanes per rotary half
+                        float o[8];
+#pragma unroll
+                        for (int e = 0; e < 8; e++)
+                            o[e] = __shfl_sync(0xffffffffu, v[e], lane < hl ? lane + hl : lane - hl);
+                        if (e0 < p.rot_dim) {
+                            const bool first = lane < hl;
+#pragma unroll
+                            for (int e = 0; e < 8; e++) {
+                                float c, sn;
+                                rope_cs_pf(p, pos, (first ? e0 : e0 - half) + e, c, sn);
+                                v[e] = first ? __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(o[e], sn))
+                                             : __fadd_rn(__fmul_rn(v[e], c), __fmul_rn(o[e], sn));
+                            }
+                        }
+                    }
+                }
+            }
+            if (is_q) {
+                const int h = s >> 1;
+                *reinterpret_cast<uint4*>(p.Qh + (((long long)b * Hq + h) * p.n_pad + t) * kD + e0) = half8(x[i]);
+            } else if (is_gate) {
+                if (p.SG) {  // sigmoid of the gate for the TMA epilogue (mul_sigmoid_inplace, cpu_ops.cpp:15-22);
+                             // stored as fp16, so the hardware exp2 and reciprocal are exact enough
+                    float g[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) g[e] = rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * v[e]));
+                    *reinterpret_cast<uint4*>(p.SG + (((long long)b * p.n + t) * Hq + (s >> 1)) * kD + e0) = half8(g);
+                }
+            } else {
+                const int kh = is_k ? s - 2 * Hq : s - 2 * Hq - Hkv;
+                const uint4 hv = half8(x[i]);
+                const long long o = (((long long)b * Hkv + kh) * p.n_pad + t) * kD + e0;
+                *reinterpret_cast<uint4*>((is_k ? p.Kh : p.Vh) + o) = hv;
+                if (p.k_pool)  // ring append at slot t (qwen3_5.cpp:984-986)
+                    *reinterpret_cast<uint4*>((is_k ? p.k_pool : p.v_pool) + (slot_row + kh) * kD + e0) = hv;
+            }
+        }
+    }
+    if (t == 0 && threadIdx.x == 0 && p.kv_len) {
         p.kv_len[seq] = p.n;
         p.kv_start[seq] = 0;
     }
@@ -584,10 +714,15 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
                      (!p.gate || make_map_rows(&mG, ANELM_F16, sg, (uint64_t)p.Hq * kD, p.n, p.B,
                                                (uint64_t)p.Hq * kD));
     if (p.tma_epilogue && p.gate) p.SG = sg;
-    const size_t prep_smem = (size_t)(p.Hq + 2 * p.Hkv) * kD * sizeof(float);
-    if (prep_smem > 48 * 1024)
-        cudaFuncSetAttribute(fa_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
-    fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
+    const long long row_bytes = p.proj_stride * dtype_bytes(p.proj_dtype);
+    if ((uintptr_t)p.proj % 16 == 0 && row_bytes % 16 == 0 && p.rot_dim % 16 == 0) {
+        fa_prefill_prep_vec_kernel<<<dim3(p.n_pad, p.B), 256, 0, stream>>>(p);
+    } else {
+        const size_t prep_smem = (size_t)(p.Hq + 2 * p.Hkv) * kD * sizeof(float);
+        if (prep_smem > 48 * 1024)
+            cudaFuncSetAttribute(fa_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
+        fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
+    }
     transpose_v_kernel<<<dim3(p.n_pad / 32, kD / 32, p.B * p.Hkv), dim3(32, 8), 0, stream>>>(p.Vh, p.Vt, p.n_pad);
     cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
