@@ -79,6 +79,9 @@ SIGNATURES = {
     "anelm_full_attn_decode": [_vp, _vp, _i, _vp, _i, _vp, _vp, _i, _vp],
     "anelm_deltanet_decode": [_vp, _vp, _i, _vp, _i, _vp, _i, _vp],
     "anelm_full_attn_prefill": [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _vp],
+    "anelm_deltanet_prefill": [_vp, _vp, _i, _i, _vp, _i, _vp, _i, _vp],
+    "anelm_gated_delta_chunked": [_vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp,
+                                  ctypes.c_size_t, _vp],
     "anelm_py_cpu_attention": [_vp, _i, _i, _u16p, _u16p, _u16p, _i, _u16p, _vp],
     "anelm_gqa_attention": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "anelm_gqa_attention_noalloc": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],
@@ -124,6 +127,8 @@ def lib() -> ctypes.CDLL:
     L.anelm_last_error.restype = ctypes.c_char_p
     L.anelm_version.argtypes = []
     L.anelm_version.restype = ctypes.c_char_p
+    L.anelm_gated_delta_chunked_workspace_bytes.argtypes = [_i, _i, _i, _i]
+    L.anelm_gated_delta_chunked_workspace_bytes.restype = ctypes.c_size_t
     _lib = L
     return L
 

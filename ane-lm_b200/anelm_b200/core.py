@@ -246,6 +246,19 @@ class Context:
                                             _dtype_code(out), _stream(proj.device)), "anelm_full_attn_prefill")
         return out
 
+    def deltanet_prefill(self, plan: Plan, layer: int, proj: torch.Tensor, out=None, out_dtype=torch.float32):
+        """Chunkwise prefill of a DeltaNet layer: proj [B][n][gdn_proj_dim] for the plan's B sequences;
+        returns out [B][n][Hv*dv].  Continues from (and updates) each sequence's state and conv ring."""
+        assert proj.is_cuda and proj.is_contiguous() and proj.dim() == 3 and proj.shape[0] == plan.n
+        assert proj.shape[2] == self.gdn_proj_dim
+        n = proj.shape[1]
+        if out is None:
+            out = torch.empty((plan.n, n, self.gdn_out_dim), dtype=out_dtype, device=proj.device)
+        check(lib().anelm_deltanet_prefill(self.handle, plan.handle, layer, n, ctypes.c_void_p(proj.data_ptr()),
+                                           _dtype_code(proj), ctypes.c_void_p(out.data_ptr()), _dtype_code(out),
+                                           _stream(proj.device)), "anelm_deltanet_prefill")
+        return out
+
     def deltanet_decode(self, plan: Plan, layer: int, proj: torch.Tensor, out=None, out_dtype=torch.float32):
         assert proj.is_cuda and proj.is_contiguous() and proj.shape == (plan.n, self.gdn_proj_dim)
         if out is None:
@@ -254,3 +267,27 @@ class Context:
                                           _dtype_code(proj), ctypes.c_void_p(out.data_ptr()), _dtype_code(out),
                                           _stream(proj.device)), "anelm_deltanet_decode")
         return out
+
+
+def gated_delta_chunked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, log_decay: torch.Tensor,
+                        beta: torch.Tensor, state: torch.Tensor, delta_mode: int = 0, y=None,
+                        y_dtype=torch.float32, workspace=None) -> torch.Tensor:
+    """The chunked gated delta rule on the GPU (anelm_gated_delta_chunked): q, k [B][T][Hk][128],
+    v [B][T][Hv][128] (f32/f16/bf16), log_decay, beta [B][T][Hv] fp32, state [B][Hv][128][128] fp32
+    updated in place.  Returns y [B][T][Hv][128]."""
+    B, T, Hk, dk = q.shape
+    Hv, dv = v.shape[2], v.shape[3]
+    for t in (q, k, v, log_decay, beta, state):
+        assert t.is_cuda and t.is_contiguous()
+    assert log_decay.dtype == torch.float32 and beta.dtype == torch.float32 and state.dtype == torch.float32
+    if y is None:
+        y = torch.empty((B, T, Hv, dv), dtype=y_dtype, device=q.device)
+    need = lib().anelm_gated_delta_chunked_workspace_bytes(B, T, Hk, Hv)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    check(lib().anelm_gated_delta_chunked(
+        ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()), ctypes.c_void_p(v.data_ptr()), _dtype_code(q),
+        ctypes.c_void_p(log_decay.data_ptr()), ctypes.c_void_p(beta.data_ptr()), ctypes.c_void_p(state.data_ptr()),
+        B, T, Hk, Hv, dk, dv, delta_mode, ctypes.c_void_p(y.data_ptr()), _dtype_code(y),
+        ctypes.c_void_p(workspace.data_ptr()), workspace.numel(), _stream(q.device)), "anelm_gated_delta_chunked")
+    return y

@@ -119,6 +119,8 @@ struct anelm_ctx {
     std::vector<char> fresh;    // [n_fa][max_seqs]: ring known to be empty (prefill may start it)
     void* prefill_ws = nullptr;  // prefill staging (Q, K, V, V^T, sigmoid(gate)), grown on demand
     size_t prefill_ws_bytes = 0;
+    void* gdn_prefill_ws = nullptr;  // DeltaNet prefill staging (chunk operands), grown on demand
+    size_t gdn_prefill_ws_bytes = 0;
     __half* py_proj = nullptr;  // staging for anelm_py_cpu_attention
     __half* py_out = nullptr;
     std::vector<void*> allocs;
@@ -561,6 +563,7 @@ ANELM_API int anelm_destroy(anelm_ctx* ctx) {
     cudaDeviceSynchronize();
     for (auto& kv : ctx->single) free_plan(kv.second);
     if (ctx->prefill_ws) cudaFree(ctx->prefill_ws);
+    if (ctx->gdn_prefill_ws) cudaFree(ctx->gdn_prefill_ws);
     for (void* a : ctx->allocs) cudaFree(a);
     delete ctx;
     return ANELM_OK;
@@ -855,6 +858,108 @@ ANELM_API int anelm_deltanet_from_proj(anelm_ctx* ctx, int layer, int seq, const
     }
     if (rc) return rc;
     return gdn_launch(ctx, plan, layer, proj, proj_dtype, out, out_dtype, stream);
+}
+
+ANELM_API int anelm_deltanet_prefill(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,
+                                     const void* proj, int proj_dtype, void* out, int out_dtype, void* stream) {
+    if (int rc = check_layer(ctx, layer, ANELM_LAYER_LINEAR_ATTN)) return rc;
+    if (!plan || plan->ctx != ctx) return fail(ANELM_ERR_INVALID_ARG, "plan belongs to another context");
+    if (!proj || !out || n_tokens <= 0) return fail(ANELM_ERR_INVALID_ARG, "null tensor or no tokens");
+    if (int rc = check_dtype(proj_dtype)) return rc;
+    if (int rc = check_dtype(out_dtype)) return rc;
+    const anelm_config& c = ctx->cfg;
+    if (c.lin_key_dim != 128 || c.lin_val_dim != 128)
+        return fail(ANELM_ERR_UNSUPPORTED, "DeltaNet prefill is built for key/value head dims 128");
+    if (c.conv_kernel != 4) return fail(ANELM_ERR_UNSUPPORTED, "DeltaNet prefill is built for conv kernel 4");
+    const int gi = ctx->gdn_idx[layer];
+    if (!ctx->gdn_w_set[gi]) return fail(ANELM_ERR_STATE, "DeltaNet weights of layer %d not set", layer);
+    DeviceGuard dg(ctx->device);
+    const size_t need = gdn_prefill_workspace_bytes(plan->n, n_tokens, c.lin_num_key_heads, c.lin_num_val_heads,
+                                                    ctx->C, true);
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        if (need > ctx->gdn_prefill_ws_bytes) {
+            if (ctx->gdn_prefill_ws) cudaFree(ctx->gdn_prefill_ws);
+            ctx->gdn_prefill_ws = nullptr;
+            ctx->gdn_prefill_ws_bytes = 0;
+            cudaError_t e = cudaMalloc(&ctx->gdn_prefill_ws, need);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return fail(ANELM_ERR_NOMEM, "DeltaNet prefill workspace of %zu bytes: %s", need, cudaGetErrorString(e));
+            }
+            ctx->gdn_prefill_ws_bytes = need;
+        }
+    }
+    GdnPrefillParams p{};
+    p.B = plan->n;
+    p.n = n_tokens;
+    p.Hk = c.lin_num_key_heads;
+    p.Hv = c.lin_num_val_heads;
+    p.dk = c.lin_key_dim;
+    p.dv = c.lin_val_dim;
+    p.C = ctx->C;
+    p.delta_mode = c.delta_mode;
+    p.l2_eps = c.l2_eps;
+    p.conv_w = ctx->conv_w[gi];
+    p.A = ctx->A[gi];
+    p.dt_bias = ctx->dt_bias[gi];
+    p.norm_w = ctx->norm_w[gi];
+    p.conv = ctx->conv[gi];
+    p.conv_pos = ctx->conv_pos + (long long)gi * c.max_seqs * c.lin_num_key_heads;
+    p.proj = proj;
+    p.proj_dtype = proj_dtype;
+    p.proj_stride = ctx->gdn_proj;
+    p.out = out;
+    p.out_dtype = out_dtype;
+    p.out_stride = (long long)c.lin_num_val_heads * c.lin_val_dim;
+    p.state = ctx->ssm[gi];
+    p.seq_ids = plan->seq_d;
+    p.err = ctx->err;
+    return launch_status(launch_gdn_prefill(p, ctx->gdn_prefill_ws, static_cast<cudaStream_t>(stream)),
+                         "deltanet_prefill");
+}
+
+ANELM_API size_t anelm_gated_delta_chunked_workspace_bytes(int B, int T, int Hk, int Hv) {
+    if (B <= 0 || T <= 0 || Hk <= 0 || Hv <= 0) return 0;
+    return gdn_prefill_workspace_bytes(B, T, Hk, Hv, 0, false);
+}
+
+ANELM_API int anelm_gated_delta_chunked(const void* q, const void* k, const void* v, int qkv_dtype,
+                                        const float* log_decay, const float* beta, float* state, int B, int T,
+                                        int Hk, int Hv, int dk, int dv, int delta_mode, void* y, int y_dtype,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+    if (!q || !k || !v || !log_decay || !beta || !state || !y || !workspace)
+        return fail(ANELM_ERR_INVALID_ARG, "null pointer");
+    if (B <= 0 || T <= 0 || Hk <= 0 || Hv <= 0 || Hv % Hk)
+        return fail(ANELM_ERR_INVALID_ARG, "bad sizes B=%d T=%d Hk=%d Hv=%d", B, T, Hk, Hv);
+    if (dk != 128 || dv != 128) return fail(ANELM_ERR_UNSUPPORTED, "chunked delta rule is built for dk = dv = 128");
+    if (delta_mode != ANELM_DELTA_CPUOPS && delta_mode != ANELM_DELTA_HF)
+        return fail(ANELM_ERR_INVALID_ARG, "unknown delta mode %d", delta_mode);
+    if (int rc = check_dtype(qkv_dtype)) return rc;
+    if (int rc = check_dtype(y_dtype)) return rc;
+    const size_t need = gdn_prefill_workspace_bytes(B, T, Hk, Hv, 0, false);
+    if (workspace_bytes < need)
+        return fail(ANELM_ERR_CAPACITY, "workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    GdnPrefillParams p{};
+    p.B = B;
+    p.n = T;
+    p.Hk = Hk;
+    p.Hv = Hv;
+    p.dk = dk;
+    p.dv = dv;
+    p.delta_mode = delta_mode;
+    p.q_in = q;
+    p.k_in = k;
+    p.v_in = v;
+    p.in_dtype = qkv_dtype;
+    p.lg_in = log_decay;
+    p.beta_in = beta;
+    p.state = state;
+    p.y = y;
+    p.y_dtype = y_dtype;
+    p.y_stride = (long long)Hv * dv;
+    return launch_status(launch_gated_delta_chunked(p, workspace, static_cast<cudaStream_t>(stream)),
+                         "gated_delta_chunked");
 }
 
 ANELM_API int anelm_deltanet_decode(anelm_ctx* ctx, const anelm_plan* plan, int layer, const void* proj,

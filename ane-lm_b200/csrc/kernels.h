@@ -108,6 +108,56 @@ struct FaPrefillParams {
     int tma_epilogue;      // set by launch_fa_prefill: gate tile loaded and output stored by TMA
 };
 
+// Chunkwise Gated DeltaNet prefill (layer path: from projections) and the bare chunked
+// delta rule (core op: from q, k, v, log g, beta).
+struct GdnPrefillParams {
+    int B, n, T_pad, Hk, Hv, dk, dv, C, delta_mode;
+    float l2_eps;
+    // layer path
+    const float* conv_w;
+    const float* A;
+    const float* dt_bias;
+    const float* norm_w;
+    float* conv;           // [max_seqs][C][3]
+    int* conv_pos;         // [max_seqs][Hk]
+    const void* proj;      // [B][n][proj_stride]
+    int proj_dtype;
+    long long proj_stride;
+    void* out;             // [B][n][out_stride]
+    int out_dtype;
+    long long out_stride;
+    // core op inputs (token-major)
+    const void* q_in;
+    const void* k_in;
+    const void* v_in;
+    int in_dtype;
+    const float* lg_in;
+    const float* beta_in;
+    // state [seq][Hv][dk][dv], row b uses seq_ids[b] (or b)
+    float* state;
+    const int* seq_ids;
+    // y = S^T q per token: [B][n][y_stride]
+    void* y;
+    int y_dtype;
+    long long y_stride;
+    // workspace (carved by the launcher)
+    float* qb;             // [B][Hk][T_pad][dk]
+    float* kb;
+    float* vb;             // [B][Hv][T_pad][dv]
+    float* lg;             // [B][Hv][T_pad]
+    float* beta;
+    float* Wb;             // [B][Hv][T_pad][dk]
+    float* Ub;             // [B][Hv][T_pad][dv]
+    float* Mb;             // [B][Hv][T_pad][64]
+    float* lcb;            // [B][Hv][T_pad]
+    float* ring_snap;      // [B][C][3]
+    int* pos_snap;         // [B][Hk]
+    int* err;
+};
+size_t gdn_prefill_workspace_bytes(int B, int n, int Hk, int Hv, int C, bool layer);
+int launch_gdn_prefill(GdnPrefillParams p, void* workspace, cudaStream_t stream);
+int launch_gated_delta_chunked(GdnPrefillParams p, void* workspace, cudaStream_t stream);
+
 size_t fa_prefill_workspace_bytes(int B, int n, int Hq, int Hkv, int head_dim);
 int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream);
 

@@ -88,10 +88,18 @@ class ClockSampler:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        # nvidia-smi takes a while to start: wait (up to 5 s) for its first sample so that the
+        # samples cover the timed region that follows
+        t_end = time.time() + 5.0
+        while time.time() < t_end and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if not self.proc:
@@ -293,7 +301,7 @@ def run_gpu(args):
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(fa_gbs / hbm_peak, 4),
                      "peak_kind": peak_kind, "traffic": None,
                      "algorithmic_bytes_per_launch": int(fa_per_launch)},
-        "roofline_gdn": {"bound": "hbm", "kernel": "gdn_decode_kernel<4>", "achieved": round(gdn_gbs, 1),
+        "roofline_gdn": {"bound": "hbm", "kernel": "gdn_decode_kernel", "achieved": round(gdn_gbs, 1),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(gdn_gbs / hbm_peak, 4),
                          "algorithmic_bytes_per_launch": int(gdn_per_launch)},
         "e2e": e2e,
@@ -400,6 +408,8 @@ def run_prefill(args, torch, device):
         call()
     torch.cuda.synchronize(device)
     times = []
+    clocks = ClockSampler(device.index or 0)
+    clocks.start()
     for _ in range(args.steps):
         ctx.reset(-1)  # synchronous; outside the timed region
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -408,6 +418,7 @@ def run_prefill(args, torch, device):
         t1.record()
         torch.cuda.synchronize(device)
         times.append(t0.elapsed_time(t1))
+    ck = clocks.stop()
     ms = statistics.median(times)
     flops = 4.0 * n * n * HD * HQ / 2 * B  # causal: half of the S x S score / PV work
     tf = flops / (ms * 1e-3) / 1e12
@@ -421,6 +432,7 @@ def run_prefill(args, torch, device):
         "roofline": {"bound": "tensor", "kernel": "fa_prefill_kernel", "achieved": round(tf, 1), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(tf / peak, 4), "peak_kind": peak_kind, "traffic": None,
                      "algorithmic_flops_per_launch": flops},
+        "clocks": ck,
         "gpu_launches": 3 * args.steps}), flush=True)
     plan.close()
     ctx.close()

@@ -221,6 +221,31 @@ ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, in
                                       const void* proj, int proj_dtype, int start_pos, void* out, int out_dtype,
                                       void* stream);
 
+/* Prefill of the plan's sequences through a Gated DeltaNet layer: equivalent to n_tokens
+ * successive forward_deltanet_from_proj calls (qwen3_5.cpp:849-909, the per-token loop
+ * of qwen3_5.cpp:1205-1217), computed chunkwise (64-token chunks, WY form).  Continues
+ * from each sequence's current state, conv ring and ring position, and leaves them as
+ * the token loop would.  proj: [n_seqs][n_tokens][proj_dim]; out: [n_seqs][n_tokens][Hv*dv].
+ * key/value head dims 128 only.  Uses a context-owned staging buffer: prefill calls on
+ * one context must not overlap on the GPU. */
+ANELM_API int anelm_deltanet_prefill(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,
+                                     const void* proj, int proj_dtype, void* out, int out_dtype, void* stream);
+
+/* The chunked gated delta rule alone (no conv, norms or gates): for each of B sequences
+ * and value head h (key head h / (Hv/Hk)), over tokens t = 0..T-1,
+ *   ANELM_DELTA_CPUOPS (ssm_step, cpu_ops.cpp:131-146): S = g S + beta k (v - S^T k)^T
+ *   ANELM_DELTA_HF (export_hybrid_chunks.py:142-147):    S = g S; S += beta k (v - S^T k)^T
+ * then y = S^T q, with g = exp(log_decay).  q, k [B][T][Hk][dk], v [B][T][Hv][dv] of
+ * qkv_dtype (device); log_decay, beta [B][T][Hv] fp32; state [B][Hv][dk][dv] fp32, read
+ * and written in place; y [B][T][Hv][dv] of y_dtype.  dk = dv = 128.  workspace: device
+ * memory of at least anelm_gated_delta_chunked_workspace_bytes(B, T, Hk, Hv) bytes (the
+ * call allocates nothing). */
+ANELM_API size_t anelm_gated_delta_chunked_workspace_bytes(int B, int T, int Hk, int Hv);
+ANELM_API int anelm_gated_delta_chunked(const void* q, const void* k, const void* v, int qkv_dtype,
+                                        const float* log_decay, const float* beta, float* state, int B, int T,
+                                        int Hk, int Hv, int dk, int dv, int delta_mode, void* y, int y_dtype,
+                                        void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- Python route: scripts/serve_hybrid.py cpu_attention ---- */
 
 /* Drop-in for cpu_attention(q_gate_fp16, k_fp16, v_fp16, pos, kv_caches, layer_idx)

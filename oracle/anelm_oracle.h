@@ -88,6 +88,9 @@ int orc_deltanet_from_proj(const orc_shape* s, const orc_variant* var,
 /* Convenience: n_tokens successive DeltaNet steps (the per-token loop of
  * qwen3_5.cpp:1205-1217).  proj is [n_tokens][proj_dim] (copied, not modified),
  * out is [n_tokens][Hv*dv]. */
+int orc_gated_delta_tokens(int T, int Hk, int Hv, int dk, int dv, int delta_hf, const float* q,
+                           const float* k, const float* v, const float* log_decay,
+                           const float* beta, float* state, float* y);
 int orc_deltanet_tokens(const orc_shape* s, const orc_variant* var,
                         const float* conv_w, const float* A, const float* dt_bias,
                         const float* norm_w, float* ssm_state, float* conv_state,

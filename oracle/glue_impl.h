@@ -218,6 +218,33 @@ int GLUE(deltanet_from_proj)(const orc_shape* s, const orc_variant* var,
     return 0;
 }
 
+/* The delta-rule core alone over T tokens (the per-head step of qwen3_5.cpp:889-900 without
+ * conv, norms and gates): q, k [T][Hk][dk], v [T][Hv][dv], log_decay, beta [T][Hv],
+ * state [Hv][dk][dv] (updated in place), y [T][Hv][dv].  Value head h reads key head
+ * h / (Hv / Hk) (qwen3_5.cpp:891).  delta_hf selects the decay-first order. */
+int GLUE(gated_delta_tokens)(int T, int Hk, int Hv, int dk, int dv, int delta_hf, const float* q,
+                             const float* k, const float* v, const float* log_decay,
+                             const float* beta, float* state, float* y) {
+    if (Hk <= 0 || Hv <= 0 || Hv % Hk) return -1;
+    const int group = Hv / Hk;
+    for (int t = 0; t < T; t++)
+        for (int h = 0; h < Hv; h++) {
+            const int kh = h / group;
+            const float* qh = q + ((size_t)t * Hk + kh) * dk;
+            const float* kp = k + ((size_t)t * Hk + kh) * dk;
+            const float* vh = v + ((size_t)t * Hv + h) * dv;
+            float* yh = y + ((size_t)t * Hv + h) * dv;
+            float* st = state + (size_t)h * dk * dv;
+            const float decay = expf(log_decay[(size_t)t * Hv + h]);
+            const float b = beta[(size_t)t * Hv + h];
+            if (!delta_hf)
+                OP(ssm_step)(yh, st, qh, kp, vh, decay, b, dk, dv);
+            else
+                glue_ssm_step_hf(yh, st, qh, kp, vh, decay, b, dk, dv);
+        }
+    return 0;
+}
+
 /* Per-token loop of qwen3_5.cpp:1205-1217 for the DeltaNet layer. */
 int GLUE(deltanet_tokens)(const orc_shape* s, const orc_variant* var,
                           const float* conv_w, const float* A, const float* dt_bias,

@@ -197,6 +197,22 @@ def full_attn_tokens(kind: str, shape: Shape, var: Variant, q_norm, k_norm, ring
     return out
 
 
+def gated_delta_tokens(kind: str, q, k, v, log_decay, beta, state, delta_hf: int = 0):
+    """The bare delta-rule recurrence over T tokens: q, k [T][Hk][dk], v [T][Hv][dv], log_decay,
+    beta [T][Hv]; state [Hv][dk][dv] float32, updated in place.  Returns y [T][Hv][dv]."""
+    q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+    log_decay, beta = np.ascontiguousarray(log_decay, np.float32), np.ascontiguousarray(beta, np.float32)
+    T, Hk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    assert state.dtype == np.float32 and state.flags["C_CONTIGUOUS"] and state.shape == (Hv, dk, dv)
+    y = np.zeros((T, Hv, dv), np.float32)
+    rc = fn(kind, "gated_delta_tokens")(T, Hk, Hv, dk, dv, int(delta_hf), P(q), P(k), P(v), P(log_decay),
+                                        P(beta), P(state), P(y))
+    if rc != 0:
+        raise RuntimeError(f"oracle gated_delta_tokens failed rc={rc}")
+    return y
+
+
 def deltanet_tokens(kind: str, shape: Shape, var: Variant, conv_w, A, dt_bias, norm_w,
                     state: DeltaState, proj: np.ndarray):
     """Runs len(proj) successive DeltaNet core steps; updates state in place."""
