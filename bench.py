@@ -209,6 +209,8 @@ def run_gpu(args):
 
     if args.workload == "fa_prefill":
         return run_prefill(args, torch, device)
+    if args.workload == "gdn_prefill":
+        return run_gdn_prefill(args, torch, device, hbm_peak, peak_kind)
     if args.workload != "serve":
         return run_gpu_single(args, torch, device, hbm_peak, peak_kind)
 
@@ -438,6 +440,100 @@ def run_prefill(args, torch, device):
     ctx.close()
 
 
+def gdn_chunk_flops(T, Hv, B=1, C=64, dk=128, dv=128):
+    """Algorithmic FLOPs of the chunked delta rule: per chunk and value head 2C^2(3dk + 2dv)
+    (K K^T, Q K^T, W, U, M D) + 6 C dk dv (W S, Q S, K^T D)."""
+    n_chunks = (T + C - 1) // C
+    return float(2 * C * C * (3 * dk + 2 * dv) + 6 * C * dk * dv) * n_chunks * Hv * B
+
+
+def cpu_reference_gdn_chunk(T_sample, Hk, Hv):
+    """The reference delta-rule step (core/cpu_ops.cpp ssm_step via oracle/_ref/libref_core_fast.so)
+    over a token sample of the config-4 workload, one host thread; returns seconds per token."""
+    from oracle import pyoracle as po
+
+    kind = "ref_fast" if po.available("ref_fast") else "oracle"
+    rng = np.random.default_rng(1)
+    q = rng.standard_normal((T_sample, Hk, 128)).astype(np.float32)
+    k = q / np.linalg.norm(q, axis=-1, keepdims=True)
+    v = rng.standard_normal((T_sample, Hv, 128)).astype(np.float32)
+    lg = (-0.1 * rng.random((T_sample, Hv))).astype(np.float32)
+    beta = rng.random((T_sample, Hv)).astype(np.float32)
+    st = np.zeros((Hv, 128, 128), np.float32)
+    t0 = time.perf_counter()
+    po.gated_delta_tokens(kind, q, k, v, lg, beta, st, 0)
+    return (time.perf_counter() - t0) / T_sample, kind
+
+
+def run_gdn_prefill(args, torch, device, hbm_peak, peak_kind):
+    """the chunked gated delta rule, Hv 32 / Hk 16, dk = dv = 128, seq 8192,
+    batch 1; bf16 q / k / v N(0, 1) with L2-normalised k, log g ~ U(-0.1, 0), beta ~ U(0, 1)."""
+    from anelm_b200.core import gated_delta_chunked
+    import anelm_b200 as ab
+
+    try:
+        tpeak = float(json.load(open(PEAKS))["bf16_tflops"])
+        tpeak_kind = "measured"
+    except Exception:
+        tpeak, tpeak_kind = 1590.0, "fallback"
+    B, T, Hk, Hv = args.prefill_batch, args.gdn_len, 16, 32
+    g = torch.Generator(device=device)
+    g.manual_seed(4)
+    q = torch.randn(B, T, Hk, 128, generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn(B, T, Hk, 128, generator=g, device=device)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    v = torch.randn(B, T, Hv, 128, generator=g, device=device).to(torch.bfloat16)
+    lg = -0.1 * torch.rand(B, T, Hv, generator=g, device=device)
+    beta = torch.rand(B, T, Hv, generator=g, device=device)
+    state = torch.zeros(B, Hv, 128, 128, device=device)
+    y = torch.empty(B, T, Hv, 128, device=device, dtype=torch.bfloat16)
+    ws = torch.empty(ab.lib().anelm_gated_delta_chunked_workspace_bytes(B, T, Hk, Hv), dtype=torch.uint8,
+                     device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > 126 MB L2
+
+    def call():
+        gated_delta_chunked(q, k, v, lg, beta, state, ab.DELTA_CPUOPS, y=y, workspace=ws)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index or 0)
+    clocks.start()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()  # inputs (24 MB) would otherwise stay in L2 between iterations
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        call()
+        t1.record()
+        torch.cuda.synchronize(device)
+        times.append(t0.elapsed_time(t1))
+    ck = clocks.stop()
+    ms = statistics.median(times)
+    flops = gdn_chunk_flops(T, Hv, B)
+    tf = flops / (ms * 1e-3) / 1e12
+    nbytes = B * (2 * T * Hk * 128 * 2 + T * Hv * 128 * 2 + 2 * T * Hv * 4 + T * Hv * 128 * 2 + 2 * Hv * 128 * 128 * 4)
+    sec_tok, kind = cpu_reference_gdn_chunk(64, Hk, Hv)
+    cpu_tf = flops / (sec_tok * T * B) / 1e12
+    print(json.dumps({
+        "metric": "chunked Gated DeltaNet prefill TFLOP/s (cfg4, Hv 32 / Hk 16, d 128)", "value": round(tf, 2),
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 in, fp32 (hi/lo fp16 split) tensor-core products and state", "data": "synthetic",
+        "config": {"workload": f"BASELINE cfg4 chunked delta rule B={B} S={T} chunk 64", "Hk": Hk, "Hv": Hv,
+                   "dk": 128, "dv": 128, "l2": "256 MB buffer written between timed iterations"},
+        "roofline": {"bound": "tensor", "kernel": "gdn_pf_chain_kernel + gdn_pf_chunk_kernel", "achieved": round(tf, 2),
+                     "peak": tpeak, "unit": "TFLOP/s", "frac": round(tf / tpeak, 4), "peak_kind": tpeak_kind,
+                     "traffic": None, "algorithmic_flops_per_launch": flops,
+                     "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4), "algorithmic_bytes": nbytes},
+        "cpu_baseline": {"value": round(cpu_tf, 6), "unit": "TFLOP/s", "cores": 1,
+                         "kind": "reference" if kind == "ref_fast" else "port",
+                         "sample": "64 tokens x 32 value heads of the token recurrence (ssm_step), scaled to "
+                                   "the workload's algorithmic FLOPs"},
+        "clocks": ck,
+        "gpu_launches": 3 * args.steps}), flush=True)
+
+
 def run_gpu_single(args, torch, device, hbm_peak, peak_kind):
     """BASELINE configs 1 and 2: one sequence, one layer call per step, replayed from a CUDA graph."""
     import anelm_b200 as ab
@@ -618,7 +714,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="anelm", choices=["anelm", "reference"])
-    ap.add_argument("--workload", default="serve", choices=["serve", "fa_b1", "gdn_b1", "fa_prefill"])
+    ap.add_argument("--workload", default="serve", choices=["serve", "fa_b1", "gdn_b1", "fa_prefill", "gdn_prefill"])
+    ap.add_argument("--gdn-len", type=int, default=8192)
     ap.add_argument("--prefill-batch", type=int, default=1)
     ap.add_argument("--prefill-len", type=int, default=4096)
     ap.add_argument("--seqs", type=int, default=256)
