@@ -8,29 +8,31 @@
 // as one causal attention.
 //
 // Three launches:
-//   fa_prefill_prep_kernel  per token: RMSNorm + RoPE of the q heads and k heads
-//                           (same arithmetic as the decode prologue), fp16
-//                           Q [B][Hq][n_pad][D], K [B][Hkv][n_pad][D] and V, and
-//                           the ring append (slot t, len = n, start = 0);
-//   transpose_v_kernel      V -> V^T [B][Hkv][D][n_pad] so both MMA operands of
-//                           P V are K-major;
-//   fa_prefill_kernel       one CTA per (128-row query tile, q head, sequence):
-//     warps 4, 6  TMA producers (K; V^T): tiles of 64 keys into 3-stage
-//             rings of 128B-swizzled shared-memory buffers, each ring refilled as
-//             soon as its own slot frees;
-//     warp 5  MMA issuer (one thread): S = Q K^T  (M=128, N=64, K=256) into one of
-//             two TMEM S buffers, O += P V^T (M=128, N=256, K=64) into TMEM.  Q is the
-//             TMEM (A) operand of Q K^T (each softmax thread stores its row once), which
-//             leaves shared memory to the K / V rings and two P buffers, so Q K^T of
-//             tile j+2 queues behind P V of tile j without waiting for it;
-//     warps 0-3  softmax, one query row per thread: tcgen05.ld of its S row,
-//             causal mask, running max with lazy rescaling of O (only when the max
-//             grows by more than 2^8), P (fp16) into one of two swizzled shared-memory
-//             buffers, so the softmax of tile j+1 overlaps P V of tile j; at the end
-//             O / l is staged row by row in shared memory and each warp applies the
-//             sigmoid gate and stores whole rows (coalesced).
-//   All MMAs are kind::f16 (fp16 operands, fp32 accumulation in TMEM).  Every
-//   mbarrier wait is bounded and records ANELM_ERR_TIMEOUT instead of hanging.
+//   fa_prefill_prep_vec_kernel  per token: RMSNorm + RoPE of the q and k heads (same arithmetic
+//                           as the decode prologue), fp16 Q [B][Hq][n_pad][D], K and V
+//                           [B][Hkv][n_pad][D], sigmoid(gate) for the epilogue, and the ring
+//                           append (slot t, len = n, start = 0).  Warp per 256-element segment,
+//                           16-byte lanes (fa_prefill_prep_kernel: same work for any shape);
+//   transpose_v_kernel      V -> V^T [B][Hkv][D][n_pad] so both MMA operands of P V are K-major;
+//   fa_prefill_kernel       one CTA per (128-row query tile, q head, sequence), longest causal
+//                           tiles first, 11 warps:
+//     warps 0-7  softmax: warps w and w+4 share TMEM lanes [32(w%4), +32) and take keys
+//             [0, 64) / [64, 128) of each 128-key S tile; tcgen05.ld of the S row, causal mask,
+//             row max exchanged through shared memory (pairwise named barriers), lazy rescale
+//             of O (only when the max grows by more than 2^8), P = exp2(...) as fp16 pairs
+//             written over the first 64 columns of the S buffer (tcgen05.st);
+//     warp 8  TMA producer: Q (4 boxes), then one 64 KB K tile per key tile, then the
+//             sigmoid(gate) tile into the K buffer once the last Q K^T has read it;
+//     warp 9  MMA issuer (one thread): S = Q K^T (M=128, N=128, K=256) into one of two
+//             128-column TMEM S buffers, O += P V^T with A = P from TMEM (M=128, N=256,
+//             K=128) into the 256-column O accumulator, so Q K^T of tile j+1 overlaps the
+//             softmax of tile j;
+//     warp 10 TMA producer: one 64 KB V^T tile per key tile.
+//   Epilogue: O / l * sigmoid(gate) into 128B-swizzled tiles in the idle Q buffer and four TMA
+//   tile stores (a 3D tensor map clips rows past the sequence end); other output dtypes /
+//   alignments store rows from a staged fp32 copy.  All MMAs are kind::f16 (fp16 operands,
+//   fp32 accumulation in TMEM).  Every mbarrier wait is bounded and records ANELM_ERR_TIMEOUT
+//   instead of hanging.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
