@@ -20,11 +20,17 @@
 // Only ratios of decays appear (no 1/g), so small g is harmless.  The columns of S are
 // independent, so the sequential part runs one chain per (sequence, value head, 32 state columns).
 //
+// Precision: every tensor-core operand is held as an fp16 hi + lo pair (x = hi + lo to ~2^-22
+// relative) and each product is three mma.sync m16n8k16 (hi*hi + lo*hi + hi*lo) with fp32
+// accumulation, so the products match fp32 arithmetic; plain fp16 operands would let the gated
+// RMSNorm amplify their 2^-12 rounding past the tolerance.  Operands live in memory as a hi
+// plane followed by a lo plane and reach the MMAs through ldmatrix.
+//
 // Launches:
 //   gdn_pf_snapshot_kernel  copy of the conv rings / positions of the plan's sequences (the
 //                           prep kernel reads the old ring while the last tokens overwrite it)
-//   gdn_pf_prep_kernel      per token: conv + SiLU + L2 / scale, gates; q, k, v in chunk
-//                           layout, log g and beta; the last 3 inputs into the ring, new position
+//   gdn_pf_prep_kernel      per token: conv + SiLU + L2 / scale, gates; q, k, v (hi / lo) in
+//                           chunk layout, log g and beta; the last 3 inputs into the ring
 //   gdn_pf_pack_kernel      (core op only) token-major q, k, v, log g, beta -> chunk layout
 //   gdn_pf_chunk_kernel     per (chunk, value head): K K^T, Q K^T, T by forward substitution,
 //                           W, U, M
@@ -32,9 +38,6 @@
 //                           the state block; each operand buffer is refilled with the next
 //                           chunk's data (cp.async) as soon as this chunk's last reader is done
 //   gdn_pf_out_kernel       gated RMSNorm of y with z (layer path)
-// Products run on the tensor cores (mma.sync m16n8k16) with every operand split into an fp16
-// hi + lo pair (three MMAs per product), so they carry ~2^-22 relative error like the fp32
-// reference arithmetic; operands are kept in fp32 in memory.
 #include <math.h>
 
 #include "common.cuh"
@@ -48,67 +51,84 @@ constexpr int kC = 64;     // chunk length
 constexpr int kDk = 128;   // key head dim of these kernels
 constexpr int kDv = 128;   // value head dim
 constexpr int kDvb = 32;   // state columns per chain CTA
-constexpr int kLd = kDk + 4;  // fp32 row pitch of the 64 x 128 tiles in shared memory (bank spread)
+constexpr int kP = kDk + 8;   // fp16 pitch of 128-wide tiles (272 B: ldmatrix rows hit distinct banks)
+constexpr int kPc = kC + 8;   // fp16 pitch of 64-wide tiles (144 B)
 
-// ---------------------------------------------------------------- mma.sync fragments
-// m16n8k16, fp16 operands, fp32 accumulate.  g = lane / 4, c = lane % 4:
-//   A (16 x 16, row):  a0 = A[g][2c..2c+1], a1 = A[g+8][2c..], a2 = A[g][2c+8..], a3 = A[g+8][2c+8..]
-//   B (16 x 8, col):   b0 = B[2c..2c+1][g], b1 = B[2c+8..2c+9][g]
-//   C (16 x 8):        c0 = C[g][2c], c1 = C[g][2c+1], c2 = C[g+8][2c], c3 = C[g+8][2c+1]
-__device__ __forceinline__ uint32_t h2(float lo, float hi) {
-    const __half2 t = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t*>(&t);
-}
-// fp32 pair -> (hi, lo) fp16 pairs with hi + lo = x to ~2^-22 relative
-__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-    const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-    hi = pack_half2(h0, h1);
-    lo = h2(x0 - __half2float(h0), x1 - __half2float(h1));
+// ---------------------------------------------------------------- fragments (mma.sync m16n8k16)
+
+__device__ __forceinline__ void split_store(__half* hi, __half* lo, float x) {
+    const __half h = __float2half_rn(x);
+    *hi = h;
+    *lo = __float2half_rn(x - __half2float(h));
 }
 
-// acc[MT][NT] += A[r0 .. r0 + 16 MT) x B[.. , n0 .. n0 + 8 NT) over k in [0, K).
-// fa(r, k), fb(k, n) return fp32 values; SA / SB: split that operand into hi + lo fp16 parts
-// (two extra MMAs per step: hi*hi + lo*hi + hi*lo).
-template <bool SA, bool SB, int MT, int NT, class FA, class FB>
-__device__ __forceinline__ void warp_gemm(float (&acc)[MT][NT][4], int r0, int n0, int K, int lane, FA fa, FB fb) {
-    const int g = lane >> 2, c = lane & 3;
+// A (16 x 16) at (r0, k0) of a row-major tile base[r][k]
+__device__ __forceinline__ void lda(uint32_t (&a)[4], const __half* base, int pitch, int r0, int k0, int lane) {
+    ldmatrix_x4(smem_u32(base + (r0 + (lane & 15)) * pitch + k0 + (lane >> 4) * 8), a[0], a[1], a[2], a[3]);
+}
+// A (16 x 16) at (r0, k0) of A[r][k] = base[k][r] (the tile is stored transposed)
+__device__ __forceinline__ void lda_t(uint32_t (&a)[4], const __half* base, int pitch, int r0, int k0, int lane) {
+    const int mat = lane >> 3, i = lane & 7;
+    ldmatrix_x4_trans(smem_u32(base + (k0 + i + (mat >> 1) * 8) * pitch + r0 + (mat & 1) * 8), a[0], a[1], a[2], a[3]);
+}
+// B (16 x 8) fragments of two n-tiles n0, n0 + 8 at k0, with B[k][n] = base[n][k]
+__device__ __forceinline__ void ldb2(uint32_t (&b)[4], const __half* base, int pitch, int n0, int k0, int lane) {
+    const int mat = lane >> 3, i = lane & 7;
+    ldmatrix_x4(smem_u32(base + (n0 + i + (mat >> 1) * 8) * pitch + k0 + (mat & 1) * 8), b[0], b[1], b[2], b[3]);
+}
+// the same with B[k][n] = base[k][n]
+__device__ __forceinline__ void ldb2_t(uint32_t (&b)[4], const __half* base, int pitch, int n0, int k0, int lane) {
+    const int mat = lane >> 3, i = lane & 7;
+    ldmatrix_x4_trans(smem_u32(base + (k0 + i + (mat & 1) * 8) * pitch + n0 + (mat >> 1) * 8), b[0], b[1], b[2], b[3]);
+}
+// d += (ah + al)(bh + bl) without the lo*lo term
+__device__ __forceinline__ void mma3(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0,
+                                     uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+    mma_16816(d, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+    mma_16816(d, al[0], al[1], al[2], al[3], bh0, bh1);
+    mma_16816(d, ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+}
+
+// acc[NT] (16 rows x 8 NT columns) += A[r0.., 0..K) B[0..K, n0..); A and B as hi / lo tiles.
+// TA: A stored transposed; TB: B stored [k][n] (else [n][k]).
+template <bool TA, bool TB, int NT>
+__device__ __forceinline__ void gemm16(float (&acc)[NT][4], const __half* ahi, const __half* alo, int pa,
+                                       const __half* bhi, const __half* blo, int pb, int r0, int n0, int K, int lane) {
+    static_assert(NT % 2 == 0, "n-tiles come in pairs");
+#pragma unroll
     for (int k0 = 0; k0 < K; k0 += 16) {
-        uint32_t ah[MT][4], al[MT][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; mt++) {
-            const int r = r0 + mt * 16 + g;
-            const int k = k0 + 2 * c;
-            if (SA) {
-                split2(fa(r, k), fa(r, k + 1), ah[mt][0], al[mt][0]);
-                split2(fa(r + 8, k), fa(r + 8, k + 1), ah[mt][1], al[mt][1]);
-                split2(fa(r, k + 8), fa(r, k + 9), ah[mt][2], al[mt][2]);
-                split2(fa(r + 8, k + 8), fa(r + 8, k + 9), ah[mt][3], al[mt][3]);
-            } else {
-                ah[mt][0] = h2(fa(r, k), fa(r, k + 1));
-                ah[mt][1] = h2(fa(r + 8, k), fa(r + 8, k + 1));
-                ah[mt][2] = h2(fa(r, k + 8), fa(r, k + 9));
-                ah[mt][3] = h2(fa(r + 8, k + 8), fa(r + 8, k + 9));
-            }
+        uint32_t ah[4], al[4];
+        if (TA) {
+            lda_t(ah, ahi, pa, r0, k0, lane);
+            lda_t(al, alo, pa, r0, k0, lane);
+        } else {
+            lda(ah, ahi, pa, r0, k0, lane);
+            lda(al, alo, pa, r0, k0, lane);
         }
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            const int n = n0 + nt * 8 + g;
-            const int k = k0 + 2 * c;
-            uint32_t bh0, bh1, bl0 = 0, bl1 = 0;
-            if (SB) {
-                split2(fb(k, n), fb(k + 1, n), bh0, bl0);
-                split2(fb(k + 8, n), fb(k + 9, n), bh1, bl1);
+        for (int np = 0; np < NT / 2; np++) {
+            uint32_t bh[4], bl[4];
+            if (TB) {
+                ldb2_t(bh, bhi, pb, n0 + 16 * np, k0, lane);
+                ldb2_t(bl, blo, pb, n0 + 16 * np, k0, lane);
             } else {
-                bh0 = h2(fb(k, n), fb(k + 1, n));
-                bh1 = h2(fb(k + 8, n), fb(k + 9, n));
+                ldb2(bh, bhi, pb, n0 + 16 * np, k0, lane);
+                ldb2(bl, blo, pb, n0 + 16 * np, k0, lane);
             }
-#pragma unroll
-            for (int mt = 0; mt < MT; mt++) {
-                mma_16816(acc[mt][nt], ah[mt][0], ah[mt][1], ah[mt][2], ah[mt][3], bh0, bh1);
-                if (SA) mma_16816(acc[mt][nt], al[mt][0], al[mt][1], al[mt][2], al[mt][3], bh0, bh1);
-                if (SB) mma_16816(acc[mt][nt], ah[mt][0], ah[mt][1], ah[mt][2], ah[mt][3], bl0, bl1);
-            }
+            mma3(acc[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+            mma3(acc[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
         }
+    }
+}
+
+// 16-byte cp.async copies of `rows` rows of `cols` fp16 (hi and lo planes) into a pitched tile pair
+__device__ __forceinline__ void cp_tile_hl(__half* dhi, __half* dlo, int pitch, const __half* src, long long plane,
+                                           int rows, int cols, int tid, int nthreads) {
+    const int vpr = cols / 8;
+    for (int i = tid; i < rows * vpr; i += nthreads) {
+        const int r = i / vpr, cv = i % vpr;
+        cp_async_16(smem_u32(dhi + r * pitch + cv * 8), src + (long long)r * cols + cv * 8, 16);
+        cp_async_16(smem_u32(dlo + r * pitch + cv * 8), src + plane + (long long)r * cols + cv * 8, 16);
     }
 }
 
@@ -125,6 +145,10 @@ __global__ void gdn_pf_snapshot_kernel(const GdnPrefillParams p) {
 
 // ---------------------------------------------------------------- prep (one CTA per token)
 
+__device__ __forceinline__ void put_hl(__half* hi, long long plane, long long i, float x) {
+    split_store(hi + i, hi + plane + i, x);
+}
+
 __global__ void __launch_bounds__(256) gdn_pf_prep_kernel(const GdnPrefillParams p) {
     extern __shared__ float ys[];  // [C] conv + SiLU outputs of this token
     const int t = blockIdx.x, b = blockIdx.y;
@@ -137,10 +161,10 @@ __global__ void __launch_bounds__(256) gdn_pf_prep_kernel(const GdnPrefillParams
     if (t >= p.n) {  // padding tokens of the last chunk: no effect on the state (beta = 0, g = 1, k = v = 0)
         for (int i = tid; i < Hk * kDk; i += 256) {
             const long long o = (qrow + (long long)(i / kDk) * p.T_pad) * kDk + i % kDk;
-            p.qb[o] = 0.f;
-            p.kb[o] = 0.f;
+            put_hl(p.qh, p.q_plane, o, 0.f);
+            put_hl(p.kh, p.q_plane, o, 0.f);
         }
-        for (int i = tid; i < Hv * kDv; i += 256) p.vb[(vrow + (long long)(i / kDv) * p.T_pad) * kDv + i % kDv] = 0.f;
+        for (int i = tid; i < Hv * kDv; i += 256) put_hl(p.vh, p.v_plane, (vrow + (long long)(i / kDv) * p.T_pad) * kDv + i % kDv, 0.f);
         for (int h = tid; h < Hv; h += 256) {
             p.lg[vrow + (long long)h * p.T_pad] = 0.f;
             p.beta[vrow + (long long)h * p.T_pad] = 0.f;
@@ -190,14 +214,15 @@ __global__ void __launch_bounds__(256) gdn_pf_prep_kernel(const GdnPrefillParams
         for (int i = lane; i < kDk; i += 32) ss += x[i] * x[i];
         ss = warp_sum(ss);
         const float inv = 1.0f / sqrtf(ss + p.l2_eps);
-        float* dst = (isq ? p.qb : p.kb) + (qrow + (long long)kh * p.T_pad) * kDk;
+        const long long o = (qrow + (long long)kh * p.T_pad) * kDk;
         for (int i = lane; i < kDk; i += 32) {
             float v = __fmul_rn(x[i], inv);
             if (isq) v = __fmul_rn(v, qscale);
-            dst[i] = v;
+            put_hl(isq ? p.qh : p.kh, p.q_plane, o + i, v);
         }
     }
-    for (int i = tid; i < Hv * kDv; i += 256) p.vb[(vrow + (long long)(i / kDv) * p.T_pad) * kDv + i % kDv] = ys[2 * key_total + i];
+    for (int i = tid; i < Hv * kDv; i += 256)
+        put_hl(p.vh, p.v_plane, (vrow + (long long)(i / kDv) * p.T_pad) * kDv + i % kDv, ys[2 * key_total + i]);
 }
 
 // ---------------------------------------------------------------- pack (core op: token-major inputs)
@@ -209,12 +234,12 @@ __global__ void __launch_bounds__(256) gdn_pf_pack_kernel(const GdnPrefillParams
     const long long tok = (long long)b * p.n + t;
     for (int i = tid; i < Hk * kDk; i += 256) {
         const long long o = (((long long)b * Hk + i / kDk) * p.T_pad + t) * kDk + i % kDk;
-        p.qb[o] = live ? load_as_float(p.q_in, p.in_dtype, tok * Hk * kDk + i) : 0.f;
-        p.kb[o] = live ? load_as_float(p.k_in, p.in_dtype, tok * Hk * kDk + i) : 0.f;
+        put_hl(p.qh, p.q_plane, o, live ? load_as_float(p.q_in, p.in_dtype, tok * Hk * kDk + i) : 0.f);
+        put_hl(p.kh, p.q_plane, o, live ? load_as_float(p.k_in, p.in_dtype, tok * Hk * kDk + i) : 0.f);
     }
     for (int i = tid; i < Hv * kDv; i += 256) {
         const long long o = (((long long)b * Hv + i / kDv) * p.T_pad + t) * kDv + i % kDv;
-        p.vb[o] = live ? load_as_float(p.v_in, p.in_dtype, tok * Hv * kDv + i) : 0.f;
+        put_hl(p.vh, p.v_plane, o, live ? load_as_float(p.v_in, p.in_dtype, tok * Hv * kDv + i) : 0.f);
     }
     for (int h = tid; h < Hv; h += 256) {
         const long long o = ((long long)b * Hv + h) * p.T_pad + t;
@@ -226,18 +251,12 @@ __global__ void __launch_bounds__(256) gdn_pf_pack_kernel(const GdnPrefillParams
 // ---------------------------------------------------------------- per-chunk quantities
 
 struct ChunkSmem {
-    float k[kC][kLd];
-    float qv[kC][kLd];        // Q, then V
-    float a[kC][kC + 1];      // A, then T = (I + A)^{-1} in place
+    __half khi[kC][kP], klo[kC][kP];
+    __half qhi[kC][kP], qlo[kC][kP];    // Q, then V
+    float a[kC][kC + 1];                // A, then T = (I + A)^{-1}
+    __half thi[kC][kPc], tlo[kC][kPc];  // T scaled by columns (W's, then U's factors)
     float lc[kC], lt[kC], bt[kC];
 };
-
-__device__ __forceinline__ void load_tile(float (*dst)[kLd], const float* src, int tid) {
-    for (int i = tid; i < kC * (kDk / 4); i += 256) {
-        const int r = i / (kDk / 4), cv = i % (kDk / 4);
-        *reinterpret_cast<float4*>(&dst[r][cv * 4]) = *reinterpret_cast<const float4*>(src + (long long)r * kDk + cv * 4);
-    }
-}
 
 __global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -249,8 +268,9 @@ __global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParam
     const int t0 = ci * kC;
     const long long krow = ((long long)b * p.Hk + kh) * p.T_pad + t0;
     const long long vrow = ((long long)b * p.Hv + h) * p.T_pad + t0;
-    load_tile(sm.k, p.kb + krow * kDk, tid);
-    load_tile(sm.qv, p.qb + krow * kDk, tid);
+    cp_tile_hl(&sm.khi[0][0], &sm.klo[0][0], kP, p.kh + krow * kDk, p.q_plane, kC, kDk, tid, 256);
+    cp_tile_hl(&sm.qhi[0][0], &sm.qlo[0][0], kP, p.qh + krow * kDk, p.q_plane, kC, kDk, tid, 256);
+    cp_async_commit();
     if (warp == 0) {  // inclusive prefix sum of log g over the chunk (two tokens per lane)
         const float g0 = p.lg[vrow + 2 * lane], g1 = p.lg[vrow + 2 * lane + 1];
         float s = g0 + g1;
@@ -268,66 +288,81 @@ __global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParam
         sm.bt[2 * lane] = p.beta[vrow + 2 * lane];
         sm.bt[2 * lane + 1] = p.beta[vrow + 2 * lane + 1];
     }
+    cp_async_wait<0>();
     __syncthreads();
     // K K^T -> A (strictly lower), Q K^T -> M (lower incl. diagonal): warp -> 16 rows x 32 columns
     {
         const int r0 = 16 * (warp & 3), n0 = 32 * (warp >> 2);
-        float kk[1][4][4] = {}, qk[1][4][4] = {};
-        warp_gemm<true, true, 1, 4>(kk, r0, n0, kDk, lane, [&](int r, int k) { return sm.k[r][k]; },
-                                    [&](int k, int n) { return sm.k[n][k]; });
-        warp_gemm<true, true, 1, 4>(qk, r0, n0, kDk, lane, [&](int r, int k) { return sm.qv[r][k]; },
-                                    [&](int k, int n) { return sm.k[n][k]; });
-        float* mrow = p.Mb + vrow * kC;
+        float kk[4][4] = {}, qk[4][4] = {};
+        gemm16<false, false, 4>(kk, &sm.khi[0][0], &sm.klo[0][0], kP, &sm.khi[0][0], &sm.klo[0][0], kP, r0, n0, kDk, lane);
+        gemm16<false, false, 4>(qk, &sm.qhi[0][0], &sm.qlo[0][0], kP, &sm.khi[0][0], &sm.klo[0][0], kP, r0, n0, kDk, lane);
+        __half* mhi = p.mh + vrow * kC;
 #pragma unroll
         for (int nt = 0; nt < 4; nt++)
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const int r = r0 + g + (e >> 1) * 8, i = n0 + nt * 8 + 2 * c + (e & 1);
-                sm.a[r][i] = i < r ? sm.bt[r] * expf(sm.lt[r] - sm.lc[i]) * kk[0][nt][e] : 0.f;
-                mrow[r * kC + i] = i <= r ? expf(sm.lc[r] - sm.lc[i]) * qk[0][nt][e] : 0.f;
+                sm.a[r][i] = i < r ? sm.bt[r] * expf(sm.lt[r] - sm.lc[i]) * kk[nt][e] : 0.f;
+                put_hl(mhi, p.m_plane, r * kC + i, i <= r ? expf(sm.lc[r] - sm.lc[i]) * qk[nt][e] : 0.f);
             }
     }
     if (tid < kC) p.lcb[vrow + tid] = sm.lc[tid];
-    __syncthreads();  // Q no longer needed
-    load_tile(sm.qv, p.vb + vrow * kDv, tid);
+    __syncthreads();  // Q no longer needed: V into its buffers
+    cp_tile_hl(&sm.qhi[0][0], &sm.qlo[0][0], kP, p.vh + vrow * kDv, p.v_plane, kC, kDv, tid, 256);
+    cp_async_commit();
     // T = (I + A)^{-1} by forward substitution, one column per 4 threads: x_t = [t == j] - sum_{i<t} A_ti x_i.
     // Thread part pt keeps x_i for i = 4m + pt in registers; each row's sum is reduced over the 4 threads.
-    {
-        const int j = tid >> 2, pt = tid & 3;
-        float xs[kC / 4];
+    const int j = tid >> 2, pt = tid & 3;
+    float xs[kC / 4];
 #pragma unroll
-        for (int m = 0; m < kC / 4; m++) xs[m] = 0.f;
+    for (int m = 0; m < kC / 4; m++) xs[m] = 0.f;
 #pragma unroll
-        for (int t = 0; t < kC; t++) {
-            float s = 0.f;
+    for (int t = 0; t < kC; t++) {
+        float s = 0.f;
 #pragma unroll
-            for (int m = 0; m < kC / 4; m++)
-                if (4 * m + pt < t) s = fmaf(sm.a[t][4 * m + pt], xs[m], s);
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            const float x = (t == j ? 1.0f : 0.0f) - s;
-            if (pt == (t & 3)) xs[t >> 2] = x;
-        }
-        __syncthreads();  // every thread has read A (and V has landed)
+        for (int m = 0; m < kC / 4; m++)
+            if (4 * m + pt < t) s = fmaf(sm.a[t][4 * m + pt], xs[m], s);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        const float x = (t == j ? 1.0f : 0.0f) - s;
+        if (pt == (t & 3)) xs[t >> 2] = x;
+    }
+    {  // T' = T diag(beta e^{lt}) (W's factor) as hi / lo; column j belongs to this thread group
+        const float fw = sm.bt[j] * expf(sm.lt[j]);
 #pragma unroll
-        for (int m = 0; m < kC / 4; m++) sm.a[4 * m + pt][j] = xs[m];
+        for (int m = 0; m < kC / 4; m++) split_store(&sm.thi[4 * m + pt][j], &sm.tlo[4 * m + pt][j], xs[m] * fw);
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    const int r0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);  // warp -> 16 rows x 64 columns of W / U
+    {  // W = T diag(beta e^{lt}) K
+        float w[8][4] = {};
+        gemm16<false, true, 8>(w, &sm.thi[0][0], &sm.tlo[0][0], kPc, &sm.khi[0][0], &sm.klo[0][0], kP, r0, n0, kC, lane);
+        __half* whi = p.wh + vrow * kDk;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int r = r0 + g + (e >> 1) * 8, n = n0 + nt * 8 + 2 * c + (e & 1);
+                put_hl(whi, p.v_plane, r * kDk + n, w[nt][e]);
+            }
+    }
+    __syncthreads();  // T' read by every warp
+    {  // T'' = T diag(beta) (U's factor)
+        const float fu = sm.bt[j];
+#pragma unroll
+        for (int m = 0; m < kC / 4; m++) split_store(&sm.thi[4 * m + pt][j], &sm.tlo[4 * m + pt][j], xs[m] * fu);
     }
     __syncthreads();
-    // W = T diag(beta e^{lt}) K,  U = T diag(beta) V: warp -> 16 rows x 64 columns
-    {
-        const int r0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
-        float w[1][8][4] = {}, u[1][8][4] = {};
-        warp_gemm<true, true, 1, 8>(w, r0, n0, kC, lane, [&](int r, int k) { return sm.a[r][k] * sm.bt[k] * expf(sm.lt[k]); },
-                                    [&](int k, int n) { return sm.k[k][n]; });
-        warp_gemm<true, true, 1, 8>(u, r0, n0, kC, lane, [&](int r, int k) { return sm.a[r][k] * sm.bt[k]; },
-                                    [&](int k, int n) { return sm.qv[k][n]; });
+    {  // U = T diag(beta) V
+        float u[8][4] = {};
+        gemm16<false, true, 8>(u, &sm.thi[0][0], &sm.tlo[0][0], kPc, &sm.qhi[0][0], &sm.qlo[0][0], kP, r0, n0, kC, lane);
 #pragma unroll
         for (int nt = 0; nt < 8; nt++)
 #pragma unroll
             for (int e = 0; e < 4; e += 2) {
                 const int r = r0 + g + (e >> 1) * 8, n = n0 + nt * 8 + 2 * c;
-                *reinterpret_cast<float2*>(p.Wb + (vrow + r) * kDk + n) = make_float2(w[0][nt][e], w[0][nt][e + 1]);
-                *reinterpret_cast<float2*>(p.Ub + (vrow + r) * kDv + n) = make_float2(u[0][nt][e], u[0][nt][e + 1]);
+                *reinterpret_cast<float2*>(p.Ub + (vrow + r) * kDv + n) = make_float2(u[nt][e], u[nt][e + 1]);
             }
     }
 }
@@ -335,22 +370,23 @@ __global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParam
 // ---------------------------------------------------------------- the recurrence over chunks
 
 struct ChainSmem {
-    float w[kC][kLd], q[kC][kLd], k[kC][kLd];  // this chunk's W, Q, K
-    float u[kC][kDvb + 4];                     // U columns of this block
-    float m[kC][kC + 4];                       // M
-    float lc[2][kC];                           // in-chunk cumulative log decay, by chunk parity
-    float s[kDk][kDvb + 1];                    // state block (fp32 master)
-    float d[kC][kDvb + 1];                     // corrected values D of the chunk
+    __half whi[kC][kP], wlo[kC][kP];          // W[t][d]
+    __half qhi[kC][kP], qlo[kC][kP];          // Q[t][d]
+    __half khi[kC][kP], klo[kC][kP];          // K[i][d]
+    __half mhi[kC][kPc], mlo[kC][kPc];        // M[t][i]
+    float u[kC][kDvb + 4];                    // U columns of this block
+    float lc[2][kC];                          // in-chunk cumulative log decay, by chunk parity
+    float s[kDk][kDvb + 1];                   // state block S[d][j] (fp32 master)
+    __half sthi[kDvb][kP], stlo[kDvb][kP];    // S^T [j][d] hi / lo
+    __half dthi[kDvb][kPc], dtlo[kDvb][kPc];  // D^T [j][t]
+    __half ethi[kDvb][kPc], etlo[kDvb][kPc];  // (diag(e^{lc_C - lc}) D)^T
 };
 
 // cp.async of this chunk's W, Q, U columns and lc (read by the [W; Q] S product and D = U - W S)
 __device__ __forceinline__ void chain_load_wqu(ChainSmem& sm, const GdnPrefillParams& p, long long krow, long long vrow,
                                                int j0, int par, int tid) {
-    for (int i = tid; i < kC * (kDk / 4); i += 256) {
-        const int r = i / (kDk / 4), cv = i % (kDk / 4);
-        cp_async_16(smem_u32(&sm.w[r][cv * 4]), p.Wb + (vrow + r) * kDk + cv * 4, 16);
-        cp_async_16(smem_u32(&sm.q[r][cv * 4]), p.qb + (krow + r) * kDk + cv * 4, 16);
-    }
+    cp_tile_hl(&sm.whi[0][0], &sm.wlo[0][0], kP, p.wh + vrow * kDk, p.v_plane, kC, kDk, tid, 256);
+    cp_tile_hl(&sm.qhi[0][0], &sm.qlo[0][0], kP, p.qh + krow * kDk, p.q_plane, kC, kDk, tid, 256);
     for (int i = tid; i < kC * (kDvb / 4); i += 256) {
         const int r = i / (kDvb / 4), cv = i % (kDvb / 4);
         cp_async_16(smem_u32(&sm.u[r][cv * 4]), p.Ub + (vrow + r) * kDv + j0 + cv * 4, 16);
@@ -361,14 +397,8 @@ __device__ __forceinline__ void chain_load_wqu(ChainSmem& sm, const GdnPrefillPa
 // cp.async of this chunk's M and K (read by Y = ... + M D and the state update)
 __device__ __forceinline__ void chain_load_mk(ChainSmem& sm, const GdnPrefillParams& p, long long krow, long long vrow,
                                               int tid) {
-    for (int i = tid; i < kC * (kDk / 4); i += 256) {
-        const int r = i / (kDk / 4), cv = i % (kDk / 4);
-        cp_async_16(smem_u32(&sm.k[r][cv * 4]), p.kb + (krow + r) * kDk + cv * 4, 16);
-    }
-    for (int i = tid; i < kC * (kC / 4); i += 256) {
-        const int r = i / (kC / 4), cv = i % (kC / 4);
-        cp_async_16(smem_u32(&sm.m[r][cv * 4]), p.Mb + (vrow + r) * kC + cv * 4, 16);
-    }
+    cp_tile_hl(&sm.khi[0][0], &sm.klo[0][0], kP, p.kh + krow * kDk, p.q_plane, kC, kDk, tid, 256);
+    cp_tile_hl(&sm.mhi[0][0], &sm.mlo[0][0], kPc, p.mh + vrow * kC, p.m_plane, kC, kC, tid, 256);
     cp_async_commit();
 }
 
@@ -382,7 +412,12 @@ __global__ void __launch_bounds__(256) gdn_pf_chain_kernel(const GdnPrefillParam
     const int kh = h / (p.Hv / p.Hk);
     const int seq = p.seq_ids ? p.seq_ids[b] : b;
     float* S = p.state + ((long long)seq * p.Hv + h) * kDk * kDv;
-    for (int i = tid; i < kDk * kDvb; i += 256) sm.s[i / kDvb][i % kDvb] = S[(long long)(i / kDvb) * kDv + j0 + i % kDvb];
+    for (int i = tid; i < kDk * kDvb; i += 256) {
+        const int d = i / kDvb, jj = i % kDvb;
+        const float x = S[(long long)d * kDv + j0 + jj];
+        sm.s[d][jj] = x;
+        split_store(&sm.sthi[jj][d], &sm.stlo[jj][d], x);
+    }
     const int nC = p.T_pad / kC;
     const long long krow0 = ((long long)b * p.Hk + kh) * p.T_pad;
     const long long vrow0 = ((long long)b * p.Hv + h) * p.T_pad;
@@ -394,20 +429,30 @@ __global__ void __launch_bounds__(256) gdn_pf_chain_kernel(const GdnPrefillParam
         const int par = ci & 1;
         const bool more = ci + 1 < nC;
         cp_async_wait<1>();
-        __syncthreads();  // W, Q, U, lc of this chunk (and the state block) are in shared memory
+        __syncthreads();  // W, Q, U, lc of this chunk (and S^T) are in shared memory
+        const float* lc = sm.lc[par];
+        const float lcC = lc[kC - 1];
         // [W; Q] S: warps 0-3 the W rows (-> D = U - W S), warps 4-7 the Q rows (kept for Y)
-        float ws[1][4][4] = {};
-        warp_gemm<true, true, 1, 4>(ws, r16, 0, kDk, lane,
-                                    [&](int r, int k) { return warp < 4 ? sm.w[r][k] : sm.q[r][k]; },
-                                    [&](int k, int n) { return sm.s[k][n]; });
+        float ws[4][4] = {};
+        if (warp < 4)
+            gemm16<false, false, 4>(ws, &sm.whi[0][0], &sm.wlo[0][0], kP, &sm.sthi[0][0], &sm.stlo[0][0], kP, r16, 0, kDk,
+                                    lane);
+        else
+            gemm16<false, false, 4>(ws, &sm.qhi[0][0], &sm.qlo[0][0], kP, &sm.sthi[0][0], &sm.stlo[0][0], kP, r16, 0, kDk,
+                                    lane);
         if (warp < 4) {
 #pragma unroll
-            for (int nt = 0; nt < 4; nt++)
+            for (int e = 0; e < 4; e++) {
+                const int t = r16 + g + (e >> 1) * 8;
+                const float f = expf(lcC - lc[t]);
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int r = r16 + g + (e >> 1) * 8, n = nt * 8 + 2 * c + (e & 1);
-                    sm.d[r][n] = sm.u[r][n] - ws[0][nt][e];
+                for (int nt = 0; nt < 4; nt++) {
+                    const int n = nt * 8 + 2 * c + (e & 1);
+                    const float dv = sm.u[t][n] - ws[nt][e];
+                    split_store(&sm.dthi[n][t], &sm.dtlo[n][t], dv);
+                    split_store(&sm.ethi[n][t], &sm.etlo[n][t], f * dv);
                 }
+            }
         }
         __syncthreads();  // D complete; W, Q, U free
         if (more) {
@@ -417,13 +462,11 @@ __global__ void __launch_bounds__(256) gdn_pf_chain_kernel(const GdnPrefillParam
             cp_async_wait<0>();
         }
         __syncthreads();  // M, K of this chunk are in shared memory
-        const float* lc = sm.lc[par];
-        const float lcC = lc[kC - 1];
         if (warp >= 4) {
             // Y = diag(e^lc) Q S + M D for this warp's 16 rows
-            float md[1][4][4] = {};
-            warp_gemm<true, true, 1, 4>(md, r16, 0, kC, lane, [&](int r, int k) { return sm.m[r][k]; },
-                                        [&](int k, int n) { return sm.d[k][n]; });
+            float md[4][4] = {};
+            gemm16<false, false, 4>(md, &sm.mhi[0][0], &sm.mlo[0][0], kPc, &sm.dthi[0][0], &sm.dtlo[0][0], kPc, r16, 0,
+                                    kC, lane);
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const int r = r16 + g + (e >> 1) * 8;
@@ -434,23 +477,25 @@ __global__ void __launch_bounds__(256) gdn_pf_chain_kernel(const GdnPrefillParam
 #pragma unroll
                 for (int nt = 0; nt < 4; nt++) {
                     const int n = nt * 8 + 2 * c + (e & 1);
-                    store_from_float(p.y, p.y_dtype, o + n, fmaf(gam, ws[0][nt][e], md[0][nt][e]));
+                    store_from_float(p.y, p.y_dtype, o + n, fmaf(gam, ws[nt][e], md[nt][e]));
                 }
             }
         }
         // S = e^{lc_C} S + K^T diag(e^{lc_C - lc}) D: warp -> 16 rows of d
         {
-            float kd[1][4][4] = {};
+            float kd[4][4] = {};
             const int d0 = 16 * warp;
-            warp_gemm<true, true, 1, 4>(kd, d0, 0, kC, lane, [&](int r, int k) { return sm.k[k][r]; },
-                                        [&](int k, int n) { return expf(lcC - lc[k]) * sm.d[k][n]; });
+            gemm16<true, false, 4>(kd, &sm.khi[0][0], &sm.klo[0][0], kP, &sm.ethi[0][0], &sm.etlo[0][0], kPc, d0, 0, kC,
+                                   lane);
             const float gC = expf(lcC);
 #pragma unroll
             for (int nt = 0; nt < 4; nt++)
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
                     const int r = d0 + g + (e >> 1) * 8, n = nt * 8 + 2 * c + (e & 1);
-                    sm.s[r][n] = fmaf(gC, sm.s[r][n], kd[0][nt][e]);
+                    const float x = fmaf(gC, sm.s[r][n], kd[nt][e]);
+                    sm.s[r][n] = x;
+                    split_store(&sm.sthi[n][r], &sm.stlo[n][r], x);
                 }
         }
         __syncthreads();  // S updated; M, K, D free
@@ -480,12 +525,12 @@ __global__ void __launch_bounds__(256) gdn_pf_out_kernel(const GdnPrefillParams 
         const long long orow = ((long long)b * p.n + t) * p.out_stride + (long long)h * kDv;
 #pragma unroll
         for (int e = 0; e < kDv / 32; e++) {
-            const int j = e * 32 + lane;
-            const float z = load_as_float(row, p.proj_dtype, p.C + (long long)h * kDv + j);
-            float o = __fmul_rn(__fmul_rn(v[e], rinv), p.norm_w[j]);
+            const int jj = e * 32 + lane;
+            const float z = load_as_float(row, p.proj_dtype, p.C + (long long)h * kDv + jj);
+            float o = __fmul_rn(__fmul_rn(v[e], rinv), p.norm_w[jj]);
             o = o / (1.0f + expf(-z));
             o = __fmul_rn(o, z);
-            store_from_float(p.out, p.out_dtype, orow + j, o);
+            store_from_float(p.out, p.out_dtype, orow + jj, o);
         }
     }
 }
@@ -498,14 +543,14 @@ size_t gdn_prefill_workspace_bytes(int B, int n, int Hk, int Hv, int C, bool lay
     const long long Tp = (long long)(n + kC - 1) / kC * kC;
     size_t s = 0;
     auto add = [&](size_t bytes) { s += (bytes + 255) / 256 * 256; };
-    add((size_t)B * Hk * Tp * kDk * 4);  // qb
-    add((size_t)B * Hk * Tp * kDk * 4);  // kb
-    add((size_t)B * Hv * Tp * kDv * 4);  // vb
+    add((size_t)B * Hk * Tp * kDk * 4);  // q hi + lo
+    add((size_t)B * Hk * Tp * kDk * 4);  // k hi + lo
+    add((size_t)B * Hv * Tp * kDv * 4);  // v hi + lo
     add((size_t)B * Hv * Tp * 4);        // lg
     add((size_t)B * Hv * Tp * 4);        // beta
-    add((size_t)B * Hv * Tp * kDk * 4);  // W
+    add((size_t)B * Hv * Tp * kDk * 4);  // W hi + lo
     add((size_t)B * Hv * Tp * kDv * 4);  // U
-    add((size_t)B * Hv * Tp * kC * 4);   // M
+    add((size_t)B * Hv * Tp * kC * 4);   // M hi + lo
     add((size_t)B * Hv * Tp * 4);        // lc
     if (layer) {
         add((size_t)B * n * Hv * kDv * 4);  // y
@@ -523,14 +568,17 @@ static void carve(GdnPrefillParams& p, void* ws, bool layer) {
         c += (bytes + 255) / 256 * 256;
         return r;
     };
-    p.qb = reinterpret_cast<float*>(take((size_t)p.B * p.Hk * Tp * kDk * 4));
-    p.kb = reinterpret_cast<float*>(take((size_t)p.B * p.Hk * Tp * kDk * 4));
-    p.vb = reinterpret_cast<float*>(take((size_t)p.B * p.Hv * Tp * kDv * 4));
+    p.q_plane = (long long)p.B * p.Hk * Tp * kDk;
+    p.v_plane = (long long)p.B * p.Hv * Tp * kDv;
+    p.m_plane = (long long)p.B * p.Hv * Tp * kC;
+    p.qh = reinterpret_cast<__half*>(take((size_t)p.q_plane * 4));
+    p.kh = reinterpret_cast<__half*>(take((size_t)p.q_plane * 4));
+    p.vh = reinterpret_cast<__half*>(take((size_t)p.v_plane * 4));
     p.lg = reinterpret_cast<float*>(take((size_t)p.B * p.Hv * Tp * 4));
     p.beta = reinterpret_cast<float*>(take((size_t)p.B * p.Hv * Tp * 4));
-    p.Wb = reinterpret_cast<float*>(take((size_t)p.B * p.Hv * Tp * kDk * 4));
+    p.wh = reinterpret_cast<__half*>(take((size_t)p.v_plane * 4));
     p.Ub = reinterpret_cast<float*>(take((size_t)p.B * p.Hv * Tp * kDv * 4));
-    p.Mb = reinterpret_cast<float*>(take((size_t)p.B * p.Hv * Tp * kC * 4));
+    p.mh = reinterpret_cast<__half*>(take((size_t)p.m_plane * 4));
     p.lcb = reinterpret_cast<float*>(take((size_t)p.B * p.Hv * Tp * 4));
     if (layer) {
         p.y = take((size_t)p.B * p.n * p.Hv * kDv * 4);

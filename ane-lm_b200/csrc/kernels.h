@@ -140,15 +140,17 @@ struct GdnPrefillParams {
     void* y;
     int y_dtype;
     long long y_stride;
-    // workspace (carved by the launcher)
-    float* qb;             // [B][Hk][T_pad][dk]
-    float* kb;
-    float* vb;             // [B][Hv][T_pad][dv]
+    // workspace (carved by the launcher); tensor-core operands as an fp16 hi plane followed by a
+    // lo plane (x = hi + lo)
+    __half* qh;            // [B][Hk][T_pad][dk], lo plane at + q_plane
+    __half* kh;
+    __half* vh;            // [B][Hv][T_pad][dv], lo plane at + v_plane
+    long long q_plane, v_plane, m_plane;
     float* lg;             // [B][Hv][T_pad]
     float* beta;
-    float* Wb;             // [B][Hv][T_pad][dk]
+    __half* wh;            // [B][Hv][T_pad][dk], lo plane at + v_plane
     float* Ub;             // [B][Hv][T_pad][dv]
-    float* Mb;             // [B][Hv][T_pad][64]
+    __half* mh;            // [B][Hv][T_pad][64], lo plane at + m_plane
     float* lcb;            // [B][Hv][T_pad]
     float* ring_snap;      // [B][C][3]
     int* pos_snap;         // [B][Hk]
