@@ -14,7 +14,8 @@
 // fp32 state S[k][v].  The delta rule is column-separable (column j of S needs
 // only k, q and v[j]), so every CTA streams its 128 x W block of S (W = 128 /
 // NSPLIT) from HBM into registers once, updates it and writes it back once; the
-// loads are issued first so their latency overlaps the prologue.
+// block's loads are issued right after the conv inputs', so the conv, the q/k
+// exchange and the norms overlap its transfer.
 //
 // Conv ring ownership.  Each conv channel of the row belongs to exactly one CTA
 // of exactly one cluster: the cluster of kh owns the 256 q/k channels of kh
@@ -141,46 +142,84 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
     const int key_total = p.Hk * kDk;
     const int j0 = cb * W;
 
-    // ---- 1. state block loads first (HBM latency overlaps the prologue) ----
+    // ---- 1. loads: the small inputs of the conv / gates first, then the 32 KB state block ----
+    // Requests are served roughly in issue order, so small loads issued after the state block
+    // would wait for it; issued first, the conv, the q/k exchange and the norms run while the
+    // state block streams in, and only the delta rule waits for it.
     const int cq = tid % QPR, rg = tid / QPR;
     float* Sbase = p.ssm + (((long long)seq * p.Hv + h) * kDk) * kDv + j0 + 4 * cq;
+    const char* proj_row = reinterpret_cast<const char*>(p.proj) +
+                           (long long)b * p.proj_stride * dtype_bytes(p.proj_dtype);
+    int* pos_ptr = p.conv_pos + (long long)seq * p.Hk + kh;
+    float* ring = p.conv + (long long)seq * C * 3;
+    const int n = *pos_ptr;                     // ring position (reference conv_pos)
+    // all three ring slots are loaded (the position selects among them once it arrives)
+    struct ConvIn { float4 w; float r0, r1, r2, x; };
+    auto conv_load = [&](int c) -> ConvIn {
+        ConvIn ci;
+        ci.w = *reinterpret_cast<const float4*>(p.conv_w + (long long)c * 4);
+        ci.r0 = ring[c * 3];
+        ci.r1 = ring[c * 3 + 1];
+        ci.r2 = ring[c * 3 + 2];
+        ci.x = load_as_float(proj_row, p.proj_dtype, c);
+        return ci;
+    };
+    constexpr int NV = (W + THREADS - 1) / THREADS;
+    ConvIn vin[NV], qkin[NU];
+    float zin[NV], nwin[NV];
+#pragma unroll
+    for (int u = 0; u < NV; u++) {
+        const int i = tid + u * THREADS;
+        if (i < W) {
+            vin[u] = conv_load(2 * key_total + h * kDv + j0 + i);
+            zin[u] = load_as_float(proj_row, p.proj_dtype, C + (long long)h * kDv + j0 + i);
+            nwin[u] = p.norm_w[j0 + i];
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < NU; u++) {
+        const int i = tid + u * THREADS;
+        if (i < QKP) {
+            const int ci = rank * QKP + i;  // 0..255 within (q | k) of key head kh
+            qkin[u] = conv_load((ci < kDk) ? kh * kDk + ci : key_total + kh * kDk + (ci - kDk));
+        }
+    }
+    float ga = 0.f, gb = 0.f;
+    if (tid == 0) {
+        ga = load_as_float(proj_row, p.proj_dtype, C + (long long)p.Hv * kDv + h);
+        gb = load_as_float(proj_row, p.proj_dtype, C + (long long)p.Hv * kDv + p.Hv + h);
+    }
     float4 S[NR];
 #pragma unroll
     for (int i = 0; i < NR; i++) S[i] = __ldcs(reinterpret_cast<const float4*>(Sbase + (long long)(rg + RPP * i) * kDv));
 
-    const char* proj_row = reinterpret_cast<const char*>(p.proj) +
-                           (long long)b * p.proj_stride * dtype_bytes(p.proj_dtype);
-    int* pos_ptr = p.conv_pos + (long long)seq * p.Hk + kh;
-    const int n = *pos_ptr;                     // ring position (reference conv_pos)
     int p1 = n + 1;
     if (p1 == 3) p1 = 0;
     int p2 = p1 + 1;
     if (p2 == 3) p2 = 0;
-    float* ring = p.conv + (long long)seq * C * 3;
-
     // conv1d_update (cpu_ops.cpp:95-110) + SiLU (cpu_ops.cpp:6-13) of one channel.  The new input x
-    // goes into ring slot n only after the last cluster barrier (a barrier's release would
-    // otherwise wait for that global store to be acknowledged).
-    auto conv_ch = [&](int c, float& x) -> float {
-        const float4 w = *reinterpret_cast<const float4*>(p.conv_w + (long long)c * 4);
-        const float s0 = ring[c * 3 + n], s1 = ring[c * 3 + p1], s2 = ring[c * 3 + p2];
-        x = load_as_float(proj_row, p.proj_dtype, c);
-        const float y = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(s0, w.x), __fmul_rn(s1, w.y)), __fmul_rn(s2, w.z)),
-                                  __fmul_rn(x, w.w));
+    // goes into ring slot n only after the exchanges (a barrier's release would otherwise wait for
+    // that global store to be acknowledged).
+    auto conv_ch = [&](const ConvIn& ci) -> float {
+        const float s0 = n == 0 ? ci.r0 : n == 1 ? ci.r1 : ci.r2;
+        const float s1 = p1 == 0 ? ci.r0 : p1 == 1 ? ci.r1 : ci.r2;
+        const float s2 = p2 == 0 ? ci.r0 : p2 == 1 ? ci.r1 : ci.r2;
+        const float y = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(s0, ci.w.x), __fmul_rn(s1, ci.w.y)), __fmul_rn(s2, ci.w.z)),
+                                  __fmul_rn(ci.x, ci.w.w));
         return y / (1.0f + expf(-y));
     };
 
     // ---- 2. this CTA's v / z columns and its slice of the q/k channels ----
-    constexpr int NV = (W + THREADS - 1) / THREADS;
     float xv[NV], xqk[NU];
 #pragma unroll
     for (int u = 0; u < NV; u++) {
         const int i = tid + u * THREADS;
         xv[u] = 0.f;
         if (i < W) {
-            v_s[i] = conv_ch(2 * key_total + h * kDv + j0 + i, xv[u]);
-            z_s[i] = load_as_float(proj_row, p.proj_dtype, C + (long long)h * kDv + j0 + i);
-            w_s[i] = p.norm_w[j0 + i];
+            v_s[i] = conv_ch(vin[u]);
+            xv[u] = vin[u].x;
+            z_s[i] = zin[u];
+            w_s[i] = nwin[u];
         }
     }
     float qk_mine[NU];
@@ -190,16 +229,13 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
         qk_mine[u] = 0.f;
         xqk[u] = 0.f;
         if (i < QKP) {
-            const int ci = rank * QKP + i;  // 0..255 within (q | k) of key head kh
-            const int c = (ci < kDk) ? kh * kDk + ci : key_total + kh * kDk + (ci - kDk);
-            qk_mine[u] = conv_ch(c, xqk[u]);
+            qk_mine[u] = conv_ch(qkin[u]);
+            xqk[u] = qkin[u].x;
         }
     }
     if (tid == 0) {
-        const float a = load_as_float(proj_row, p.proj_dtype, C + (long long)p.Hv * kDv + h);
-        const float bb = load_as_float(proj_row, p.proj_dtype, C + (long long)p.Hv * kDv + p.Hv + h);
-        scal[0] = sigmoid_ref(bb);                                     // qwen3_5.cpp:897
-        scal[1] = expf(-p.A[h] * softplus_ref(a + p.dt_bias[h]));      // qwen3_5.cpp:898
+        scal[0] = sigmoid_ref(gb);                                     // qwen3_5.cpp:897
+        scal[1] = expf(-p.A[h] * softplus_ref(ga + p.dt_bias[h]));     // qwen3_5.cpp:898
     }
     cluster_wait();  // every CTA of the cluster has initialised its barriers
 #pragma unroll
@@ -346,6 +382,7 @@ __global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodePara
         store_from_float(p.out, p.out_dtype, orow + i, o);
     }
 }
+
 
 template <int RATIO, int NSPLIT, int THREADS>
 int launch_cfg(const GdnDecodeParams& p, int n_rows, cudaStream_t stream) {

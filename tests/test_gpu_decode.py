@@ -210,6 +210,39 @@ def test_deltanet_batched():
     np.testing.assert_array_equal(ssm, states[2].ssm)
 
 
+@pytest.mark.parametrize("delta_mode", [ab.DELTA_CPUOPS, ab.DELTA_HF])
+def test_deltanet_batched_gqa(delta_mode):
+    """A larger batch (40 rows x 16 key heads = 640 clusters) in the 4B GQA shape, 3 steps, rows in
+    shuffled order, both delta-rule orders: every row's outputs / state / conv ring / position vs
+    the oracle."""
+    rng = np.random.default_rng(40 + delta_mode)
+    shape = gdn_shape(16, 32)
+    n_seq, steps = 40, 3
+    order = list(rng.permutation(n_seq))
+    proj, conv_w, A, dt_bias, norm_w = gdn_inputs(rng, shape, steps * n_seq)
+    proj = proj.reshape(steps, n_seq, -1)
+    C = conv_w.shape[0]
+    states = [po.DeltaState((0.1 * rng.standard_normal((32, 128, 128))).astype(np.float32),
+                            rng.standard_normal((C, 3)).astype(np.float32), s % 3) for s in range(n_seq)]
+    var = po.make_variant(delta_hf=int(delta_mode == ab.DELTA_HF))
+    with gdn_ctx(shape, max_seqs=n_seq, delta_mode=delta_mode) as ctx:
+        ctx.set_deltanet_weights(0, conv_w, A, dt_bias, norm_w)
+        for s, st in enumerate(states):
+            ctx.deltanet_state_import(0, s, st.ssm, st.conv, st.conv_pos)
+        plan = ctx.plan(order)
+        got = torch.stack([ctx.deltanet_decode(plan, 0, dev(proj[t], torch.float16)) for t in range(steps)])
+        got = got.cpu().numpy()
+        exported = [ctx.deltanet_state_export(0, s) for s in range(n_seq)]
+        plan.close()
+    for i, s in enumerate(order):
+        want = po.deltanet_tokens("oracle", shape, var, conv_w, A, dt_bias, norm_w, states[s], proj[:, i])
+        assert_close(got[:, i], want, what=f"row {i} (seq {s})")
+        ssm, conv, pos = exported[s]
+        assert_close(ssm, states[s].ssm, what=f"state {s}")
+        np.testing.assert_array_equal(conv, states[s].conv)
+        assert pos == states[s].conv_pos
+
+
 # ---------------------------------------------------------------- variants
 
 def test_deltanet_hf_variant():
