@@ -96,7 +96,9 @@ __device__ __forceinline__ bool mbar_wait0(uint64_t* bar, int* err) {
 }
 
 template <int RATIO, int NSPLIT, int THREADS>
-__global__ void __launch_bounds__(THREADS) gdn_decode_kernel(const GdnDecodeParams p) {
+// 128-thread CTAs are held to 96 registers: at 102 the per-warp allocation rounds to 3,328 and
+// only four CTAs fit an SM, at 96 five do (a 20-byte spill).
+__global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_kernel(const GdnDecodeParams p) {
     constexpr int CS = RATIO * NSPLIT;     // CTAs per cluster
     constexpr int W = kDv / NSPLIT;        // value columns per CTA
     constexpr int QPR = W / 4;             // float4 quads per row segment
