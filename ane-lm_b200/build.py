@@ -33,7 +33,7 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompil
 
 def _newest_header() -> float:
     hs = glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
-        glob.glob(os.path.join(INCLUDE, "*.h"))
+        glob.glob(os.path.join(INCLUDE, "**", "*.h"), recursive=True)
     return max((os.path.getmtime(h) for h in hs), default=0.0)
 
 

@@ -2,6 +2,7 @@
 point include/anelm_b200.h declares, validates arguments before touching a GPU,
 and fails loudly (no CPU fallback) when no sm_100 device is present."""
 import ctypes
+import os
 
 import pytest
 
@@ -47,3 +48,32 @@ def test_no_cpu_fallback():
     h = ctypes.c_void_p()
     rc = lib().anelm_create(ctypes.byref(c), 0, ctypes.byref(h))
     assert rc == ab._lib.ERR_CUDA and not h.value
+
+
+def test_cpu_ops_compat_exports_and_links(tmp_path):
+    """include/cpu_ops_compat/cpu_ops.h declares core/cpu_ops.h's functions (namespace ane_lm);
+    the library exports each with that signature, and the oracle's layer glue, written against
+    core/cpu_ops.h, compiles and links against the shim unchanged (no GPU needed)."""
+    import re
+    import shutil
+    import subprocess
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    hdr = open(os.path.join(repo, "include", "cpu_ops_compat", "cpu_ops.h")).read()
+    names = [n for n in re.findall(r"^void\s+(\w+)\s*\(", hdr, re.M)]
+    assert len(names) == 11, names
+    nm = shutil.which("nm")
+    if nm:
+        syms = subprocess.run([nm, "-DC", ab.LIB_PATH], capture_output=True, text=True).stdout
+        for n in names:
+            assert re.search(rf" T ane_lm::{n}\(", syms), n
+        assert "ane_lm::gqa_attention(float*, float const*, float const*, float const*, int, int, int, int, int, int, int)" in syms
+    gxx = shutil.which("g++")
+    if not gxx:
+        pytest.skip("no g++")
+    libdir = os.path.dirname(ab.LIB_PATH)
+    out = tmp_path / "libshim_glue.so"
+    r = subprocess.run([gxx, "-O1", "-fPIC", "-shared", "-std=c++17", f"-I{repo}/include/cpu_ops_compat",
+                        f"-I{repo}/oracle", f"{repo}/oracle/ref_glue.cpp", f"-L{libdir}", "-lanelm_b200",
+                        f"-Wl,-rpath,{libdir}", "-Wl,--no-undefined", "-o", str(out)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-3000:]
