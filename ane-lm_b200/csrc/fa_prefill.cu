@@ -7,13 +7,12 @@
 // tokens [0, t], sigmoid gate.  The result is the same set of outputs, computed
 // as one causal attention.
 //
-// Three launches:
+// Two launches:
 //   fa_prefill_prep_vec_kernel  per token: RMSNorm + RoPE of the q and k heads (same arithmetic
 //                           as the decode prologue), fp16 Q [B][Hq][n_pad][D], K and V
 //                           [B][Hkv][n_pad][D], sigmoid(gate) for the epilogue, and the ring
 //                           append (slot t, len = n, start = 0).  Warp per 256-element segment,
 //                           16-byte lanes (fa_prefill_prep_kernel: same work for any shape);
-//   transpose_v_kernel      V -> V^T [B][Hkv][D][n_pad] so both MMA operands of P V are K-major;
 //   fa_prefill_kernel       one CTA per (128-row query tile, q head, sequence), longest causal
 //                           tiles first, 11 warps:
 //     warps 0-7  softmax: warps w and w+4 share TMEM lanes [32(w%4), +32) and take keys
@@ -24,10 +23,10 @@
 //     warp 8  TMA producer: Q (4 boxes), then one 64 KB K tile per key tile, then the
 //             sigmoid(gate) tile into the K buffer once the last Q K^T has read it;
 //     warp 9  MMA issuer (one thread): S = Q K^T (M=128, N=128, K=256) into one of two
-//             128-column TMEM S buffers, O += P V^T with A = P from TMEM (M=128, N=256,
-//             K=128) into the 256-column O accumulator, so Q K^T of tile j+1 overlaps the
-//             softmax of tile j;
-//     warp 10 TMA producer: one 64 KB V^T tile per key tile.
+//             128-column TMEM S buffers, O += P V with A = P from TMEM and B = V read
+//             MN-major from its natural [key][d] layout (M=128, N=256, K=128) into the
+//             256-column O accumulator, so Q K^T of tile j+1 overlaps the softmax of tile j;
+//     warp 10 TMA producer: one 64 KB V tile per key tile.
 //   Epilogue: O / l * sigmoid(gate) into 128B-swizzled tiles in the idle Q buffer and four TMA
 //   tile stores (a 3D tensor map clips rows past the sequence end); other output dtypes /
 //   alignments store rows from a staged fp32 copy.  All MMAs are kind::f16 (fp16 operands,
@@ -52,7 +51,7 @@ constexpr int kBN = 128;   // keys per tile (Q K^T at N = 128: a tcgen05.mma cos
 constexpr int kD = 256;    // head dim of this kernel
 constexpr int kQBytes = kBM * kD * 2;        // 64 KB: 4 boxes of 128 rows x 64 d
 constexpr int kKBytes = kBN * kD * 2;        // 64 KB: 4 boxes of 128 keys x 64 d
-constexpr int kVBytes = kD * kBN * 2;        // 64 KB: V^T, 2 boxes of 256 d x 64 keys
+constexpr int kVBytes = kD * kBN * 2;        // 64 KB: V, 4 boxes of 128 keys x 64 d (MN-major B of P V)
 constexpr int kSmemTiles = kQBytes + kKBytes + kVBytes;
 constexpr int kSmemBytes = kSmemTiles + 256 + 6 * 128 * 4 + 1024;  // barriers, softmax exchange, alignment
 constexpr int kSoftmaxWarps = 8;             // two per TMEM lane quadrant, 64 keys of each tile each
@@ -335,18 +334,6 @@ __global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPre
     }
 }
 
-// V [BH][n_pad][kD] -> V^T [BH][kD][n_pad], 32 x 32 tiles.
-__global__ void transpose_v_kernel(const __half* __restrict__ v, __half* __restrict__ vt, int n_pad) {
-    __shared__ __half tile[32][33];
-    const int bh = blockIdx.z;
-    const int t0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-    const __half* src = v + (long long)bh * n_pad * kD;
-    __half* dst = vt + (long long)bh * kD * n_pad;
-    for (int r = threadIdx.y; r < 32; r += 8) tile[r][threadIdx.x] = src[(long long)(t0 + r) * kD + d0 + threadIdx.x];
-    __syncthreads();
-    for (int r = threadIdx.y; r < 32; r += 8) dst[(long long)(d0 + r) * n_pad + t0 + threadIdx.x] = tile[threadIdx.x][r];
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG,
@@ -386,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == kWarpK || warp == kWarpV) {
-        // ---------------- TMA producers: one warp streams Q then K (then the gate tile), one streams V^T ----------------
+        // ---------------- TMA producers: one warp streams Q then K (then the gate tile), one streams V ----------------
         if (lane == 0 && nT > 0) {
             const int krow0 = (b * p.Hkv + kvh) * p.n_pad;
             const int vrow0 = (b * p.Hkv + kvh) * kD;
@@ -416,8 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < nT; j++) {
                     if (j >= 1) tc::mbar_wait(&bars[V_EMPTY], (j - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                     tc::mbar_arrive_expect_tx(&bars[V_FULL], kVBytes);
-                    for (int kb = 0; kb < 2; kb++)
-                        tc::tma_load_2d(sV + kb * (kD * 128), &tmV, &bars[V_FULL], j * kBN + kb * 64, vrow0);
+                    for (int kb = 0; kb < 4; kb++)
+                        tc::tma_load_2d(sV + kb * (kBN * 128), &tmV, &bars[V_FULL], kb * 64, krow0 + j * kBN);
                 }
             }
         }
@@ -426,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- MMA issuer ----------------
         if (lane == 0 && nT > 0) {
             constexpr uint32_t id_qk = tc::idesc_f16_f32(kBM, kBN);
-            constexpr uint32_t id_pv = tc::idesc_f16_f32(kBM, kD);
+            constexpr uint32_t id_pv = tc::idesc_f16_f32_bmn(kBM, kD);  // V[key][d]: d contiguous
             const uint32_t aQ = (uint32_t)__cvta_generic_to_shared(sQ);
             const uint32_t aK = (uint32_t)__cvta_generic_to_shared(sK);
             const uint32_t aV = (uint32_t)__cvta_generic_to_shared(sV);
@@ -451,11 +438,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc::mbar_wait(&bars[P_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::mbar_wait(&bars[V_FULL], j & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::tc_fence_after();
+                // A = P from TMEM (16 keys = 8 columns per step); B = V, MN-major: 16 key rows of the
+                // four 64-d boxes (boxes kBN * 128 bytes apart, 8-row groups 1024 bytes apart)
 #pragma unroll
-                for (int ks = 0; ks < kBN / 16; ks++)  // A = P from TMEM: 16 keys = 8 columns per step
+                for (int ks = 0; ks < kBN / 16; ks++)
                     tc::mma_f16_ts(tmem + kOCol, tmem + s * kBN + ks * 8,
-                                   tc::desc_kmajor_sw128(aV + (ks >> 2) * (kD * 128) + (ks & 3) * 32), id_pv,
-                                   (j > 0) || (ks > 0));
+                                   tc::desc_sw128(aV + ks * 16 * 128, kBN * 128, 1024), id_pv, (j > 0) || (ks > 0));
                 tc::mma_commit(&bars[PV_DONE + s]);
                 tc::mma_commit(&bars[V_EMPTY]);
             };
@@ -687,8 +675,8 @@ bool make_map_rows(CUtensorMap* m, int dtype, const void* base, uint64_t cols, u
 
 size_t fa_prefill_workspace_bytes(int B, int n, int Hq, int Hkv, int head_dim) {
     const long long n_pad = (n + kBM - 1) / kBM * kBM;
-    // fp16 Q, K, V, V^T and sigmoid(gate) [B][n][Hq][D]
-    return (size_t)B * n_pad * head_dim * 2 * (2 * (size_t)Hq + 3 * (size_t)Hkv);
+    // fp16 Q, K, V and sigmoid(gate) [B][n][Hq][D]
+    return (size_t)B * n_pad * head_dim * 2 * (2 * (size_t)Hq + 2 * (size_t)Hkv);
 }
 
 int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream) {
@@ -699,17 +687,16 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
     p.Qh = ws;
     p.Kh = ws + nq;
     p.Vh = p.Kh + nk;
-    p.Vt = p.Vh + nk;
     p.SG = nullptr;
     CUtensorMap mQ, mK, mV;
     if (!make_map(&mQ, p.Qh, (uint64_t)p.B * p.Hq * p.n_pad, kD, kBM) ||
         !make_map(&mK, p.Kh, (uint64_t)p.B * p.Hkv * p.n_pad, kD, kBN) ||
-        !make_map(&mV, p.Vt, (uint64_t)p.B * p.Hkv * kD, p.n_pad, kD))
+        !make_map(&mV, p.Vh, (uint64_t)p.B * p.Hkv * p.n_pad, kD, kBN))
         return ANELM_ERR_CUDA;
     // TMA epilogue: 16-bit output with a 16-byte aligned base and row stride; sigmoid(gate) as fp16
-    // [B][n][Hq * D] after V^T in the workspace
+    // [B][n][Hq * D] after V in the workspace
     CUtensorMap mG = mQ, mO = mQ;
-    __half* sg = p.Vt + nk;
+    __half* sg = p.Vh + nk;
     p.tma_epilogue = (p.out_dtype == ANELM_BF16 || p.out_dtype == ANELM_F16) && ((uintptr_t)p.out % 16 == 0) &&
                      (p.out_stride % 8 == 0) &&
                      make_map_rows(&mO, p.out_dtype, p.out, (uint64_t)p.Hq * kD, p.n, p.B, p.out_stride) &&
@@ -725,7 +712,6 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
             cudaFuncSetAttribute(fa_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
         fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
     }
-    transpose_v_kernel<<<dim3(p.n_pad / 32, kD / 32, p.B * p.Hkv), dim3(32, 8), 0, stream>>>(p.Vh, p.Vt, p.n_pad);
     cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;

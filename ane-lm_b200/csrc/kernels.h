@@ -93,7 +93,6 @@ struct FaPrefillParams {
     __half* Qh;            // [B][Hq][n_pad][D]   (workspace)
     __half* Kh;            // [B][Hkv][n_pad][D]
     __half* Vh;            // [B][Hkv][n_pad][D]
-    __half* Vt;            // [B][Hkv][D][n_pad]
     __half* SG;            // [B][n][Hq * D] sigmoid(gate), written by the prep kernel for the TMA epilogue
     __half* k_pool;        // ring pools of the layer (nullptr: no append)
     __half* v_pool;

@@ -227,6 +227,19 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
     return d;
 }
 
+// The same descriptor with explicit byte offsets: for an MN-major operand (MN contiguous) with
+// the 128-byte swizzle, atoms of 64 MN-elements x 8 K-rows; LBO = offset between atoms along
+// MN, SBO = offset between 8-row groups along K.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
 // Instruction descriptor for kind::f16: fp16 A and B (both K-major), fp32 D, M x N.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
     return (1u << 4)                          // D format: F32
@@ -234,6 +247,8 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
            | ((uint32_t)(N >> 3) << 17)       // N >> 3
            | ((uint32_t)(M >> 4) << 24);      // M >> 4
 }
+// The same with B MN-major (transpose-B bit): B[k][n] stored with n contiguous.
+__host__ __device__ constexpr uint32_t idesc_f16_f32_bmn(int M, int N) { return idesc_f16_f32(M, N) | (1u << 16); }
 
 }  // namespace tc
 }  // namespace anelm
