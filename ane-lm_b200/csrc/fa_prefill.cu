@@ -376,7 +376,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- TMA producers: one warp streams Q then K (then the gate tile), one streams V ----------------
         if (lane == 0 && nT > 0) {
             const int krow0 = (b * p.Hkv + kvh) * p.n_pad;
-            const int vrow0 = (b * p.Hkv + kvh) * kD;
             if (warp == kWarpK) {
                 tc::prefetch_tmap(&tmQ);
                 tc::prefetch_tmap(&tmK);

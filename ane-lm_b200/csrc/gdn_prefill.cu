@@ -81,23 +81,17 @@ __device__ __forceinline__ void ldb2_t(uint32_t (&b)[4], const __half* base, int
     const int mat = lane >> 3, i = lane & 7;
     ldmatrix_x4_trans(smem_u32(base + (k0 + i + (mat & 1) * 8) * pitch + n0 + (mat >> 1) * 8), b[0], b[1], b[2], b[3]);
 }
-// d += (ah + al)(bh + bl) without the lo*lo term
-__device__ __forceinline__ void mma3(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0,
-                                     uint32_t bh1, uint32_t bl0, uint32_t bl1) {
-    mma_16816(d, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
-    mma_16816(d, al[0], al[1], al[2], al[3], bh0, bh1);
-    mma_16816(d, ah[0], ah[1], ah[2], ah[3], bl0, bl1);
-}
-
 // acc[NT] (16 rows x 8 NT columns) += A[r0.., 0..K) B[0..K, n0..); A and B as hi / lo tiles.
-// TA: A stored transposed; TB: B stored [k][n] (else [n][k]).
+// TA: A stored transposed; TB: B stored [k][n] (else [n][k]).  Per k-step all fragments are
+// loaded first and each of the three product terms is issued across the NT accumulators in
+// turn, so consecutive MMAs into one accumulator are NT instructions apart.
 template <bool TA, bool TB, int NT>
 __device__ __forceinline__ void gemm16(float (&acc)[NT][4], const __half* ahi, const __half* alo, int pa,
                                        const __half* bhi, const __half* blo, int pb, int r0, int n0, int K, int lane) {
     static_assert(NT % 2 == 0, "n-tiles come in pairs");
 #pragma unroll
     for (int k0 = 0; k0 < K; k0 += 16) {
-        uint32_t ah[4], al[4];
+        uint32_t ah[4], al[4], bh[NT / 2][4], bl[NT / 2][4];
         if (TA) {
             lda_t(ah, ahi, pa, r0, k0, lane);
             lda_t(al, alo, pa, r0, k0, lane);
@@ -107,17 +101,23 @@ __device__ __forceinline__ void gemm16(float (&acc)[NT][4], const __half* ahi, c
         }
 #pragma unroll
         for (int np = 0; np < NT / 2; np++) {
-            uint32_t bh[4], bl[4];
             if (TB) {
-                ldb2_t(bh, bhi, pb, n0 + 16 * np, k0, lane);
-                ldb2_t(bl, blo, pb, n0 + 16 * np, k0, lane);
+                ldb2_t(bh[np], bhi, pb, n0 + 16 * np, k0, lane);
+                ldb2_t(bl[np], blo, pb, n0 + 16 * np, k0, lane);
             } else {
-                ldb2(bh, bhi, pb, n0 + 16 * np, k0, lane);
-                ldb2(bl, blo, pb, n0 + 16 * np, k0, lane);
+                ldb2(bh[np], bhi, pb, n0 + 16 * np, k0, lane);
+                ldb2(bl[np], blo, pb, n0 + 16 * np, k0, lane);
             }
-            mma3(acc[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
-            mma3(acc[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
         }
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+            mma_16816(acc[nt], ah[0], ah[1], ah[2], ah[3], bh[nt / 2][2 * (nt & 1)], bh[nt / 2][2 * (nt & 1) + 1]);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+            mma_16816(acc[nt], al[0], al[1], al[2], al[3], bh[nt / 2][2 * (nt & 1)], bh[nt / 2][2 * (nt & 1) + 1]);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+            mma_16816(acc[nt], ah[0], ah[1], ah[2], ah[3], bl[nt / 2][2 * (nt & 1)], bl[nt / 2][2 * (nt & 1) + 1]);
     }
 }
 
