@@ -149,6 +149,36 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
 #pragma unroll
     for (int i = 0; i < MT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
+    // ---- 0. the first K / V tiles start loading now: they depend only on the ring metadata, so
+    // their latency overlaps the prologue (projection loads, norms, RoPE) ----
+    const int t_new = p.append ? len1 - 1 : -1;  // logical index of the new token
+    const __half* kpool = p.k_pool;
+    const __half* vpool = p.v_pool;
+    auto issue = [&](int j) {
+        const int stage = j % kStages;
+        const int tile = j >> 1;
+        const __half* pool = (j & 1) ? vpool : kpool;
+        const uint32_t sbase = smem_u32(smem + S::tiles + stage * S::tile_bytes);
+        for (int idx = tid; idx < kTile * CPR; idx += kThreads) {
+            const int r = idx / CPR, ch = idx - r * CPR;
+            const int t = t_begin + tile * kTile + r;
+            const bool valid = (t < t_end) && (t < n_old);
+            int s = start1 + t;
+            if (s >= cap) s -= cap;
+            const __half* src = pool + ((base + (valid ? s : 0)) * Hkv + kvh) * (long long)D + ch * 8;
+            const uint32_t dst = sbase + (uint32_t)(r * D + ((ch ^ (r & 7)) * 8)) * 2u;
+            cp_async_16(dst, src, valid ? 16 : 0);
+        }
+    };
+    const int n_jobs = 2 * n_tiles;
+    if (n_tok > 0) {
+#pragma unroll
+        for (int j = 0; j < kStages - 1; j++) {
+            if (j < n_jobs) issue(j);
+            cp_async_commit();
+        }
+    }
+
     if (n_tok > 0) {
         // ---- 1. prologue: queries, new k/v ----
         for (int idx = tid; idx < kGP * D; idx += kThreads) {
@@ -261,32 +291,6 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
         }
         for (int idx = tid; idx < 2 * kGP * kPRow; idx += kThreads) P_s[idx] = __float2half_rn(0.f);
 
-        const int t_new = p.append ? len1 - 1 : -1;  // logical index of the new token
-        const __half* kpool = p.k_pool;
-        const __half* vpool = p.v_pool;
-        auto issue = [&](int j) {
-            const int stage = j % kStages;
-            const int tile = j >> 1;
-            const __half* pool = (j & 1) ? vpool : kpool;
-            const uint32_t sbase = smem_u32(smem + S::tiles + stage * S::tile_bytes);
-            for (int idx = tid; idx < kTile * CPR; idx += kThreads) {
-                const int r = idx / CPR, ch = idx - r * CPR;
-                const int t = t_begin + tile * kTile + r;
-                const bool valid = (t < t_end) && (t < n_old);
-                int s = start1 + t;
-                if (s >= cap) s -= cap;
-                const __half* src = pool + ((base + (valid ? s : 0)) * Hkv + kvh) * (long long)D + ch * 8;
-                const uint32_t dst = sbase + (uint32_t)(r * D + ((ch ^ (r & 7)) * 8)) * 2u;
-                cp_async_16(dst, src, valid ? 16 : 0);
-            }
-        };
-
-        const int n_jobs = 2 * n_tiles;
-#pragma unroll
-        for (int j = 0; j < kStages - 1; j++) {
-            if (j < n_jobs) issue(j);
-            cp_async_commit();
-        }
         for (int j = 0; j < n_jobs; j++) {
             cp_async_wait<kStages - 2>();
             __syncthreads();
@@ -447,19 +451,39 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
         if (lane == 0) s_L[h] = L;
     }
     __syncthreads();
-    for (int idx4 = tid; idx4 < (G * D) / 4; idx4 += kThreads) {
-        const int g = (idx4 * 4) / D, i = idx4 * 4 - g * D;
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-        for (int s = 0; s < ns; s++) {
-            const float w = wts[s * kGP + g];
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(
-                p.part_o + ((p0 + s) * Hkv + kvh) * kGP * D + g * D + i));
-            o.x += w * v.x;
-            o.y += w * v.y;
-            o.z += w * v.z;
-            o.w += w * v.w;
+    // Each thread merges two float4 columns (G * D / 4 <= 2 * kThreads) and keeps the loads of eight
+    // splits of both in flight at once: the merge is bound by L2 latency, not bandwidth.
+    constexpr int kMB = 8;
+    static_assert(kGP * D / 4 <= 2 * kThreads, "two float4 columns per thread");
+    const int nitem = (G * D) / 4;
+    const int ia = tid, ib = tid + kThreads;
+    const int ga = (ia * 4) / D, gb = (ib * 4) / D;
+    const float* pa = p.part_o + (p0 * Hkv + kvh) * kGP * D + (long long)ia * 4;
+    const float* pb = p.part_o + (p0 * Hkv + kvh) * kGP * D + (long long)ib * 4;
+    const long long sstride = (long long)Hkv * kGP * D;
+    float4 oa = make_float4(0.f, 0.f, 0.f, 0.f), ob = oa;
+    for (int s0 = 0; s0 < ns; s0 += kMB) {
+        float4 va[kMB], vb[kMB];
+#pragma unroll
+        for (int j = 0; j < kMB; j++) {
+            const bool ok = s0 + j < ns;
+            va[j] = (ok && ia < nitem) ? __ldcg(reinterpret_cast<const float4*>(pa + (s0 + j) * sstride)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            vb[j] = (ok && ib < nitem) ? __ldcg(reinterpret_cast<const float4*>(pb + (s0 + j) * sstride)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+#pragma unroll
+        for (int j = 0; j < kMB; j++) {
+            if (s0 + j >= ns) break;
+            const float wa = ia < nitem ? wts[(s0 + j) * kGP + ga] : 0.f;
+            const float wb = ib < nitem ? wts[(s0 + j) * kGP + gb] : 0.f;
+            oa.x += wa * va[j].x; oa.y += wa * va[j].y; oa.z += wa * va[j].z; oa.w += wa * va[j].w;
+            ob.x += wb * vb[j].x; ob.y += wb * vb[j].y; ob.z += wb * vb[j].z; ob.w += wb * vb[j].w;
+        }
+    }
+    for (int which = 0; which < 2; which++) {
+        const int idx4 = which ? ib : ia;
+        if (idx4 >= nitem) continue;
+        const int g = (idx4 * 4) / D, i = idx4 * 4 - g * D;
+        const float4 o = which ? ob : oa;
         const float L = s_L[g];
         float ov[4] = {o.x, o.y, o.z, o.w};
         const int h = kvh * G + g;
