@@ -92,6 +92,43 @@ __device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
     return static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
 }
 
+// 8 consecutive 16-bit values (bf16 or fp16) <-> fp32
+__device__ __forceinline__ void unpack8(const uint4 v, bool bf, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        float2 t;
+        if (bf) t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        else t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8], bool bf) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        if (bf) {
+            const __nv_bfloat162 t = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&t);
+        } else {
+            const __half2 t = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&t);
+        }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+// 8 consecutive elements of a dtype row (16-byte aligned: row + e0 * dtype bytes) as fp32
+__device__ __forceinline__ void load8(const char* row, int dtype, long long e0, float (&x)[8]) {
+    if (dtype == ANELM_F32) {
+        const float4 a = *reinterpret_cast<const float4*>(row + e0 * 4);
+        const float4 c = *reinterpret_cast<const float4*>(row + e0 * 4 + 16);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+    } else {
+        unpack8(*reinterpret_cast<const uint4*>(row + e0 * 2), dtype == ANELM_BF16, x);
+    }
+}
+
 // Loads that bypass L1 (data written by other CTAs of the same launch).
 __device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
 

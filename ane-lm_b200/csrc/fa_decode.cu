@@ -91,6 +91,20 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
     const int Hkv = p.Hkv;
     const int G = p.Hq / Hkv;
     const int seq = p.seq_ids ? p.seq_ids[b] : 0;
+    const char* proj_row = reinterpret_cast<const char*>(p.proj) +
+                           (long long)b * p.proj_stride * dtype_bytes(p.proj_dtype);
+
+    // ---- the projection values this CTA needs, first: one 16-byte q chunk per thread (head
+    // tid / CPR of the group) and, for the append, one k or v chunk; issued ahead of the ring
+    // metadata and the K / V tiles, so they do not queue behind the tile loads ----
+    const int qg = tid / CPR, qc = tid % CPR;
+    const bool has_q = p.proj_vec && tid < kGP * CPR && qg < G;
+    const bool has_k = p.proj_vec && p.append && tid < CPR;
+    const bool has_v = p.proj_vec && p.append && tid >= CPR && tid < 2 * CPR;
+    float q8[8], kv8[8];
+    if (has_q) load8(proj_row, p.proj_dtype, (long long)(kvh * G + qg) * p.q_head_stride + qc * 8, q8);
+    if (has_k) load8(proj_row, p.proj_dtype, p.k_off + (long long)kvh * D + tid * 8, kv8);
+    if (has_v) load8(proj_row, p.proj_dtype, p.v_off + (long long)kvh * D + (tid - CPR) * 8, kv8);
 
     // ---- ring metadata (models/llm/qwen3_5.cpp:973-983) ----
     int cap, len0, start0;
@@ -142,8 +156,6 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
     __half* P_s = reinterpret_cast<__half*>(smem + S::P);
     float* misc = reinterpret_cast<float*>(smem + S::misc);
     // misc: [0..3] m_run, [4..7] l_run, [8..11] alpha, [12..15] score scale
-    const char* proj_row = reinterpret_cast<const char*>(p.proj) +
-                           (long long)b * p.proj_stride * dtype_bytes(p.proj_dtype);
 
     float acc[MT][4];
 #pragma unroll
@@ -181,16 +193,28 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
 
     if (n_tok > 0) {
         // ---- 1. prologue: queries, new k/v ----
-        for (int idx = tid; idx < kGP * D; idx += kThreads) {
-            int g = idx / D, i = idx - g * D;
-            q_s[idx] = (g < G) ? load_as_float(proj_row, p.proj_dtype,
-                                               (long long)(kvh * G + g) * p.q_head_stride + i)
-                               : 0.f;
-        }
-        if (p.append) {
-            for (int i = tid; i < D; i += kThreads) {
-                kf_s[i] = load_as_float(proj_row, p.proj_dtype, p.k_off + (long long)kvh * D + i);
-                vf_s[i] = load_as_float(proj_row, p.proj_dtype, p.v_off + (long long)kvh * D + i);
+        if (p.proj_vec) {
+            if (tid < kGP * CPR) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) q_s[qg * D + qc * 8 + e] = has_q ? q8[e] : 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                if (has_k) kf_s[tid * 8 + e] = kv8[e];
+                if (has_v) vf_s[(tid - CPR) * 8 + e] = kv8[e];
+            }
+        } else {
+            for (int idx = tid; idx < kGP * D; idx += kThreads) {
+                int g = idx / D, i = idx - g * D;
+                q_s[idx] = (g < G) ? load_as_float(proj_row, p.proj_dtype,
+                                                   (long long)(kvh * G + g) * p.q_head_stride + i)
+                                   : 0.f;
+            }
+            if (p.append) {
+                for (int i = tid; i < D; i += kThreads) {
+                    kf_s[i] = load_as_float(proj_row, p.proj_dtype, p.k_off + (long long)kvh * D + i);
+                    vf_s[i] = load_as_float(proj_row, p.proj_dtype, p.v_off + (long long)kvh * D + i);
+                }
             }
         }
         __syncthreads();
@@ -523,7 +547,11 @@ size_t fa_decode_smem_bytes(int head_dim) {
     return head_dim == 256 ? Smem<256>::total : Smem<128>::total;
 }
 
-int launch_fa_decode(const FaDecodeParams& p, int head_dim, int n_blocks, cudaStream_t stream) {
+int launch_fa_decode(const FaDecodeParams& p0, int head_dim, int n_blocks, cudaStream_t stream) {
+    FaDecodeParams p = p0;
+    const int eb = dtype_bytes(p.proj_dtype);
+    p.proj_vec = (uintptr_t)p.proj % 16 == 0 && (p.proj_stride * eb) % 16 == 0 && ((long long)p.q_head_stride * eb) % 16 == 0 &&
+                 (p.k_off * eb) % 16 == 0 && (p.v_off * eb) % 16 == 0 && head_dim % 8 == 0;
     dim3 grid(n_blocks, p.Hkv);
     if (head_dim == 256) {
         const size_t sm = Smem<256>::total;

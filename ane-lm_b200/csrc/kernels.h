@@ -37,6 +37,7 @@ struct FaDecodeParams {
     int q_head_stride;         // elements between q heads inside a proj row (2*D in the glue)
     long long k_off, v_off;    // element offsets of the new k / v inside a proj row
     long long gate_off;        // element offset of head 0's gate inside a proj row (q_head_stride apart)
+    int proj_vec;              // proj rows and the q / k / v offsets are 16-byte aligned (vector loads)
     void* out;
     int out_dtype;
     long long out_stride;
