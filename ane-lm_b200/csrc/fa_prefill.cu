@@ -33,6 +33,7 @@
 //   fp32 accumulation in TMEM).  Every mbarrier wait is bounded and records ANELM_ERR_TIMEOUT
 //   instead of hanging.
 #include <cuda.h>
+#include <algorithm>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -195,21 +196,99 @@ constexpr int kPrepBatch = 4;  // segments whose loads a warp issues together (m
                                // cost occupancy: 5 at 3 CTAs per SM ran slower than 4 at 4)
 __device__ __forceinline__ uint4 half8(const float (&x)[8]) { return pack8(x, false); }
 
+// The prep arithmetic of one 16-byte lane (elements e0 = 8 lane .. +8) of segment s of a token's
+// projection row [q_0 | gate_0 | ... | q_{Hq-1} | gate_{Hq-1} | k_0 .. k_{Hkv-1} | v_0 .. v_{Hkv-1}]:
+// RMSNorm + RoPE of q / k, sigmoid of the gate, and the fp16 stores (Q, K, V, SG, ring pools).
+// `qn` / `kn` hold this lane's 8 norm weights; `cs(j, c, s)` gives the RoPE cos / sin of pair j.
+template <class CS>
+__device__ __forceinline__ void prep_segment(const FaPrefillParams& p, float (&v)[8], int s, int lane, int b, int t,
+                                             long long slot_row, const float* qn, const float* kn, CS cs) {
+    const int Hq = p.Hq, Hkv = p.Hkv;
+    const int e0 = 8 * lane, half = p.rot_dim >> 1;
+    const bool is_q = s < 2 * Hq && !(s & 1), is_gate = s < 2 * Hq && (s & 1);
+    const bool is_k = s >= 2 * Hq && s < 2 * Hq + Hkv;
+    if (is_q || is_k) {
+        if (p.qk_norm) {  // rmsnorm, cpu_ops.cpp:24-30 (qwen3_5.cpp:952-959)
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) ss += v[e] * v[e];
+            ss = warp_sum(ss);
+            const float r = 1.0f / sqrtf(ss / (float)kD + p.rms_eps);
+            const float* w = is_q ? qn : kn;
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fmul_rn(v[e], r), w[e]);
+        }
+        if (p.rot_dim > 0) {  // apply_rope_cached, cpu_ops.cpp:40-63 (or rotate-half)
+            if (p.rope_mode == ANELM_ROPE_INTERLEAVED) {
+                if (e0 < p.rot_dim) {
+#pragma unroll
+                    for (int e = 0; e < 8; e += 2) {
+                        float c, sn;
+                        cs((e0 + e) >> 1, c, sn);
+                        const float v0 = v[e], v1 = v[e + 1];
+                        v[e] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, sn));
+                        v[e + 1] = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, c));
+                    }
+                }
+            } else {
+                const int hl = half >> 3;  // lanes per rotary half
+                float o[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) o[e] = __shfl_sync(0xffffffffu, v[e], lane < hl ? lane + hl : lane - hl);
+                if (e0 < p.rot_dim) {
+                    const bool first = lane < hl;
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        float c, sn;
+                        cs((first ? e0 : e0 - half) + e, c, sn);
+                        v[e] = first ? __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(o[e], sn))
+                                     : __fadd_rn(__fmul_rn(v[e], c), __fmul_rn(o[e], sn));
+                    }
+                }
+            }
+        }
+    }
+    if (is_q) {
+        const int h = s >> 1;
+        *reinterpret_cast<uint4*>(p.Qh + (((long long)b * Hq + h) * p.n_pad + t) * kD + e0) = half8(v);
+    } else if (is_gate) {
+        if (p.SG) {  // sigmoid of the gate for the TMA epilogue (mul_sigmoid_inplace, cpu_ops.cpp:15-22);
+                     // stored as fp16, so the hardware exp2 and reciprocal are exact enough
+            float g[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) g[e] = rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * v[e]));
+            *reinterpret_cast<uint4*>(p.SG + (((long long)b * p.n + t) * Hq + (s >> 1)) * kD + e0) = half8(g);
+        }
+    } else {
+        const int kh = is_k ? s - 2 * Hq : s - 2 * Hq - Hkv;
+        const uint4 hv = half8(v);
+        const long long o = (((long long)b * Hkv + kh) * p.n_pad + t) * kD + e0;
+        *reinterpret_cast<uint4*>((is_k ? p.Kh : p.Vh) + o) = hv;
+        if (p.k_pool)  // ring append at slot t (qwen3_5.cpp:984-986)
+            *reinterpret_cast<uint4*>((is_k ? p.k_pool : p.v_pool) + (slot_row + kh) * kD + e0) = hv;
+    }
+}
+
+// Padding rows t >= n of token (b, t): finite zeros in Q, K and V (this warp's heads).
+__device__ __forceinline__ void prep_zero_row(const FaPrefillParams& p, int b, int t, int warp, int nwarps, int e0) {
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int h = warp; h < p.Hq; h += nwarps)
+        *reinterpret_cast<uint4*>(p.Qh + (((long long)b * p.Hq + h) * p.n_pad + t) * kD + e0) = z;
+    for (int h = warp; h < p.Hkv; h += nwarps) {
+        const long long o = (((long long)b * p.Hkv + h) * p.n_pad + t) * kD + e0;
+        *reinterpret_cast<uint4*>(p.Kh + o) = z;
+        *reinterpret_cast<uint4*>(p.Vh + o) = z;
+    }
+}
+
 __global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPrefillParams p) {
     const int t = blockIdx.x, b = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int Hq = p.Hq, Hkv = p.Hkv;
     const int nseg = 2 * Hq + 2 * Hkv;
     const int e0 = 8 * lane;  // this lane's first element within a 256-element segment
-    if (t >= p.n) {  // padding rows: finite zeros in Q, K, V
-        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-        for (int h = warp; h < Hq; h += 8)
-            *reinterpret_cast<uint4*>(p.Qh + (((long long)b * Hq + h) * p.n_pad + t) * kD + e0) = z;
-        for (int h = warp; h < Hkv; h += 8) {
-            const long long o = (((long long)b * Hkv + h) * p.n_pad + t) * kD + e0;
-            *reinterpret_cast<uint4*>(p.Kh + o) = z;
-            *reinterpret_cast<uint4*>(p.Vh + o) = z;
-        }
+    if (t >= p.n) {
+        prep_zero_row(p, b, t, warp, 8, e0);
         return;
     }
     const char* row = reinterpret_cast<const char*>(p.proj) +
@@ -217,7 +296,7 @@ __global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPre
     const int pos = p.start_pos + t;
     const int seq = p.seq_ids ? p.seq_ids[b] : 0;
     const long long slot_row = p.kv_base ? (p.kv_base[seq] + t) * Hkv : 0;
-    const int half = p.rot_dim >> 1;
+    const auto cs = [&](int j, float& c, float& sn) { rope_cs_pf(p, pos, j, c, sn); };
     for (int s0 = warp; s0 < nseg; s0 += 8 * kPrepBatch) {
         float x[kPrepBatch][8];
 #pragma unroll
@@ -227,75 +306,126 @@ __global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPre
         for (int i = 0; i < kPrepBatch; i++) {
             const int s = s0 + 8 * i;
             if (s >= nseg) break;
-            const bool is_q = s < 2 * Hq && !(s & 1), is_gate = s < 2 * Hq && (s & 1);
-            const bool is_k = s >= 2 * Hq && s < 2 * Hq + Hkv;
-            float* v = x[i];
-            if (is_q || is_k) {
-                if (p.qk_norm) {  // rmsnorm, cpu_ops.cpp:24-30 (qwen3_5.cpp:952-959)
-                    float ss = 0.f;
-#pragma unroll
-                    for (int e = 0; e < 8; e++) ss += v[e] * v[e];
-                    ss = warp_sum(ss);
-                    const float r = 1.0f / sqrtf(ss / (float)kD + p.rms_eps);
-                    const float* w = (is_q ? p.q_norm : p.k_norm) + e0;
-#pragma unroll
-                    for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fmul_rn(v[e], r), w[e]);
-                }
-                if (p.rot_dim > 0) {  // apply_rope_cached, cpu_ops.cpp:40-63 (or rotate-half)
-                    if (p.rope_mode == ANELM_ROPE_INTERLEAVED) {
-                        if (e0 < p.rot_dim) {
-#pragma unroll
-                            for (int e = 0; e < 8; e += 2) {
-                                float c, sn;
-                                rope_cs_pf(p, pos, (e0 + e) >> 1, c, sn);
-                                const float v0 = v[e], v1 = v[e + 1];
-                                v[e] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, sn));
-                                v[e + 1] = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, c));
-                            }
-                        }
-                    } else {
-                        const int hl = half >> 3;  // lanes per rotary half
-                        float o[8];
-#pragma unroll
-                        for (int e = 0; e < 8; e++)
-                            o[e] = __shfl_sync(0xffffffffu, v[e], lane < hl ? lane + hl : lane - hl);
-                        if (e0 < p.rot_dim) {
-                            const bool first = lane < hl;
-#pragma unroll
-                            for (int e = 0; e < 8; e++) {
-                                float c, sn;
-                                rope_cs_pf(p, pos, (first ? e0 : e0 - half) + e, c, sn);
-                                v[e] = first ? __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(o[e], sn))
-                                             : __fadd_rn(__fmul_rn(v[e], c), __fmul_rn(o[e], sn));
-                            }
-                        }
-                    }
-                }
-            }
-            if (is_q) {
-                const int h = s >> 1;
-                *reinterpret_cast<uint4*>(p.Qh + (((long long)b * Hq + h) * p.n_pad + t) * kD + e0) = half8(x[i]);
-            } else if (is_gate) {
-                if (p.SG) {  // sigmoid of the gate for the TMA epilogue (mul_sigmoid_inplace, cpu_ops.cpp:15-22);
-                             // stored as fp16, so the hardware exp2 and reciprocal are exact enough
-                    float g[8];
-#pragma unroll
-                    for (int e = 0; e < 8; e++) g[e] = rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * v[e]));
-                    *reinterpret_cast<uint4*>(p.SG + (((long long)b * p.n + t) * Hq + (s >> 1)) * kD + e0) = half8(g);
-                }
-            } else {
-                const int kh = is_k ? s - 2 * Hq : s - 2 * Hq - Hkv;
-                const uint4 hv = half8(x[i]);
-                const long long o = (((long long)b * Hkv + kh) * p.n_pad + t) * kD + e0;
-                *reinterpret_cast<uint4*>((is_k ? p.Kh : p.Vh) + o) = hv;
-                if (p.k_pool)  // ring append at slot t (qwen3_5.cpp:984-986)
-                    *reinterpret_cast<uint4*>((is_k ? p.k_pool : p.v_pool) + (slot_row + kh) * kD + e0) = hv;
-            }
+            prep_segment(p, x[i], s, lane, b, t, slot_row, p.q_norm + e0, p.k_norm + e0, cs);
         }
     }
     if (t == 0 && threadIdx.x == 0 && p.kv_len) {
         p.kv_len[seq] = p.n;
         p.kv_start[seq] = 0;
+    }
+}
+
+// Streaming form of the prep for 16-bit projections: a persistent CTA walks the tokens
+// u = blockIdx.x, blockIdx.x + gridDim.x, ... of the [B][n_pad] grid.  Warp 8 copies each
+// token's whole projection row (and its RoPE table rows) into one of kPrepStages shared-memory
+// stages with untiled bulk copies, kPrepStages - 1 tokens ahead; warps 0-7 run prep_segment on
+// the staged row.  The same arithmetic as fa_prefill_prep_vec_kernel, with the loads kept in
+// flight across tokens instead of one row at a time per CTA.
+constexpr int kPrepStages = 4;
+constexpr int kPrepWarps = 8;  // consumer warps; warp kPrepWarps is the copy producer
+constexpr int kPrepStageMax = 54 * 1024;  // stage bytes that still let two CTAs share an SM
+
+__global__ void __launch_bounds__(32 * (kPrepWarps + 1), 2)
+    fa_prefill_prep_bulk_kernel(const FaPrefillParams p, int stage_bytes, int rope_off) {
+    extern __shared__ __align__(128) uint8_t prep_smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(prep_smem);
+    uint64_t* empty = full + kPrepStages;
+    volatile int* abort = reinterpret_cast<volatile int*>(empty + kPrepStages);
+    uint8_t* stage0 = prep_smem + 128;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int Hq = p.Hq, Hkv = p.Hkv;
+    const int nseg = 2 * Hq + 2 * Hkv;
+    const uint32_t row_bytes = (uint32_t)nseg * kD * 2;
+    const int half = p.rot_dim >> 1;
+    const long long total = (long long)p.B * p.n_pad;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPrepStages; s++) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], kPrepWarps);
+        }
+        *abort = 0;
+        tc::fence_barrier_init();
+    }
+    __syncthreads();
+    if (warp == kPrepWarps) {  // producer: one thread issues every copy
+        if (lane != 0) return;
+        long long last[kPrepStages];
+#pragma unroll
+        for (int s = 0; s < kPrepStages; s++) last[s] = -1;
+        long long k = 0;
+        for (long long u = blockIdx.x; u < total; u += gridDim.x, k++) {
+            const int s = (int)(k % kPrepStages);
+            if (k >= kPrepStages &&
+                !tc::mbar_wait(&empty[s], (uint32_t)((k / kPrepStages) - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort))
+                break;
+            const int b = (int)(u / p.n_pad), t = (int)(u % p.n_pad);
+            last[s] = k;
+            if (t >= p.n) {  // padding row: nothing to copy
+                tc::mbar_arrive(&full[s]);
+                continue;
+            }
+            uint8_t* st = stage0 + (size_t)s * stage_bytes;
+            const int pos = p.start_pos + t;
+            const bool tab = p.rot_dim > 0 && p.rope_cos && pos >= 0 && pos < p.rope_len;
+            tc::mbar_arrive_expect_tx(&full[s], row_bytes + (tab ? 8u * half : 0u));
+            tc::bulk_load(st, reinterpret_cast<const char*>(p.proj) + ((long long)b * p.n + t) * p.proj_stride * 2,
+                          row_bytes, &full[s]);
+            if (tab) {
+                tc::bulk_load(st + rope_off, p.rope_cos + (long long)pos * half, 4u * half, &full[s]);
+                tc::bulk_load(st + rope_off + 4 * half, p.rope_sin + (long long)pos * half, 4u * half, &full[s]);
+            }
+        }
+        // every issued copy has landed before the CTA can exit (normally the consumers already
+        // waited for them; after a timeout this bounds the wait for the ones still in flight)
+#pragma unroll
+        for (int s = 0; s < kPrepStages; s++)
+            if (last[s] >= 0)
+                for (uint32_t i = 0; i < tc::kWaitPolls; i++)
+                    if (tc::mbar_try_wait(&full[s], (uint32_t)(last[s] / kPrepStages) & 1)) break;
+        return;
+    }
+    const int e0 = 8 * lane;
+    float qn[8], kn[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        qn[e] = p.qk_norm ? p.q_norm[e0 + e] : 0.f;
+        kn[e] = p.qk_norm ? p.k_norm[e0 + e] : 0.f;
+    }
+    const bool bf = p.proj_dtype == ANELM_BF16;
+    long long k = 0;
+    for (long long u = blockIdx.x; u < total; u += gridDim.x, k++) {
+        const int s = (int)(k % kPrepStages);
+        if (!tc::mbar_wait(&full[s], (uint32_t)(k / kPrepStages) & 1, p.err, ANELM_ERR_TIMEOUT, abort)) break;
+        const int b = (int)(u / p.n_pad), t = (int)(u % p.n_pad);
+        if (t >= p.n) {
+            prep_zero_row(p, b, t, warp, kPrepWarps, e0);
+        } else {
+            const uint8_t* st = stage0 + (size_t)s * stage_bytes;
+            const int pos = p.start_pos + t;
+            const int seq = p.seq_ids ? p.seq_ids[b] : 0;
+            const long long slot_row = p.kv_base ? (p.kv_base[seq] + t) * Hkv : 0;
+            const bool tab = p.rot_dim > 0 && p.rope_cos && pos >= 0 && pos < p.rope_len;
+            const float* tc_cos = reinterpret_cast<const float*>(st + rope_off);
+            const auto cs = [&](int j, float& c, float& sn) {
+                if (tab) {
+                    c = tc_cos[j];
+                    sn = tc_cos[half + j];
+                } else {
+                    rope_cs_pf(p, pos, j, c, sn);
+                }
+            };
+            for (int sg = warp; sg < nseg; sg += kPrepWarps) {
+                float x[8];
+                unpack8(*reinterpret_cast<const uint4*>(st + (size_t)sg * kD * 2 + 16 * lane), bf, x);
+                prep_segment(p, x, sg, lane, b, t, slot_row, qn, kn, cs);
+            }
+            if (t == 0 && warp == 0 && lane == 0 && p.kv_len) {
+                p.kv_len[seq] = p.n;
+                p.kv_start[seq] = 0;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[s]);
     }
 }
 
@@ -668,7 +798,23 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
                                                (uint64_t)p.Hq * kD));
     if (p.tma_epilogue && p.gate) p.SG = sg;
     const long long row_bytes = p.proj_stride * dtype_bytes(p.proj_dtype);
-    if ((uintptr_t)p.proj % 16 == 0 && row_bytes % 16 == 0 && p.rot_dim % 16 == 0) {
+    const bool vec = (uintptr_t)p.proj % 16 == 0 && row_bytes % 16 == 0 && p.rot_dim % 16 == 0;
+    // streaming prep: 16-bit projection, 16-byte aligned RoPE table rows, two CTAs per SM
+    const int nseg = 2 * p.Hq + 2 * p.Hkv;
+    const int rope_off = nseg * kD * 2;
+    const int stage_bytes = (rope_off + 8 * (p.rot_dim >> 1) + 127) / 128 * 128;
+    const bool bulk = vec && dtype_bytes(p.proj_dtype) == 2 && stage_bytes <= kPrepStageMax &&
+                      (!p.rope_cos || ((uintptr_t)p.rope_cos % 16 == 0 && (uintptr_t)p.rope_sin % 16 == 0));
+    if (bulk) {
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const long long total = (long long)p.B * p.n_pad;
+        const int grid = (int)std::min<long long>(total, 2LL * sms);
+        const int smem = 128 + kPrepStages * stage_bytes;
+        cudaFuncSetAttribute(fa_prefill_prep_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        fa_prefill_prep_bulk_kernel<<<grid, 32 * (kPrepWarps + 1), smem, stream>>>(p, stage_bytes, rope_off);
+    } else if (vec) {
         fa_prefill_prep_vec_kernel<<<dim3(p.n_pad, p.B), 256, 0, stream>>>(p);
     } else {
         const size_t prep_smem = (size_t)(p.Hq + 2 * p.Hkv) * kD * sizeof(float);

@@ -227,19 +227,53 @@ __global__ void __launch_bounds__(256) gdn_pf_prep_kernel(const GdnPrefillParams
 
 // ---------------------------------------------------------------- pack (core op: token-major inputs)
 
+// 8 consecutive values (i a multiple of 8) as hi / lo planes, 16-byte stores
+__device__ __forceinline__ void put_hl8(__half* hi, long long plane, long long i, const float (&x)[8]) {
+    float h[8], l[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const __half q = __float2half_rn(x[e]);
+        h[e] = __half2float(q);
+        l[e] = x[e] - h[e];
+    }
+    *reinterpret_cast<uint4*>(hi + i) = pack8(h, false);
+    *reinterpret_cast<uint4*>(hi + plane + i) = pack8(l, false);
+}
+
 __global__ void __launch_bounds__(256) gdn_pf_pack_kernel(const GdnPrefillParams p) {
     const int t = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const int Hk = p.Hk, Hv = p.Hv;
     const bool live = t < p.n;
     const long long tok = (long long)b * p.n + t;
-    for (int i = tid; i < Hk * kDk; i += 256) {
-        const long long o = (((long long)b * Hk + i / kDk) * p.T_pad + t) * kDk + i % kDk;
-        put_hl(p.qh, p.q_plane, o, live ? load_as_float(p.q_in, p.in_dtype, tok * Hk * kDk + i) : 0.f);
-        put_hl(p.kh, p.q_plane, o, live ? load_as_float(p.k_in, p.in_dtype, tok * Hk * kDk + i) : 0.f);
-    }
-    for (int i = tid; i < Hv * kDv; i += 256) {
-        const long long o = (((long long)b * Hv + i / kDv) * p.T_pad + t) * kDv + i % kDv;
-        put_hl(p.vh, p.v_plane, o, live ? load_as_float(p.v_in, p.in_dtype, tok * Hv * kDv + i) : 0.f);
+    if (p.in_vec) {  // 16-byte aligned rows: 8 values per thread and step
+        const int nq = Hk * kDk / 8, nv = Hv * kDv / 8;
+        const int eb = dtype_bytes(p.in_dtype);
+        for (int gi = tid; gi < 2 * nq + nv; gi += 256) {
+            float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (gi < 2 * nq) {
+                const bool isk = gi >= nq;
+                const int e = (isk ? gi - nq : gi) * 8;
+                if (live)
+                    load8(reinterpret_cast<const char*>(isk ? p.k_in : p.q_in) + tok * Hk * kDk * eb, p.in_dtype, e, x);
+                const long long o = (((long long)b * Hk + e / kDk) * p.T_pad + t) * kDk + e % kDk;
+                put_hl8(isk ? p.kh : p.qh, p.q_plane, o, x);
+            } else {
+                const int e = (gi - 2 * nq) * 8;
+                if (live) load8(reinterpret_cast<const char*>(p.v_in) + tok * Hv * kDv * eb, p.in_dtype, e, x);
+                const long long o = (((long long)b * Hv + e / kDv) * p.T_pad + t) * kDv + e % kDv;
+                put_hl8(p.vh, p.v_plane, o, x);
+            }
+        }
+    } else {
+        for (int i = tid; i < Hk * kDk; i += 256) {
+            const long long o = (((long long)b * Hk + i / kDk) * p.T_pad + t) * kDk + i % kDk;
+            put_hl(p.qh, p.q_plane, o, live ? load_as_float(p.q_in, p.in_dtype, tok * Hk * kDk + i) : 0.f);
+            put_hl(p.kh, p.q_plane, o, live ? load_as_float(p.k_in, p.in_dtype, tok * Hk * kDk + i) : 0.f);
+        }
+        for (int i = tid; i < Hv * kDv; i += 256) {
+            const long long o = (((long long)b * Hv + i / kDv) * p.T_pad + t) * kDv + i % kDv;
+            put_hl(p.vh, p.v_plane, o, live ? load_as_float(p.v_in, p.in_dtype, tok * Hv * kDv + i) : 0.f);
+        }
     }
     for (int h = tid; h < Hv; h += 256) {
         const long long o = ((long long)b * Hv + h) * p.T_pad + t;
@@ -253,7 +287,7 @@ __global__ void __launch_bounds__(256) gdn_pf_pack_kernel(const GdnPrefillParams
 struct ChunkSmem {
     __half khi[kC][kP], klo[kC][kP];
     __half qhi[kC][kP], qlo[kC][kP];    // Q, then V
-    float a[kC][kC + 1];                // A, then T = (I + A)^{-1}
+    float at[kC][kC];                   // A^T, rows interleaved: at[i][16 (t % 4) + t / 4] = A[t][i]
     __half thi[kC][kPc], tlo[kC][kPc];  // T scaled by columns (W's, then U's factors)
     float lc[kC], lt[kC], bt[kC];
 };
@@ -302,7 +336,7 @@ __global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParam
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const int r = r0 + g + (e >> 1) * 8, i = n0 + nt * 8 + 2 * c + (e & 1);
-                sm.a[r][i] = i < r ? sm.bt[r] * expf(sm.lt[r] - sm.lc[i]) * kk[nt][e] : 0.f;
+                sm.at[i][16 * (r & 3) + (r >> 2)] = i < r ? sm.bt[r] * expf(sm.lt[r] - sm.lc[i]) * kk[nt][e] : 0.f;
                 put_hl(mhi, p.m_plane, r * kC + i, i <= r ? expf(sm.lc[r] - sm.lc[i]) * qk[nt][e] : 0.f);
             }
     }
@@ -310,22 +344,28 @@ __global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParam
     __syncthreads();  // Q no longer needed: V into its buffers
     cp_tile_hl(&sm.qhi[0][0], &sm.qlo[0][0], kP, p.vh + vrow * kDv, p.v_plane, kC, kDv, tid, 256);
     cp_async_commit();
-    // T = (I + A)^{-1} by forward substitution, one column per 4 threads: x_t = [t == j] - sum_{i<t} A_ti x_i.
-    // Thread part pt keeps x_i for i = 4m + pt in registers; each row's sum is reduced over the 4 threads.
+    // T = (I + A)^{-1} by forward substitution, one column j per 4 threads: x_t = [t == j] - sum_{i<t} A_ti x_i,
+    // right-looking: thread part pt keeps the running sums r of rows t = 4m + pt; once x_t is final (in the
+    // thread owning row t) it is broadcast to the 4 threads, which add A[4m + pt][t] x_t to their rows'
+    // sums (column t of A read as four 16-byte words).  A is strictly lower, so rows <= t add zeros.
     const int j = tid >> 2, pt = tid & 3;
-    float xs[kC / 4];
+    float xs[kC / 4], rs[kC / 4];
 #pragma unroll
-    for (int m = 0; m < kC / 4; m++) xs[m] = 0.f;
+    for (int m = 0; m < kC / 4; m++) xs[m] = rs[m] = 0.f;
 #pragma unroll
     for (int t = 0; t < kC; t++) {
-        float s = 0.f;
-#pragma unroll
-        for (int m = 0; m < kC / 4; m++)
-            if (4 * m + pt < t) s = fmaf(sm.a[t][4 * m + pt], xs[m], s);
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        const float x = (t == j ? 1.0f : 0.0f) - s;
+        const float x = __shfl_sync(0xffffffffu, (t == j ? 1.0f : 0.0f) - rs[t >> 2], (lane & ~3) | (t & 3));
         if (pt == (t & 3)) xs[t >> 2] = x;
+        const float4* col = reinterpret_cast<const float4*>(&sm.at[t][16 * pt]);
+#pragma unroll
+        for (int q = 0; q < kC / 16; q++) {
+            if (16 * q + 15 <= t) continue;  // rows 4m + pt <= 4m + 3 <= t of this word are final
+            const float4 a4 = col[q];
+            rs[4 * q] = fmaf(a4.x, x, rs[4 * q]);
+            rs[4 * q + 1] = fmaf(a4.y, x, rs[4 * q + 1]);
+            rs[4 * q + 2] = fmaf(a4.z, x, rs[4 * q + 2]);
+            rs[4 * q + 3] = fmaf(a4.w, x, rs[4 * q + 3]);
+        }
     }
     {  // T' = T diag(beta e^{lt}) (W's factor) as hi / lo; column j belongs to this thread group
         const float fw = sm.bt[j] * expf(sm.lt[j]);
@@ -617,6 +657,7 @@ int launch_gated_delta_chunked(GdnPrefillParams p, void* workspace, cudaStream_t
     if (p.dk != kDk || p.dv != kDv || p.Hv % p.Hk) return ANELM_ERR_UNSUPPORTED;
     p.T_pad = (p.n + kC - 1) / kC * kC;
     carve(p, workspace, false);
+    p.in_vec = (uintptr_t)p.q_in % 16 == 0 && (uintptr_t)p.k_in % 16 == 0 && (uintptr_t)p.v_in % 16 == 0;
     gdn_pf_pack_kernel<<<dim3(p.T_pad, p.B), 256, 0, stream>>>(p);
     return launch_chunks_and_chain(p, stream);
 }

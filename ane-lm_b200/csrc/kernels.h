@@ -131,6 +131,7 @@ struct GdnPrefillParams {
     const void* k_in;
     const void* v_in;
     int in_dtype;
+    int in_vec;            // set by the launcher: q_in, k_in, v_in 16-byte aligned
     const float* lg_in;
     const float* beta_in;
     // state [seq][Hv][dk][dv], row b uses seq_ids[b] (or b)

@@ -148,11 +148,15 @@ def test_prefill_state_errors():
         plan.close()
 
 
-@pytest.mark.parametrize("case", ["rope_half_f32_proj", "rot40_fallback_prep"])
+@pytest.mark.parametrize("case", ["rope_half_f32_proj", "rope_half_bf16_proj", "rot40_fallback_prep",
+                                  "past_table_bf16_proj"])
 def test_prefill_prep_variants(case):
-    """The projection prep (RMSNorm, RoPE, fp16 Q/K/V, ring append) has a vectorised path (16-byte
-    rows, rot_dim % 16 == 0) and a general one: rotate-half RoPE on an fp32 projection exercises the
-    vectorised lane-pair shuffle, rot_dim 40 the general kernel.  Both against the oracle."""
+    """The projection prep (RMSNorm, RoPE, fp16 Q/K/V, ring append) has a streaming path (16-bit
+    projection rows staged by bulk copies), a vectorised one (16-byte rows, rot_dim % 16 == 0) and a
+    general one: rotate-half RoPE on a bf16 projection exercises the streaming kernel's lane-pair
+    shuffle, on an fp32 projection the vectorised kernel's, rot_dim 40 the general kernel; positions
+    4000-4149 cross the end of the 4096-row RoPE table (computed angles past it, cpu_ops.cpp:51-56).
+    All against the oracle."""
     rng = np.random.default_rng(11)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(11)
@@ -161,21 +165,22 @@ def test_prefill_prep_variants(case):
     rot = 64 if half else 40
     qn, kn = weights(rng)
     proj = torch.randn(1, n, PROJ, generator=gen, device="cuda")
-    if not half:
+    if not case.endswith("f32_proj"):
         proj = proj.to(torch.bfloat16)
     rope = po.rope_table(4096, rot, 1e7)
     shape = fa_shape(HQ, HKV, D, rot, 1e7)
     variant = po.make_variant(rope_half=int(half), kv_round_f16=1)
+    start = 4000 if case.startswith("past_table") else 0
     with Context(layer_types=[ab.LAYER_FULL_ATTN], num_q_heads=HQ, num_kv_heads=HKV, head_dim=D, rot_dim=rot,
                  rope_theta=1e7, max_seqs=1, kv_capacity=cap,
                  rope_mode=ab.ROPE_HALF if half else ab.ROPE_INTERLEAVED) as ctx:
         ctx.set_full_attn_weights(0, qn, kn)
         plan = ctx.plan([0])
-        out = ctx.full_attn_prefill(plan, 0, proj, out_dtype=torch.float16).float().cpu().numpy()
+        out = ctx.full_attn_prefill(plan, 0, proj, start_pos=start, out_dtype=torch.float16).float().cpu().numpy()
         k, v, ln, st = ctx.kv_export(0, 0)
         plan.close()
     ring = po.KVRing.empty(cap, HKV, D)
-    want = po.full_attn_tokens("oracle", shape, variant, qn, kn, ring, proj.float().cpu().numpy()[0], 0, rope)
+    want = po.full_attn_tokens("oracle", shape, variant, qn, kn, ring, proj.float().cpu().numpy()[0], start, rope)
     assert_close(out[0], want, what=f"prefill {case}")
     assert (ln, st) == (n, 0)
     np.testing.assert_array_equal(v[:n], ring.v[:n])
