@@ -121,6 +121,11 @@ __device__ __forceinline__ void gemm16(float (&acc)[NT][4], const __half* ahi, c
     }
 }
 
+// Named barrier over `count` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void named_bar_sync_cta(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
 // 16-byte cp.async copies of `rows` rows of `cols` fp16 (hi and lo planes) into a pitched tile pair
 __device__ __forceinline__ void cp_tile_hl(__half* dhi, __half* dlo, int pitch, const __half* src, long long plane,
                                            int rows, int cols, int tid, int nthreads) {
@@ -409,139 +414,241 @@ __global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParam
 
 // ---------------------------------------------------------------- the recurrence over chunks
 
+// One chain CTA per (sequence, value head, 32 state columns j0 .. j0 + 32), four warps: warp
+// (jg, dh) = (warp / 2, warp % 2) keeps S^T rows j0 + 16 jg .. + 16 (state columns) times key dims
+// d in [64 dh, 64 dh + 64) in registers, in the accumulator layout of mma.m16n8k16, which is also
+// the A-operand layout: S^T feeds W S and Q S directly (as hi / lo pairs), and the state update
+// S^T += E^T K accumulates into the same registers.  The two warps of a column group hold the two
+// halves of d, so their partial W S and Q S sums meet in shared memory.  Per chunk and warp:
+//   [W; Q] S over its d half -> exchange -> D = U - W S (all 64 rows t), Y = e^lc Q S + M D for
+//   its 32 rows t, S = e^{lc_C} S + K^T (e^{lc_C - lc} D) for its d half.
+constexpr int kChainThreads = 128;
 struct ChainSmem {
-    __half whi[kC][kP], wlo[kC][kP];          // W[t][d]
-    __half qhi[kC][kP], qlo[kC][kP];          // Q[t][d]
-    __half khi[kC][kP], klo[kC][kP];          // K[i][d]
-    __half mhi[kC][kPc], mlo[kC][kPc];        // M[t][i]
-    float u[kC][kDvb + 4];                    // U columns of this block
-    float lc[2][kC];                          // in-chunk cumulative log decay, by chunk parity
-    float s[kDk][kDvb + 1];                   // state block S[d][j] (fp32 master)
-    __half sthi[kDvb][kP], stlo[kDvb][kP];    // S^T [j][d] hi / lo
-    __half dthi[kDvb][kPc], dtlo[kDvb][kPc];  // D^T [j][t]
-    __half ethi[kDvb][kPc], etlo[kDvb][kPc];  // (diag(e^{lc_C - lc}) D)^T
+    __half whi[kC][kP], wlo[kC][kP];   // W[t][d]
+    __half qhi[kC][kP], qlo[kC][kP];   // Q[t][d]
+    __half khi[kC][kP], klo[kC][kP];   // K[t][d]
+    __half mhi[kC][kPc], mlo[kC][kPc]; // M[t][i]
+    float u[kC][kDvb + 4];             // U columns of this block
+    float lc[2][kC];                   // in-chunk cumulative log decay, by chunk parity
+    float xd[4][32][32];               // partial W S of each warp, [warp][register][lane]
+    float xy[4][32][32];               // partial Q S
 };
 
-// cp.async of this chunk's W, Q, U columns and lc (read by the [W; Q] S product and D = U - W S)
-__device__ __forceinline__ void chain_load_wqu(ChainSmem& sm, const GdnPrefillParams& p, long long krow, long long vrow,
-                                               int j0, int par, int tid) {
-    cp_tile_hl(&sm.whi[0][0], &sm.wlo[0][0], kP, p.wh + vrow * kDk, p.v_plane, kC, kDk, tid, 256);
-    cp_tile_hl(&sm.qhi[0][0], &sm.qlo[0][0], kP, p.qh + krow * kDk, p.q_plane, kC, kDk, tid, 256);
-    for (int i = tid; i < kC * (kDvb / 4); i += 256) {
+__device__ __forceinline__ uint32_t h2u(const __half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+// x0, x1 as an fp16 hi pair and the fp16 pair of the remainders
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    hi = h2u(h);
+    lo = h2u(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
+}
+// A fragments (hi / lo) of k-step ks from accumulator tiles acc[2 ks] (k 0-7) and acc[2 ks + 1]
+// (k 8-15), each column scaled by sc (sc[nt][0 / 1]: columns 8 nt + 2 c, + 1)
+template <int NT>
+__device__ __forceinline__ void afrag(const float (&acc)[NT][4], const float (&sc)[NT][2], int ks, uint32_t (&ah)[4],
+                                      uint32_t (&al)[4]) {
+    const int t0 = 2 * ks, t1 = 2 * ks + 1;
+    split2(acc[t0][0] * sc[t0][0], acc[t0][1] * sc[t0][1], ah[0], al[0]);
+    split2(acc[t0][2] * sc[t0][0], acc[t0][3] * sc[t0][1], ah[1], al[1]);
+    split2(acc[t1][0] * sc[t1][0], acc[t1][1] * sc[t1][1], ah[2], al[2]);
+    split2(acc[t1][2] * sc[t1][0], acc[t1][3] * sc[t1][1], ah[3], al[3]);
+}
+template <int NT>
+__device__ __forceinline__ void afrag(const float (&acc)[NT][4], int ks, uint32_t (&ah)[4], uint32_t (&al)[4]) {
+    const int t0 = 2 * ks, t1 = 2 * ks + 1;
+    split2(acc[t0][0], acc[t0][1], ah[0], al[0]);
+    split2(acc[t0][2], acc[t0][3], ah[1], al[1]);
+    split2(acc[t1][0], acc[t1][1], ah[2], al[2]);
+    split2(acc[t1][2], acc[t1][3], ah[3], al[3]);
+}
+// acc[0 / 1] += A B for the n-tile pair of b (hi / lo fragments from ldb2 / ldb2_t): three terms
+__device__ __forceinline__ void mma3x2(float (&a0)[4], float (&a1)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                       const uint32_t (&bh)[4], const uint32_t (&bl)[4]) {
+    mma_16816(a0, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+    mma_16816(a1, ah[0], ah[1], ah[2], ah[3], bh[2], bh[3]);
+    mma_16816(a0, al[0], al[1], al[2], al[3], bh[0], bh[1]);
+    mma_16816(a1, al[0], al[1], al[2], al[3], bh[2], bh[3]);
+    mma_16816(a0, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+    mma_16816(a1, ah[0], ah[1], ah[2], ah[3], bl[2], bl[3]);
+}
+
+// cp.async of a chunk's W and Q (read by [W; Q] S)
+__device__ __forceinline__ void chain_load_wq(ChainSmem& sm, const GdnPrefillParams& p, long long krow, long long vrow,
+                                              int tid) {
+    cp_tile_hl(&sm.whi[0][0], &sm.wlo[0][0], kP, p.wh + vrow * kDk, p.v_plane, kC, kDk, tid, kChainThreads);
+    cp_tile_hl(&sm.qhi[0][0], &sm.qlo[0][0], kP, p.qh + krow * kDk, p.q_plane, kC, kDk, tid, kChainThreads);
+    cp_async_commit();
+}
+// cp.async of a chunk's U columns and lc (read by D = U - W S and the decay factors)
+__device__ __forceinline__ void chain_load_u(ChainSmem& sm, const GdnPrefillParams& p, long long vrow, int j0, int par,
+                                             int tid) {
+    for (int i = tid; i < kC * (kDvb / 4); i += kChainThreads) {
         const int r = i / (kDvb / 4), cv = i % (kDvb / 4);
         cp_async_16(smem_u32(&sm.u[r][cv * 4]), p.Ub + (vrow + r) * kDv + j0 + cv * 4, 16);
     }
     if (tid < kC / 4) cp_async_16(smem_u32(&sm.lc[par][tid * 4]), p.lcb + vrow + tid * 4, 16);
     cp_async_commit();
 }
-// cp.async of this chunk's M and K (read by Y = ... + M D and the state update)
+// cp.async of a chunk's M and K (read by M D and the state update)
 __device__ __forceinline__ void chain_load_mk(ChainSmem& sm, const GdnPrefillParams& p, long long krow, long long vrow,
                                               int tid) {
-    cp_tile_hl(&sm.khi[0][0], &sm.klo[0][0], kP, p.kh + krow * kDk, p.q_plane, kC, kDk, tid, 256);
-    cp_tile_hl(&sm.mhi[0][0], &sm.mlo[0][0], kPc, p.mh + vrow * kC, p.m_plane, kC, kC, tid, 256);
+    cp_tile_hl(&sm.khi[0][0], &sm.klo[0][0], kP, p.kh + krow * kDk, p.q_plane, kC, kDk, tid, kChainThreads);
+    cp_tile_hl(&sm.mhi[0][0], &sm.mlo[0][0], kPc, p.mh + vrow * kC, p.m_plane, kC, kC, tid, kChainThreads);
     cp_async_commit();
 }
 
-__global__ void __launch_bounds__(256) gdn_pf_chain_kernel(const GdnPrefillParams p) {
+__global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const GdnPrefillParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     ChainSmem& sm = *reinterpret_cast<ChainSmem*>(smem_raw);
     const int nblk = kDv / kDvb;
     const int h = blockIdx.x / nblk, j0 = (blockIdx.x % nblk) * kDvb, b = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, c = lane & 3;
+    const int jg = warp >> 1, dh = warp & 1;
+    const int jr = 16 * jg;      // this warp's state columns j0 + jr .. + 16
+    const int dbase = 64 * dh;   // and key dims dbase .. + 64
     const int kh = h / (p.Hv / p.Hk);
     const int seq = p.seq_ids ? p.seq_ids[b] : b;
     float* S = p.state + ((long long)seq * p.Hv + h) * kDk * kDv;
-    for (int i = tid; i < kDk * kDvb; i += 256) {
-        const int d = i / kDvb, jj = i % kDvb;
-        const float x = S[(long long)d * kDv + j0 + jj];
-        sm.s[d][jj] = x;
-        split_store(&sm.sthi[jj][d], &sm.stlo[jj][d], x);
-    }
+    // s[nt][e] = S[d][j0 + j], j = jr + g + 8 (e / 2), d = dbase + 8 nt + 2 c + (e % 2)
+    float s[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            s[nt][e] = S[(long long)(dbase + 8 * nt + 2 * c + (e & 1)) * kDv + j0 + jr + g + 8 * (e >> 1)];
     const int nC = p.T_pad / kC;
     const long long krow0 = ((long long)b * p.Hk + kh) * p.T_pad;
     const long long vrow0 = ((long long)b * p.Hv + h) * p.T_pad;
-    // cp.async groups in flight at the top of chunk ci: [WQU(ci), MK(ci)]
-    chain_load_wqu(sm, p, krow0, vrow0, j0, 0, tid);
+    // cp.async groups in flight at the top of chunk ci: [WQ(ci), U(ci), MK(ci)]
+    chain_load_wq(sm, p, krow0, vrow0, tid);
+    chain_load_u(sm, p, vrow0, j0, 0, tid);
     chain_load_mk(sm, p, krow0, vrow0, tid);
-    const int r16 = 16 * (warp & 3);  // this warp's 16 rows of W (warps 0-3) or Q (warps 4-7)
     for (int ci = 0; ci < nC; ci++) {
         const int par = ci & 1;
         const bool more = ci + 1 < nC;
-        cp_async_wait<1>();
-        __syncthreads();  // W, Q, U, lc of this chunk (and S^T) are in shared memory
+        cp_async_wait<2>();
+        __syncthreads();  // W and Q of this chunk are in shared memory
+        // ---- [W; Q] S over this warp's half of d: D part and Y part, all 64 rows t ----
+        float ad[8][4], ay[8][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) ad[nt][e] = ay[nt][e] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+            uint32_t ah[4], al[4];
+            afrag(s, ks, ah, al);
+            const int k0 = dbase + 16 * ks;
+#pragma unroll
+            for (int np = 0; np < 4; np++) {
+                uint32_t bh[4], bl[4];
+                ldb2(bh, &sm.whi[0][0], kP, 16 * np, k0, lane);
+                ldb2(bl, &sm.wlo[0][0], kP, 16 * np, k0, lane);
+                mma3x2(ad[2 * np], ad[2 * np + 1], ah, al, bh, bl);
+                ldb2(bh, &sm.qhi[0][0], kP, 16 * np, k0, lane);
+                ldb2(bl, &sm.qlo[0][0], kP, 16 * np, k0, lane);
+                mma3x2(ay[2 * np], ay[2 * np + 1], ah, al, bh, bl);
+            }
+        }
+        __syncthreads();  // W, Q free
+        if (more) chain_load_wq(sm, p, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC, tid);
+        // ---- the two d halves of this column group meet ----
+#pragma unroll
+        for (int r = 0; r < 32; r++) {
+            sm.xd[warp][r][lane] = ad[r >> 2][r & 3];
+            sm.xy[warp][r][lane] = ay[r >> 2][r & 3];
+        }
+        named_bar_sync_cta(1 + jg, 64);
+        // Q S of this warp's rows t in [32 dh, 32 dh + 32) (the other half is the partner's)
+        float y[4][4];
+#pragma unroll
+        for (int n4 = 0; n4 < 4; n4++)
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                y[n4][e] = (dh ? ay[4 + n4][e] : ay[n4][e]) + sm.xy[warp ^ 1][4 * (4 * dh + n4) + e][lane];
+#pragma unroll
+        for (int r = 0; r < 32; r++) ad[r >> 2][r & 3] += sm.xd[warp ^ 1][r][lane];
+        if (more) cp_async_wait<2>();
+        else cp_async_wait<1>();
+        __syncthreads();  // U and lc of this chunk are in shared memory
         const float* lc = sm.lc[par];
         const float lcC = lc[kC - 1];
-        // [W; Q] S: warps 0-3 the W rows (-> D = U - W S), warps 4-7 the Q rows (kept for Y)
-        float ws[4][4] = {};
-        if (warp < 4)
-            gemm16<false, false, 4>(ws, &sm.whi[0][0], &sm.wlo[0][0], kP, &sm.sthi[0][0], &sm.stlo[0][0], kP, r16, 0, kDk,
-                                    lane);
-        else
-            gemm16<false, false, 4>(ws, &sm.qhi[0][0], &sm.qlo[0][0], kP, &sm.sthi[0][0], &sm.stlo[0][0], kP, r16, 0, kDk,
-                                    lane);
-        if (warp < 4) {
+        // D = U - W S (in place of ad)
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int t = r16 + g + (e >> 1) * 8;
-                const float f = expf(lcC - lc[t]);
+        for (int nt = 0; nt < 8; nt++)
 #pragma unroll
-                for (int nt = 0; nt < 4; nt++) {
-                    const int n = nt * 8 + 2 * c + (e & 1);
-                    const float dv = sm.u[t][n] - ws[nt][e];
-                    split_store(&sm.dthi[n][t], &sm.dtlo[n][t], dv);
-                    split_store(&sm.ethi[n][t], &sm.etlo[n][t], f * dv);
-                }
-            }
-        }
-        __syncthreads();  // D complete; W, Q, U free
-        if (more) {
-            chain_load_wqu(sm, p, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC, j0, par ^ 1, tid);
-            cp_async_wait<1>();  // MK(ci) done, WQU(ci + 1) in flight
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();  // M, K of this chunk are in shared memory
-        if (warp >= 4) {
-            // Y = diag(e^lc) Q S + M D for this warp's 16 rows
-            float md[4][4] = {};
-            gemm16<false, false, 4>(md, &sm.mhi[0][0], &sm.mlo[0][0], kPc, &sm.dthi[0][0], &sm.dtlo[0][0], kPc, r16, 0,
-                                    kC, lane);
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int r = r16 + g + (e >> 1) * 8;
-                const int t = ci * kC + r;
-                if (t >= p.n) continue;
-                const float gam = expf(lc[r]);
-                const long long o = ((long long)b * p.n + t) * p.y_stride + (long long)h * kDv + j0;
-#pragma unroll
-                for (int nt = 0; nt < 4; nt++) {
-                    const int n = nt * 8 + 2 * c + (e & 1);
-                    store_from_float(p.y, p.y_dtype, o + n, fmaf(gam, ws[nt][e], md[nt][e]));
-                }
-            }
-        }
-        // S = e^{lc_C} S + K^T diag(e^{lc_C - lc}) D: warp -> 16 rows of d
+            for (int e = 0; e < 4; e++)
+                ad[nt][e] = sm.u[8 * nt + 2 * c + (e & 1)][jr + g + 8 * (e >> 1)] - ad[nt][e];
+        if (more) cp_async_wait<1>();
+        else cp_async_wait<0>();
+        __syncthreads();  // M and K of this chunk are in shared memory; U read by every warp
+        if (more) chain_load_u(sm, p, vrow0 + (ci + 1) * kC, j0, par ^ 1, tid);
+        // ---- Y = e^lc Q S + M D for rows t in [32 dh, 32 dh + 32) ----
         {
-            float kd[4][4] = {};
-            const int d0 = 16 * warp;
-            gemm16<true, false, 4>(kd, &sm.khi[0][0], &sm.klo[0][0], kP, &sm.ethi[0][0], &sm.etlo[0][0], kPc, d0, 0, kC,
-                                   lane);
-            const float gC = expf(lcC);
+            const int tt = 32 * dh;
 #pragma unroll
-            for (int nt = 0; nt < 4; nt++)
+            for (int n4 = 0; n4 < 4; n4++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) y[n4][e] *= expf(lc[tt + 8 * n4 + 2 * c + (e & 1)]);
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                if (16 * ks >= tt + 32) break;  // M[t][i] = 0 for i > t
+                uint32_t ah[4], al[4];
+                afrag(ad, ks, ah, al);
+#pragma unroll
+                for (int np = 0; np < 2; np++) {
+                    uint32_t bh[4], bl[4];
+                    ldb2(bh, &sm.mhi[0][0], kPc, tt + 16 * np, 16 * ks, lane);
+                    ldb2(bl, &sm.mlo[0][0], kPc, tt + 16 * np, 16 * ks, lane);
+                    mma3x2(y[2 * np], y[2 * np + 1], ah, al, bh, bl);
+                }
+            }
+#pragma unroll
+            for (int n4 = 0; n4 < 4; n4++)
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const int r = d0 + g + (e >> 1) * 8, n = nt * 8 + 2 * c + (e & 1);
-                    const float x = fmaf(gC, sm.s[r][n], kd[nt][e]);
-                    sm.s[r][n] = x;
-                    split_store(&sm.sthi[n][r], &sm.stlo[n][r], x);
+                    const int t = ci * kC + tt + 8 * n4 + 2 * c + (e & 1);
+                    if (t < p.n)
+                        store_from_float(p.y, p.y_dtype,
+                                         ((long long)b * p.n + t) * p.y_stride + (long long)h * kDv + j0 + jr + g +
+                                             8 * (e >> 1),
+                                         y[n4][e]);
                 }
         }
-        __syncthreads();  // S updated; M, K, D free
+        // ---- S = e^{lc_C} S + K^T diag(e^{lc_C - lc}) D over this warp's half of d ----
+        {
+            const float gC = expf(lcC);
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) s[nt][e] *= gC;
+            float fs[8][2];  // e^{lc_C - lc_t}, t = 8 nt + 2 c + e
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) fs[nt][e] = expf(lcC - lc[8 * nt + 2 * c + e]);
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                uint32_t ah[4], al[4];
+                afrag(ad, fs, ks, ah, al);
+#pragma unroll
+                for (int np = 0; np < 4; np++) {
+                    uint32_t bh[4], bl[4];
+                    ldb2_t(bh, &sm.khi[0][0], kP, dbase + 16 * np, 16 * ks, lane);
+                    ldb2_t(bl, &sm.klo[0][0], kP, dbase + 16 * np, 16 * ks, lane);
+                    mma3x2(s[2 * np], s[2 * np + 1], ah, al, bh, bl);
+                }
+            }
+        }
+        __syncthreads();  // M, K free
         if (more) chain_load_mk(sm, p, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC, tid);
     }
-    for (int i = tid; i < kDk * kDvb; i += 256) S[(long long)(i / kDvb) * kDv + j0 + i % kDvb] = sm.s[i / kDvb][i % kDvb];
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            S[(long long)(dbase + 8 * nt + 2 * c + (e & 1)) * kDv + j0 + jr + g + 8 * (e >> 1)] = s[nt][e];
 }
 
 // ---------------------------------------------------------------- gated RMSNorm (layer path)
@@ -633,7 +740,7 @@ static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t strea
     cudaFuncSetAttribute(gdn_pf_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
     cudaFuncSetAttribute(gdn_pf_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chain_smem);
     gdn_pf_chunk_kernel<<<dim3(nC, p.Hv, p.B), 256, chunk_smem, stream>>>(p);
-    gdn_pf_chain_kernel<<<dim3(p.Hv * (kDv / kDvb), p.B), 256, chain_smem, stream>>>(p);
+    gdn_pf_chain_kernel<<<dim3(p.Hv * (kDv / kDvb), p.B), kChainThreads, chain_smem, stream>>>(p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 
