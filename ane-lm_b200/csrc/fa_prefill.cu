@@ -723,17 +723,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
-        cudaDriverEntryPointQueryResult q;
-        void* f = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }
-    return fn;
-}
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tc::tmap_encode_fn(); }
 
 // 2D fp16 tensor map, inner dimension `cols` (contiguous), 128B swizzle, box {64, box_rows}.
 bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {

@@ -42,6 +42,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc100.cuh"
 
 namespace anelm {
 
@@ -62,15 +63,6 @@ __device__ __forceinline__ void split_store(__half* hi, __half* lo, float x) {
     *lo = __float2half_rn(x - __half2float(h));
 }
 
-// A (16 x 16) at (r0, k0) of a row-major tile base[r][k]
-__device__ __forceinline__ void lda(uint32_t (&a)[4], const __half* base, int pitch, int r0, int k0, int lane) {
-    ldmatrix_x4(smem_u32(base + (r0 + (lane & 15)) * pitch + k0 + (lane >> 4) * 8), a[0], a[1], a[2], a[3]);
-}
-// A (16 x 16) at (r0, k0) of A[r][k] = base[k][r] (the tile is stored transposed)
-__device__ __forceinline__ void lda_t(uint32_t (&a)[4], const __half* base, int pitch, int r0, int k0, int lane) {
-    const int mat = lane >> 3, i = lane & 7;
-    ldmatrix_x4_trans(smem_u32(base + (k0 + i + (mat >> 1) * 8) * pitch + r0 + (mat & 1) * 8), a[0], a[1], a[2], a[3]);
-}
 // B (16 x 8) fragments of two n-tiles n0, n0 + 8 at k0, with B[k][n] = base[n][k]
 __device__ __forceinline__ void ldb2(uint32_t (&b)[4], const __half* base, int pitch, int n0, int k0, int lane) {
     const int mat = lane >> 3, i = lane & 7;
@@ -81,46 +73,6 @@ __device__ __forceinline__ void ldb2_t(uint32_t (&b)[4], const __half* base, int
     const int mat = lane >> 3, i = lane & 7;
     ldmatrix_x4_trans(smem_u32(base + (k0 + i + (mat & 1) * 8) * pitch + n0 + (mat >> 1) * 8), b[0], b[1], b[2], b[3]);
 }
-// acc[NT] (16 rows x 8 NT columns) += A[r0.., 0..K) B[0..K, n0..); A and B as hi / lo tiles.
-// TA: A stored transposed; TB: B stored [k][n] (else [n][k]).  Per k-step all fragments are
-// loaded first and each of the three product terms is issued across the NT accumulators in
-// turn, so consecutive MMAs into one accumulator are NT instructions apart.
-template <bool TA, bool TB, int NT>
-__device__ __forceinline__ void gemm16(float (&acc)[NT][4], const __half* ahi, const __half* alo, int pa,
-                                       const __half* bhi, const __half* blo, int pb, int r0, int n0, int K, int lane) {
-    static_assert(NT % 2 == 0, "n-tiles come in pairs");
-#pragma unroll
-    for (int k0 = 0; k0 < K; k0 += 16) {
-        uint32_t ah[4], al[4], bh[NT / 2][4], bl[NT / 2][4];
-        if (TA) {
-            lda_t(ah, ahi, pa, r0, k0, lane);
-            lda_t(al, alo, pa, r0, k0, lane);
-        } else {
-            lda(ah, ahi, pa, r0, k0, lane);
-            lda(al, alo, pa, r0, k0, lane);
-        }
-#pragma unroll
-        for (int np = 0; np < NT / 2; np++) {
-            if (TB) {
-                ldb2_t(bh[np], bhi, pb, n0 + 16 * np, k0, lane);
-                ldb2_t(bl[np], blo, pb, n0 + 16 * np, k0, lane);
-            } else {
-                ldb2(bh[np], bhi, pb, n0 + 16 * np, k0, lane);
-                ldb2(bl[np], blo, pb, n0 + 16 * np, k0, lane);
-            }
-        }
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-            mma_16816(acc[nt], ah[0], ah[1], ah[2], ah[3], bh[nt / 2][2 * (nt & 1)], bh[nt / 2][2 * (nt & 1) + 1]);
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-            mma_16816(acc[nt], al[0], al[1], al[2], al[3], bh[nt / 2][2 * (nt & 1)], bh[nt / 2][2 * (nt & 1) + 1]);
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-            mma_16816(acc[nt], ah[0], ah[1], ah[2], ah[3], bl[nt / 2][2 * (nt & 1)], bl[nt / 2][2 * (nt & 1) + 1]);
-    }
-}
-
 // Named barrier over `count` threads (a multiple of 32) of this CTA.
 __device__ __forceinline__ void named_bar_sync_cta(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
@@ -289,28 +241,79 @@ __global__ void __launch_bounds__(256) gdn_pf_pack_kernel(const GdnPrefillParams
 
 // ---------------------------------------------------------------- per-chunk quantities
 
+// One CTA per (chunk, value head, sequence), 256 threads, two tcgen05 GEMMs (fp32 accumulators in
+// TMEM, fp16 operands staged by TMA with the 128-byte swizzle, each product as three MMAs over the
+// hi / lo planes: hi*hi + lo*hi + hi*lo):
+//   GEMM 1  [K; Q] K^T  (M 128 = 64 K rows + 64 Q rows, N 64, K 128): K K^T -> A, Q K^T -> M;
+//   GEMM 2  [T'; T''] [K | V]  (M 128, N 256, K 64) with T' = T diag(beta e^{lt}), T'' = T diag(beta):
+//           its diagonal blocks are W = T' K and U = T'' V (the off-diagonal ones are not used).
+// The operand buffer of each plane is [K d0-63 | Q d0-63 | K d64-127 | Q d64-127] (8 KB boxes of
+// 64 rows x 128 bytes): read as the K-major A of GEMM 1 (two 16 KB boxes of 128 rows), as its
+// K-major B (the K rows), and, once V has replaced Q, as the MN-major B of GEMM 2 (N boxes K0, V0,
+// K1, V1, 8 KB apart).  T = (I + A)^{-1} by forward substitution on the CUDA cores in between.
+constexpr int kChunkThreads = 256;
+constexpr int kOpPlane = 32768;            // bytes of one plane of the operand buffer
+constexpr int kTPlane = 16384;             // bytes of one plane of [T'; T''] (128 rows x 128 bytes)
+constexpr int kAtRow = 80;                 // fp32 words per row of A^T (4 groups of 16 + padding)
+constexpr uint32_t kChunkTmemCols = 256;
 struct ChunkSmem {
-    __half khi[kC][kP], klo[kC][kP];
-    __half qhi[kC][kP], qlo[kC][kP];    // Q, then V
-    float at[kC][kC];                   // A^T, rows interleaved: at[i][16 (t % 4) + t / 4] = A[t][i]
-    __half thi[kC][kPc], tlo[kC][kPc];  // T scaled by columns (W's, then U's factors)
+    uint8_t op[2][kOpPlane];               // hi, lo planes (1024-byte aligned)
+    union {
+        uint8_t t[2][kTPlane];             // [T'; T''] hi, lo (K-major, 128-byte swizzle)
+        float at[kC][kAtRow];              // A^T, rows interleaved: at[i][20 (t % 4) + t / 4] = A[t][i]
+    };
     float lc[kC], lt[kC], bt[kC];
+    uint64_t bar[4];                       // K+Q loaded, GEMM 1 done, V loaded, GEMM 2 done
+    uint32_t tmem_slot;
+    int abort;
 };
+static_assert(kC * kAtRow * 4 <= 2 * kTPlane, "A^T fits the T buffer");
 
-__global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParams p) {
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    ChunkSmem& sm = *reinterpret_cast<ChunkSmem*>(smem_raw);
+// byte offset of element (row, col) (fp16, 64 columns per 128-byte row) in a 128B-swizzled tile
+__device__ __forceinline__ int sw128_off(int row, int col) {
+    return row * 128 + ((((col >> 3) ^ row) & 7) << 4) + (col & 7) * 2;
+}
+
+__global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                                      const __grid_constant__ CUtensorMap tmQ,
+                                                                      const __grid_constant__ CUtensorMap tmV,
+                                                                      const GdnPrefillParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    ChunkSmem& sm = *reinterpret_cast<ChunkSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int ci = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, c = lane & 3;
     const int kh = h / (p.Hv / p.Hk);
     const int t0 = ci * kC;
     const long long krow = ((long long)b * p.Hk + kh) * p.T_pad + t0;
     const long long vrow = ((long long)b * p.Hv + h) * p.T_pad + t0;
-    cp_tile_hl(&sm.khi[0][0], &sm.klo[0][0], kP, p.kh + krow * kDk, p.q_plane, kC, kDk, tid, 256);
-    cp_tile_hl(&sm.qhi[0][0], &sm.qlo[0][0], kP, p.qh + krow * kDk, p.q_plane, kC, kDk, tid, 256);
-    cp_async_commit();
-    if (warp == 0) {  // inclusive prefix sum of log g over the chunk (two tokens per lane)
+    volatile int* abort = &sm.abort;
+    uint64_t* bar = sm.bar;
+    if (tid == 0) {
+        sm.abort = 0;
+        for (int i = 0; i < 4; i++) tc::mbar_init(&bar[i], 1);
+        tc::fence_barrier_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(&sm.tmem_slot, kChunkTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = sm.tmem_slot;
+    const uint32_t aop = (uint32_t)__cvta_generic_to_shared(&sm.op[0][0]);
+    const uint32_t at_ = (uint32_t)__cvta_generic_to_shared(&sm.t[0][0]);
+    if (tid == 0) {  // K and Q, both planes, into the operand buffers
+        tc::prefetch_tmap(&tmK);
+        tc::prefetch_tmap(&tmQ);
+        tc::mbar_arrive_expect_tx(&bar[0], 2 * kOpPlane);
+        for (int pl = 0; pl < 2; pl++)
+            for (int kb = 0; kb < 2; kb++) {
+                tc::tma_load_3d(&sm.op[pl][kb * 16384], &tmK, &bar[0], kb * 64, (int)krow, pl);
+                tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmQ, &bar[0], kb * 64, (int)krow, pl);
+            }
+    }
+    if (warp == 1) {  // inclusive prefix sum of log g over the chunk (two tokens per lane)
         const float g0 = p.lg[vrow + 2 * lane], g1 = p.lg[vrow + 2 * lane + 1];
         float s = g0 + g1;
 #pragma unroll
@@ -327,32 +330,68 @@ __global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParam
         sm.bt[2 * lane] = p.beta[vrow + 2 * lane];
         sm.bt[2 * lane + 1] = p.beta[vrow + 2 * lane + 1];
     }
-    cp_async_wait<0>();
-    __syncthreads();
-    // K K^T -> A (strictly lower), Q K^T -> M (lower incl. diagonal): warp -> 16 rows x 32 columns
-    {
-        const int r0 = 16 * (warp & 3), n0 = 32 * (warp >> 2);
-        float kk[4][4] = {}, qk[4][4] = {};
-        gemm16<false, false, 4>(kk, &sm.khi[0][0], &sm.klo[0][0], kP, &sm.khi[0][0], &sm.klo[0][0], kP, r0, n0, kDk, lane);
-        gemm16<false, false, 4>(qk, &sm.qhi[0][0], &sm.qlo[0][0], kP, &sm.khi[0][0], &sm.klo[0][0], kP, r0, n0, kDk, lane);
-        __half* mhi = p.mh + vrow * kC;
+    if (tid == 0) {  // GEMM 1: [K; Q] K^T -> TMEM columns [0, 64)
+        if (tc::mbar_wait(&bar[0], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {
+            tc::tc_fence_after();
+            constexpr uint32_t id1 = tc::idesc_f16_f32(128, kC);
 #pragma unroll
-        for (int nt = 0; nt < 4; nt++)
+            for (int term = 0; term < 3; term++) {
+                const uint32_t pa = aop + (term == 1 ? kOpPlane : 0), pb = aop + (term == 2 ? kOpPlane : 0);
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int r = r0 + g + (e >> 1) * 8, i = n0 + nt * 8 + 2 * c + (e & 1);
-                sm.at[i][16 * (r & 3) + (r >> 2)] = i < r ? sm.bt[r] * expf(sm.lt[r] - sm.lc[i]) * kk[nt][e] : 0.f;
-                put_hl(mhi, p.m_plane, r * kC + i, i <= r ? expf(sm.lc[r] - sm.lc[i]) * qk[nt][e] : 0.f);
+                for (int kb = 0; kb < 2; kb++)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ks++)
+                        tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(pa + kb * 16384 + ks * 32),
+                                       tc::desc_kmajor_sw128(pb + kb * 16384 + ks * 32), id1, (term | kb | ks) != 0);
             }
+            tc::mma_commit(&bar[1]);
+        }
+    }
+    // ---- epilogue 1: A (rows 0-63) into shared memory, M (rows 64-127) to global ----
+    const bool ok1 = tc::mbar_wait(&bar[1], 0, p.err, ANELM_ERR_TIMEOUT, abort);
+    tc::tc_fence_after();
+    __syncthreads();  // lc / lt / bt visible; every thread past GEMM 1 (Q no longer read)
+    if (tid == 0 && ok1) {  // V replaces Q in the operand buffers
+        tc::prefetch_tmap(&tmV);
+        tc::mbar_arrive_expect_tx(&bar[2], kOpPlane);
+        for (int pl = 0; pl < 2; pl++)
+            for (int kb = 0; kb < 2; kb++)
+                tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmV, &bar[2], kb * 64, (int)vrow, pl);
+    }
+    {
+        const int q = warp & 3, hc = warp >> 2;
+        const int r = 32 * q + lane;
+        uint32_t x[32];
+        tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32 * hc, x);
+        tc::tmem_ld_wait();
+        if (r < kC) {  // A_ti = beta_t e^{lt_t - lc_i} k_t.k_i (i < t)
+            const int t = r;
+            const float bt = sm.bt[t], lt = sm.lt[t];
+            float* dst = &sm.at[0][20 * (t & 3) + (t >> 2)];
+#pragma unroll
+            for (int c = 0; c < 32; c++) {
+                const int i = 32 * hc + c;
+                dst[i * kAtRow] = i < t ? bt * expf(lt - sm.lc[i]) * __uint_as_float(x[c]) : 0.f;
+            }
+        } else {  // M_ti = e^{lc_t - lc_i} q_t.k_i (i <= t), hi / lo planes
+            const int t = r - kC;
+            const float lct = sm.lc[t];
+            __half* mhi = p.mh + (vrow + t) * kC + 32 * hc;
+#pragma unroll
+            for (int c8 = 0; c8 < 4; c8++) {
+                float v[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const int i = 32 * hc + 8 * c8 + e;
+                    v[e] = i <= t ? expf(lct - sm.lc[i]) * __uint_as_float(x[8 * c8 + e]) : 0.f;
+                }
+                put_hl8(mhi, p.m_plane, 8 * c8, v);
+            }
+        }
     }
     if (tid < kC) p.lcb[vrow + tid] = sm.lc[tid];
-    __syncthreads();  // Q no longer needed: V into its buffers
-    cp_tile_hl(&sm.qhi[0][0], &sm.qlo[0][0], kP, p.vh + vrow * kDv, p.v_plane, kC, kDv, tid, 256);
-    cp_async_commit();
-    // T = (I + A)^{-1} by forward substitution, one column j per 4 threads: x_t = [t == j] - sum_{i<t} A_ti x_i,
-    // right-looking: thread part pt keeps the running sums r of rows t = 4m + pt; once x_t is final (in the
-    // thread owning row t) it is broadcast to the 4 threads, which add A[4m + pt][t] x_t to their rows'
-    // sums (column t of A read as four 16-byte words).  A is strictly lower, so rows <= t add zeros.
+    __syncthreads();  // A^T complete
+    // ---- T = (I + A)^{-1} by forward substitution, one column j per 4 threads, right-looking ----
     const int j = tid >> 2, pt = tid & 3;
     float xs[kC / 4], rs[kC / 4];
 #pragma unroll
@@ -361,54 +400,95 @@ __global__ void __launch_bounds__(256) gdn_pf_chunk_kernel(const GdnPrefillParam
     for (int t = 0; t < kC; t++) {
         const float x = __shfl_sync(0xffffffffu, (t == j ? 1.0f : 0.0f) - rs[t >> 2], (lane & ~3) | (t & 3));
         if (pt == (t & 3)) xs[t >> 2] = x;
-        const float4* col = reinterpret_cast<const float4*>(&sm.at[t][16 * pt]);
+        const float4* col = reinterpret_cast<const float4*>(&sm.at[t][20 * pt]);
 #pragma unroll
-        for (int q = 0; q < kC / 16; q++) {
-            if (16 * q + 15 <= t) continue;  // rows 4m + pt <= 4m + 3 <= t of this word are final
-            const float4 a4 = col[q];
-            rs[4 * q] = fmaf(a4.x, x, rs[4 * q]);
-            rs[4 * q + 1] = fmaf(a4.y, x, rs[4 * q + 1]);
-            rs[4 * q + 2] = fmaf(a4.z, x, rs[4 * q + 2]);
-            rs[4 * q + 3] = fmaf(a4.w, x, rs[4 * q + 3]);
+        for (int q4 = 0; q4 < kC / 16; q4++) {
+            if (16 * q4 + 15 <= t) continue;  // rows 4m + pt <= 4m + 3 <= t of this word are final
+            const float4 a4 = col[q4];
+            rs[4 * q4] = fmaf(a4.x, x, rs[4 * q4]);
+            rs[4 * q4 + 1] = fmaf(a4.y, x, rs[4 * q4 + 1]);
+            rs[4 * q4 + 2] = fmaf(a4.z, x, rs[4 * q4 + 2]);
+            rs[4 * q4 + 3] = fmaf(a4.w, x, rs[4 * q4 + 3]);
         }
     }
-    {  // T' = T diag(beta e^{lt}) (W's factor) as hi / lo; column j belongs to this thread group
-        const float fw = sm.bt[j] * expf(sm.lt[j]);
+    __syncthreads();  // A^T no longer read: its space becomes [T'; T'']
+    {  // T' = T diag(beta e^{lt}) in rows 0-63, T'' = T diag(beta) in rows 64-127, column j
+        const float fw = sm.bt[j] * expf(sm.lt[j]), fu = sm.bt[j];
 #pragma unroll
-        for (int m = 0; m < kC / 4; m++) split_store(&sm.thi[4 * m + pt][j], &sm.tlo[4 * m + pt][j], xs[m] * fw);
-    }
-    cp_async_wait<0>();
-    __syncthreads();
-    const int r0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);  // warp -> 16 rows x 64 columns of W / U
-    {  // W = T diag(beta e^{lt}) K
-        float w[8][4] = {};
-        gemm16<false, true, 8>(w, &sm.thi[0][0], &sm.tlo[0][0], kPc, &sm.khi[0][0], &sm.klo[0][0], kP, r0, n0, kC, lane);
-        __half* whi = p.wh + vrow * kDk;
+        for (int m = 0; m < kC / 4; m++) {
+            const int t = 4 * m + pt;
 #pragma unroll
-        for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int r = r0 + g + (e >> 1) * 8, n = n0 + nt * 8 + 2 * c + (e & 1);
-                put_hl(whi, p.v_plane, r * kDk + n, w[nt][e]);
+            for (int half = 0; half < 2; half++) {
+                const float v = xs[m] * (half ? fu : fw);
+                const __half hv = __float2half_rn(v);
+                const int off = sw128_off(half * kC + t, j);
+                *reinterpret_cast<__half*>(&sm.t[0][off]) = hv;
+                *reinterpret_cast<__half*>(&sm.t[1][off]) = __float2half_rn(v - __half2float(hv));
             }
+        }
     }
-    __syncthreads();  // T' read by every warp
-    {  // T'' = T diag(beta) (U's factor)
-        const float fu = sm.bt[j];
+    tc::fence_proxy_async_smem();
+    __syncthreads();  // [T'; T''] visible to the tensor core
+    if (tid == 0 && ok1) {  // GEMM 2: [T'; T''] [K0 V0 K1 V1] -> TMEM columns [0, 256)
+        if (tc::mbar_wait(&bar[2], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {
+            tc::tc_fence_after();
+            constexpr uint32_t id2 = tc::idesc_f16_f32_bmn(128, 256);
 #pragma unroll
-        for (int m = 0; m < kC / 4; m++) split_store(&sm.thi[4 * m + pt][j], &sm.tlo[4 * m + pt][j], xs[m] * fu);
-    }
-    __syncthreads();
-    {  // U = T diag(beta) V
-        float u[8][4] = {};
-        gemm16<false, true, 8>(u, &sm.thi[0][0], &sm.tlo[0][0], kPc, &sm.qhi[0][0], &sm.qlo[0][0], kP, r0, n0, kC, lane);
+            for (int term = 0; term < 3; term++) {
+                const uint32_t pa = at_ + (term == 1 ? kTPlane : 0), pb = aop + (term == 2 ? kOpPlane : 0);
 #pragma unroll
-        for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-            for (int e = 0; e < 4; e += 2) {
-                const int r = r0 + g + (e >> 1) * 8, n = n0 + nt * 8 + 2 * c;
-                *reinterpret_cast<float2*>(p.Ub + (vrow + r) * kDv + n) = make_float2(u[nt][e], u[nt][e + 1]);
+                for (int ks = 0; ks < 4; ks++)
+                    tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(pa + ks * 32), tc::desc_sw128(pb + ks * 16 * 128, 8192, 1024),
+                                   id2, (term | ks) != 0);
             }
+            tc::mma_commit(&bar[3]);
+        }
+    }
+    // ---- epilogue 2: W = T' K (rows 0-63) hi / lo, U = T'' V (rows 64-127) fp32 ----
+    if (tc::mbar_wait(&bar[3], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {
+        tc::tc_fence_after();
+        const int q = warp & 3, hc = warp >> 2;  // hc: key / value dims [64 hc, 64 hc + 64)
+        const int r = 32 * q + lane;
+        const bool is_w = r < kC;
+        const int t = is_w ? r : r - kC;
+        const uint32_t col0 = (is_w ? 0 : 64) + 128 * hc;
+#pragma unroll
+        for (int h32 = 0; h32 < 2; h32++) {
+            uint32_t x[32];
+            tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + col0 + 32 * h32, x);
+            tc::tmem_ld_wait();
+            const int d0 = 64 * hc + 32 * h32;
+            if (is_w) {
+                __half* whi = p.wh + (vrow + t) * kDk + d0;
+#pragma unroll
+                for (int c8 = 0; c8 < 4; c8++) {
+                    float v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] = __uint_as_float(x[8 * c8 + e]);
+                    put_hl8(whi, p.v_plane, 8 * c8, v);
+                }
+            } else {
+                float4* u = reinterpret_cast<float4*>(p.Ub + (vrow + t) * kDv + d0);
+#pragma unroll
+                for (int c4 = 0; c4 < 8; c4++)
+                    u[c4] = make_float4(__uint_as_float(x[4 * c4]), __uint_as_float(x[4 * c4 + 1]),
+                                        __uint_as_float(x[4 * c4 + 2]), __uint_as_float(x[4 * c4 + 3]));
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        if (lane == 0) {  // nothing of this CTA's may still be in flight when its TMEM is released
+            for (int i = 0; i < 4; i++)
+                for (uint32_t n = 0; n < tc::kWaitPolls && !tc::mbar_try_wait(&bar[i], 0); n++) {
+                    if (i == 2 && !ok1) break;  // V was never requested
+                    if ((i == 1 || i == 3) && *abort) break;
+                }
+        }
+        __syncwarp();
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kChunkTmemCols);
     }
 }
 
@@ -430,6 +510,7 @@ struct ChainSmem {
     __half mhi[kC][kPc], mlo[kC][kPc]; // M[t][i]
     float u[kC][kDvb + 4];             // U columns of this block
     float lc[2][kC];                   // in-chunk cumulative log decay, by chunk parity
+    float eg[kC], ef[kC];              // e^{lc_t}, e^{lc_C - lc_t} of the current chunk
     float xd[4][32][32];               // partial W S of each warp, [warp][register][lane]
     float xy[4][32][32];               // partial Q S
 };
@@ -461,15 +542,26 @@ __device__ __forceinline__ void afrag(const float (&acc)[NT][4], int ks, uint32_
     split2(acc[t1][0], acc[t1][1], ah[2], al[2]);
     split2(acc[t1][2], acc[t1][3], ah[3], al[3]);
 }
-// acc[0 / 1] += A B for the n-tile pair of b (hi / lo fragments from ldb2 / ldb2_t): three terms
-__device__ __forceinline__ void mma3x2(float (&a0)[4], float (&a1)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
-                                       const uint32_t (&bh)[4], const uint32_t (&bl)[4]) {
-    mma_16816(a0, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
-    mma_16816(a1, ah[0], ah[1], ah[2], ah[3], bh[2], bh[3]);
-    mma_16816(a0, al[0], al[1], al[2], al[3], bh[0], bh[1]);
-    mma_16816(a1, al[0], al[1], al[2], al[3], bh[2], bh[3]);
-    mma_16816(a0, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
-    mma_16816(a1, ah[0], ah[1], ah[2], ah[3], bl[2], bl[3]);
+// acc[2 np], acc[2 np + 1] += A B over NP n-tile pairs (fragments bh[np], bl[np]), issued term by
+// term across all 2 NP accumulators so dependent MMAs are 2 NP instructions apart
+template <int NP>
+__device__ __forceinline__ void mma3_tm(float (*acc)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                        const uint32_t (&bh)[NP][4], const uint32_t (&bl)[NP][4]) {
+#pragma unroll
+    for (int np = 0; np < NP; np++) {
+        mma_16816(acc[2 * np], ah[0], ah[1], ah[2], ah[3], bh[np][0], bh[np][1]);
+        mma_16816(acc[2 * np + 1], ah[0], ah[1], ah[2], ah[3], bh[np][2], bh[np][3]);
+    }
+#pragma unroll
+    for (int np = 0; np < NP; np++) {
+        mma_16816(acc[2 * np], al[0], al[1], al[2], al[3], bh[np][0], bh[np][1]);
+        mma_16816(acc[2 * np + 1], al[0], al[1], al[2], al[3], bh[np][2], bh[np][3]);
+    }
+#pragma unroll
+    for (int np = 0; np < NP; np++) {
+        mma_16816(acc[2 * np], ah[0], ah[1], ah[2], ah[3], bl[np][0], bl[np][1]);
+        mma_16816(acc[2 * np + 1], ah[0], ah[1], ah[2], ah[3], bl[np][2], bl[np][3]);
+    }
 }
 
 // cp.async of a chunk's W and Q (read by [W; Q] S)
@@ -541,14 +633,18 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const Gd
             afrag(s, ks, ah, al);
             const int k0 = dbase + 16 * ks;
 #pragma unroll
-            for (int np = 0; np < 4; np++) {
-                uint32_t bh[4], bl[4];
-                ldb2(bh, &sm.whi[0][0], kP, 16 * np, k0, lane);
-                ldb2(bl, &sm.wlo[0][0], kP, 16 * np, k0, lane);
-                mma3x2(ad[2 * np], ad[2 * np + 1], ah, al, bh, bl);
-                ldb2(bh, &sm.qhi[0][0], kP, 16 * np, k0, lane);
-                ldb2(bl, &sm.qlo[0][0], kP, 16 * np, k0, lane);
-                mma3x2(ay[2 * np], ay[2 * np + 1], ah, al, bh, bl);
+            for (int n2 = 0; n2 < 2; n2++) {
+                uint32_t bwh[2][4], bwl[2][4], bqh[2][4], bql[2][4];
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    const int n0 = 32 * n2 + 16 * q;
+                    ldb2(bwh[q], &sm.whi[0][0], kP, n0, k0, lane);
+                    ldb2(bwl[q], &sm.wlo[0][0], kP, n0, k0, lane);
+                    ldb2(bqh[q], &sm.qhi[0][0], kP, n0, k0, lane);
+                    ldb2(bql[q], &sm.qlo[0][0], kP, n0, k0, lane);
+                }
+                mma3_tm<2>(&ad[4 * n2], ah, al, bwh, bwl);
+                mma3_tm<2>(&ay[4 * n2], ah, al, bqh, bql);
             }
         }
         __syncthreads();  // W, Q free
@@ -574,6 +670,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const Gd
         __syncthreads();  // U and lc of this chunk are in shared memory
         const float* lc = sm.lc[par];
         const float lcC = lc[kC - 1];
+        if (tid < kC) {  // published by the barrier before M D
+            sm.eg[tid] = expf(lc[tid]);
+            sm.ef[tid] = expf(lcC - lc[tid]);
+        }
         // D = U - W S (in place of ad)
 #pragma unroll
         for (int nt = 0; nt < 8; nt++)
@@ -590,19 +690,19 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const Gd
 #pragma unroll
             for (int n4 = 0; n4 < 4; n4++)
 #pragma unroll
-                for (int e = 0; e < 4; e++) y[n4][e] *= expf(lc[tt + 8 * n4 + 2 * c + (e & 1)]);
+                for (int e = 0; e < 4; e++) y[n4][e] *= sm.eg[tt + 8 * n4 + 2 * c + (e & 1)];
 #pragma unroll
             for (int ks = 0; ks < 4; ks++) {
                 if (16 * ks >= tt + 32) break;  // M[t][i] = 0 for i > t
                 uint32_t ah[4], al[4];
                 afrag(ad, ks, ah, al);
+                uint32_t bh[2][4], bl[2][4];
 #pragma unroll
                 for (int np = 0; np < 2; np++) {
-                    uint32_t bh[4], bl[4];
-                    ldb2(bh, &sm.mhi[0][0], kPc, tt + 16 * np, 16 * ks, lane);
-                    ldb2(bl, &sm.mlo[0][0], kPc, tt + 16 * np, 16 * ks, lane);
-                    mma3x2(y[2 * np], y[2 * np + 1], ah, al, bh, bl);
+                    ldb2(bh[np], &sm.mhi[0][0], kPc, tt + 16 * np, 16 * ks, lane);
+                    ldb2(bl[np], &sm.mlo[0][0], kPc, tt + 16 * np, 16 * ks, lane);
                 }
+                mma3_tm<2>(y, ah, al, bh, bl);
             }
 #pragma unroll
             for (int n4 = 0; n4 < 4; n4++)
@@ -627,18 +727,18 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const Gd
 #pragma unroll
             for (int nt = 0; nt < 8; nt++)
 #pragma unroll
-                for (int e = 0; e < 2; e++) fs[nt][e] = expf(lcC - lc[8 * nt + 2 * c + e]);
+                for (int e = 0; e < 2; e++) fs[nt][e] = sm.ef[8 * nt + 2 * c + e];
 #pragma unroll
             for (int ks = 0; ks < 4; ks++) {
                 uint32_t ah[4], al[4];
                 afrag(ad, fs, ks, ah, al);
+                uint32_t bh[4][4], bl[4][4];
 #pragma unroll
                 for (int np = 0; np < 4; np++) {
-                    uint32_t bh[4], bl[4];
-                    ldb2_t(bh, &sm.khi[0][0], kP, dbase + 16 * np, 16 * ks, lane);
-                    ldb2_t(bl, &sm.klo[0][0], kP, dbase + 16 * np, 16 * ks, lane);
-                    mma3x2(s[2 * np], s[2 * np + 1], ah, al, bh, bl);
+                    ldb2_t(bh[np], &sm.khi[0][0], kP, dbase + 16 * np, 16 * ks, lane);
+                    ldb2_t(bl[np], &sm.klo[0][0], kP, dbase + 16 * np, 16 * ks, lane);
                 }
+                mma3_tm<4>(s, ah, al, bh, bl);
             }
         }
         __syncthreads();  // M, K free
@@ -734,12 +834,30 @@ static void carve(GdnPrefillParams& p, void* ws, bool layer) {
     }
 }
 
+// 3D fp16 tensor map over the hi / lo planes of a [rows][128] operand: box {64, 64, 1}, 128B swizzle
+static bool make_plane_map(CUtensorMap* m, const __half* base, uint64_t rows, long long plane) {
+    auto fn = tc::tmap_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {128, rows, 2};
+    cuuint64_t strides[2] = {256, (cuuint64_t)plane * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)kC, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t stream) {
     const int nC = p.T_pad / kC;
-    const size_t chunk_smem = sizeof(ChunkSmem), chain_smem = sizeof(ChainSmem);
+    const size_t chunk_smem = sizeof(ChunkSmem) + 1024, chain_smem = sizeof(ChainSmem);
+    CUtensorMap mK, mQ, mV;
+    if (!make_plane_map(&mK, p.kh, (uint64_t)p.B * p.Hk * p.T_pad, p.q_plane) ||
+        !make_plane_map(&mQ, p.qh, (uint64_t)p.B * p.Hk * p.T_pad, p.q_plane) ||
+        !make_plane_map(&mV, p.vh, (uint64_t)p.B * p.Hv * p.T_pad, p.v_plane))
+        return ANELM_ERR_CUDA;
     cudaFuncSetAttribute(gdn_pf_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
     cudaFuncSetAttribute(gdn_pf_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chain_smem);
-    gdn_pf_chunk_kernel<<<dim3(nC, p.Hv, p.B), 256, chunk_smem, stream>>>(p);
+    gdn_pf_chunk_kernel<<<dim3(nC, p.Hv, p.B), kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, p);
     gdn_pf_chain_kernel<<<dim3(p.Hv * (kDv / kDvb), p.B), kChainThreads, chain_smem, stream>>>(p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }

@@ -6,10 +6,24 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <stdint.h>
 
 namespace anelm {
 namespace tc {
+
+// The driver's tensor-map encoder (cuTensorMapEncodeTiled), looked up once.
+inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
 
 // ---------------------------------------------------------------- mbarrier
 
