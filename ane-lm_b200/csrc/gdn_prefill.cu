@@ -52,8 +52,6 @@ constexpr int kC = 64;     // chunk length
 constexpr int kDk = 128;   // key head dim of these kernels
 constexpr int kDv = 128;   // value head dim
 constexpr int kDvb = 32;   // state columns per chain CTA
-constexpr int kP = kDk + 8;   // fp16 pitch of 128-wide tiles (272 B: ldmatrix rows hit distinct banks)
-constexpr int kPc = kC + 8;   // fp16 pitch of 64-wide tiles (144 B)
 
 // ---------------------------------------------------------------- fragments (mma.sync m16n8k16)
 
@@ -63,30 +61,27 @@ __device__ __forceinline__ void split_store(__half* hi, __half* lo, float x) {
     *lo = __float2half_rn(x - __half2float(h));
 }
 
-// B (16 x 8) fragments of two n-tiles n0, n0 + 8 at k0, with B[k][n] = base[n][k]
-__device__ __forceinline__ void ldb2(uint32_t (&b)[4], const __half* base, int pitch, int n0, int k0, int lane) {
-    const int mat = lane >> 3, i = lane & 7;
-    ldmatrix_x4(smem_u32(base + (n0 + i + (mat >> 1) * 8) * pitch + k0 + (mat & 1) * 8), b[0], b[1], b[2], b[3]);
+// B (16 x 8) fragments of two n-tiles n0, n0 + 8 at k0 (ldmatrix), with B[k][n] = T[n][k] (ldb2_sw)
+// or B[k][n] = T[k][n] (ldb2_t_sw) for a tile T in shared memory.
+// Tiles are in the TMA's 128B-swizzled layout of 64-column boxes: element (row, col) of a tile at shared
+// address `tile` lives in box col / 64, 8192 bytes per box of 64 rows.
+__device__ __forceinline__ uint32_t sw_addr(uint32_t tile, int row, int col) {
+    return tile + (uint32_t)((col >> 6) * 8192 + row * 128 + ((((col & 63) >> 3) ^ row) & 7) * 16 + (col & 7) * 2);
 }
-// the same with B[k][n] = base[k][n]
-__device__ __forceinline__ void ldb2_t(uint32_t (&b)[4], const __half* base, int pitch, int n0, int k0, int lane) {
+__device__ __forceinline__ void ldb2_sw(uint32_t (&b)[4], uint32_t tile, int n0, int k0, int lane) {
     const int mat = lane >> 3, i = lane & 7;
-    ldmatrix_x4_trans(smem_u32(base + (k0 + i + (mat & 1) * 8) * pitch + n0 + (mat >> 1) * 8), b[0], b[1], b[2], b[3]);
+    ldmatrix_x4(sw_addr(tile, n0 + i + (mat >> 1) * 8, k0 + (mat & 1) * 8), b[0], b[1], b[2], b[3]);
 }
-// Named barrier over `count` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void ldb2_t_sw(uint32_t (&b)[4], uint32_t tile, int n0, int k0, int lane) {
+    const int mat = lane >> 3, i = lane & 7;
+    ldmatrix_x4_trans(sw_addr(tile, k0 + i + (mat & 1) * 8, n0 + (mat >> 1) * 8), b[0], b[1], b[2], b[3]);
+}
+// Named barrier over `count` threads (a multiple of 32) of this CTA: wait, or arrive without waiting.
 __device__ __forceinline__ void named_bar_sync_cta(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
-
-// 16-byte cp.async copies of `rows` rows of `cols` fp16 (hi and lo planes) into a pitched tile pair
-__device__ __forceinline__ void cp_tile_hl(__half* dhi, __half* dlo, int pitch, const __half* src, long long plane,
-                                           int rows, int cols, int tid, int nthreads) {
-    const int vpr = cols / 8;
-    for (int i = tid; i < rows * vpr; i += nthreads) {
-        const int r = i / vpr, cv = i % vpr;
-        cp_async_16(smem_u32(dhi + r * pitch + cv * 8), src + (long long)r * cols + cv * 8, 16);
-        cp_async_16(smem_u32(dlo + r * pitch + cv * 8), src + plane + (long long)r * cols + cv * 8, 16);
-    }
+__device__ __forceinline__ void named_bar_arrive_cta(uint32_t id, uint32_t count) {
+    asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---------------------------------------------------------------- snapshot
@@ -494,26 +489,38 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
 
 // ---------------------------------------------------------------- the recurrence over chunks
 
-// One chain CTA per (sequence, value head, 32 state columns j0 .. j0 + 32), four warps: warp
-// (jg, dh) = (warp / 2, warp % 2) keeps S^T rows j0 + 16 jg .. + 16 (state columns) times key dims
+// One chain CTA per (sequence, value head, 32 state columns j0 .. j0 + 32), eight warps.  State warp
+// w < 4, (jg, dh) = (w / 2, w % 2), keeps S^T rows j0 + 16 jg .. + 16 (state columns) times key dims
 // d in [64 dh, 64 dh + 64) in registers, in the accumulator layout of mma.m16n8k16, which is also
-// the A-operand layout: S^T feeds W S and Q S directly (as hi / lo pairs), and the state update
-// S^T += E^T K accumulates into the same registers.  The two warps of a column group hold the two
-// halves of d, so their partial W S and Q S sums meet in shared memory.  Per chunk and warp:
-//   [W; Q] S over its d half -> exchange -> D = U - W S (all 64 rows t), Y = e^lc Q S + M D for
-//   its 32 rows t, S = e^{lc_C} S + K^T (e^{lc_C - lc} D) for its d half.
-constexpr int kChainThreads = 128;
+// the A-operand layout: S^T feeds W S directly (as hi / lo pairs), and the state update
+// S^T += E^T K accumulates into the same registers.  The two state warps of a column group hold the
+// two halves of d, so their partial W S sums meet in shared memory.  Output warp 4 + w computes,
+// beside state warp w, Q S over the same d half from the state warp's S^T fragments (handed over
+// in shared memory) and then Y = e^lc Q S + M D for 32 rows t from the group's D fragments, so
+// only W S, D and the state update are on the recurrence's critical path.  Per chunk:
+//   state:  S^T fragments -> W S -> exchange -> D = U - W S -> D fragments -> S = e^{lc_C} S + K^T E
+//   output:                  Q S -> exchange ->                 e^lc Q S + M D -> Y
+constexpr int kChainThreads = 256;
 struct ChainSmem {
-    __half whi[kC][kP], wlo[kC][kP];   // W[t][d]
-    __half qhi[kC][kP], qlo[kC][kP];   // Q[t][d]
-    __half khi[kC][kP], klo[kC][kP];   // K[t][d]
-    __half mhi[kC][kPc], mlo[kC][kPc]; // M[t][i]
-    float u[kC][kDvb + 4];             // U columns of this block
+    // operand tiles in the TMA's 128B-swizzled layout (1024-byte aligned): [plane][box][64 rows][128 B]
+    uint8_t w[2][2][8192];             // W[t][d], d in boxes of 64
+    uint8_t q[2][2][8192];             // Q[t][d]
+    uint8_t k[2][2][8192];             // K[t][d]
+    uint8_t m[2][8192];                // M[t][i]
+    uint8_t u[8192];                   // U[t][j0 .. j0 + 32] fp32, 128-byte rows
     float lc[2][kC];                   // in-chunk cumulative log decay, by chunk parity
     float eg[kC], ef[kC];              // e^{lc_t}, e^{lc_C - lc_t} of the current chunk
-    float xd[4][32][32];               // partial W S of each warp, [warp][register][lane]
-    float xy[4][32][32];               // partial Q S
+    float xd[4][32][32];               // partial W S of each state warp, [warp][register][lane]
+    float xy[4][32][32];               // partial Q S of each output warp
+    uint32_t sa[4][4][8][32];          // S^T fragments of each state warp: [warp][k-step][hi 0-3, lo 0-3][lane]
+    uint32_t sdf[2][4][8][32];         // D fragments of each column group: [jg][k-step][8][lane]
+    uint64_t bar[3];                   // W+Q, U+lc, M+K of the chunk landed (one phase per chunk)
+    int abort;
 };
+// U[t][j] (fp32, j < 32) in its 128B-swizzled tile
+__device__ __forceinline__ float u_at(const ChainSmem& sm, int t, int j) {
+    return *reinterpret_cast<const float*>(&sm.u[t * 128 + ((((j >> 2) ^ t) & 7) << 4) + (j & 3) * 4]);
+}
 
 __device__ __forceinline__ uint32_t h2u(const __half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
 // x0, x1 as an fp16 hi pair and the fp16 pair of the remainders
@@ -564,109 +571,148 @@ __device__ __forceinline__ void mma3_tm(float (*acc)[4], const uint32_t (&ah)[4]
     }
 }
 
-// cp.async of a chunk's W and Q (read by [W; Q] S)
-__device__ __forceinline__ void chain_load_wq(ChainSmem& sm, const GdnPrefillParams& p, long long krow, long long vrow,
-                                              int tid) {
-    cp_tile_hl(&sm.whi[0][0], &sm.wlo[0][0], kP, p.wh + vrow * kDk, p.v_plane, kC, kDk, tid, kChainThreads);
-    cp_tile_hl(&sm.qhi[0][0], &sm.qlo[0][0], kP, p.qh + krow * kDk, p.q_plane, kC, kDk, tid, kChainThreads);
-    cp_async_commit();
+// A chunk's operand tiles are fetched by one thread as TMA tile copies (64 rows x 128 bytes, 128B
+// swizzle; the fragment loads undo the swizzle), completing on one mbarrier per group.
+struct ChainMaps {
+    CUtensorMap w, q, k, m, u;
+};
+// W and Q, hi and lo planes (read by W S and Q S)
+__device__ __forceinline__ void chain_load_wq(ChainSmem& sm, const ChainMaps& mp, long long krow, long long vrow) {
+    tc::mbar_arrive_expect_tx(&sm.bar[0], 2 * 2 * 2 * 8192);
+    for (int pl = 0; pl < 2; pl++)
+        for (int bx = 0; bx < 2; bx++) {
+            tc::tma_load_3d(sm.w[pl][bx], &mp.w, &sm.bar[0], 64 * bx, (int)vrow, pl);
+            tc::tma_load_3d(sm.q[pl][bx], &mp.q, &sm.bar[0], 64 * bx, (int)krow, pl);
+        }
 }
-// cp.async of a chunk's U columns and lc (read by D = U - W S and the decay factors)
-__device__ __forceinline__ void chain_load_u(ChainSmem& sm, const GdnPrefillParams& p, long long vrow, int j0, int par,
-                                             int tid) {
-    for (int i = tid; i < kC * (kDvb / 4); i += kChainThreads) {
-        const int r = i / (kDvb / 4), cv = i % (kDvb / 4);
-        cp_async_16(smem_u32(&sm.u[r][cv * 4]), p.Ub + (vrow + r) * kDv + j0 + cv * 4, 16);
+// this block's U columns and lc (read by D = U - W S and the decay factors)
+__device__ __forceinline__ void chain_load_u(ChainSmem& sm, const ChainMaps& mp, const GdnPrefillParams& p,
+                                             long long vrow, int j0, int par) {
+    tc::mbar_arrive_expect_tx(&sm.bar[1], 8192 + kC * 4);
+    tc::tma_load_2d(sm.u, &mp.u, &sm.bar[1], j0, (int)vrow);
+    tc::bulk_load(sm.lc[par], p.lcb + vrow, kC * 4, &sm.bar[1]);
+}
+// K and M, hi and lo planes (read by the state update and M D)
+__device__ __forceinline__ void chain_load_mk(ChainSmem& sm, const ChainMaps& mp, long long krow, long long vrow) {
+    tc::mbar_arrive_expect_tx(&sm.bar[2], 2 * 2 * 8192 + 2 * 8192);
+    for (int pl = 0; pl < 2; pl++) {
+        for (int bx = 0; bx < 2; bx++) tc::tma_load_3d(sm.k[pl][bx], &mp.k, &sm.bar[2], 64 * bx, (int)krow, pl);
+        tc::tma_load_3d(sm.m[pl], &mp.m, &sm.bar[2], 0, (int)vrow, pl);
     }
-    if (tid < kC / 4) cp_async_16(smem_u32(&sm.lc[par][tid * 4]), p.lcb + vrow + tid * 4, 16);
-    cp_async_commit();
-}
-// cp.async of a chunk's M and K (read by M D and the state update)
-__device__ __forceinline__ void chain_load_mk(ChainSmem& sm, const GdnPrefillParams& p, long long krow, long long vrow,
-                                              int tid) {
-    cp_tile_hl(&sm.khi[0][0], &sm.klo[0][0], kP, p.kh + krow * kDk, p.q_plane, kC, kDk, tid, kChainThreads);
-    cp_tile_hl(&sm.mhi[0][0], &sm.mlo[0][0], kPc, p.mh + vrow * kC, p.m_plane, kC, kC, tid, kChainThreads);
-    cp_async_commit();
 }
 
-__global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const GdnPrefillParams p) {
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    ChainSmem& sm = *reinterpret_cast<ChainSmem*>(smem_raw);
+__global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const __grid_constant__ ChainMaps mp,
+                                                                        const GdnPrefillParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    ChainSmem& sm = *reinterpret_cast<ChainSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int nblk = kDv / kDvb;
     const int h = blockIdx.x / nblk, j0 = (blockIdx.x % nblk) * kDvb, b = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, c = lane & 3;
-    const int jg = warp >> 1, dh = warp & 1;
+    const bool state = warp < 4;
+    const int w4 = warp & 3, jg = w4 >> 1, dh = w4 & 1;
     const int jr = 16 * jg;      // this warp's state columns j0 + jr .. + 16
     const int dbase = 64 * dh;   // and key dims dbase .. + 64
     const int kh = h / (p.Hv / p.Hk);
     const int seq = p.seq_ids ? p.seq_ids[b] : b;
     float* S = p.state + ((long long)seq * p.Hv + h) * kDk * kDv;
-    // s[nt][e] = S[d][j0 + j], j = jr + g + 8 (e / 2), d = dbase + 8 nt + 2 c + (e % 2)
+    // state warps: s[nt][e] = S[d][j0 + j], j = jr + g + 8 (e / 2), d = dbase + 8 nt + 2 c + (e % 2)
     float s[8][4];
 #pragma unroll
     for (int nt = 0; nt < 8; nt++)
 #pragma unroll
         for (int e = 0; e < 4; e++)
-            s[nt][e] = S[(long long)(dbase + 8 * nt + 2 * c + (e & 1)) * kDv + j0 + jr + g + 8 * (e >> 1)];
+            s[nt][e] = state ? S[(long long)(dbase + 8 * nt + 2 * c + (e & 1)) * kDv + j0 + jr + g + 8 * (e >> 1)] : 0.f;
     const int nC = p.T_pad / kC;
     const long long krow0 = ((long long)b * p.Hk + kh) * p.T_pad;
     const long long vrow0 = ((long long)b * p.Hv + h) * p.T_pad;
-    // cp.async groups in flight at the top of chunk ci: [WQ(ci), U(ci), MK(ci)]
-    chain_load_wq(sm, p, krow0, vrow0, tid);
-    chain_load_u(sm, p, vrow0, j0, 0, tid);
-    chain_load_mk(sm, p, krow0, vrow0, tid);
+    // the loads of chunk ci complete phase ci of bar[0] (W, Q), bar[1] (U, lc), bar[2] (M, K); output
+    // warps 4, 5, 6 issue them once the previous chunk's readers are done
+    if (tid == 0) {
+        for (int i = 0; i < 3; i++) tc::mbar_init(&sm.bar[i], 1);
+        sm.abort = 0;
+        tc::fence_barrier_init();
+    }
+    __syncthreads();
+    volatile int* abort = &sm.abort;
+    const bool loader = tid == 4 * 32;  // lane 0 of output warp 4 issues every copy
+    if (loader) {
+        chain_load_wq(sm, mp, krow0, vrow0);
+        chain_load_u(sm, mp, p, vrow0, j0, 0);
+        chain_load_mk(sm, mp, krow0, vrow0);
+    }
+    const uint32_t a_w = smem_u32(sm.w), a_q = smem_u32(sm.q), a_k = smem_u32(sm.k), a_m = smem_u32(sm.m);
+    // named barriers: 1 + jg state pair, 3 + jg output pair (64 threads); 5 + jg S^T fragments and
+    // 7 + jg D fragments, state warps arrive, output warps wait (128 threads)
     for (int ci = 0; ci < nC; ci++) {
         const int par = ci & 1;
         const bool more = ci + 1 < nC;
-        cp_async_wait<2>();
+        tc::mbar_wait(&sm.bar[0], par, p.err, ANELM_ERR_TIMEOUT, abort);
         __syncthreads();  // W and Q of this chunk are in shared memory
-        // ---- [W; Q] S over this warp's half of d: D part and Y part, all 64 rows t ----
-        float ad[8][4], ay[8][4];
+        // ---- W S (state warps) and Q S (output warps) over this warp's half of d, all 64 rows t ----
+        float acc[8][4];
 #pragma unroll
         for (int nt = 0; nt < 8; nt++)
 #pragma unroll
-            for (int e = 0; e < 4; e++) ad[nt][e] = ay[nt][e] = 0.f;
+            for (int e = 0; e < 4; e++) acc[nt][e] = 0.f;
+        {
+            const uint32_t bhi = state ? a_w : a_q, blo = bhi + 16384;
+            uint32_t fa[4][4], fl[4][4];
+            if (state) {
 #pragma unroll
-        for (int ks = 0; ks < 4; ks++) {
-            uint32_t ah[4], al[4];
-            afrag(s, ks, ah, al);
-            const int k0 = dbase + 16 * ks;
+                for (int ks = 0; ks < 4; ks++) {
+                    afrag(s, ks, fa[ks], fl[ks]);
 #pragma unroll
-            for (int n2 = 0; n2 < 2; n2++) {
-                uint32_t bwh[2][4], bwl[2][4], bqh[2][4], bql[2][4];
-#pragma unroll
-                for (int q = 0; q < 2; q++) {
-                    const int n0 = 32 * n2 + 16 * q;
-                    ldb2(bwh[q], &sm.whi[0][0], kP, n0, k0, lane);
-                    ldb2(bwl[q], &sm.wlo[0][0], kP, n0, k0, lane);
-                    ldb2(bqh[q], &sm.qhi[0][0], kP, n0, k0, lane);
-                    ldb2(bql[q], &sm.qlo[0][0], kP, n0, k0, lane);
+                    for (int r = 0; r < 4; r++) {
+                        sm.sa[w4][ks][r][lane] = fa[ks][r];
+                        sm.sa[w4][ks][4 + r][lane] = fl[ks][r];
+                    }
                 }
-                mma3_tm<2>(&ad[4 * n2], ah, al, bwh, bwl);
-                mma3_tm<2>(&ay[4 * n2], ah, al, bqh, bql);
+                named_bar_arrive_cta(5 + jg, 128);
+            } else {
+                named_bar_sync_cta(5 + jg, 128);
+#pragma unroll
+                for (int ks = 0; ks < 4; ks++)
+#pragma unroll
+                    for (int r = 0; r < 4; r++) {
+                        fa[ks][r] = sm.sa[w4][ks][r][lane];
+                        fl[ks][r] = sm.sa[w4][ks][4 + r][lane];
+                    }
+            }
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                const int k0 = dbase + 16 * ks;
+#pragma unroll
+                for (int n2 = 0; n2 < 2; n2++) {
+                    uint32_t bh[2][4], bl[2][4];
+#pragma unroll
+                    for (int q = 0; q < 2; q++) {
+                        ldb2_sw(bh[q], bhi, 32 * n2 + 16 * q, k0, lane);
+                        ldb2_sw(bl[q], blo, 32 * n2 + 16 * q, k0, lane);
+                    }
+                    mma3_tm<2>(&acc[4 * n2], fa[ks], fl[ks], bh, bl);
+                }
             }
         }
         __syncthreads();  // W, Q free
-        if (more) chain_load_wq(sm, p, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC, tid);
-        // ---- the two d halves of this column group meet ----
+        if (more && loader) chain_load_wq(sm, mp, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC);
+        // ---- the two d halves of a column group meet ----
+        float (*xb)[32][32] = state ? sm.xd : sm.xy;
 #pragma unroll
-        for (int r = 0; r < 32; r++) {
-            sm.xd[warp][r][lane] = ad[r >> 2][r & 3];
-            sm.xy[warp][r][lane] = ay[r >> 2][r & 3];
+        for (int r = 0; r < 32; r++) xb[w4][r][lane] = acc[r >> 2][r & 3];
+        named_bar_sync_cta((state ? 1 : 3) + jg, 64);
+        float y[4][4];  // output warps: Q S for rows t in [32 dh, 32 dh + 32)
+        if (state) {
+#pragma unroll
+            for (int r = 0; r < 32; r++) acc[r >> 2][r & 3] += xb[w4 ^ 1][r][lane];
+        } else {
+#pragma unroll
+            for (int n4 = 0; n4 < 4; n4++)
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    y[n4][e] = (dh ? acc[4 + n4][e] : acc[n4][e]) + xb[w4 ^ 1][4 * (4 * dh + n4) + e][lane];
         }
-        named_bar_sync_cta(1 + jg, 64);
-        // Q S of this warp's rows t in [32 dh, 32 dh + 32) (the other half is the partner's)
-        float y[4][4];
-#pragma unroll
-        for (int n4 = 0; n4 < 4; n4++)
-#pragma unroll
-            for (int e = 0; e < 4; e++)
-                y[n4][e] = (dh ? ay[4 + n4][e] : ay[n4][e]) + sm.xy[warp ^ 1][4 * (4 * dh + n4) + e][lane];
-#pragma unroll
-        for (int r = 0; r < 32; r++) ad[r >> 2][r & 3] += sm.xd[warp ^ 1][r][lane];
-        if (more) cp_async_wait<2>();
-        else cp_async_wait<1>();
+        tc::mbar_wait(&sm.bar[1], par, p.err, ANELM_ERR_TIMEOUT, abort);
         __syncthreads();  // U and lc of this chunk are in shared memory
         const float* lc = sm.lc[par];
         const float lcC = lc[kC - 1];
@@ -674,33 +720,51 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const Gd
             sm.eg[tid] = expf(lc[tid]);
             sm.ef[tid] = expf(lcC - lc[tid]);
         }
-        // D = U - W S (in place of ad)
+        if (state) {
+            // D = U - W S (in place of acc); its fragments (k-steps 2 dh, 2 dh + 1) for the output warps
 #pragma unroll
-        for (int nt = 0; nt < 8; nt++)
+            for (int nt = 0; nt < 8; nt++)
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-                ad[nt][e] = sm.u[8 * nt + 2 * c + (e & 1)][jr + g + 8 * (e >> 1)] - ad[nt][e];
-        if (more) cp_async_wait<1>();
-        else cp_async_wait<0>();
-        __syncthreads();  // M and K of this chunk are in shared memory; U read by every warp
-        if (more) chain_load_u(sm, p, vrow0 + (ci + 1) * kC, j0, par ^ 1, tid);
-        // ---- Y = e^lc Q S + M D for rows t in [32 dh, 32 dh + 32) ----
-        {
+                for (int e = 0; e < 4; e++)
+                    acc[nt][e] = u_at(sm, 8 * nt + 2 * c + (e & 1), jr + g + 8 * (e >> 1)) - acc[nt][e];
+#pragma unroll
+            for (int k2 = 0; k2 < 2; k2++) {
+                uint32_t ah[4], al[4];
+                if (dh) afrag(acc, 2 + k2, ah, al);
+                else afrag(acc, k2, ah, al);
+#pragma unroll
+                for (int r = 0; r < 4; r++) {
+                    sm.sdf[jg][2 * dh + k2][r][lane] = ah[r];
+                    sm.sdf[jg][2 * dh + k2][4 + r][lane] = al[r];
+                }
+            }
+            named_bar_arrive_cta(7 + jg, 128);
+        }
+        tc::mbar_wait(&sm.bar[2], par, p.err, ANELM_ERR_TIMEOUT, abort);
+        __syncthreads();  // M and K of this chunk are in shared memory; U read; e^lc factors visible
+        if (more && loader) chain_load_u(sm, mp, p, vrow0 + (ci + 1) * kC, j0, par ^ 1);
+        if (!state) {
+            // ---- Y = e^lc Q S + M D for rows t in [32 dh, 32 dh + 32) ----
             const int tt = 32 * dh;
 #pragma unroll
             for (int n4 = 0; n4 < 4; n4++)
 #pragma unroll
                 for (int e = 0; e < 4; e++) y[n4][e] *= sm.eg[tt + 8 * n4 + 2 * c + (e & 1)];
+            named_bar_sync_cta(7 + jg, 128);
 #pragma unroll
             for (int ks = 0; ks < 4; ks++) {
                 if (16 * ks >= tt + 32) break;  // M[t][i] = 0 for i > t
                 uint32_t ah[4], al[4];
-                afrag(ad, ks, ah, al);
+#pragma unroll
+                for (int r = 0; r < 4; r++) {
+                    ah[r] = sm.sdf[jg][ks][r][lane];
+                    al[r] = sm.sdf[jg][ks][4 + r][lane];
+                }
                 uint32_t bh[2][4], bl[2][4];
 #pragma unroll
                 for (int np = 0; np < 2; np++) {
-                    ldb2(bh[np], &sm.mhi[0][0], kPc, tt + 16 * np, 16 * ks, lane);
-                    ldb2(bl[np], &sm.mlo[0][0], kPc, tt + 16 * np, 16 * ks, lane);
+                    ldb2_sw(bh[np], a_m, tt + 16 * np, 16 * ks, lane);
+                    ldb2_sw(bl[np], a_m + 8192, tt + 16 * np, 16 * ks, lane);
                 }
                 mma3_tm<2>(y, ah, al, bh, bl);
             }
@@ -715,9 +779,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const Gd
                                              8 * (e >> 1),
                                          y[n4][e]);
                 }
-        }
-        // ---- S = e^{lc_C} S + K^T diag(e^{lc_C - lc}) D over this warp's half of d ----
-        {
+        } else {
+            // ---- S = e^{lc_C} S + K^T diag(e^{lc_C - lc}) D over this warp's half of d ----
             const float gC = expf(lcC);
 #pragma unroll
             for (int nt = 0; nt < 8; nt++)
@@ -731,24 +794,26 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const Gd
 #pragma unroll
             for (int ks = 0; ks < 4; ks++) {
                 uint32_t ah[4], al[4];
-                afrag(ad, fs, ks, ah, al);
+                afrag(acc, fs, ks, ah, al);
                 uint32_t bh[4][4], bl[4][4];
 #pragma unroll
                 for (int np = 0; np < 4; np++) {
-                    ldb2_t(bh[np], &sm.khi[0][0], kP, dbase + 16 * np, 16 * ks, lane);
-                    ldb2_t(bl[np], &sm.klo[0][0], kP, dbase + 16 * np, 16 * ks, lane);
+                    ldb2_t_sw(bh[np], a_k, dbase + 16 * np, 16 * ks, lane);
+                    ldb2_t_sw(bl[np], a_k + 16384, dbase + 16 * np, 16 * ks, lane);
                 }
                 mma3_tm<4>(s, ah, al, bh, bl);
             }
         }
         __syncthreads();  // M, K free
-        if (more) chain_load_mk(sm, p, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC, tid);
+        if (more && loader) chain_load_mk(sm, mp, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC);
     }
+    if (state) {
 #pragma unroll
-    for (int nt = 0; nt < 8; nt++)
+        for (int nt = 0; nt < 8; nt++)
 #pragma unroll
-        for (int e = 0; e < 4; e++)
-            S[(long long)(dbase + 8 * nt + 2 * c + (e & 1)) * kDv + j0 + jr + g + 8 * (e >> 1)] = s[nt][e];
+            for (int e = 0; e < 4; e++)
+                S[(long long)(dbase + 8 * nt + 2 * c + (e & 1)) * kDv + j0 + jr + g + 8 * (e >> 1)] = s[nt][e];
+    }
 }
 
 // ---------------------------------------------------------------- gated RMSNorm (layer path)
@@ -834,12 +899,12 @@ static void carve(GdnPrefillParams& p, void* ws, bool layer) {
     }
 }
 
-// 3D fp16 tensor map over the hi / lo planes of a [rows][128] operand: box {64, 64, 1}, 128B swizzle
-static bool make_plane_map(CUtensorMap* m, const __half* base, uint64_t rows, long long plane) {
+// 3D fp16 tensor map over the hi / lo planes of a [rows][cols] operand: box {64, 64, 1}, 128B swizzle
+static bool make_plane_map(CUtensorMap* m, const __half* base, uint64_t rows, long long plane, uint64_t cols = 128) {
     auto fn = tc::tmap_encode_fn();
     if (!fn) return false;
-    cuuint64_t dims[3] = {128, rows, 2};
-    cuuint64_t strides[2] = {256, (cuuint64_t)plane * 2};
+    cuuint64_t dims[3] = {cols, rows, 2};
+    cuuint64_t strides[2] = {cols * 2, (cuuint64_t)plane * 2};
     cuuint32_t box[3] = {64, (cuuint32_t)kC, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, estr,
@@ -849,16 +914,31 @@ static bool make_plane_map(CUtensorMap* m, const __half* base, uint64_t rows, lo
 
 static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t stream) {
     const int nC = p.T_pad / kC;
-    const size_t chunk_smem = sizeof(ChunkSmem) + 1024, chain_smem = sizeof(ChainSmem);
+    const size_t chunk_smem = sizeof(ChunkSmem) + 1024, chain_smem = sizeof(ChainSmem) + 1024;
+    const uint64_t krows = (uint64_t)p.B * p.Hk * p.T_pad, vrows = (uint64_t)p.B * p.Hv * p.T_pad;
     CUtensorMap mK, mQ, mV;
-    if (!make_plane_map(&mK, p.kh, (uint64_t)p.B * p.Hk * p.T_pad, p.q_plane) ||
-        !make_plane_map(&mQ, p.qh, (uint64_t)p.B * p.Hk * p.T_pad, p.q_plane) ||
-        !make_plane_map(&mV, p.vh, (uint64_t)p.B * p.Hv * p.T_pad, p.v_plane))
+    ChainMaps cm;
+    if (!make_plane_map(&mK, p.kh, krows, p.q_plane) || !make_plane_map(&mQ, p.qh, krows, p.q_plane) ||
+        !make_plane_map(&mV, p.vh, vrows, p.v_plane))
         return ANELM_ERR_CUDA;
+    cm.k = mK;
+    cm.q = mQ;
+    {  // W (hi / lo like V), M (64 columns), U (fp32, 32-column boxes of this block's state columns)
+        auto fn = tc::tmap_encode_fn();
+        cuuint64_t dims[2] = {(cuuint64_t)kDv, vrows};
+        cuuint64_t strides[1] = {(cuuint64_t)kDv * 4};
+        cuuint32_t box[2] = {(cuuint32_t)kDvb, (cuuint32_t)kC};
+        cuuint32_t estr[2] = {1, 1};
+        if (!make_plane_map(&cm.w, p.wh, vrows, p.v_plane) || !make_plane_map(&cm.m, p.mh, vrows, p.m_plane, kC) ||
+            fn(&cm.u, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.Ub, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return ANELM_ERR_CUDA;
+    }
     cudaFuncSetAttribute(gdn_pf_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
     cudaFuncSetAttribute(gdn_pf_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chain_smem);
     gdn_pf_chunk_kernel<<<dim3(nC, p.Hv, p.B), kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, p);
-    gdn_pf_chain_kernel<<<dim3(p.Hv * (kDv / kDvb), p.B), kChainThreads, chain_smem, stream>>>(p);
+    gdn_pf_chain_kernel<<<dim3(p.Hv * (kDv / kDvb), p.B), kChainThreads, chain_smem, stream>>>(cm, p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 
