@@ -321,11 +321,12 @@ __global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPre
 // stages with untiled bulk copies, kPrepStages - 1 tokens ahead; warps 0-7 run prep_segment on
 // the staged row.  The same arithmetic as fa_prefill_prep_vec_kernel, with the loads kept in
 // flight across tokens instead of one row at a time per CTA.
-constexpr int kPrepStages = 4;
+constexpr int kPrepStages = 3;
 constexpr int kPrepWarps = 8;  // consumer warps; warp kPrepWarps is the copy producer
-constexpr int kPrepStageMax = 54 * 1024;  // stage bytes that still let two CTAs share an SM
+constexpr int kPrepCtas = 3;   // CTAs per SM: the consumers' latency (warp reductions) needs the warps
+constexpr int kPrepStageMax = 24 * 1024;  // stage bytes that still let kPrepCtas CTAs share an SM
 
-__global__ void __launch_bounds__(32 * (kPrepWarps + 1), 2)
+__global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
     fa_prefill_prep_bulk_kernel(const FaPrefillParams p, int stage_bytes, int rope_off) {
     extern __shared__ __align__(128) uint8_t prep_smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(prep_smem);
@@ -392,6 +393,8 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), 2)
         kn[e] = p.qk_norm ? p.k_norm[e0 + e] : 0.f;
     }
     const bool bf = p.proj_dtype == ANELM_BF16;
+    int cur_b = -1, seq = 0;  // the sequence of row b and its pool base, reloaded when b changes
+    long long kv0 = 0;
     long long k = 0;
     for (long long u = blockIdx.x; u < total; u += gridDim.x, k++) {
         const int s = (int)(k % kPrepStages);
@@ -402,8 +405,12 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), 2)
         } else {
             const uint8_t* st = stage0 + (size_t)s * stage_bytes;
             const int pos = p.start_pos + t;
-            const int seq = p.seq_ids ? p.seq_ids[b] : 0;
-            const long long slot_row = p.kv_base ? (p.kv_base[seq] + t) * Hkv : 0;
+            if (b != cur_b) {
+                cur_b = b;
+                seq = p.seq_ids ? p.seq_ids[b] : 0;
+                kv0 = p.kv_base ? p.kv_base[seq] : 0;
+            }
+            const long long slot_row = p.kv_base ? (kv0 + t) * Hkv : 0;
             const bool tab = p.rot_dim > 0 && p.rope_cos && pos >= 0 && pos < p.rope_len;
             const float* tc_cos = reinterpret_cast<const float*>(st + rope_off);
             const auto cs = [&](int j, float& c, float& sn) {
@@ -800,7 +807,7 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const long long total = (long long)p.B * p.n_pad;
-        const int grid = (int)std::min<long long>(total, 2LL * sms);
+        const int grid = (int)std::min<long long>(total, (long long)kPrepCtas * sms);
         const int smem = 128 + kPrepStages * stage_bytes;
         cudaFuncSetAttribute(fa_prefill_prep_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         fa_prefill_prep_bulk_kernel<<<grid, 32 * (kPrepWarps + 1), smem, stream>>>(p, stage_bytes, rope_off);
