@@ -421,7 +421,16 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
                     rope_cs_pf(p, pos, j, c, sn);
                 }
             };
-            for (int sg = warp; sg < nseg; sg += kPrepWarps) {
+            // job j of the token -> segment: with Hq a multiple of 8, blocks of 8 jobs alternate q heads and
+            // gates (q 0-7, gate 0-7, q 8-15, ...), so each warp gets the same number of RMSNorm + RoPE
+            // segments (the warps' slowest bounds the stage's release); k and v heads follow
+            const bool mix = (Hq & 7) == 0;
+            for (int j = warp; j < nseg; j += kPrepWarps) {
+                int sg = j;
+                if (mix && j < 2 * Hq) {
+                    const int bk = j >> 3;
+                    sg = 2 * ((bk >> 1) * 8 + (j & 7)) + (bk & 1);
+                }
                 float x[8];
                 unpack8(*reinterpret_cast<const uint4*>(st + (size_t)sg * kD * 2 + 16 * lane), bf, x);
                 prep_segment(p, x, sg, lane, b, t, slot_row, qn, kn, cs);
