@@ -185,3 +185,32 @@ def test_prefill_prep_variants(case):
     assert (ln, st) == (n, 0)
     np.testing.assert_array_equal(v[:n], ring.v[:n])
     assert_close(k[:n], ring.k[:n], atol=2e-3, rtol=2e-3, what=f"K ring {case}")
+
+
+@pytest.mark.parametrize("hq,hkv", [(8, 2), (6, 2), (4, 1)])
+def test_prefill_other_head_counts(hq, hkv):
+    """Head counts other than the 4B shape's: 8/2 (the 0.8B shape; q and gate segments interleaved
+    across the prep's warps), 6/2 and 4/1 (head counts that are not a multiple of 8 keep the
+    prep's segment order), bf16 projections through the streaming prep, against the oracle."""
+    rng = np.random.default_rng(40 + hq)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(40 + hq)
+    n, cap = 140, 160
+    qn, kn = weights(rng)
+    proj = torch.randn(1, n, hq * 2 * D + 2 * hkv * D, generator=gen, device="cuda").to(torch.bfloat16)
+    rope = po.rope_table(4096, R, 1e7)
+    shape = fa_shape(hq, hkv, D, R, 1e7)
+    with Context(layer_types=[ab.LAYER_FULL_ATTN], num_q_heads=hq, num_kv_heads=hkv, head_dim=D, rot_dim=R,
+                 rope_theta=1e7, max_seqs=1, kv_capacity=cap) as ctx:
+        ctx.set_full_attn_weights(0, qn, kn)
+        plan = ctx.plan([0])
+        out = ctx.full_attn_prefill(plan, 0, proj, out_dtype=torch.bfloat16).float().cpu().numpy()
+        k, v, ln, st = ctx.kv_export(0, 0)
+        plan.close()
+    ring = po.KVRing.empty(cap, hkv, D)
+    want = po.full_attn_tokens("oracle", shape, po.make_variant(kv_round_f16=1), qn, kn, ring,
+                               proj.float().cpu().numpy()[0], 0, rope)
+    assert_close(out[0], want, what=f"prefill {hq}/{hkv} heads")
+    assert (ln, st) == (n, 0)
+    np.testing.assert_array_equal(v[:n], ring.v[:n])
+    assert_close(k[:n], ring.k[:n], atol=2e-3, rtol=2e-3, what=f"K ring {hq}/{hkv} heads")
