@@ -249,20 +249,24 @@ __global__ void __launch_bounds__(256) gdn_pf_pack_kernel(const GdnPrefillParams
 constexpr int kChunkThreads = 256;
 constexpr int kOpPlane = 32768;            // bytes of one plane of the operand buffer
 constexpr int kTPlane = 16384;             // bytes of one plane of [T'; T''] (128 rows x 128 bytes)
-constexpr int kAtRow = 80;                 // fp32 words per row of A^T (4 groups of 16 + padding)
+constexpr int kTs = kC + 4;                // fp32 pitch of A and T in the inversion
 constexpr uint32_t kChunkTmemCols = 256;
 struct ChunkSmem {
     uint8_t op[2][kOpPlane];               // hi, lo planes (1024-byte aligned)
     union {
         uint8_t t[2][kTPlane];             // [T'; T''] hi, lo (K-major, 128-byte swizzle)
-        float at[kC][kAtRow];              // A^T, rows interleaved: at[i][20 (t % 4) + t / 4] = A[t][i]
+        struct {
+            float a[kC][kTs];              // A (strictly lower)
+            float tm[kC][kTs];             // T = (I + A)^{-1}
+            float z[3][16][17];            // block products of one level
+        } inv;
     };
     float lc[kC], lt[kC], bt[kC];
     uint64_t bar[4];                       // K+Q loaded, GEMM 1 done, V loaded, GEMM 2 done
     uint32_t tmem_slot;
     int abort;
 };
-static_assert(kC * kAtRow * 4 <= 2 * kTPlane, "A^T fits the T buffer");
+
 
 // byte offset of element (row, col) (fp16, 64 columns per 128-byte row) in a 128B-swizzled tile
 __device__ __forceinline__ int sw128_off(int row, int col) {
@@ -362,11 +366,16 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
         if (r < kC) {  // A_ti = beta_t e^{lt_t - lc_i} k_t.k_i (i < t)
             const int t = r;
             const float bt = sm.bt[t], lt = sm.lt[t];
-            float* dst = &sm.at[0][20 * (t & 3) + (t >> 2)];
+            float4* dst = reinterpret_cast<float4*>(&sm.inv.a[t][32 * hc]);
 #pragma unroll
-            for (int c = 0; c < 32; c++) {
-                const int i = 32 * hc + c;
-                dst[i * kAtRow] = i < t ? bt * expf(lt - sm.lc[i]) * __uint_as_float(x[c]) : 0.f;
+            for (int c4 = 0; c4 < 8; c4++) {
+                float v[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int i = 32 * hc + 4 * c4 + e;
+                    v[e] = i < t ? bt * __expf(lt - sm.lc[i]) * __uint_as_float(x[4 * c4 + e]) : 0.f;
+                }
+                dst[c4] = make_float4(v[0], v[1], v[2], v[3]);
             }
         } else {  // M_ti = e^{lc_t - lc_i} q_t.k_i (i <= t), hi / lo planes
             const int t = r - kC;
@@ -378,34 +387,75 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
                     const int i = 32 * hc + 8 * c8 + e;
-                    v[e] = i <= t ? expf(lct - sm.lc[i]) * __uint_as_float(x[8 * c8 + e]) : 0.f;
+                    v[e] = i <= t ? __expf(lct - sm.lc[i]) * __uint_as_float(x[8 * c8 + e]) : 0.f;
                 }
                 put_hl8(mhi, p.m_plane, 8 * c8, v);
             }
         }
     }
     if (tid < kC) p.lcb[vrow + tid] = sm.lc[tid];
-    __syncthreads();  // A^T complete
-    // ---- T = (I + A)^{-1} by forward substitution, one column j per 4 threads, right-looking ----
-    const int j = tid >> 2, pt = tid & 3;
-    float xs[kC / 4], rs[kC / 4];
+    __syncthreads();  // A complete
+    // ---- T = (I + A)^{-1}, blocked by 16: the four diagonal blocks T_ii = (I + A_ii)^{-1} by forward
+    // substitution (one column per thread), then the sub-diagonals d = 1, 2, 3 in turn:
+    //   Z_ij = sum_{k=j}^{i-1} A_ik T_kj,  T_ij = -T_ii Z_ij   (i - j = d), 16 x 16 blocks ----
+    if (tid < kC) {
+        const int o = 16 * (tid >> 4), jj = tid & 15;
+        float rsum[16], xv[16];
 #pragma unroll
-    for (int m = 0; m < kC / 4; m++) xs[m] = rs[m] = 0.f;
+        for (int t = 0; t < 16; t++) rsum[t] = 0.f;
 #pragma unroll
-    for (int t = 0; t < kC; t++) {
-        const float x = __shfl_sync(0xffffffffu, (t == j ? 1.0f : 0.0f) - rs[t >> 2], (lane & ~3) | (t & 3));
-        if (pt == (t & 3)) xs[t >> 2] = x;
-        const float4* col = reinterpret_cast<const float4*>(&sm.at[t][20 * pt]);
+        for (int t = 0; t < 16; t++) {
+            xv[t] = (t == jj ? 1.0f : 0.0f) - rsum[t];
 #pragma unroll
-        for (int q4 = 0; q4 < kC / 16; q4++) {
-            if (16 * q4 + 15 <= t) continue;  // rows 4m + pt <= 4m + 3 <= t of this word are final
-            const float4 a4 = col[q4];
-            rs[4 * q4] = fmaf(a4.x, x, rs[4 * q4]);
-            rs[4 * q4 + 1] = fmaf(a4.y, x, rs[4 * q4 + 1]);
-            rs[4 * q4 + 2] = fmaf(a4.z, x, rs[4 * q4 + 2]);
-            rs[4 * q4 + 3] = fmaf(a4.w, x, rs[4 * q4 + 3]);
+            for (int u = t + 1; u < 16; u++) rsum[u] = fmaf(sm.inv.a[o + u][o + t], xv[t], rsum[u]);
+        }
+#pragma unroll
+        for (int t = 0; t < 16; t++) sm.inv.tm[o + t][o + jj] = xv[t];
+    } else {  // blocks above the diagonal are zero
+        for (int e = tid - kC; e < 6 * 256; e += kChunkThreads - kC) {
+            const int blk = e >> 8, r = (e >> 4) & 15, c = e & 15;
+            const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
+            sm.inv.tm[16 * bi + r][16 * bj + c] = 0.f;
         }
     }
+    __syncthreads();
+#pragma unroll 1
+    for (int d = 1; d < 4; d++) {
+        const int nb = 4 - d;  // blocks (j + d, j), j = 0 .. nb - 1
+        for (int e = tid; e < nb * 256; e += kChunkThreads) {
+            const int j = e >> 8, i = j + d, r = (e >> 4) & 15, c = e & 15;
+            const float* arow = &sm.inv.a[16 * i + r][16 * j];
+            float s0 = 0.f, s1 = 0.f;
+            for (int k = 0; k < 16 * d; k += 4) {
+                const float4 a4 = *reinterpret_cast<const float4*>(arow + k);
+                s0 = fmaf(a4.x, sm.inv.tm[16 * j + k][16 * j + c], s0);
+                s1 = fmaf(a4.y, sm.inv.tm[16 * j + k + 1][16 * j + c], s1);
+                s0 = fmaf(a4.z, sm.inv.tm[16 * j + k + 2][16 * j + c], s0);
+                s1 = fmaf(a4.w, sm.inv.tm[16 * j + k + 3][16 * j + c], s1);
+            }
+            sm.inv.z[j][r][c] = s0 + s1;
+        }
+        __syncthreads();
+        for (int e = tid; e < nb * 256; e += kChunkThreads) {
+            const int j = e >> 8, i = j + d, r = (e >> 4) & 15, c = e & 15;
+            const float* trow = &sm.inv.tm[16 * i + r][16 * i];
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; k += 4) {
+                const float4 t4 = *reinterpret_cast<const float4*>(trow + k);
+                s0 = fmaf(t4.x, sm.inv.z[j][k][c], s0);
+                s1 = fmaf(t4.y, sm.inv.z[j][k + 1][c], s1);
+                s0 = fmaf(t4.z, sm.inv.z[j][k + 2][c], s0);
+                s1 = fmaf(t4.w, sm.inv.z[j][k + 3][c], s1);
+            }
+            sm.inv.tm[16 * i + r][16 * j + c] = -(s0 + s1);
+        }
+        __syncthreads();
+    }
+    const int j = tid >> 2, pt = tid & 3;  // column j, rows 4 m + pt of T into registers
+    float xs[kC / 4];
+#pragma unroll
+    for (int m = 0; m < kC / 4; m++) xs[m] = sm.inv.tm[4 * m + pt][j];
     __syncthreads();  // A^T no longer read: its space becomes [T'; T'']
     {  // T' = T diag(beta e^{lt}) in rows 0-63, T'' = T diag(beta) in rows 64-127, column j
         const float fw = sm.bt[j] * expf(sm.lt[j]), fu = sm.bt[j];
