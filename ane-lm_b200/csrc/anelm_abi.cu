@@ -81,6 +81,7 @@ struct anelm_plan {
     int* seq_d = nullptr;
     int CH = 64;
     int n_blocks = 0;
+    int ns0 = 0;  // splits of the single row of a one-row plan (0 otherwise)
     int* blk_b = nullptr;
     int* blk_split = nullptr;
     int* nsplit = nullptr;
@@ -219,6 +220,10 @@ int build_plan(anelm_ctx* ctx, int n, const int* seqs, anelm_plan** out) {
         return cleanup(fail(ANELM_ERR_CUDA, "plan upload failed"));
     if (ctx->n_fa > 0) {
         p->CH = choose_split_tokens(ctx, p->seq_h);
+        if (n == 1) {  // one row: at most 16 splits, so they can merge inside one thread-block cluster
+            const int cap = ctx->cap_h[seqs[0]];
+            p->CH = std::max(p->CH, ((cap + 15) / 16 + 63) / 64 * 64);
+        }
         std::vector<int> bb, bs, ns(n);
         std::vector<long long> off(n);
         long long tot = 0;
@@ -235,6 +240,7 @@ int build_plan(anelm_ctx* ctx, int n, const int* seqs, anelm_plan** out) {
             }
         }
         p->n_blocks = (int)bb.size();
+        p->ns0 = n == 1 ? ns[0] : 0;
         const int Hkv = ctx->cfg.num_kv_heads, D = ctx->cfg.head_dim;
         PALLOC(p->blk_b, bb.size());
         PALLOC(p->blk_split, bs.size());
@@ -307,6 +313,7 @@ FaDecodeParams fa_params(anelm_ctx* ctx, int layer, const anelm_plan* plan, cons
     p.nsplit = plan->nsplit;
     p.part_off = plan->part_off;
     p.CH = plan->CH;
+    p.cluster_ns = plan->ns0;
     p.part_o = plan->part_o;
     p.part_ml = plan->part_ml;
     p.cnt_head = plan->cnt_head;

@@ -23,12 +23,17 @@
 //      writes an unnormalised partial (O, m, l).
 // The last CTA of a (row, kv head) -- found with an atomic counter, no waiting
 // -- merges the partials, applies the sigmoid gate and writes the output; the
-// last of those updates the ring's len/start.
+// last of those updates the ring's len/start.  For a single row with at most 16
+// splits the splits of a kv head instead form one thread-block cluster: each CTA
+// keeps its partial in shared memory and, after a cluster barrier, merges a
+// slice of the output columns from all of them through distributed shared
+// memory (no global round trip, no serial merging CTA).
 //
 // New-token handling: the slot being written is never one of the old tokens the
 // other CTAs read (it is either empty or the evicted oldest slot), so the
 // append and the reads of the same launch do not race.  The CTA whose tile
 // holds the new token patches that row in shared memory with the fp16 k/v.
+#include <cooperative_groups.h>
 #include <math.h>
 
 #include "common.cuh"
@@ -77,7 +82,89 @@ __device__ __forceinline__ void set_err(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
+// Merge of one row's splits inside a thread-block cluster (one CTA per split of kv head kvh): every
+// CTA holds its unnormalised partial O [kGP][D] and (m, l) [kGP][2] in shared memory at `po`.  After a
+// cluster barrier, warp g < G of each CTA turns the heads' (m, l) of all splits into merge weights,
+// and each CTA merges its slice of the G * D / 4 float4 output columns (8 lanes per column, each
+// over every eighth split) from its peers' shared memory, then gates and stores them.  A second
+// cluster barrier keeps every CTA resident until its peers have read it.
 template <int D>
+__device__ __forceinline__ void cluster_merge(const FaDecodeParams& p, uint8_t* smem, const float* po, int b, int kvh,
+                                              int G, int seq, const char* proj_row, int len1, int start1) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rank = (int)cl.block_rank(), ns = (int)cl.num_blocks();
+    __shared__ float s_w[16][kGP];  // merge weight of split r for head g
+    __shared__ float s_L[kGP];
+    cl.sync();  // every split's partial is in its shared memory
+    if (warp < G) {
+        const int g = warp;
+        float m = -INFINITY, l = 0.f;
+        if (lane < ns) {
+            const float* ml = cl.map_shared_rank(po + kGP * D, lane);
+            m = ml[2 * g];
+            l = ml[2 * g + 1];
+        }
+        const float M = warp_max(m);
+        const float w = (m == -INFINITY) ? 0.f : expf(m - M);
+        const float L = warp_sum(w * l);
+        if (lane < ns) s_w[lane][g] = w;
+        if (lane == 0) s_L[g] = L;
+    }
+    __syncthreads();
+    const int nitem = G * D / 4;
+    const int per = (nitem + ns - 1) / ns;
+    const int i0 = rank * per, i1 = min(nitem, i0 + per);
+    const int sub = tid & 7;
+    for (int base = i0; base < i1; base += kThreads / 8) {  // uniform trip count: whole warps shuffle
+        const int it = base + (tid >> 3);
+        const bool valid = it < i1;
+        const int g = valid ? (it * 4) / D : 0, col = valid ? it * 4 - g * D : 0;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = sub; r < ns && valid; r += 8) {
+            const float4 v = *reinterpret_cast<const float4*>(cl.map_shared_rank(po + g * D + col, r));
+            const float w = s_w[r][g];
+            o.x += w * v.x; o.y += w * v.y; o.z += w * v.z; o.w += w * v.w;
+        }
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) {
+            o.x += __shfl_xor_sync(0xffffffffu, o.x, off);
+            o.y += __shfl_xor_sync(0xffffffffu, o.y, off);
+            o.z += __shfl_xor_sync(0xffffffffu, o.z, off);
+            o.w += __shfl_xor_sync(0xffffffffu, o.w, off);
+        }
+        if (sub == 0 && valid) {
+            const float L = s_L[g];
+            const float ov[4] = {o.x, o.y, o.z, o.w};
+            const int h = kvh * G + g;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                float O = (L > 0.f) ? ov[e] / L : 0.f;
+                if (p.gate) {  // mul_sigmoid_inplace, core/cpu_ops.cpp:15-22
+                    const float z = load_as_float(proj_row, p.proj_dtype,
+                                                  p.gate_off + (long long)h * p.q_head_stride + col + e);
+                    O = O / (1.0f + expf(-z));
+                }
+                store_from_float(p.out, p.out_dtype, (long long)b * p.out_stride + (long long)h * D + col + e, O);
+            }
+        }
+    }
+    cl.sync();  // peers are done reading this CTA's partial
+    if (rank == 0 && tid == 0) {  // the last kv head of the row updates the ring metadata
+        __threadfence();
+        const int prev = atomicAdd(&p.cnt_seq[b], 1);
+        if (prev == p.Hkv - 1) {
+            if (p.append && p.kv_len) {
+                p.kv_len[seq] = len1;
+                p.kv_start[seq] = start1;
+            }
+            p.cnt_seq[b] = 0;
+        }
+    }
+}
+
+template <int D, bool CM>
 __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     using S = Smem<D>;
@@ -416,9 +503,11 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
         __syncthreads();
     }
 
-    // ---- 4. partial (O unnormalised, m, l) ----
+    // ---- 4. partial (O unnormalised, m, l): to global memory, or to this CTA's shared memory
+    // for the cluster merge (the tile buffers are free now) ----
     const long long pidx = (p.part_off[b] + split) * Hkv + kvh;
-    float* po = p.part_o + pidx * kGP * D;
+    float* po = CM ? reinterpret_cast<float*>(smem + S::tiles) : p.part_o + pidx * kGP * D;
+    float* pml = CM ? po + kGP * D : p.part_ml + pidx * kGP * 2;
     {
         const int c = lane & 3;
 #pragma unroll
@@ -437,9 +526,13 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
             }
         }
         if (tid < kGP) {
-            p.part_ml[pidx * kGP * 2 + 2 * tid] = (n_tok > 0) ? misc[tid] : -INFINITY;
-            p.part_ml[pidx * kGP * 2 + 2 * tid + 1] = (n_tok > 0) ? misc[4 + tid] : 0.f;
+            pml[2 * tid] = (n_tok > 0) ? misc[tid] : -INFINITY;
+            pml[2 * tid + 1] = (n_tok > 0) ? misc[4 + tid] : 0.f;
         }
+    }
+    if constexpr (CM) {
+        cluster_merge<D>(p, smem, po, b, kvh, G, seq, proj_row, len1, start1);
+        return;
     }
     __threadfence();
     __syncthreads();
@@ -553,17 +646,31 @@ int launch_fa_decode(const FaDecodeParams& p0, int head_dim, int n_blocks, cudaS
     p.proj_vec = (uintptr_t)p.proj % 16 == 0 && (p.proj_stride * eb) % 16 == 0 && ((long long)p.q_head_stride * eb) % 16 == 0 &&
                  (p.k_off * eb) % 16 == 0 && (p.v_off * eb) % 16 == 0 && head_dim % 8 == 0;
     dim3 grid(n_blocks, p.Hkv);
-    if (head_dim == 256) {
-        const size_t sm = Smem<256>::total;
-        cudaFuncSetAttribute(fa_decode_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        fa_decode_kernel<256><<<grid, kThreads, sm, stream>>>(p);
-    } else if (head_dim == 128) {
-        const size_t sm = Smem<128>::total;
-        cudaFuncSetAttribute(fa_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        fa_decode_kernel<128><<<grid, kThreads, sm, stream>>>(p);
-    } else {
-        return ANELM_ERR_UNSUPPORTED;
+    if (head_dim != 256 && head_dim != 128) return ANELM_ERR_UNSUPPORTED;
+    const size_t sm = head_dim == 256 ? Smem<256>::total : Smem<128>::total;
+    if (p.cluster_ns >= 2 && p.cluster_ns <= 16 && n_blocks == p.cluster_ns) {
+        // one row: its splits of each kv head form a cluster and merge through shared memory
+        auto kern = head_dim == 256 ? fa_decode_kernel<256, true> : fa_decode_kernel<128, true>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (p.cluster_ns > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = sm;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = p.cluster_ns;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess) return ANELM_OK;
+        cudaGetLastError();  // a cluster that cannot be placed: merge through global memory instead
     }
+    auto kern = head_dim == 256 ? fa_decode_kernel<256, false> : fa_decode_kernel<128, false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    kern<<<grid, kThreads, sm, stream>>>(p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 

@@ -38,6 +38,8 @@ struct FaDecodeParams {
     long long k_off, v_off;    // element offsets of the new k / v inside a proj row
     long long gate_off;        // element offset of head 0's gate inside a proj row (q_head_stride apart)
     int proj_vec;              // proj rows and the q / k / v offsets are 16-byte aligned (vector loads)
+    int cluster_ns;            // >= 2: one row whose ns splits form a thread-block cluster and merge
+                               // through distributed shared memory (0: partials through global memory)
     void* out;
     int out_dtype;
     long long out_stride;
