@@ -90,6 +90,24 @@ def head_shard(n_q_heads: int, n_kv_heads: int, world: int, rank: int):
     return [kv * G + part * per + g for g in range(per)], [kv]
 
 
+def value_head_shard(n_key_heads: int, n_val_heads: int, world: int, rank: int):
+    """Key and value heads owned by `rank` for value-head-sharded Gated DeltaNet prefill.
+
+    Value heads are split into `world` contiguous blocks; a rank also takes the key heads
+    its value heads read (value head h reads key head h // (Hv / Hk), qwen3_5.cpp:880-890),
+    so a key head is duplicated when its value heads land on different ranks.
+    Returns (key_heads, val_heads): lists of global head indices, in order."""
+    if n_val_heads % n_key_heads:
+        raise ValueError("value heads must be a multiple of the key heads")
+    if n_val_heads % world:
+        raise ValueError("value heads must divide evenly over the ranks")
+    ratio = n_val_heads // n_key_heads
+    per = n_val_heads // world
+    vals = list(range(rank * per, (rank + 1) * per))
+    keys = sorted({h // ratio for h in vals})
+    return keys, vals
+
+
 def gather_heads(local_out, n_q_heads: int, n_kv_heads: int, head_dim: int, group=None):
     """All-gather of head-sharded outputs: local_out [tokens][len(my q heads) * head_dim]
     on every rank -> [tokens][n_q_heads * head_dim] in global head order."""

@@ -1,6 +1,6 @@
 """Multi-GPU paths on real GPUs (skipped with fewer than two): head-sharded causal prefill
-over 2 ranks (torchrun, NCCL) against the full-head prefill of one GPU — identical per-head
-arithmetic, so identical outputs."""
+and value-head-sharded chunked DeltaNet prefill over 2 ranks (torchrun, NCCL) against the
+unsharded call on one GPU — identical per-head arithmetic, so identical outputs and state."""
 import os
 import socket
 import subprocess
@@ -33,3 +33,17 @@ def test_head_sharded_prefill_two_ranks(tmp_path):
     d = np.load(out)
     assert int(d["world"]) == 2
     np.testing.assert_array_equal(d["sharded"], d["full"])
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_value_head_sharded_deltanet_two_ranks(tmp_path):
+    out = tmp_path / "sharded_gdn.npz"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           os.path.join(HERE, "mgpu_gdn_worker.py"), str(out)]
+    r = subprocess.run(["timeout", "-k", "30", "240"] + cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    d = np.load(out)
+    assert int(d["world"]) == 2
+    np.testing.assert_array_equal(d["sharded"], d["full"])
+    np.testing.assert_array_equal(d["state_sharded"], d["state_full"])
