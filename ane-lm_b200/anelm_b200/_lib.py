@@ -83,6 +83,7 @@ SIGNATURES = {
     "anelm_gated_delta_chunked": [_vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp,
                                   ctypes.c_size_t, _vp],
     "anelm_py_cpu_attention": [_vp, _i, _i, _u16p, _u16p, _u16p, _i, _u16p, _vp],
+    "anelm_gemm_bf16": [_vp, ctypes.c_longlong, _vp, ctypes.c_longlong, _vp, ctypes.c_longlong, _i, _i, _i, _i, _vp],
     "anelm_gqa_attention": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "anelm_gqa_attention_noalloc": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],
     "anelm_ssm_step": [_vp, _vp, _vp, _vp, _vp, _f, _f, _i, _i, _vp],

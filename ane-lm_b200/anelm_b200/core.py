@@ -291,3 +291,19 @@ def gated_delta_chunked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, log_d
         B, T, Hk, Hv, dk, dv, delta_mode, ctypes.c_void_p(y.data_ptr()), _dtype_code(y),
         ctypes.c_void_p(workspace.data_ptr()), workspace.numel(), _stream(q.device)), "anelm_gated_delta_chunked")
     return y
+
+
+def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, out=None) -> torch.Tensor:
+    """a [M][K] @ b[N][K]^T on the tensor cores (anelm_gemm_bf16): bf16 inputs (row-major, unit
+    column stride), fp32 accumulation, result [M][N] of out_dtype (bf16 / fp16 / fp32)."""
+    assert a.is_cuda and b.is_cuda and a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16
+    assert a.dim() == 2 and b.dim() == 2 and a.stride(1) == 1 and b.stride(1) == 1 and a.shape[1] == b.shape[1]
+    M, K = a.shape
+    N = b.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    assert out.stride(1) == 1
+    check(lib().anelm_gemm_bf16(ctypes.c_void_p(a.data_ptr()), a.stride(0), ctypes.c_void_p(b.data_ptr()), b.stride(0),
+                                ctypes.c_void_p(out.data_ptr()), out.stride(0), _dtype_code(out), M, N, K,
+                                _stream(a.device)), "anelm_gemm_bf16")
+    return out

@@ -1158,6 +1158,15 @@ ANELM_API int anelm_gqa_attention(float* out, const float* q, const void* k_cach
     return launch_status(rc, "gqa_attention");
 }
 
+ANELM_API int anelm_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc,
+                              int c_dtype, int M, int N, int K, void* stream) {
+    if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || c_dtype < ANELM_F32 || c_dtype > ANELM_BF16)
+        return fail(ANELM_ERR_INVALID_ARG, "bad argument");
+    return launch_status(launch_gemm_bf16_tn(A, lda, B, ldb, C, ldc, c_dtype, M, N, K, nullptr,
+                                             static_cast<cudaStream_t>(stream)),
+                         "gemm_bf16");
+}
+
 ANELM_API int anelm_ssm_step(float* y, float* state, const float* q, const float* k, const float* v, float decay,
                              float beta, int key_dim, int value_dim, void* stream) {
     if (!y || !state || !q || !k || !v || key_dim <= 0 || value_dim <= 0) return fail(ANELM_ERR_INVALID_ARG, "bad argument");

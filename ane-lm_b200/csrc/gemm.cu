@@ -1,0 +1,267 @@
+// bf16 GEMM C = A B^T on tcgen05 (sm_100a): the projections on either side of the attention core.
+//
+// In the reference the Apple Neural Engine runs them: first_proj (hidden -> the q|gate|k|v or
+// qkv|z|a|b projection rows the core consumes) and o_proj (core output -> hidden),
+// models/llm/qwen3_5.cpp:912-1012 with core/ane_runtime.cpp:279-361 running the compiled
+// chunks.  Here they are plain dense GEMMs in the nn.Linear layout, A [M][K] (activations,
+// rows = tokens or sequences) times B [N][K] (weights, [out][in]), fp32 accumulation, so the
+// projections never leave the device around the core.
+//
+// One CTA per 128 x 256 output tile, 192 threads: warp 4 streams 128 x 64 tiles of A and 256 x 64
+// tiles of B (TMA, 128B swizzle, zero fill past M / N / K) through a 4-stage ring, one thread of
+// warp 5 issues tcgen05.mma (M = 128, N = 256, K = 16, both operands K-major from shared memory)
+// into a 256-column fp32 accumulator in TMEM and frees each stage with tcgen05.commit, warps 0-3
+// read the accumulator (one row per thread) and store it as bf16 / fp16 / fp32.  N = 256 halves the
+// operand bytes per FLOP against 128 x 128 tiles (whose loads ran at the L2-to-SM limit).
+// Grids of few tiles (decode-size M with a small N) split K over a thread-block cluster of up to
+// 8 CTAs per tile: each CTA accumulates its K range in TMEM, parks the fp32 partial in its (now
+// idle) stage buffers, and after a cluster barrier each CTA sums its share of the tile's rows over
+// all partials through distributed shared memory and stores them.  Every mbarrier wait
+// is bounded and reports ANELM_ERR_TIMEOUT.
+#include <algorithm>
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc100.cuh"
+
+namespace anelm {
+
+namespace {
+
+constexpr int kGBM = 128, kGBN = 256, kGBK = 64, kGStages = 4;
+constexpr int kGThreads = 192;
+constexpr int kGTileA = kGBM * kGBK * 2;  // 16 KB: 128 rows x 128 bytes
+constexpr int kGTileB = kGBN * kGBK * 2;  // 32 KB: 256 rows x 128 bytes
+constexpr int kGSmem = kGStages * (kGTileA + kGTileB) + 256 + 1024;
+constexpr int kGPartPitch = kGBN + 4;  // fp32 words per row of a parked split-K partial
+static_assert(kGBM * kGPartPitch * 4 <= kGStages * (kGTileA + kGTileB), "partial fits the stage buffers");
+
+// kind::f16 instruction descriptor with bf16 A and B (formats 1), fp32 D, both K-major
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
+    return tc::idesc_f16_f32(M, N) | (1u << 7) | (1u << 10);
+}
+
+__global__ void __launch_bounds__(kGThreads, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C,
+                        long long ldc, int c_dtype, int M, int N, int K, int ks, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kGStages * kGTileA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kGStages * kGTileB);
+    uint64_t* empty = full + kGStages;
+    uint64_t* done = empty + kGStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // ks > 1: blockIdx.x = tile * ks + split, the ks CTAs of a tile form one cluster
+    const int split = blockIdx.x % ks;
+    const int n0 = (blockIdx.x / ks) * kGBN, m0 = blockIdx.y * kGBM;
+    const int nk_all = (K + kGBK - 1) / kGBK;
+    const int per = (nk_all + ks - 1) / ks;
+    const int kt0 = split * per;
+    const int nk = max(0, min(nk_all, kt0 + per) - kt0);  // this CTA's k-tiles
+    if (tid == 0) {
+        *abort = 0;
+        for (int s = 0; s < kGStages; s++) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        tc::mbar_init(done, 1);
+        tc::fence_barrier_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, kGBN);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) {  // TMA producer
+            tc::prefetch_tmap(&tmA);
+            tc::prefetch_tmap(&tmB);
+            for (int kt = 0; kt < nk; kt++) {
+                const int s = kt % kGStages;
+                if (kt >= kGStages &&
+                    !tc::mbar_wait(&empty[s], (uint32_t)((kt / kGStages) - 1) & 1, err, ANELM_ERR_TIMEOUT, abort))
+                    break;
+                tc::mbar_arrive_expect_tx(&full[s], kGTileA + kGTileB);
+                tc::tma_load_2d(sA + s * kGTileA, &tmA, &full[s], (kt0 + kt) * kGBK, m0);
+                tc::tma_load_2d(sB + s * kGTileB, &tmB, &full[s], (kt0 + kt) * kGBK, n0);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = idesc_bf16_f32(kGBM, kGBN);
+            const uint32_t aA = (uint32_t)__cvta_generic_to_shared(sA), aB = (uint32_t)__cvta_generic_to_shared(sB);
+            int kt = 0;
+            for (; kt < nk; kt++) {
+                const int s = kt % kGStages;
+                if (!tc::mbar_wait(&full[s], (uint32_t)(kt / kGStages) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
+                tc::tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < kGBK / 16; ks++)
+                    tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(aA + s * kGTileA + ks * 32),
+                                   tc::desc_kmajor_sw128(aB + s * kGTileB + ks * 32), idesc, (kt | ks) != 0);
+                tc::mma_commit(&empty[s]);
+            }
+            tc::mma_commit(done);  // all MMAs issued (an aborted loop still completes `done`)
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: thread = accumulator row m0 + 32 warp + lane ----------------
+        const bool ok = tc::mbar_wait(done, 0, err, ANELM_ERR_TIMEOUT, abort);
+        tc::tc_fence_after();
+        const int m = m0 + 32 * warp + lane;
+        const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+        if (ks > 1) {  // park this split's partial (zeros for an empty K range) in the stage buffers
+            float* part = reinterpret_cast<float*>(smem) + (32 * warp + lane) * kGPartPitch;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kGBN; c0 += 32) {
+                uint32_t x[32];
+                tc::tmem_ld32(trow + c0, x);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int c4 = 0; c4 < 8; c4++)
+                    *reinterpret_cast<float4*>(part + c0 + 4 * c4) =
+                        nk > 0 ? make_float4(__uint_as_float(x[4 * c4]), __uint_as_float(x[4 * c4 + 1]),
+                                             __uint_as_float(x[4 * c4 + 2]), __uint_as_float(x[4 * c4 + 3]))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll 1
+        for (int c0 = 0; c0 < (ks > 1 ? 0 : kGBN); c0 += 32) {
+            uint32_t x[32];
+            tc::tmem_ld32(trow + c0, x);
+            tc::tmem_ld_wait();
+            if (!ok || m >= M) continue;
+            const int nb = n0 + c0;
+            if (nb + 32 <= N && c_dtype != ANELM_F32 && (ldc % 8) == 0 && ((uintptr_t)C % 16) == 0) {
+                uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(C) + (long long)m * ldc + nb);
+#pragma unroll
+                for (int c8 = 0; c8 < 4; c8++) {
+                    float v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] = __uint_as_float(x[8 * c8 + e]);
+                    dst[c8] = pack8(v, c_dtype == ANELM_BF16);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 32; c++)
+                    if (nb + c < N) store_from_float(C, c_dtype, (long long)m * ldc + nb + c, __uint_as_float(x[c]));
+            }
+        }
+    }
+    if (ks > 1) {
+        // ---------------- split-K: rows [split R, split R + R) summed over the cluster's partials ----------------
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();  // every split's partial is parked
+        const int R = (kGBM + ks - 1) / ks;
+        const int r0 = split * R, r1 = min(kGBM, r0 + R);
+        const float* part0 = reinterpret_cast<const float*>(smem);
+        for (int i = tid; i < (r1 - r0) * (kGBN / 4); i += kGThreads) {
+            const int r = r0 + i / (kGBN / 4), c = 4 * (i % (kGBN / 4));
+            const int m = m0 + r, n = n0 + c;
+            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q = 0; q < ks; q++) {
+                const float4 v = *reinterpret_cast<const float4*>(cl.map_shared_rank(part0 + r * kGPartPitch + c, q));
+                s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+            }
+            if (m >= M) continue;
+            const float o[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (n + e < N) store_from_float(C, c_dtype, (long long)m * ldc + n + e, o[e]);
+        }
+        cl.sync();  // peers are done reading this CTA's partial
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kGBN);
+    }
+}
+
+// 2D bf16 tensor map over a row-major [rows][cols] matrix (row stride ld elements), box {64, box_rows}
+bool make_bf16_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+    auto fn = tc::tmap_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kGBK, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int c_dtype,
+                        int M, int N, int K, int* err, cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0) return ANELM_ERR_INVALID_ARG;
+    if ((uintptr_t)A % 16 || (uintptr_t)B % 16 || (lda * 2) % 16 || (ldb * 2) % 16 || lda < K || ldb < K || ldc < N)
+        return ANELM_ERR_UNSUPPORTED;
+    CUtensorMap mA, mB;
+    if (!make_bf16_map(&mA, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, kGBM) ||
+        !make_bf16_map(&mB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, kGBN))
+        return ANELM_ERR_CUDA;
+    cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem);
+    const int tiles = ((N + kGBN - 1) / kGBN) * ((M + kGBM - 1) / kGBM);
+    const int nk = (K + kGBK - 1) / kGBK;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // split K over a cluster when the tiles fill less than half of the SMs: the largest cluster
+    // size (<= 8) of which the GPU can hold one cluster per tile at once (GPC packing caps it below
+    // the SM count / tiles), measured once per device and size
+    int ks = 1;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.blockDim = dim3(kGThreads);
+    cfg.dynamicSmemBytes = kGSmem;
+    cfg.stream = stream;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (2 * tiles < sms) {
+        static int active[16][9];  // [device][cluster size]: clusters resident at once (0 = not measured)
+        for (int c = std::min(8, std::min(nk, sms / tiles)); c >= 2 && ks == 1; c--) {
+            int& a = active[dev & 15][c];
+            if (a == 0) {
+                cfg.gridDim = dim3(c, 1);
+                attr[0].val.clusterDim.x = c;
+                if (cudaOccupancyMaxActiveClusters(&a, (void*)gemm_bf16_tn_kernel, &cfg) != cudaSuccess || a <= 0) {
+                    cudaGetLastError();
+                    a = -1;
+                }
+            }
+            if (a >= tiles) ks = c;
+        }
+        if (ks > 1) ks = (nk + ((nk + ks - 1) / ks) - 1) / ((nk + ks - 1) / ks);  // no empty K range
+    }
+    if (ks > 1) {
+        cfg.gridDim = dim3(((N + kGBN - 1) / kGBN) * ks, (M + kGBM - 1) / kGBM);
+        attr[0].val.clusterDim.x = ks;
+        if (cudaLaunchKernelEx(&cfg, gemm_bf16_tn_kernel, mA, mB, C, ldc, c_dtype, M, N, K, ks, err) == cudaSuccess)
+            return ANELM_OK;
+        cudaGetLastError();  // a cluster that cannot be placed: one CTA per tile instead
+    }
+    dim3 grid((N + kGBN - 1) / kGBN, (M + kGBM - 1) / kGBM);
+    gemm_bf16_tn_kernel<<<grid, kGThreads, kGSmem, stream>>>(mA, mB, C, ldc, c_dtype, M, N, K, 1, err);
+    return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
+}
+
+}  // namespace anelm

@@ -175,4 +175,9 @@ void set_last_error(const char* msg);
 
 int launch_gdn_decode(const GdnDecodeParams& p, int n_rows, int key_dim, int val_dim, cudaStream_t stream);
 
+// bf16 GEMM C[M][N] = A[M][K] B[N][K]^T (nn.Linear layout), fp32 accumulation, C of c_dtype.
+// A, B 16-byte aligned with row strides lda, ldb (elements) multiples of 8.
+int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int c_dtype,
+                        int M, int N, int K, int* err, cudaStream_t stream);
+
 }  // namespace anelm

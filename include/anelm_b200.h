@@ -268,6 +268,15 @@ ANELM_API int anelm_gqa_attention(float* out, const float* q, const void* k_cach
                                   int head_dim, int q_head_stride, int cache_start, int cache_len,
                                   int cache_capacity, void* stream);
 
+/* Dense projection on the tensor cores: C[M][N] = A[M][K] * B[N][K]^T with bf16 A, B
+ * (nn.Linear layout: A = activations [rows][in], B = weights [out][in]), fp32 accumulation,
+ * C of c_dtype (ANELM_BF16 / ANELM_F16 / ANELM_F32) with row stride ldc.  The reference runs
+ * these projections on the ANE around the CPU core: first_proj and o_proj,
+ * models/llm/qwen3_5.cpp:912-1012, core/ane_runtime.cpp:279-361.  Device pointers; A and B
+ * 16-byte aligned, lda and ldb multiples of 8 (ANELM_ERR_UNSUPPORTED otherwise). */
+ANELM_API int anelm_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc,
+                              int c_dtype, int M, int N, int K, void* stream);
+
 /* Allocation-free variant of anelm_gqa_attention for fp16 caches.  No
  * counterpart in the reference.  For callers that cannot allocate device memory
  * where attention runs: a server whose own pool already holds all free HBM (a
