@@ -78,6 +78,8 @@ SIGNATURES = {
     "anelm_plan_info": [_vp, _ip, _ip],
     "anelm_full_attn_decode": [_vp, _vp, _i, _vp, _i, _vp, _vp, _i, _vp],
     "anelm_deltanet_decode": [_vp, _vp, _i, _vp, _i, _vp, _i, _vp],
+    "anelm_set_layer_projections": [_vp, _i, _i, _vp, _vp],
+    "anelm_layer_decode": [_vp, _vp, _i, _vp, _vp, _vp, _vp],
     "anelm_full_attn_prefill": [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _vp],
     "anelm_deltanet_prefill": [_vp, _vp, _i, _i, _vp, _i, _vp, _i, _vp],
     "anelm_gated_delta_chunked": [_vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp,

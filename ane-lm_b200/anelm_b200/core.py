@@ -259,6 +259,25 @@ class Context:
                                            _stream(proj.device)), "anelm_deltanet_prefill")
         return out
 
+    def set_layer_projections(self, layer: int, w_in: torch.Tensor, w_out: torch.Tensor):
+        """bf16 projection weights of a layer (anelm_set_layer_projections): w_in [proj_dim][hidden],
+        w_out [hidden][core out], CPU or CUDA tensors."""
+        assert w_in.dtype == torch.bfloat16 and w_out.dtype == torch.bfloat16
+        w_in, w_out = w_in.contiguous(), w_out.contiguous()
+        check(lib().anelm_set_layer_projections(self.handle, layer, w_in.shape[1], ctypes.c_void_p(w_in.data_ptr()),
+                                                ctypes.c_void_p(w_out.data_ptr())), "anelm_set_layer_projections")
+
+    def layer_decode(self, plan: Plan, layer: int, x: torch.Tensor, pos: torch.Tensor = None, y=None):
+        """One decode layer on the device (anelm_layer_decode): x [n][hidden] bf16 -> in-projection,
+        core, out-projection -> y [n][hidden] bf16; pos [n] int32 for attention layers."""
+        assert x.is_cuda and x.is_contiguous() and x.dtype == torch.bfloat16 and x.shape[0] == plan.n
+        if y is None:
+            y = torch.empty_like(x)
+        pp = ctypes.c_void_p(pos.data_ptr()) if pos is not None else None
+        check(lib().anelm_layer_decode(self.handle, plan.handle, layer, ctypes.c_void_p(x.data_ptr()), pp,
+                                       ctypes.c_void_p(y.data_ptr()), _stream(x.device)), "anelm_layer_decode")
+        return y
+
     def deltanet_decode(self, plan: Plan, layer: int, proj: torch.Tensor, out=None, out_dtype=torch.float32):
         assert proj.is_cuda and proj.is_contiguous() and proj.shape == (plan.n, self.gdn_proj_dim)
         if out is None:

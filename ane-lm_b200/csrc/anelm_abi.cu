@@ -7,6 +7,7 @@
 // (qwen3_5.cpp:849-1002) into launches of the fused kernels.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -122,6 +123,10 @@ struct anelm_ctx {
     size_t prefill_ws_bytes = 0;
     void* gdn_prefill_ws = nullptr;  // DeltaNet prefill staging (chunk operands), grown on demand
     size_t gdn_prefill_ws_bytes = 0;
+    std::vector<void*> w_in, w_out;  // per layer, bf16: [proj_dim][hidden], [hidden][core out] (or null)
+    std::vector<int> hidden;         // per layer hidden size of the projections (0: not set)
+    void* layer_ws = nullptr;        // layer-step staging (projection rows, core output), grown on demand
+    size_t layer_ws_bytes = 0;
     __half* py_proj = nullptr;  // staging for anelm_py_cpu_attention
     __half* py_out = nullptr;
     std::vector<void*> allocs;
@@ -455,6 +460,9 @@ ANELM_API int anelm_create(const anelm_config* cfg, int device, anelm_ctx** out)
     ctx->cfg = c;
     ctx->device = device;
     ctx->layer_types.resize(c.num_layers);
+    ctx->w_in.assign(c.num_layers, nullptr);
+    ctx->w_out.assign(c.num_layers, nullptr);
+    ctx->hidden.assign(c.num_layers, 0);
     for (int l = 0; l < c.num_layers; l++) {
         if (c.layer_types) {
             ctx->layer_types[l] = c.layer_types[l];
@@ -571,6 +579,9 @@ ANELM_API int anelm_destroy(anelm_ctx* ctx) {
     for (auto& kv : ctx->single) free_plan(kv.second);
     if (ctx->prefill_ws) cudaFree(ctx->prefill_ws);
     if (ctx->gdn_prefill_ws) cudaFree(ctx->gdn_prefill_ws);
+    if (ctx->layer_ws) cudaFree(ctx->layer_ws);
+    for (void* w : ctx->w_in) if (w) cudaFree(w);
+    for (void* w : ctx->w_out) if (w) cudaFree(w);
     for (void* a : ctx->allocs) cudaFree(a);
     delete ctx;
     return ANELM_OK;
@@ -972,6 +983,87 @@ ANELM_API int anelm_gated_delta_chunked(const void* q, const void* k, const void
 ANELM_API int anelm_deltanet_decode(anelm_ctx* ctx, const anelm_plan* plan, int layer, const void* proj,
                                     int proj_dtype, void* out, int out_dtype, void* stream) {
     return gdn_launch(ctx, plan, layer, proj, proj_dtype, out, out_dtype, stream);
+}
+
+// Projection widths around the core of a layer: rows in (the projections the core reads) and
+// the core's output row.
+static void layer_widths(const anelm_ctx* ctx, int layer, int* proj_dim, int* out_dim) {
+    const anelm_config& c = ctx->cfg;
+    if (ctx->layer_types[layer] == ANELM_LAYER_FULL_ATTN) {
+        *proj_dim = ctx->fa_proj;
+        *out_dim = c.num_q_heads * c.head_dim;
+    } else {
+        *proj_dim = ctx->gdn_proj;
+        *out_dim = c.lin_num_val_heads * c.lin_val_dim;
+    }
+}
+
+ANELM_API int anelm_set_layer_projections(anelm_ctx* ctx, int layer, int hidden, const void* w_in,
+                                          const void* w_out) {
+    if (!ctx) return fail(ANELM_ERR_INVALID_ARG, "null context");
+    if (layer < 0 || layer >= ctx->cfg.num_layers)
+        return fail(ANELM_ERR_INVALID_ARG, "layer %d out of range [0,%d)", layer, ctx->cfg.num_layers);
+    if (!w_in || !w_out || hidden <= 0 || hidden % 8)
+        return fail(ANELM_ERR_INVALID_ARG, "projection weights need hidden > 0, a multiple of 8");
+    int pd = 0, od = 0;
+    layer_widths(ctx, layer, &pd, &od);
+    if (pd % 8 || od % 8) return fail(ANELM_ERR_UNSUPPORTED, "projection widths %d / %d not multiples of 8", pd, od);
+    DeviceGuard dg(ctx->device);
+    for (void** w : {&ctx->w_in[layer], &ctx->w_out[layer]}) {
+        if (*w) cudaFree(*w);
+        *w = nullptr;
+    }
+    ctx->hidden[layer] = 0;
+    const size_t bi = (size_t)pd * hidden * 2, bo = (size_t)hidden * od * 2;
+    if (cudaMalloc(&ctx->w_in[layer], bi) != cudaSuccess || cudaMalloc(&ctx->w_out[layer], bo) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ANELM_ERR_NOMEM, "projection weights of layer %d", layer);
+    }
+    CUDA_TRY(cudaMemcpy(ctx->w_in[layer], w_in, bi, cudaMemcpyDefault));
+    CUDA_TRY(cudaMemcpy(ctx->w_out[layer], w_out, bo, cudaMemcpyDefault));
+    ctx->hidden[layer] = hidden;
+    return ANELM_OK;
+}
+
+ANELM_API int anelm_layer_decode(anelm_ctx* ctx, const anelm_plan* plan, int layer, const void* x, const int* pos,
+                                 void* y, void* stream) {
+    if (!ctx) return fail(ANELM_ERR_INVALID_ARG, "null context");
+    if (layer < 0 || layer >= ctx->cfg.num_layers)
+        return fail(ANELM_ERR_INVALID_ARG, "layer %d out of range [0,%d)", layer, ctx->cfg.num_layers);
+    if (!plan || plan->ctx != ctx) return fail(ANELM_ERR_INVALID_ARG, "plan belongs to another context");
+    if (!x || !y) return fail(ANELM_ERR_INVALID_ARG, "null tensor");
+    const int H = ctx->hidden[layer];
+    if (!H) return fail(ANELM_ERR_STATE, "projections of layer %d not set", layer);
+    const bool fa = ctx->layer_types[layer] == ANELM_LAYER_FULL_ATTN;
+    if (fa && !pos) return fail(ANELM_ERR_INVALID_ARG, "null positions");
+    int pd = 0, od = 0;
+    layer_widths(ctx, layer, &pd, &od);
+    const int n = plan->n;
+    DeviceGuard dg(ctx->device);
+    const size_t need = (size_t)n * (pd + od) * 2 + 256;
+    if (need > ctx->layer_ws_bytes) {
+        if (ctx->layer_ws) cudaFree(ctx->layer_ws);
+        ctx->layer_ws = nullptr;
+        ctx->layer_ws_bytes = 0;
+        if (cudaMalloc(&ctx->layer_ws, need) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ANELM_ERR_NOMEM, "layer-step staging of %zu bytes", need);
+        }
+        ctx->layer_ws_bytes = need;
+    }
+    __nv_bfloat16* proj = static_cast<__nv_bfloat16*>(ctx->layer_ws);
+    __nv_bfloat16* core = proj + ((size_t)n * pd + 127) / 128 * 128;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // first_proj on the device: [n][hidden] x [proj_dim][hidden]^T -> projection rows
+    if (int rc = launch_status(launch_gemm_bf16_tn(x, H, ctx->w_in[layer], H, proj, pd, ANELM_BF16, n, pd, H, ctx->err, st),
+                               "layer in-projection"))
+        return rc;
+    const int rc = fa ? fa_launch(ctx, plan, layer, proj, ANELM_BF16, pos, 0, core, ANELM_BF16, stream)
+                      : gdn_launch(ctx, plan, layer, proj, ANELM_BF16, core, ANELM_BF16, stream);
+    if (rc) return rc;
+    // o_proj: [n][core out] x [hidden][core out]^T -> hidden rows
+    return launch_status(launch_gemm_bf16_tn(core, od, ctx->w_out[layer], od, y, H, ANELM_BF16, n, H, od, ctx->err, st),
+                         "layer out-projection");
 }
 
 ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,

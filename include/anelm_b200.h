@@ -205,6 +205,22 @@ ANELM_API int anelm_deltanet_decode(anelm_ctx* ctx, const anelm_plan* plan, int 
                                     const void* proj, int proj_dtype, void* out, int out_dtype,
                                     void* stream);
 
+/* ---- layer steps: projections on the device around the core ----
+ * The reference runs first_proj and o_proj on the ANE and hands the core host fp32
+ * projection rows (models/llm/qwen3_5.cpp:912-1012, core/ane_runtime.cpp:279-361).  With the
+ * projection weights in the context, one call runs a decode layer's in-projection (tcgen05
+ * GEMM), its core (anelm_full_attn_decode / anelm_deltanet_decode) and its out-projection
+ * without leaving the device.
+ * w_in: bf16 [proj_dim][hidden] (attention: Hq*2d + 2*Hkv*d rows in the q|gate, k, v order of
+ * qwen3_5.cpp:948-950; DeltaNet: 2*Hk*dk + 2*Hv*dv + 2*Hv rows, qkv | z | a | b of
+ * qwen3_5.cpp:853-860); w_out: bf16 [hidden][core out] (Hq*d or Hv*dv).  Host or device
+ * pointers; hidden a multiple of 8. */
+ANELM_API int anelm_set_layer_projections(anelm_ctx* ctx, int layer, int hidden, const void* w_in,
+                                          const void* w_out);
+/* x [n][hidden] bf16 -> y [n][hidden] bf16 for the plan's n rows; pos [n] (attention layers). */
+ANELM_API int anelm_layer_decode(anelm_ctx* ctx, const anelm_plan* plan, int layer, const void* x,
+                                 const int* pos, void* y, void* stream);
+
 /* ---- prefill ---- */
 
 /* Causal prefill of the plan's sequences, each of n_tokens prompt tokens, into
