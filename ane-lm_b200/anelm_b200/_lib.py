@@ -86,6 +86,8 @@ SIGNATURES = {
                                   ctypes.c_size_t, _vp],
     "anelm_py_cpu_attention": [_vp, _i, _i, _u16p, _u16p, _u16p, _i, _u16p, _vp],
     "anelm_gemm_bf16": [_vp, ctypes.c_longlong, _vp, ctypes.c_longlong, _vp, ctypes.c_longlong, _i, _i, _i, _i, _vp],
+    "anelm_lm_head_topk": [_vp, ctypes.c_longlong, _vp, ctypes.c_longlong, _i, _i, _i, _i, _vp, _vp, _vp,
+                           ctypes.c_size_t, _vp],
     "anelm_gqa_attention": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "anelm_gqa_attention_noalloc": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],
     "anelm_ssm_step": [_vp, _vp, _vp, _vp, _vp, _f, _f, _i, _i, _vp],
@@ -132,6 +134,8 @@ def lib() -> ctypes.CDLL:
     L.anelm_version.restype = ctypes.c_char_p
     L.anelm_gated_delta_chunked_workspace_bytes.argtypes = [_i, _i, _i, _i]
     L.anelm_gated_delta_chunked_workspace_bytes.restype = ctypes.c_size_t
+    L.anelm_lm_head_topk_workspace_bytes.argtypes = [_i, _i]
+    L.anelm_lm_head_topk_workspace_bytes.restype = ctypes.c_size_t
     _lib = L
     return L
 

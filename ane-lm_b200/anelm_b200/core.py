@@ -326,3 +326,23 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, out=No
                                 ctypes.c_void_p(out.data_ptr()), out.stride(0), _dtype_code(out), M, N, K,
                                 _stream(a.device)), "anelm_gemm_bf16")
     return out
+
+
+def lm_head_topk(h: torch.Tensor, w: torch.Tensor, k: int = 32, workspace=None):
+    """Top-k logits of h [n][hidden] @ w[vocab][hidden]^T without materialising the logits
+    (anelm_lm_head_topk): bf16 inputs; returns (values fp32 [n][k], indices int32 [n][k]),
+    sorted descending."""
+    assert h.is_cuda and w.is_cuda and h.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+    assert h.dim() == 2 and w.dim() == 2 and h.stride(1) == 1 and w.stride(1) == 1 and h.shape[1] == w.shape[1]
+    n, hidden = h.shape
+    vocab = w.shape[0]
+    vals = torch.empty((n, k), dtype=torch.float32, device=h.device)
+    idx = torch.empty((n, k), dtype=torch.int32, device=h.device)
+    need = lib().anelm_lm_head_topk_workspace_bytes(n, vocab)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=h.device)
+    check(lib().anelm_lm_head_topk(ctypes.c_void_p(h.data_ptr()), h.stride(0), ctypes.c_void_p(w.data_ptr()),
+                                   w.stride(0), n, vocab, hidden, k, ctypes.c_void_p(vals.data_ptr()),
+                                   ctypes.c_void_p(idx.data_ptr()), ctypes.c_void_p(workspace.data_ptr()),
+                                   workspace.numel(), _stream(h.device)), "anelm_lm_head_topk")
+    return vals, idx

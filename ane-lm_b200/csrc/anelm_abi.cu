@@ -1259,6 +1259,24 @@ ANELM_API int anelm_gemm_bf16(const void* A, long long lda, const void* B, long 
                          "gemm_bf16");
 }
 
+ANELM_API size_t anelm_lm_head_topk_workspace_bytes(int n, int vocab) {
+    return (n > 0 && vocab > 0) ? lm_head_topk_workspace_bytes(n, vocab) : 0;
+}
+
+ANELM_API int anelm_lm_head_topk(const void* h, long long ldh, const void* W, long long ldw, int n, int vocab,
+                                 int hidden, int k, float* top_vals, int* top_idx, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+    if (!h || !W || !top_vals || !top_idx || !workspace || n <= 0 || vocab <= 0 || hidden <= 0 || k < 1 || k > 32 ||
+        k > vocab)
+        return fail(ANELM_ERR_INVALID_ARG, "bad argument");
+    if (workspace_bytes < lm_head_topk_workspace_bytes(n, vocab))
+        return fail(ANELM_ERR_CAPACITY, "workspace of %zu bytes, %zu needed", workspace_bytes,
+                    lm_head_topk_workspace_bytes(n, vocab));
+    return launch_status(launch_lm_head_topk(h, ldh, W, ldw, n, vocab, hidden, k, top_vals, top_idx, workspace,
+                                             workspace_bytes, nullptr, static_cast<cudaStream_t>(stream)),
+                         "lm_head_topk");
+}
+
 ANELM_API int anelm_ssm_step(float* y, float* state, const float* q, const float* k, const float* v, float decay,
                              float beta, int key_dim, int value_dim, void* stream) {
     if (!y || !state || !q || !k || !v || key_dim <= 0 || value_dim <= 0) return fail(ANELM_ERR_INVALID_ARG, "bad argument");

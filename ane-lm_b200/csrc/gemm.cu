@@ -16,7 +16,15 @@
 // Grids of few tiles (decode-size M with a small N) split K over a thread-block cluster of up to
 // 8 CTAs per tile: each CTA accumulates its K range in TMEM, parks the fp32 partial in its (now
 // idle) stage buffers, and after a cluster barrier each CTA sums its share of the tile's rows over
-// all partials through distributed shared memory and stores them.  Every mbarrier wait
+// all partials through distributed shared memory and stores them.
+//
+// The LM head with in-model top-k (export_hybrid_chunks.py:409-421, LMHeadArgmax: logits =
+// x W^T over the vocabulary, then torch.topk(32), read by serve_hybrid.py:283-307) reuses the
+// same tiles in a persistent kernel: each CTA walks a strided set of 256-column vocabulary tiles
+// for its 128 rows, with two TMEM accumulators so that the MMAs of tile i+1 run while the
+// epilogue folds tile i into each row's running top-32 (kept sorted in registers); it writes one
+// candidate list per row, and lm_topk_merge_kernel reduces the CTAs' lists to the row's top-k.
+// The vocabulary logits never reach memory.  Every mbarrier wait
 // is bounded and reports ANELM_ERR_TIMEOUT.
 #include <algorithm>
 #include <cooperative_groups.h>
@@ -38,11 +46,30 @@ constexpr int kGTileA = kGBM * kGBK * 2;  // 16 KB: 128 rows x 128 bytes
 constexpr int kGTileB = kGBN * kGBK * 2;  // 32 KB: 256 rows x 128 bytes
 constexpr int kGSmem = kGStages * (kGTileA + kGTileB) + 256 + 1024;
 constexpr int kGPartPitch = kGBN + 4;  // fp32 words per row of a parked split-K partial
+// LM head: stage ring, barriers, and a [128][33] fp32 chunk staging area for the epilogue
+constexpr int kLmSmem = kGStages * (kGTileA + kGTileB) + 256 + 128 * 33 * 4 + 1024;
 static_assert(kGBM * kGPartPitch * 4 <= kGStages * (kGTileA + kGTileB), "partial fits the stage buffers");
 
 // kind::f16 instruction descriptor with bf16 A and B (formats 1), fp32 D, both K-major
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
     return tc::idesc_f16_f32(M, N) | (1u << 7) | (1u << 10);
+}
+
+// Insert (v, id) into the descending list (tv, ti) of 32 (static indices: registers).  Every top-k
+// with k <= 32 is the head of the top-32, so the lists always hold 32.
+constexpr int kTopK = 32;
+__device__ __forceinline__ void topk_insert(float (&tv)[kTopK], int (&ti)[kTopK], float v, int id) {
+#pragma unroll
+    for (int j = 0; j < kTopK; j++) {
+        if (v > tv[j]) {
+            const float tf = tv[j];
+            const int tn = ti[j];
+            tv[j] = v;
+            ti[j] = id;
+            v = tf;
+            id = tn;
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kGThreads, 1)
@@ -261,6 +288,245 @@ int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long l
     }
     dim3 grid((N + kGBN - 1) / kGBN, (M + kGBM - 1) / kGBM);
     gemm_bf16_tn_kernel<<<grid, kGThreads, kGSmem, stream>>>(mA, mB, C, ldc, c_dtype, M, N, K, 1, err);
+    return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
+}
+
+namespace {
+
+// Persistent LM-head kernel: CTA (g, mt) handles vocabulary tiles g, g + G, ... (G = gridDim.x)
+// for rows [128 mt, 128 mt + 128).  Warp 4: TMA ring (A rows, B vocabulary rows); warp 5: MMAs
+// of each tile into TMEM buffer (i & 1) once the epilogue released it; warps 0-3: per row, the
+// running top-32 over all its tiles, then one candidate list [M][G][32] (values, then indices).
+__global__ void __launch_bounds__(kGThreads, 1)
+    lm_head_topk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* cand,
+                        int M, int N, int K, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kGStages * kGTileA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kGStages * kGTileB);
+    uint64_t* empty = full + kGStages;
+    uint64_t* tfull = empty + kGStages;  // [2] accumulator b holds a finished tile
+    uint64_t* tfree = tfull + 2;         // [2] the epilogue has read accumulator b
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* rows = reinterpret_cast<float*>(tmem_slot + 4);  // [128][33] chunk staging
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, g = blockIdx.x, m0 = blockIdx.y * kGBM;
+    const int ntile = (N + kGBN - 1) / kGBN;
+    const int my_tiles = g < ntile ? (ntile - 1 - g) / G + 1 : 0;
+    const int nk = (K + kGBK - 1) / kGBK;
+    if (tid == 0) {
+        *abort = 0;
+        for (int s = 0; s < kGStages; s++) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            tc::mbar_init(&tfull[b], 1);
+            tc::mbar_init(&tfree[b], 128);
+        }
+        tc::fence_barrier_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, 2 * kGBN);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) {  // TMA producer over (tile, k-step), one continuous ring
+            tc::prefetch_tmap(&tmA);
+            tc::prefetch_tmap(&tmB);
+            long long q = 0;
+            for (int i = 0; i < my_tiles && !*abort; i++) {
+                const int n0 = (g + i * G) * kGBN;
+                for (int kt = 0; kt < nk; kt++, q++) {
+                    const int s = (int)(q % kGStages);
+                    if (q >= kGStages &&
+                        !tc::mbar_wait(&empty[s], (uint32_t)((q / kGStages) - 1) & 1, err, ANELM_ERR_TIMEOUT, abort))
+                        break;
+                    tc::mbar_arrive_expect_tx(&full[s], kGTileA + kGTileB);
+                    tc::tma_load_2d(sA + s * kGTileA, &tmA, &full[s], kt * kGBK, m0);
+                    tc::tma_load_2d(sB + s * kGTileB, &tmB, &full[s], kt * kGBK, n0);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = idesc_bf16_f32(kGBM, kGBN);
+            const uint32_t aA = (uint32_t)__cvta_generic_to_shared(sA), aB = (uint32_t)__cvta_generic_to_shared(sB);
+            long long q = 0;
+            for (int i = 0; i < my_tiles; i++) {
+                const int b = i & 1;
+                if (i >= 2 && !tc::mbar_wait(&tfree[b], (uint32_t)((i >> 1) - 1) & 1, err, ANELM_ERR_TIMEOUT, abort))
+                    break;
+                tc::tc_fence_after();
+                bool ok = true;
+                for (int kt = 0; kt < nk; kt++, q++) {
+                    const int s = (int)(q % kGStages);
+                    if (!tc::mbar_wait(&full[s], (uint32_t)(q / kGStages) & 1, err, ANELM_ERR_TIMEOUT, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < kGBK / 16; ks++)
+                        tc::mma_f16_ss(tmem + b * kGBN, tc::desc_kmajor_sw128(aA + s * kGTileA + ks * 32),
+                                       tc::desc_kmajor_sw128(aB + s * kGTileB + ks * 32), idesc, (kt | ks) != 0);
+                    tc::mma_commit(&empty[s]);
+                }
+                tc::mma_commit(&tfull[b]);
+                if (!ok) break;
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: row m = m0 + tid, running top-32 over this CTA's tiles ----------------
+        const int m = m0 + tid;
+        const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+        float* row = rows + tid * 33;
+        float tv[kTopK];
+        int ti[kTopK];
+#pragma unroll
+        for (int j = 0; j < kTopK; j++) {
+            tv[j] = -INFINITY;
+            ti[j] = -1;
+        }
+        for (int i = 0; i < my_tiles; i++) {
+            const int b = i & 1, n0 = (g + i * G) * kGBN;
+            if (!tc::mbar_wait(&tfull[b], (uint32_t)(i >> 1) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
+            tc::tc_fence_after();
+#pragma unroll 1
+            for (int c0 = 0; c0 < kGBN; c0 += 32) {
+                uint32_t x[32];
+                tc::tmem_ld32(trow + b * kGBN + c0, x);
+                tc::tmem_ld_wait();
+                if (c0 == kGBN - 32) {  // every column of accumulator b is read: the MMAs may reuse it
+                    tc::tc_fence_before();
+                    tc::mbar_arrive(&tfree[b]);
+                }
+#pragma unroll
+                for (int c = 0; c < 32; c++) row[c] = __uint_as_float(x[c]);
+#pragma unroll 1
+                for (int c = 0; c < 32; c++) {
+                    const int n = n0 + c0 + c;
+                    const float v = row[c];
+                    if (n < N && v > tv[kTopK - 1]) topk_insert(tv, ti, v, n);
+                }
+            }
+        }
+        if (m < M) {
+            float4* cv = reinterpret_cast<float4*>(cand + ((long long)m * G + g) * kTopK);
+            int4* ci = reinterpret_cast<int4*>(reinterpret_cast<int*>(cand + (long long)M * G * kTopK) +
+                                               ((long long)m * G + g) * kTopK);
+#pragma unroll
+            for (int j = 0; j < kTopK / 4; j++) {
+                cv[j] = make_float4(tv[4 * j], tv[4 * j + 1], tv[4 * j + 2], tv[4 * j + 3]);
+                ci[j] = make_int4(ti[4 * j], ti[4 * j + 1], ti[4 * j + 2], ti[4 * j + 3]);
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 2 * kGBN);
+    }
+}
+
+}  // namespace
+
+namespace {
+
+// One CTA per row: each thread keeps the top-32 of its share of the row's n_tiles * 32 candidates,
+// then pairs of lists merge in shared memory (7 levels) into the row's top-32, sorted descending;
+// the first k are written.
+constexpr int kMergeThreads = 128;
+__global__ void __launch_bounds__(kMergeThreads) lm_topk_merge_kernel(const float* cand, int M, int ntile, int k,
+                                                                       float* top_vals, int* top_idx) {
+    __shared__ float sv[kMergeThreads][kTopK + 1];
+    __shared__ int si[kMergeThreads][kTopK + 1];
+    const int m = blockIdx.x, tid = threadIdx.x;
+    const long long nc = (long long)ntile * kTopK;
+    const float* cv = cand + (long long)m * nc;
+    const int* ci = reinterpret_cast<const int*>(cand + (long long)M * nc) + (long long)m * nc;
+    float tv[kTopK];
+    int ti[kTopK];
+#pragma unroll
+    for (int j = 0; j < kTopK; j++) {
+        tv[j] = -INFINITY;
+        ti[j] = -1;
+    }
+    for (long long i = tid; i < nc; i += kMergeThreads) {
+        const float v = cv[i];
+        if (v > tv[kTopK - 1]) topk_insert(tv, ti, v, ci[i]);
+    }
+#pragma unroll
+    for (int j = 0; j < kTopK; j++) {
+        sv[tid][j] = tv[j];
+        si[tid][j] = ti[j];
+    }
+    __syncthreads();
+    for (int s = 1; s < kMergeThreads; s <<= 1) {
+        if ((tid & (2 * s - 1)) == 0) {
+            for (int j = 0; j < kTopK; j++) {
+                const float v = sv[tid + s][j];
+                if (!(v > tv[kTopK - 1])) break;  // the partner's list is sorted: the rest cannot enter
+                topk_insert(tv, ti, v, si[tid + s][j]);
+            }
+#pragma unroll
+            for (int j = 0; j < kTopK; j++) {
+                sv[tid][j] = tv[j];
+                si[tid][j] = ti[j];
+            }
+        }
+        __syncthreads();
+    }
+    if (tid < k) {
+        top_vals[(long long)m * k + tid] = sv[0][tid];
+        top_idx[(long long)m * k + tid] = si[0][tid];
+    }
+}
+
+}  // namespace
+
+// CTAs over the vocabulary per 128-row tile (about one CTA per SM overall, at most one per tile)
+static int lm_groups(int n, int vocab) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int mt = (n + kGBM - 1) / kGBM, ntile = (vocab + kGBN - 1) / kGBN;
+    return std::max(1, std::min(ntile, sms / mt));
+}
+
+size_t lm_head_topk_workspace_bytes(int n, int vocab) {
+    return (size_t)n * lm_groups(n, vocab) * kTopK * 8;
+}
+
+int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long ldw, int n, int vocab, int hidden, int k,
+                        float* top_vals, int* top_idx, void* workspace, size_t workspace_bytes, int* err,
+                        cudaStream_t stream) {
+    if (n <= 0 || vocab <= 0 || hidden <= 0 || k < 1 || k > 32 || k > vocab) return ANELM_ERR_INVALID_ARG;
+    if (workspace_bytes < lm_head_topk_workspace_bytes(n, vocab)) return ANELM_ERR_CAPACITY;
+    if ((uintptr_t)h % 16 || (uintptr_t)W % 16 || (ldh * 2) % 16 || (ldw * 2) % 16 || ldh < hidden || ldw < hidden ||
+        (uintptr_t)workspace % 16)
+        return ANELM_ERR_UNSUPPORTED;
+    CUtensorMap mA, mB;
+    if (!make_bf16_map(&mA, h, (uint64_t)n, (uint64_t)hidden, (uint64_t)ldh, kGBM) ||
+        !make_bf16_map(&mB, W, (uint64_t)vocab, (uint64_t)hidden, (uint64_t)ldw, kGBN))
+        return ANELM_ERR_CUDA;
+    constexpr int smem = kLmSmem;
+    cudaFuncSetAttribute(lm_head_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    const int G = lm_groups(n, vocab);
+    dim3 grid(G, (n + kGBM - 1) / kGBM);
+    lm_head_topk_kernel<<<grid, kGThreads, smem, stream>>>(mA, mB, static_cast<float*>(workspace), n, vocab, hidden, err);
+    lm_topk_merge_kernel<<<n, kMergeThreads, 0, stream>>>(static_cast<const float*>(workspace), n, G, k, top_vals,
+                                                          top_idx);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 

@@ -179,5 +179,11 @@ int launch_gdn_decode(const GdnDecodeParams& p, int n_rows, int key_dim, int val
 // A, B 16-byte aligned with row strides lda, ldb (elements) multiples of 8.
 int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int c_dtype,
                         int M, int N, int K, int* err, cudaStream_t stream);
+// LM head with in-model top-k (k <= 32): top_vals / top_idx [n][k] of h [n][hidden] W [vocab][hidden]^T,
+// sorted descending; workspace of lm_head_topk_workspace_bytes(n, vocab) bytes (16-byte aligned).
+size_t lm_head_topk_workspace_bytes(int n, int vocab);
+int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long ldw, int n, int vocab, int hidden, int k,
+                        float* top_vals, int* top_idx, void* workspace, size_t workspace_bytes, int* err,
+                        cudaStream_t stream);
 
 }  // namespace anelm

@@ -293,6 +293,19 @@ ANELM_API int anelm_gqa_attention(float* out, const float* q, const void* k_cach
 ANELM_API int anelm_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc,
                               int c_dtype, int M, int N, int K, void* stream);
 
+/* LM head with in-model top-k: the k (<= 32) largest logits of each row of h [n][hidden] times
+ * W [vocab][hidden]^T (bf16, nn.Linear layout), values (fp32) and vocabulary indices sorted
+ * descending — LMHeadArgmax of scripts/export_hybrid_chunks.py:409-421 (torch.topk(32) on the
+ * ANE so that 2 x 32 values instead of the vocabulary's logits leave it), read by
+ * serve_hybrid.py:283-307.  The logits are never written: the GEMM's epilogue keeps each row's
+ * top-32 per 256-column vocabulary tile (candidates in `workspace`, at least
+ * anelm_lm_head_topk_workspace_bytes(n, vocab) bytes, 16-byte aligned) and a second kernel
+ * merges them.  Ties between equal logits may order differently than torch.topk. */
+ANELM_API size_t anelm_lm_head_topk_workspace_bytes(int n, int vocab);
+ANELM_API int anelm_lm_head_topk(const void* h, long long ldh, const void* W, long long ldw, int n, int vocab,
+                                 int hidden, int k, float* top_vals, int* top_idx, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* Allocation-free variant of anelm_gqa_attention for fp16 caches.  No
  * counterpart in the reference.  For callers that cannot allocate device memory
  * where attention runs: a server whose own pool already holds all free HBM (a

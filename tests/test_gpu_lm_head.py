@@ -1,0 +1,41 @@
+"""GPU parity of the LM head with in-model top-k (anelm_lm_head_topk; LMHeadArgmax of
+scripts/export_hybrid_chunks.py:409-421) against torch.topk over a plain PyTorch fp32 matmul of
+the same bf16 operands: the values agree within fp32 accumulation-order rounding (1e-4 of the
+row scale), and every returned index is a top-k index of the reference up to near-ties (its
+reference logit is within that tolerance of the k-th largest).  Qwen3.5 vocabulary (248,320) at
+hidden 2560 for one row and a batch; a ragged vocabulary and k < 32."""
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from anelm_b200.core import lm_head_topk  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(n, vocab, hidden, k, seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    h = torch.randn(n, hidden, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(vocab, hidden, generator=g, device="cuda") / hidden ** 0.5).to(torch.bfloat16)
+    vals, idx = lm_head_topk(h, w, k)
+    logits = h.float() @ w.float().T
+    want_v, want_i = torch.topk(logits, k, dim=-1)
+    scale = logits.abs().amax(dim=-1, keepdim=True)
+    tol = 1e-4 * scale
+    assert ((vals - want_v).abs() <= tol).all(), float(((vals - want_v).abs() / scale).max())
+    assert (vals[:, :-1] >= vals[:, 1:]).all()          # sorted descending
+    got_logit = logits.gather(1, idx.long())          # the reference logit of every returned index
+    assert (got_logit >= want_v[:, -1:] - tol).all()
+    assert ((got_logit - vals).abs() <= tol).all()
+    assert all(len(set(r.tolist())) == k for r in idx)  # no index twice
+
+
+@pytest.mark.parametrize("n", [1, 64, 256])
+def test_lm_head_top32_qwen_vocab(n):
+    _check(n, 248320, 2560, 32, seed=n)
+
+
+@pytest.mark.parametrize("k", [1, 5, 32])
+def test_lm_head_ragged_vocab(k):
+    _check(3, 1000, 136, k, seed=k)
