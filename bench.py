@@ -13,6 +13,8 @@ each rank owns its own 256 sequences (weak scaling, no data-path collective).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
     python bench.py --workload fa_b1|gdn_b1      # BASELINE configs 1 / 2 (single sequence)
     python bench.py --workload fa_prefill [--prefill-batch 8]
+    python bench.py --workload gdn_prefill
+    python bench.py --workload proj|lm_head [--seqs 256]       # the steps next to the core
 
 The reference arm (--impl reference) times the reference's own CPU attention
 core (core/cpu_ops.cpp compiled unmodified + the qwen3_5.cpp glue, oracle/_ref)
@@ -211,6 +213,8 @@ def run_gpu(args):
         return run_prefill(args, torch, device)
     if args.workload == "gdn_prefill":
         return run_gdn_prefill(args, torch, device, hbm_peak, peak_kind)
+    if args.workload in ("proj", "lm_head"):
+        return run_proj(args, torch, device, hbm_peak, peak_kind)
     if args.workload != "serve":
         return run_gpu_single(args, torch, device, hbm_peak, peak_kind)
 
@@ -534,6 +538,117 @@ def run_gdn_prefill(args, torch, device, hbm_peak, peak_kind):
         "gpu_launches": 3 * args.steps}), flush=True)
 
 
+def run_proj(args, torch, device, hbm_peak, peak_kind):
+    """The steps next to the core (widening beyond the core): "proj" = the in- and out-projection
+    GEMMs of one attention and one DeltaNet decode layer of the Qwen3.5-4B shape for `--seqs` rows
+    (anelm_gemm_bf16); "lm_head" = the in-model top-32 LM head over the 248,320-token vocabulary
+    for `--seqs` rows (anelm_lm_head_topk).  bf16 N(0,1) activations, N(0, 1/hidden) weights."""
+    from anelm_b200.core import gemm_bf16, lm_head_topk
+
+    try:
+        tpeak = float(json.load(open(PEAKS))["bf16_tflops"])
+        tpeak_kind = "measured"
+    except Exception:
+        tpeak, tpeak_kind = 1590.0, "fallback"
+    n, H = args.seqs, 2560
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+
+    def w(rows, cols):
+        return (torch.randn(rows, cols, generator=g, device=device) / cols ** 0.5).to(torch.bfloat16)
+
+    if args.workload == "proj":
+        # attention: q|gate|k|v rows 16*512 + 2*4*256 = 10240, o_proj 2560 x 4096; DeltaNet:
+        # qkv|z|a|b rows 2*16*128 + 2*32*128 + 2*32 = 12352, o_proj 2560 x 4096
+        shapes = [(10240, H), (H, 4096), (12352, H), (H, 4096)]
+        ws = [w(N, K) for N, K in shapes]
+        xs = [torch.randn(n, K, generator=g, device=device).to(torch.bfloat16) for _, K in shapes]
+        ys = [torch.empty(n, N, device=device, dtype=torch.bfloat16) for N, _ in shapes]
+
+        def call():
+            for x, wt, y in zip(xs, ws, ys):
+                gemm_bf16(x, wt, out=y)
+
+        flops = sum(2 * n * N * K for N, K in shapes)
+        nbytes = sum((N * K + n * K + n * N) * 2 for N, K in shapes)
+        metric = "decode-layer projection GEMMs TFLOP/s (Qwen3.5-4B attention + DeltaNet layer, bf16)"
+        kernel, launches = "gemm_bf16_tn_kernel", len(shapes)
+        cfg = {"workload": f"in/out projections of one attention and one DeltaNet layer, {n} rows",
+               "gemms": [f"{n}x{N}x{K}" for N, K in shapes]}
+    else:
+        V = 248320
+        wt = w(V, H)
+        x = torch.randn(n, H, generator=g, device=device).to(torch.bfloat16)
+        wsp = torch.empty(n * V, dtype=torch.uint8, device=device)  # >= the candidate buffer
+
+        def call():
+            lm_head_topk(x, wt, 32, wsp)
+
+        flops, nbytes = 2 * n * V * H, (V * H + n * H) * 2 + n * 32 * 8
+        metric = "LM head with in-model top-32 TFLOP/s (248,320-token vocabulary, hidden 2560, bf16)"
+        kernel, launches = "lm_head_topk_kernel + lm_topk_merge_kernel", 2
+        cfg = {"workload": f"top-32 LM head, {n} rows x 248320 x 2560"}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index or 0)
+    clocks.start()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()  # weights would otherwise stay in L2 between iterations
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        call()
+        t1.record()
+        torch.cuda.synchronize(device)
+        times.append(t0.elapsed_time(t1))
+    ck = clocks.stop()
+    ms = statistics.median(times)
+    tf = flops / (ms * 1e-3) / 1e12
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    bound = "tensor" if flops / nbytes > tpeak * 1e12 / (hbm_peak * 1e9) else "hbm"
+    roof = ({"bound": "tensor", "achieved": round(tf, 2), "peak": tpeak, "unit": "TFLOP/s",
+             "frac": round(tf / tpeak, 4), "peak_kind": tpeak_kind} if bound == "tensor" else
+            {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+             "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind})
+    roof.update({"kernel": kernel, "traffic": None, "algorithmic_flops_per_launch": flops,
+                 "algorithmic_bytes": nbytes})
+    # CPU baseline: numpy (BLAS) on an 8-row sample of the same products (the reference runs them
+    # on the ANE, so there is no reference CPU code for this step)
+    rows = min(8, n)
+    cpu_t = 0.0
+    if not args.no_cpu_baseline:
+        import time
+        xs_c = np.random.default_rng(0).standard_normal((rows, H)).astype(np.float32)
+        if args.workload == "proj":
+            mats = [np.random.default_rng(i).standard_normal((N, K)).astype(np.float32) for i, (N, K) in
+                    enumerate(shapes)]
+            xin = [np.random.default_rng(9).standard_normal((rows, K)).astype(np.float32) for _, K in shapes]
+            t0 = time.perf_counter()
+            for xi, m in zip(xin, mats):
+                xi @ m.T
+            cpu_t = time.perf_counter() - t0
+        else:
+            m = np.random.default_rng(1).standard_normal((V // 8, H)).astype(np.float32)  # 1/8 of the vocabulary
+            t0 = time.perf_counter()
+            lg = xs_c @ m.T
+            np.argpartition(lg, -32, axis=1)[:, -32:]
+            cpu_t = (time.perf_counter() - t0) * 8
+    cpu_tf = (flops * rows / n) / cpu_t / 1e12 if cpu_t > 0 else None
+    print(json.dumps({
+        "metric": metric, "value": round(tf, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 in, fp32 accumulate", "data": "synthetic",
+        "config": dict(cfg, l2="256 MB buffer written between timed iterations"),
+        "hbm_gbs_step": round(gbs, 1), "roofline": roof,
+        "cpu_baseline": {"value": round(cpu_tf, 6) if cpu_tf else None, "unit": "TFLOP/s",
+                         "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"numpy fp32 matmul on {rows} rows" +
+                                   (" of 1/8 of the vocabulary, scaled" if args.workload == "lm_head" else "")},
+        "clocks": ck, "gpu_launches": launches * args.steps}), flush=True)
+
+
 def run_gpu_single(args, torch, device, hbm_peak, peak_kind):
     """BASELINE configs 1 and 2: one sequence, one layer call per step, replayed from a CUDA graph."""
     import anelm_b200 as ab
@@ -714,7 +829,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="anelm", choices=["anelm", "reference"])
-    ap.add_argument("--workload", default="serve", choices=["serve", "fa_b1", "gdn_b1", "fa_prefill", "gdn_prefill"])
+    ap.add_argument("--workload", default="serve",
+                    choices=["serve", "fa_b1", "gdn_b1", "fa_prefill", "gdn_prefill", "proj", "lm_head"])
     ap.add_argument("--gdn-len", type=int, default=8192)
     ap.add_argument("--prefill-batch", type=int, default=1)
     ap.add_argument("--prefill-len", type=int, default=4096)
