@@ -49,6 +49,7 @@ namespace {
 
 constexpr int kDk = 128;
 constexpr int kDv = 128;
+constexpr int kPrefetchItems = 192;  // ~ the (row, key head) items resident at once (5 CTAs per SM)
 
 __device__ __forceinline__ void cluster_arrive_relaxed() {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
@@ -194,6 +195,18 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_ke
     float4 S[NR];
 #pragma unroll
     for (int i = 0; i < NR; i++) S[i] = __ldcs(reinterpret_cast<const float4*>(Sbase + (long long)(rg + RPP * i) * kDv));
+    // L2 prefetch of the state head that the CTA about one resident wave later (kPrefetchItems
+    // (row, key head) items on) will stream: its 64 KB are in L2 when it starts, which adds bytes
+    // in flight beyond what the register-resident blocks hold
+    if (cb == 0 && tid == 0) {
+        const int item2 = item + kPrefetchItems;
+        if (item2 < (int)(gridDim.x / CS)) {
+            const int b2 = item2 / p.Hk, kh2 = item2 % p.Hk;
+            const int seq2 = p.seq_ids ? p.seq_ids[b2] : p.seq_scalar;
+            const float* S2 = p.ssm + ((long long)seq2 * p.Hv + kh2 * RATIO + hl) * kDk * kDv;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(S2), "r"(kDk * kDv * 4) : "memory");
+        }
+    }
 
     int p1 = n + 1;
     if (p1 == 3) p1 = 0;
