@@ -15,6 +15,7 @@ each rank owns its own 256 sequences (weak scaling, no data-path collective).
     python bench.py --workload fa_prefill [--prefill-batch 8]
     python bench.py --workload gdn_prefill
     python bench.py --workload proj|lm_head [--seqs 256]       # the steps next to the core
+    python bench.py --workload gdn_layer [--seqs 256]          # one DeltaNet decode layer (ncu size)
 
 The reference arm (--impl reference) times the reference's own CPU attention
 core (core/cpu_ops.cpp compiled unmodified + the qwen3_5.cpp glue, oracle/_ref)
@@ -215,6 +216,8 @@ def run_gpu(args):
         return run_gdn_prefill(args, torch, device, hbm_peak, peak_kind)
     if args.workload in ("proj", "lm_head"):
         return run_proj(args, torch, device, hbm_peak, peak_kind)
+    if args.workload == "gdn_layer":
+        return run_gdn_layer(args, torch, device, hbm_peak, peak_kind)
     if args.workload != "serve":
         return run_gpu_single(args, torch, device, hbm_peak, peak_kind)
 
@@ -649,6 +652,52 @@ def run_proj(args, torch, device, hbm_peak, peak_kind):
         "clocks": ck, "gpu_launches": launches * args.steps}), flush=True)
 
 
+def run_gdn_layer(args, torch, device, hbm_peak, peak_kind):
+    """One DeltaNet decode layer of the config-5 shape over `--seqs` sequences (the kernel of the
+    serving step on its own, a few hundred MB of state: the size for an ncu capture)."""
+    import anelm_b200 as ab
+    from anelm_b200.core import Context
+
+    n = args.seqs
+    ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_LINEAR_ATTN], lin_num_key_heads=HK,
+                  lin_num_val_heads=HV, max_seqs=n, kv_capacity=16)
+    rng = np.random.default_rng(0)
+    cw = (0.5 * rng.standard_normal((C_CONV, 4))).astype(np.float16).astype(np.float32)
+    ctx.set_deltanet_weights(0, cw, np.ones(HV, np.float32), np.zeros(HV, np.float32),
+                             (1 + 0.1 * rng.standard_normal(DV)).astype(np.float32))
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    st = (0.1 * torch.randn(HV, DK, DV, generator=g, device=device)).contiguous()
+    for s in range(n):
+        ctx.deltanet_state_write(0, s, st)
+    plan = ctx.plan(list(range(n)))
+    proj = torch.randn(n, GDN_PROJ, generator=g, device=device, dtype=torch.float16)
+    out = torch.empty(n, GDN_OUT, device=device, dtype=torch.float16)
+    for _ in range(args.warmup):
+        ctx.deltanet_decode(plan, 0, proj, out=out)
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ctx.deltanet_decode(plan, 0, proj, out=out)
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = step_bytes(np.full(n, 1), 0)[1]              # same accounting as the serving step
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "DeltaNet decode layer GB/s (config-5 shape, one layer)", "value": round(gbs, 1), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"one DeltaNet layer, {n} sequences", "l2": f"state {n * HV * DK * DV * 4 >> 20} MB"},
+        "roofline": {"bound": "hbm", "kernel": "gdn_decode_kernel", "achieved": round(gbs, 1), "peak": hbm_peak,
+                     "unit": "GB/s", "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": nbytes},
+        "gpu_launches": args.steps}), flush=True)
+    plan.close()
+    ctx.close()
+
+
 def run_gpu_single(args, torch, device, hbm_peak, peak_kind):
     """BASELINE configs 1 and 2: one sequence, one layer call per step, replayed from a CUDA graph."""
     import anelm_b200 as ab
@@ -830,7 +879,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="anelm", choices=["anelm", "reference"])
     ap.add_argument("--workload", default="serve",
-                    choices=["serve", "fa_b1", "gdn_b1", "fa_prefill", "gdn_prefill", "proj", "lm_head"])
+                    choices=["serve", "fa_b1", "gdn_b1", "fa_prefill", "gdn_prefill", "proj", "lm_head",
+                             "gdn_layer"])
     ap.add_argument("--gdn-len", type=int, default=8192)
     ap.add_argument("--prefill-batch", type=int, default=1)
     ap.add_argument("--prefill-len", type=int, default=4096)
