@@ -13,8 +13,8 @@
 //                           [B][Hkv][n_pad][D], sigmoid(gate) for the epilogue, and the ring
 //                           append (slot t, len = n, start = 0).  Warp per 256-element segment,
 //                           16-byte lanes (fa_prefill_prep_kernel: same work for any shape);
-//   fa_prefill_kernel       one CTA per (128-row query tile, q head, sequence), longest causal
-//                           tiles first, 11 warps:
+//   fa_prefill_kernel       one CTA per (q head, 128-row query tile, sequence); within a sequence
+//                           all heads' longest causal tiles are dispatched first; 11 warps:
 //     warps 0-7  softmax: warps w and w+4 share TMEM lanes [32(w%4), +32) and take keys
 //             [0, 64) / [64, 128) of each 128-key S tile; tcgen05.ld of the S row, causal mask,
 //             row max exchanged through shared memory (pairwise named barriers), lazy rescale
@@ -461,8 +461,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n_qt = p.n_pad / kBM;
-    const int qt = n_qt - 1 - (int)blockIdx.x;  // longest (causal) tiles first
-    const int h = blockIdx.y, b = blockIdx.z;
+    // CTAs are dispatched in blockIdx order (x fastest): within a sequence, every head's longest
+    // causal tile goes out before any shorter one (longest-processing-time-first packing onto the SMs)
+    const int qt = n_qt - 1 - (int)blockIdx.y;
+    const int h = blockIdx.x, b = blockIdx.z;
     const int G = p.Hq / p.Hkv;
     const int kvh = h / G;
     const int q0 = qt * kBM;
@@ -829,7 +831,7 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
         fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
     }
     cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    fa_prefill_kernel<<<dim3(p.n_pad / kBM, p.Hq, p.B), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
+    fa_prefill_kernel<<<dim3(p.Hq, p.n_pad / kBM, p.B), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 

@@ -109,6 +109,29 @@ def test_prefill_matches_oracle_with_padding_and_decode_after(out_dtype):
         assert_close(k[:ring.len], ring.k[:ring.len], atol=2e-3, rtol=2e-3, what="K ring after prefill")
 
 
+@pytest.mark.parametrize("n,out_dtype", [(520, "float32"), (700, "bfloat16"), (256, "float16")])
+def test_prefill_ragged_query_tiles(n, out_dtype):
+    """Several 128-row query tiles per head with a ragged last one: n = 520 leaves the last tile 8
+    rows, n = 700 leaves it 60, n = 256 fills two tiles exactly; tiles are dispatched longest first
+    across heads and sequences (B = 2).  Row-store (fp32) and TMA tile-store (16-bit) epilogues,
+    against the fp32 PyTorch restatement."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(n)
+    rng = np.random.default_rng(n)
+    B = 2
+    qn, kn = weights(rng)
+    proj = bf16_proj(gen, B, n)
+    rope = po.rope_table(4096, R, 1e7)
+    with ctx_for(B, n) as ctx:
+        ctx.set_full_attn_weights(0, qn, kn)
+        plan = ctx.plan([0, 1])
+        out = ctx.full_attn_prefill(plan, 0, proj, start_pos=0, out_dtype=getattr(torch, out_dtype))
+        torch.cuda.synchronize()
+        plan.close()
+    want = torch_reference(proj, qn, kn, 0, rope)
+    assert_close(out.float().cpu().numpy(), want.cpu().numpy(), what=f"prefill n={n}")
+
+
 @pytest.mark.parametrize("B,out_dtype", [(1, "float32"), (8, "bfloat16")])
 def test_prefill_config3_full_size(B, out_dtype):
     """Qwen3.5-4B shape, seq 4096, bf16 inputs N(0,1)."""
