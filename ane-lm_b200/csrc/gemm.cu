@@ -44,7 +44,8 @@ constexpr int kGBM = 128, kGBN = 256, kGBK = 64, kGStages = 4;
 constexpr int kGThreads = 192;
 constexpr int kGTileA = kGBM * kGBK * 2;  // 16 KB: 128 rows x 128 bytes
 constexpr int kGTileB = kGBN * kGBK * 2;  // 32 KB: 256 rows x 128 bytes
-constexpr int kGSmem = kGStages * (kGTileA + kGTileB) + 256 + 1024;
+constexpr int kGMaxStages = 8;         // projection GEMM: stages in flight for narrow B tiles
+constexpr int kGSmemMax = 227 * 1024;  // dynamic shared memory per CTA
 constexpr int kGPartPitch = kGBN + 4;  // fp32 words per row of a parked split-K partial
 // LM head: stage ring, barriers, and a [128][33] fp32 chunk staging area for the epilogue
 constexpr int kLmSmem = kGStages * (kGTileA + kGTileB) + 256 + 128 * 33 * 4 + 1024;
@@ -72,29 +73,36 @@ __device__ __forceinline__ void topk_insert(float (&tv)[kTopK], int (&ti)[kTopK]
     }
 }
 
+// kNarrow: tile width bn and stage count nst as given (one partial wave of narrower tiles);
+// otherwise the compile-time 256 columns and kGStages stages.
+template <bool kNarrow>
 __global__ void __launch_bounds__(kGThreads, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C,
-                        long long ldc, int c_dtype, int M, int N, int K, int ks, int* err) {
+                        long long ldc, int c_dtype, int M, int N, int K, int ks, int bn_arg, int nst_arg, int* err) {
+    // nst stages of [A 128 x 64 | B bn x 64] (narrower B tiles leave room for more stages in flight)
+    const int bn = kNarrow ? bn_arg : kGBN;
+    const int nst = kNarrow ? nst_arg : kGStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tileB = bn * kGBK * 2;
     uint8_t* sA = smem;
-    uint8_t* sB = smem + kGStages * kGTileA;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kGStages * kGTileB);
-    uint64_t* empty = full + kGStages;
-    uint64_t* done = empty + kGStages;
+    uint8_t* sB = smem + nst * kGTileA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + nst * tileB);
+    uint64_t* empty = full + kGMaxStages;
+    uint64_t* done = empty + kGMaxStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // ks > 1: blockIdx.x = tile * ks + split, the ks CTAs of a tile form one cluster
     const int split = blockIdx.x % ks;
-    const int n0 = (blockIdx.x / ks) * kGBN, m0 = blockIdx.y * kGBM;
+    const int n0 = (blockIdx.x / ks) * bn, m0 = blockIdx.y * kGBM;
     const int nk_all = (K + kGBK - 1) / kGBK;
     const int per = (nk_all + ks - 1) / ks;
     const int kt0 = split * per;
     const int nk = max(0, min(nk_all, kt0 + per) - kt0);  // this CTA's k-tiles
     if (tid == 0) {
         *abort = 0;
-        for (int s = 0; s < kGStages; s++) {
+        for (int s = 0; s < nst; s++) {
             tc::mbar_init(&full[s], 1);
             tc::mbar_init(&empty[s], 1);
         }
@@ -102,7 +110,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
         tc::fence_barrier_init();
     }
     if (warp == 0) {
-        tc::tmem_alloc(tmem_slot, kGBN);
+        tc::tmem_alloc(tmem_slot, kGBN);  // bn <= 256 columns used
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
@@ -114,31 +122,35 @@ __global__ void __launch_bounds__(kGThreads, 1)
         if (lane == 0) {  // TMA producer
             tc::prefetch_tmap(&tmA);
             tc::prefetch_tmap(&tmB);
-            for (int kt = 0; kt < nk; kt++) {
-                const int s = kt % kGStages;
-                if (kt >= kGStages &&
-                    !tc::mbar_wait(&empty[s], (uint32_t)((kt / kGStages) - 1) & 1, err, ANELM_ERR_TIMEOUT, abort))
-                    break;
-                tc::mbar_arrive_expect_tx(&full[s], kGTileA + kGTileB);
+            // stage s and its use count u (kt = u * nst + s), stepped without division
+            for (int kt = 0, s = 0, u = 0; kt < nk; kt++) {
+                if (u > 0 && !tc::mbar_wait(&empty[s], (uint32_t)(u - 1) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
+                tc::mbar_arrive_expect_tx(&full[s], kGTileA + tileB);
                 tc::tma_load_2d(sA + s * kGTileA, &tmA, &full[s], (kt0 + kt) * kGBK, m0);
-                tc::tma_load_2d(sB + s * kGTileB, &tmB, &full[s], (kt0 + kt) * kGBK, n0);
+                tc::tma_load_2d(sB + s * tileB, &tmB, &full[s], (kt0 + kt) * kGBK, n0);
+                if (++s == nst) {
+                    s = 0;
+                    u++;
+                }
             }
         }
         __syncwarp();
     } else if (warp == 5) {
         if (lane == 0) {  // MMA issuer
-            constexpr uint32_t idesc = idesc_bf16_f32(kGBM, kGBN);
+            const uint32_t idesc = idesc_bf16_f32(kGBM, bn);
             const uint32_t aA = (uint32_t)__cvta_generic_to_shared(sA), aB = (uint32_t)__cvta_generic_to_shared(sB);
-            int kt = 0;
-            for (; kt < nk; kt++) {
-                const int s = kt % kGStages;
-                if (!tc::mbar_wait(&full[s], (uint32_t)(kt / kGStages) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
+            for (int kt = 0, s = 0, u = 0; kt < nk; kt++) {
+                if (!tc::mbar_wait(&full[s], (uint32_t)u & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
                 tc::tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < kGBK / 16; ks++)
                     tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(aA + s * kGTileA + ks * 32),
-                                   tc::desc_kmajor_sw128(aB + s * kGTileB + ks * 32), idesc, (kt | ks) != 0);
+                                   tc::desc_kmajor_sw128(aB + s * tileB + ks * 32), idesc, (kt | ks) != 0);
                 tc::mma_commit(&empty[s]);
+                if (++s == nst) {
+                    s = 0;
+                    u++;
+                }
             }
             tc::mma_commit(done);  // all MMAs issued (an aborted loop still completes `done`)
         }
@@ -152,12 +164,14 @@ __global__ void __launch_bounds__(kGThreads, 1)
         if (ks > 1) {  // park this split's partial (zeros for an empty K range) in the stage buffers
             float* part = reinterpret_cast<float*>(smem) + (32 * warp + lane) * kGPartPitch;
 #pragma unroll 1
-            for (int c0 = 0; c0 < kGBN; c0 += 32) {
+            for (int c0 = 0; c0 < bn; c0 += 32) {
                 uint32_t x[32];
-                tc::tmem_ld32(trow + c0, x);
+                const int w = kNarrow ? min(32, bn - c0) : 32;  // 32, or 16 for the last chunk of a bn = 16 (mod 32)
+                if (w == 32) tc::tmem_ld32(trow + c0, x); else tc::tmem_ld16(trow + c0, x);
                 tc::tmem_ld_wait();
 #pragma unroll
                 for (int c4 = 0; c4 < 8; c4++)
+                    if (c4 < w / 4)
                     *reinterpret_cast<float4*>(part + c0 + 4 * c4) =
                         nk > 0 ? make_float4(__uint_as_float(x[4 * c4]), __uint_as_float(x[4 * c4 + 1]),
                                              __uint_as_float(x[4 * c4 + 2]), __uint_as_float(x[4 * c4 + 3]))
@@ -165,16 +179,18 @@ __global__ void __launch_bounds__(kGThreads, 1)
             }
         }
 #pragma unroll 1
-        for (int c0 = 0; c0 < (ks > 1 ? 0 : kGBN); c0 += 32) {
+        for (int c0 = 0; c0 < (ks > 1 ? 0 : bn); c0 += 32) {
             uint32_t x[32];
-            tc::tmem_ld32(trow + c0, x);
+            const int w = kNarrow ? min(32, bn - c0) : 32;
+            if (w == 32) tc::tmem_ld32(trow + c0, x); else tc::tmem_ld16(trow + c0, x);
             tc::tmem_ld_wait();
             if (!ok || m >= M) continue;
             const int nb = n0 + c0;
-            if (nb + 32 <= N && c_dtype != ANELM_F32 && (ldc % 8) == 0 && ((uintptr_t)C % 16) == 0) {
+            if (nb + w <= N && c_dtype != ANELM_F32 && (ldc % 8) == 0 && ((uintptr_t)C % 16) == 0) {
                 uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(C) + (long long)m * ldc + nb);
 #pragma unroll
                 for (int c8 = 0; c8 < 4; c8++) {
+                    if (c8 >= w / 8) break;
                     float v[8];
 #pragma unroll
                     for (int e = 0; e < 8; e++) v[e] = __uint_as_float(x[8 * c8 + e]);
@@ -183,7 +199,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
             } else {
 #pragma unroll
                 for (int c = 0; c < 32; c++)
-                    if (nb + c < N) store_from_float(C, c_dtype, (long long)m * ldc + nb + c, __uint_as_float(x[c]));
+                    if (c < w && nb + c < N) store_from_float(C, c_dtype, (long long)m * ldc + nb + c, __uint_as_float(x[c]));
             }
         }
     }
@@ -195,8 +211,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
         const int R = (kGBM + ks - 1) / ks;
         const int r0 = split * R, r1 = min(kGBM, r0 + R);
         const float* part0 = reinterpret_cast<const float*>(smem);
-        for (int i = tid; i < (r1 - r0) * (kGBN / 4); i += kGThreads) {
-            const int r = r0 + i / (kGBN / 4), c = 4 * (i % (kGBN / 4));
+        for (int i = tid; i < (r1 - r0) * (bn / 4); i += kGThreads) {
+            const int r = r0 + i / (bn / 4), c = 4 * (i % (bn / 4));
             const int m = m0 + r, n = n0 + c;
             float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int q = 0; q < ks; q++) {
@@ -219,6 +235,78 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
 }
 
+// Few-row products (M <= kGvMaxM): C[m][n] = sum_k A[m][k] B[n][k] on the CUDA cores.  A 128-row
+// tensor-core tile would be almost all padding; the cost is streaming B (the weights) from HBM.
+// The M rows of A are staged in shared memory (bf16); each warp takes kGvRows rows of B and keeps
+// kGvUnroll 16-byte loads per row in flight, fp32 accumulation, one warp reduction per output.
+constexpr int kGvRows = 2, kGvUnroll = 4, kGvThreads = 256, kGvMaxM = 4;
+
+__device__ __forceinline__ uint4 ld_stream16(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__global__ void __launch_bounds__(kGvThreads) gemv_bf16_kernel(const __nv_bfloat16* A, long long lda,
+                                                               const __nv_bfloat16* B, long long ldb, void* C,
+                                                               long long ldc, int c_dtype, int M, int N, int K) {
+    extern __shared__ uint4 xs[];  // [M][K / 8]
+    const int kc = K / 8;
+    for (int i = threadIdx.x; i < M * kc; i += kGvThreads) {
+        const int m = i / kc, c = i - m * kc;
+        xs[i] = *reinterpret_cast<const uint4*>(A + (long long)m * lda + (long long)c * 8);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = (blockIdx.x * (kGvThreads / 32) + warp) * kGvRows;
+    if (n0 >= N) return;
+    const uint4* brow[kGvRows];
+#pragma unroll
+    for (int r = 0; r < kGvRows; r++)
+        brow[r] = reinterpret_cast<const uint4*>(B + (long long)min(n0 + r, N - 1) * ldb);
+    float acc[kGvRows][kGvMaxM];
+#pragma unroll
+    for (int r = 0; r < kGvRows; r++)
+#pragma unroll
+        for (int m = 0; m < kGvMaxM; m++) acc[r][m] = 0.f;
+    for (int c0 = lane; c0 < kc; c0 += 32 * kGvUnroll) {
+        uint4 w[kGvRows][kGvUnroll];
+#pragma unroll
+        for (int u = 0; u < kGvUnroll; u++)
+#pragma unroll
+            for (int r = 0; r < kGvRows; r++)
+                w[r][u] = (c0 + 32 * u < kc) ? ld_stream16(brow[r] + c0 + 32 * u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < kGvUnroll; u++) {
+            const int c = c0 + 32 * u;
+            if (c >= kc) break;
+            float wf[kGvRows][8];
+#pragma unroll
+            for (int r = 0; r < kGvRows; r++) unpack8(w[r][u], true, wf[r]);
+#pragma unroll
+            for (int m = 0; m < kGvMaxM; m++) {
+                if (m >= M) break;
+                float xf[8];
+                unpack8(xs[m * kc + c], true, xf);
+#pragma unroll
+                for (int r = 0; r < kGvRows; r++)
+#pragma unroll
+                    for (int e = 0; e < 8; e++) acc[r][m] = fmaf(wf[r][e], xf[e], acc[r][m]);
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kGvRows; r++)
+#pragma unroll
+        for (int m = 0; m < kGvMaxM; m++) {
+            if (m >= M) break;
+            const float s = warp_sum(acc[r][m]);
+            if (lane == 0 && n0 + r < N) store_from_float(C, c_dtype, (long long)m * ldc + n0 + r, s);
+        }
+}
+
 // 2D bf16 tensor map over a row-major [rows][cols] matrix (row stride ld elements), box {64, box_rows}
 bool make_bf16_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
     auto fn = tc::tmap_encode_fn();
@@ -239,16 +327,48 @@ int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long l
     if (M <= 0 || N <= 0 || K <= 0) return ANELM_ERR_INVALID_ARG;
     if ((uintptr_t)A % 16 || (uintptr_t)B % 16 || (lda * 2) % 16 || (ldb * 2) % 16 || lda < K || ldb < K || ldc < N)
         return ANELM_ERR_UNSUPPORTED;
-    CUtensorMap mA, mB;
-    if (!make_bf16_map(&mA, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, kGBM) ||
-        !make_bf16_map(&mB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, kGBN))
-        return ANELM_ERR_CUDA;
-    cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem);
-    const int tiles = ((N + kGBN - 1) / kGBN) * ((M + kGBM - 1) / kGBM);
+    if (M <= kGvMaxM && K % 8 == 0 && (size_t)M * K * 2 <= 160 * 1024) {
+        // few rows: stream the weights on the CUDA cores
+        const int smem = M * K * 2;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        const int rows_per_block = kGvRows * (kGvThreads / 32);
+        gemv_bf16_kernel<<<(N + rows_per_block - 1) / rows_per_block, kGvThreads, smem, stream>>>(
+            static_cast<const __nv_bfloat16*>(A), lda, static_cast<const __nv_bfloat16*>(B), ldb, C, ldc, c_dtype, M,
+            N, K);
+        return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
+    }
+    const int mt = (M + kGBM - 1) / kGBM;
+    const int tiles = ((N + kGBN - 1) / kGBN) * mt;
     const int nk = (K + kGBK - 1) / kGBK;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // tile width: when the 256-wide tiles make one partial wave (half the SMs to all of them), the
+    // width in [128, 256] (step 16) with the fewest columns per SM (waves x width): e.g. M = 256,
+    // N = 10240 takes 144 tiles of 144 columns instead of 80 tiles of 256; fewer tiles than that
+    // split K instead (below); several waves keep 256
+    int bn = kGBN;
+    if (2 * tiles >= sms && tiles <= sms) {
+        long long best = -1;
+        for (int b = kGBN; b >= 128; b -= 16) {
+            const long long t = (long long)mt * ((N + b - 1) / b);
+            const long long cost = ((t + sms - 1) / sms) * b;
+            if (best < 0 || cost < best) {
+                best = cost;
+                bn = b;
+            }
+        }
+    }
+    // narrower tiles: as many stages as shared memory holds (at most kGMaxStages)
+    const int nst = bn == kGBN ? kGStages
+                               : std::min(kGMaxStages, (kGSmemMax - 1280) / (kGTileA + bn * kGBK * 2));
+    const int smem = nst * (kGTileA + bn * kGBK * 2) + 256 + 1024;  // + barriers, alignment
+    auto kern = bn == kGBN ? gemm_bf16_tn_kernel<false> : gemm_bf16_tn_kernel<true>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    CUtensorMap mA, mB;
+    if (!make_bf16_map(&mA, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, kGBM) ||
+        !make_bf16_map(&mB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)bn))
+        return ANELM_ERR_CUDA;
     // split K over a cluster when the tiles fill less than half of the SMs: the largest cluster
     // size (<= 8) of which the GPU can hold one cluster per tile at once (GPC packing caps it below
     // the SM count / tiles), measured once per device and size
@@ -256,7 +376,7 @@ int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long l
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     cfg.blockDim = dim3(kGThreads);
-    cfg.dynamicSmemBytes = kGSmem;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.y = 1;
@@ -270,7 +390,7 @@ int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long l
             if (a == 0) {
                 cfg.gridDim = dim3(c, 1);
                 attr[0].val.clusterDim.x = c;
-                if (cudaOccupancyMaxActiveClusters(&a, (void*)gemm_bf16_tn_kernel, &cfg) != cudaSuccess || a <= 0) {
+                if (cudaOccupancyMaxActiveClusters(&a, (void*)kern, &cfg) != cudaSuccess || a <= 0) {
                     cudaGetLastError();
                     a = -1;
                 }
@@ -282,12 +402,12 @@ int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long l
     if (ks > 1) {
         cfg.gridDim = dim3(((N + kGBN - 1) / kGBN) * ks, (M + kGBM - 1) / kGBM);
         attr[0].val.clusterDim.x = ks;
-        if (cudaLaunchKernelEx(&cfg, gemm_bf16_tn_kernel, mA, mB, C, ldc, c_dtype, M, N, K, ks, err) == cudaSuccess)
+        if (cudaLaunchKernelEx(&cfg, kern, mA, mB, C, ldc, c_dtype, M, N, K, ks, bn, nst, err) == cudaSuccess)
             return ANELM_OK;
         cudaGetLastError();  // a cluster that cannot be placed: one CTA per tile instead
     }
-    dim3 grid((N + kGBN - 1) / kGBN, (M + kGBM - 1) / kGBM);
-    gemm_bf16_tn_kernel<<<grid, kGThreads, kGSmem, stream>>>(mA, mB, C, ldc, c_dtype, M, N, K, 1, err);
+    dim3 grid((N + bn - 1) / bn, mt);
+    kern<<<grid, kGThreads, smem, stream>>>(mA, mB, C, ldc, c_dtype, M, N, K, 1, bn, nst, err);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 

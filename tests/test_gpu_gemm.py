@@ -34,6 +34,23 @@ def test_gemm_projection_shapes(M, N, K):
 
 
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(1, 12352, 2560), (4, 10240, 2560), (2, 2561, 4096), (3, 17, 8)])
+def test_gemm_few_rows(M, N, K, out_dtype):
+    """1-4 rows take the CUDA-core path that streams the weights (single-sequence layer steps):
+    decode shapes, an odd row count N, and a K of one 16-byte chunk."""
+    _check(M, N, K, out_dtype, seed=M * N)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(256, 12352, 2560), (256, 10240, 2560), (1024, 5000, 256)])
+def test_gemm_narrow_tiles(M, N, K, out_dtype):
+    """Shapes whose 256-wide tiles would leave SMs idle take narrower tiles: DeltaNet in-projection
+    (12352 rows: 176-wide tiles, a 16-column TMEM tail and a ragged last tile), full-attention
+    in-projection (144-wide), and a 1024 x 5000 case; fp32 and 16-bit (vector-store tail) outputs."""
+    _check(M, N, K, out_dtype, seed=N)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("M,N,K", [(77, 200, 136), (130, 129, 72), (3, 64, 40)])
 def test_gemm_ragged(M, N, K, out_dtype):
     _check(M, N, K, out_dtype, seed=M + N + K)
