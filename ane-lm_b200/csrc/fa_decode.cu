@@ -90,7 +90,8 @@ __device__ __forceinline__ void set_err(int* err, int code) {
 // cluster barrier keeps every CTA resident until its peers have read it.
 template <int D>
 __device__ __forceinline__ void cluster_merge(const FaDecodeParams& p, uint8_t* smem, const float* po, int b, int kvh,
-                                              int G, int seq, const char* proj_row, int len1, int start1) {
+                                              int G, int seq, const char* proj_row, int len1, int start1,
+                                              const float (&gate4)[4]) {
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -141,9 +142,10 @@ __device__ __forceinline__ void cluster_merge(const FaDecodeParams& p, uint8_t* 
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 float O = (L > 0.f) ? ov[e] / L : 0.f;
-                if (p.gate) {  // mul_sigmoid_inplace, core/cpu_ops.cpp:15-22
-                    const float z = load_as_float(proj_row, p.proj_dtype,
-                                                  p.gate_off + (long long)h * p.q_head_stride + col + e);
+                if (p.gate) {  // mul_sigmoid_inplace, core/cpu_ops.cpp:15-22 (first item: prefetched)
+                    const float z = base == i0 ? gate4[e]
+                                               : load_as_float(proj_row, p.proj_dtype,
+                                                               p.gate_off + (long long)h * p.q_head_stride + col + e);
                     O = O / (1.0f + expf(-z));
                 }
                 store_from_float(p.out, p.out_dtype, (long long)b * p.out_stride + (long long)h * D + col + e, O);
@@ -174,7 +176,8 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int blk = blockIdx.x, kvh = blockIdx.y;
-    const int b = p.blk_b[blk], split = p.blk_split[blk];
+    // the cluster-merge form serves a one-row plan with one CTA per split: no table lookup
+    const int b = CM ? 0 : p.blk_b[blk], split = CM ? blk : p.blk_split[blk];
     const int Hkv = p.Hkv;
     const int G = p.Hq / Hkv;
     const int seq = p.seq_ids ? p.seq_ids[b] : 0;
@@ -193,6 +196,38 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
     if (has_k) load8(proj_row, p.proj_dtype, p.k_off + (long long)kvh * D + tid * 8, kv8);
     if (has_v) load8(proj_row, p.proj_dtype, p.v_off + (long long)kvh * D + (tid - CPR) * 8, kv8);
 
+    // ---- per-thread constants of the prologue and the merge, loaded now so their latency overlaps
+    // the projection loads: the QK-norm weights of this lane's elements, the RoPE angle of the pair
+    // this thread rotates (the same pair index for every vector when the thread count is a
+    // multiple of the half rotary width), and, for the cluster merge, the gate values of the first
+    // output columns this thread merges ----
+    const int pos = p.pos_arr ? p.pos_arr[b] : p.pos_scalar;
+    constexpr int NW = D / 32;
+    float wq[NW], wk[NW];
+    if (p.qk_norm) {
+#pragma unroll
+        for (int m = 0; m < NW; m++) {
+            wq[m] = p.q_norm[lane + 32 * m];
+            wk[m] = p.k_norm[lane + 32 * m];
+        }
+    }
+    const int rhalf = p.rot_dim >> 1;
+    const bool rope_pre = rhalf > 0 && kThreads % rhalf == 0;
+    float rc = 1.f, rs = 0.f;
+    if (rope_pre) rope_cs(p, pos, tid % rhalf, rc, rs);
+    float gate4[4] = {0.f, 0.f, 0.f, 0.f};
+    if (CM && p.gate && (tid & 7) == 0) {
+        const int ns = p.cluster_ns, nitem = G * D / 4, per = (nitem + ns - 1) / ns;
+        const int it = blk * per + (tid >> 3);
+        if (it < min(nitem, blk * per + per)) {
+            const int g = (it * 4) / D, col = it * 4 - g * D;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                gate4[e] = load_as_float(proj_row, p.proj_dtype,
+                                         p.gate_off + (long long)(kvh * G + g) * p.q_head_stride + col + e);
+        }
+    }
+
     // ---- ring metadata (models/llm/qwen3_5.cpp:973-983) ----
     int cap, len0, start0;
     long long base;
@@ -207,7 +242,6 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
         start0 = p.start_s;
         base = 0;
     }
-    const int pos = p.pos_arr ? p.pos_arr[b] : p.pos_scalar;
     int len1 = len0, start1 = start0, slot = -1;
     if (p.append) {
         if (p.kv_mode == ANELM_KV_LINEAR) {  // scripts/serve_hybrid.py:105-108
@@ -309,12 +343,13 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
         if (p.qk_norm) {  // rmsnorm, core/cpu_ops.cpp:24-30
             for (int vec = warp; vec < nvec; vec += kWarps) {
                 float* x = vec < G ? q_s + vec * D : kf_s;
-                const float* w = vec < G ? p.q_norm : p.k_norm;
                 float ss = 0.f;
                 for (int i = lane; i < D; i += 32) ss += x[i] * x[i];
                 ss = warp_sum(ss);
                 const float r = 1.0f / sqrtf(ss / (float)D + p.rms_eps);
-                for (int i = lane; i < D; i += 32) x[i] = __fmul_rn(__fmul_rn(x[i], r), w[i]);
+#pragma unroll
+                for (int m = 0; m < NW; m++)
+                    x[lane + 32 * m] = __fmul_rn(__fmul_rn(x[lane + 32 * m], r), vec < G ? wq[m] : wk[m]);
             }
             __syncthreads();
         }
@@ -323,8 +358,8 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
             for (int idx = tid; idx < nvec * half; idx += kThreads) {
                 int vec = idx / half, j = idx - vec * half;
                 float* x = vec < G ? q_s + vec * D : kf_s;
-                float c, s;
-                rope_cs(p, pos, j, c, s);
+                float c = rc, s = rs;
+                if (!rope_pre) rope_cs(p, pos, j, c, s);
                 int i0, i1;
                 if (p.rope_mode == ANELM_ROPE_INTERLEAVED) {
                     i0 = 2 * j;
@@ -531,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
         }
     }
     if constexpr (CM) {
-        cluster_merge<D>(p, smem, po, b, kvh, G, seq, proj_row, len1, start1);
+        cluster_merge<D>(p, smem, po, b, kvh, G, seq, proj_row, len1, start1, gate4);
         return;
     }
     __threadfence();
