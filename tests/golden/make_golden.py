@@ -1,6 +1,6 @@
 """Generates the golden fixtures in tests/golden/ from the REFERENCE itself.
 
-Run in a container that has the reference sources (default /root/reference) and
+Run where the reference sources are present (--ref, or ANELM_REFERENCE) and
 after ``make -C oracle`` has built oracle/_ref/libref_core.so from the
 reference's unmodified core/cpu_ops.cpp:
 
