@@ -237,8 +237,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
 
 // Few-row products (M <= kGvMaxM): C[m][n] = sum_k A[m][k] B[n][k] on the CUDA cores.  A 128-row
 // tensor-core tile would be almost all padding; the cost is streaming B (the weights) from HBM.
-// The M rows of A are staged in shared memory (bf16); each warp takes kGvRows rows of B and keeps
-// kGvUnroll 16-byte loads per row in flight, fp32 accumulation, one warp reduction per output.
+// The M rows of A are staged in shared memory (bf16); each warp walks groups of kGvRows rows of B
+// (grid-stride over all warps of a grid sized to the resident capacity, so no partial last
+// wave), kGvUnroll 16-byte loads per row in flight, fp32 accumulation, one warp reduction per output.
 constexpr int kGvRows = 2, kGvUnroll = 4, kGvThreads = 256, kGvMaxM = 4;
 
 __device__ __forceinline__ uint4 ld_stream16(const uint4* p) {
@@ -260,8 +261,8 @@ __global__ void __launch_bounds__(kGvThreads) gemv_bf16_kernel(const __nv_bfloat
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = (blockIdx.x * (kGvThreads / 32) + warp) * kGvRows;
-    if (n0 >= N) return;
+    const int nwarps = gridDim.x * (kGvThreads / 32);
+    for (int n0 = (blockIdx.x * (kGvThreads / 32) + warp) * kGvRows; n0 < N; n0 += nwarps * kGvRows) {
     const uint4* brow[kGvRows];
 #pragma unroll
     for (int r = 0; r < kGvRows; r++)
@@ -305,6 +306,7 @@ __global__ void __launch_bounds__(kGvThreads) gemv_bf16_kernel(const __nv_bfloat
             const float s = warp_sum(acc[r][m]);
             if (lane == 0 && n0 + r < N) store_from_float(C, c_dtype, (long long)m * ldc + n0 + r, s);
         }
+    }
 }
 
 // 2D bf16 tensor map over a row-major [rows][cols] matrix (row stride ld elements), box {64, box_rows}
@@ -332,7 +334,16 @@ int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long l
         const int smem = M * K * 2;
         if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         const int rows_per_block = kGvRows * (kGvThreads / 32);
-        gemv_bf16_kernel<<<(N + rows_per_block - 1) / rows_per_block, kGvThreads, smem, stream>>>(
+        int dev = 0, sms = 148, per_sm = 1;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_bf16_kernel, kGvThreads, smem) != cudaSuccess ||
+            per_sm < 1) {
+            cudaGetLastError();
+            per_sm = 1;
+        }
+        const int blocks = std::min((N + rows_per_block - 1) / rows_per_block, sms * per_sm);
+        gemv_bf16_kernel<<<blocks, kGvThreads, smem, stream>>>(
             static_cast<const __nv_bfloat16*>(A), lda, static_cast<const __nv_bfloat16*>(B), ldb, C, ldc, c_dtype, M,
             N, K);
         return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
