@@ -419,13 +419,18 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
         }
     }
     __syncthreads();
-#pragma unroll 1
+    // d and the block index j unrolled: every trip count is a constant, so each thread's shared-memory
+    // loads of a phase issue together instead of one dependent round trip per k-step
+#pragma unroll
     for (int d = 1; d < 4; d++) {
         const int nb = 4 - d;  // blocks (j + d, j), j = 0 .. nb - 1
-        for (int e = tid; e < nb * 256; e += kChunkThreads) {
+#pragma unroll
+        for (int jb = 0; jb < nb; jb++) {
+            const int e = jb * 256 + tid;
             const int j = e >> 8, i = j + d, r = (e >> 4) & 15, c = e & 15;
             const float* arow = &sm.inv.a[16 * i + r][16 * j];
             float s0 = 0.f, s1 = 0.f;
+#pragma unroll
             for (int k = 0; k < 16 * d; k += 4) {
                 const float4 a4 = *reinterpret_cast<const float4*>(arow + k);
                 s0 = fmaf(a4.x, sm.inv.tm[16 * j + k][16 * j + c], s0);
@@ -436,7 +441,9 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
             sm.inv.z[j][r][c] = s0 + s1;
         }
         __syncthreads();
-        for (int e = tid; e < nb * 256; e += kChunkThreads) {
+#pragma unroll
+        for (int jb = 0; jb < nb; jb++) {
+            const int e = jb * 256 + tid;
             const int j = e >> 8, i = j + d, r = (e >> 4) & 15, c = e & 15;
             const float* trow = &sm.inv.tm[16 * i + r][16 * i];
             float s0 = 0.f, s1 = 0.f;
@@ -497,11 +504,13 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
         const bool is_w = r < kC;
         const int t = is_w ? r : r - kC;
         const uint32_t col0 = (is_w ? 0 : 64) + 128 * hc;
+        uint32_t xx[2][32];  // both 32-column loads in flight before the one wait
+        tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + col0, xx[0]);
+        tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + col0 + 32, xx[1]);
+        tc::tmem_ld_wait();
 #pragma unroll
         for (int h32 = 0; h32 < 2; h32++) {
-            uint32_t x[32];
-            tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + col0 + 32 * h32, x);
-            tc::tmem_ld_wait();
+            const uint32_t (&x)[32] = xx[h32];
             const int d0 = 64 * hc + 32 * h32;
             if (is_w) {
                 __half* whi = p.wh + (vrow + t) * kDk + d0;
