@@ -99,6 +99,19 @@ __device__ __forceinline__ void cluster_merge(const FaDecodeParams& p, uint8_t* 
     __shared__ float s_w[16][kGP];  // merge weight of split r for head g
     __shared__ float s_L[kGP];
     cl.sync();  // every split's partial is in its shared memory
+    // every CTA of this kv head is past its reads of the ring metadata: count the kv head now (the
+    // last of the row's kv heads updates len / start), overlapping the merge below
+    if (rank == 0 && tid == 0) {
+        __threadfence();  // this CTA's ring append is visible before it is counted
+        const int prev = atomicAdd(&p.cnt_seq[b], 1);
+        if (prev == p.Hkv - 1) {
+            if (p.append && p.kv_len) {
+                p.kv_len[seq] = len1;
+                p.kv_start[seq] = start1;
+            }
+            p.cnt_seq[b] = 0;
+        }
+    }
     if (warp < G) {
         const int g = warp;
         float m = -INFINITY, l = 0.f;
@@ -153,17 +166,6 @@ __device__ __forceinline__ void cluster_merge(const FaDecodeParams& p, uint8_t* 
         }
     }
     cl.sync();  // peers are done reading this CTA's partial
-    if (rank == 0 && tid == 0) {  // the last kv head of the row updates the ring metadata
-        __threadfence();
-        const int prev = atomicAdd(&p.cnt_seq[b], 1);
-        if (prev == p.Hkv - 1) {
-            if (p.append && p.kv_len) {
-                p.kv_len[seq] = len1;
-                p.kv_start[seq] = start1;
-            }
-            p.cnt_seq[b] = 0;
-        }
-    }
 }
 
 template <int D, bool CM>
