@@ -44,6 +44,7 @@ constexpr int kGBM = 128, kGBN = 256, kGBK = 64, kGStages = 4;
 constexpr int kGThreads = 192;
 constexpr int kGTileA = kGBM * kGBK * 2;  // 16 KB: 128 rows x 128 bytes
 constexpr int kGTileB = kGBN * kGBK * 2;  // 32 KB: 256 rows x 128 bytes
+constexpr int kGroupM = 16;          // row tiles per raster band of a multi-wave GEMM
 constexpr int kGMaxStages = 8;         // projection GEMM: stages in flight for narrow B tiles
 constexpr int kGSmemMax = 227 * 1024;  // dynamic shared memory per CTA
 constexpr int kGPartPitch = kGBN + 4;  // fp32 words per row of a parked split-K partial
@@ -95,7 +96,20 @@ __global__ void __launch_bounds__(kGThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // ks > 1: blockIdx.x = tile * ks + split, the ks CTAs of a tile form one cluster
     const int split = blockIdx.x % ks;
-    const int n0 = (blockIdx.x / ks) * bn, m0 = blockIdx.y * kGBM;
+    // several waves of 256-wide tiles: block ids (dispatched x fastest) walk bands of kGroupM row
+    // tiles column by column, so the tiles in flight share ~kGroupM rows of A and a band of B in L2
+    // instead of every wave sweeping all of B
+    int nt_i = blockIdx.x / ks, mt_i = blockIdx.y;
+    if (!kNarrow && ks == 1 && (int)gridDim.y > kGroupM) {
+        const int ntn = gridDim.x, mtn = gridDim.y;
+        const int id = blockIdx.y * ntn + blockIdx.x;
+        const int grp = id / (kGroupM * ntn), first_m = grp * kGroupM;
+        const int gm = min(mtn - first_m, kGroupM);
+        const int r = id - grp * kGroupM * ntn;
+        mt_i = first_m + r % gm;
+        nt_i = r / gm;
+    }
+    const int n0 = nt_i * bn, m0 = mt_i * kGBM;
     const int nk_all = (K + kGBK - 1) / kGBK;
     const int per = (nk_all + ks - 1) / ks;
     const int kt0 = split * per;
