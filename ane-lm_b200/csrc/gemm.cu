@@ -96,20 +96,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // ks > 1: blockIdx.x = tile * ks + split, the ks CTAs of a tile form one cluster
     const int split = blockIdx.x % ks;
-    // several waves of 256-wide tiles: block ids (dispatched x fastest) walk bands of kGroupM row
-    // tiles column by column, so the tiles in flight share ~kGroupM rows of A and a band of B in L2
-    // instead of every wave sweeping all of B
-    int nt_i = blockIdx.x / ks, mt_i = blockIdx.y;
-    if (!kNarrow && ks == 1 && (int)gridDim.y > kGroupM) {
-        const int ntn = gridDim.x, mtn = gridDim.y;
-        const int id = blockIdx.y * ntn + blockIdx.x;
-        const int grp = id / (kGroupM * ntn), first_m = grp * kGroupM;
-        const int gm = min(mtn - first_m, kGroupM);
-        const int r = id - grp * kGroupM * ntn;
-        mt_i = first_m + r % gm;
-        nt_i = r / gm;
-    }
-    const int n0 = nt_i * bn, m0 = mt_i * kGBM;
+    const int n0 = (blockIdx.x / ks) * bn, m0 = blockIdx.y * kGBM;
     const int nk_all = (K + kGBK - 1) / kGBK;
     const int per = (nk_all + ks - 1) / ks;
     const int kt0 = split * per;
@@ -246,6 +233,159 @@ __global__ void __launch_bounds__(kGThreads, 1)
     if (warp == 0) {
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, kGBN);
+    }
+}
+
+// Persistent form for several waves of 256-wide tiles: one CTA per SM walks tiles c, c + G, ...
+// (G = gridDim.x) in the banded order (16 row tiles, column by column).  Warp 4: TMA ring over
+// (tile, k-step); warp 5: MMAs of tile i into TMEM accumulator i & 1 once the epilogue released
+// it; warps 0-3: drain accumulator i & 1 (row = thread) and store, while the MMAs of tile i + 1
+// run into the other accumulator.
+__device__ __forceinline__ void banded_tile(int t, int ntn, int mtn, int& mt, int& nt) {
+    const int grp = t / (kGroupM * ntn), first_m = grp * kGroupM;
+    const int gm = min(mtn - first_m, kGroupM);
+    const int r = t - grp * kGroupM * ntn;
+    mt = first_m + r % gm;
+    nt = r / gm;
+}
+
+__global__ void __launch_bounds__(kGThreads, 1)
+    gemm_bf16_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                void* C, long long ldc, int c_dtype, int M, int N, int K, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kGStages * kGTileA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kGStages * kGTileB);
+    uint64_t* empty = full + kGStages;
+    uint64_t* tfull = empty + kGStages;  // [2] accumulator b holds a finished tile
+    uint64_t* tfree = tfull + 2;         // [2] the epilogue has read accumulator b
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, g = blockIdx.x;
+    const int ntn = (N + kGBN - 1) / kGBN, mtn = (M + kGBM - 1) / kGBM;
+    const int ntile = ntn * mtn;
+    const int my_tiles = g < ntile ? (ntile - 1 - g) / G + 1 : 0;
+    const int nk = (K + kGBK - 1) / kGBK;
+    if (tid == 0) {
+        *abort = 0;
+        for (int s = 0; s < kGStages; s++) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            tc::mbar_init(&tfull[b], 1);
+            tc::mbar_init(&tfree[b], 128);
+        }
+        tc::fence_barrier_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, 2 * kGBN);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) {  // TMA producer over (tile, k-step), one continuous ring
+            tc::prefetch_tmap(&tmA);
+            tc::prefetch_tmap(&tmB);
+            int s = 0, u = 0;
+            for (int i = 0; i < my_tiles && !*abort; i++) {
+                int mt, nt;
+                banded_tile(g + i * G, ntn, mtn, mt, nt);
+                for (int kt = 0; kt < nk; kt++) {
+                    if (u > 0 && !tc::mbar_wait(&empty[s], (uint32_t)(u - 1) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
+                    tc::mbar_arrive_expect_tx(&full[s], kGTileA + kGTileB);
+                    tc::tma_load_2d(sA + s * kGTileA, &tmA, &full[s], kt * kGBK, mt * kGBM);
+                    tc::tma_load_2d(sB + s * kGTileB, &tmB, &full[s], kt * kGBK, nt * kGBN);
+                    if (++s == kGStages) {
+                        s = 0;
+                        u++;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = idesc_bf16_f32(kGBM, kGBN);
+            const uint32_t aA = (uint32_t)__cvta_generic_to_shared(sA), aB = (uint32_t)__cvta_generic_to_shared(sB);
+            int s = 0, u = 0;
+            for (int i = 0; i < my_tiles; i++) {
+                const int b = i & 1;
+                if (i >= 2 && !tc::mbar_wait(&tfree[b], (uint32_t)((i >> 1) - 1) & 1, err, ANELM_ERR_TIMEOUT, abort))
+                    break;
+                tc::tc_fence_after();
+                bool ok = true;
+                for (int kt = 0; kt < nk; kt++) {
+                    if (!tc::mbar_wait(&full[s], (uint32_t)u & 1, err, ANELM_ERR_TIMEOUT, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < kGBK / 16; ks++)
+                        tc::mma_f16_ss(tmem + b * kGBN, tc::desc_kmajor_sw128(aA + s * kGTileA + ks * 32),
+                                       tc::desc_kmajor_sw128(aB + s * kGTileB + ks * 32), idesc, (kt | ks) != 0);
+                    tc::mma_commit(&empty[s]);
+                    if (++s == kGStages) {
+                        s = 0;
+                        u++;
+                    }
+                }
+                tc::mma_commit(&tfull[b]);  // an aborted loop still completes the tile's barrier
+                if (!ok) break;
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: thread = row 32 warp + lane of each tile ----------------
+        const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+        const bool vec = c_dtype != ANELM_F32 && (ldc % 8) == 0 && ((uintptr_t)C % 16) == 0;
+        for (int i = 0; i < my_tiles; i++) {
+            const int b = i & 1;
+            int mt, nt;
+            banded_tile(g + i * G, ntn, mtn, mt, nt);
+            const int m = mt * kGBM + 32 * warp + lane;
+            if (!tc::mbar_wait(&tfull[b], (uint32_t)(i >> 1) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
+            tc::tc_fence_after();
+#pragma unroll 1
+            for (int c0 = 0; c0 < kGBN; c0 += 32) {
+                uint32_t x[32];
+                tc::tmem_ld32(trow + b * kGBN + c0, x);
+                tc::tmem_ld_wait();
+                if (c0 == kGBN - 32) {  // every column of accumulator b is read: the MMAs may reuse it
+                    tc::tc_fence_before();
+                    tc::mbar_arrive(&tfree[b]);
+                }
+                if (m >= M) continue;
+                const int nb = nt * kGBN + c0;
+                if (nb + 32 <= N && vec) {
+                    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(C) + (long long)m * ldc + nb);
+#pragma unroll
+                    for (int c8 = 0; c8 < 4; c8++) {
+                        float v[8];
+#pragma unroll
+                        for (int e = 0; e < 8; e++) v[e] = __uint_as_float(x[8 * c8 + e]);
+                        dst[c8] = pack8(v, c_dtype == ANELM_BF16);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; c++)
+                        if (nb + c < N) store_from_float(C, c_dtype, (long long)m * ldc + nb + c, __uint_as_float(x[c]));
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 2 * kGBN);
     }
 }
 
@@ -394,6 +534,12 @@ int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long l
     if (!make_bf16_map(&mA, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, kGBM) ||
         !make_bf16_map(&mB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)bn))
         return ANELM_ERR_CUDA;
+    if (tiles > sms) {  // several waves of 256-wide tiles: one persistent CTA per SM
+        constexpr int psmem = kGStages * (kGTileA + kGTileB) + 256 + 1024;
+        cudaFuncSetAttribute(gemm_bf16_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, psmem);
+        gemm_bf16_persistent_kernel<<<sms, kGThreads, psmem, stream>>>(mA, mB, C, ldc, c_dtype, M, N, K, err);
+        return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
+    }
     // split K over a cluster when the tiles fill less than half of the SMs: the largest cluster
     // size (<= 8) of which the GPU can hold one cluster per tile at once (GPC packing caps it below
     // the SM count / tiles), measured once per device and size

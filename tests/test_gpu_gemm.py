@@ -33,11 +33,13 @@ def test_gemm_projection_shapes(M, N, K):
     _check(M, N, K, torch.float32)
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("M,N,K", [(4096, 2560, 128), (2304, 5000, 64)])
-def test_gemm_multi_wave_raster(M, N, K):
-    """Several waves of 256-wide tiles walk bands of 16 row tiles: two full bands (4096 rows) and a
-    full band plus a partial one of 2 row tiles (2304 rows, ragged N)."""
-    _check(M, N, K, torch.float32, seed=M + N)
+def test_gemm_multi_wave_persistent(M, N, K, out_dtype):
+    """Several waves of 256-wide tiles run persistent CTAs (two TMEM accumulators, each tile's
+    epilogue beside the next tile's MMAs) over bands of 16 row tiles: two full bands (4096 rows),
+    and a full band plus a partial one of 2 row tiles (2304 rows, ragged N)."""
+    _check(M, N, K, out_dtype, seed=M + N)
 
 
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
