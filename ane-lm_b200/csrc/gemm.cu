@@ -395,6 +395,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
 // (grid-stride over all warps of a grid sized to the resident capacity, so no partial last
 // wave), kGvUnroll 16-byte loads per row in flight, fp32 accumulation, one warp reduction per output.
 constexpr int kGvRows = 2, kGvUnroll = 4, kGvThreads = 256, kGvMaxM = 4;
+constexpr int kGvBlocksPerSm = 2;  // few-row LM head: CTAs per SM (78 registers a thread)
+constexpr int kLmGemvRows = 1;      // LM head rows that take the CUDA-core path (at 4 rows the
+                                    // tensor-core path is faster: 380 vs 464 us at 248,320 x 2560)
 
 __device__ __forceinline__ uint4 ld_stream16(const uint4* p) {
     uint4 v;
@@ -734,6 +737,118 @@ __global__ void __launch_bounds__(kGThreads, 1)
 
 namespace {
 
+// LM head for a few rows (n <= kLmGemvRows <= kGvMaxM): the weight read is the cost, so the CUDA cores stream the
+// vocabulary rows as gemv_bf16_kernel does (rows of h staged in shared memory, two vocabulary rows
+// per warp, 16-byte loads) and each warp keeps, per row of h, a running top-32 spread across its
+// lanes (lane j holds the j-th largest; a ballot places a new logit, a shuffle shifts the tail).
+// The CTA's eight lists per row are merged by warp 0 into one candidate list [M][G][32] (values,
+// then indices) for lm_topk_merge_kernel.  Logits are never written.
+__device__ __forceinline__ void warp_topk_insert(float& tv, int& ti, float v, int id, int lane) {
+    // v and id are the same in every lane; the list is sorted descending across lanes
+    if (!(v > __shfl_sync(0xffffffffu, tv, 31))) return;
+    const int pos = __ffs(__ballot_sync(0xffffffffu, tv < v)) - 1;  // first lane below v (a suffix)
+    const float up_v = __shfl_up_sync(0xffffffffu, tv, 1);
+    const int up_i = __shfl_up_sync(0xffffffffu, ti, 1);
+    if (lane > pos) {
+        tv = up_v;
+        ti = up_i;
+    } else if (lane == pos) {
+        tv = v;
+        ti = id;
+    }
+}
+
+__global__ void __launch_bounds__(kGvThreads) lm_head_gemv_topk_kernel(const __nv_bfloat16* A, long long lda,
+                                                                       const __nv_bfloat16* B, long long ldb, float* cand,
+                                                                       int M, int N, int K) {
+    extern __shared__ uint4 xs[];  // [M][K / 8]
+    __shared__ float s_v[kGvThreads / 32][kGvMaxM][32];
+    __shared__ int s_i[kGvThreads / 32][kGvMaxM][32];
+    const int kc = K / 8;
+    for (int i = threadIdx.x; i < M * kc; i += kGvThreads) {
+        const int m = i / kc, c = i - m * kc;
+        xs[i] = *reinterpret_cast<const uint4*>(A + (long long)m * lda + (long long)c * 8);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = gridDim.x * (kGvThreads / 32);
+    float tv[kGvMaxM];
+    int ti[kGvMaxM];
+#pragma unroll
+    for (int m = 0; m < kGvMaxM; m++) {
+        tv[m] = -INFINITY;
+        ti[m] = -1;
+    }
+    for (int n0 = (blockIdx.x * (kGvThreads / 32) + warp) * kGvRows; n0 < N; n0 += nwarps * kGvRows) {
+        const uint4* brow[kGvRows];
+#pragma unroll
+        for (int r = 0; r < kGvRows; r++)
+            brow[r] = reinterpret_cast<const uint4*>(B + (long long)min(n0 + r, N - 1) * ldb);
+        float acc[kGvRows][kGvMaxM];
+#pragma unroll
+        for (int r = 0; r < kGvRows; r++)
+#pragma unroll
+            for (int m = 0; m < kGvMaxM; m++) acc[r][m] = 0.f;
+        for (int c0 = lane; c0 < kc; c0 += 32 * kGvUnroll) {
+            uint4 w[kGvRows][kGvUnroll];
+#pragma unroll
+            for (int u = 0; u < kGvUnroll; u++)
+#pragma unroll
+                for (int r = 0; r < kGvRows; r++)
+                    w[r][u] = (c0 + 32 * u < kc) ? ld_stream16(brow[r] + c0 + 32 * u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int u = 0; u < kGvUnroll; u++) {
+                const int c = c0 + 32 * u;
+                if (c >= kc) break;
+                float wf[kGvRows][8];
+#pragma unroll
+                for (int r = 0; r < kGvRows; r++) unpack8(w[r][u], true, wf[r]);
+#pragma unroll
+                for (int m = 0; m < kGvMaxM; m++) {
+                    if (m >= M) break;
+                    float xf[8];
+                    unpack8(xs[m * kc + c], true, xf);
+#pragma unroll
+                    for (int r = 0; r < kGvRows; r++)
+#pragma unroll
+                        for (int e = 0; e < 8; e++) acc[r][m] = fmaf(wf[r][e], xf[e], acc[r][m]);
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kGvRows; r++)
+#pragma unroll
+            for (int m = 0; m < kGvMaxM; m++) {
+                if (m >= M) break;
+                // lane 0's sum for every lane: the butterfly's lanes can differ in the last bit
+                const float s = __shfl_sync(0xffffffffu, warp_sum(acc[r][m]), 0);
+                if (n0 + r < N) warp_topk_insert(tv[m], ti[m], s, n0 + r, lane);
+            }
+    }
+#pragma unroll
+    for (int m = 0; m < kGvMaxM; m++) {
+        s_v[warp][m][lane] = tv[m];
+        s_i[warp][m][lane] = ti[m];
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const long long G = gridDim.x;
+#pragma unroll
+        for (int m = 0; m < kGvMaxM; m++) {
+            if (m >= M) break;
+            for (int w = 1; w < kGvThreads / 32; w++)
+                for (int j = 0; j < 32; j++) {
+                    const float v = s_v[w][m][j];
+                    if (!(v > __shfl_sync(0xffffffffu, tv[m], 31))) break;  // sorted: the rest cannot enter
+                    warp_topk_insert(tv[m], ti[m], v, s_i[w][m][j], lane);
+                }
+            cand[((long long)m * G + blockIdx.x) * kTopK + lane] = tv[m];
+            reinterpret_cast<int*>(cand + (long long)M * G * kTopK)[((long long)m * G + blockIdx.x) * kTopK + lane] =
+                ti[m];
+        }
+    }
+}
+
 // One CTA per row: each thread keeps the top-32 of its share of the row's n_tiles * 32 candidates,
 // then pairs of lists merge in shared memory (7 levels) into the row's top-32, sorted descending;
 // the first k are written.
@@ -795,8 +910,18 @@ static int lm_groups(int n, int vocab) {
     return std::max(1, std::min(ntile, sms / mt));
 }
 
+// CTAs of the few-row path: at most kGvBlocksPerSm per SM, at most one per 16 vocabulary rows
+static int lm_gemv_groups(int vocab) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int rows_per_block = kGvRows * (kGvThreads / 32);
+    return std::max(1, std::min((vocab + rows_per_block - 1) / rows_per_block, sms * kGvBlocksPerSm));
+}
+
 size_t lm_head_topk_workspace_bytes(int n, int vocab) {
-    return (size_t)n * lm_groups(n, vocab) * kTopK * 8;
+    const int g = n <= kLmGemvRows ? std::max(lm_groups(n, vocab), lm_gemv_groups(vocab)) : lm_groups(n, vocab);
+    return (size_t)n * g * kTopK * 8;
 }
 
 int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long ldw, int n, int vocab, int hidden, int k,
@@ -807,6 +932,16 @@ int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long l
     if ((uintptr_t)h % 16 || (uintptr_t)W % 16 || (ldh * 2) % 16 || (ldw * 2) % 16 || ldh < hidden || ldw < hidden ||
         (uintptr_t)workspace % 16)
         return ANELM_ERR_UNSUPPORTED;
+    if (n <= kLmGemvRows && hidden % 8 == 0 && (size_t)n * hidden * 2 <= 48 * 1024) {
+        // one row (single-sequence decode): stream the weights on the CUDA cores, top-32 kept per warp
+        const int G = lm_gemv_groups(vocab);
+        lm_head_gemv_topk_kernel<<<G, kGvThreads, n * hidden * 2, stream>>>(
+            static_cast<const __nv_bfloat16*>(h), ldh, static_cast<const __nv_bfloat16*>(W), ldw,
+            static_cast<float*>(workspace), n, vocab, hidden);
+        lm_topk_merge_kernel<<<n, kMergeThreads, 0, stream>>>(static_cast<const float*>(workspace), n, G, k, top_vals,
+                                                              top_idx);
+        return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
+    }
     CUtensorMap mA, mB;
     if (!make_bf16_map(&mA, h, (uint64_t)n, (uint64_t)hidden, (uint64_t)ldh, kGBM) ||
         !make_bf16_map(&mB, W, (uint64_t)vocab, (uint64_t)hidden, (uint64_t)ldw, kGBN))

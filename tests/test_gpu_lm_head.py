@@ -3,7 +3,8 @@ scripts/export_hybrid_chunks.py:409-421) against torch.topk over a plain PyTorch
 the same bf16 operands: the values agree within fp32 accumulation-order rounding (1e-4 of the
 row scale), and every returned index is a top-k index of the reference up to near-ties (its
 reference logit is within that tolerance of the k-th largest).  Qwen3.5 vocabulary (248,320) at
-hidden 2560 for one row and a batch; a ragged vocabulary and k < 32."""
+hidden 2560 for one row (CUDA-core path) and batches (tensor-core path); a ragged vocabulary
+(three rows) and k < 32."""
 import pytest
 
 torch = pytest.importorskip("torch")
@@ -31,11 +32,14 @@ def _check(n, vocab, hidden, k, seed):
     assert all(len(set(r.tolist())) == k for r in idx)  # no index twice
 
 
-@pytest.mark.parametrize("n", [1, 64, 256])
+@pytest.mark.parametrize("n", [1, 4, 5, 64, 256])
 def test_lm_head_top32_qwen_vocab(n):
+    """One row takes the CUDA-core path (weights streamed, per-warp running top-32), more rows the
+    tensor-core path."""
     _check(n, 248320, 2560, 32, seed=n)
 
 
 @pytest.mark.parametrize("k", [1, 5, 32])
-def test_lm_head_ragged_vocab(k):
-    _check(3, 1000, 136, k, seed=k)
+@pytest.mark.parametrize("n", [1, 3])
+def test_lm_head_ragged_vocab(n, k):
+    _check(n, 1000, 136, k, seed=k + 10 * n)
