@@ -395,7 +395,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
 // (grid-stride over all warps of a grid sized to the resident capacity, so no partial last
 // wave), kGvUnroll 16-byte loads per row in flight, fp32 accumulation, one warp reduction per output.
 constexpr int kGvRows = 2, kGvUnroll = 4, kGvThreads = 256, kGvMaxM = 4;
-constexpr int kGvBlocksPerSm = 2;  // few-row LM head: CTAs per SM (78 registers a thread)
+constexpr int kGvBlocksPerSm = 2;  // few-row LM head: CTAs per SM (128 registers a thread)
+constexpr int kLmGvRows = 4, kLmGvUnroll = 4;  // its vocabulary rows per warp, loads in flight per row
 constexpr int kLmGemvRows = 1;      // LM head rows that take the CUDA-core path (at 4 rows the
                                     // tensor-core path is faster: 380 vs 464 us at 248,320 x 2560)
 
@@ -738,7 +739,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
 namespace {
 
 // LM head for a few rows (n <= kLmGemvRows <= kGvMaxM): the weight read is the cost, so the CUDA cores stream the
-// vocabulary rows as gemv_bf16_kernel does (rows of h staged in shared memory, two vocabulary rows
+// vocabulary rows as gemv_bf16_kernel does (rows of h staged in shared memory, four vocabulary rows
 // per warp, 16-byte loads) and each warp keeps, per row of h, a running top-32 spread across its
 // lanes (lane j holds the j-th largest; a ballot places a new logit, a shuffle shifts the tail).
 // The CTA's eight lists per row are merged by warp 0 into one candidate list [M][G][32] (values,
@@ -779,44 +780,44 @@ __global__ void __launch_bounds__(kGvThreads) lm_head_gemv_topk_kernel(const __n
         tv[m] = -INFINITY;
         ti[m] = -1;
     }
-    for (int n0 = (blockIdx.x * (kGvThreads / 32) + warp) * kGvRows; n0 < N; n0 += nwarps * kGvRows) {
-        const uint4* brow[kGvRows];
+    for (int n0 = (blockIdx.x * (kGvThreads / 32) + warp) * kLmGvRows; n0 < N; n0 += nwarps * kLmGvRows) {
+        const uint4* brow[kLmGvRows];
 #pragma unroll
-        for (int r = 0; r < kGvRows; r++)
+        for (int r = 0; r < kLmGvRows; r++)
             brow[r] = reinterpret_cast<const uint4*>(B + (long long)min(n0 + r, N - 1) * ldb);
-        float acc[kGvRows][kGvMaxM];
+        float acc[kLmGvRows][kGvMaxM];
 #pragma unroll
-        for (int r = 0; r < kGvRows; r++)
+        for (int r = 0; r < kLmGvRows; r++)
 #pragma unroll
             for (int m = 0; m < kGvMaxM; m++) acc[r][m] = 0.f;
-        for (int c0 = lane; c0 < kc; c0 += 32 * kGvUnroll) {
-            uint4 w[kGvRows][kGvUnroll];
+        for (int c0 = lane; c0 < kc; c0 += 32 * kLmGvUnroll) {
+            uint4 w[kLmGvRows][kLmGvUnroll];
 #pragma unroll
-            for (int u = 0; u < kGvUnroll; u++)
+            for (int u = 0; u < kLmGvUnroll; u++)
 #pragma unroll
-                for (int r = 0; r < kGvRows; r++)
+                for (int r = 0; r < kLmGvRows; r++)
                     w[r][u] = (c0 + 32 * u < kc) ? ld_stream16(brow[r] + c0 + 32 * u) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-            for (int u = 0; u < kGvUnroll; u++) {
+            for (int u = 0; u < kLmGvUnroll; u++) {
                 const int c = c0 + 32 * u;
                 if (c >= kc) break;
-                float wf[kGvRows][8];
+                float wf[kLmGvRows][8];
 #pragma unroll
-                for (int r = 0; r < kGvRows; r++) unpack8(w[r][u], true, wf[r]);
+                for (int r = 0; r < kLmGvRows; r++) unpack8(w[r][u], true, wf[r]);
 #pragma unroll
                 for (int m = 0; m < kGvMaxM; m++) {
                     if (m >= M) break;
                     float xf[8];
                     unpack8(xs[m * kc + c], true, xf);
 #pragma unroll
-                    for (int r = 0; r < kGvRows; r++)
+                    for (int r = 0; r < kLmGvRows; r++)
 #pragma unroll
                         for (int e = 0; e < 8; e++) acc[r][m] = fmaf(wf[r][e], xf[e], acc[r][m]);
                 }
             }
         }
 #pragma unroll
-        for (int r = 0; r < kGvRows; r++)
+        for (int r = 0; r < kLmGvRows; r++)
 #pragma unroll
             for (int m = 0; m < kGvMaxM; m++) {
                 if (m >= M) break;
@@ -910,12 +911,12 @@ static int lm_groups(int n, int vocab) {
     return std::max(1, std::min(ntile, sms / mt));
 }
 
-// CTAs of the few-row path: at most kGvBlocksPerSm per SM, at most one per 16 vocabulary rows
+// CTAs of the few-row path: at most kGvBlocksPerSm per SM, at most one per 32 vocabulary rows
 static int lm_gemv_groups(int vocab) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int rows_per_block = kGvRows * (kGvThreads / 32);
+    const int rows_per_block = kLmGvRows * (kGvThreads / 32);
     return std::max(1, std::min((vocab + rows_per_block - 1) / rows_per_block, sms * kGvBlocksPerSm));
 }
 
