@@ -588,10 +588,39 @@ int launch_gemm_bf16_tn(const void* A, long long lda, const void* B, long long l
 
 namespace {
 
+// Running top-32 of one row spread over a warp: lane j holds the j-th largest (value, index).
+// Branch-free form: every lane runs every shuffle whatever `valid` is (valid, v, id warp-uniform).
+__device__ __forceinline__ void warp_topk_insert_if(float& tv, int& ti, bool valid, float v, int id, int lane) {
+    const bool ok = valid && v > __shfl_sync(0xffffffffu, tv, 31);
+    const unsigned lt = __ballot_sync(0xffffffffu, tv < v);
+    const int pos = lt ? __ffs(lt) - 1 : 32;
+    const float up_v = __shfl_up_sync(0xffffffffu, tv, 1);
+    const int up_i = __shfl_up_sync(0xffffffffu, ti, 1);
+    const float nv = lane > pos ? up_v : (lane == pos ? v : tv);
+    const int ni = lane > pos ? up_i : (lane == pos ? id : ti);
+    tv = ok ? nv : tv;
+    ti = ok ? ni : ti;
+}
+__device__ __forceinline__ void warp_topk_insert(float& tv, int& ti, float v, int id, int lane) {
+    // v and id are the same in every lane; the list is sorted descending across lanes
+    if (!(v > __shfl_sync(0xffffffffu, tv, 31))) return;
+    const int pos = __ffs(__ballot_sync(0xffffffffu, tv < v)) - 1;  // first lane below v (a suffix)
+    const float up_v = __shfl_up_sync(0xffffffffu, tv, 1);
+    const int up_i = __shfl_up_sync(0xffffffffu, ti, 1);
+    if (lane > pos) {
+        tv = up_v;
+        ti = up_i;
+    } else if (lane == pos) {
+        tv = v;
+        ti = id;
+    }
+}
+
 // Persistent LM-head kernel: CTA (g, mt) handles vocabulary tiles g, g + G, ... (G = gridDim.x)
 // for rows [128 mt, 128 mt + 128).  Warp 4: TMA ring (A rows, B vocabulary rows); warp 5: MMAs
 // of each tile into TMEM buffer (i & 1) once the epilogue released it; warps 0-3: per row, the
-// running top-32 over all its tiles, then one candidate list [M][G][32] (values, then indices).
+// running top-32 over all its tiles (spread over a warp's lanes), then one candidate list
+// [M][G][32] (values, then indices).
 __global__ void __launch_bounds__(kGThreads, 1)
     lm_head_topk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* cand,
                         int M, int N, int K, int* err) {
@@ -681,16 +710,18 @@ __global__ void __launch_bounds__(kGThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue: row m = m0 + tid, running top-32 over this CTA's tiles ----------------
-        const int m = m0 + tid;
+        // ---------------- epilogue: running top-32 of rows 32 warp + r, spread over the warp's lanes ----------------
+        // Each 32-column chunk (thread = row) is transposed through shared memory; then, row by row,
+        // every lane tests one column against the row's 32nd value and only the ballot's survivors
+        // are inserted (warp-uniform work: no lane idles through another lane's insertion).
         const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
-        float* row = rows + tid * 33;
-        float tv[kTopK];
-        int ti[kTopK];
+        float* stage = rows + warp * 32 * 33;  // [32 rows][33]
+        float lv[32];
+        int li[32];
 #pragma unroll
-        for (int j = 0; j < kTopK; j++) {
-            tv[j] = -INFINITY;
-            ti[j] = -1;
+        for (int r = 0; r < 32; r++) {
+            lv[r] = -INFINITY;
+            li[r] = -1;
         }
         for (int i = 0; i < my_tiles; i++) {
             const int b = i & 1, n0 = (g + i * G) * kGBN;
@@ -706,23 +737,42 @@ __global__ void __launch_bounds__(kGThreads, 1)
                     tc::mbar_arrive(&tfree[b]);
                 }
 #pragma unroll
-                for (int c = 0; c < 32; c++) row[c] = __uint_as_float(x[c]);
-#pragma unroll 1
-                for (int c = 0; c < 32; c++) {
-                    const int n = n0 + c0 + c;
-                    const float v = row[c];
-                    if (n < N && v > tv[kTopK - 1]) topk_insert(tv, ti, v, n);
+                for (int c = 0; c < 32; c++) stage[lane * 33 + c] = __uint_as_float(x[c]);
+                __syncwarp();
+                const int n = n0 + c0 + lane;  // the column this lane tests
+                const int nrow = M - (m0 + 32 * warp);  // rows of this warp inside the matrix
+                // first every row's survivors (32 independent ballots, which pipeline), then the
+                // insertions of the survivors (each re-read from the staging rows as a broadcast)
+                unsigned masks[32];
+#pragma unroll
+                for (int r = 0; r < 32; r++) {
+                    const float thr = __shfl_sync(0xffffffffu, lv[r], 31);  // every lane shuffles (outside the &&)
+                    masks[r] = __ballot_sync(0xffffffffu, r < nrow && n < N && stage[r * 33 + lane] > thr);
                 }
+                // four rows' insertions interleaved (branch-free, so their shuffle chains overlap)
+#pragma unroll
+                for (int r0 = 0; r0 < 32; r0 += 4) {
+                    unsigned mk[4] = {masks[r0], masks[r0 + 1], masks[r0 + 2], masks[r0 + 3]};
+                    while (mk[0] | mk[1] | mk[2] | mk[3]) {
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            const bool has = mk[q] != 0;
+                            const int src = has ? __ffs(mk[q]) - 1 : 0;
+                            mk[q] &= mk[q] - 1;
+                            warp_topk_insert_if(lv[r0 + q], li[r0 + q], has, stage[(r0 + q) * 33 + src],
+                                                n0 + c0 + src, lane);
+                        }
+                    }
+                }
+                __syncwarp();  // the next chunk overwrites the staging rows
             }
         }
-        if (m < M) {
-            float4* cv = reinterpret_cast<float4*>(cand + ((long long)m * G + g) * kTopK);
-            int4* ci = reinterpret_cast<int4*>(reinterpret_cast<int*>(cand + (long long)M * G * kTopK) +
-                                               ((long long)m * G + g) * kTopK);
 #pragma unroll
-            for (int j = 0; j < kTopK / 4; j++) {
-                cv[j] = make_float4(tv[4 * j], tv[4 * j + 1], tv[4 * j + 2], tv[4 * j + 3]);
-                ci[j] = make_int4(ti[4 * j], ti[4 * j + 1], ti[4 * j + 2], ti[4 * j + 3]);
+        for (int r = 0; r < 32; r++) {
+            const int m = m0 + 32 * warp + r;
+            if (m < M) {
+                cand[((long long)m * G + g) * kTopK + lane] = lv[r];
+                reinterpret_cast<int*>(cand + (long long)M * G * kTopK)[((long long)m * G + g) * kTopK + lane] = li[r];
             }
         }
     }
@@ -744,21 +794,6 @@ namespace {
 // lanes (lane j holds the j-th largest; a ballot places a new logit, a shuffle shifts the tail).
 // The CTA's eight lists per row are merged by warp 0 into one candidate list [M][G][32] (values,
 // then indices) for lm_topk_merge_kernel.  Logits are never written.
-__device__ __forceinline__ void warp_topk_insert(float& tv, int& ti, float v, int id, int lane) {
-    // v and id are the same in every lane; the list is sorted descending across lanes
-    if (!(v > __shfl_sync(0xffffffffu, tv, 31))) return;
-    const int pos = __ffs(__ballot_sync(0xffffffffu, tv < v)) - 1;  // first lane below v (a suffix)
-    const float up_v = __shfl_up_sync(0xffffffffu, tv, 1);
-    const int up_i = __shfl_up_sync(0xffffffffu, ti, 1);
-    if (lane > pos) {
-        tv = up_v;
-        ti = up_i;
-    } else if (lane == pos) {
-        tv = v;
-        ti = id;
-    }
-}
-
 __global__ void __launch_bounds__(kGvThreads) lm_head_gemv_topk_kernel(const __nv_bfloat16* A, long long lda,
                                                                        const __nv_bfloat16* B, long long ldb, float* cand,
                                                                        int M, int N, int K) {
