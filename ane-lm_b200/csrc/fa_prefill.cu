@@ -318,14 +318,112 @@ __global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPre
 // Streaming form of the prep for 16-bit projections: a persistent CTA walks the tokens
 // u = blockIdx.x, blockIdx.x + gridDim.x, ... of the [B][n_pad] grid.  Warp 8 copies each
 // token's whole projection row (and its RoPE table rows) into one of kPrepStages shared-memory
-// stages with untiled bulk copies, kPrepStages - 1 tokens ahead; warps 0-7 run prep_segment on
-// the staged row.  The same arithmetic as fa_prefill_prep_vec_kernel, with the loads kept in
-// flight across tokens instead of one row at a time per CTA.
+// stages with untiled bulk copies, kPrepStages - 1 tokens ahead; warps 0-7 take the staged row's
+// segments.  The arithmetic is prep_segment's (same roundings, same results); the work is laid
+// out for instruction count, which bounds this kernel once the copies stream: a lane's RoPE
+// cos / sin (8 pairs) are read once per token as 16-byte words, a segment's role is a
+// warp-uniform branch, lanes past rot_dim select their unrotated value instead of branching,
+// and token / stage indices advance incrementally (no 64-bit division per token).
 constexpr int kPrepStages = 3;
 constexpr int kPrepWarps = 8;  // consumer warps; warp kPrepWarps is the copy producer
 constexpr int kPrepCtas = 3;   // CTAs per SM: the consumers' latency (warp reductions) needs the warps
 constexpr int kPrepStageMax = 24 * 1024;  // stage bytes that still let kPrepCtas CTAs share an SM
 
+// RoPE coefficients of lane elements e0 + e (e0 = 8 lane) at one position.  Rotate-half: element
+// e0 + e rotates with element e0 + e -+ half by angle index (e0 mod half) + e, and `sg` carries
+// the sign of the partner term (-sin in the first half, +sin in the second).  Interleaved: pair
+// (e0 + e, e0 + e + 1), e even, uses angle index (e0 + e) / 2.  Lanes past rot_dim keep (1, 0).
+template <bool kHalf>
+__device__ __forceinline__ void prep_rope_lane(const FaPrefillParams& p, bool tab, const float* tcos, int pos,
+                                               int lane, float (&c)[8], float (&sg)[8]) {
+    const int e0 = 8 * lane, half = p.rot_dim >> 1;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        c[e] = 1.f;
+        sg[e] = 0.f;
+    }
+    if (e0 >= p.rot_dim) return;
+    if (kHalf) {
+        const bool first = e0 < half;
+        const int j0 = first ? e0 : e0 - half;
+        if (tab) {
+            const float4 c0 = *reinterpret_cast<const float4*>(tcos + j0);
+            const float4 c1 = *reinterpret_cast<const float4*>(tcos + j0 + 4);
+            const float4 s0 = *reinterpret_cast<const float4*>(tcos + half + j0);
+            const float4 s1 = *reinterpret_cast<const float4*>(tcos + half + j0 + 4);
+            const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                c[e] = cc[e];
+                sg[e] = first ? -ss[e] : ss[e];
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                float s;
+                rope_cs_pf(p, pos, j0 + e, c[e], s);
+                sg[e] = first ? -s : s;
+            }
+        }
+    } else {
+        const int j0 = e0 >> 1;
+        if (tab) {
+            const float4 c0 = *reinterpret_cast<const float4*>(tcos + j0);
+            const float4 s0 = *reinterpret_cast<const float4*>(tcos + half + j0);
+            const float cc[4] = {c0.x, c0.y, c0.z, c0.w}, ss[4] = {s0.x, s0.y, s0.z, s0.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                c[2 * i] = c[2 * i + 1] = cc[i];
+                sg[2 * i] = sg[2 * i + 1] = ss[i];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                rope_cs_pf(p, pos, j0 + i, c[2 * i], sg[2 * i]);
+                c[2 * i + 1] = c[2 * i];
+                sg[2 * i + 1] = sg[2 * i];
+            }
+        }
+    }
+}
+
+// RMSNorm (cpu_ops.cpp:24-30) and RoPE (cpu_ops.cpp:40-63, or rotate-half) of one q / k segment,
+// with prep_segment's roundings; `rot` is false for lanes past rot_dim.
+template <bool kHalf>
+__device__ __forceinline__ void prep_qk_lane(const FaPrefillParams& p, float (&v)[8], const float (&w)[8],
+                                             const float (&c)[8], const float (&sg)[8], bool rot, int partner) {
+    if (p.qk_norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss += v[e] * v[e];
+        ss = warp_sum(ss);
+        const float r = 1.0f / sqrtf(ss / (float)kD + p.rms_eps);
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fmul_rn(v[e], r), w[e]);
+    }
+    if (p.rot_dim > 0) {
+        if (kHalf) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float o = __shfl_sync(0xffffffffu, v[e], partner);
+                const float y = __fadd_rn(__fmul_rn(v[e], c[e]), __fmul_rn(o, sg[e]));
+                v[e] = rot ? y : v[e];
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                const float v0 = v[e], v1 = v[e + 1];
+                const float y0 = __fsub_rn(__fmul_rn(v0, c[e]), __fmul_rn(v1, sg[e]));
+                const float y1 = __fadd_rn(__fmul_rn(v0, sg[e]), __fmul_rn(v1, c[e]));
+                v[e] = rot ? y0 : v0;
+                v[e + 1] = rot ? y1 : v1;
+            }
+        }
+    }
+}
+
+template <bool kHalf, bool kBf>
 __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
     fa_prefill_prep_bulk_kernel(const FaPrefillParams p, int stage_bytes, int rope_off) {
     extern __shared__ __align__(128) uint8_t prep_smem[];
@@ -334,11 +432,11 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
     volatile int* abort = reinterpret_cast<volatile int*>(empty + kPrepStages);
     uint8_t* stage0 = prep_smem + 128;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int Hq = p.Hq, Hkv = p.Hkv;
+    const int Hq = p.Hq, Hkv = p.Hkv, n = p.n, n_pad = p.n_pad;
     const int nseg = 2 * Hq + 2 * Hkv;
     const uint32_t row_bytes = (uint32_t)nseg * kD * 2;
     const int half = p.rot_dim >> 1;
-    const long long total = (long long)p.B * p.n_pad;
+    const int G = gridDim.x;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kPrepStages; s++) {
             tc::mbar_init(&full[s], 1);
@@ -348,41 +446,48 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
         tc::fence_barrier_init();
     }
     __syncthreads();
+    // token u = b n_pad + t, advanced by G per step (the host keeps B n_pad + G below 2^31)
     if (warp == kPrepWarps) {  // producer: one thread issues every copy
         if (lane != 0) return;
-        long long last[kPrepStages];
+        int last_ph[kPrepStages];
 #pragma unroll
-        for (int s = 0; s < kPrepStages; s++) last[s] = -1;
-        long long k = 0;
-        for (long long u = blockIdx.x; u < total; u += gridDim.x, k++) {
-            const int s = (int)(k % kPrepStages);
-            if (k >= kPrepStages &&
-                !tc::mbar_wait(&empty[s], (uint32_t)((k / kPrepStages) - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort))
-                break;
-            const int b = (int)(u / p.n_pad), t = (int)(u % p.n_pad);
-            last[s] = k;
-            if (t >= p.n) {  // padding row: nothing to copy
+        for (int s = 0; s < kPrepStages; s++) last_ph[s] = -1;
+        int b = blockIdx.x / n_pad, t = blockIdx.x % n_pad, s = 0;
+        uint32_t ph = 0;  // this pass's phase of stage s (flips each time s wraps)
+        for (int k = 0; b < p.B; k++) {
+            if (k >= kPrepStages && !tc::mbar_wait(&empty[s], ph ^ 1u, p.err, ANELM_ERR_TIMEOUT, abort)) break;
+            last_ph[s] = (int)ph;
+            if (t >= n) {  // padding row: nothing to copy
                 tc::mbar_arrive(&full[s]);
-                continue;
+            } else {
+                uint8_t* st = stage0 + (size_t)s * stage_bytes;
+                const int pos = p.start_pos + t;
+                const bool tab = p.rot_dim > 0 && p.rope_cos && pos >= 0 && pos < p.rope_len;
+                tc::mbar_arrive_expect_tx(&full[s], row_bytes + (tab ? 8u * half : 0u));
+                tc::bulk_load(st, reinterpret_cast<const char*>(p.proj) + ((long long)b * n + t) * p.proj_stride * 2,
+                              row_bytes, &full[s]);
+                if (tab) {
+                    tc::bulk_load(st + rope_off, p.rope_cos + (long long)pos * half, 4u * half, &full[s]);
+                    tc::bulk_load(st + rope_off + 4 * half, p.rope_sin + (long long)pos * half, 4u * half, &full[s]);
+                }
             }
-            uint8_t* st = stage0 + (size_t)s * stage_bytes;
-            const int pos = p.start_pos + t;
-            const bool tab = p.rot_dim > 0 && p.rope_cos && pos >= 0 && pos < p.rope_len;
-            tc::mbar_arrive_expect_tx(&full[s], row_bytes + (tab ? 8u * half : 0u));
-            tc::bulk_load(st, reinterpret_cast<const char*>(p.proj) + ((long long)b * p.n + t) * p.proj_stride * 2,
-                          row_bytes, &full[s]);
-            if (tab) {
-                tc::bulk_load(st + rope_off, p.rope_cos + (long long)pos * half, 4u * half, &full[s]);
-                tc::bulk_load(st + rope_off + 4 * half, p.rope_sin + (long long)pos * half, 4u * half, &full[s]);
+            t += G;
+            while (t >= n_pad) {
+                t -= n_pad;
+                b++;
+            }
+            if (++s == kPrepStages) {
+                s = 0;
+                ph ^= 1u;
             }
         }
         // every issued copy has landed before the CTA can exit (normally the consumers already
         // waited for them; after a timeout this bounds the wait for the ones still in flight)
 #pragma unroll
-        for (int s = 0; s < kPrepStages; s++)
-            if (last[s] >= 0)
+        for (int s2 = 0; s2 < kPrepStages; s2++)
+            if (last_ph[s2] >= 0)
                 for (uint32_t i = 0; i < tc::kWaitPolls; i++)
-                    if (tc::mbar_try_wait(&full[s], (uint32_t)(last[s] / kPrepStages) & 1)) break;
+                    if (tc::mbar_try_wait(&full[s2], (uint32_t)last_ph[s2])) break;
         return;
     }
     const int e0 = 8 * lane;
@@ -392,15 +497,21 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
         qn[e] = p.qk_norm ? p.q_norm[e0 + e] : 0.f;
         kn[e] = p.qk_norm ? p.k_norm[e0 + e] : 0.f;
     }
-    const bool bf = p.proj_dtype == ANELM_BF16;
+    const bool rot = e0 < p.rot_dim;
+    const int hl = half >> 3;  // lanes per rotary half (rotate-half partner lane = lane +- hl)
+    const int partner = lane < hl ? lane + hl : lane - hl;
+    const long long q_hstride = (long long)n_pad * kD;  // Q / K / V: [B][H][n_pad][kD]
+    // job j of the token -> segment: with Hq a multiple of 8, blocks of 8 jobs alternate q heads and
+    // gates (q 0-7, gate 0-7, q 8-15, ...), so each warp gets the same number of RMSNorm + RoPE
+    // segments (the warps' slowest bounds the stage's release); k and v heads follow
+    const bool mix = (Hq & 7) == 0;
     int cur_b = -1, seq = 0;  // the sequence of row b and its pool base, reloaded when b changes
     long long kv0 = 0;
-    long long k = 0;
-    for (long long u = blockIdx.x; u < total; u += gridDim.x, k++) {
-        const int s = (int)(k % kPrepStages);
-        if (!tc::mbar_wait(&full[s], (uint32_t)(k / kPrepStages) & 1, p.err, ANELM_ERR_TIMEOUT, abort)) break;
-        const int b = (int)(u / p.n_pad), t = (int)(u % p.n_pad);
-        if (t >= p.n) {
+    int b = blockIdx.x / n_pad, t = blockIdx.x % n_pad, s = 0;
+    uint32_t ph = 0;
+    while (b < p.B) {
+        if (!tc::mbar_wait(&full[s], ph, p.err, ANELM_ERR_TIMEOUT, abort)) break;
+        if (t >= n) {
             prep_zero_row(p, b, t, warp, kPrepWarps, e0);
         } else {
             const uint8_t* st = stage0 + (size_t)s * stage_bytes;
@@ -410,38 +521,62 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
                 seq = p.seq_ids ? p.seq_ids[b] : 0;
                 kv0 = p.kv_base ? p.kv_base[seq] : 0;
             }
-            const long long slot_row = p.kv_base ? (kv0 + t) * Hkv : 0;
             const bool tab = p.rot_dim > 0 && p.rope_cos && pos >= 0 && pos < p.rope_len;
-            const float* tc_cos = reinterpret_cast<const float*>(st + rope_off);
-            const auto cs = [&](int j, float& c, float& sn) {
-                if (tab) {
-                    c = tc_cos[j];
-                    sn = tc_cos[half + j];
-                } else {
-                    rope_cs_pf(p, pos, j, c, sn);
-                }
-            };
-            // job j of the token -> segment: with Hq a multiple of 8, blocks of 8 jobs alternate q heads and
-            // gates (q 0-7, gate 0-7, q 8-15, ...), so each warp gets the same number of RMSNorm + RoPE
-            // segments (the warps' slowest bounds the stage's release); k and v heads follow
-            const bool mix = (Hq & 7) == 0;
+            float c[8], sg[8];
+            prep_rope_lane<kHalf>(p, tab, reinterpret_cast<const float*>(st + rope_off), pos, lane, c, sg);
+            __half* qrow = p.Qh + ((long long)b * Hq * n_pad + t) * kD + e0;
+            __half* krow = p.Kh + ((long long)b * Hkv * n_pad + t) * kD + e0;
+            __half* vrow = p.Vh + ((long long)b * Hkv * n_pad + t) * kD + e0;
+            __half* grow = p.SG ? p.SG + ((long long)b * n + t) * Hq * kD + e0 : nullptr;
+            const long long pool = (p.kv_base ? (kv0 + t) * Hkv * kD : 0) + e0;  // ring slot row (qwen3_5.cpp:984-986)
             for (int j = warp; j < nseg; j += kPrepWarps) {
-                int sg = j;
+                int sgm = j;
                 if (mix && j < 2 * Hq) {
                     const int bk = j >> 3;
-                    sg = 2 * ((bk >> 1) * 8 + (j & 7)) + (bk & 1);
+                    sgm = 2 * ((bk >> 1) * 8 + (j & 7)) + (bk & 1);
                 }
                 float x[8];
-                unpack8(*reinterpret_cast<const uint4*>(st + (size_t)sg * kD * 2 + 16 * lane), bf, x);
-                prep_segment(p, x, sg, lane, b, t, slot_row, qn, kn, cs);
+                unpack8(*reinterpret_cast<const uint4*>(st + (size_t)sgm * kD * 2 + 16 * lane), kBf, x);
+                if (sgm < 2 * Hq) {
+                    const int h = sgm >> 1;
+                    if (!(sgm & 1)) {  // q head h
+                        prep_qk_lane<kHalf>(p, x, qn, c, sg, rot, partner);
+                        *reinterpret_cast<uint4*>(qrow + h * q_hstride) = half8(x);
+                    } else if (grow) {  // sigmoid(gate) (mul_sigmoid_inplace, cpu_ops.cpp:15-22), fp16
+                        float g[8];
+#pragma unroll
+                        for (int e = 0; e < 8; e++) g[e] = rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * x[e]));
+                        *reinterpret_cast<uint4*>(grow + h * kD) = half8(g);
+                    }
+                } else if (sgm < 2 * Hq + Hkv) {  // k head
+                    const int kh = sgm - 2 * Hq;
+                    prep_qk_lane<kHalf>(p, x, kn, c, sg, rot, partner);
+                    const uint4 hv = half8(x);
+                    *reinterpret_cast<uint4*>(krow + kh * q_hstride) = hv;
+                    if (p.k_pool) *reinterpret_cast<uint4*>(p.k_pool + pool + kh * kD) = hv;  // ring append
+                } else {  // v head
+                    const int vh = sgm - 2 * Hq - Hkv;
+                    const uint4 hv = half8(x);
+                    *reinterpret_cast<uint4*>(vrow + vh * q_hstride) = hv;
+                    if (p.k_pool) *reinterpret_cast<uint4*>(p.v_pool + pool + vh * kD) = hv;
+                }
             }
             if (t == 0 && warp == 0 && lane == 0 && p.kv_len) {
-                p.kv_len[seq] = p.n;
+                p.kv_len[seq] = n;
                 p.kv_start[seq] = 0;
             }
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&empty[s]);
+        t += G;
+        while (t >= n_pad) {
+            t -= n_pad;
+            b++;
+        }
+        if (++s == kPrepStages) {
+            s = 0;
+            ph ^= 1u;
+        }
     }
 }
 
@@ -812,6 +947,7 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
     const int rope_off = nseg * kD * 2;
     const int stage_bytes = (rope_off + 8 * (p.rot_dim >> 1) + 127) / 128 * 128;
     const bool bulk = vec && dtype_bytes(p.proj_dtype) == 2 && stage_bytes <= kPrepStageMax &&
+                      (long long)p.B * p.n_pad + 4LL * kPrepCtas * 1024 < (1LL << 31) &&
                       (!p.rope_cos || ((uintptr_t)p.rope_cos % 16 == 0 && (uintptr_t)p.rope_sin % 16 == 0));
     if (bulk) {
         int dev = 0, sms = 148;
@@ -820,8 +956,11 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
         const long long total = (long long)p.B * p.n_pad;
         const int grid = (int)std::min<long long>(total, (long long)kPrepCtas * sms);
         const int smem = 128 + kPrepStages * stage_bytes;
-        cudaFuncSetAttribute(fa_prefill_prep_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        fa_prefill_prep_bulk_kernel<<<grid, 32 * (kPrepWarps + 1), smem, stream>>>(p, stage_bytes, rope_off);
+        const bool half = p.rope_mode != ANELM_ROPE_INTERLEAVED, bf = p.proj_dtype == ANELM_BF16;
+        auto kern = half ? (bf ? fa_prefill_prep_bulk_kernel<true, true> : fa_prefill_prep_bulk_kernel<true, false>)
+                         : (bf ? fa_prefill_prep_bulk_kernel<false, true> : fa_prefill_prep_bulk_kernel<false, false>);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        kern<<<grid, 32 * (kPrepWarps + 1), smem, stream>>>(p, stage_bytes, rope_off);
     } else if (vec) {
         fa_prefill_prep_vec_kernel<<<dim3(p.n_pad, p.B), 256, 0, stream>>>(p);
     } else {
