@@ -444,6 +444,10 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
         }
         *abort = 0;
         tc::fence_barrier_init();
+        // the attention launch that follows may start its prologue now: every CTA of this persistent
+        // grid is resident, so its CTAs only take SMs this grid has left (they wait for its results
+        // at griddepcontrol.wait)
+        asm volatile("griddepcontrol.launch_dependents;");
     }
     __syncthreads();
     // token u = b n_pad + t, advanced by G per step (the host keeps B n_pad + G below 2^31)
@@ -619,6 +623,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // launched as a programmatic dependent of the prep: Q, K, V and sigmoid(gate) are read only
+    // after the prep grid has completed and its writes are visible (a no-op for a plain launch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == kWarpK || warp == kWarpV) {
         // ---------------- TMA producers: one warp streams Q then K (then the gate tile), one streams V ----------------
@@ -970,7 +977,22 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
         fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
     }
     cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    fa_prefill_kernel<<<dim3(p.Hq, p.n_pad / kBM, p.B), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
+    // programmatic dependent launch: the prologue (barriers, TMEM allocation) overlaps the prep's
+    // tail; the kernel reads the prep's outputs only after griddepcontrol.wait
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.Hq, p.n_pad / kBM, p.B);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, fa_prefill_kernel, mQ, mK, mV, mG, mO, p) != cudaSuccess) {
+        cudaGetLastError();  // clear, then the plain launch
+        fa_prefill_kernel<<<cfg.gridDim, kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
+    }
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 
