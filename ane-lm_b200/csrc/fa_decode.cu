@@ -178,6 +178,21 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int blk = blockIdx.x, kvh = blockIdx.y;
+    // Programmatic dependent launch (the one-row cluster form is launched as one): a following
+    // launch may start once every CTA of this grid is resident; before griddepcontrol.wait this
+    // CTA reads only the QK-norm weights (never written by a kernel), after it everything else
+    // (the projection row, ring metadata, positions, K / V pools).  Both are no-ops without PDL.
+    asm volatile("griddepcontrol.launch_dependents;");
+    constexpr int NW = D / 32;
+    float wq[NW], wk[NW];
+    if (p.qk_norm) {
+#pragma unroll
+        for (int m = 0; m < NW; m++) {
+            wq[m] = p.q_norm[lane + 32 * m];
+            wk[m] = p.k_norm[lane + 32 * m];
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // the cluster-merge form serves a one-row plan with one CTA per split: no table lookup
     const int b = CM ? 0 : p.blk_b[blk], split = CM ? blk : p.blk_split[blk];
     const int Hkv = p.Hkv;
@@ -199,20 +214,11 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
     if (has_v) load8(proj_row, p.proj_dtype, p.v_off + (long long)kvh * D + (tid - CPR) * 8, kv8);
 
     // ---- per-thread constants of the prologue and the merge, loaded now so their latency overlaps
-    // the projection loads: the QK-norm weights of this lane's elements, the RoPE angle of the pair
+    // the projection loads (the QK-norm weights came before the dependency wait): the RoPE angle of the pair
     // this thread rotates (the same pair index for every vector when the thread count is a
     // multiple of the half rotary width), and, for the cluster merge, the gate values of the first
     // output columns this thread merges ----
     const int pos = p.pos_arr ? p.pos_arr[b] : p.pos_scalar;
-    constexpr int NW = D / 32;
-    float wq[NW], wk[NW];
-    if (p.qk_norm) {
-#pragma unroll
-        for (int m = 0; m < NW; m++) {
-            wq[m] = p.q_norm[lane + 32 * m];
-            wk[m] = p.k_norm[lane + 32 * m];
-        }
-    }
     const int rhalf = p.rot_dim >> 1;
     const bool rope_pre = rhalf > 0 && kThreads % rhalf == 0;
     float rc = 1.f, rs = 0.f;
@@ -695,13 +701,15 @@ int launch_fa_decode(const FaDecodeParams& p0, int head_dim, int n_blocks, cudaS
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = sm;
         cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = p.cluster_ns;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // prologue overlaps the previous kernel
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = 2;
         if (cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess) return ANELM_OK;
         cudaGetLastError();  // a cluster that cannot be placed: merge through global memory instead
     }
