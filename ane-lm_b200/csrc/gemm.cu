@@ -888,50 +888,46 @@ __global__ void __launch_bounds__(kGvThreads) lm_head_gemv_topk_kernel(const __n
 // One CTA per row: each thread keeps the top-32 of its share of the row's n_tiles * 32 candidates,
 // then pairs of lists merge in shared memory (7 levels) into the row's top-32, sorted descending;
 // the first k are written.
-constexpr int kMergeThreads = 128;
-__global__ void __launch_bounds__(kMergeThreads) lm_topk_merge_kernel(const float* cand, int M, int ntile, int k,
-                                                                       float* top_vals, int* top_idx) {
-    __shared__ float sv[kMergeThreads][kTopK + 1];
-    __shared__ int si[kMergeThreads][kTopK + 1];
-    const int m = blockIdx.x, tid = threadIdx.x;
+constexpr int kMergeWarps = 8;
+// One CTA per row.  Each warp folds a strided share of the row's candidates (32 at a time, one per
+// lane) into a running top-32 spread over its lanes: a ballot picks the candidates above the list's
+// 32nd value and only those are inserted (warp_topk_insert_if re-checks each against the current
+// 32nd).  Warp 0 then folds the other warps' lists in the same way.  Every loop trip count and
+// ballot mask is warp-uniform, so all lanes take part in every shuffle.
+__global__ void __launch_bounds__(32 * kMergeWarps) lm_topk_merge_kernel(const float* cand, int M, int ntile, int k,
+                                                                         float* top_vals, int* top_idx) {
+    __shared__ float sv[kMergeWarps][kTopK];
+    __shared__ int si[kMergeWarps][kTopK];
+    const int m = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long long nc = (long long)ntile * kTopK;
     const float* cv = cand + (long long)m * nc;
     const int* ci = reinterpret_cast<const int*>(cand + (long long)M * nc) + (long long)m * nc;
-    float tv[kTopK];
-    int ti[kTopK];
-#pragma unroll
-    for (int j = 0; j < kTopK; j++) {
-        tv[j] = -INFINITY;
-        ti[j] = -1;
-    }
-    for (long long i = tid; i < nc; i += kMergeThreads) {
-        const float v = cv[i];
-        if (v > tv[kTopK - 1]) topk_insert(tv, ti, v, ci[i]);
-    }
-#pragma unroll
-    for (int j = 0; j < kTopK; j++) {
-        sv[tid][j] = tv[j];
-        si[tid][j] = ti[j];
-    }
-    __syncthreads();
-    for (int s = 1; s < kMergeThreads; s <<= 1) {
-        if ((tid & (2 * s - 1)) == 0) {
-            for (int j = 0; j < kTopK; j++) {
-                const float v = sv[tid + s][j];
-                if (!(v > tv[kTopK - 1])) break;  // the partner's list is sorted: the rest cannot enter
-                topk_insert(tv, ti, v, si[tid + s][j]);
-            }
-#pragma unroll
-            for (int j = 0; j < kTopK; j++) {
-                sv[tid][j] = tv[j];
-                si[tid][j] = ti[j];
-            }
+    float tv = -INFINITY;  // lane j: the j-th largest value so far (ties keep the earlier entry first)
+    int ti = -1;
+    auto fold = [&](float v, int id, bool in) {
+        unsigned mk = __ballot_sync(0xffffffffu, in && v > __shfl_sync(0xffffffffu, tv, 31));
+        while (mk) {
+            const int src = __ffs(mk) - 1;
+            mk &= mk - 1;
+            const float x = __shfl_sync(0xffffffffu, v, src);
+            const int xi = __shfl_sync(0xffffffffu, id, src);
+            warp_topk_insert_if(tv, ti, true, x, xi, lane);
         }
-        __syncthreads();
+    };
+    for (long long base = 32LL * warp; base < nc; base += 32LL * kMergeWarps) {
+        const long long i = base + lane;
+        const bool in = i < nc;
+        fold(in ? cv[i] : -INFINITY, in ? ci[i] : -1, in);
     }
-    if (tid < k) {
-        top_vals[(long long)m * k + tid] = sv[0][tid];
-        top_idx[(long long)m * k + tid] = si[0][tid];
+    sv[warp][lane] = tv;
+    si[warp][lane] = ti;
+    __syncthreads();
+    if (warp == 0) {
+        for (int w = 1; w < kMergeWarps; w++) fold(sv[w][lane], si[w][lane], true);
+        if (lane < k) {
+            top_vals[(long long)m * k + lane] = tv;
+            top_idx[(long long)m * k + lane] = ti;
+        }
     }
 }
 
@@ -974,7 +970,7 @@ int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long l
         lm_head_gemv_topk_kernel<<<G, kGvThreads, n * hidden * 2, stream>>>(
             static_cast<const __nv_bfloat16*>(h), ldh, static_cast<const __nv_bfloat16*>(W), ldw,
             static_cast<float*>(workspace), n, vocab, hidden);
-        lm_topk_merge_kernel<<<n, kMergeThreads, 0, stream>>>(static_cast<const float*>(workspace), n, G, k, top_vals,
+        lm_topk_merge_kernel<<<n, 32 * kMergeWarps, 0, stream>>>(static_cast<const float*>(workspace), n, G, k, top_vals,
                                                               top_idx);
         return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
     }
@@ -987,7 +983,7 @@ int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long l
     const int G = lm_groups(n, vocab);
     dim3 grid(G, (n + kGBM - 1) / kGBM);
     lm_head_topk_kernel<<<grid, kGThreads, smem, stream>>>(mA, mB, static_cast<float*>(workspace), n, vocab, hidden, err);
-    lm_topk_merge_kernel<<<n, kMergeThreads, 0, stream>>>(static_cast<const float*>(workspace), n, G, k, top_vals,
+    lm_topk_merge_kernel<<<n, 32 * kMergeWarps, 0, stream>>>(static_cast<const float*>(workspace), n, G, k, top_vals,
                                                           top_idx);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
