@@ -57,22 +57,8 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
     return tc::idesc_f16_f32(M, N) | (1u << 7) | (1u << 10);
 }
 
-// Insert (v, id) into the descending list (tv, ti) of 32 (static indices: registers).  Every top-k
-// with k <= 32 is the head of the top-32, so the lists always hold 32.
+// Every top-k with k <= 32 is the head of the top-32, so the running lists always hold 32.
 constexpr int kTopK = 32;
-__device__ __forceinline__ void topk_insert(float (&tv)[kTopK], int (&ti)[kTopK], float v, int id) {
-#pragma unroll
-    for (int j = 0; j < kTopK; j++) {
-        if (v > tv[j]) {
-            const float tf = tv[j];
-            const int tn = ti[j];
-            tv[j] = v;
-            ti[j] = id;
-            v = tf;
-            id = tn;
-        }
-    }
-}
 
 // kNarrow: tile width bn and stage count nst as given (one partial wave of narrower tiles);
 // otherwise the compile-time 256 columns and kGStages stages.
@@ -619,11 +605,14 @@ __device__ __forceinline__ void warp_topk_insert(float& tv, int& ti, float v, in
 // Persistent LM-head kernel: CTA (g, mt) handles vocabulary tiles g, g + G, ... (G = gridDim.x)
 // for rows [128 mt, 128 mt + 128).  Warp 4: TMA ring (A rows, B vocabulary rows); warp 5: MMAs
 // of each tile into TMEM buffer (i & 1) once the epilogue released it; warps 0-3: per row, the
-// running top-32 over all its tiles (spread over a warp's lanes), then one candidate list
-// [M][G][32] (values, then indices).
+// running top-32 over all its tiles (spread over a warp's lanes), then candidate lists
+// [M][G rep][32] (values, then indices).  With M <= 64 (one row tile) the A tile holds rep = 128 / rr
+// copies of the rr-row block (rr = 32 or 64, one TMA box each, tmA's box is rr rows), so every
+// epilogue warp has rows: the warps reading copy cp take columns [cp 256 / rep, (cp + 1) 256 / rep)
+// of each tile and keep their own list (copy cp's list of CTA g is candidate list g rep + cp).
 __global__ void __launch_bounds__(kGThreads, 1)
     lm_head_topk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* cand,
-                        int M, int N, int K, int* err) {
+                        int M, int N, int K, int rep, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -674,7 +663,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
                         !tc::mbar_wait(&empty[s], (uint32_t)((q / kGStages) - 1) & 1, err, ANELM_ERR_TIMEOUT, abort))
                         break;
                     tc::mbar_arrive_expect_tx(&full[s], kGTileA + kGTileB);
-                    tc::tma_load_2d(sA + s * kGTileA, &tmA, &full[s], kt * kGBK, m0);
+                    for (int c = 0; c < rep; c++)  // rep boxes of kGBM / rep rows (whole 8-row swizzle atoms)
+                        tc::tma_load_2d(sA + s * kGTileA + c * (kGBM / rep) * 128, &tmA, &full[s], kt * kGBK, m0);
                     tc::tma_load_2d(sB + s * kGTileB, &tmB, &full[s], kt * kGBK, n0);
                 }
             }
@@ -716,6 +706,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
         // are inserted (warp-uniform work: no lane idles through another lane's insertion).
         const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
         float* stage = rows + warp * 32 * 33;  // [32 rows][33]
+        const int rr = kGBM / rep;                    // rows per copy of the A block
+        const int cp = (32 * warp) / rr;              // the copy this warp's TMEM lanes hold
+        const int rbase = (32 * warp) % rr;           // its first row within the copy
+        const int cbeg = cp * (kGBN / rep), cend = cbeg + kGBN / rep;  // its columns of every tile
+        const int nrow = M - (m0 + rbase);            // rows of this warp inside the matrix
         float lv[32];
         int li[32];
 #pragma unroll
@@ -728,11 +723,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
             if (!tc::mbar_wait(&tfull[b], (uint32_t)(i >> 1) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
             tc::tc_fence_after();
 #pragma unroll 1
-            for (int c0 = 0; c0 < kGBN; c0 += 32) {
+            for (int c0 = cbeg; c0 < cend; c0 += 32) {
                 uint32_t x[32];
                 tc::tmem_ld32(trow + b * kGBN + c0, x);
                 tc::tmem_ld_wait();
-                if (c0 == kGBN - 32) {  // every column of accumulator b is read: the MMAs may reuse it
+                if (c0 == cend - 32) {  // this warp's last read of accumulator b: the MMAs may reuse it
                     tc::tc_fence_before();
                     tc::mbar_arrive(&tfree[b]);
                 }
@@ -740,7 +735,6 @@ __global__ void __launch_bounds__(kGThreads, 1)
                 for (int c = 0; c < 32; c++) stage[lane * 33 + c] = __uint_as_float(x[c]);
                 __syncwarp();
                 const int n = n0 + c0 + lane;  // the column this lane tests
-                const int nrow = M - (m0 + 32 * warp);  // rows of this warp inside the matrix
                 // first every row's survivors (32 independent ballots, which pipeline), then the
                 // insertions of the survivors (each re-read from the staging rows as a broadcast)
                 unsigned masks[32];
@@ -769,10 +763,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
         }
 #pragma unroll
         for (int r = 0; r < 32; r++) {
-            const int m = m0 + 32 * warp + r;
-            if (m < M) {
-                cand[((long long)m * G + g) * kTopK + lane] = lv[r];
-                reinterpret_cast<int*>(cand + (long long)M * G * kTopK)[((long long)m * G + g) * kTopK + lane] = li[r];
+            const int m = m0 + rbase + r;
+            if (r < nrow) {
+                const long long slot = ((long long)m * G + g) * rep + cp;
+                cand[slot * kTopK + lane] = lv[r];
+                reinterpret_cast<int*>(cand + (long long)M * G * rep * kTopK)[slot * kTopK + lane] = li[r];
             }
         }
     }
@@ -951,8 +946,14 @@ static int lm_gemv_groups(int vocab) {
     return std::max(1, std::min((vocab + rows_per_block - 1) / rows_per_block, sms * kGvBlocksPerSm));
 }
 
+// copies of the row block in the tensor-core path's A tile, so every epilogue warp has rows (measured:
+// 32 rows 650 -> 475 us, 64 rows 659 -> 557 us); up to 8 rows the insertions are few and the extra
+// candidate lists cost the merge more than the split saves (4 rows 286 -> 297 us with four copies)
+static int lm_rep(int n) { return n <= 8 ? 1 : n <= 32 ? 4 : n <= 64 ? 2 : 1; }
+
 size_t lm_head_topk_workspace_bytes(int n, int vocab) {
-    const int g = n <= kLmGemvRows ? std::max(lm_groups(n, vocab), lm_gemv_groups(vocab)) : lm_groups(n, vocab);
+    const int tc_lists = lm_groups(n, vocab) * lm_rep(n);
+    const int g = n <= kLmGemvRows ? std::max(tc_lists, lm_gemv_groups(vocab)) : tc_lists;
     return (size_t)n * g * kTopK * 8;
 }
 
@@ -974,17 +975,19 @@ int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long l
                                                               top_idx);
         return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
     }
+    const int rep = lm_rep(n);
     CUtensorMap mA, mB;
-    if (!make_bf16_map(&mA, h, (uint64_t)n, (uint64_t)hidden, (uint64_t)ldh, kGBM) ||
+    if (!make_bf16_map(&mA, h, (uint64_t)n, (uint64_t)hidden, (uint64_t)ldh, kGBM / rep) ||
         !make_bf16_map(&mB, W, (uint64_t)vocab, (uint64_t)hidden, (uint64_t)ldw, kGBN))
         return ANELM_ERR_CUDA;
     constexpr int smem = kLmSmem;
     cudaFuncSetAttribute(lm_head_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     const int G = lm_groups(n, vocab);
     dim3 grid(G, (n + kGBM - 1) / kGBM);
-    lm_head_topk_kernel<<<grid, kGThreads, smem, stream>>>(mA, mB, static_cast<float*>(workspace), n, vocab, hidden, err);
-    lm_topk_merge_kernel<<<n, 32 * kMergeWarps, 0, stream>>>(static_cast<const float*>(workspace), n, G, k, top_vals,
-                                                          top_idx);
+    lm_head_topk_kernel<<<grid, kGThreads, smem, stream>>>(mA, mB, static_cast<float*>(workspace), n, vocab, hidden,
+                                                           rep, err);
+    lm_topk_merge_kernel<<<n, 32 * kMergeWarps, 0, stream>>>(static_cast<const float*>(workspace), n, G * rep, k,
+                                                          top_vals, top_idx);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 
