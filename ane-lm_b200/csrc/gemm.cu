@@ -884,6 +884,7 @@ __global__ void __launch_bounds__(kGvThreads) lm_head_gemv_topk_kernel(const __n
 // then pairs of lists merge in shared memory (7 levels) into the row's top-32, sorted descending;
 // the first k are written.
 constexpr int kMergeWarps = 8;
+constexpr int kMergeBatch = 8;  // rounds of 32 candidates whose loads a warp keeps in flight together
 // One CTA per row.  Each warp folds a strided share of the row's candidates (32 at a time, one per
 // lane) into a running top-32 spread over its lanes: a ballot picks the candidates above the list's
 // 32nd value and only those are inserted (warp_topk_insert_if re-checks each against the current
@@ -909,10 +910,19 @@ __global__ void __launch_bounds__(32 * kMergeWarps) lm_topk_merge_kernel(const f
             warp_topk_insert_if(tv, ti, true, x, xi, lane);
         }
     };
-    for (long long base = 32LL * warp; base < nc; base += 32LL * kMergeWarps) {
-        const long long i = base + lane;
-        const bool in = i < nc;
-        fold(in ? cv[i] : -INFINITY, in ? ci[i] : -1, in);
+    // kMergeBatch rounds' loads are issued together (one latency per batch, not per round):
+    // round u of batch k covers candidates 32 (warp + W (u + kMergeBatch k)) + lane, W = kMergeWarps
+    for (long long base = 32LL * warp; base < nc; base += 32LL * kMergeWarps * kMergeBatch) {
+        float v[kMergeBatch];
+        int id[kMergeBatch];
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; u++) {
+            const long long i = base + 32LL * kMergeWarps * u + lane;
+            v[u] = i < nc ? cv[i] : -INFINITY;
+            id[u] = i < nc ? ci[i] : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; u++) fold(v[u], id[u], base + 32LL * kMergeWarps * u + lane < nc);
     }
     sv[warp][lane] = tv;
     si[warp][lane] = ti;
