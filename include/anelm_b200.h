@@ -297,10 +297,10 @@ ANELM_API int anelm_gemm_bf16(const void* A, long long lda, const void* B, long 
  * W [vocab][hidden]^T (bf16, nn.Linear layout), values (fp32) and vocabulary indices sorted
  * descending — LMHeadArgmax of scripts/export_hybrid_chunks.py:409-421 (torch.topk(32) on the
  * ANE so that 2 x 32 values instead of the vocabulary's logits leave it), read by
- * serve_hybrid.py:283-307.  The logits are never written: the GEMM's epilogue keeps each row's
- * top-32 per 256-column vocabulary tile (candidates in `workspace`, at least
- * anelm_lm_head_topk_workspace_bytes(n, vocab) bytes, 16-byte aligned) and a second kernel
- * merges them.  Ties between equal logits may order differently than torch.topk. */
+ * serve_hybrid.py:283-307.  The logits are never written: each CTA keeps, per row, a running
+ * top-32 over the vocabulary tiles it streams (candidate lists in `workspace`, at least
+ * anelm_lm_head_topk_workspace_bytes(n, vocab) bytes, 16-byte aligned; the size depends on n)
+ * and a second kernel merges them.  Ties between equal logits may order differently than torch.topk. */
 ANELM_API size_t anelm_lm_head_topk_workspace_bytes(int n, int vocab);
 ANELM_API int anelm_lm_head_topk(const void* h, long long ldh, const void* W, long long ldw, int n, int vocab,
                                  int hidden, int k, float* top_vals, int* top_idx, void* workspace,
