@@ -779,6 +779,169 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
 }
 
+// LM head for 2-16 rows with the roles swapped: D^T [128 vocabulary rows][16] = W_tile . h^T, so the
+// streamed weights are the M = 128 operand (16 KB a k-step, kLsStages of them in flight) and the
+// rows of h the N = 16 operand, loaded once for the whole K and kept in shared memory.  TMEM lane =
+// vocabulary row, column = row of h: epilogue warp w reads its 32 vocabulary rows of a tile with
+// one tcgen05.ld and keeps, per row of h, a running top-32 spread over its lanes (a ballot over the
+// 32 logits, survivors inserted); its lists are candidate lists g 4 + w.  Warp 4: TMA (h once, then
+// the weight ring); warp 5: MMAs into one of kLsBufs 16-column accumulators per tile.
+constexpr int kLsN = 16, kLsBM = 128, kLsStages = 8, kLsBufs = 4;
+constexpr int kLsTileW = kLsBM * kGBK * 2;  // 16 KB
+constexpr int kLsTileH = kLsN * kGBK * 2;   // 2 KB: 16 rows x 128 bytes (two swizzle atoms)
+static size_t lm_swap_smem(int K) { return (size_t)kLsStages * kLsTileW + (size_t)((K + kGBK - 1) / kGBK) * kLsTileH + 256 + 1024; }
+
+__global__ void __launch_bounds__(kGThreads, 1)
+    lm_head_swap_topk_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmH,
+                             float* cand, int M, int N, int K, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int nk = (K + kGBK - 1) / kGBK;
+    uint8_t* sW = smem;
+    uint8_t* sH = smem + kLsStages * kLsTileW;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sH + nk * kLsTileH);
+    uint64_t* empty = full + kLsStages;
+    uint64_t* tfull = empty + kLsStages;  // [kLsBufs]
+    uint64_t* tfree = tfull + kLsBufs;    // [kLsBufs]
+    uint64_t* hfull = tfree + kLsBufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hfull + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, g = blockIdx.x;
+    const int ntile = (N + kLsBM - 1) / kLsBM;
+    const int my_tiles = g < ntile ? (ntile - 1 - g) / G + 1 : 0;
+    if (tid == 0) {
+        *abort = 0;
+        for (int s = 0; s < kLsStages; s++) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < kLsBufs; b++) {
+            tc::mbar_init(&tfull[b], 1);
+            tc::mbar_init(&tfree[b], 128);
+        }
+        tc::mbar_init(hfull, 1);
+        tc::fence_barrier_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, kLsBufs * kLsN);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) {  // TMA: the rows of h for every k-step (rows >= M zero-filled), then the weight ring
+            tc::prefetch_tmap(&tmW);
+            tc::prefetch_tmap(&tmH);
+            tc::mbar_arrive_expect_tx(hfull, (uint32_t)(nk * kLsTileH));
+            for (int kt = 0; kt < nk; kt++) tc::tma_load_2d(sH + kt * kLsTileH, &tmH, hfull, kt * kGBK, 0);
+            int s = 0;
+            uint32_t ph = 0;
+            long long q = 0;
+            for (int i = 0; i < my_tiles && !*abort; i++) {
+                const int r0 = (g + i * G) * kLsBM;
+                for (int kt = 0; kt < nk; kt++, q++) {
+                    if (q >= kLsStages && !tc::mbar_wait(&empty[s], ph ^ 1u, err, ANELM_ERR_TIMEOUT, abort)) break;
+                    tc::mbar_arrive_expect_tx(&full[s], kLsTileW);
+                    tc::tma_load_2d(sW + s * kLsTileW, &tmW, &full[s], kt * kGBK, r0);
+                    if (++s == kLsStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = idesc_bf16_f32(kLsBM, kLsN);
+            const uint32_t aW = (uint32_t)__cvta_generic_to_shared(sW), aH = (uint32_t)__cvta_generic_to_shared(sH);
+            bool ok = tc::mbar_wait(hfull, 0, err, ANELM_ERR_TIMEOUT, abort);
+            int s = 0;
+            uint32_t ph = 0;
+            for (int i = 0; i < my_tiles && ok; i++) {
+                const int b = i % kLsBufs;
+                if (i >= kLsBufs &&
+                    !tc::mbar_wait(&tfree[b], (uint32_t)((i / kLsBufs) - 1) & 1, err, ANELM_ERR_TIMEOUT, abort))
+                    break;
+                tc::tc_fence_after();
+                for (int kt = 0; kt < nk; kt++) {
+                    if (!tc::mbar_wait(&full[s], ph, err, ANELM_ERR_TIMEOUT, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < kGBK / 16; ks++)
+                        tc::mma_f16_ss(tmem + b * kLsN, tc::desc_kmajor_sw128(aW + s * kLsTileW + ks * 32),
+                                       tc::desc_kmajor_sw128(aH + kt * kLsTileH + ks * 32), idesc, (kt | ks) != 0);
+                    tc::mma_commit(&empty[s]);
+                    if (++s == kLsStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                tc::mma_commit(&tfull[b]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: warp w's 32 vocabulary rows of each tile (TMEM lanes 32 w + lane) ----------------
+        float lv[kLsN];
+        int li[kLsN];
+#pragma unroll
+        for (int j = 0; j < kLsN; j++) {
+            lv[j] = -INFINITY;
+            li[j] = -1;
+        }
+        const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+        for (int i = 0; i < my_tiles; i++) {
+            const int b = i % kLsBufs;
+            if (!tc::mbar_wait(&tfull[b], (uint32_t)(i / kLsBufs) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
+            tc::tc_fence_after();
+            uint32_t x[kLsN];
+            tc::tmem_ld16(trow + b * kLsN, x);
+            tc::tmem_ld_wait();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&tfree[b]);  // accumulator b read: the MMAs may reuse it
+            const int v0 = (g + i * G) * kLsBM + 32 * warp;  // this warp's first vocabulary row
+            const bool in = v0 + lane < N;
+#pragma unroll
+            for (int j = 0; j < kLsN; j++) {
+                if (j < M) {  // warp-uniform
+                    const float v = __uint_as_float(x[j]);
+                    const float thr = __shfl_sync(0xffffffffu, lv[j], 31);
+                    unsigned mk = __ballot_sync(0xffffffffu, in && v > thr);
+                    while (mk) {
+                        const int src = __ffs(mk) - 1;
+                        mk &= mk - 1;
+                        const float xv = __shfl_sync(0xffffffffu, v, src);
+                        warp_topk_insert_if(lv[j], li[j], true, xv, v0 + src, lane);
+                    }
+                }
+            }
+        }
+        const long long lists = (long long)G * 4;
+#pragma unroll
+        for (int j = 0; j < kLsN; j++) {
+            if (j < M) {
+                const long long slot = (long long)j * lists + (long long)g * 4 + warp;
+                cand[slot * kTopK + lane] = lv[j];
+                reinterpret_cast<int*>(cand + (long long)M * lists * kTopK)[slot * kTopK + lane] = li[j];
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kLsBufs * kLsN);
+    }
+}
+
 }  // namespace
 
 namespace {
@@ -961,9 +1124,18 @@ static int lm_gemv_groups(int vocab) {
 // candidate lists cost the merge more than the split saves (4 rows 286 -> 297 us with four copies)
 static int lm_rep(int n) { return n <= 8 ? 1 : n <= 32 ? 4 : n <= 64 ? 2 : 1; }
 
+// CTAs of the swapped few-row path: one per SM, at most one per 128 vocabulary rows
+static int lm_swap_groups(int vocab) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return std::max(1, std::min((vocab + kLsBM - 1) / kLsBM, sms));
+}
+
 size_t lm_head_topk_workspace_bytes(int n, int vocab) {
-    const int tc_lists = lm_groups(n, vocab) * lm_rep(n);
-    const int g = n <= kLmGemvRows ? std::max(tc_lists, lm_gemv_groups(vocab)) : tc_lists;
+    int g = lm_groups(n, vocab) * lm_rep(n);                      // tensor-core path
+    if (n <= kLmGemvRows) g = std::max(g, lm_gemv_groups(vocab));  // CUDA-core path
+    if (n <= kLsN) g = std::max(g, lm_swap_groups(vocab) * 4);      // swapped path
     return (size_t)n * g * kTopK * 8;
 }
 
@@ -983,6 +1155,21 @@ int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long l
             static_cast<float*>(workspace), n, vocab, hidden);
         lm_topk_merge_kernel<<<n, 32 * kMergeWarps, 0, stream>>>(static_cast<const float*>(workspace), n, G, k, top_vals,
                                                               top_idx);
+        return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
+    }
+    if (n <= kLsN && lm_swap_smem(hidden) <= (size_t)kGSmemMax) {
+        // 2-16 rows: weights as the M operand, h resident in shared memory (see lm_head_swap_topk_kernel)
+        CUtensorMap mW, mH;
+        if (!make_bf16_map(&mW, W, (uint64_t)vocab, (uint64_t)hidden, (uint64_t)ldw, kLsBM) ||
+            !make_bf16_map(&mH, h, (uint64_t)n, (uint64_t)hidden, (uint64_t)ldh, kLsN))
+            return ANELM_ERR_CUDA;
+        const int smem = (int)lm_swap_smem(hidden);
+        cudaFuncSetAttribute(lm_head_swap_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        const int G = lm_swap_groups(vocab);
+        lm_head_swap_topk_kernel<<<G, kGThreads, smem, stream>>>(mW, mH, static_cast<float*>(workspace), n, vocab,
+                                                                hidden, err);
+        lm_topk_merge_kernel<<<n, 32 * kMergeWarps, 0, stream>>>(static_cast<const float*>(workspace), n, G * 4, k,
+                                                              top_vals, top_idx);
         return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
     }
     const int rep = lm_rep(n);

@@ -32,7 +32,7 @@ def _check(n, vocab, hidden, k, seed):
     assert all(len(set(r.tolist())) == k for r in idx)  # no index twice
 
 
-@pytest.mark.parametrize("n", [1, 4, 5, 17, 33, 64, 65, 256])
+@pytest.mark.parametrize("n", [1, 4, 5, 16, 17, 33, 64, 65, 256])
 def test_lm_head_top32_qwen_vocab(n):
     """One row takes the CUDA-core path (weights streamed, per-warp running top-32), more rows the
     tensor-core path: 9-32 rows with four copies of the row block in the A tile (each epilogue warp
