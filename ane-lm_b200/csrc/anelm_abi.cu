@@ -118,7 +118,10 @@ struct anelm_ctx {
     float* rope_cos = nullptr;
     float* rope_sin = nullptr;
     int* err = nullptr;
-    std::vector<char> fresh;    // [n_fa][max_seqs]: ring known to be empty (prefill may start it)
+    // [n_fa][max_seqs]: host record of each ring's len, kept by every call that changes it (reset,
+    // import / set_meta, decode: one append per row, prefill: n appends, each capped at the
+    // capacity).  Prefill sizes its old-token rows from it; the device's len / start stay the truth.
+    std::vector<int> len_h;
     void* prefill_ws = nullptr;  // prefill staging (Q, K, V, V^T, sigmoid(gate)), grown on demand
     size_t prefill_ws_bytes = 0;
     void* gdn_prefill_ws = nullptr;  // DeltaNet prefill staging (chunk operands), grown on demand
@@ -512,7 +515,7 @@ ANELM_API int anelm_create(const anelm_config* cfg, int device, anelm_ctx** out)
         cudaMemcpy(ctx->kv_cap, ctx->cap_h.data(), c.max_seqs * sizeof(int), cudaMemcpyHostToDevice))
         return bail(fail(ANELM_ERR_CUDA, "metadata upload failed"));
     if (ctx->n_fa > 0) {
-        ctx->fresh.assign((size_t)ctx->n_fa * c.max_seqs, 1);
+        ctx->len_h.assign((size_t)ctx->n_fa * c.max_seqs, 0);
         CALLOC(ctx->kv_len, (size_t)ctx->n_fa * c.max_seqs);
         CALLOC(ctx->kv_start, (size_t)ctx->n_fa * c.max_seqs);
         const size_t row = (size_t)c.num_kv_heads * c.head_dim;
@@ -627,7 +630,7 @@ ANELM_API int anelm_reset(anelm_ctx* ctx, int seq) {
         CUDA_TRY(cudaMemset(ctx->v_pool[f] + a * row, 0, (e - a) * row * 2));
         CUDA_TRY(cudaMemset(ctx->kv_len + (size_t)f * c.max_seqs + s0, 0, (s1 - s0) * 4));
         CUDA_TRY(cudaMemset(ctx->kv_start + (size_t)f * c.max_seqs + s0, 0, (s1 - s0) * 4));
-        for (int s = s0; s < s1; s++) ctx->fresh[(size_t)f * c.max_seqs + s] = 1;
+        for (int s = s0; s < s1; s++) ctx->len_h[(size_t)f * c.max_seqs + s] = 0;
     }
     const size_t st = (size_t)c.lin_num_val_heads * c.lin_key_dim * c.lin_val_dim;
     for (int g = 0; g < ctx->n_gdn; g++) {
@@ -688,7 +691,7 @@ ANELM_API int anelm_kv_import(anelm_ctx* ctx, int layer, int seq, const float* k
     }
     CUDA_TRY(cudaMemcpy(ctx->kv_len + (size_t)f * c.max_seqs + seq, &len, 4, cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(ctx->kv_start + (size_t)f * c.max_seqs + seq, &start, 4, cudaMemcpyHostToDevice));
-    ctx->fresh[(size_t)f * c.max_seqs + seq] = (len == 0);
+    ctx->len_h[(size_t)f * c.max_seqs + seq] = len;
     return ANELM_OK;
 }
 
@@ -720,7 +723,7 @@ ANELM_API int anelm_kv_set_meta(anelm_ctx* ctx, int layer, int seq, int len, int
     const int f = ctx->fa_idx[layer];
     CUDA_TRY(cudaMemcpy(ctx->kv_len + (size_t)f * ctx->cfg.max_seqs + seq, &len, 4, cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(ctx->kv_start + (size_t)f * ctx->cfg.max_seqs + seq, &start, 4, cudaMemcpyHostToDevice));
-    ctx->fresh[(size_t)f * ctx->cfg.max_seqs + seq] = (len == 0);
+    ctx->len_h[(size_t)f * ctx->cfg.max_seqs + seq] = len;
     return ANELM_OK;
 }
 
@@ -821,7 +824,10 @@ static int fa_launch(anelm_ctx* ctx, const anelm_plan* plan, int layer, const vo
     if (ctx->cfg.qk_norm_in_core && !ctx->fa_w_set[ctx->fa_idx[layer]])
         return fail(ANELM_ERR_STATE, "full-attention weights of layer %d not set", layer);
     DeviceGuard dg(ctx->device);
-    for (int s : plan->seq_h) ctx->fresh[(size_t)ctx->fa_idx[layer] * ctx->cfg.max_seqs + s] = 0;
+    for (int s : plan->seq_h) {  // one append per row (a linear cache's length follows the position: unknown here)
+        int& len = ctx->len_h[(size_t)ctx->fa_idx[layer] * ctx->cfg.max_seqs + s];
+        len = ctx->cfg.kv_mode == ANELM_KV_LINEAR ? ctx->cap_h[s] : std::min(len + 1, ctx->cap_h[s]);
+    }
     FaDecodeParams p = fa_params(ctx, layer, plan, proj, proj_dtype, pos_arr, pos_scalar, out, out_dtype);
     return launch_status(launch_fa_decode(p, ctx->cfg.head_dim, plan->n_blocks, static_cast<cudaStream_t>(stream)),
                          "fa_decode");
@@ -1081,15 +1087,18 @@ ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, in
     if (c.qk_norm_in_core && !ctx->fa_w_set[ctx->fa_idx[layer]])
         return fail(ANELM_ERR_STATE, "full-attention weights of layer %d not set", layer);
     const int f = ctx->fa_idx[layer];
+    // old-token rows: the first new token of a sequence sees min(len, capacity - 1) old tokens
+    int P = 0;
     for (int s : plan->seq_h) {
-        if (!ctx->fresh[(size_t)f * c.max_seqs + s])
-            return fail(ANELM_ERR_STATE, "prefill needs an empty ring (sequence %d, layer %d): reset it first", s, layer);
-        if (n_tokens > ctx->cap_h[s])
-            return fail(ANELM_ERR_CAPACITY, "%d prompt tokens exceed the ring capacity %d of sequence %d", n_tokens,
+        const int len = ctx->len_h[(size_t)f * c.max_seqs + s];
+        if (c.kv_mode == ANELM_KV_LINEAR && (len != 0 || n_tokens > ctx->cap_h[s]))
+            return fail(ANELM_ERR_CAPACITY, "linear-cache prefill fills an empty cache of %d positions (sequence %d)",
                         ctx->cap_h[s], s);
+        P = std::max(P, std::min(len, ctx->cap_h[s] - 1));
     }
+    P = (P + 127) / 128 * 128;
     DeviceGuard dg(ctx->device);
-    const size_t need = fa_prefill_workspace_bytes(plan->n, n_tokens, c.num_q_heads, c.num_kv_heads, c.head_dim);
+    const size_t need = fa_prefill_workspace_bytes(plan->n, n_tokens, P, c.num_q_heads, c.num_kv_heads, c.head_dim);
     {
         std::lock_guard<std::mutex> lk(ctx->mu);
         if (need > ctx->prefill_ws_bytes) {
@@ -1116,6 +1125,7 @@ ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, in
     p.rope_mode = c.rope_mode;
     p.gate = c.attn_output_gate;
     p.start_pos = start_pos;
+    p.P = P;
     p.q_norm = ctx->q_norm[f];
     p.k_norm = ctx->k_norm[f];
     p.rope_cos = ctx->rope_cos;
@@ -1130,13 +1140,17 @@ ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, in
     p.seq_ids = plan->seq_d;
     p.kv_len = ctx->kv_len + (size_t)f * c.max_seqs;
     p.kv_start = ctx->kv_start + (size_t)f * c.max_seqs;
+    p.kv_cap = ctx->kv_cap;
     p.out = out;
     p.out_dtype = out_dtype;
     p.out_stride = (long long)c.num_q_heads * c.head_dim;
     p.err = ctx->err;
     const int rc = launch_fa_prefill(p, ctx->prefill_ws, c.head_dim, static_cast<cudaStream_t>(stream));
     if (rc) return launch_status(rc, "fa_prefill");
-    for (int s : plan->seq_h) ctx->fresh[(size_t)f * c.max_seqs + s] = 0;
+    for (int s : plan->seq_h) {
+        int& len = ctx->len_h[(size_t)f * c.max_seqs + s];
+        len = (int)std::min<long long>((long long)len + n_tokens, ctx->cap_h[s]);
+    }
     return ANELM_OK;
 }
 

@@ -1,17 +1,27 @@
 // Causal prefill for the Qwen3.5 gated full-attention core (sm_100a, tcgen05 + TMA).
 //
 // Replaces the per-token prefill loop of the reference (qwen3_5.cpp:1205-1217,
-// serve_hybrid.py:368-370), which runs forward_full_attn_from_proj
-// (qwen3_5.cpp:944-1002) once per prompt token: for each token t, QK RMSNorm,
-// RoPE at position start_pos + t, ring append at slot t, softmax attention over
-// tokens [0, t], sigmoid gate.  The result is the same set of outputs, computed
-// as one causal attention.
+// serve_hybrid.py:368-370; the chunks of forward_batch, qwen3_5.cpp:1164-1217, called by
+// generate.cpp:57-73 at a running start_pos), which runs forward_full_attn_from_proj
+// (qwen3_5.cpp:944-1002) once per prompt token: for each token t, QK RMSNorm, RoPE at
+// position start_pos + t, ring append (qwen3_5.cpp:974-986: slot start + len, or the
+// oldest slot once the ring is full), softmax attention over the ring, sigmoid gate.  The
+// result is the same set of outputs, computed as one causal attention over [old | new]
+// keys: new token t sees the ring's old tokens and the new tokens 0..t, at most `capacity`
+// tokens in all (the ring's window), so prompts may continue a non-empty ring and may be
+// longer than the ring.
 //
-// Two launches:
+// Three launches:
+//   fa_prefill_gather_kernel  per sequence: snapshot of the ring's len / start / capacity and
+//                           copy of the old tokens the first new token still sees (the last
+//                           min(len, capacity - 1), in the ring's logical order) into the key
+//                           rows ahead of the new tokens;
 //   fa_prefill_prep_vec_kernel  per token: RMSNorm + RoPE of the q and k heads (same arithmetic
 //                           as the decode prologue), fp16 Q [B][Hq][n_pad][D], K and V
-//                           [B][Hkv][n_pad][D], sigmoid(gate) for the epilogue, and the ring
-//                           append (slot t, len = n, start = 0).  Warp per 256-element segment,
+//                           [B][Hkv][P + n_pad][D] (new token t at row P + t), sigmoid(gate) for
+//                           the epilogue, and the ring append (slot (start + len + t) mod
+//                           capacity for the tokens that stay in the ring; final len / start as
+//                           the per-token updates leave them).  Warp per 256-element segment,
 //                           16-byte lanes (fa_prefill_prep_kernel: same work for any shape);
 //   fa_prefill_kernel       one CTA per (q head, 128-row query tile, sequence); within a sequence
 //                           all heads' longest causal tiles are dispatched first; 11 warps:
@@ -78,6 +88,71 @@ __device__ __forceinline__ float rcp_approx(float x) {
 }
 
 
+// ---- the ring of one sequence as it was before this call (written by the gather kernel) ----
+struct RingSnap {
+    int len, start, cap, Pb;  // Pb: old tokens in key rows [P - Pb, P)
+};
+
+__device__ __forceinline__ RingSnap ring_snap(const FaPrefillParams& p, int b) {
+    const int4 m = *reinterpret_cast<const int4*>(p.meta + 4 * b);
+    return {m.x, m.y, m.z, m.w};
+}
+
+// Ring slot of new token t: the update of qwen3_5.cpp:974-983 applied once per token puts token t
+// at slot start + len + t modulo the capacity; -1 if a later token of this call takes that slot.
+__device__ __forceinline__ int ring_slot(const RingSnap& r, int n, int t) {
+    if (t < n - r.cap) return -1;
+    return (int)(((long long)r.start + r.len + t) % r.cap);
+}
+
+// len / start after the n appends of this call (the same per-token updates).
+__device__ __forceinline__ void ring_finish(const FaPrefillParams& p, const RingSnap& r, int seq) {
+    const long long total = (long long)r.len + p.n;
+    p.kv_len[seq] = (int)(total < r.cap ? total : r.cap);
+    p.kv_start[seq] = (int)(((long long)r.start + (total > r.cap ? total - r.cap : 0)) % r.cap);
+}
+
+// One CTA per 64 key rows (at least one per sequence).  Takes the snapshot of sequence b's ring
+// and copies its last Pb tokens, oldest first from `start` as gqa_attention reads them
+// (cpu_ops.cpp:161-163), into key rows [P - Pb, P); rows of the first key tile below P - Pb are
+// zeroed (an attention tile reads them, masked, and P V needs them finite).  Runs before the
+// prep appends to the ring, so it reads the old tokens only.
+__global__ void __launch_bounds__(256) fa_prefill_gather_kernel(const FaPrefillParams p) {
+    const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int seq = p.seq_ids ? p.seq_ids[b] : 0;
+    const int len = p.kv_len[seq], start = p.kv_start[seq], cap = p.kv_cap[seq];
+    int Pb = min(len, cap - 1);
+    if (Pb > p.P) {  // the host sizes P from its record of every ring's length; that record was wrong
+        if (blockIdx.x == 0 && threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, ANELM_ERR_STATE);
+        Pb = p.P;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<int4*>(p.meta + 4 * b) = make_int4(len, start, cap, Pb);
+    const int first = (p.P - Pb) / kBN * kBN;
+    const int r1 = min(p.P, ((int)blockIdx.x + 1) * 64);
+    const long long base = p.kv_base[seq];
+    const int vecs = p.Hkv * (kD / 8);  // 16-byte vectors per slot row [Hkv][kD]
+    for (int r = (int)blockIdx.x * 64 + warp; r < r1; r += 8) {
+        if (r < first) continue;
+        const bool old = r >= p.P - Pb;
+        long long src = 0;
+        if (old) {
+            const int j = len - (p.P - r);  // logical index, 0 = oldest
+            src = (base + (long long)(((long long)start + j) % cap)) * p.Hkv * kD;
+        }
+        for (int e = lane; e < vecs; e += 32) {
+            const int kh = e / (kD / 8), c = e % (kD / 8);
+            const long long dst = (((long long)b * p.Hkv + kh) * p.n_tot + r) * kD + 8 * c;
+            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+            if (old) {
+                kv = *reinterpret_cast<const uint4*>(p.k_pool + src + (long long)e * 8);
+                vv = *reinterpret_cast<const uint4*>(p.v_pool + src + (long long)e * 8);
+            }
+            *reinterpret_cast<uint4*>(p.Kh + dst) = kv;
+            *reinterpret_cast<uint4*>(p.Vh + dst) = vv;
+        }
+    }
+}
+
 // Single-stage K and V buffers: a 64 KB load (~0.4 us) hides behind the other operand's
 // MMAs (~1.4 us per tile).  Each barrier is used once per tile (K, V) or once per use of
 // a TMEM buffer (S_FULL, P_FULL, PV_DONE), so no barrier runs two phases ahead of a waiter.
@@ -106,12 +181,12 @@ __global__ void __launch_bounds__(256) fa_prefill_prep_kernel(const FaPrefillPar
     const int Hq = p.Hq, Hkv = p.Hkv;
     const int nvec = Hq + Hkv;
     const long long qrow = ((long long)b * Hq) * p.n_pad + t;
-    const long long krow = ((long long)b * Hkv) * p.n_pad + t;
+    const long long krow = ((long long)b * Hkv) * p.n_tot + p.P + t;
     if (t >= p.n) {  // padding rows: finite zeros
         for (int idx = tid; idx < Hq * kD; idx += 256)
             p.Qh[(qrow + (long long)(idx / kD) * p.n_pad) * kD + idx % kD] = __float2half_rn(0.f);
         for (int idx = tid; idx < Hkv * kD; idx += 256) {
-            const long long o = (krow + (long long)(idx / kD) * p.n_pad) * kD + idx % kD;
+            const long long o = (krow + (long long)(idx / kD) * p.n_tot) * kD + idx % kD;
             p.Kh[o] = __float2half_rn(0.f);
             p.Vh[o] = __float2half_rn(0.f);
         }
@@ -158,17 +233,19 @@ __global__ void __launch_bounds__(256) fa_prefill_prep_kernel(const FaPrefillPar
         __syncthreads();
     }
     const int seq = p.seq_ids ? p.seq_ids[b] : 0;
-    const long long slot_row = p.kv_base ? (p.kv_base[seq] + t) * Hkv : 0;
+    const RingSnap rs = ring_snap(p, b);
+    const int slot = ring_slot(rs, p.n, t);
+    const long long slot_row = slot >= 0 ? (p.kv_base[seq] + slot) * Hkv : -1;
     for (int idx = tid; idx < Hq * kD; idx += 256)
         p.Qh[(qrow + (long long)(idx / kD) * p.n_pad) * kD + idx % kD] = __float2half_rn(xs[idx]);
     for (int idx = tid; idx < Hkv * kD; idx += 256) {
         const int v = idx / kD, i = idx % kD;
         const __half kh = __float2half_rn(xs[(Hq + v) * kD + i]);
         const __half vh = __float2half_rn(vs[idx]);
-        const long long o = (krow + (long long)v * p.n_pad) * kD + i;
+        const long long o = (krow + (long long)v * p.n_tot) * kD + i;
         p.Kh[o] = kh;
         p.Vh[o] = vh;
-        if (p.k_pool) {  // ring append at slot t (qwen3_5.cpp:984-986)
+        if (slot_row >= 0) {  // ring append (qwen3_5.cpp:984-986)
             p.k_pool[(slot_row + v) * kD + i] = kh;
             p.v_pool[(slot_row + v) * kD + i] = vh;
         }
@@ -180,10 +257,7 @@ __global__ void __launch_bounds__(256) fa_prefill_prep_kernel(const FaPrefillPar
             sg[idx] = __float2half_rn(1.0f / (1.0f + expf(-g)));
         }
     }
-    if (t == 0 && tid == 0 && p.kv_len) {
-        p.kv_len[seq] = p.n;
-        p.kv_start[seq] = 0;
-    }
+    if (t == 0 && tid == 0) ring_finish(p, rs, seq);
 }
 
 // Same work as fa_prefill_prep_kernel, organised for bandwidth: one CTA per token, each warp owns
@@ -262,9 +336,9 @@ __device__ __forceinline__ void prep_segment(const FaPrefillParams& p, float (&v
     } else {
         const int kh = is_k ? s - 2 * Hq : s - 2 * Hq - Hkv;
         const uint4 hv = half8(v);
-        const long long o = (((long long)b * Hkv + kh) * p.n_pad + t) * kD + e0;
+        const long long o = (((long long)b * Hkv + kh) * p.n_tot + p.P + t) * kD + e0;
         *reinterpret_cast<uint4*>((is_k ? p.Kh : p.Vh) + o) = hv;
-        if (p.k_pool)  // ring append at slot t (qwen3_5.cpp:984-986)
+        if (slot_row >= 0)  // ring append (qwen3_5.cpp:984-986)
             *reinterpret_cast<uint4*>((is_k ? p.k_pool : p.v_pool) + (slot_row + kh) * kD + e0) = hv;
     }
 }
@@ -275,7 +349,7 @@ __device__ __forceinline__ void prep_zero_row(const FaPrefillParams& p, int b, i
     for (int h = warp; h < p.Hq; h += nwarps)
         *reinterpret_cast<uint4*>(p.Qh + (((long long)b * p.Hq + h) * p.n_pad + t) * kD + e0) = z;
     for (int h = warp; h < p.Hkv; h += nwarps) {
-        const long long o = (((long long)b * p.Hkv + h) * p.n_pad + t) * kD + e0;
+        const long long o = (((long long)b * p.Hkv + h) * p.n_tot + p.P + t) * kD + e0;
         *reinterpret_cast<uint4*>(p.Kh + o) = z;
         *reinterpret_cast<uint4*>(p.Vh + o) = z;
     }
@@ -295,7 +369,9 @@ __global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPre
                       ((long long)b * p.n + t) * p.proj_stride * dtype_bytes(p.proj_dtype);
     const int pos = p.start_pos + t;
     const int seq = p.seq_ids ? p.seq_ids[b] : 0;
-    const long long slot_row = p.kv_base ? (p.kv_base[seq] + t) * Hkv : 0;
+    const RingSnap rs = ring_snap(p, b);
+    const int slot = ring_slot(rs, p.n, t);
+    const long long slot_row = slot >= 0 ? (p.kv_base[seq] + slot) * Hkv : -1;
     const auto cs = [&](int j, float& c, float& sn) { rope_cs_pf(p, pos, j, c, sn); };
     for (int s0 = warp; s0 < nseg; s0 += 8 * kPrepBatch) {
         float x[kPrepBatch][8];
@@ -309,10 +385,7 @@ __global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPre
             prep_segment(p, x[i], s, lane, b, t, slot_row, p.q_norm + e0, p.k_norm + e0, cs);
         }
     }
-    if (t == 0 && threadIdx.x == 0 && p.kv_len) {
-        p.kv_len[seq] = p.n;
-        p.kv_start[seq] = 0;
-    }
+    if (t == 0 && threadIdx.x == 0) ring_finish(p, rs, seq);
 }
 
 // Streaming form of the prep for 16-bit projections: a persistent CTA walks the tokens
@@ -504,13 +577,15 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
     const bool rot = e0 < p.rot_dim;
     const int hl = half >> 3;  // lanes per rotary half (rotate-half partner lane = lane +- hl)
     const int partner = lane < hl ? lane + hl : lane - hl;
-    const long long q_hstride = (long long)n_pad * kD;  // Q / K / V: [B][H][n_pad][kD]
+    const long long q_hstride = (long long)n_pad * kD;    // Q: [B][Hq][n_pad][kD]
+    const long long k_hstride = (long long)p.n_tot * kD;  // K / V: [B][Hkv][P + n_pad][kD]
     // job j of the token -> segment: with Hq a multiple of 8, blocks of 8 jobs alternate q heads and
     // gates (q 0-7, gate 0-7, q 8-15, ...), so each warp gets the same number of RMSNorm + RoPE
     // segments (the warps' slowest bounds the stage's release); k and v heads follow
     const bool mix = (Hq & 7) == 0;
-    int cur_b = -1, seq = 0;  // the sequence of row b and its pool base, reloaded when b changes
+    int cur_b = -1, seq = 0;  // the sequence of row b, its pool base and ring snapshot, reloaded when b changes
     long long kv0 = 0;
+    RingSnap rs{0, 0, 1, 0};
     int b = blockIdx.x / n_pad, t = blockIdx.x % n_pad, s = 0;
     uint32_t ph = 0;
     while (b < p.B) {
@@ -523,16 +598,18 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
             if (b != cur_b) {
                 cur_b = b;
                 seq = p.seq_ids ? p.seq_ids[b] : 0;
-                kv0 = p.kv_base ? p.kv_base[seq] : 0;
+                kv0 = p.kv_base[seq];
+                rs = ring_snap(p, b);
             }
             const bool tab = p.rot_dim > 0 && p.rope_cos && pos >= 0 && pos < p.rope_len;
             float c[8], sg[8];
             prep_rope_lane<kHalf>(p, tab, reinterpret_cast<const float*>(st + rope_off), pos, lane, c, sg);
             __half* qrow = p.Qh + ((long long)b * Hq * n_pad + t) * kD + e0;
-            __half* krow = p.Kh + ((long long)b * Hkv * n_pad + t) * kD + e0;
-            __half* vrow = p.Vh + ((long long)b * Hkv * n_pad + t) * kD + e0;
+            __half* krow = p.Kh + ((long long)b * Hkv * p.n_tot + p.P + t) * kD + e0;
+            __half* vrow = p.Vh + ((long long)b * Hkv * p.n_tot + p.P + t) * kD + e0;
             __half* grow = p.SG ? p.SG + ((long long)b * n + t) * Hq * kD + e0 : nullptr;
-            const long long pool = (p.kv_base ? (kv0 + t) * Hkv * kD : 0) + e0;  // ring slot row (qwen3_5.cpp:984-986)
+            const int slot = ring_slot(rs, n, t);  // ring append (qwen3_5.cpp:984-986), if the token stays
+            const long long pool = slot >= 0 ? (kv0 + slot) * Hkv * kD + e0 : -1;
             for (int j = warp; j < nseg; j += kPrepWarps) {
                 int sgm = j;
                 if (mix && j < 2 * Hq) {
@@ -556,19 +633,16 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
                     const int kh = sgm - 2 * Hq;
                     prep_qk_lane<kHalf>(p, x, kn, c, sg, rot, partner);
                     const uint4 hv = half8(x);
-                    *reinterpret_cast<uint4*>(krow + kh * q_hstride) = hv;
-                    if (p.k_pool) *reinterpret_cast<uint4*>(p.k_pool + pool + kh * kD) = hv;  // ring append
+                    *reinterpret_cast<uint4*>(krow + kh * k_hstride) = hv;
+                    if (pool >= 0) *reinterpret_cast<uint4*>(p.k_pool + pool + kh * kD) = hv;  // ring append
                 } else {  // v head
                     const int vh = sgm - 2 * Hq - Hkv;
                     const uint4 hv = half8(x);
-                    *reinterpret_cast<uint4*>(vrow + vh * q_hstride) = hv;
-                    if (p.k_pool) *reinterpret_cast<uint4*>(p.v_pool + pool + vh * kD) = hv;
+                    *reinterpret_cast<uint4*>(vrow + vh * k_hstride) = hv;
+                    if (pool >= 0) *reinterpret_cast<uint4*>(p.v_pool + pool + vh * kD) = hv;
                 }
             }
-            if (t == 0 && warp == 0 && lane == 0 && p.kv_len) {
-                p.kv_len[seq] = n;
-                p.kv_start[seq] = 0;
-            }
+            if (t == 0 && warp == 0 && lane == 0) ring_finish(p, rs, seq);
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&empty[s]);
@@ -607,8 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int G = p.Hq / p.Hkv;
     const int kvh = h / G;
     const int q0 = qt * kBM;
-    const int kv_end = min(q0 + kBM, p.n);
-    const int nT = (kv_end + kBN - 1) / kBN;
+    const int P = p.P;
 
     if (tid == 0) {
         *abort = 0;
@@ -626,11 +699,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // launched as a programmatic dependent of the prep: Q, K, V and sigmoid(gate) are read only
     // after the prep grid has completed and its writes are visible (a no-op for a plain launch)
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Keys of query row q (new token q) among the [old | new] key rows: [lo(q), P + q] with
+    // lo(q) = max(P - Pb, P + q + 1 - capacity) -- the old tokens still in the ring and, once
+    // more than `capacity` tokens precede it, only the last `capacity` (qwen3_5.cpp:974-983).
+    const RingSnap rs = ring_snap(p, b);
+    const int lo_base = P - rs.Pb, lo_win = P + 1 - rs.cap;
+    const int lo_max = max(lo_base, lo_win + q0 + kBM - 1);  // largest lower bound of the tile's rows
+    const int kt0 = max(lo_base, lo_win + q0) / kBN;         // first key tile (row q0 has the smallest bound)
+    const int nT = (P + min(q0 + kBM, p.n) + kBN - 1) / kBN - kt0;
 
     if (warp == kWarpK || warp == kWarpV) {
         // ---------------- TMA producers: one warp streams Q then K (then the gate tile), one streams V ----------------
         if (lane == 0 && nT > 0) {
-            const int krow0 = (b * p.Hkv + kvh) * p.n_pad;
+            const int krow0 = (b * p.Hkv + kvh) * p.n_tot + kt0 * kBN;
             if (warp == kWarpK) {
                 tc::prefetch_tmap(&tmQ);
                 tc::prefetch_tmap(&tmK);
@@ -721,13 +802,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int s = j & 1, u = j >> 1;
             tc::mbar_wait(&bars[S_FULL + s], u & 1, p.err, ANELM_ERR_TIMEOUT, abort);
             tc::tc_fence_after();
-            const int k0 = j * kBN + hf * 64;
+            const int k0 = (kt0 + j) * kBN + hf * 64;  // key row of x[0]
             tc::tmem_ld64(trow + s * kBN + hf * 64, x);
             tc::tmem_ld_wait();
-            if ((k0 + 63 > q0) || (k0 + 64 > p.n)) {  // diagonal or ragged: masked scores become -inf (exp2 -> 0)
+            if ((k0 + 63 > P + q0) || (k0 + 64 > P + p.n) || (k0 < lo_max)) {
+                // diagonal, ragged end or window edge: masked scores become -inf (exp2 -> 0)
+                const int lo_r = max(lo_base, lo_win + qpos);
 #pragma unroll
                 for (int c = 0; c < 64; c++)
-                    if (k0 + c > qpos || k0 + c >= p.n) x[c] = -INFINITY;
+                    if (k0 + c > P + qpos || k0 + c >= P + p.n || k0 + c < lo_r) x[c] = -INFINITY;
             }
             float m4[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
@@ -744,10 +827,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool grow = (m_used == -INFINITY) || ((m_new - m_used) * sl2 > 8.0f);
             if (j > 0 && __any_sync(0xffffffffu, grow)) {
                 // O is stable once P V of the previous tile completed; this half rescales O columns
-                // [128 hf, 128 hf + 128)
+                // [128 hf, 128 hf + 128).  A row with no visible key yet (max still -inf) has O = 0.
                 tc::mbar_wait(&bars[PV_DONE + ((j - 1) & 1)], ((j - 1) >> 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
                 tc::tc_fence_after();
-                const float alpha = grow ? exp2f((m_used - m_new) * sl2) : 1.0f;
+                const float alpha = (grow && m_new != -INFINITY) ? exp2f((m_used - m_new) * sl2) : 1.0f;
 #pragma unroll 1
                 for (int ch = 0; ch < 4; ch++) {  // 32 columns at a time: the S row stays in registers
                     uint32_t o[32];
@@ -761,7 +844,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l *= alpha;
             }
             if (grow) m_used = m_new;
-            const float nm = -m_used * sl2;
+            const float nm = m_used == -INFINITY ? 0.f : -m_used * sl2;  // all -inf: exp2 gives P = 0
             // P = exp2((s - m) * log2(e)/sqrt(d)) as fp16 pairs: half hf fills columns [32 hf, 32 hf + 32) of
             // the S buffer (both halves read their S columns before the pair barrier above)
             float s4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -917,26 +1000,33 @@ bool make_map_rows(CUtensorMap* m, int dtype, const void* base, uint64_t cols, u
 
 }  // namespace
 
-size_t fa_prefill_workspace_bytes(int B, int n, int Hq, int Hkv, int head_dim) {
+size_t fa_prefill_workspace_bytes(int B, int n, int P, int Hq, int Hkv, int head_dim) {
     const long long n_pad = (n + kBM - 1) / kBM * kBM;
-    // fp16 Q, K, V and sigmoid(gate) [B][n][Hq][D]
-    return (size_t)B * n_pad * head_dim * 2 * (2 * (size_t)Hq + 2 * (size_t)Hkv);
+    // fp16 Q [B][Hq][n_pad][D], K and V [B][Hkv][P + n_pad][D], sigmoid(gate) [B][n][Hq][D]; the
+    // ring snapshots [B][4] ints
+    return (size_t)B * head_dim * 2 * (2 * (size_t)Hq * n_pad + 2 * (size_t)Hkv * (P + n_pad)) + (size_t)B * 16;
 }
 
 int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream) {
-    if (head_dim != kD) return ANELM_ERR_UNSUPPORTED;
+    if (head_dim != kD || p.P < 0 || p.P % kBN || !p.kv_len || !p.kv_start || !p.kv_cap || !p.kv_base ||
+        !p.k_pool || !p.v_pool)
+        return ANELM_ERR_UNSUPPORTED;
     p.n_pad = (p.n + kBM - 1) / kBM * kBM;
-    const long long nq = (long long)p.B * p.Hq * p.n_pad * kD, nk = (long long)p.B * p.Hkv * p.n_pad * kD;
+    p.n_tot = p.P + p.n_pad;
+    const long long nq = (long long)p.B * p.Hq * p.n_pad * kD, nk = (long long)p.B * p.Hkv * p.n_tot * kD;
     __half* ws = static_cast<__half*>(workspace);
     p.Qh = ws;
     p.Kh = ws + nq;
     p.Vh = p.Kh + nk;
     p.SG = nullptr;
+    p.meta = reinterpret_cast<int*>(p.Vh + nk + nq);  // after sigmoid(gate) (<= nq halves), 16-byte aligned
     CUtensorMap mQ, mK, mV;
     if (!make_map(&mQ, p.Qh, (uint64_t)p.B * p.Hq * p.n_pad, kD, kBM) ||
-        !make_map(&mK, p.Kh, (uint64_t)p.B * p.Hkv * p.n_pad, kD, kBN) ||
-        !make_map(&mV, p.Vh, (uint64_t)p.B * p.Hkv * p.n_pad, kD, kBN))
+        !make_map(&mK, p.Kh, (uint64_t)p.B * p.Hkv * p.n_tot, kD, kBN) ||
+        !make_map(&mV, p.Vh, (uint64_t)p.B * p.Hkv * p.n_tot, kD, kBN))
         return ANELM_ERR_CUDA;
+    // ring snapshots and the old tokens still visible, before the prep appends to the rings
+    fa_prefill_gather_kernel<<<dim3(std::max(1, (p.P + 63) / 64), p.B), 256, 0, stream>>>(p);
     // TMA epilogue: 16-bit output with a 16-byte aligned base and row stride; sigmoid(gate) as fp16
     // [B][n][Hq * D] after V in the workspace
     CUtensorMap mG = mQ, mO = mQ;

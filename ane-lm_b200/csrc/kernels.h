@@ -82,7 +82,12 @@ struct GdnDecodeParams {
 
 // Causal prefill of a fresh ring: B sequences of n tokens each.
 struct FaPrefillParams {
-    int B, n, n_pad, Hq, Hkv, rot_dim;
+    // n new tokens per sequence (n_pad: rounded up to the 128-row tile).  The attention keys of
+    // sequence b are [old | new]: the last P_b <= P tokens its ring held before the call (the ones
+    // the first new token still sees: P_b = min(len, capacity - 1)), right-aligned in rows
+    // [P - P_b, P), then the n new tokens in rows [P, P + n); P is a multiple of 128 and
+    // n_tot = P + n_pad rows per (sequence, kv head).
+    int B, n, n_pad, Hq, Hkv, rot_dim, P, n_tot;
     float rope_theta, rms_eps;
     int qk_norm, rope_mode, gate, start_pos;
     const float* q_norm;
@@ -103,6 +108,8 @@ struct FaPrefillParams {
     const int* seq_ids;    // [B]
     int* kv_len;
     int* kv_start;
+    const int* kv_cap;     // [max_seqs] ring capacity per sequence
+    int* meta;             // [B][4] (workspace): len, start, capacity, P_b of each ring before the call
     void* out;             // [B][n][out_stride]
     int out_dtype;
     long long out_stride;
@@ -163,7 +170,7 @@ size_t gdn_prefill_workspace_bytes(int B, int n, int Hk, int Hv, int C, bool lay
 int launch_gdn_prefill(GdnPrefillParams p, void* workspace, cudaStream_t stream);
 int launch_gated_delta_chunked(GdnPrefillParams p, void* workspace, cudaStream_t stream);
 
-size_t fa_prefill_workspace_bytes(int B, int n, int Hq, int Hkv, int head_dim);
+size_t fa_prefill_workspace_bytes(int B, int n, int P, int Hq, int Hkv, int head_dim);
 int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream);
 
 int launch_fa_decode(const FaDecodeParams& p, int head_dim, int n_blocks, cudaStream_t stream);

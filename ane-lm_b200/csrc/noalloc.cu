@@ -17,9 +17,13 @@
 // nothing ordering them) race on it.
 //
 // Host code must not pass the array's name to a kernel: on the host it is only
-// a stand-in symbol.  The device address is fetched once per device with
-// cudaGetSymbolAddress, on the first call made while that device is current;
-// make that first call before any stream capture.
+// a stand-in symbol.  The device address is fetched with cudaGetSymbolAddress on
+// the first call made while a device is current; make that first call before any
+// stream capture.  The address is cached per device together with the CUDA
+// context that was current: after a device reset (a new primary context, in which
+// the library's module and the array are loaded again) the next call looks the
+// address up again instead of writing through a stale pointer.
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -40,6 +44,21 @@ static __device__ __align__(256) unsigned char g_gqa_scratch[ANELM_GQA_NOALLOC_S
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch_dev[kMaxDevices] = {nullptr};
+CUcontext g_scratch_ctx[kMaxDevices] = {nullptr};
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library links no libcuda).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<CtxGetCurrentFn>(f);
+    }();
+    return fn;
+}
 
 int noalloc_fail(int code, const char* msg) {
     set_last_error(msg);
@@ -64,7 +83,12 @@ int scratch_for_current_device(void** out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
         return noalloc_fail(ANELM_ERR_CUDA, "no current CUDA device");
+    // A cached address is used only while the context it was taken in is still the current one.
+    CUcontext cur = nullptr;
+    CtxGetCurrentFn get = ctx_get_current();
     std::lock_guard<std::mutex> lk(g_mu);
+    if (get && g_scratch_dev[dev] && (get(&cur) != CUDA_SUCCESS || cur != g_scratch_ctx[dev]))
+        g_scratch_dev[dev] = nullptr;  // another context than the one the address was taken in
     if (!g_scratch_dev[dev]) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_gqa_scratch);
@@ -72,7 +96,10 @@ int scratch_for_current_device(void** out) {
             set_last_error((std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e)).c_str());
             return ANELM_ERR_CUDA;
         }
+        cur = nullptr;
+        if (get && get(&cur) != CUDA_SUCCESS) cur = nullptr;
         g_scratch_dev[dev] = p;
+        g_scratch_ctx[dev] = cur;
     }
     *out = g_scratch_dev[dev];
     return ANELM_OK;

@@ -1,25 +1,32 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 attention core (one JSON line on rank 0).
 
-Default workload: batched serving decode of a Qwen3.5-4B
-shaped 32-layer stack (24 Gated DeltaNet + 8 gated full-attention layers, 3:1),
-256 concurrent sequences per GPU with ragged KV lengths ~ U[512, 32768] (fp16
-N(0,1)) and per-sequence fp32 DeltaNet state N(0, 0.1).  One step = one decode
-token for every sequence through all 32 layers' attention cores, each layer one
-call of the C ABI (anelm_full_attn_decode / anelm_deltanet_decode) on the
-layer's synthetic projection rows.  Sequences are independent: under torchrun
-each rank owns its own 256 sequences (weak scaling, no data-path collective).
+Default workload: batched serving decode of a Qwen3.5-4B shaped 32-layer
+stack (24 Gated DeltaNet + 8 gated full-attention layers, 3:1), 256 concurrent sequences with
+ragged KV lengths ~ U[512, 32768] (fp16 N(0,1)) and per-sequence fp32 DeltaNet state
+N(0, 0.1).  One step = one decode token for every sequence through all 32 layers' attention
+cores, each layer one call of the C ABI (anelm_full_attn_decode / anelm_deltanet_decode) on the
+layer's synthetic projection rows.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
-    python bench.py --workload fa_b1|gdn_b1      # BASELINE configs 1 / 2 (single sequence)
-    python bench.py --workload fa_prefill [--prefill-batch 8]
-    python bench.py --workload gdn_prefill
+Multi-GPU (torchrun, one process per GPU): the 256 sequences are split over the ranks by
+greedy longest-first bin packing of their per-step bytes (strong scaling, the headline at
+N > 1; no data-path collective).  The line also carries a weak-scaling measurement (256
+sequences on every rank) under "weak".
+
+At N = 1 the line carries BASELINE configs 1-4 under "workloads" (single-sequence decode of
+each block, causal prefill at B = 1 and 8, chunked DeltaNet prefill), each with its roofline
+fraction, clocks and the reference CPU core timed on the same inputs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--no-workloads]
+    python bench.py --workload fa_b1|gdn_b1      # BASELINE configs 1 / 2 alone
+    python bench.py --workload fa_prefill [--prefill-batch 8]   # BASELINE config 3 alone
+    python bench.py --workload gdn_prefill                      # BASELINE config 4 alone
     python bench.py --workload proj|lm_head [--seqs 256]       # the steps next to the core
     python bench.py --workload gdn_layer [--seqs 256]          # one DeltaNet decode layer (ncu size)
 
-The reference arm (--impl reference) times the reference's own CPU attention
-core (core/cpu_ops.cpp compiled unmodified + the qwen3_5.cpp glue, oracle/_ref)
-on the host cores over a bounded sample of the same workload.
+The reference arm (--impl reference) times the reference's own CPU attention core
+(core/cpu_ops.cpp compiled unmodified + the qwen3_5.cpp glue, oracle/_ref) on the host cores
+over a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -31,7 +38,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
 
@@ -42,7 +48,7 @@ sys.path.insert(0, REPO)
 sys.path.insert(0, os.path.join(REPO, "ane-lm_b200"))
 
 PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
-FALLBACK_HBM = 6650.0
+FALLBACK_HBM, FALLBACK_BF16 = 6650.0, 1590.0
 
 # Qwen3.5-4B attention-core shape (serve_hybrid.py:32-47)
 HQ, HKV, HD, ROT = 16, 4, 256, 64
@@ -54,6 +60,9 @@ FA_PROJ = HQ * 2 * HD + 2 * HKV * HD
 GDN_PROJ = C_CONV + HV * DV + 2 * HV
 FA_OUT = HQ * HD
 GDN_OUT = HV * DV
+GLOBAL_SEQS = 256
+METRIC = "decode attn-core tok/s (batched serving decode, 32-layer 3:1 DeltaNet:attention stack)"
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
 def env_rank():
@@ -61,15 +70,26 @@ def env_rank():
 
 
 def peaks():
+    """(HBM GB/s, bf16 TFLOP/s, kind) from MEASURED_PEAKS.json, else the pool's fallback."""
     try:
         d = json.load(open(PEAKS))
-        return float(d["hbm_gbs"]), "measured"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     except Exception:
-        return FALLBACK_HBM, "fallback"
+        return FALLBACK_HBM, FALLBACK_BF16, "fallback"
 
 
 def kv_lengths(n, seed=0):
     return np.random.default_rng(seed).integers(512, 32768, size=n, endpoint=True).astype(np.int64)
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return ""
 
 
 # ------------------------------------------------------------------ clocks
@@ -95,7 +115,7 @@ class ClockSampler:
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
-            return
+            return self
         # nvidia-smi takes a while to start: wait (up to 5 s) for its first sample so that the
         # samples cover the timed region that follows
         t_end = time.time() + 5.0
@@ -103,6 +123,7 @@ class ClockSampler:
             if os.path.getsize(self.path) > 0:
                 break
             time.sleep(0.02)
+        return self
 
     def stop(self):
         if not self.proc:
@@ -128,12 +149,25 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-# ------------------------------------------------------------------ GPU arm
+def hbm_roof(gbs, peak, kind, kernel, nbytes):
+    return {"bound": "hbm", "kernel": kernel, "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(gbs / peak, 4), "peak_kind": kind, "traffic": None, "algorithmic_bytes_per_launch": nbytes}
 
-def setup_serving(torch, n_seqs, lengths, slack, seed, device):
+
+def tensor_roof(tf, peak, kind, kernel, flops):
+    return {"bound": "tensor", "kernel": kernel, "achieved": round(tf, 2), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(tf / peak, 4), "peak_kind": kind, "traffic": None, "algorithmic_flops_per_launch": flops}
+
+
+# ------------------------------------------------------------------ serving decode (config 5)
+
+def setup_serving(torch, lengths, slack, seed, device):
+    """A context holding every sequence of `lengths` (KV rings filled to their length, random
+    DeltaNet states) and one projection / output buffer per layer for up to len(lengths) rows."""
     import anelm_b200 as ab
     from anelm_b200.core import Context
 
+    n_seqs = len(lengths)
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     caps = [int(L) + slack for L in lengths]
@@ -175,232 +209,338 @@ def setup_serving(torch, n_seqs, lengths, slack, seed, device):
             ctx.deltanet_state_write(l, s, st[(s + l) % 16])
     torch.cuda.synchronize(device)
     del st
-    plan = ctx.plan(list(range(n_seqs)))
     projs = []
     for t in LAYER_TYPES:
         w = FA_PROJ if t == ab.LAYER_FULL_ATTN else GDN_PROJ
         projs.append(torch.randn(n_seqs, w, generator=g, device=device, dtype=torch.float16))
     outs = [torch.empty(n_seqs, FA_OUT if t == ab.LAYER_FULL_ATTN else GDN_OUT, device=device,
                         dtype=torch.float16) for t in LAYER_TYPES]
-    return ctx, plan, projs, outs
+    return ctx, projs, outs
 
 
-def step_bytes(lengths, step_offset):
-    """Algorithmic HBM bytes of ONE full-attention layer launch and ONE DeltaNet layer
-    launch over all sequences at `step_offset` tokens past the initial lengths."""
-    n = len(lengths)
-    Lcur = lengths + step_offset
-    fa = 0
-    fa += int((2 * Lcur * HKV * HD * 2).sum())          # K and V rows read (old tokens)
-    fa += n * (FA_PROJ * 2 + FA_OUT * 2 + 2 * HKV * HD * 2)  # projection in, output, appended k/v
-    gdn = n * (2 * HV * DK * DV * 4                      # state read + write
-               + C_CONV * 16                             # conv ring: 3 old inputs read + 1 written
-               + GDN_PROJ * 2 + GDN_OUT * 2) + C_CONV * 16  # projection in, output; conv weights
+def layer_bytes(kv_lens):
+    """Algorithmic HBM bytes of ONE full-attention layer launch and ONE DeltaNet layer launch
+    over sequences whose rings hold kv_lens tokens before the step."""
+    n = len(kv_lens)
+    fa = int((2 * np.asarray(kv_lens) * HKV * HD * 2).sum())   # K and V rows read (old tokens)
+    fa += n * (FA_PROJ * 2 + FA_OUT * 2 + 2 * HKV * HD * 2)   # projection in, output, appended k/v
+    gdn = n * (2 * HV * DK * DV * 4                           # state read + write
+               + C_CONV * 16                                  # conv ring: 3 old inputs read + 1 written
+               + GDN_PROJ * 2 + GDN_OUT * 2) + C_CONV * 16    # projection in, output; conv weights
     return fa, gdn
 
 
-def run_gpu(args):
-    import torch
-    import torch.distributed as dist
+class ServeRun:
+    """One rank's serving decode: a context over all sequences it may run and host-side ring
+    lengths, so each timed loop knows its positions and bytes."""
 
-    rank, world, local = env_rank()
-    if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    hbm_peak, peak_kind = peaks()
+    def __init__(self, torch, device, lengths, slack, seed):
+        self.torch, self.device = torch, device
+        self.ctx, self.projs, self.outs = setup_serving(torch, lengths, slack, seed, device)
+        self.cur = np.asarray(lengths, np.int64).copy()  # tokens in each ring
+        self.stream = torch.cuda.current_stream(device)
+        self.fa_layers = [l for l, t in enumerate(LAYER_TYPES) if t == 1]
 
-    if args.workload == "fa_prefill":
-        return run_prefill(args, torch, device)
-    if args.workload == "gdn_prefill":
-        return run_gdn_prefill(args, torch, device, hbm_peak, peak_kind)
-    if args.workload in ("proj", "lm_head"):
-        return run_proj(args, torch, device, hbm_peak, peak_kind)
-    if args.workload == "gdn_layer":
-        return run_gdn_layer(args, torch, device, hbm_peak, peak_kind)
-    if args.workload != "serve":
-        return run_gpu_single(args, torch, device, hbm_peak, peak_kind)
+    def positions(self, ids, n_steps, pinned=False):
+        """Absolute positions [n_steps][len(ids)] int32 of the next n_steps tokens of `ids`: on
+        the device, or in pinned host memory for the end-to-end loop to copy in step by step."""
+        pos = self.torch.from_numpy(np.stack([self.cur[ids] + k for k in range(n_steps)]).astype(np.int32))
+        return pos.pin_memory() if pinned else pos.to(self.device)
 
-    n = args.seqs
-    lengths = kv_lengths(n, 0)
-    slack = args.warmup + args.steps + 16
-    ctx, plan, projs, outs = setup_serving(torch, n, lengths, slack, 1000 + rank, device)
-    import anelm_b200 as ab
+    def loop(self, ids, n_steps, pos, events=False, host_io=None):
+        """n_steps decode steps of the sequences `ids` at positions pos (from `positions`); returns
+        per-step per-layer event pairs if `events`.  host_io = (host_in, host_out, copy_stream):
+        every step first copies its positions and each layer's projection rows from pinned host
+        memory and copies each layer's outputs back (the copies run on copy_stream, overlapped
+        with earlier layers)."""
+        torch = self.torch
+        import anelm_b200 as ab
 
-    pos = [torch.tensor(lengths + k, dtype=torch.int32, device=device) for k in range(args.warmup + args.steps + 1)]
-    fa_layers = [l for l, t in enumerate(LAYER_TYPES) if t == ab.LAYER_FULL_ATTN]
-    stream = torch.cuda.current_stream(device)
-
-    def step(k, ev=None):
-        for l, t in enumerate(LAYER_TYPES):
-            if t == ab.LAYER_FULL_ATTN:
-                if ev is not None:
-                    ev[l][0].record(stream)
-                ctx.full_attn_decode(plan, l, projs[l], pos[k], outs[l])
-                if ev is not None:
-                    ev[l][1].record(stream)
+        plan = self._plan(ids)
+        n = len(ids)
+        comp = self.stream
+        evs = []
+        if host_io:
+            host_in, host_out, copy = host_io
+            ev_in = [torch.cuda.Event() for _ in LAYER_TYPES]
+            ev_out = [torch.cuda.Event() for _ in LAYER_TYPES]
+            pos_dev = torch.empty((n_steps, n), dtype=torch.int32, device=self.device)
+        for k in range(n_steps):
+            ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in LAYER_TYPES] \
+                if events else None
+            if host_io:
+                copy.wait_stream(comp)
+                with torch.cuda.stream(copy):
+                    pos_dev[k].copy_(pos[k], non_blocking=True)
+                    for l in range(N_LAYERS):
+                        self.projs[l][:n].copy_(host_in[l][:n], non_blocking=True)
+                        ev_in[l].record(copy)
+                pk = pos_dev[k]
             else:
-                if ev is not None:
-                    ev[l][0].record(stream)
-                ctx.deltanet_decode(plan, l, projs[l], outs[l])
-                if ev is not None:
-                    ev[l][1].record(stream)
+                pk = pos[k]
+            for l, t in enumerate(LAYER_TYPES):
+                if host_io:
+                    comp.wait_event(ev_in[l])
+                if ev:
+                    ev[l][0].record(comp)
+                if t == ab.LAYER_FULL_ATTN:
+                    self.ctx.full_attn_decode(plan, l, self.projs[l][:n], pk, self.outs[l][:n])
+                else:
+                    self.ctx.deltanet_decode(plan, l, self.projs[l][:n], self.outs[l][:n])
+                if ev:
+                    ev[l][1].record(comp)
+                if host_io:
+                    ev_out[l].record(comp)
+                    with torch.cuda.stream(copy):
+                        copy.wait_event(ev_out[l])
+                        host_out[l][:n].copy_(self.outs[l][:n], non_blocking=True)
+            if host_io:
+                comp.wait_stream(copy)
+            if ev:
+                evs.append((self.cur[ids].copy(), ev))
+            self.cur[ids] += 1
+        return evs
 
-    for k in range(args.warmup):
-        step(k)
-    torch.cuda.synchronize(device)
+    def _plan(self, ids):
+        key = tuple(int(i) for i in ids)
+        if getattr(self, "_plans", None) is None:
+            self._plans = {}
+        if key not in self._plans:
+            self._plans[key] = self.ctx.plan(list(key))
+        return self._plans[key]
+
+    def close(self):
+        for p in (getattr(self, "_plans", None) or {}).values():
+            p.close()
+        self.ctx.close()
+
+
+def barrier(world):
     if world > 1:
+        import torch.distributed as dist
         dist.barrier()
-    ev_steps = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in LAYER_TYPES]
-                for _ in range(args.steps)]
-    clocks = ClockSampler(local)
-    clocks.start()
+
+
+def timed_serving(sr, ids, args, world, local, hbm_peak, peak_kind):
+    """Warm-up, then exactly args.steps timed steps of the sequences `ids` (barrier +
+    synchronize on both sides, device events, max over ranks).  Returns the measurement dict."""
+    torch = sr.torch
+    from anelm_b200.shard import max_over_ranks
+
+    sr.loop(ids, args.warmup, sr.positions(ids, args.warmup))
+    pos = sr.positions(ids, args.steps)
+    torch.cuda.synchronize(sr.device)
+    barrier(world)
+    clocks = ClockSampler(local).start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(device)
-    t0.record(stream)
-    for k in range(args.steps):
-        step(args.warmup + k, ev_steps[k])
-    t1.record(stream)
-    torch.cuda.synchronize(device)
+    torch.cuda.synchronize(sr.device)
+    t0.record(sr.stream)
+    evs = sr.loop(ids, args.steps, pos, events=True)
+    t1.record(sr.stream)
+    torch.cuda.synchronize(sr.device)
     ck = clocks.stop()
-    ms = t0.elapsed_time(t1)
-    if world > 1:
-        tt = torch.tensor([ms], device=device)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
-        dist.barrier()
-    err = ctx.device_error()
-    assert err == 0, f"device reported status {err}"
-
-    # per-kernel times (events on the launching stream)
-    fa_ms = [ev_steps[k][l][0].elapsed_time(ev_steps[k][l][1]) for k in range(args.steps) for l in fa_layers]
-    gdn_ms = [ev_steps[k][l][0].elapsed_time(ev_steps[k][l][1]) for k in range(args.steps)
-              for l, t in enumerate(LAYER_TYPES) if t == 0]
-    n_fa = len(fa_layers)
-    n_gdn = N_LAYERS - n_fa
-    fa_b = gdn_b = 0  # per-launch bytes summed over the timed steps
-    for k in range(args.steps):
-        a, b = step_bytes(lengths, args.warmup + k)
+    ms = max_over_ranks(t0.elapsed_time(t1), sr.device)
+    barrier(world)
+    fa_ms, gdn_ms, fa_b, gdn_b = [], [], 0, 0
+    for lens, ev in evs:
+        a, b = layer_bytes(lens)
         fa_b += a
         gdn_b += b
-    fa_per_launch = fa_b / args.steps
-    gdn_per_launch = gdn_b / args.steps
+        for l, t in enumerate(LAYER_TYPES):
+            (fa_ms if t == 1 else gdn_ms).append(ev[l][0].elapsed_time(ev[l][1]))
+    fa_per_launch, gdn_per_launch = fa_b / args.steps, gdn_b / args.steps
     fa_gbs = fa_per_launch / (statistics.mean(fa_ms) * 1e-3) / 1e9
     gdn_gbs = gdn_per_launch / (statistics.mean(gdn_ms) * 1e-3) / 1e9
-    ms_step = ms / args.steps
-    tok_s = n * world / (ms_step * 1e-3)
-    step_gb = (n_fa * fa_per_launch + n_gdn * gdn_per_launch) / 1e9
+    n_fa = len(sr.fa_layers)
+    return {"ms": ms, "ms_step": ms / args.steps, "clocks": ck,
+            "step_gb": (n_fa * fa_per_launch + (N_LAYERS - n_fa) * gdn_per_launch) / 1e9,
+            "roofline": hbm_roof(fa_gbs, hbm_peak, peak_kind, "fa_decode_kernel<256>", int(fa_per_launch)),
+            "roofline_gdn": hbm_roof(gdn_gbs, hbm_peak, peak_kind, "gdn_decode_kernel", int(gdn_per_launch)),
+            "kernel_ms_per_step": {"fa_decode": round(n_fa * statistics.mean(fa_ms), 3),
+                                   "gdn_decode": round((N_LAYERS - n_fa) * statistics.mean(gdn_ms), 3)}}
 
-    # e2e: same step through the C ABI with host (pinned) buffers, copies inside the timed region
-    e2e = run_e2e(args, torch, ctx, plan, projs, outs, pos, device, world)
 
+def e2e_serving(sr, ids, args, world):
+    """The same loop as the device-timed one (same calls, same per-layer events, positions
+    advancing the same way) with every step's projection rows copied in from pinned host memory
+    and its outputs copied back; host clock around synchronised ends, max over ranks."""
+    torch = sr.torch
+    from anelm_b200.shard import max_over_ranks
+
+    n = len(ids)
+    host_in = [p[:n].cpu().pin_memory() for p in sr.projs]
+    host_out = [torch.empty(o[:n].shape, dtype=o.dtype).pin_memory() for o in sr.outs]
+    copy = torch.cuda.Stream(sr.device)
+    io = (host_in, host_out, copy)
+    sr.loop(ids, 1, sr.positions(ids, 1, pinned=True), events=True, host_io=io)
+    pos = sr.positions(ids, args.steps, pinned=True)
+    torch.cuda.synchronize(sr.device)
+    barrier(world)
+    t = time.perf_counter()
+    sr.loop(ids, args.steps, pos, events=True, host_io=io)
+    torch.cuda.synchronize(sr.device)
+    dt = max_over_ranks(time.perf_counter() - t, sr.device) / args.steps
+    barrier(world)
+    h2d = sum(h.numel() * h.element_size() for h in host_in) + pos[0].numel() * 4
+    return dt, h2d, sum(h.numel() * h.element_size() for h in host_out)
+
+
+def run_serve(args, torch, device, world, rank, local):
+    import anelm_b200 as ab  # noqa: F401  (fail loudly here if the library is missing)
+    from anelm_b200.shard import assign_sequences, seq_step_bytes
+
+    hbm_peak, _, peak_kind = peaks()
+    lengths = kv_lengths(GLOBAL_SEQS, 0)
+    n_runs = 2 if world > 1 else 1
+    slack = n_runs * (args.warmup + 2 * args.steps + 1) + 16
+    sr = ServeRun(torch, device, lengths, slack, 1000 + rank)
+    costs = [seq_step_bytes(int(L), 8, HKV, HD, 24, HV) for L in lengths]
+    mine = assign_sequences(costs, world, rank, mode="strong")
+    mine_np = np.asarray(mine, np.int64)
+    m = timed_serving(sr, mine_np, args, world, local, hbm_peak, peak_kind)
+    dt, h2d, d2h = e2e_serving(sr, mine_np, args, world)
+    err = sr.ctx.device_error()
+    assert err == 0, f"device reported status {err}"
+    tok_s = GLOBAL_SEQS / (m["ms_step"] * 1e-3)
+    rank_bytes = np.zeros(world)
+    for r in range(world):
+        rank_bytes[r] = sum(costs[i] for i in assign_sequences(costs, world, r, mode="strong"))
     result = {
-        "metric": "decode attn-core tok/s (batched serving decode, 32-layer 3:1 DeltaNet:attention stack)",
-        "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic",
+        "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(m["ms_step"], 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "BASELINE cfg5: batched serving decode, Qwen3.5-4B-shaped 32 layers (24 GDN + 8 FA)",
-                   "seqs_per_gpu": n, "global_batch": n * world, "kv_len": "U[512,32768] seed 0",
+                   "global_batch": GLOBAL_SEQS, "seqs_on_rank0": len(mine), "kv_len": "U[512,32768] seed 0",
                    "kv_storage": "fp16 ring [slots][4][256]", "state": "fp32 [32][128][128] per seq per GDN layer",
                    "proj_io": "fp16", "Hq": HQ, "Hkv": HKV, "head_dim": HD, "rot_dim": ROT, "Hv": HV, "Hk": HK,
-                   "parallelism": f"sequence-sharded x{world}, no collective",
-                   "l2": f"inputs {step_gb:.1f} GB/step > 126 MB L2 (no flush needed)"},
-        "hbm_gbs_step": round(step_gb / (ms_step * 1e-3), 1),
-        "roofline": {"bound": "hbm", "kernel": "fa_decode_kernel<256>", "achieved": round(fa_gbs, 1),
-                     "peak": hbm_peak, "unit": "GB/s", "frac": round(fa_gbs / hbm_peak, 4),
-                     "peak_kind": peak_kind, "traffic": None,
-                     "algorithmic_bytes_per_launch": int(fa_per_launch)},
-        "roofline_gdn": {"bound": "hbm", "kernel": "gdn_decode_kernel", "achieved": round(gdn_gbs, 1),
-                         "peak": hbm_peak, "unit": "GB/s", "frac": round(gdn_gbs / hbm_peak, 4),
-                         "algorithmic_bytes_per_launch": int(gdn_per_launch)},
-        "e2e": e2e,
-        "kernel_ms_per_step": {"fa_decode": round(n_fa * statistics.mean(fa_ms), 3),
-                               "gdn_decode": round(n_gdn * statistics.mean(gdn_ms), 3)},
+                   "parallelism": (f"{GLOBAL_SEQS} sequences split over {world} GPUs by greedy longest-first bin "
+                                   f"packing of per-step bytes, no collective" if world > 1 else "1 GPU"),
+                   "rank_bytes_imbalance": round(float(rank_bytes.max() / rank_bytes.mean()), 4),
+                   "l2": f"inputs {m['step_gb']:.1f} GB/step on rank 0 > 126 MB L2 (no flush needed)"},
+        "hbm_gbs_step": round(m["step_gb"] / (m["ms_step"] * 1e-3), 1),
+        "roofline": m["roofline"], "roofline_gdn": m["roofline_gdn"],
+        "e2e": {"value": round(GLOBAL_SEQS / dt, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h), "steps": args.steps,
+                "note": "the device-timed loop plus, every step, fp16 projection rows in from pinned host memory "
+                        "and outputs back (side-stream copies); host clock, synchronised ends, max over ranks"},
+        "kernel_ms_per_step": m["kernel_ms_per_step"],
         "gpu_launches": args.steps * N_LAYERS,
-        "clocks": ck,
+        "clocks": m["clocks"],
     }
     if args.traffic_json and os.path.exists(args.traffic_json):
         tr = json.load(open(args.traffic_json))
-        result["roofline"]["traffic"] = tr.get("fa_decode_bytes_per_launch")
+        ratio = tr.get("fa_decode_traffic_over_algorithmic")
+        if ratio:
+            result["roofline"]["traffic"] = int(ratio * m["roofline"]["algorithmic_bytes_per_launch"])
+            result["roofline"]["traffic_kind"] = ("scaled: ncu DRAM read+write / algorithmic bytes of a "
+                                                  "32-sequence capture, times this launch's algorithmic bytes")
+    if world > 1:
+        # weak scaling beside it: every rank decodes all 256 sequences of its own context
+        w = timed_serving(sr, np.arange(GLOBAL_SEQS), args, world, local, hbm_peak, peak_kind)
+        result["weak"] = {"value": round(GLOBAL_SEQS * world / (w["ms_step"] * 1e-3), 1), "unit": "tok/s",
+                          "seqs_per_gpu": GLOBAL_SEQS, "ms_per_step": round(w["ms_step"], 4),
+                          "roofline_frac": w["roofline"]["frac"], "roofline_gdn_frac": w["roofline_gdn"]["frac"],
+                          "clocks": w["clocks"]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_reference_serving(args.cpu_seconds, threads=None, kind="reference")
-    if rank == 0:
-        print(json.dumps(result), flush=True)
-    plan.close()
-    ctx.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    sr.close()
+    return result
 
 
-def run_e2e(args, torch, ctx, plan, projs, outs, pos, device, world):
-    """The step with projections coming from pinned HOST memory and outputs going back
-    to the host every step (copies on a side stream, overlapped with earlier layers)."""
-    import anelm_b200 as ab
-    import torch.distributed as dist
+# ------------------------------------------------------------------ BASELINE configs 1-4
 
-    host_in = [p.cpu().pin_memory() for p in projs]
-    host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
-    comp = torch.cuda.current_stream(device)
-    copy = torch.cuda.Stream(device)
-    ev_in = [torch.cuda.Event() for _ in LAYER_TYPES]
-    ev_out = [torch.cuda.Event() for _ in LAYER_TYPES]
-    h2d = sum(h.numel() * h.element_size() for h in host_in)
-    d2h = sum(h.numel() * h.element_size() for h in host_out)
-    base = args.warmup + args.steps  # positions continue after the device-resident run
-    # each e2e step appends one more token; capacity slack covers warmup + steps + 16
-
-    def step(k):
-        with torch.cuda.stream(copy):
-            for l in range(N_LAYERS):
-                projs[l].copy_(host_in[l], non_blocking=True)
-                ev_in[l].record(copy)
-        for l, t in enumerate(LAYER_TYPES):
-            comp.wait_event(ev_in[l])
-            if t == ab.LAYER_FULL_ATTN:
-                ctx.full_attn_decode(plan, l, projs[l], pos[min(k, len(pos) - 1)], outs[l])
-            else:
-                ctx.deltanet_decode(plan, l, projs[l], outs[l])
-            ev_out[l].record(comp)
-            with torch.cuda.stream(copy):
-                copy.wait_event(ev_out[l])
-                host_out[l].copy_(outs[l], non_blocking=True)
-        copy.synchronize()
-
-    n_steps = max(1, min(args.steps, 8))
-    step(base)
+def graph_replay_us(torch, device, calls, reps_per_graph, replays):
+    """Captures `calls` (a list of closures, one launch each) into one CUDA graph and returns the
+    device time per call over `replays` replays (after a warm-up replay)."""
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            for c in calls:
+                c()
     torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    t = time.perf_counter()
-    for k in range(n_steps):
-        step(base)
+    graph.replay()
     torch.cuda.synchronize(device)
-    dt = (time.perf_counter() - t) / n_steps
-    if world > 1:
-        tt = torch.tensor([dt], device=device)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        dt = float(tt.item())
-    n = plan.n
-    return {"value": round(n * world / dt, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "steps": n_steps,
-            "note": "host pinned projections in / outputs out each step, timed on the host clock"}
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(replays):
+        graph.replay()
+    t1.record()
+    torch.cuda.synchronize(device)
+    us = t0.elapsed_time(t1) * 1e3 / (replays * len(calls))
+    del graph
+    return us
 
 
-def run_prefill(args, torch, device):
-    """causal full-attention prefill, Qwen3.5-4B shape, 4096 tokens, bf16 inputs."""
+def wl_decode_b1(args, torch, device, which):
+    """BASELINE config 1 (attention decode, 0.8B shape, ring of 2048 fp16) or config 2 (DeltaNet
+    decode, 16 heads, fp32 state): the single-sequence entry point, one call per token.  The
+    timed calls rotate over `n_copies` independent sequences whose data together exceed the 126 MB
+    L2, so every call streams its KV / state from HBM; calls replay from a CUDA graph."""
     import anelm_b200 as ab
     from anelm_b200.core import Context
 
-    try:
-        peak = float(json.load(open(PEAKS))["bf16_tflops"])
-        peak_kind = "measured"
-    except Exception:
-        peak, peak_kind = 1590.0, "fallback"
+    hbm_peak, _, peak_kind = peaks()
     rng = np.random.default_rng(0)
     g = torch.Generator(device=device)
     g.manual_seed(0)
-    B, n = args.prefill_batch, args.prefill_len
+    if which == "fa":
+        n_copies = 64                                        # 64 x 4.2 MB = 268 MB
+        ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_FULL_ATTN], max_seqs=n_copies,
+                      kv_capacity=2048)
+        ctx.set_full_attn_weights(0, (1 + 0.02 * rng.standard_normal(256)).astype(np.float32),
+                                  (1 + 0.02 * rng.standard_normal(256)).astype(np.float32))
+        for s in range(n_copies):
+            kv = torch.randn(2048, 2, 256, generator=g, device=device, dtype=torch.float16)
+            ctx.kv_write(0, s, 0, kv, kv.flip(0).contiguous())
+            ctx.kv_set_meta(0, s, 2048, 0)
+        projs = torch.randn(n_copies, ctx.fa_proj_dim, generator=g, device=device, dtype=torch.float16)
+        outs = torch.empty(n_copies, ctx.fa_out_dim, device=device, dtype=torch.float16)
+        calls = [(lambda s=s: ctx.full_attn_from_proj(0, s, projs[s], 3000, outs[s])) for s in range(n_copies)]
+        nbytes = 2 * 2048 * 2 * 256 * 2 + ctx.fa_proj_dim * 2 + ctx.fa_out_dim * 2 + 2 * 2 * 256 * 2
+        metric, kname = "attention decode tok/s (cfg1, 0.8B shape, KV 2048 fp16, batch 1)", "fa_decode_kernel<256,1>"
+    else:
+        n_copies = 128                                       # 128 x 2.3 MB = 295 MB
+        ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_LINEAR_ATTN], max_seqs=n_copies)
+        C = ctx.conv_channels
+        ctx.set_deltanet_weights(0, (0.5 * rng.standard_normal((C, 4))).astype(np.float16).astype(np.float32),
+                                 np.ones(16, np.float32), np.zeros(16, np.float32), np.ones(128, np.float32))
+        for s in range(n_copies):
+            ctx.deltanet_state_write(0, s, (0.1 * torch.randn(16, 128, 128, generator=g, device=device)).contiguous())
+        projs = torch.randn(n_copies, ctx.gdn_proj_dim, generator=g, device=device, dtype=torch.float16)
+        outs = torch.empty(n_copies, ctx.gdn_out_dim, device=device, dtype=torch.float16)
+        calls = [(lambda s=s: ctx.deltanet_from_proj(0, s, projs[s], outs[s])) for s in range(n_copies)]
+        nbytes = 2 * 16 * 128 * 128 * 4 + C * 16 + C * 16 + ctx.gdn_proj_dim * 2 + ctx.gdn_out_dim * 2
+        metric, kname = "DeltaNet decode tok/s (cfg2, 16 heads, fp32 state, batch 1)", "gdn_decode_kernel<1,8,128>"
+    for c in calls:  # the first call per sequence builds its batch-1 plan (allocations: not inside a capture)
+        c()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index or 0).start()
+    replays = 20
+    us = graph_replay_us(torch, device, calls, len(calls), replays)
+    ck = clocks.stop()
+    err = ctx.device_error()
+    ctx.close()
+    assert err == 0, f"device reported status {err}"
+    gbs = nbytes / (us * 1e-6) / 1e9
+    cpu = cpu_reference_decode_b1(which, args.cpu_seconds_wl)
+    return {"metric": metric, "value": round(1e6 / us, 1), "unit": "tok/s", "us_per_call": round(us, 3),
+            "calls_timed": replays * len(calls), "roofline": hbm_roof(gbs, hbm_peak, peak_kind, kname, nbytes),
+            "l2": f"calls rotate over {n_copies} sequences ({n_copies * nbytes >> 20} MB > 126 MB L2); CUDA graph",
+            "clocks": ck, "cpu_baseline": cpu, "gpu_launches": replays * len(calls)}
+
+
+def wl_fa_prefill(args, torch, device, B, n=4096, steps=10):
+    """causal full-attention prefill, Qwen3.5-4B shape, n tokens per sequence,
+    B sequences, bf16 inputs; the whole call (prep: QK-norm, RoPE, ring append; attention)."""
+    import anelm_b200 as ab
+    from anelm_b200.core import Context
+
+    _, tpeak, tkind = peaks()
+    rng = np.random.default_rng(0)
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
     ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_FULL_ATTN], num_q_heads=HQ, num_kv_heads=HKV,
                   head_dim=HD, rot_dim=ROT, rope_theta=1e7, max_seqs=B, kv_capacity=n)
     ctx.set_full_attn_weights(0, (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32),
@@ -408,19 +548,16 @@ def run_prefill(args, torch, device):
     plan = ctx.plan(list(range(B)))
     proj = torch.randn(B, n, FA_PROJ, generator=g, device=device).to(torch.bfloat16)
     out = torch.empty(B, n, FA_OUT, device=device, dtype=torch.bfloat16)
-
-    def call():
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    for _ in range(max(3, args.warmup)):
         ctx.reset(-1)
         ctx.full_attn_prefill(plan, 0, proj, 0, out)
-
-    for _ in range(args.warmup):
-        call()
     torch.cuda.synchronize(device)
     times = []
-    clocks = ClockSampler(device.index or 0)
-    clocks.start()
-    for _ in range(args.steps):
-        ctx.reset(-1)  # synchronous; outside the timed region
+    clocks = ClockSampler(device.index or 0).start()
+    for _ in range(steps):
+        ctx.reset(-1)      # synchronous; outside the timed region
+        flush.zero_()      # the B = 1 inputs (84 MB) would otherwise sit in L2
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
         ctx.full_attn_prefill(plan, 0, proj, 0, out)
@@ -428,62 +565,30 @@ def run_prefill(args, torch, device):
         torch.cuda.synchronize(device)
         times.append(t0.elapsed_time(t1))
     ck = clocks.stop()
+    err = ctx.device_error()
+    plan.close()
+    ctx.close()
+    assert err == 0, f"device reported status {err}"
     ms = statistics.median(times)
     flops = 4.0 * n * n * HD * HQ / 2 * B  # causal: half of the S x S score / PV work
     tf = flops / (ms * 1e-3) / 1e12
-    print(json.dumps({
-        "metric": "causal prefill attention TFLOP/s (cfg3, Qwen3.5-4B shape)", "value": round(tf, 1),
-        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate",
-        "data": "synthetic",
-        "config": {"workload": f"BASELINE cfg3 prefill B={B} S={n}", "Hq": HQ, "Hkv": HKV, "head_dim": HD,
-                   "proj": "bf16 N(0,1)", "timed": "whole call: prep (norm, RoPE, ring append) + V^T + attention"},
-        "roofline": {"bound": "tensor", "kernel": "fa_prefill_kernel", "achieved": round(tf, 1), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(tf / peak, 4), "peak_kind": peak_kind, "traffic": None,
-                     "algorithmic_flops_per_launch": flops},
-        "clocks": ck,
-        "gpu_launches": 3 * args.steps}), flush=True)
-    plan.close()
-    ctx.close()
+    return {"metric": f"causal prefill attention TFLOP/s (cfg3, Qwen3.5-4B shape, B={B}, S={n})",
+            "value": round(tf, 1), "unit": "TFLOP/s", "ms": round(ms, 4), "steps": steps,
+            "roofline": tensor_roof(tf, tpeak, tkind, "fa_prefill_prep_bulk_kernel + fa_prefill_kernel (whole call)",
+                                    flops),
+            "timed": "whole call: prep (QK-norm, RoPE, fp16 Q/K/V, sigmoid gate, ring append) + attention",
+            "l2": "256 MB buffer written before each timed call", "clocks": ck,
+            "cpu_baseline": cpu_reference_prefill(B, n, args.cpu_seconds_wl, flops), "gpu_launches": 2 * steps}
 
 
-def gdn_chunk_flops(T, Hv, B=1, C=64, dk=128, dv=128):
-    """Algorithmic FLOPs of the chunked delta rule: per chunk and value head 2C^2(3dk + 2dv)
-    (K K^T, Q K^T, W, U, M D) + 6 C dk dv (W S, Q S, K^T D)."""
-    n_chunks = (T + C - 1) // C
-    return float(2 * C * C * (3 * dk + 2 * dv) + 6 * C * dk * dv) * n_chunks * Hv * B
-
-
-def cpu_reference_gdn_chunk(T_sample, Hk, Hv):
-    """The reference delta-rule step (core/cpu_ops.cpp ssm_step via oracle/_ref/libref_core_fast.so)
-    over a token sample of the config-4 workload, one host thread; returns seconds per token."""
-    from oracle import pyoracle as po
-
-    kind = "ref_fast" if po.available("ref_fast") else "oracle"
-    rng = np.random.default_rng(1)
-    q = rng.standard_normal((T_sample, Hk, 128)).astype(np.float32)
-    k = q / np.linalg.norm(q, axis=-1, keepdims=True)
-    v = rng.standard_normal((T_sample, Hv, 128)).astype(np.float32)
-    lg = (-0.1 * rng.random((T_sample, Hv))).astype(np.float32)
-    beta = rng.random((T_sample, Hv)).astype(np.float32)
-    st = np.zeros((Hv, 128, 128), np.float32)
-    t0 = time.perf_counter()
-    po.gated_delta_tokens(kind, q, k, v, lg, beta, st, 0)
-    return (time.perf_counter() - t0) / T_sample, kind
-
-
-def run_gdn_prefill(args, torch, device, hbm_peak, peak_kind):
+def wl_gdn_prefill(args, torch, device, B=1, T=8192, steps=10):
     """the chunked gated delta rule, Hv 32 / Hk 16, dk = dv = 128, seq 8192,
     batch 1; bf16 q / k / v N(0, 1) with L2-normalised k, log g ~ U(-0.1, 0), beta ~ U(0, 1)."""
     from anelm_b200.core import gated_delta_chunked
     import anelm_b200 as ab
 
-    try:
-        tpeak = float(json.load(open(PEAKS))["bf16_tflops"])
-        tpeak_kind = "measured"
-    except Exception:
-        tpeak, tpeak_kind = 1590.0, "fallback"
-    B, T, Hk, Hv = args.prefill_batch, args.gdn_len, 16, 32
+    hbm_peak, tpeak, tkind = peaks()
+    Hk, Hv = 16, 32
     g = torch.Generator(device=device)
     g.manual_seed(4)
     q = torch.randn(B, T, Hk, 128, generator=g, device=device).to(torch.bfloat16)
@@ -496,18 +601,17 @@ def run_gdn_prefill(args, torch, device, hbm_peak, peak_kind):
     y = torch.empty(B, T, Hv, 128, device=device, dtype=torch.bfloat16)
     ws = torch.empty(ab.lib().anelm_gated_delta_chunked_workspace_bytes(B, T, Hk, Hv), dtype=torch.uint8,
                      device=device)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > 126 MB L2
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
 
     def call():
         gated_delta_chunked(q, k, v, lg, beta, state, ab.DELTA_CPUOPS, y=y, workspace=ws)
 
-    for _ in range(args.warmup):
+    for _ in range(max(3, args.warmup)):
         call()
     torch.cuda.synchronize(device)
-    clocks = ClockSampler(device.index or 0)
-    clocks.start()
+    clocks = ClockSampler(device.index or 0).start()
     times = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         flush.zero_()  # inputs (24 MB) would otherwise stay in L2 between iterations
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -520,39 +624,44 @@ def run_gdn_prefill(args, torch, device, hbm_peak, peak_kind):
     flops = gdn_chunk_flops(T, Hv, B)
     tf = flops / (ms * 1e-3) / 1e12
     nbytes = B * (2 * T * Hk * 128 * 2 + T * Hv * 128 * 2 + 2 * T * Hv * 4 + T * Hv * 128 * 2 + 2 * Hv * 128 * 128 * 4)
-    sec_tok, kind = cpu_reference_gdn_chunk(64, Hk, Hv)
-    cpu_tf = flops / (sec_tok * T * B) / 1e12
-    print(json.dumps({
-        "metric": "chunked Gated DeltaNet prefill TFLOP/s (cfg4, Hv 32 / Hk 16, d 128)", "value": round(tf, 2),
-        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16 in, fp32 (hi/lo fp16 split) tensor-core products and state", "data": "synthetic",
-        "config": {"workload": f"BASELINE cfg4 chunked delta rule B={B} S={T} chunk 64", "Hk": Hk, "Hv": Hv,
-                   "dk": 128, "dv": 128, "l2": "256 MB buffer written between timed iterations"},
-        "roofline": {"bound": "tensor", "kernel": "gdn_pf_chain_kernel + gdn_pf_chunk_kernel", "achieved": round(tf, 2),
-                     "peak": tpeak, "unit": "TFLOP/s", "frac": round(tf / tpeak, 4), "peak_kind": tpeak_kind,
-                     "traffic": None, "algorithmic_flops_per_launch": flops,
-                     "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4), "algorithmic_bytes": nbytes},
-        "cpu_baseline": {"value": round(cpu_tf, 6), "unit": "TFLOP/s", "cores": 1,
-                         "kind": "reference" if kind == "ref_fast" else "port",
-                         "sample": "64 tokens x 32 value heads of the token recurrence (ssm_step), scaled to "
-                                   "the workload's algorithmic FLOPs"},
-        "clocks": ck,
-        "gpu_launches": 3 * args.steps}), flush=True)
+    roof = tensor_roof(tf, tpeak, tkind, "gdn_pf_pack + gdn_pf_chunk + gdn_pf_chain (whole call)", flops)
+    roof.update({"hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4), "algorithmic_bytes": nbytes})
+    return {"metric": f"chunked Gated DeltaNet prefill TFLOP/s (cfg4, Hv 32 / Hk 16, d 128, S={T}, B={B})",
+            "value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4), "steps": steps, "roofline": roof,
+            "l2": "256 MB buffer written before each timed call", "clocks": ck,
+            "cpu_baseline": cpu_reference_gdn_chunk(T, B, Hk, Hv, flops, args.cpu_seconds_wl),
+            "gpu_launches": 3 * steps}
 
 
-def run_proj(args, torch, device, hbm_peak, peak_kind):
+def gdn_chunk_flops(T, Hv, B=1, C=64, dk=128, dv=128):
+    """Algorithmic FLOPs of the chunked delta rule: per chunk and value head 2C^2(3dk + 2dv)
+    (K K^T, Q K^T, W, U, M D) + 6 C dk dv (W S, Q S, K^T D)."""
+    n_chunks = (T + C - 1) // C
+    return float(2 * C * C * (3 * dk + 2 * dv) + 6 * C * dk * dv) * n_chunks * Hv * B
+
+
+def run_workloads(args, torch, device):
+    out = {}
+    for name, fn in (("cfg1", lambda: wl_decode_b1(args, torch, device, "fa")),
+                     ("cfg2", lambda: wl_decode_b1(args, torch, device, "gdn")),
+                     ("cfg3_b1", lambda: wl_fa_prefill(args, torch, device, 1)),
+                     ("cfg3_b8", lambda: wl_fa_prefill(args, torch, device, 8)),
+                     ("cfg4", lambda: wl_gdn_prefill(args, torch, device))):
+        out[name] = fn()
+        torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------ the steps next to the core
+
+def run_proj(args, torch, device):
     """The steps next to the core (widening beyond the core): "proj" = the in- and out-projection
     GEMMs of one attention and one DeltaNet decode layer of the Qwen3.5-4B shape for `--seqs` rows
     (anelm_gemm_bf16); "lm_head" = the in-model top-32 LM head over the 248,320-token vocabulary
     for `--seqs` rows (anelm_lm_head_topk).  bf16 N(0,1) activations, N(0, 1/hidden) weights."""
     from anelm_b200.core import gemm_bf16, lm_head_topk
 
-    try:
-        tpeak = float(json.load(open(PEAKS))["bf16_tflops"])
-        tpeak_kind = "measured"
-    except Exception:
-        tpeak, tpeak_kind = 1590.0, "fallback"
+    hbm_peak, tpeak, tpeak_kind = peaks()
     n, H = args.seqs, 2560
     g = torch.Generator(device=device)
     g.manual_seed(0)
@@ -591,12 +700,11 @@ def run_proj(args, torch, device, hbm_peak, peak_kind):
         metric = "LM head with in-model top-32 TFLOP/s (248,320-token vocabulary, hidden 2560, bf16)"
         kernel, launches = "lm_head_topk_kernel + lm_topk_merge_kernel", 2
         cfg = {"workload": f"top-32 LM head, {n} rows x 248320 x 2560"}
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     for _ in range(args.warmup):
         call()
     torch.cuda.synchronize(device)
-    clocks = ClockSampler(device.index or 0)
-    clocks.start()
+    clocks = ClockSampler(device.index or 0).start()
     times = []
     for _ in range(args.steps):
         flush.zero_()  # weights would otherwise stay in L2 between iterations
@@ -611,18 +719,13 @@ def run_proj(args, torch, device, hbm_peak, peak_kind):
     tf = flops / (ms * 1e-3) / 1e12
     gbs = nbytes / (ms * 1e-3) / 1e9
     bound = "tensor" if flops / nbytes > tpeak * 1e12 / (hbm_peak * 1e9) else "hbm"
-    roof = ({"bound": "tensor", "achieved": round(tf, 2), "peak": tpeak, "unit": "TFLOP/s",
-             "frac": round(tf / tpeak, 4), "peak_kind": tpeak_kind} if bound == "tensor" else
-            {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-             "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind})
-    roof.update({"kernel": kernel, "traffic": None, "algorithmic_flops_per_launch": flops,
-                 "algorithmic_bytes": nbytes})
+    roof = (tensor_roof(tf, tpeak, tpeak_kind, kernel, flops) if bound == "tensor" else
+            hbm_roof(gbs, hbm_peak, tpeak_kind, kernel, nbytes))
     # CPU baseline: numpy (BLAS) on an 8-row sample of the same products (the reference runs them
     # on the ANE, so there is no reference CPU code for this step)
     rows = min(8, n)
     cpu_t = 0.0
     if not args.no_cpu_baseline:
-        import time
         xs_c = np.random.default_rng(0).standard_normal((rows, H)).astype(np.float32)
         if args.workload == "proj":
             mats = [np.random.default_rng(i).standard_normal((N, K)).astype(np.float32) for i, (N, K) in
@@ -639,7 +742,7 @@ def run_proj(args, torch, device, hbm_peak, peak_kind):
             np.argpartition(lg, -32, axis=1)[:, -32:]
             cpu_t = (time.perf_counter() - t0) * 8
     cpu_tf = (flops * rows / n) / cpu_t / 1e12 if cpu_t > 0 else None
-    print(json.dumps({
+    return {
         "metric": metric, "value": round(tf, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16 in, fp32 accumulate", "data": "synthetic",
@@ -649,15 +752,16 @@ def run_proj(args, torch, device, hbm_peak, peak_kind):
                          "cores": os.cpu_count(), "kind": "port",
                          "sample": f"numpy fp32 matmul on {rows} rows" +
                                    (" of 1/8 of the vocabulary, scaled" if args.workload == "lm_head" else "")},
-        "clocks": ck, "gpu_launches": launches * args.steps}), flush=True)
+        "clocks": ck, "gpu_launches": launches * args.steps}
 
 
-def run_gdn_layer(args, torch, device, hbm_peak, peak_kind):
+def run_gdn_layer(args, torch, device):
     """One DeltaNet decode layer of the config-5 shape over `--seqs` sequences (the kernel of the
     serving step on its own, a few hundred MB of state: the size for an ncu capture)."""
     import anelm_b200 as ab
     from anelm_b200.core import Context
 
+    hbm_peak, _, peak_kind = peaks()
     n = args.seqs
     ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_LINEAR_ATTN], lin_num_key_heads=HK,
                   lin_num_val_heads=HV, max_seqs=n, kv_capacity=16)
@@ -683,102 +787,90 @@ def run_gdn_layer(args, torch, device, hbm_peak, peak_kind):
     e1.record()
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1) / args.steps
-    nbytes = step_bytes(np.full(n, 1), 0)[1]              # same accounting as the serving step
+    nbytes = layer_bytes(np.full(n, 1))[1]              # same accounting as the serving step
     gbs = nbytes / (ms * 1e-3) / 1e9
-    print(json.dumps({
-        "metric": "DeltaNet decode layer GB/s (config-5 shape, one layer)", "value": round(gbs, 1), "unit": "GB/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"one DeltaNet layer, {n} sequences", "l2": f"state {n * HV * DK * DV * 4 >> 20} MB"},
-        "roofline": {"bound": "hbm", "kernel": "gdn_decode_kernel", "achieved": round(gbs, 1), "peak": hbm_peak,
-                     "unit": "GB/s", "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_launch": nbytes},
-        "gpu_launches": args.steps}), flush=True)
     plan.close()
     ctx.close()
+    return {"metric": "DeltaNet decode layer GB/s (config-5 shape, one layer)", "value": round(gbs, 1),
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"one DeltaNet layer, {n} sequences", "l2": f"state {n * HV * DK * DV * 4 >> 20} MB"},
+            "roofline": hbm_roof(gbs, hbm_peak, peak_kind, "gdn_decode_kernel", nbytes),
+            "gpu_launches": args.steps}
 
 
-def run_gpu_single(args, torch, device, hbm_peak, peak_kind):
-    """BASELINE configs 1 and 2: one sequence, one layer call per step, replayed from a CUDA graph."""
-    import anelm_b200 as ab
-    from anelm_b200.core import Context
-
-    rng = np.random.default_rng(0)
-    g = torch.Generator(device=device)
-    g.manual_seed(0)
-    if args.workload == "fa_b1":
-        ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_FULL_ATTN], max_seqs=1, kv_capacity=2048)
-        ctx.set_full_attn_weights(0, (1 + 0.02 * rng.standard_normal(256)).astype(np.float32),
-                                  (1 + 0.02 * rng.standard_normal(256)).astype(np.float32))
-        kv = torch.randn(2048, 2, 256, generator=g, device=device, dtype=torch.float16)
-        ctx.kv_write(0, 0, 0, kv, kv.flip(0).contiguous())
-        ctx.kv_set_meta(0, 0, 2048, 0)
-        proj = torch.randn(ctx.fa_proj_dim, generator=g, device=device, dtype=torch.float16)
-        out = torch.empty(ctx.fa_out_dim, device=device, dtype=torch.float16)
-        call = lambda: ctx.full_attn_from_proj(0, 0, proj, 5000, out)  # noqa: E731
-        nbytes = 2 * 2048 * 2 * 256 * 2 + ctx.fa_proj_dim * 2 + ctx.fa_out_dim * 2 + 2 * 2 * 256 * 2
-        metric, kname = "FA decode step tok/s (cfg1, 0.8B shape, KV 2048 fp16)", "fa_decode_kernel<256>"
-    else:
-        ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_LINEAR_ATTN], max_seqs=1)
-        C = ctx.conv_channels
-        ctx.set_deltanet_weights(0, (0.5 * rng.standard_normal((C, 4))).astype(np.float16).astype(np.float32),
-                                 np.ones(16, np.float32), np.zeros(16, np.float32), np.ones(128, np.float32))
-        st = (0.1 * torch.randn(16, 128, 128, generator=g, device=device)).contiguous()
-        ctx.deltanet_state_write(0, 0, st)
-        proj = torch.randn(ctx.gdn_proj_dim, generator=g, device=device, dtype=torch.float16)
-        out = torch.empty(ctx.gdn_out_dim, device=device, dtype=torch.float16)
-        call = lambda: ctx.deltanet_from_proj(0, 0, proj, out)  # noqa: E731
-        nbytes = 2 * 16 * 128 * 128 * 4 + C * 16 + C * 16 + ctx.gdn_proj_dim * 2 + ctx.gdn_out_dim * 2
-        metric, kname = "GDN decode step tok/s (cfg2, 16 heads, fp32 state)", "gdn_decode_kernel<8>"
-    for _ in range(max(3, args.warmup)):
-        call()
-    torch.cuda.synchronize(device)
-    reps = 64
-    graph = torch.cuda.CUDAGraph()
-    s = torch.cuda.Stream(device)
-    s.wait_stream(torch.cuda.current_stream(device))
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(graph, stream=s):
-            for _ in range(reps):
-                call()
-    torch.cuda.synchronize(device)
-    graph.replay()
-    torch.cuda.synchronize(device)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        graph.replay()
-    t1.record()
-    torch.cuda.synchronize(device)
-    us = t0.elapsed_time(t1) * 1e3 / (args.steps * reps)
-    gbs = nbytes / (us * 1e-6) / 1e9
-    print(json.dumps({"metric": metric, "value": round(1e6 / us, 1), "unit": "tok/s", "n_gpus": 1,
-                      "steps": args.steps * reps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 6),
-                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                      "data": "synthetic", "config": {"workload": args.workload, "graph_replay": reps},
-                      "roofline": {"bound": "hbm", "kernel": kname, "achieved": round(gbs, 1), "peak": hbm_peak,
-                                   "unit": "GB/s", "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind,
-                                   "traffic": None, "algorithmic_bytes_per_launch": nbytes},
-                      "gpu_launches": args.steps * reps}), flush=True)
-    ctx.close()
+def single_line(args, wl):
+    """The one-workload form of a configs 1-4 entry, as a full bench line."""
+    line = {"metric": wl["metric"], "value": wl["value"], "unit": wl["unit"], "n_gpus": 1, "steps": wl.get("steps"),
+            "warmup": args.warmup, "ms_per_step": wl.get("ms", wl.get("us_per_call", 0) / 1e3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "see metric",
+            "data": "synthetic", "config": {"workload": args.workload, "l2": wl["l2"]}}
+    line.update({k: v for k, v in wl.items() if k not in line and k not in ("metric", "value", "unit")})
+    return line
 
 
-# ------------------------------------------------------------------ CPU reference arm
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = env_rank()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    try:
+        if args.workload == "serve":
+            result = run_serve(args, torch, device, world, rank, local)
+            if world == 1 and not args.no_workloads:
+                result["workloads"] = run_workloads(args, torch, device)
+                result["gpu_launches"] += sum(w["gpu_launches"] for w in result["workloads"].values())
+        elif args.workload in ("fa_b1", "gdn_b1"):
+            result = single_line(args, wl_decode_b1(args, torch, device, args.workload[:-3]))
+        elif args.workload == "fa_prefill":
+            result = single_line(args, wl_fa_prefill(args, torch, device, args.prefill_batch, args.prefill_len,
+                                                     args.steps))
+        elif args.workload == "gdn_prefill":
+            result = single_line(args, wl_gdn_prefill(args, torch, device, args.prefill_batch, args.gdn_len,
+                                                      args.steps))
+        elif args.workload in ("proj", "lm_head"):
+            result = run_proj(args, torch, device)
+        else:
+            result = run_gdn_layer(args, torch, device)
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+    except BaseException:
+        if world > 1:
+            dist.destroy_process_group()  # no barrier: the other ranks learn of it by their own timeout
+        raise
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ CPU reference (oracle/_ref)
+
+def _ref_kind():
+    from oracle import pyoracle as po
+    return "ref_fast" if po.available("ref_fast") else "oracle"
+
 
 def cpu_reference_serving(seconds: float, threads=None, kind="reference"):
     """The reference CPU attention core (oracle/_ref/libref_core_fast.so: core/cpu_ops.cpp,
-    unmodified, + the qwen3_5.cpp glue restated) on a bounded sample of the serving
-    workload: `threads` sequences, each decoded token by token through all 32 layers
-    (fp32 KV ring of its length, fp32 DeltaNet state), one host thread per sequence.
-    Returns tokens/s over the sample."""
+    unmodified, + the qwen3_5.cpp glue restated) on a bounded sample of the serving workload:
+    one host thread per sampled sequence, each decoding token by token through all 32 layers
+    (fp32 KV ring of its length, fp32 DeltaNet state).  The sample takes the sequences at evenly
+    spaced quantiles of the 256-sequence length draw, so its mean KV length matches the
+    workload's.  Returns tokens/s over the sample (all threads together)."""
     from oracle import pyoracle as po
 
-    lib_kind = "ref_fast" if po.available("ref_fast") else "oracle"
-    threads = threads or max(1, min(os.cpu_count() or 1, 32))
+    lib_kind = _ref_kind()
+    threads = threads or max(1, os.cpu_count() or 1)
     shape = po.make_shape(num_q_heads=HQ, num_kv_heads=HKV, head_dim=HD, rot_dim=ROT, rope_theta=1e7,
                           lin_num_key_heads=HK, lin_num_val_heads=HV)
     var = po.make_variant()
-    lengths = kv_lengths(256, 0)[:threads]
+    population = np.sort(kv_lengths(GLOBAL_SEQS, 0))
+    pick = ((np.arange(threads) + 0.5) * GLOBAL_SEQS / threads).astype(int).clip(0, GLOBAL_SEQS - 1)
+    lengths = population[pick]
     rng = np.random.default_rng(0)
     qn = (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32)
     cw = (0.5 * rng.standard_normal((C_CONV, 4))).astype(np.float16).astype(np.float32)
@@ -840,18 +932,132 @@ def cpu_reference_serving(seconds: float, threads=None, kind="reference"):
         res = list(ex.map(worker, range(threads)))
     toks = sum(r[0] for r in res)
     wall = max(r[1] for r in res)
-    cpu_model = ""
-    try:
-        for line in open("/proc/cpuinfo"):
-            if line.startswith("model name"):
-                cpu_model = line.split(":", 1)[1].strip()
-                break
-    except Exception:
-        pass
     return {"value": round(toks / wall, 3), "unit": "tok/s", "cores": threads, "kind": kind,
-            "sample": (f"{threads} sequences (KV lengths = the first {threads} of the workload's U[512,32768] draw), "
-                       f"{toks} tokens through all 32 layers, fp32 KV/state, {wall:.1f} s wall; "
-                       f"lib={os.path.basename(po.LIBS[lib_kind])}; cpu={cpu_model}; nproc={os.cpu_count()}")}
+            "sample_mean_kv": round(float(lengths.mean()), 1), "workload_mean_kv": round(float(population.mean()), 1),
+            "sample": (f"{threads} sequences at evenly spaced quantiles of the workload's 256-sequence U[512,32768] "
+                       f"draw (mean KV {lengths.mean():.0f} vs {population.mean():.0f}), {toks} tokens through all "
+                       f"32 layers, fp32 KV/state, one thread per sequence, {wall:.1f} s wall; "
+                       f"lib={os.path.basename(po.LIBS[lib_kind])}; cpu={cpu_model()}; nproc={os.cpu_count()}")}
+
+
+def cpu_reference_decode_b1(which, seconds):
+    """The reference core (oracle/_ref/libref_core_fast.so) on configs 1 / 2: one sequence, one
+    thread (the reference's core is single-threaded and batch 1 has nothing else to spread),
+    token by token for up to `seconds`."""
+    from oracle import pyoracle as po
+
+    kind = _ref_kind()
+    P = po.P
+    rng = np.random.default_rng(0)
+    if which == "fa":
+        shape = po.make_shape()
+        qn = (1 + 0.02 * rng.standard_normal(256)).astype(np.float32)
+        k = rng.standard_normal((2048, 2, 256)).astype(np.float32)
+        v = rng.standard_normal((2048, 2, 256)).astype(np.float32)
+        ln, st = ctypes.c_int(2048), ctypes.c_int(0)
+        rope = po.rope_table(4096, 64, 1e7)
+        proj = rng.standard_normal(8 * 512 + 2 * 2 * 256).astype(np.float32)
+        pbuf, out, tmp = np.empty_like(proj), np.zeros(8 * 256, np.float32), np.zeros(256, np.float32)
+        f = po.fn(kind, "full_attn_from_proj")
+
+        def step(i):
+            pbuf[:] = proj
+            f(ctypes.byref(shape), ctypes.byref(po.make_variant()), P(qn), P(qn), P(k), P(v), ctypes.byref(ln),
+              ctypes.byref(st), 2048, P(rope[0]), P(rope[1]), 4096, P(pbuf), 3000 + i, P(out), P(tmp))
+        what = "ring of 2048 (full, sliding), 8/2 heads"
+    else:
+        shape = po.make_shape(lin_num_key_heads=16, lin_num_val_heads=16)
+        C = 6144
+        cw = (0.5 * rng.standard_normal((C, 4))).astype(np.float16).astype(np.float32)
+        A, dtb, nw = np.ones(16, np.float32), np.zeros(16, np.float32), np.ones(128, np.float32)
+        s = po.DeltaState.zeros(shape)
+        s.ssm[:] = (0.1 * rng.standard_normal(s.ssm.shape)).astype(np.float32)
+        proj = rng.standard_normal(C + 16 * 128 + 32).astype(np.float32)
+        out, scratch = np.zeros(16 * 128, np.float32), np.zeros(2 * C + 16 * 128, np.float32)
+        cp = ctypes.c_int(0)
+        f = po.fn(kind, "deltanet_from_proj")
+
+        def step(i):
+            f(ctypes.byref(shape), ctypes.byref(po.make_variant()), P(cw), P(A), P(dtb), P(nw), P(s.ssm), P(s.conv),
+              ctypes.byref(cp), P(proj), P(out), P(scratch))
+        what = "16/16 heads, fp32 state 128x128 per head"
+    step(0)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds and n < 100000:
+        step(n)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 2), "unit": "tok/s", "cores": 1, "kind": "reference" if kind == "ref_fast" else "port",
+            "sample": f"{n} successive tokens, {what}, {dt:.1f} s; lib={os.path.basename(po.LIBS[kind])}; "
+                      f"cpu={cpu_model()}"}
+
+
+def cpu_reference_prefill(B, n, seconds, flops):
+    """The reference's prefill of config 3 is its per-token loop (qwen3_5.cpp:1205-1217): token t
+    runs forward_full_attn_from_proj over a ring holding t keys.  Sample: tokens at evenly spaced
+    positions of the prompt, each timed over a ring filled to that position; the prompt's time is
+    the sample mean times n.  One thread per sequence, B sequences at once."""
+    from oracle import pyoracle as po
+
+    kind = _ref_kind()
+    P = po.P
+    shape = po.make_shape(num_q_heads=HQ, num_kv_heads=HKV, head_dim=HD, rot_dim=ROT, rope_theta=1e7)
+    rope = po.rope_table(4096, ROT, 1e7)
+    f = po.fn(kind, "full_attn_from_proj")
+    K = 16
+
+    def worker(b):
+        rng = np.random.default_rng(b)
+        qn = (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32)
+        k = rng.standard_normal((n, HKV, HD)).astype(np.float32)
+        v = rng.standard_normal((n, HKV, HD)).astype(np.float32)
+        proj = rng.standard_normal(FA_PROJ).astype(np.float32)
+        pbuf, out, tmp = np.empty_like(proj), np.zeros(FA_OUT, np.float32), np.zeros(HD, np.float32)
+        total, done, t_end = 0.0, 0, time.perf_counter() + seconds
+        for i in range(K):
+            p = int((i + 0.5) * n / K)
+            ln, st = ctypes.c_int(p), ctypes.c_int(0)
+            pbuf[:] = proj
+            t0 = time.perf_counter()
+            f(ctypes.byref(shape), ctypes.byref(po.make_variant()), P(qn), P(qn), P(k), P(v), ctypes.byref(ln),
+              ctypes.byref(st), n, P(rope[0]), P(rope[1]), 4096, P(pbuf), p, P(out), P(tmp))
+            total += time.perf_counter() - t0
+            done += 1
+            if time.perf_counter() > t_end:
+                break
+        return total / done * n, done
+
+    with ThreadPoolExecutor(max_workers=B) as ex:
+        res = list(ex.map(worker, range(B)))
+    wall = max(r[0] for r in res)   # B sequences on B threads: the slowest one's prompt time
+    return {"value": round(flops / wall / 1e12, 6), "unit": "TFLOP/s", "cores": B,
+            "kind": "reference" if kind == "ref_fast" else "port", "est_prompt_s": round(wall, 2),
+            "sample": (f"{res[0][1]} tokens per sequence at evenly spaced positions of the {n}-token prompt "
+                       f"(forward_full_attn_from_proj over a ring filled to that position), mean x {n} = the "
+                       f"per-token prefill loop's time; {B} thread(s); lib={os.path.basename(po.LIBS[kind])}")}
+
+
+def cpu_reference_gdn_chunk(T, B, Hk, Hv, flops, seconds):
+    """The reference delta-rule step (core/cpu_ops.cpp ssm_step via oracle/_ref) over a token sample
+    of the config-4 workload, one host thread; scaled to the workload's tokens."""
+    from oracle import pyoracle as po
+
+    kind = _ref_kind()
+    rng = np.random.default_rng(1)
+    T_s = 64
+    q = rng.standard_normal((T_s, Hk, 128)).astype(np.float32)
+    k = q / np.linalg.norm(q, axis=-1, keepdims=True)
+    v = rng.standard_normal((T_s, Hv, 128)).astype(np.float32)
+    lg = (-0.1 * rng.random((T_s, Hv))).astype(np.float32)
+    beta = rng.random((T_s, Hv)).astype(np.float32)
+    st = np.zeros((Hv, 128, 128), np.float32)
+    t0 = time.perf_counter()
+    po.gated_delta_tokens(kind, q, k, v, lg, beta, st, 0)
+    sec_tok = (time.perf_counter() - t0) / T_s
+    return {"value": round(flops / (sec_tok * T * B) / 1e12, 6), "unit": "TFLOP/s", "cores": 1,
+            "kind": "reference" if kind == "ref_fast" else "port",
+            "sample": f"{T_s} tokens x {Hv} value heads of the token recurrence (ssm_step), scaled to the "
+                      f"workload's {T * B} tokens and its algorithmic FLOPs"}
 
 
 def run_reference(args):
@@ -860,13 +1066,13 @@ def run_reference(args):
         return
     cb = cpu_reference_serving(args.cpu_seconds, threads=None, kind="reference")
     print(json.dumps({
-        "impl": "reference",
-        "metric": "decode attn-core tok/s (batched serving decode, 32-layer 3:1 DeltaNet:attention stack)",
+        "impl": "reference", "metric": METRIC,
         "value": cb["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "ms_per_step": None, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": "BASELINE cfg5: batched serving decode, Qwen3.5-4B-shaped 32 layers (24 GDN + 8 FA)",
-                   "seqs_per_gpu": args.seqs, "kv_len": "U[512,32768] seed 0"},
+                   "global_batch": GLOBAL_SEQS, "kv_len": "U[512,32768] seed 0",
+                   "note": "the host's cores run the reference CPU core; the GPU count does not change it"},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -884,9 +1090,11 @@ def main():
     ap.add_argument("--gdn-len", type=int, default=8192)
     ap.add_argument("--prefill-batch", type=int, default=1)
     ap.add_argument("--prefill-len", type=int, default=4096)
-    ap.add_argument("--seqs", type=int, default=256)
+    ap.add_argument("--seqs", type=int, default=256, help="rows for the proj / lm_head / gdn_layer workloads")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-seconds-wl", type=float, default=3.0, help="CPU sample per configs 1-4 entry")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-workloads", action="store_true", help="skip the configs 1-4 entries of the default line")
     ap.add_argument("--traffic-json", default=os.path.join(REPO, "profiles", "traffic.json"))
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

@@ -223,16 +223,23 @@ ANELM_API int anelm_layer_decode(anelm_ctx* ctx, const anelm_plan* plan, int lay
 
 /* ---- prefill ---- */
 
-/* Causal prefill of the plan's sequences, each of n_tokens prompt tokens, into
- * EMPTY rings (fresh context or after anelm_reset).  Equivalent to n_tokens
- * successive forward_full_attn_from_proj calls at positions start_pos,
- * start_pos+1, ... (the per-token loop of qwen3_5.cpp:1205-1217 /
- * serve_hybrid.py:368-370), computed as one causal attention on the tcgen05
- * tensor cores.  proj: [n_seqs][n_tokens][proj_dim] of proj_dtype; out:
- * [n_seqs][n_tokens][Hq*d].  Afterwards each ring holds the n_tokens keys and
- * values (len = n_tokens, start = 0) and decode continues from there.
- * head_dim 256 only; n_tokens <= each ring's capacity.  Uses a context-owned
- * staging buffer: prefill calls on one context must not overlap on the GPU. */
+/* Causal prefill of the plan's sequences, each of n_tokens prompt tokens, on top
+ * of whatever their rings already hold.  Equivalent to n_tokens successive
+ * forward_full_attn_from_proj calls at positions start_pos, start_pos+1, ... (the
+ * per-token loop of qwen3_5.cpp:1205-1217 / serve_hybrid.py:368-370, and the
+ * chunks of forward_batch, qwen3_5.cpp:1164-1217, that generate.cpp:57-73 feeds at
+ * a running start_pos), computed as one causal attention on the tcgen05 tensor
+ * cores: token t attends to the ring's old tokens and the new tokens 0..t, at most
+ * `capacity` tokens in all, and is appended as the reference's ring update does
+ * (qwen3_5.cpp:974-983), so a prompt may continue an earlier turn and may be
+ * longer than the ring (the ring slides).  Afterwards len / start are what the
+ * per-token loop leaves and decode continues from there.  One start_pos for all
+ * the plan's sequences.  proj: [n_seqs][n_tokens][proj_dim] of proj_dtype; out:
+ * [n_seqs][n_tokens][Hq*d].  head_dim 256 only.  A linear cache (kv_mode
+ * ANELM_KV_LINEAR) is filled only from position 0 of an empty cache, n_tokens <=
+ * capacity.  Uses a context-owned staging buffer sized for the old tokens the
+ * first new token sees (min(len, capacity - 1) per sequence): prefill calls on
+ * one context must not overlap on the GPU. */
 ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,
                                       const void* proj, int proj_dtype, int start_pos, void* out, int out_dtype,
                                       void* stream);

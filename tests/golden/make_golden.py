@@ -4,7 +4,7 @@ Run where the reference sources are present (--ref, or ANELM_REFERENCE) and
 after ``make -C oracle`` has built oracle/_ref/libref_core.so from the
 reference's unmodified core/cpu_ops.cpp:
 
-    python tests/golden/make_golden.py [--ref /path/to/ANE-LM]
+    python tests/golden/make_golden.py --ref <ANE-LM root> [--only deltanet_hf ...]
 
 Fixtures written (seeded, numpy default_rng):
 
@@ -18,7 +18,15 @@ Fixtures written (seeded, numpy default_rng):
 * ``serve_hybrid_ref.npz`` -- scripts/serve_hybrid.py:85-132 ``cpu_attention`` run from
   the reference file's own source (parsed with ast; the two Accelerate sgemm
   calls replaced by numpy matmul, the only Apple dependency of that function)
-  over 12 positions at the reference's Qwen3.5-4B constants.
+  over 12 positions at the reference's Qwen3.5-4B constants;
+* ``deltanet_hf_ref.npz``  -- the decay-first (HF-order) DeltaNet layer of the hybrid v2
+  export, scripts/export_hybrid_chunks.py:83-160 ``DeltaNetLayer``, run from the
+  reference file's own class source (parsed with ast; coremltools, which that file
+  imports at module level, is not needed by the class) over 16 tokens, 4 value / 2 key
+  heads, dk=dv=128: its shift-register conv state, F.normalize of q/k, decay-first
+  update and [y, -y] LayerNorm.  The layer's own input norm and in_proj are replaced by
+  identities so that it consumes the projection row directly, and its out_proj by a
+  module that records the core output (y_normed) and returns zeros.
 
 The C++ glue around cpu_ops is the restatement in oracle/glue_impl.h (the
 reference's qwen3_5.cpp cannot be compiled off macOS); the ops it calls are the
@@ -201,16 +209,91 @@ def gen_serve_hybrid(rng, ref_root):
                         rope_theta=np.float32(g["ROPE_THETA"]))
 
 
+def load_reference_deltanet_layer(ref_root):
+    """Executes the reference's RMSNorm, SwiGLUFFN and DeltaNetLayer class definitions from
+    scripts/export_hybrid_chunks.py (nothing else of that file) and returns DeltaNetLayer."""
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    path = os.path.join(ref_root, "scripts", "export_hybrid_chunks.py")
+    tree = ast.parse(open(path).read(), path)
+    body = [n for n in tree.body if isinstance(n, ast.ClassDef) and n.name in ("RMSNorm", "SwiGLUFFN",
+                                                                              "DeltaNetLayer")]
+    assert len(body) == 3, "expected RMSNorm, SwiGLUFFN and DeltaNetLayer in export_hybrid_chunks.py"
+    g = {"torch": torch, "nn": nn, "F": F, "math": __import__("math")}
+    exec(compile(ast.Module(body=body, type_ignores=[]), path, "exec"), g)
+    return g["DeltaNetLayer"]
+
+
+def gen_deltanet_hf(rng, ref_root):
+    import torch
+    import torch.nn as nn
+
+    Layer = load_reference_deltanet_layer(ref_root)
+    Hv, Hk, dk, dv, K, T = 4, 2, 128, 128, 4, 16
+    C = 2 * Hk * dk + Hv * dv
+    proj_dim = C + Hv * dv + 2 * Hv
+    proj = f16(rng.standard_normal((T, proj_dim)))
+    conv_w = f16(0.5 * rng.standard_normal((C, K)))
+    A_log = (0.3 * rng.standard_normal(Hv)).astype(np.float32)
+    dt_bias = (0.5 * rng.standard_normal(Hv)).astype(np.float32)
+    norm_w = (1 + 0.1 * rng.standard_normal(dv)).astype(np.float32)
+    shift0 = rng.standard_normal((C, K)).astype(np.float32)
+    ssm0 = (0.1 * rng.standard_normal((Hv, dk, dv))).astype(np.float32)
+
+    layer = Layer(hidden_size=proj_dim, intermediate_size=8, lin_qkv_dim=C, lin_total_val=Hv * dv,
+                  lin_num_val_heads=Hv, lin_key_dim=dk, lin_val_dim=dv, lin_num_key_heads=Hk, conv_kernel=K)
+    captured = []
+
+    class Capture(nn.Module):  # stands in for out_proj: keeps the core output, adds nothing
+        def forward(self, x):
+            captured.append(x.detach().clone())
+            return torch.zeros(x.shape[0], proj_dim)
+
+    layer.input_layernorm = nn.Identity()
+    layer.in_proj = nn.Identity()
+    layer.out_proj = Capture()
+    with torch.no_grad():
+        layer.conv_weight.copy_(torch.from_numpy(conv_w))
+        layer.A_log.copy_(torch.from_numpy(A_log))
+        layer.dt_bias.copy_(torch.from_numpy(dt_bias))
+        layer.norm_weight.copy_(torch.from_numpy(norm_w))
+        conv, ssm = torch.from_numpy(shift0), torch.from_numpy(ssm0)
+        for t in range(T):
+            _, conv, ssm = layer(torch.from_numpy(proj[t:t + 1]), conv, ssm)
+    out = torch.cat(captured, 0).numpy()
+    assert out.shape == (T, Hv * dv)
+    np.savez_compressed(os.path.join(OUT, "deltanet_hf_ref.npz"), proj=proj.astype(np.float16), conv_w=conv_w,
+                        A=np.exp(A_log).astype(np.float32), A_log=A_log, dt_bias=dt_bias, norm_w=norm_w,
+                        shift0=shift0, ssm0=ssm0, out=out, ssm=ssm.numpy(), shift=conv.numpy(),
+                        dims=np.array([Hk, Hv, dk, dv, K], np.int32))
+
+
+GENERATORS = ("cpu_ops", "full_attn", "deltanet", "serve_hybrid", "deltanet_hf")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("ANELM_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("ANELM_REFERENCE"),
+                    help="root of the ANE-LM sources (or set ANELM_REFERENCE)")
+    ap.add_argument("--only", nargs="*", choices=GENERATORS, help="regenerate only these fixtures")
     a = ap.parse_args()
-    if not po.available("ref"):
-        sys.exit("oracle/_ref/libref_core.so missing: run make -C oracle with the reference present")
-    gen_cpu_ops(np.random.default_rng(0))
-    gen_full_attn(np.random.default_rng(1))
-    gen_deltanet(np.random.default_rng(2))
-    gen_serve_hybrid(np.random.default_rng(3), a.ref)
+    if not a.ref or not os.path.isdir(a.ref):
+        sys.exit("give the ANE-LM source root with --ref or ANELM_REFERENCE")
+    only = set(a.only or GENERATORS)
+    if not po.available("ref") and only & {"cpu_ops", "full_attn", "deltanet"}:
+        sys.exit("oracle/_ref/libref_core.so missing: run make -C oracle REF=<ANE-LM root>")
+    if "cpu_ops" in only:
+        gen_cpu_ops(np.random.default_rng(0))
+    if "full_attn" in only:
+        gen_full_attn(np.random.default_rng(1))
+    if "deltanet" in only:
+        gen_deltanet(np.random.default_rng(2))
+    if "serve_hybrid" in only:
+        gen_serve_hybrid(np.random.default_rng(3), a.ref)
+    if "deltanet_hf" in only:
+        gen_deltanet_hf(np.random.default_rng(4), a.ref)
     for f in sorted(os.listdir(OUT)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(OUT, f)))

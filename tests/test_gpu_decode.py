@@ -120,10 +120,12 @@ def test_deltanet_successive_tokens(Hk, Hv, T):
 
 
 def test_deltanet_long_run_state_stays_close():
-    """512 successive tokens (BASELINE config 2 runs 1..4096): no drift beyond tolerance."""
+    """BASELINE config 2 over its full length: 4096 successive tokens through one 16/16-head
+    layer from a state N(0, 0.1), every output and the final state / conv ring / position
+    against the oracle -- no drift beyond tolerance."""
     rng = np.random.default_rng(7)
     shape = gdn_shape(16, 16)
-    T = 512
+    T = 4096
     proj, conv_w, A, dt_bias, norm_w = gdn_inputs(rng, shape, T)
     st = po.DeltaState.zeros(shape)
     st.ssm[:] = (0.1 * rng.standard_normal(st.ssm.shape)).astype(np.float32)
@@ -134,8 +136,8 @@ def test_deltanet_long_run_state_stays_close():
         got = torch.stack([ctx.deltanet_from_proj(0, 0, p[t].contiguous()) for t in range(T)]).cpu().numpy()
         ssm, conv, pos = ctx.deltanet_state_export(0, 0)
     want = po.deltanet_tokens("oracle", shape, po.make_variant(), conv_w, A, dt_bias, norm_w, st, proj)
-    assert_close(got, want, what="outputs over 512 tokens")
-    assert_close(ssm, st.ssm, what="state after 512 tokens")
+    assert_close(got, want, what=f"outputs over {T} tokens")
+    assert_close(ssm, st.ssm, what=f"state after {T} tokens")
     np.testing.assert_array_equal(conv, st.conv)
     assert pos == st.conv_pos
 
@@ -177,6 +179,44 @@ def test_full_attn_batched_ragged():
     k, v, ln, st = exported[2]
     assert (ln, st) == lens[2]
     np.testing.assert_array_equal(v, rings[2].v)
+
+
+def test_full_attn_batched_serving_lengths():
+    """The multi-row plan at the serving workload's KV lengths (U[512, 32768]):
+    a full 32,768-slot ring wrapped at slot 5000, one just short of full, lengths down to 512, and
+    one ring that fills and starts evicting during the steps.  These are the long splits and the
+    global-memory merge that the serving bench times; every row vs the oracle, ring metadata and
+    V rows bit-exact."""
+    rng = np.random.default_rng(21)
+    shape = fa_shape(16, 4, 256, 64, 1e7)
+    caps = [32768, 512, 20003, 32768, 8193, 700]
+    lens = [(32768, 5000), (512, 0), (20001, 3), (31000, 0), (8191, 8000), (600, 650)]
+    order = [2, 0, 5, 3, 1, 4]
+    steps = 3
+    rope = po.rope_table(4096, 64, 1e7)
+    rings = [random_ring(rng, c, 4, 256, l, s) for c, (l, s) in zip(caps, lens)]
+    _, qn, kn = fa_inputs(rng, shape, 1)
+    projs = f16(rng.standard_normal((steps, len(order), shape.num_q_heads * 512 + 2 * 4 * 256)))
+    pos0 = np.array([40000, 512, 20001, 31000, 8191, 600], np.int32)
+    with fa_ctx(shape, caps=caps, max_seqs=len(caps)) as ctx:
+        ctx.set_full_attn_weights(0, qn, kn)
+        for s, r in enumerate(rings):
+            ctx.kv_import(0, s, r.k, r.v, r.len, r.start)
+        plan = ctx.plan(order)
+        outs = []
+        for t in range(steps):
+            pos = dev(pos0[order] + t, torch.int32)
+            outs.append(ctx.full_attn_decode(plan, 0, dev(projs[t], torch.float16), pos))
+        got = torch.stack(outs).cpu().numpy()
+        exported = [ctx.kv_export(0, s) for s in range(len(caps))]
+        plan.close()
+    for i, s in enumerate(order):
+        want = po.full_attn_tokens("oracle", shape, po.make_variant(kv_round_f16=1), qn, kn, rings[s],
+                                   projs[:, i], int(pos0[s]), rope)
+        assert_close(got[:, i], want, what=f"row {i} (seq {s}, len {lens[s][0]})")
+        k, v, ln, st = exported[s]
+        assert (ln, st) == (rings[s].len, rings[s].start), f"seq {s} ring metadata"
+        np.testing.assert_array_equal(v, rings[s].v)
 
 
 def test_deltanet_batched():
@@ -261,6 +301,36 @@ def test_deltanet_hf_variant():
     want = po.deltanet_tokens("oracle", shape, po.make_variant(delta_hf=1, l2_eps=1e-6), conv_w, A, dt_bias,
                               norm_w, st, proj)
     assert_close(got, want, what="HF-order DeltaNet")
+
+
+@pytest.mark.parametrize("route", ["decode", "prefill"])
+def test_deltanet_hf_variant_matches_reference_layer(golden, route):
+    """The decay-first variant against the hybrid v2 export's own DeltaNetLayer
+    (scripts/export_hybrid_chunks.py:83-160, run from the reference source into
+    tests/golden/deltanet_hf_ref.npz): its shift-register conv state converted to the
+    context's ring, 16 tokens token by token (decode) or as one chunked prefill."""
+    from anelm_b200.state_layout import conv_ring_to_shift, conv_shift_to_ring
+
+    g = golden("deltanet_hf_ref.npz")
+    Hk, Hv, dk, dv, K = (int(x) for x in g["dims"])
+    shape = gdn_shape(Hk, Hv, dk, dv)
+    ring, pos0 = conv_shift_to_ring(g["shift0"])
+    proj = g["proj"].astype(np.float32)
+    with gdn_ctx(shape, delta_mode=ab.DELTA_HF) as ctx:
+        ctx.set_deltanet_weights(0, g["conv_w"], g["A"], g["dt_bias"], g["norm_w"])
+        ctx.deltanet_state_import(0, 0, g["ssm0"], ring, pos0)
+        p = dev(proj, torch.float16)
+        if route == "decode":
+            got = torch.stack([ctx.deltanet_from_proj(0, 0, p[t].contiguous()) for t in range(p.shape[0])])
+        else:
+            plan = ctx.plan([0])
+            got = ctx.deltanet_prefill(plan, 0, p[None].contiguous())[0]
+            plan.close()
+        got = got.cpu().numpy()
+        ssm, conv, pos = ctx.deltanet_state_export(0, 0)
+    assert_close(got, g["out"], what=f"HF-order {route} vs export_hybrid_chunks DeltaNetLayer")
+    assert_close(ssm, g["ssm"], what="HF-order state")
+    np.testing.assert_array_equal(conv_ring_to_shift(conv, pos)[:, 1:], g["shift"][:, 1:])
 
 
 def test_full_attn_python_route_variant():

@@ -12,7 +12,7 @@ torch = pytest.importorskip("torch")
 
 import anelm_b200 as ab  # noqa: E402
 from anelm_b200.core import Context  # noqa: E402
-from helpers import assert_close, fa_shape  # noqa: E402
+from helpers import assert_close, f16, fa_shape  # noqa: E402
 from oracle import pyoracle as po  # noqa: E402
 
 pytestmark = pytest.mark.gpu
@@ -154,21 +154,149 @@ def test_prefill_config3_full_size(B, out_dtype):
     assert_close(out[check].float().cpu().numpy(), want.cpu().numpy(), what=f"config-3 prefill B={B}")
 
 
-def test_prefill_state_errors():
-    with ctx_for(1, 64, qk_norm_in_core=0) as ctx:
+def test_prefill_linear_cache_errors():
+    """A linear cache (slot = position, serve_hybrid.py:105-108) is filled from position 0 of an
+    empty cache and never slides: longer prompts, later starts and second prefills are errors."""
+    with ctx_for(1, 64, qk_norm_in_core=0, kv_mode=ab.KV_LINEAR) as ctx:
         plan = ctx.plan([0])
         p = torch.zeros(1, 65, PROJ, device="cuda")
         with pytest.raises(ab.AnelmError) as e:
-            ctx.full_attn_prefill(plan, 0, p)        # more tokens than the ring holds
+            ctx.full_attn_prefill(plan, 0, p)        # more tokens than the cache has positions
         assert e.value.status == 2
+        with pytest.raises(ab.AnelmError) as e:
+            ctx.full_attn_prefill(plan, 0, p[:, :10].contiguous(), start_pos=10)
+        assert e.value.status == 5
         ctx.full_attn_prefill(plan, 0, p[:, :10].contiguous())
         with pytest.raises(ab.AnelmError) as e:
-            ctx.full_attn_prefill(plan, 0, p[:, :10].contiguous())   # ring is no longer empty
-        assert e.value.status == 6
+            ctx.full_attn_prefill(plan, 0, p[:, :10].contiguous())   # the cache is no longer empty
+        assert e.value.status == 2
         ctx.reset(0)
         ctx.full_attn_prefill(plan, 0, p[:, :10].contiguous())
         torch.cuda.synchronize()
+        assert ctx.device_error() == 0
         plan.close()
+
+
+def generate_chunks(n):
+    """Chunk sizes of generate.cpp:57-73: the largest of 8 / 4 / 2 / 1 that fits what remains."""
+    out = []
+    while n > 0:
+        c = next(b for b in (8, 4, 2, 1) if b <= n)
+        out.append(c)
+        n -= c
+    return out
+
+
+def test_prefill_continues_rings_in_generate_chunks():
+    """Prefill on top of existing KV: generate.cpp:57-73 feeds the prompt to forward_batch in
+    chunks of 8 / 4 / 2 / 1 at a running start_pos (qwen3_5.cpp:1164-1217), each chunk attending
+    to every earlier token still in the ring.  Two sequences (rings of 512 and 200 slots) start
+    from prompts of 100 and 37 tokens, continue together in one plan through 45 tokens of such
+    chunks (their old-token prefixes differ), decode 3 tokens, then take a 150-token second turn
+    that overflows the 200-slot ring mid-call (it slides: its oldest tokens leave the window of
+    later queries) and a last 8-token chunk over a wrapped ring.  Everything against the
+    oracle's per-token loop over the same positions; ring len / start and V bit-exact."""
+    rng = np.random.default_rng(77)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(77)
+    caps = [512, 200]
+    qn, kn = weights(rng)
+    rope = po.rope_table(4096, R, 1e7)
+    shape = fa_shape(HQ, HKV, D, R, 1e7)
+    var = po.make_variant(kv_round_f16=1)
+    rings = [po.KVRing.empty(c, HKV, D) for c in caps]
+    got = [[], []]
+    want = [[], []]
+
+    def oracle(s, proj, pos):
+        want[s].append(po.full_attn_tokens("oracle", shape, var, qn, kn, rings[s], proj.float().cpu().numpy(),
+                                           pos, rope))
+
+    with Context(layer_types=[ab.LAYER_FULL_ATTN], num_q_heads=HQ, num_kv_heads=HKV, head_dim=D, rot_dim=R,
+                 rope_theta=1e7, seq_kv_capacity=caps) as ctx:
+        ctx.set_full_attn_weights(0, qn, kn)
+        plans = [ctx.plan([0]), ctx.plan([1]), ctx.plan([0, 1])]
+        # first prompts, one sequence each
+        for s, n in ((0, 100), (1, 37)):
+            p = bf16_proj(gen, 1, n)
+            got[s].append(ctx.full_attn_prefill(plans[s], 0, p, start_pos=0)[0].cpu().numpy())
+            oracle(s, p[0], 0)
+        # both sequences continue in generate.cpp's chunks (one start position for the plan)
+        pos = 200
+        for c in generate_chunks(45):
+            p = bf16_proj(gen, 2, c)
+            out = ctx.full_attn_prefill(plans[2], 0, p, start_pos=pos).cpu().numpy()
+            for s in (0, 1):
+                got[s].append(out[s])
+                oracle(s, p[s], pos)
+            pos += c
+        # decode
+        for _ in range(3):
+            p = bf16_proj(gen, 2, 1)[:, 0].contiguous()
+            out = ctx.full_attn_decode(plans[2], 0, p, torch.tensor([pos, pos], dtype=torch.int32,
+                                                                     device="cuda")).cpu().numpy()
+            for s in (0, 1):
+                got[s].append(out[s:s + 1])
+                oracle(s, p[s:s + 1], pos)
+            pos += 1
+        # second turn: 150 tokens (sequence 1's ring overflows), then 8 more over a wrapped ring
+        for n in (150, 8):
+            p = bf16_proj(gen, 2, n)
+            out = ctx.full_attn_prefill(plans[2], 0, p, start_pos=pos).cpu().numpy()
+            for s in (0, 1):
+                got[s].append(out[s])
+                oracle(s, p[s], pos)
+            pos += n
+        torch.cuda.synchronize()
+        assert ctx.device_error() == 0
+        exported = [ctx.kv_export(0, s) for s in (0, 1)]
+        for pl in plans:
+            pl.close()
+    assert rings[1].start != 0 and rings[1].len == caps[1]  # the small ring slid and wrapped
+    for s in (0, 1):
+        assert_close(np.concatenate(got[s]), np.concatenate(want[s]), what=f"sequence {s}")
+        k, v, ln, st = exported[s]
+        assert (ln, st) == (rings[s].len, rings[s].start), f"sequence {s} ring metadata"
+        np.testing.assert_array_equal(v, rings[s].v)
+        assert_close(k, rings[s].k, atol=2e-3, rtol=2e-3, what=f"sequence {s} K ring")
+
+
+@pytest.mark.parametrize("n,cap,start_len", [(3000, 2048, 0), (700, 300, 250)])
+def test_prefill_longer_than_ring(n, cap, start_len):
+    """A prompt longer than the ring: the reference's ring slides once full (qwen3_5.cpp:974-983),
+    so token t sees only the last `cap` tokens and the ring ends holding the last `cap` of the
+    prompt with start = (old start + overflow) mod cap.  3,000 tokens into the reference's
+    2,048-slot ring (0.8B shape, fresh ring), and 700 tokens into a 300-slot ring that already
+    holds 250 (wrapped at slot 123).  Against the oracle's per-token loop; metadata and V exact."""
+    hq, hkv = 8, 2
+    rng = np.random.default_rng(n)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(n)
+    qn, kn = weights(rng)
+    rope = po.rope_table(4096, R, 1e7)
+    shape = fa_shape(hq, hkv, D, R, 1e7)
+    ring = po.KVRing.empty(cap, hkv, D)
+    if start_len:
+        ring.k[:] = f16(rng.standard_normal(ring.k.shape))
+        ring.v[:] = f16(rng.standard_normal(ring.v.shape))
+        ring.len, ring.start = start_len, 123
+    proj = torch.randn(1, n, hq * 2 * D + 2 * hkv * D, generator=gen, device="cuda").to(torch.bfloat16)
+    with Context(layer_types=[ab.LAYER_FULL_ATTN], num_q_heads=hq, num_kv_heads=hkv, head_dim=D, rot_dim=R,
+                 rope_theta=1e7, max_seqs=1, kv_capacity=cap) as ctx:
+        ctx.set_full_attn_weights(0, qn, kn)
+        if start_len:
+            ctx.kv_import(0, 0, ring.k, ring.v, ring.len, ring.start)
+        plan = ctx.plan([0])
+        out = ctx.full_attn_prefill(plan, 0, proj, start_pos=start_len).cpu().numpy()[0]
+        assert ctx.device_error() == 0
+        k, v, ln, st = ctx.kv_export(0, 0)
+        plan.close()
+    want = po.full_attn_tokens("oracle", shape, po.make_variant(kv_round_f16=1), qn, kn, ring,
+                               proj.float().cpu().numpy()[0], start_len, rope)
+    assert_close(out, want, what=f"{n} tokens into a {cap}-slot ring")
+    assert (ln, st) == (ring.len, ring.start) == (cap, (123 * bool(start_len) + start_len + n - cap) % cap)
+    np.testing.assert_array_equal(v, ring.v)
+    assert_close(k, ring.k, atol=2e-3, rtol=2e-3, what="K ring")
 
 
 @pytest.mark.parametrize("case", ["rope_half_f32_proj", "rope_half_bf16_proj", "rot40_fallback_prep",

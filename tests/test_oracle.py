@@ -132,3 +132,89 @@ def test_oracle_equals_reference_live(seed):
         res.append((po.deltanet_tokens(kind, shape, var, cw, A, dtb, nw, st, proj), st.ssm.copy()))
     np.testing.assert_array_equal(res[0][0], res[1][0])
     np.testing.assert_array_equal(res[0][1], res[1][1])
+
+
+# ---------------------------------------------------------------- decay-first (HF-order) DeltaNet
+
+def _hf_oracle_run(g, l2_eps):
+    from anelm_b200.state_layout import conv_shift_to_ring
+
+    Hk, Hv, dk, dv, K = (int(x) for x in g["dims"])
+    shape = po.make_shape(lin_num_key_heads=Hk, lin_num_val_heads=Hv, lin_key_dim=dk, lin_val_dim=dv,
+                          conv_kernel=K)
+    ring, pos = conv_shift_to_ring(g["shift0"])
+    st = po.DeltaState(g["ssm0"].copy(), ring.copy(), pos)
+    out = po.deltanet_tokens("oracle", shape, po.make_variant(delta_hf=1, l2_eps=l2_eps), g["conv_w"], g["A"],
+                             g["dt_bias"], g["norm_w"], st, g["proj"].astype(np.float32))
+    return out, st
+
+
+@pytest.mark.parametrize("l2_eps", [0.0, 1e-6])
+def test_oracle_hf_order_matches_reference_layer(golden, l2_eps):
+    """The oracle's decay-first branch against the hybrid v2 export's own DeltaNetLayer
+    (scripts/export_hybrid_chunks.py:83-160, run from the reference source by
+    tests/golden/make_golden.py): outputs and state within the parity tolerance, the conv
+    shift register bit-exact.  Both L2 forms agree with F.normalize here: cpu_ops's
+    sqrt(sum + 1e-12) (l2_eps 0) and the validators' rsqrt(sum + 1e-6)."""
+    from anelm_b200.state_layout import conv_ring_to_shift
+    from helpers import assert_close
+
+    g = golden("deltanet_hf_ref.npz")
+    out, st = _hf_oracle_run(g, l2_eps)
+    assert_close(out, g["out"], what="HF-order outputs vs export_hybrid_chunks DeltaNetLayer")
+    assert_close(st.ssm, g["ssm"], what="HF-order state")
+    np.testing.assert_array_equal(conv_ring_to_shift(st.conv, st.conv_pos)[:, 1:], g["shift"][:, 1:])
+    # much closer than the tolerance: the same fp32 math in another order
+    assert np.abs(out - g["out"]).max() < 1e-4
+
+
+def test_oracle_hf_order_is_not_the_cpuops_order(golden):
+    """The fixture separates the two delta-rule orders: the cpu_ops order misses it."""
+    from anelm_b200.state_layout import conv_shift_to_ring
+
+    g = golden("deltanet_hf_ref.npz")
+    Hk, Hv, dk, dv, K = (int(x) for x in g["dims"])
+    shape = po.make_shape(lin_num_key_heads=Hk, lin_num_val_heads=Hv, lin_key_dim=dk, lin_val_dim=dv)
+    ring, pos = conv_shift_to_ring(g["shift0"])
+    st = po.DeltaState(g["ssm0"].copy(), ring.copy(), pos)
+    out = po.deltanet_tokens("oracle", shape, po.make_variant(), g["conv_w"], g["A"], g["dt_bias"], g["norm_w"],
+                             st, g["proj"].astype(np.float32))
+    assert np.abs(out - g["out"]).max() > 1e-2
+
+
+@pytest.mark.parametrize("Hk,Hv,T", [(2, 4, 70), (1, 2, 130)])
+def test_oracle_delta_rule_matches_transformers(Hk, Hv, T):
+    """The bare decay-first delta rule (oracle gated_delta_tokens, delta_hf=1) against the
+    installed transformers Qwen3.5 implementation, called as a library:
+    torch_recurrent_gated_delta_rule and the chunked torch_chunk_gated_delta_rule (chunk 64,
+    T not a multiple of it), from a nonzero initial state.  transformers scales q by
+    1/sqrt(dk) itself and wants q/k repeated to the value heads."""
+    torch = pytest.importorskip("torch")
+    mq = pytest.importorskip("transformers.models.qwen3_5.modeling_qwen3_5")
+    from helpers import assert_close
+
+    rng = np.random.default_rng(T)
+    dk = dv = 128
+    q = rng.standard_normal((T, Hk, dk)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k = rng.standard_normal((T, Hk, dk)).astype(np.float32)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((T, Hv, dv)).astype(np.float32)
+    lg = (-0.1 * rng.random((T, Hv)) - 0.01).astype(np.float32)
+    beta = rng.random((T, Hv)).astype(np.float32)
+    s0 = (0.1 * rng.standard_normal((Hv, dk, dv))).astype(np.float32)
+    st = s0.copy()
+    y = po.gated_delta_tokens("oracle", q / np.sqrt(dk), k, v, lg, beta, st, delta_hf=1)
+
+    rep = Hv // Hk
+    tq = torch.from_numpy(np.repeat(q, rep, axis=1))[None]
+    tk = torch.from_numpy(np.repeat(k, rep, axis=1))[None]
+    tv, tg, tb = (torch.from_numpy(a)[None] for a in (v, lg, beta))
+    init = torch.from_numpy(s0)[None]
+    y_rec, s_rec = mq.torch_recurrent_gated_delta_rule(tq, tk, tv, tg, tb, init.clone(), True)
+    assert_close(y, y_rec[0].numpy(), what="vs torch_recurrent_gated_delta_rule")
+    assert_close(st, s_rec[0].numpy(), what="state vs torch_recurrent_gated_delta_rule")
+    y_ch, s_ch = mq.torch_chunk_gated_delta_rule(tq, tk, tv, tg, tb, initial_state=init.clone(),
+                                                 output_final_state=True)
+    assert_close(y, y_ch[0].numpy(), what="vs torch_chunk_gated_delta_rule")
+    assert_close(st, s_ch[0].numpy(), what="state vs torch_chunk_gated_delta_rule")
