@@ -11,7 +11,7 @@ decodes them with its own context.  This module holds the host-side pieces:
 * `max_over_ranks` -- the step time reported for a multi-GPU run (the slowest
   rank), one all-reduce outside the timed region.
 * `gather_heads` -- the single collective of head-sharded prefill: every rank
-  computed the output columns of its heads; one all-gather and a reorder give
+  computed the output columns of its heads; one all-gather and a transpose give
   every rank the full [tokens][Hq*d] output.
 
 Works with any torch.distributed backend (NCCL on GPUs, gloo in the CPU tests).
@@ -110,18 +110,19 @@ def value_head_shard(n_key_heads: int, n_val_heads: int, world: int, rank: int):
 
 def gather_heads(local_out, n_q_heads: int, n_kv_heads: int, head_dim: int, group=None):
     """All-gather of head-sharded outputs: local_out [tokens][len(my q heads) * head_dim]
-    on every rank -> [tokens][n_q_heads * head_dim] in global head order."""
+    on every rank -> [tokens][n_q_heads * head_dim] in global head order.
+
+    head_shard gives every rank a contiguous block of query heads, in rank order, all of the
+    same size, so one all_gather_into_tensor ([world][tokens][cols]) and one transpose to
+    [tokens][world][cols] put every column in place."""
     import torch
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
-    parts = [torch.empty_like(local_out) for _ in range(world)]
-    dist.all_gather(parts, local_out.contiguous(), group=group)
-    tokens = local_out.shape[0]
-    out = torch.empty(tokens, n_q_heads * head_dim, dtype=local_out.dtype, device=local_out.device)
-    for r, part in enumerate(parts):
+    for r in range(world):  # the layout this relies on (cheap host-side check)
         qh, _ = head_shard(n_q_heads, n_kv_heads, world, r)
-        pv = part.view(tokens, len(qh), head_dim)
-        for j, h in enumerate(qh):
-            out[:, h * head_dim:(h + 1) * head_dim] = pv[:, j]
-    return out
+        assert qh == list(range(r * len(qh), (r + 1) * len(qh))), "head shards must be contiguous and in rank order"
+    tokens, cols = local_out.shape
+    parts = torch.empty(world * tokens, cols, dtype=local_out.dtype, device=local_out.device)
+    dist.all_gather_into_tensor(parts, local_out.contiguous(), group=group)
+    return parts.view(world, tokens, cols).transpose(0, 1).reshape(tokens, world * cols)

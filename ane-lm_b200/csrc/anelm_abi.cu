@@ -22,6 +22,7 @@
 #include "anelm_b200.h"
 #include "kernels.h"
 #include "ops.h"
+#include "tc100.cuh"
 
 using namespace anelm;
 
@@ -1178,6 +1179,34 @@ ANELM_API int anelm_py_cpu_attention(anelm_ctx* ctx, int layer, int seq, const u
         cudaMemset(ctx->err, 0, 4);
         return fail(code, "device reported status %d", code);
     }
+    return ANELM_OK;
+}
+
+// ---- bounded-wait self-test ----
+
+namespace {
+// One thread waits on an mbarrier that nothing arrives on, with the same bounded wait every
+// tensor-core kernel uses; after `polls` polls it records ANELM_ERR_TIMEOUT in the context's error
+// word and returns.  No copy or MMA is in flight, so the give-up path leaves nothing behind.
+__global__ void bounded_wait_probe_kernel(int* err, uint32_t polls) {
+    __shared__ uint64_t bar;
+    __shared__ int abort;
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&bar, 1);
+        abort = 0;
+        tc::fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) tc::mbar_wait_polls(&bar, 0, err, ANELM_ERR_TIMEOUT, &abort, polls);
+}
+}  // namespace
+
+ANELM_API int anelm_selftest_wait_timeout(anelm_ctx* ctx, unsigned polls, void* stream) {
+    if (!ctx) return fail(ANELM_ERR_INVALID_ARG, "null context");
+    if (polls == 0 || polls > tc::kWaitPolls) return fail(ANELM_ERR_INVALID_ARG, "polls must be in [1, %u]", tc::kWaitPolls);
+    DeviceGuard dg(ctx->device);
+    bounded_wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(ctx->err, polls);
+    CUDA_TRY(cudaGetLastError());
     return ANELM_OK;
 }
 

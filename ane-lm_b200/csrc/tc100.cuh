@@ -64,15 +64,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // already gave up (*abort != 0); the first thread to give up records `code` in
 // *err and raises *abort, so every role of the CTA runs to its exit quickly.
 constexpr uint32_t kWaitPolls = 1u << 22;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
-                                          volatile int* abort) {
-    for (uint32_t i = 0; i < kWaitPolls; i++) {
+__device__ __forceinline__ bool mbar_wait_polls(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                volatile int* abort, uint32_t polls) {
+    for (uint32_t i = 0; i < polls; i++) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255) == 255 && *abort) return false;
     }
     *abort = 1;
     if (err) atomicCAS(err, 0, code);
     return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          volatile int* abort) {
+    return mbar_wait_polls(bar, parity, err, code, abort, kWaitPolls);
 }
 
 // ---------------------------------------------------------------- TMA

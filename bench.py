@@ -21,6 +21,7 @@ fraction, clocks and the reference CPU core timed on the same inputs.
     python bench.py --workload fa_b1|gdn_b1      # BASELINE configs 1 / 2 alone
     python bench.py --workload fa_prefill [--prefill-batch 8]   # BASELINE config 3 alone
     python bench.py --workload gdn_prefill                      # BASELINE config 4 alone
+    torchrun ... bench.py --workload fa_prefill|gdn_prefill     # configs 3 (B=1) / 4 head-sharded over N GPUs
     python bench.py --workload proj|lm_head [--seqs 256]       # the steps next to the core
     python bench.py --workload gdn_layer [--seqs 256]          # one DeltaNet decode layer (ncu size)
 
@@ -640,6 +641,124 @@ def gdn_chunk_flops(T, Hv, B=1, C=64, dk=128, dv=128):
     return float(2 * C * C * (3 * dk + 2 * dv) + 6 * C * dk * dv) * n_chunks * Hv * B
 
 
+def wl_prefill_sharded(args, torch, device, world, rank, which):
+    """Configs 3 (B = 1) and 4 split over the ranks for a single long sequence: causal prefill by
+    KV-head group (shard.head_shard, parallel.sharded_full_attn_prefill) or the chunked delta rule by
+    value head (shard.value_head_shard); each rank computes its heads, then one all-gather gives every
+    rank the full output.  Each rank's input columns are selected before the timed region (in a model
+    they come from that rank's share of the in-projection).  Time = max over ranks of the whole step;
+    the all-gather's share is timed with events around it."""
+    import torch.distributed as dist
+
+    import anelm_b200 as ab
+    from anelm_b200.core import Context, gated_delta_chunked
+    from anelm_b200.parallel import local_proj_columns
+    from anelm_b200.shard import gather_heads, head_shard, max_over_ranks, value_head_shard
+
+    _, tpeak, tkind = peaks()
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    if which == "fa":
+        n = args.prefill_len
+        rng = np.random.default_rng(0)
+        qh, kvh = head_shard(HQ, HKV, world, rank)
+        ctx = Context(device=device.index or 0, layer_types=[ab.LAYER_FULL_ATTN], num_q_heads=len(qh),
+                      num_kv_heads=len(kvh), head_dim=HD, rot_dim=ROT, rope_theta=1e7, max_seqs=1, kv_capacity=n)
+        ctx.set_full_attn_weights(0, (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32),
+                                  (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32))
+        plan = ctx.plan([0])
+        proj = torch.randn(n, FA_PROJ, generator=g, device=device).to(torch.bfloat16)
+        cols = local_proj_columns(HQ, HKV, HD, qh, kvh).to(device)
+        local = proj.index_select(1, cols).unsqueeze(0).contiguous()
+        out_local = torch.empty(1, n, len(qh) * HD, device=device, dtype=torch.bfloat16)
+
+        def compute():
+            ctx.full_attn_prefill(plan, 0, local, 0, out_local)
+
+        def collect():
+            return gather_heads(out_local[0], HQ, HKV, HD)
+
+        def before():
+            ctx.reset(-1)
+
+        flops = 4.0 * n * n * HD * HQ / 2
+        metric = f"head-sharded causal prefill TFLOP/s (cfg3 B=1, S={n}, {world} GPUs)"
+        shard = f"q heads {qh[0]}-{qh[-1]}, kv heads {kvh}"
+        gathered = n * HQ * HD * 2
+    else:
+        T, Hk, Hv = args.gdn_len, 16, 32
+        keys, vals = value_head_shard(Hk, Hv, world, rank)
+        k0, k1, v0, v1 = keys[0], keys[-1] + 1, vals[0], vals[-1] + 1
+        q = torch.randn(1, T, Hk, 128, generator=g, device=device).to(torch.bfloat16)
+        k = torch.randn(1, T, Hk, 128, generator=g, device=device)
+        k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+        v = torch.randn(1, T, Hv, 128, generator=g, device=device).to(torch.bfloat16)
+        lg = -0.1 * torch.rand(1, T, Hv, generator=g, device=device)
+        beta = torch.rand(1, T, Hv, generator=g, device=device)
+        ql, kl = q[:, :, k0:k1].contiguous(), k[:, :, k0:k1].contiguous()
+        vl, lgl, bl = v[:, :, v0:v1].contiguous(), lg[:, :, v0:v1].contiguous(), beta[:, :, v0:v1].contiguous()
+        state = torch.zeros(1, v1 - v0, 128, 128, device=device)
+        y = torch.empty(1, T, v1 - v0, 128, device=device, dtype=torch.bfloat16)
+        ws = torch.empty(ab.lib().anelm_gated_delta_chunked_workspace_bytes(1, T, k1 - k0, v1 - v0),
+                         dtype=torch.uint8, device=device)
+        parts = torch.empty(world * T, (v1 - v0) * 128, device=device, dtype=torch.bfloat16)
+
+        def compute():
+            gated_delta_chunked(ql, kl, vl, lgl, bl, state, ab.DELTA_CPUOPS, y=y, workspace=ws)
+
+        def collect():
+            dist.all_gather_into_tensor(parts, y.view(T, -1))
+            return parts.view(world, T, -1).transpose(0, 1).reshape(T, -1)
+
+        def before():
+            pass
+
+        flops = gdn_chunk_flops(T, Hv, 1)
+        metric = f"value-head-sharded chunked DeltaNet prefill TFLOP/s (cfg4, S={T}, {world} GPUs)"
+        shard = f"value heads {v0}-{v1 - 1}, key heads {k0}-{k1 - 1}"
+        gathered = T * Hv * 128 * 2
+    for _ in range(max(3, args.warmup)):
+        before()
+        compute()
+        collect()
+    torch.cuda.synchronize(device)
+    steps = max(args.steps, 5)
+    tot, gat = [], []
+    clocks = ClockSampler(device.index or 0).start()
+    for _ in range(steps):
+        before()
+        flush.zero_()
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        compute()
+        e1.record()
+        collect()
+        e2.record()
+        torch.cuda.synchronize(device)
+        tot.append(max_over_ranks(e0.elapsed_time(e2), device))
+        gat.append(max_over_ranks(e1.elapsed_time(e2), device))
+    ck = clocks.stop()
+    ms = statistics.median(tot)
+    if which == "fa":
+        plan.close()
+        ctx.close()
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"metric": metric, "value": round(tf, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 in, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": metric, "rank0_shard": shard, "l2": "256 MB buffer written before each step",
+                       "parallelism": f"heads over {world} GPUs, one all-gather of the output"},
+            "roofline": tensor_roof(tf / world, tpeak, tkind, "per GPU, whole step", flops / world),
+            "allgather": {"ms": round(statistics.median(gat), 4), "share": round(statistics.median(gat) / ms, 4),
+                          "bytes_gathered": gathered,
+                          "gbs_per_gpu_in": round(gathered * (world - 1) / world / (statistics.median(gat) * 1e-3) / 1e9,
+                                                  1)},
+            "clocks": ck, "gpu_launches": steps * (3 if which == "fa" else 3)}
+
+
 def run_workloads(args, torch, device):
     out = {}
     for name, fn in (("cfg1", lambda: wl_decode_b1(args, torch, device, "fa")),
@@ -826,6 +945,8 @@ def run_gpu(args):
                 result["gpu_launches"] += sum(w["gpu_launches"] for w in result["workloads"].values())
         elif args.workload in ("fa_b1", "gdn_b1"):
             result = single_line(args, wl_decode_b1(args, torch, device, args.workload[:-3]))
+        elif args.workload in ("fa_prefill", "gdn_prefill") and world > 1:
+            result = wl_prefill_sharded(args, torch, device, world, rank, args.workload[:-8])
         elif args.workload == "fa_prefill":
             result = single_line(args, wl_fa_prefill(args, torch, device, args.prefill_batch, args.prefill_len,
                                                      args.steps))

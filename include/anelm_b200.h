@@ -370,6 +370,13 @@ ANELM_API int anelm_softmax(float* x, int n, int rows, void* stream);
 ANELM_API int anelm_matvec(float* y, const float* W, const float* x, int out_dim, int in_dim,
                            void* stream);
 
+/* Self-test of the failure path every tensor-core kernel here shares: one thread waits on an
+ * mbarrier that nothing ever arrives on, with the kernels' bounded wait, gives up after `polls`
+ * polls (1 .. 2^22) and records ANELM_ERR_TIMEOUT in the context's device error word, which
+ * anelm_get_device_error then returns (and clears); the context stays usable.  No counterpart in
+ * the reference (its CPU core has no waits).  Asynchronous on `stream`. */
+ANELM_API int anelm_selftest_wait_timeout(anelm_ctx* ctx, unsigned polls, void* stream);
+
 /* Library / device introspection (no GPU needed for the version). */
 ANELM_API const char* anelm_version(void);
 ANELM_API int anelm_device_check(int device);

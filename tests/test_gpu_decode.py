@@ -389,3 +389,28 @@ def test_errors_are_status_codes():
         with pytest.raises(ab.AnelmError) as e:
             ctx.deltanet_from_proj(0, 0, torch.zeros(ctx.gdn_proj_dim, device="cuda"))
         assert e.value.status == 6                        # weights not set
+
+
+def test_bounded_wait_gives_up_and_the_context_stays_usable():
+    """The failure path of every mbarrier wait in the tensor-core kernels: a wait on a barrier that
+    nothing arrives on gives up after its poll budget, records ANELM_ERR_TIMEOUT in the context's
+    error word and returns (no trap, no hang); the status is read on the host and cleared, and the
+    context then decodes correctly."""
+    from anelm_b200._lib import lib
+
+    rng = np.random.default_rng(31)
+    shape = fa_shape()
+    proj, qn, kn = fa_inputs(rng, shape, 2)
+    with fa_ctx(shape, cap=64) as ctx:
+        ctx.set_full_attn_weights(0, qn, kn)
+        assert ctx.device_error() == 0
+        assert lib().anelm_selftest_wait_timeout(ctx.handle, 4096, None) == 0
+        assert ctx.device_error() == ab._lib.ERR_TIMEOUT
+        assert ctx.device_error() == 0                      # read and cleared
+        assert lib().anelm_selftest_wait_timeout(ctx.handle, 0, None) == ab._lib.ERR_INVALID_ARG
+        p = dev(proj, torch.float16)
+        got = torch.stack([ctx.full_attn_from_proj(0, 0, p[t].contiguous(), t) for t in range(2)]).cpu().numpy()
+        assert ctx.device_error() == 0
+    want = po.full_attn_tokens("oracle", shape, po.make_variant(kv_round_f16=1), qn, kn, po.KVRing.empty(64, 2, 256),
+                               proj, 0, po.rope_table(4096, 64, 1e7))
+    assert_close(got, want, what="decode after a timed-out wait")
