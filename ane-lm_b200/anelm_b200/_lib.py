@@ -91,6 +91,10 @@ SIGNATURES = {
     "anelm_gqa_attention": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "anelm_gqa_attention_noalloc": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],
     "anelm_selftest_wait_timeout": [_vp, ctypes.c_uint, _vp],
+    "anelm_full_attn_prefill_gather": [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _i, _i, _i, _vp],
+    "anelm_ipc_handle": [_vp, _vp, ctypes.POINTER(ctypes.c_size_t)],
+    "anelm_ipc_open": [_vp, ctypes.c_size_t, _i, ctypes.POINTER(ctypes.c_void_p)],
+    "anelm_ipc_close": [_vp],
     "anelm_ssm_step": [_vp, _vp, _vp, _vp, _vp, _f, _f, _i, _i, _vp],
     "anelm_conv1d_update": [_vp, _vp, _ip, _vp, _vp, _i, _i, _vp],
     "anelm_rmsnorm": [_vp, _vp, _vp, _i, _f, _i, _vp],

@@ -22,7 +22,7 @@
 #include "anelm_b200.h"
 #include "kernels.h"
 #include "ops.h"
-#include "tc100.cuh"
+#include "tc100.cuh"  // (also brings cuda.h: CUresult / CUdeviceptr for the IPC helpers)
 
 using namespace anelm;
 
@@ -1073,9 +1073,9 @@ ANELM_API int anelm_layer_decode(anelm_ctx* ctx, const anelm_plan* plan, int lay
                          "layer out-projection");
 }
 
-ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,
-                                      const void* proj, int proj_dtype, int start_pos, void* out, int out_dtype,
-                                      void* stream) {
+static int full_attn_prefill_impl(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens, const void* proj,
+                                  int proj_dtype, int start_pos, void* out, int out_dtype, long long out_stride,
+                                  const PrefillDests* dests, void* stream) {
     if (int rc = check_layer(ctx, layer, ANELM_LAYER_FULL_ATTN)) return rc;
     if (!plan || plan->ctx != ctx) return fail(ANELM_ERR_INVALID_ARG, "plan belongs to another context");
     if (!proj || !out || n_tokens <= 0) return fail(ANELM_ERR_INVALID_ARG, "null tensor or no tokens");
@@ -1144,14 +1144,99 @@ ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, in
     p.kv_cap = ctx->kv_cap;
     p.out = out;
     p.out_dtype = out_dtype;
-    p.out_stride = (long long)c.num_q_heads * c.head_dim;
+    p.out_stride = out_stride;
     p.err = ctx->err;
-    const int rc = launch_fa_prefill(p, ctx->prefill_ws, c.head_dim, static_cast<cudaStream_t>(stream));
+    const int rc = launch_fa_prefill(p, ctx->prefill_ws, c.head_dim, static_cast<cudaStream_t>(stream), dests);
     if (rc) return launch_status(rc, "fa_prefill");
     for (int s : plan->seq_h) {
         int& len = ctx->len_h[(size_t)f * c.max_seqs + s];
         len = (int)std::min<long long>((long long)len + n_tokens, ctx->cap_h[s]);
     }
+    return ANELM_OK;
+}
+
+ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,
+                                      const void* proj, int proj_dtype, int start_pos, void* out, int out_dtype,
+                                      void* stream) {
+    if (!ctx) return fail(ANELM_ERR_INVALID_ARG, "null context");
+    return full_attn_prefill_impl(ctx, plan, layer, n_tokens, proj, proj_dtype, start_pos, out, out_dtype,
+                                  (long long)ctx->cfg.num_q_heads * ctx->cfg.head_dim, nullptr, stream);
+}
+
+ANELM_API int anelm_full_attn_prefill_gather(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,
+                                             const void* proj, int proj_dtype, int start_pos, void* const* outs,
+                                             int n_outs, int col0, int out_cols, int out_dtype, void* stream) {
+    if (!ctx || !outs) return fail(ANELM_ERR_INVALID_ARG, "null argument");
+    if (n_outs < 1 || n_outs > 8) return fail(ANELM_ERR_INVALID_ARG, "1 to 8 output buffers");
+    for (int r = 0; r < n_outs; r++)
+        if (!outs[r] || (uintptr_t)outs[r] % 16) return fail(ANELM_ERR_INVALID_ARG, "output %d null or not 16-byte aligned", r);
+    if (out_dtype != ANELM_BF16 && out_dtype != ANELM_F16) return fail(ANELM_ERR_UNSUPPORTED, "16-bit outputs only");
+    const long long cols = (long long)ctx->cfg.num_q_heads * ctx->cfg.head_dim;
+    if (col0 < 0 || col0 % 64 || out_cols % 8 || col0 + cols > out_cols)
+        return fail(ANELM_ERR_INVALID_ARG, "columns [%d, %lld) outside a row of %d (or not 64-aligned)", col0, col0 + cols,
+                    out_cols);
+    PrefillDests d{outs, n_outs, col0};
+    return full_attn_prefill_impl(ctx, plan, layer, n_tokens, proj, proj_dtype, start_pos, outs[0], out_dtype,
+                                  out_cols, &d, stream);
+}
+
+// ---- CUDA IPC: map another process's device buffer (peer outputs of a sharded prefill) ----
+
+namespace {
+typedef CUresult (*AddrRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddrRangeFn addr_range_fn() {
+    static AddrRangeFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<AddrRangeFn>(f);
+    }();
+    return fn;
+}
+std::mutex g_ipc_mu;
+std::map<void*, void*> g_ipc_base;  // pointer handed out by anelm_ipc_open -> mapping base
+}  // namespace
+
+ANELM_API int anelm_ipc_handle(const void* dev_ptr, void* handle_out, size_t* offset_out) {
+    if (!dev_ptr || !handle_out || !offset_out) return fail(ANELM_ERR_INVALID_ARG, "null argument");
+    AddrRangeFn range = addr_range_fn();
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (!range || range(&base, &size, (CUdeviceptr)dev_ptr) != CUDA_SUCCESS)
+        return fail(ANELM_ERR_CUDA, "cuMemGetAddressRange failed for %p", dev_ptr);
+    cudaIpcMemHandle_t h;
+    CUDA_TRY(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    memcpy(handle_out, &h, sizeof(h));
+    *offset_out = (size_t)((CUdeviceptr)dev_ptr - base);
+    return ANELM_OK;
+}
+
+ANELM_API int anelm_ipc_open(const void* handle, size_t offset, int device, void** ptr_out) {
+    if (!handle || !ptr_out) return fail(ANELM_ERR_INVALID_ARG, "null argument");
+    DeviceGuard dg(device);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    CUDA_TRY(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+    void* p = static_cast<char*>(base) + offset;
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    g_ipc_base[p] = base;
+    *ptr_out = p;
+    return ANELM_OK;
+}
+
+ANELM_API int anelm_ipc_close(void* ptr) {
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_ipc_mu);
+        auto it = g_ipc_base.find(ptr);
+        if (it == g_ipc_base.end()) return fail(ANELM_ERR_INVALID_ARG, "%p was not opened by anelm_ipc_open", ptr);
+        base = it->second;
+        g_ipc_base.erase(it);
+    }
+    CUDA_TRY(cudaIpcCloseMemHandle(base));
     return ANELM_OK;
 }
 

@@ -157,6 +157,16 @@ __global__ void __launch_bounds__(256) fa_prefill_gather_kernel(const FaPrefillP
 // MMAs (~1.4 us per tile).  Each barrier is used once per tile (K, V) or once per use of
 // a TMEM buffer (S_FULL, P_FULL, PV_DONE), so no barrier runs two phases ahead of a waiter.
 // PV_DONE[s] frees TMEM buffer s (its P was read) and says O is stable for rescaling.
+// Destinations of the output tiles: this context's own output, or, for a head-sharded prefill, the
+// output buffer of every rank (peer buffers mapped into this process), each a [B][n][cols] tensor
+// of which this launch's heads fill columns [col0, col0 + Hq D).  wait_full: the storing thread
+// waits until the stores have completed, not just until their shared-memory source was read.
+constexpr int kMaxOuts = 8;
+struct OutMaps {
+    CUtensorMap m[kMaxOuts];
+    int n, col0, wait_full;
+};
+
 enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 2, V_FULL = 3, V_EMPTY = 4, S_FULL = 5, P_FULL = 7, PV_DONE = 9,
            G_FULL = 11, N_BARS = 12 };
 
@@ -661,7 +671,7 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
 __global__ void __launch_bounds__(kThreads, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG,
-                      const __grid_constant__ CUtensorMap tmO, const FaPrefillParams p) {
+                      const __grid_constant__ OutMaps om, const FaPrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
@@ -901,10 +911,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::fence_proxy_async_smem();
             tc::named_bar_sync(5, 2 * kBM);
             if (tid == 0) {
-                tc::prefetch_tmap(&tmO);
-                for (int ch = 0; ch < 4; ch++) tc::tma_store_3d(&tmO, sQ + ch * (kBM * 128), h * kD + ch * 64, q0, b);
+                for (int r = 0; r < om.n; r++) {
+                    tc::prefetch_tmap(&om.m[r]);
+                    for (int ch = 0; ch < 4; ch++)
+                        tc::tma_store_3d(&om.m[r], sQ + ch * (kBM * 128), om.col0 + h * kD + ch * 64, q0, b);
+                }
                 tc::bulk_commit_group();
-                tc::bulk_wait_group_read0();
+                if (om.wait_full) tc::bulk_wait_group0();
+                else tc::bulk_wait_group_read0();
             }
         } else if (nT > 0) {
             // ---------------- epilogue part 1: O / l into shared memory ----------------
@@ -1007,7 +1021,7 @@ size_t fa_prefill_workspace_bytes(int B, int n, int P, int Hq, int Hkv, int head
     return (size_t)B * head_dim * 2 * (2 * (size_t)Hq * n_pad + 2 * (size_t)Hkv * (P + n_pad)) + (size_t)B * 16;
 }
 
-int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream) {
+int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream, const PrefillDests* dests) {
     if (head_dim != kD || p.P < 0 || p.P % kBN || !p.kv_len || !p.kv_start || !p.kv_cap || !p.kv_base ||
         !p.k_pool || !p.v_pool)
         return ANELM_ERR_UNSUPPORTED;
@@ -1029,13 +1043,32 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
     fa_prefill_gather_kernel<<<dim3(std::max(1, (p.P + 63) / 64), p.B), 256, 0, stream>>>(p);
     // TMA epilogue: 16-bit output with a 16-byte aligned base and row stride; sigmoid(gate) as fp16
     // [B][n][Hq * D] after V in the workspace
-    CUtensorMap mG = mQ, mO = mQ;
+    CUtensorMap mG = mQ;
+    OutMaps om{};
     __half* sg = p.Vh + nk;
-    p.tma_epilogue = (p.out_dtype == ANELM_BF16 || p.out_dtype == ANELM_F16) && ((uintptr_t)p.out % 16 == 0) &&
-                     (p.out_stride % 8 == 0) &&
-                     make_map_rows(&mO, p.out_dtype, p.out, (uint64_t)p.Hq * kD, p.n, p.B, p.out_stride) &&
-                     (!p.gate || make_map_rows(&mG, ANELM_F16, sg, (uint64_t)p.Hq * kD, p.n, p.B,
-                                               (uint64_t)p.Hq * kD));
+    const bool out16 = p.out_dtype == ANELM_BF16 || p.out_dtype == ANELM_F16;
+    if (dests && dests->n > 0) {
+        // every destination by TMA tile stores (the only epilogue that writes them all)
+        if (!out16 || dests->n > kMaxOuts || p.out_stride % 8 || dests->col0 < 0 || dests->col0 % 64 ||
+            dests->col0 + (long long)p.Hq * kD > p.out_stride)
+            return ANELM_ERR_UNSUPPORTED;
+        for (int r = 0; r < dests->n; r++)
+            if ((uintptr_t)dests->ptrs[r] % 16 ||
+                !make_map_rows(&om.m[r], p.out_dtype, dests->ptrs[r], (uint64_t)p.out_stride, p.n, p.B, p.out_stride))
+                return ANELM_ERR_UNSUPPORTED;
+        om.n = dests->n;
+        om.col0 = dests->col0;
+        om.wait_full = 1;
+        p.tma_epilogue = !p.gate || make_map_rows(&mG, ANELM_F16, sg, (uint64_t)p.Hq * kD, p.n, p.B,
+                                                  (uint64_t)p.Hq * kD);
+        if (!p.tma_epilogue) return ANELM_ERR_UNSUPPORTED;
+    } else {
+        om.n = 1;
+        p.tma_epilogue = out16 && ((uintptr_t)p.out % 16 == 0) && (p.out_stride % 8 == 0) &&
+                         make_map_rows(&om.m[0], p.out_dtype, p.out, (uint64_t)p.Hq * kD, p.n, p.B, p.out_stride) &&
+                         (!p.gate || make_map_rows(&mG, ANELM_F16, sg, (uint64_t)p.Hq * kD, p.n, p.B,
+                                                   (uint64_t)p.Hq * kD));
+    }
     if (p.tma_epilogue && p.gate) p.SG = sg;
     const long long row_bytes = p.proj_stride * dtype_bytes(p.proj_dtype);
     const bool vec = (uintptr_t)p.proj % 16 == 0 && row_bytes % 16 == 0 && p.rot_dim % 16 == 0;
@@ -1079,9 +1112,9 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, fa_prefill_kernel, mQ, mK, mV, mG, mO, p) != cudaSuccess) {
+    if (cudaLaunchKernelEx(&cfg, fa_prefill_kernel, mQ, mK, mV, mG, om, p) != cudaSuccess) {
         cudaGetLastError();  // clear, then the plain launch
-        fa_prefill_kernel<<<cfg.gridDim, kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mG, mO, p);
+        fa_prefill_kernel<<<cfg.gridDim, kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mG, om, p);
     }
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }

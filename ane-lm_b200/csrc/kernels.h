@@ -171,7 +171,15 @@ int launch_gdn_prefill(GdnPrefillParams p, void* workspace, cudaStream_t stream)
 int launch_gated_delta_chunked(GdnPrefillParams p, void* workspace, cudaStream_t stream);
 
 size_t fa_prefill_workspace_bytes(int B, int n, int P, int Hq, int Hkv, int head_dim);
-int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream);
+// Extra destinations of a prefill's output: n device addresses (this device's memory or a peer's
+// mapped into this process) of [B][n_tokens][out_stride] 16-bit buffers; the launch's heads fill
+// columns [col0, col0 + Hq D) of each, by TMA tile stores that complete before the CTA exits.
+struct PrefillDests {
+    const void* const* ptrs;
+    int n, col0;
+};
+int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStream_t stream,
+                      const PrefillDests* dests = nullptr);
 
 int launch_fa_decode(const FaDecodeParams& p, int head_dim, int n_blocks, cudaStream_t stream);
 size_t fa_decode_smem_bytes(int head_dim);

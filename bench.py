@@ -525,7 +525,7 @@ def wl_decode_b1(args, torch, device, which):
     ctx.close()
     assert err == 0, f"device reported status {err}"
     gbs = nbytes / (us * 1e-6) / 1e9
-    cpu = cpu_reference_decode_b1(which, args.cpu_seconds_wl)
+    cpu = None if args.no_cpu_baseline else cpu_reference_decode_b1(which, args.cpu_seconds_wl)
     return {"metric": metric, "value": round(1e6 / us, 1), "unit": "tok/s", "us_per_call": round(us, 3),
             "calls_timed": replays * len(calls), "roofline": hbm_roof(gbs, hbm_peak, peak_kind, kname, nbytes),
             "l2": f"calls rotate over {n_copies} sequences ({n_copies * nbytes >> 20} MB > 126 MB L2); CUDA graph",
@@ -579,7 +579,8 @@ def wl_fa_prefill(args, torch, device, B, n=4096, steps=10):
                                     flops),
             "timed": "whole call: prep (QK-norm, RoPE, fp16 Q/K/V, sigmoid gate, ring append) + attention",
             "l2": "256 MB buffer written before each timed call", "clocks": ck,
-            "cpu_baseline": cpu_reference_prefill(B, n, args.cpu_seconds_wl, flops), "gpu_launches": 2 * steps}
+            "cpu_baseline": None if args.no_cpu_baseline else cpu_reference_prefill(B, n, args.cpu_seconds_wl, flops),
+            "gpu_launches": 3 * steps}
 
 
 def wl_gdn_prefill(args, torch, device, B=1, T=8192, steps=10):
@@ -630,7 +631,8 @@ def wl_gdn_prefill(args, torch, device, B=1, T=8192, steps=10):
     return {"metric": f"chunked Gated DeltaNet prefill TFLOP/s (cfg4, Hv 32 / Hk 16, d 128, S={T}, B={B})",
             "value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4), "steps": steps, "roofline": roof,
             "l2": "256 MB buffer written before each timed call", "clocks": ck,
-            "cpu_baseline": cpu_reference_gdn_chunk(T, B, Hk, Hv, flops, args.cpu_seconds_wl),
+            "cpu_baseline": (None if args.no_cpu_baseline else
+                             cpu_reference_gdn_chunk(T, B, Hk, Hv, flops, args.cpu_seconds_wl)),
             "gpu_launches": 3 * steps}
 
 
@@ -652,7 +654,7 @@ def wl_prefill_sharded(args, torch, device, world, rank, which):
 
     import anelm_b200 as ab
     from anelm_b200.core import Context, gated_delta_chunked
-    from anelm_b200.parallel import local_proj_columns
+    from anelm_b200.parallel import PeerOutputs, fused_sharded_full_attn_prefill, local_proj_columns
     from anelm_b200.shard import gather_heads, head_shard, max_over_ranks, value_head_shard
 
     _, tpeak, tkind = peaks()
@@ -673,17 +675,23 @@ def wl_prefill_sharded(args, torch, device, world, rank, which):
         local = proj.index_select(1, cols).unsqueeze(0).contiguous()
         out_local = torch.empty(1, n, len(qh) * HD, device=device, dtype=torch.bfloat16)
 
+        peers = PeerOutputs((1, n, HQ * HD), torch.bfloat16, device)
+
         def compute():
-            ctx.full_attn_prefill(plan, 0, local, 0, out_local)
+            if args.nccl_gather:
+                ctx.full_attn_prefill(plan, 0, local, 0, out_local)
+            else:  # the gather is inside: every rank's epilogue stores into every rank's buffer
+                fused_sharded_full_attn_prefill(ctx, plan, 0, local, peers, HQ, HKV, HD)
 
         def collect():
-            return gather_heads(out_local[0], HQ, HKV, HD)
+            return gather_heads(out_local[0], HQ, HKV, HD) if args.nccl_gather else peers.local
 
         def before():
             ctx.reset(-1)
 
         flops = 4.0 * n * n * HD * HQ / 2
-        metric = f"head-sharded causal prefill TFLOP/s (cfg3 B=1, S={n}, {world} GPUs)"
+        metric = (f"head-sharded causal prefill TFLOP/s (cfg3 B=1, S={n}, {world} GPUs, "
+                  f"{'NCCL all-gather' if args.nccl_gather else 'all-gather fused into the attention epilogue'})")
         shard = f"q heads {qh[0]}-{qh[-1]}, kv heads {kvh}"
         gathered = n * HQ * HD * 2
     else:
@@ -743,6 +751,7 @@ def wl_prefill_sharded(args, torch, device, world, rank, which):
     ck = clocks.stop()
     ms = statistics.median(tot)
     if which == "fa":
+        peers.close()
         plan.close()
         ctx.close()
     tf = flops / (ms * 1e-3) / 1e12
@@ -753,6 +762,8 @@ def wl_prefill_sharded(args, torch, device, world, rank, which):
                        "parallelism": f"heads over {world} GPUs, one all-gather of the output"},
             "roofline": tensor_roof(tf / world, tpeak, tkind, "per GPU, whole step", flops / world),
             "allgather": {"ms": round(statistics.median(gat), 4), "share": round(statistics.median(gat) / ms, 4),
+                          "form": ("NCCL all_gather_into_tensor after the prefill" if which != "fa" or args.nccl_gather
+                                   else "inside the prefill kernel (peer TMA stores); timed here: nothing left"),
                           "bytes_gathered": gathered,
                           "gbs_per_gpu_in": round(gathered * (world - 1) / world / (statistics.median(gat) * 1e-3) / 1e9,
                                                   1)},
@@ -1216,6 +1227,8 @@ def main():
     ap.add_argument("--cpu-seconds-wl", type=float, default=3.0, help="CPU sample per configs 1-4 entry")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-workloads", action="store_true", help="skip the configs 1-4 entries of the default line")
+    ap.add_argument("--nccl-gather", action="store_true",
+                    help="head-sharded prefill: all-gather with NCCL after the kernel instead of inside it")
     ap.add_argument("--traffic-json", default=os.path.join(REPO, "profiles", "traffic.json"))
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

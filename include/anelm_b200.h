@@ -244,6 +244,32 @@ ANELM_API int anelm_full_attn_prefill(anelm_ctx* ctx, const anelm_plan* plan, in
                                       const void* proj, int proj_dtype, int start_pos, void* out, int out_dtype,
                                       void* stream);
 
+/* Head-sharded prefill with the all-gather fused into the attention kernel.  A long prompt split
+ * over GPUs by head (each rank's context holds its share of the query heads and their KV heads)
+ * ends in an all-gather of the gated outputs; here each rank's attention epilogue stores its
+ * output tiles by TMA straight into every rank's output buffer (over NVLink for the peers), so the
+ * transfer overlaps the attention tile by tile and no separate collective moves the data.  outs:
+ * n_outs (<= 8) device addresses usable on this context's device -- this rank's own buffer and the
+ * peers' buffers mapped with anelm_ipc_open -- each [n_seqs][n_tokens][out_cols] of out_dtype
+ * (bf16 or fp16, 16-byte aligned); this context's Hq heads fill columns [col0, col0 + Hq*d) (col0 a
+ * multiple of 64) of every one.  Otherwise as anelm_full_attn_prefill.  The stores have completed
+ * when this call's kernels have; a rank may read its buffer once every rank's call has completed
+ * (order that with a collective on the same stream, e.g. a one-element all-reduce), and may start
+ * the next call into the same buffers only after every rank has finished reading.
+ * Replaces: the prefill loop of qwen3_5.cpp:1205-1217 for one sequence spread over GPUs (the
+ * reference has no multi-device path). */
+ANELM_API int anelm_full_attn_prefill_gather(anelm_ctx* ctx, const anelm_plan* plan, int layer, int n_tokens,
+                                             const void* proj, int proj_dtype, int start_pos, void* const* outs,
+                                             int n_outs, int col0, int out_cols, int out_dtype, void* stream);
+
+/* CUDA IPC plumbing for the peer buffers above (one process per GPU): anelm_ipc_handle gives the
+ * 64-byte handle of the allocation holding dev_ptr and dev_ptr's offset in it; another process
+ * maps it with anelm_ipc_open (peer access enabled on `device`) and unmaps it with anelm_ipc_close.
+ * No counterpart in the reference. */
+ANELM_API int anelm_ipc_handle(const void* dev_ptr, void* handle_out, size_t* offset_out);
+ANELM_API int anelm_ipc_open(const void* handle, size_t offset, int device, void** ptr_out);
+ANELM_API int anelm_ipc_close(void* ptr);
+
 /* Prefill of the plan's sequences through a Gated DeltaNet layer: equivalent to n_tokens
  * successive forward_deltanet_from_proj calls (qwen3_5.cpp:849-909, the per-token loop
  * of qwen3_5.cpp:1205-1217), computed chunkwise (64-token chunks, WY form).  Continues

@@ -1,5 +1,6 @@
 """Multi-GPU paths on real GPUs (skipped with fewer than two): head-sharded causal prefill
-and value-head-sharded chunked DeltaNet prefill over 2 ranks (torchrun, NCCL) against the
+(all-gather by NCCL, and fused into the attention kernel's epilogue over NVLink) and
+value-head-sharded chunked DeltaNet prefill over 2 ranks (torchrun, NCCL) against the
 unsharded call on one GPU — identical per-head arithmetic, so identical outputs and state."""
 import os
 import socket
@@ -33,6 +34,9 @@ def test_head_sharded_prefill_two_ranks(tmp_path):
     d = np.load(out)
     assert int(d["world"]) == 2
     np.testing.assert_array_equal(d["sharded"], d["full"])
+    # the all-gather fused into the attention kernel: every rank's copy equals the unsharded output
+    assert int(d["fused_ok_ranks"]) == 2
+    np.testing.assert_array_equal(d["fused"], d["full16"])
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
