@@ -118,6 +118,9 @@ __device__ __forceinline__ void ring_finish(const FaPrefillParams& p, const Ring
 // zeroed (an attention tile reads them, masked, and P V needs them finite).  Runs before the
 // prep appends to the ring, so it reads the old tokens only.
 __global__ void __launch_bounds__(256) fa_prefill_gather_kernel(const FaPrefillParams p) {
+    // the prep may start now (programmatic dependent launch): it waits for this grid before it reads
+    // the snapshots or appends to a ring
+    asm volatile("griddepcontrol.launch_dependents;");
     const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int seq = p.seq_ids ? p.seq_ids[b] : 0;
     const int len = p.kv_len[seq], start = p.kv_start[seq], cap = p.kv_cap[seq];
@@ -186,6 +189,7 @@ __device__ __forceinline__ void rope_cs_pf(const FaPrefillParams& p, int pos, in
 // One token of one sequence per CTA (256 threads).
 __global__ void __launch_bounds__(256) fa_prefill_prep_kernel(const FaPrefillParams p) {
     extern __shared__ float xs[];  // [(Hq + Hkv) vectors][kD], then v [Hkv][kD]
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the gather kernel's snapshots (a no-op for a plain launch)
     const int t = blockIdx.x, b = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int Hq = p.Hq, Hkv = p.Hkv;
@@ -366,6 +370,7 @@ __device__ __forceinline__ void prep_zero_row(const FaPrefillParams& p, int b, i
 }
 
 __global__ void __launch_bounds__(256, 4) fa_prefill_prep_vec_kernel(const FaPrefillParams p) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the gather kernel's snapshots (a no-op for a plain launch)
     const int t = blockIdx.x, b = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int Hq = p.Hq, Hkv = p.Hkv;
@@ -593,6 +598,9 @@ __global__ void __launch_bounds__(32 * (kPrepWarps + 1), kPrepCtas)
     // gates (q 0-7, gate 0-7, q 8-15, ...), so each warp gets the same number of RMSNorm + RoPE
     // segments (the warps' slowest bounds the stage's release); k and v heads follow
     const bool mix = (Hq & 7) == 0;
+    // consumers read the gather kernel's ring snapshots and append to the rings it read: wait for that
+    // grid (the producer's projection copies do not depend on it and run ahead)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     int cur_b = -1, seq = 0;  // the sequence of row b, its pool base and ring snapshot, reloaded when b changes
     long long kv0 = 0;
     RingSnap rs{0, 0, 1, 0};
@@ -1014,6 +1022,26 @@ bool make_map_rows(CUtensorMap* m, int dtype, const void* base, uint64_t cols, u
 
 }  // namespace
 
+// Launches `kern` as a programmatic dependent of the previous kernel on the stream (its prologue may
+// overlap that kernel; it reads that kernel's results only after griddepcontrol.wait).  Returns
+// nonzero (error cleared) if the launch was refused, so the caller can launch it plainly.
+template <class... KArgs, class... Args>
+static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess) return 0;
+    cudaGetLastError();
+    return 1;
+}
+
 size_t fa_prefill_workspace_bytes(int B, int n, int P, int Hq, int Hkv, int head_dim) {
     const long long n_pad = (n + kBM - 1) / kBM * kBM;
     // fp16 Q [B][Hq][n_pad][D], K and V [B][Hkv][P + n_pad][D], sigmoid(gate) [B][n][Hq][D]; the
@@ -1090,14 +1118,17 @@ int launch_fa_prefill(FaPrefillParams p, void* workspace, int head_dim, cudaStre
         auto kern = half ? (bf ? fa_prefill_prep_bulk_kernel<true, true> : fa_prefill_prep_bulk_kernel<true, false>)
                          : (bf ? fa_prefill_prep_bulk_kernel<false, true> : fa_prefill_prep_bulk_kernel<false, false>);
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        kern<<<grid, 32 * (kPrepWarps + 1), smem, stream>>>(p, stage_bytes, rope_off);
+        if (launch_pdl(kern, dim3(grid), dim3(32 * (kPrepWarps + 1)), smem, stream, p, stage_bytes, rope_off))
+            kern<<<grid, 32 * (kPrepWarps + 1), smem, stream>>>(p, stage_bytes, rope_off);
     } else if (vec) {
-        fa_prefill_prep_vec_kernel<<<dim3(p.n_pad, p.B), 256, 0, stream>>>(p);
+        if (launch_pdl(fa_prefill_prep_vec_kernel, dim3(p.n_pad, p.B), dim3(256), 0, stream, p))
+            fa_prefill_prep_vec_kernel<<<dim3(p.n_pad, p.B), 256, 0, stream>>>(p);
     } else {
         const size_t prep_smem = (size_t)(p.Hq + 2 * p.Hkv) * kD * sizeof(float);
         if (prep_smem > 48 * 1024)
             cudaFuncSetAttribute(fa_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
-        fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
+        if (launch_pdl(fa_prefill_prep_kernel, dim3(p.n_pad, p.B), dim3(256), prep_smem, stream, p))
+            fa_prefill_prep_kernel<<<dim3(p.n_pad, p.B), 256, prep_smem, stream>>>(p);
     }
     cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     // programmatic dependent launch: the prologue (barriers, TMEM allocation) overlaps the prep's

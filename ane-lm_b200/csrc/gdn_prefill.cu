@@ -24,7 +24,10 @@
 // relative) and each product is three mma.sync m16n8k16 (hi*hi + lo*hi + hi*lo) with fp32
 // accumulation, so the products match fp32 arithmetic; plain fp16 operands would let the gated
 // RMSNorm amplify their 2^-12 rounding past the tolerance.  Operands live in memory as a hi
-// plane followed by a lo plane and reach the MMAs through ldmatrix.
+// plane followed by a lo plane and reach the MMAs through ldmatrix.  When the bare core op gets
+// 16-bit q / k / v (bf16 values have 8 significant bits, so they are exact in fp16), their lo
+// planes are zero: they are neither written nor loaded, K K^T / Q K^T take one term, and the
+// products with K, Q or V on one side take two.
 //
 // Launches:
 //   gdn_pf_snapshot_kernel  copy of the conv rings / positions of the plan's sequences (the
@@ -179,8 +182,9 @@ __global__ void __launch_bounds__(256) gdn_pf_prep_kernel(const GdnPrefillParams
 
 // ---------------------------------------------------------------- pack (core op: token-major inputs)
 
-// 8 consecutive values (i a multiple of 8) as hi / lo planes, 16-byte stores
-__device__ __forceinline__ void put_hl8(__half* hi, long long plane, long long i, const float (&x)[8]) {
+// 8 consecutive values (i a multiple of 8) as hi / lo planes, 16-byte stores (hi only: values exact in fp16)
+__device__ __forceinline__ void put_hl8(__half* hi, long long plane, long long i, const float (&x)[8],
+                                        bool hi_only = false) {
     float h[8], l[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) {
@@ -189,7 +193,7 @@ __device__ __forceinline__ void put_hl8(__half* hi, long long plane, long long i
         l[e] = x[e] - h[e];
     }
     *reinterpret_cast<uint4*>(hi + i) = pack8(h, false);
-    *reinterpret_cast<uint4*>(hi + plane + i) = pack8(l, false);
+    if (!hi_only) *reinterpret_cast<uint4*>(hi + plane + i) = pack8(l, false);
 }
 
 __global__ void __launch_bounds__(256) gdn_pf_pack_kernel(const GdnPrefillParams p) {
@@ -208,12 +212,12 @@ __global__ void __launch_bounds__(256) gdn_pf_pack_kernel(const GdnPrefillParams
                 if (live)
                     load8(reinterpret_cast<const char*>(isk ? p.k_in : p.q_in) + tok * Hk * kDk * eb, p.in_dtype, e, x);
                 const long long o = (((long long)b * Hk + e / kDk) * p.T_pad + t) * kDk + e % kDk;
-                put_hl8(isk ? p.kh : p.qh, p.q_plane, o, x);
+                put_hl8(isk ? p.kh : p.qh, p.q_plane, o, x, p.qkv_exact);
             } else {
                 const int e = (gi - 2 * nq) * 8;
                 if (live) load8(reinterpret_cast<const char*>(p.v_in) + tok * Hv * kDv * eb, p.in_dtype, e, x);
                 const long long o = (((long long)b * Hv + e / kDv) * p.T_pad + t) * kDv + e % kDv;
-                put_hl8(p.vh, p.v_plane, o, x);
+                put_hl8(p.vh, p.v_plane, o, x, p.qkv_exact);
             }
         }
     } else {
@@ -305,12 +309,16 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
     if (tid == 0) {  // K and Q, both planes, into the operand buffers
         tc::prefetch_tmap(&tmK);
         tc::prefetch_tmap(&tmQ);
-        tc::mbar_arrive_expect_tx(&bar[0], 2 * kOpPlane);
+        const bool lo = !p.qkv_exact;  // exact 16-bit inputs: the lo plane is zero, not loaded
+        tc::mbar_arrive_expect_tx(&bar[0], (lo ? 2 : 1) * kOpPlane);
+#pragma unroll
         for (int pl = 0; pl < 2; pl++)
-            for (int kb = 0; kb < 2; kb++) {
-                tc::tma_load_3d(&sm.op[pl][kb * 16384], &tmK, &bar[0], kb * 64, (int)krow, pl);
-                tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmQ, &bar[0], kb * 64, (int)krow, pl);
-            }
+            if (pl == 0 || lo)
+#pragma unroll
+                for (int kb = 0; kb < 2; kb++) {
+                    tc::tma_load_3d(&sm.op[pl][kb * 16384], &tmK, &bar[0], kb * 64, (int)krow, pl);
+                    tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmQ, &bar[0], kb * 64, (int)krow, pl);
+                }
     }
     if (warp == 1) {  // inclusive prefix sum of log g over the chunk (two tokens per lane)
         const float g0 = p.lg[vrow + 2 * lane], g1 = p.lg[vrow + 2 * lane + 1];
@@ -333,15 +341,18 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
         if (tc::mbar_wait(&bar[0], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {
             tc::tc_fence_after();
             constexpr uint32_t id1 = tc::idesc_f16_f32(128, kC);
+            // exact inputs: K and Q are exact in fp16, so hi * hi is the whole product
+            const bool lo_terms = !p.qkv_exact;
 #pragma unroll
             for (int term = 0; term < 3; term++) {
                 const uint32_t pa = aop + (term == 1 ? kOpPlane : 0), pb = aop + (term == 2 ? kOpPlane : 0);
+                if (term == 0 || lo_terms)
 #pragma unroll
-                for (int kb = 0; kb < 2; kb++)
+                    for (int kb = 0; kb < 2; kb++)
 #pragma unroll
-                    for (int ks = 0; ks < 4; ks++)
-                        tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(pa + kb * 16384 + ks * 32),
-                                       tc::desc_kmajor_sw128(pb + kb * 16384 + ks * 32), id1, (term | kb | ks) != 0);
+                        for (int ks = 0; ks < 4; ks++)
+                            tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(pa + kb * 16384 + ks * 32),
+                                           tc::desc_kmajor_sw128(pb + kb * 16384 + ks * 32), id1, (term | kb | ks) != 0);
             }
             tc::mma_commit(&bar[1]);
         }
@@ -352,10 +363,14 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
     __syncthreads();  // lc / lt / bt visible; every thread past GEMM 1 (Q no longer read)
     if (tid == 0 && ok1) {  // V replaces Q in the operand buffers
         tc::prefetch_tmap(&tmV);
-        tc::mbar_arrive_expect_tx(&bar[2], kOpPlane);
+        const bool lo = !p.qkv_exact;
+        tc::mbar_arrive_expect_tx(&bar[2], (lo ? 2 : 1) * (kOpPlane / 2));
+#pragma unroll
         for (int pl = 0; pl < 2; pl++)
-            for (int kb = 0; kb < 2; kb++)
-                tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmV, &bar[2], kb * 64, (int)vrow, pl);
+            if (pl == 0 || lo)
+#pragma unroll
+                for (int kb = 0; kb < 2; kb++)
+                    tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmV, &bar[2], kb * 64, (int)vrow, pl);
     }
     {
         const int q = warp & 3, hc = warp >> 2;
@@ -485,13 +500,15 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
         if (tc::mbar_wait(&bar[2], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {
             tc::tc_fence_after();
             constexpr uint32_t id2 = tc::idesc_f16_f32_bmn(128, 256);
+            const bool b_lo = !p.qkv_exact;  // exact inputs: K and V have no lo plane (hi * lo vanishes)
 #pragma unroll
             for (int term = 0; term < 3; term++) {
                 const uint32_t pa = at_ + (term == 1 ? kTPlane : 0), pb = aop + (term == 2 ? kOpPlane : 0);
+                if (term < 2 || b_lo)
 #pragma unroll
-                for (int ks = 0; ks < 4; ks++)
-                    tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(pa + ks * 32), tc::desc_sw128(pb + ks * 16 * 128, 8192, 1024),
-                                   id2, (term | ks) != 0);
+                    for (int ks = 0; ks < 4; ks++)
+                        tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(pa + ks * 32),
+                                       tc::desc_sw128(pb + ks * 16 * 128, 8192, 1024), id2, (term | ks) != 0);
             }
             tc::mma_commit(&bar[3]);
         }
@@ -612,7 +629,7 @@ __device__ __forceinline__ void afrag(const float (&acc)[NT][4], int ks, uint32_
 // term across all 2 NP accumulators so dependent MMAs are 2 NP instructions apart
 template <int NP>
 __device__ __forceinline__ void mma3_tm(float (*acc)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
-                                        const uint32_t (&bh)[NP][4], const uint32_t (&bl)[NP][4]) {
+                                        const uint32_t (&bh)[NP][4], const uint32_t (&bl)[NP][4], bool b_lo = true) {
 #pragma unroll
     for (int np = 0; np < NP; np++) {
         mma_16816(acc[2 * np], ah[0], ah[1], ah[2], ah[3], bh[np][0], bh[np][1]);
@@ -623,6 +640,7 @@ __device__ __forceinline__ void mma3_tm(float (*acc)[4], const uint32_t (&ah)[4]
         mma_16816(acc[2 * np], al[0], al[1], al[2], al[3], bh[np][0], bh[np][1]);
         mma_16816(acc[2 * np + 1], al[0], al[1], al[2], al[3], bh[np][2], bh[np][3]);
     }
+    if (!b_lo) return;  // B exact in fp16 (its lo plane is zero)
 #pragma unroll
     for (int np = 0; np < NP; np++) {
         mma_16816(acc[2 * np], ah[0], ah[1], ah[2], ah[3], bl[np][0], bl[np][1]);
@@ -636,12 +654,13 @@ struct ChainMaps {
     CUtensorMap w, q, k, m, u;
 };
 // W and Q, hi and lo planes (read by W S and Q S)
-__device__ __forceinline__ void chain_load_wq(ChainSmem& sm, const ChainMaps& mp, long long krow, long long vrow) {
-    tc::mbar_arrive_expect_tx(&sm.bar[0], 2 * 2 * 2 * 8192);
+__device__ __forceinline__ void chain_load_wq(ChainSmem& sm, const ChainMaps& mp, long long krow, long long vrow,
+                                              bool exact) {
+    tc::mbar_arrive_expect_tx(&sm.bar[0], (exact ? 3 : 4) * 2 * 8192);  // exact: no Q lo plane
     for (int pl = 0; pl < 2; pl++)
         for (int bx = 0; bx < 2; bx++) {
             tc::tma_load_3d(sm.w[pl][bx], &mp.w, &sm.bar[0], 64 * bx, (int)vrow, pl);
-            tc::tma_load_3d(sm.q[pl][bx], &mp.q, &sm.bar[0], 64 * bx, (int)krow, pl);
+            if (pl == 0 || !exact) tc::tma_load_3d(sm.q[pl][bx], &mp.q, &sm.bar[0], 64 * bx, (int)krow, pl);
         }
 }
 // this block's U columns and lc (read by D = U - W S and the decay factors)
@@ -652,10 +671,12 @@ __device__ __forceinline__ void chain_load_u(ChainSmem& sm, const ChainMaps& mp,
     tc::bulk_load(sm.lc[par], p.lcb + vrow, kC * 4, &sm.bar[1]);
 }
 // K and M, hi and lo planes (read by the state update and M D)
-__device__ __forceinline__ void chain_load_mk(ChainSmem& sm, const ChainMaps& mp, long long krow, long long vrow) {
-    tc::mbar_arrive_expect_tx(&sm.bar[2], 2 * 2 * 8192 + 2 * 8192);
+__device__ __forceinline__ void chain_load_mk(ChainSmem& sm, const ChainMaps& mp, long long krow, long long vrow,
+                                              bool exact) {
+    tc::mbar_arrive_expect_tx(&sm.bar[2], (exact ? 1 : 2) * 2 * 8192 + 2 * 8192);  // exact: no K lo plane
     for (int pl = 0; pl < 2; pl++) {
-        for (int bx = 0; bx < 2; bx++) tc::tma_load_3d(sm.k[pl][bx], &mp.k, &sm.bar[2], 64 * bx, (int)krow, pl);
+        if (pl == 0 || !exact)
+            for (int bx = 0; bx < 2; bx++) tc::tma_load_3d(sm.k[pl][bx], &mp.k, &sm.bar[2], 64 * bx, (int)krow, pl);
         tc::tma_load_3d(sm.m[pl], &mp.m, &sm.bar[2], 0, (int)vrow, pl);
     }
 }
@@ -695,10 +716,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const __
     __syncthreads();
     volatile int* abort = &sm.abort;
     const bool loader = tid == 4 * 32;  // lane 0 of output warp 4 issues every copy
+    const bool exact = p.qkv_exact != 0;  // Q and K exact in fp16: their lo planes are neither loaded nor used
     if (loader) {
-        chain_load_wq(sm, mp, krow0, vrow0);
+        chain_load_wq(sm, mp, krow0, vrow0, exact);
         chain_load_u(sm, mp, p, vrow0, j0, 0);
-        chain_load_mk(sm, mp, krow0, vrow0);
+        chain_load_mk(sm, mp, krow0, vrow0, exact);
     }
     const uint32_t a_w = smem_u32(sm.w), a_q = smem_u32(sm.q), a_k = smem_u32(sm.k), a_m = smem_u32(sm.m);
     // named barriers: 1 + jg state pair, 3 + jg output pair (64 threads); 5 + jg S^T fragments and
@@ -744,17 +766,18 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const __
 #pragma unroll
                 for (int n2 = 0; n2 < 2; n2++) {
                     uint32_t bh[2][4], bl[2][4];
+                    const bool b_lo = state || !exact;  // W always has a lo plane, Q only when not exact
 #pragma unroll
                     for (int q = 0; q < 2; q++) {
                         ldb2_sw(bh[q], bhi, 32 * n2 + 16 * q, k0, lane);
-                        ldb2_sw(bl[q], blo, 32 * n2 + 16 * q, k0, lane);
+                        if (b_lo) ldb2_sw(bl[q], blo, 32 * n2 + 16 * q, k0, lane);
                     }
-                    mma3_tm<2>(&acc[4 * n2], fa[ks], fl[ks], bh, bl);
+                    mma3_tm<2>(&acc[4 * n2], fa[ks], fl[ks], bh, bl, b_lo);
                 }
             }
         }
         __syncthreads();  // W, Q free
-        if (more && loader) chain_load_wq(sm, mp, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC);
+        if (more && loader) chain_load_wq(sm, mp, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC, exact);
         // ---- the two d halves of a column group meet ----
         float (*xb)[32][32] = state ? sm.xd : sm.xy;
 #pragma unroll
@@ -858,13 +881,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const __
 #pragma unroll
                 for (int np = 0; np < 4; np++) {
                     ldb2_t_sw(bh[np], a_k, dbase + 16 * np, 16 * ks, lane);
-                    ldb2_t_sw(bl[np], a_k + 16384, dbase + 16 * np, 16 * ks, lane);
+                    if (!exact) ldb2_t_sw(bl[np], a_k + 16384, dbase + 16 * np, 16 * ks, lane);
                 }
-                mma3_tm<4>(s, ah, al, bh, bl);
+                mma3_tm<4>(s, ah, al, bh, bl, !exact);
             }
         }
         __syncthreads();  // M, K free
-        if (more && loader) chain_load_mk(sm, mp, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC);
+        if (more && loader) chain_load_mk(sm, mp, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC, exact);
     }
     if (state) {
 #pragma unroll
@@ -1005,6 +1028,7 @@ int launch_gdn_prefill(GdnPrefillParams p, void* workspace, cudaStream_t stream)
     if (p.dk != kDk || p.dv != kDv || p.Hv % p.Hk) return ANELM_ERR_UNSUPPORTED;
     p.T_pad = (p.n + kC - 1) / kC * kC;
     carve(p, workspace, true);
+    p.qkv_exact = 0;  // q, k, v come out of the conv / SiLU / L2 norm in fp32: both planes carry them
     p.y_dtype = ANELM_F32;
     p.y_stride = (long long)p.Hv * kDv;
     gdn_pf_snapshot_kernel<<<dim3((p.C * 3 + 255) / 256, p.B), 256, 0, stream>>>(p);
@@ -1022,6 +1046,8 @@ int launch_gated_delta_chunked(GdnPrefillParams p, void* workspace, cudaStream_t
     p.T_pad = (p.n + kC - 1) / kC * kC;
     carve(p, workspace, false);
     p.in_vec = (uintptr_t)p.q_in % 16 == 0 && (uintptr_t)p.k_in % 16 == 0 && (uintptr_t)p.v_in % 16 == 0;
+    // 16-bit inputs are exact in fp16 (bf16 normal values have 8 significant bits): lo planes are zero
+    p.qkv_exact = p.in_dtype == ANELM_F16 || p.in_dtype == ANELM_BF16;
     gdn_pf_pack_kernel<<<dim3(p.T_pad, p.B), 256, 0, stream>>>(p);
     return launch_chunks_and_chain(p, stream);
 }

@@ -141,6 +141,8 @@ struct GdnPrefillParams {
     const void* v_in;
     int in_dtype;
     int in_vec;            // set by the launcher: q_in, k_in, v_in 16-byte aligned
+    int qkv_exact;        // q, k, v arrive as 16-bit values: exact in fp16, their lo planes are zero and
+                          // are neither written nor read; products against them take two of the three terms
     const float* lg_in;
     const float* beta_in;
     // state [seq][Hv][dk][dv], row b uses seq_ids[b] (or b)

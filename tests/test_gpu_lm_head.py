@@ -45,3 +45,11 @@ def test_lm_head_top32_qwen_vocab(n):
 @pytest.mark.parametrize("n", [1, 3])
 def test_lm_head_ragged_vocab(n, k):
     _check(n, 1000, 136, k, seed=k + 10 * n)
+
+
+@pytest.mark.parametrize("n", [2, 8, 16])
+def test_lm_head_wide_hidden_few_rows(n):
+    """2-16 rows take the swapped-role kernel only while the rows of h fit its shared memory (hidden up
+    to about 3,100); at hidden 4,096 they fall back to the tensor-core tile kernel with one copy of the
+    row block -- that path, against the same reference."""
+    _check(n, 32768, 4096, 32, seed=100 + n)
