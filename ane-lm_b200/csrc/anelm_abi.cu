@@ -346,6 +346,7 @@ GdnDecodeParams gdn_params(anelm_ctx* ctx, int layer, const anelm_plan* plan, co
     p.dt_bias = ctx->dt_bias[gi];
     p.norm_w = ctx->norm_w[gi];
     p.ssm = ctx->ssm[gi];
+    p.ssm_rows = (long long)c.max_seqs * c.lin_num_val_heads * c.lin_key_dim;
     p.conv = ctx->conv[gi];
     p.conv_pos = ctx->conv_pos + (long long)gi * c.max_seqs * c.lin_num_key_heads;
     p.seq_ids = plan->seq_d;

@@ -37,9 +37,11 @@
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc100.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -96,10 +98,15 @@ __device__ __forceinline__ bool mbar_wait0(uint64_t* bar, int* err) {
     return false;
 }
 
-template <int RATIO, int NSPLIT, int THREADS>
+// STAGED: the CTA's 128 x W state block comes in by one TMA tile load into shared memory, issued at
+// entry (before the conv inputs), and goes back by one TMA tile store; the delta rule runs in two
+// passes over shared memory, so no registers hold the block and more CTAs fit an SM.  Otherwise the
+// block streams into registers (float4 per thread and row) and back.
+template <int RATIO, int NSPLIT, int THREADS, bool STAGED>
 // 128-thread CTAs are held to 96 registers: at 102 the per-warp allocation rounds to 3,328 and
-// only four CTAs fit an SM, at 96 five do (a 20-byte spill).
-__global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_kernel(const GdnDecodeParams p) {
+// only four CTAs fit an SM, at 96 five do (a 20-byte spill).  Staged CTAs: six per SM (shared memory).
+__global__ void __launch_bounds__(THREADS, STAGED ? 6 : (THREADS == 128 ? 5 : 1))
+    gdn_decode_kernel(const GdnDecodeParams p, const __grid_constant__ CUtensorMap tmS) {
     constexpr int CS = RATIO * NSPLIT;     // CTAs per cluster
     constexpr int W = kDv / NSPLIT;        // value columns per CTA
     constexpr int QPR = W / 4;             // float4 quads per row segment
@@ -119,7 +126,8 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_ke
     __shared__ __align__(16) float red[2][NW][W];
     __shared__ __align__(16) float ss_s[NSPLIT];
     __shared__ float scal[4];
-    __shared__ __align__(8) uint64_t bar_qk, bar_ss;
+    __shared__ __align__(8) uint64_t bar_qk, bar_ss, bar_s;
+    __shared__ __align__(128) float s_blk[STAGED ? kDk * W : 4];  // staged state block [128 rows][W]
 
     cg::cluster_group cluster = cg::this_cluster();
     if (threadIdx.x == 0) {
@@ -129,6 +137,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_ke
         // peer can deliver before the expectation exists
         mbar_expect(&bar_qk, 2 * kDk * 4);   // the whole q | k vector arrives from the cluster
         mbar_expect(&bar_ss, NSPLIT * 4);    // one partial sum of y^2 per column block of this head
+        if (STAGED) mbar_init1(&bar_s);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     cluster_arrive_relaxed();  // matched below, before the first store into a peer
@@ -144,6 +153,11 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_ke
     const int C = p.C;
     const int key_total = p.Hk * kDk;
     const int j0 = cb * W;
+    const int s_row0 = (int)(((long long)seq * p.Hv + h) * kDk);  // first row of this head's state (TMA view)
+    if (STAGED && threadIdx.x == 0) {  // the state block, first of all loads
+        mbar_expect(&bar_s, kDk * W * 4);
+        tc::tma_load_2d(s_blk, &tmS, &bar_s, j0, s_row0);
+    }
 
     // ---- 1. loads: the small inputs of the conv / gates first, then the 32 KB state block ----
     // Requests are served roughly in issue order, so small loads issued after the state block
@@ -192,9 +206,11 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_ke
         ga = load_as_float(proj_row, p.proj_dtype, C + (long long)p.Hv * kDv + h);
         gb = load_as_float(proj_row, p.proj_dtype, C + (long long)p.Hv * kDv + p.Hv + h);
     }
-    float4 S[NR];
+    float4 S[STAGED ? 1 : NR];
+    if constexpr (!STAGED) {
 #pragma unroll
-    for (int i = 0; i < NR; i++) S[i] = __ldcs(reinterpret_cast<const float4*>(Sbase + (long long)(rg + RPP * i) * kDv));
+        for (int i = 0; i < NR; i++) S[i] = __ldcs(reinterpret_cast<const float4*>(Sbase + (long long)(rg + RPP * i) * kDv));
+    }
     // L2 prefetch of the state head that the CTA about one resident wave later (kPrefetchItems
     // (row, key head) items on) will stream: its 64 KB are in L2 when it starts, which adds bytes
     // in flight beyond what the register-resident blocks hold
@@ -305,11 +321,57 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_ke
         return t;
     };
 
-    // ---- 4. delta rule on the register block ----
+    // ---- 4. delta rule on the register block (or, staged, on the shared-memory block) ----
     const float* q_s = qk_s;
     const float* k_s = qk_s + kDk;
     float4 sk = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p.delta_mode == ANELM_DELTA_CPUOPS) {
+    float4 yv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (STAGED) {
+        if (!mbar_wait0(&bar_s, p.err)) {  // the block never arrived: wait once more (bounded), then leave
+            mbar_wait0(&bar_s, nullptr);
+            return;
+        }
+        float* blk = s_blk + 4 * cq;
+        auto at = [&](int i) -> float4* { return reinterpret_cast<float4*>(blk + (rg + RPP * i) * W); };
+        const bool hf = p.delta_mode != ANELM_DELTA_CPUOPS;
+        // pass 1: Sk = S^T k (cpu_ops.cpp:134-135), or (g S)^T k when the decay comes first
+#pragma unroll
+        for (int i = 0; i < NR; i++) {
+            float4 v = *at(i);
+            if (hf) {
+                v.x = __fmul_rn(v.x, decay); v.y = __fmul_rn(v.y, decay);
+                v.z = __fmul_rn(v.z, decay); v.w = __fmul_rn(v.w, decay);
+            }
+            const float kr = k_s[rg + RPP * i];
+            sk.x += v.x * kr; sk.y += v.y * kr; sk.z += v.z * kr; sk.w += v.w * kr;
+        }
+        sk = colsum(sk, 0);
+        float4 d = make_float4(v_s[4 * cq] - sk.x, v_s[4 * cq + 1] - sk.y, v_s[4 * cq + 2] - sk.z,
+                               v_s[4 * cq + 3] - sk.w);
+        if (hf) { d.x *= beta; d.y *= beta; d.z *= beta; d.w *= beta; }
+        // pass 2: the update (cpu_ops.cpp:140-142 / export_hybrid_chunks.py:142-147) and y = S^T q (144-145)
+#pragma unroll
+        for (int i = 0; i < NR; i++) {
+            float4 v = *at(i);
+            const float kr = k_s[rg + RPP * i];
+            if (hf) {
+                v.x = __fadd_rn(__fmul_rn(v.x, decay), __fmul_rn(kr, d.x));
+                v.y = __fadd_rn(__fmul_rn(v.y, decay), __fmul_rn(kr, d.y));
+                v.z = __fadd_rn(__fmul_rn(v.z, decay), __fmul_rn(kr, d.z));
+                v.w = __fadd_rn(__fmul_rn(v.w, decay), __fmul_rn(kr, d.w));
+            } else {
+                const float ax = beta * kr;
+                v.x = __fadd_rn(__fmul_rn(v.x, decay), __fmul_rn(ax, d.x));
+                v.y = __fadd_rn(__fmul_rn(v.y, decay), __fmul_rn(ax, d.y));
+                v.z = __fadd_rn(__fmul_rn(v.z, decay), __fmul_rn(ax, d.z));
+                v.w = __fadd_rn(__fmul_rn(v.w, decay), __fmul_rn(ax, d.w));
+            }
+            *at(i) = v;
+            const float qr = q_s[rg + RPP * i];
+            yv.x += v.x * qr; yv.y += v.y * qr; yv.z += v.z * qr; yv.w += v.w * qr;
+        }
+        tc::fence_proxy_async_smem();  // this thread's block writes, for the TMA store
+    } else if (p.delta_mode == ANELM_DELTA_CPUOPS) {
         // cpu_ops.cpp:134-142: Sk = S^T k (undecayed); delta = v - Sk; S = decay*S + (beta*k) delta^T
 #pragma unroll
         for (int i = 0; i < NR; i++) {
@@ -348,16 +410,20 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_ke
             S[i].w = __fadd_rn(S[i].w, __fmul_rn(kr, d.w));
         }
     }
-    // y = S^T q (cpu_ops.cpp:144-145)
-    float4 yv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (!STAGED) {  // y = S^T q (cpu_ops.cpp:144-145)
 #pragma unroll
-    for (int i = 0; i < NR; i++) {
-        const float qr = q_s[rg + RPP * i];
-        yv.x += S[i].x * qr; yv.y += S[i].y * qr; yv.z += S[i].z * qr; yv.w += S[i].w * qr;
+        for (int i = 0; i < NR; i++) {
+            const float qr = q_s[rg + RPP * i];
+            yv.x += S[i].x * qr; yv.y += S[i].y * qr; yv.z += S[i].z * qr; yv.w += S[i].w * qr;
+        }
     }
     yv = colsum(yv, 1);
     if (rg == 0) *reinterpret_cast<float4*>(&y_s[4 * cq]) = yv;
     __syncthreads();
+    if (STAGED && tid == 0) {  // the updated block back to HBM (every thread's writes are fenced and past the barrier)
+        tc::tma_store_2d(&tmS, s_blk, j0, s_row0);
+        tc::bulk_commit_group();
+    }
 
     // ---- 5. gated RMSNorm over the head's 128 columns (rmsnorm_gated, cpu_ops.cpp:32-38) ----
     if (warp == 0) {
@@ -366,9 +432,11 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_ke
         ss = warp_sum(ss);
         if (lane < NSPLIT) st_async_f32(map_rank(&ss_s[cb], hl * NSPLIT + lane), ss, map_rank(&bar_ss, hl * NSPLIT + lane));
     }
-    // global stores: the state block and the new inputs into ring slot n (cpu_ops.cpp:109)
+    // global stores: the state block (unless staged) and the new inputs into ring slot n (cpu_ops.cpp:109)
+    if constexpr (!STAGED) {
 #pragma unroll
-    for (int i = 0; i < NR; i++) __stcs(reinterpret_cast<float4*>(Sbase + (long long)(rg + RPP * i) * kDv), S[i]);
+        for (int i = 0; i < NR; i++) __stcs(reinterpret_cast<float4*>(Sbase + (long long)(rg + RPP * i) * kDv), S[i]);
+    }
 #pragma unroll
     for (int u = 0; u < NV; u++) {
         const int i = tid + u * THREADS;
@@ -396,12 +464,29 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gdn_decode_ke
         o = __fmul_rn(o, z);
         store_from_float(p.out, p.out_dtype, orow + i, o);
     }
+    if (STAGED && tid == 0) tc::bulk_wait_group_read0();  // the block's store has read shared memory
 }
 
 
-template <int RATIO, int NSPLIT, int THREADS>
+template <int RATIO, int NSPLIT, int THREADS, bool STAGED>
 int launch_cfg(const GdnDecodeParams& p, int n_rows, cudaStream_t stream) {
     constexpr int CS = RATIO * NSPLIT;
+    CUtensorMap tmS;
+    memset(&tmS, 0, sizeof(tmS));
+    if (STAGED) {  // ssm as a [rows][128] fp32 matrix, box {W, 128} (one state block), no swizzle
+        auto enc = tc::tmap_encode_fn();
+        const cuuint64_t dims[2] = {(cuuint64_t)kDv, (cuuint64_t)p.ssm_rows};
+        const cuuint64_t strides[1] = {(cuuint64_t)kDv * 4};
+        const cuuint32_t box[2] = {(cuuint32_t)(kDv / NSPLIT), (cuuint32_t)kDk};
+        const cuuint32_t estr[2] = {1, 1};
+        if (!enc || (uintptr_t)p.ssm % 16 ||
+            enc(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.ssm, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+                CUDA_SUCCESS)
+            return ANELM_ERR_CUDA;
+        cudaFuncSetAttribute(gdn_decode_kernel<RATIO, NSPLIT, THREADS, STAGED>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((long long)n_rows * p.Hk * CS));
     cfg.blockDim = dim3(THREADS);
@@ -414,7 +499,7 @@ int launch_cfg(const GdnDecodeParams& p, int n_rows, cudaStream_t stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gdn_decode_kernel<RATIO, NSPLIT, THREADS>, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gdn_decode_kernel<RATIO, NSPLIT, THREADS, STAGED>, p, tmS);
     return e == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 
@@ -436,8 +521,14 @@ int launch_gdn_decode(const GdnDecodeParams& p, int n_rows, int key_dim, int val
         threads = 128;
         if (ratio == 4) nsplit = 2;
     }
+    // staged state blocks (TMA in / out through shared memory) for the wide-batch shape; override with
+    // ANELM_GDN_STAGED=0 / 1
+    bool staged = !small && nsplit == 2 && threads == 128;
+    if (const char* e = getenv("ANELM_GDN_STAGED")) staged = staged && atoi(e) != 0;
+    if (staged && ratio == 2) return launch_cfg<2, 2, 128, true>(p, n_rows, stream);
+    if (staged && ratio == 1) return launch_cfg<1, 2, 128, true>(p, n_rows, stream);
 #define GDN_CASE(R, NS, T) \
-    if (ratio == R && nsplit == NS && threads == T) return launch_cfg<R, NS, T>(p, n_rows, stream);
+    if (ratio == R && nsplit == NS && threads == T) return launch_cfg<R, NS, T, false>(p, n_rows, stream);
     GDN_CASE(1, 8, 128) GDN_CASE(1, 4, 128) GDN_CASE(1, 4, 256) GDN_CASE(1, 2, 256) GDN_CASE(1, 2, 128)
     GDN_CASE(2, 4, 128) GDN_CASE(2, 4, 256) GDN_CASE(2, 2, 128) GDN_CASE(2, 2, 256)
     GDN_CASE(4, 2, 128) GDN_CASE(4, 2, 256)

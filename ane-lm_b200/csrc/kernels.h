@@ -67,6 +67,7 @@ struct GdnDecodeParams {
     const float* dt_bias;  // [Hv]
     const float* norm_w;   // [dv]
     float* ssm;            // [seqs][Hv][128][128]
+    long long ssm_rows;    // seqs * Hv * 128: rows of ssm seen as a [rows][128] fp32 matrix (the TMA view)
     float* conv;           // [seqs][C][3] ring of the last 3 inputs (reference layout)
     int* conv_pos;         // [seqs][Hk] ring position, one copy per key-head cluster
     const int* seq_ids;    // [n] or nullptr

@@ -63,7 +63,7 @@ def main(out_path):
     dist.all_reduce(oks)
     if rank == 0:
         np.savez(out_path, sharded=out.cpu().numpy(), full=full.cpu().numpy(), world=world,
-                 fused_ok_ranks=int(oks.item()), fused=fused[-1], full16=full16.float().cpu().numpy()[0])
+                 fused_ok_ranks=int(oks.item()), fused=fused[-1][0], full16=full16.float().cpu().numpy()[0])
     dist.barrier()
     dist.destroy_process_group()
 
