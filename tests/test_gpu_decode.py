@@ -250,19 +250,21 @@ def test_deltanet_batched():
     np.testing.assert_array_equal(ssm, states[2].ssm)
 
 
+@pytest.mark.parametrize("Hv,n_seq", [(32, 40), (16, 24)])
 @pytest.mark.parametrize("delta_mode", [ab.DELTA_CPUOPS, ab.DELTA_HF])
-def test_deltanet_batched_gqa(delta_mode):
-    """A larger batch (40 rows x 16 key heads = 640 clusters) in the 4B GQA shape, 3 steps, rows in
-    shuffled order, both delta-rule orders: every row's outputs / state / conv ring / position vs
-    the oracle."""
-    rng = np.random.default_rng(40 + delta_mode)
-    shape = gdn_shape(16, 32)
-    n_seq, steps = 40, 3
+def test_deltanet_batched_gqa(delta_mode, Hv, n_seq):
+    """Larger batches take the staged kernel (state blocks in and out by TMA tiles through shared
+    memory): 40 rows x 16 key heads in the 4B GQA shape (two value heads per key head) and 24 rows of
+    the 0.8B shape (one), 3 steps, rows in shuffled order, both delta-rule orders: every row's
+    outputs / state / conv ring / position vs the oracle."""
+    rng = np.random.default_rng(40 + delta_mode + Hv)
+    shape = gdn_shape(16, Hv)
+    steps = 3
     order = list(rng.permutation(n_seq))
     proj, conv_w, A, dt_bias, norm_w = gdn_inputs(rng, shape, steps * n_seq)
     proj = proj.reshape(steps, n_seq, -1)
     C = conv_w.shape[0]
-    states = [po.DeltaState((0.1 * rng.standard_normal((32, 128, 128))).astype(np.float32),
+    states = [po.DeltaState((0.1 * rng.standard_normal((Hv, 128, 128))).astype(np.float32),
                             rng.standard_normal((C, 3)).astype(np.float32), s % 3) for s in range(n_seq)]
     var = po.make_variant(delta_hf=int(delta_mode == ab.DELTA_HF))
     with gdn_ctx(shape, max_seqs=n_seq, delta_mode=delta_mode) as ctx:
