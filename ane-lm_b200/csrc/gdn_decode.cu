@@ -521,10 +521,13 @@ int launch_gdn_decode(const GdnDecodeParams& p, int n_rows, int key_dim, int val
         threads = 128;
         if (ratio == 4) nsplit = 2;
     }
-    // staged state blocks (TMA in / out through shared memory) for the wide-batch shape; override with
-    // ANELM_GDN_STAGED=0 / 1
-    bool staged = !small && nsplit == 2 && threads == 128;
-    if (const char* e = getenv("ANELM_GDN_STAGED")) staged = staged && atoi(e) != 0;
+    // staged state blocks (TMA in / out through shared memory) for wide batches: measured on B200 for the
+    // 4B shape (32 value heads), one layer: 256 rows 0.190 vs 0.217 ms, 128 rows 0.103 vs 0.113; at 64
+    // rows (4,096 CTAs) and fewer the register form is slightly ahead (32 rows 0.0276 vs 0.0294 ms).
+    // Override with ANELM_GDN_STAGED=0 / 1
+    bool staged = !small && nsplit == 2 && threads == 128 && (long long)n_rows * p.Hv * nsplit >= 6144;
+    if (const char* e = getenv("ANELM_GDN_STAGED"))
+        staged = atoi(e) != 0 && !small && nsplit == 2 && threads == 128;
     if (staged && ratio == 2) return launch_cfg<2, 2, 128, true>(p, n_rows, stream);
     if (staged && ratio == 1) return launch_cfg<1, 2, 128, true>(p, n_rows, stream);
 #define GDN_CASE(R, NS, T) \

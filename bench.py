@@ -64,6 +64,15 @@ GDN_OUT = HV * DV
 GLOBAL_SEQS = 256
 METRIC = "decode attn-core tok/s (batched serving decode, 32-layer 3:1 DeltaNet:attention stack)"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+# A fixed-length spin kernel (torch.cuda._sleep, ~0.1 ms at 2 GHz) queued right before a timed call's
+# start event keeps the GPU busy while the host enqueues the call, so the events time the device work
+# of the call, not the host's launch latency.
+ENQUEUE_COVER_CYCLES = 200_000
+
+
+def flush_and_cover(torch, flush):
+    flush.zero_()
+    torch.cuda._sleep(ENQUEUE_COVER_CYCLES)
 
 
 def env_rank():
@@ -558,7 +567,7 @@ def wl_fa_prefill(args, torch, device, B, n=4096, steps=10):
     clocks = ClockSampler(device.index or 0).start()
     for _ in range(steps):
         ctx.reset(-1)      # synchronous; outside the timed region
-        flush.zero_()      # the B = 1 inputs (84 MB) would otherwise sit in L2
+        flush_and_cover(torch, flush)  # the B = 1 inputs (84 MB) would otherwise sit in L2
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
         ctx.full_attn_prefill(plan, 0, proj, 0, out)
@@ -578,7 +587,8 @@ def wl_fa_prefill(args, torch, device, B, n=4096, steps=10):
             "roofline": tensor_roof(tf, tpeak, tkind, "fa_prefill_prep_bulk_kernel + fa_prefill_kernel (whole call)",
                                     flops),
             "timed": "whole call: prep (QK-norm, RoPE, fp16 Q/K/V, sigmoid gate, ring append) + attention",
-            "l2": "256 MB buffer written before each timed call", "clocks": ck,
+            "l2": "256 MB buffer written before each timed call (then a fixed spin kernel covers the host's enqueue)",
+            "clocks": ck,
             "cpu_baseline": None if args.no_cpu_baseline else cpu_reference_prefill(B, n, args.cpu_seconds_wl, flops),
             "gpu_launches": 3 * steps}
 
@@ -614,7 +624,7 @@ def wl_gdn_prefill(args, torch, device, B=1, T=8192, steps=10):
     clocks = ClockSampler(device.index or 0).start()
     times = []
     for _ in range(steps):
-        flush.zero_()  # inputs (24 MB) would otherwise stay in L2 between iterations
+        flush_and_cover(torch, flush)  # inputs (24 MB) would otherwise stay in L2 between iterations
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
         call()
@@ -630,7 +640,8 @@ def wl_gdn_prefill(args, torch, device, B=1, T=8192, steps=10):
     roof.update({"hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4), "algorithmic_bytes": nbytes})
     return {"metric": f"chunked Gated DeltaNet prefill TFLOP/s (cfg4, Hv 32 / Hk 16, d 128, S={T}, B={B})",
             "value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4), "steps": steps, "roofline": roof,
-            "l2": "256 MB buffer written before each timed call", "clocks": ck,
+            "l2": "256 MB buffer written before each timed call (then a fixed spin kernel covers the host's enqueue)",
+            "clocks": ck,
             "cpu_baseline": (None if args.no_cpu_baseline else
                              cpu_reference_gdn_chunk(T, B, Hk, Hv, flops, args.cpu_seconds_wl)),
             "gpu_launches": 3 * steps}
@@ -736,9 +747,9 @@ def wl_prefill_sharded(args, torch, device, world, rank, which):
     clocks = ClockSampler(device.index or 0).start()
     for _ in range(steps):
         before()
-        flush.zero_()
         torch.cuda.synchronize(device)
         dist.barrier()
+        flush_and_cover(torch, flush)
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
         compute()
@@ -758,7 +769,8 @@ def wl_prefill_sharded(args, torch, device, world, rank, which):
     return {"metric": metric, "value": round(tf, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16 in, fp32 accumulate", "data": "synthetic",
-            "config": {"workload": metric, "rank0_shard": shard, "l2": "256 MB buffer written before each step",
+            "config": {"workload": metric, "rank0_shard": shard,
+                       "l2": "256 MB buffer written before each step (then a fixed spin kernel covers the host's enqueue)",
                        "parallelism": f"heads over {world} GPUs, one all-gather of the output"},
             "roofline": tensor_roof(tf / world, tpeak, tkind, "per GPU, whole step", flops / world),
             "allgather": {"ms": round(statistics.median(gat), 4), "share": round(statistics.median(gat) / ms, 4),
@@ -837,7 +849,7 @@ def run_proj(args, torch, device):
     clocks = ClockSampler(device.index or 0).start()
     times = []
     for _ in range(args.steps):
-        flush.zero_()  # weights would otherwise stay in L2 between iterations
+        flush_and_cover(torch, flush)  # weights would otherwise stay in L2 between iterations
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
         call()

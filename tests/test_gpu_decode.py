@@ -250,13 +250,16 @@ def test_deltanet_batched():
     np.testing.assert_array_equal(ssm, states[2].ssm)
 
 
+@pytest.mark.parametrize("form", ["register", "staged"])
 @pytest.mark.parametrize("Hv,n_seq", [(32, 40), (16, 24)])
 @pytest.mark.parametrize("delta_mode", [ab.DELTA_CPUOPS, ab.DELTA_HF])
-def test_deltanet_batched_gqa(delta_mode, Hv, n_seq):
-    """Larger batches take the staged kernel (state blocks in and out by TMA tiles through shared
-    memory): 40 rows x 16 key heads in the 4B GQA shape (two value heads per key head) and 24 rows of
-    the 0.8B shape (one), 3 steps, rows in shuffled order, both delta-rule orders: every row's
-    outputs / state / conv ring / position vs the oracle."""
+def test_deltanet_batched_gqa(delta_mode, Hv, n_seq, form, monkeypatch):
+    """Larger batches, both forms of the wide-batch kernel (the state block in registers, or in and
+    out by TMA tiles through shared memory -- the library picks by batch size, ANELM_GDN_STAGED
+    forces one): 40 rows x 16 key heads in the 4B GQA shape (two value heads per key head) and 24
+    rows of the 0.8B shape (one), 3 steps, rows in shuffled order, both delta-rule orders: every
+    row's outputs / state / conv ring / position vs the oracle."""
+    monkeypatch.setenv("ANELM_GDN_STAGED", "1" if form == "staged" else "0")
     rng = np.random.default_rng(40 + delta_mode + Hv)
     shape = gdn_shape(16, Hv)
     steps = 3
