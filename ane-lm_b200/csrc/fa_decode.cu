@@ -183,6 +183,39 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const FaDecodePa
     // CTA reads only the QK-norm weights (never written by a kernel), after it everything else
     // (the projection row, ring metadata, positions, K / V pools).  Both are no-ops without PDL.
     asm volatile("griddepcontrol.launch_dependents;");
+    if (CM && tid == 0) {
+        // Before the dependency wait, an L2 prefetch of this CTA's share (1 / Hkv of the rows, for K and
+        // for V) of the ring slots its split will stream, so the tiles hit L2 once the wait is over.  A
+        // prefetch is only a hint -- L2 stays coherent with whatever the previous kernel writes -- so the
+        // ring metadata it is sized from may be read here, before that kernel has finished.
+        const int sq = p.seq_ids ? p.seq_ids[0] : 0;
+        const int cap_ = p.kv_len ? p.kv_cap[sq] : p.cap_s;
+        const int len_ = p.kv_len ? p.kv_len[sq] : p.len_s;
+        const int st_ = p.kv_len ? p.kv_start[sq] : p.start_s;
+        const long long base_ = p.kv_len ? p.kv_base[sq] : 0;
+        const int t0 = blk * p.CH, t1 = min(t0 + p.CH, len_);
+        if (cap_ > 0 && t1 > t0 && st_ >= 0 && st_ < cap_) {
+            const long long row_bytes = (long long)p.Hkv * D * 2;  // one slot: every kv head
+            int s0 = st_ + t0;
+            if (s0 >= cap_) s0 -= cap_;
+            int n = t1 - t0;
+            const int share = (n + p.Hkv - 1) / p.Hkv;  // this CTA's rows of each contiguous run
+            while (n > 0) {
+                const int run = min(n, cap_ - s0);          // up to the end of the ring, then from slot 0
+                const int r0 = min(run, kvh * share), r1 = min(run, r0 + share);
+                if (r1 > r0) {
+                    const long long off = (base_ + s0 + r0) * row_bytes;
+                    const uint32_t bytes = (uint32_t)((r1 - r0) * row_bytes);
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(
+                                     reinterpret_cast<const char*>(p.k_pool) + off), "r"(bytes) : "memory");
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(
+                                     reinterpret_cast<const char*>(p.v_pool) + off), "r"(bytes) : "memory");
+                }
+                n -= run;
+                s0 = 0;
+            }
+        }
+    }
     constexpr int NW = D / 32;
     float wq[NW], wk[NW];
     if (p.qk_norm) {
