@@ -27,6 +27,7 @@
 // The vocabulary logits never reach memory.  Every mbarrier wait
 // is bounded and reports ANELM_ERR_TIMEOUT.
 #include <algorithm>
+#include <climits>
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -49,7 +50,7 @@ constexpr int kGMaxStages = 8;         // projection GEMM: stages in flight for 
 constexpr int kGSmemMax = 227 * 1024;  // dynamic shared memory per CTA
 constexpr int kGPartPitch = kGBN + 4;  // fp32 words per row of a parked split-K partial
 // LM head: stage ring, barriers, and a [128][33] fp32 chunk staging area for the epilogue
-constexpr int kLmSmem = kGStages * (kGTileA + kGTileB) + 256 + 128 * 33 * 4 + 1024;
+constexpr int kLmSmem = kGStages * (kGTileA + kGTileB) + 256 + 128 * 33 * 4 + 128 * 32 + 1024;
 static_assert(kGBM * kGPartPitch * 4 <= kGStages * (kGTileA + kGTileB), "partial fits the stage buffers");
 
 // kind::f16 instruction descriptor with bf16 A and B (formats 1), fp32 D, both K-major
@@ -59,6 +60,10 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
 
 // Every top-k with k <= 32 is the head of the top-32, so the running lists always hold 32.
 constexpr int kTopK = 32;
+// a four-row group whose rows have at most this many survivors in a 32-column chunk inserts them one
+// by one (about 35 instructions each); more, and the group sorts its survivors and merges them
+// (about 700 for the four rows)
+constexpr int kLmInsertMax = 4;
 
 // kNarrow: tile width bn and stage count nst as given (one partial wave of narrower tiles);
 // otherwise the compile-time 256 columns and kGStages stages.
@@ -587,6 +592,52 @@ __device__ __forceinline__ void warp_topk_insert_if(float& tv, int& ti, bool val
     tv = ok ? nv : tv;
     ti = ok ? ni : ti;
 }
+// Order of the running lists: a before b when a's value is larger, or equal with the smaller index.
+// Folding columns in ascending order by insertion (ties kept behind the earlier entry) and taking the
+// top 32 of a union under this order give the same list.
+__device__ __forceinline__ bool key_gt(float av, int ai, float bv, int bi) {
+    return av > bv || (av == bv && ai < bi);
+}
+
+// Bitonic sort of four rows at once, one element per lane, ascending under key_gt (lane 0 smallest);
+// the rows' shuffle chains interleave.
+__device__ __forceinline__ void warp_sort4_asc(float (&v)[4], int (&s)[4], int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const bool keep_min = ((lane & j) == 0) == ((lane & k) == 0);
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float pv = __shfl_xor_sync(0xffffffffu, v[q], j);
+                const int ps = __shfl_xor_sync(0xffffffffu, s[q], j);
+                const bool take = keep_min != key_gt(pv, ps, v[q], s[q]);
+                v[q] = take ? pv : v[q];
+                s[q] = take ? ps : s[q];
+            }
+        }
+    }
+}
+
+// Merge of 32 candidates sorted ascending (cv, ci) into the descending list (tv, ti): the larger of
+// list entry j and candidate j is the top 32 of the union as a bitonic sequence, which five
+// half-cleaner steps sort descending.
+__device__ __forceinline__ void warp_merge_sorted(float& tv, int& ti, float cv, int ci, int lane) {
+    const bool c = key_gt(cv, ci, tv, ti);
+    float v = c ? cv : tv;
+    int i = c ? ci : ti;
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) {
+        const float pv = __shfl_xor_sync(0xffffffffu, v, j);
+        const int pi = __shfl_xor_sync(0xffffffffu, i, j);
+        const bool take = ((lane & j) == 0) == key_gt(pv, pi, v, i);
+        v = take ? pv : v;
+        i = take ? pi : i;
+    }
+    tv = v;
+    ti = i;
+}
+
 __device__ __forceinline__ void warp_topk_insert(float& tv, int& ti, float v, int id, int lane) {
     // v and id are the same in every lane; the list is sorted descending across lanes
     if (!(v > __shfl_sync(0xffffffffu, tv, 31))) return;
@@ -706,6 +757,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
         // are inserted (warp-uniform work: no lane idles through another lane's insertion).
         const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
         float* stage = rows + warp * 32 * 33;  // [32 rows][33]
+        uint8_t* srcb = reinterpret_cast<uint8_t*>(rows + 128 * 33) + warp * 32 * 32;  // [32 rows][32]
         const int rr = kGBM / rep;                    // rows per copy of the A block
         const int cp = (32 * warp) / rr;              // the copy this warp's TMEM lanes hold
         const int rbase = (32 * warp) % rr;           // its first row within the copy
@@ -735,17 +787,57 @@ __global__ void __launch_bounds__(kGThreads, 1)
                 for (int c = 0; c < 32; c++) stage[lane * 33 + c] = __uint_as_float(x[c]);
                 __syncwarp();
                 const int n = n0 + c0 + lane;  // the column this lane tests
-                // first every row's survivors (32 independent ballots, which pipeline), then the
-                // insertions of the survivors (each re-read from the staging rows as a broadcast)
-                unsigned masks[32];
+                // first every row's survivors (32 independent ballots, which pipeline); lane r keeps
+                // row r's mask, and bit g of `big` marks the four-row groups with more than
+                // kLmInsertMax survivors in some row
+                unsigned masks[32], my_mask = 0, big = 0;
 #pragma unroll
                 for (int r = 0; r < 32; r++) {
                     const float thr = __shfl_sync(0xffffffffu, lv[r], 31);  // every lane shuffles (outside the &&)
                     masks[r] = __ballot_sync(0xffffffffu, r < nrow && n < N && stage[r * 33 + lane] > thr);
+                    my_mask = lane == r ? masks[r] : my_mask;
                 }
-                // four rows' insertions interleaved (branch-free, so their shuffle chains overlap)
 #pragma unroll
                 for (int r0 = 0; r0 < 32; r0 += 4) {
+                    const int mx = max(max(__popc(masks[r0]), __popc(masks[r0 + 1])),
+                                       max(__popc(masks[r0 + 2]), __popc(masks[r0 + 3])));
+                    big |= (mx > kLmInsertMax ? 1u : 0u) << (r0 >> 2);
+                }
+                // groups with many survivors: each row's survivors (the rest as -inf) sorted ascending
+                // in place in the staging row, their source lanes beside them (32: none)
+#pragma unroll 1
+                for (int gi = 0; gi < 8; gi++) {
+                    if (!((big >> gi) & 1u)) continue;
+                    float cv[4];
+                    int cs[4];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const int r = 4 * gi + q;
+                        const bool s = (__shfl_sync(0xffffffffu, my_mask, r) >> lane) & 1u;
+                        cv[q] = s ? stage[r * 33 + lane] : -INFINITY;
+                        cs[q] = s ? lane : 32;
+                    }
+                    warp_sort4_asc(cv, cs, lane);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        stage[(4 * gi + q) * 33 + lane] = cv[q];
+                        srcb[(4 * gi + q) * 32 + lane] = (uint8_t)cs[q];
+                    }
+                }
+                __syncwarp();
+                // those groups merge their sorted survivors into the lists; the others insert theirs
+                // one by one, four rows interleaved (branch-free, so their shuffle chains overlap)
+#pragma unroll
+                for (int r0 = 0; r0 < 32; r0 += 4) {
+                    if ((big >> (r0 >> 2)) & 1u) {
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            const int s = srcb[(r0 + q) * 32 + lane];
+                            warp_merge_sorted(lv[r0 + q], li[r0 + q], stage[(r0 + q) * 33 + lane],
+                                              s < 32 ? n0 + c0 + s : INT_MAX, lane);
+                        }
+                        continue;
+                    }
                     unsigned mk[4] = {masks[r0], masks[r0 + 1], masks[r0 + 2], masks[r0 + 3]};
                     while (mk[0] | mk[1] | mk[2] | mk[3]) {
 #pragma unroll
@@ -1043,16 +1135,14 @@ __global__ void __launch_bounds__(kGvThreads) lm_head_gemv_topk_kernel(const __n
     }
 }
 
-// One CTA per row: each thread keeps the top-32 of its share of the row's n_tiles * 32 candidates,
-// then pairs of lists merge in shared memory (7 levels) into the row's top-32, sorted descending;
-// the first k are written.
 constexpr int kMergeWarps = 8;
-constexpr int kMergeBatch = 8;  // rounds of 32 candidates whose loads a warp keeps in flight together
-// One CTA per row.  Each warp folds a strided share of the row's candidates (32 at a time, one per
-// lane) into a running top-32 spread over its lanes: a ballot picks the candidates above the list's
-// 32nd value and only those are inserted (warp_topk_insert_if re-checks each against the current
-// 32nd).  Warp 0 then folds the other warps' lists in the same way.  Every loop trip count and
-// ballot mask is warp-uniform, so all lanes take part in every shuffle.
+constexpr int kMergeBatch = 8;  // candidate lists whose loads a warp keeps in flight together
+// One CTA per row.  Every candidate list arrives sorted descending (lane j of the writing warp held
+// its j-th largest), so a warp folds a whole list in one step: read reversed (ascending), merged
+// into a running top-32 spread over its lanes by warp_merge_sorted.  Each warp keeps two running
+// lists so two merges' shuffle chains overlap, folds a strided share of the row's lists, then
+// merges its two lists; warp 0 merges the other warps' lists the same way.  Ties among equal
+// values keep the smaller vocabulary index first.  Every trip count is warp-uniform.
 __global__ void __launch_bounds__(32 * kMergeWarps) lm_topk_merge_kernel(const float* cand, int M, int ntile, int k,
                                                                          float* top_vals, int* top_idx) {
     __shared__ float sv[kMergeWarps][kTopK];
@@ -1061,40 +1151,33 @@ __global__ void __launch_bounds__(32 * kMergeWarps) lm_topk_merge_kernel(const f
     const long long nc = (long long)ntile * kTopK;
     const float* cv = cand + (long long)m * nc;
     const int* ci = reinterpret_cast<const int*>(cand + (long long)M * nc) + (long long)m * nc;
-    float tv = -INFINITY;  // lane j: the j-th largest value so far (ties keep the earlier entry first)
-    int ti = -1;
-    auto fold = [&](float v, int id, bool in) {
-        unsigned mk = __ballot_sync(0xffffffffu, in && v > __shfl_sync(0xffffffffu, tv, 31));
-        while (mk) {
-            const int src = __ffs(mk) - 1;
-            mk &= mk - 1;
-            const float x = __shfl_sync(0xffffffffu, v, src);
-            const int xi = __shfl_sync(0xffffffffu, id, src);
-            warp_topk_insert_if(tv, ti, true, x, xi, lane);
-        }
-    };
-    // kMergeBatch rounds' loads are issued together (one latency per batch, not per round):
-    // round u of batch k covers candidates 32 (warp + W (u + kMergeBatch k)) + lane, W = kMergeWarps
-    for (long long base = 32LL * warp; base < nc; base += 32LL * kMergeWarps * kMergeBatch) {
+    float tv[2] = {-INFINITY, -INFINITY};  // lane j: the j-th largest so far, two independent lists
+    int ti[2] = {-1, -1};
+    // list t = base + kMergeWarps u for round u of a batch; the loads of a batch are issued together
+    for (int base = warp; base < ntile; base += kMergeWarps * kMergeBatch) {
         float v[kMergeBatch];
         int id[kMergeBatch];
 #pragma unroll
         for (int u = 0; u < kMergeBatch; u++) {
-            const long long i = base + 32LL * kMergeWarps * u + lane;
-            v[u] = i < nc ? cv[i] : -INFINITY;
-            id[u] = i < nc ? ci[i] : -1;
+            const int t = base + kMergeWarps * u;
+            const long long i = (long long)t * kTopK + (kTopK - 1 - lane);  // reversed: ascending
+            v[u] = t < ntile ? cv[i] : -INFINITY;
+            id[u] = t < ntile ? ci[i] : INT_MAX;
         }
 #pragma unroll
-        for (int u = 0; u < kMergeBatch; u++) fold(v[u], id[u], base + 32LL * kMergeWarps * u + lane < nc);
+        for (int u = 0; u < kMergeBatch; u++) warp_merge_sorted(tv[u & 1], ti[u & 1], v[u], id[u], lane);
     }
-    sv[warp][lane] = tv;
-    si[warp][lane] = ti;
+    warp_merge_sorted(tv[0], ti[0], __shfl_sync(0xffffffffu, tv[1], 31 - lane),
+                      __shfl_sync(0xffffffffu, ti[1], 31 - lane), lane);
+    sv[warp][lane] = tv[0];
+    si[warp][lane] = ti[0];
     __syncthreads();
     if (warp == 0) {
-        for (int w = 1; w < kMergeWarps; w++) fold(sv[w][lane], si[w][lane], true);
+        for (int w = 1; w < kMergeWarps; w++)
+            warp_merge_sorted(tv[0], ti[0], sv[w][kTopK - 1 - lane], si[w][kTopK - 1 - lane], lane);
         if (lane < k) {
-            top_vals[(long long)m * k + lane] = tv;
-            top_idx[(long long)m * k + lane] = ti;
+            top_vals[(long long)m * k + lane] = tv[0];
+            top_idx[(long long)m * k + lane] = ti[0];
         }
     }
 }
