@@ -49,8 +49,12 @@ constexpr int kGroupM = 16;          // row tiles per raster band of a multi-wav
 constexpr int kGMaxStages = 8;         // projection GEMM: stages in flight for narrow B tiles
 constexpr int kGSmemMax = 227 * 1024;  // dynamic shared memory per CTA
 constexpr int kGPartPitch = kGBN + 4;  // fp32 words per row of a parked split-K partial
-// LM head: stage ring, barriers, and a [128][33] fp32 chunk staging area for the epilogue
-constexpr int kLmSmem = kGStages * (kGTileA + kGTileB) + 256 + 128 * 33 * 4 + 128 * 32 + 1024;
+// LM head: stage ring, barriers, and a buffer of (value, index) entries per row for the epilogue
+// (32 entries + 1 of padding, so rows whose counts agree write different banks)
+constexpr int kLmBufPitch = 33;
+constexpr int kLmSmem = kGStages * (kGTileA + kGTileB) + 256 + 128 * kLmBufPitch * 8 + 128 * 4 + 1024;
+constexpr unsigned long long kLmTauWaitNs = 20000;  // longest wait for the other CTAs' first-tile maxima
+static_assert(kLmSmem <= kGSmemMax, "LM-head stages and row buffers fit in shared memory");
 static_assert(kGBM * kGPartPitch * 4 <= kGStages * (kGTileA + kGTileB), "partial fits the stage buffers");
 
 // kind::f16 instruction descriptor with bf16 A and B (formats 1), fp32 D, both K-major
@@ -60,10 +64,6 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
 
 // Every top-k with k <= 32 is the head of the top-32, so the running lists always hold 32.
 constexpr int kTopK = 32;
-// a four-row group whose rows have at most this many survivors in a 32-column chunk inserts them one
-// by one (about 35 instructions each); more, and the group sorts its survivors and merges them
-// (about 700 for the four rows)
-constexpr int kLmInsertMax = 4;
 
 // kNarrow: tile width bn and stage count nst as given (one partial wave of narrower tiles);
 // otherwise the compile-time 256 columns and kGStages stages.
@@ -653,6 +653,17 @@ __device__ __forceinline__ void warp_topk_insert(float& tv, int& ti, float v, in
     }
 }
 
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+
 // Persistent LM-head kernel: CTA (g, mt) handles vocabulary tiles g, g + G, ... (G = gridDim.x)
 // for rows [128 mt, 128 mt + 128).  Warp 4: TMA ring (A rows, B vocabulary rows); warp 5: MMAs
 // of each tile into TMEM buffer (i & 1) once the epilogue released it; warps 0-3: per row, the
@@ -661,9 +672,18 @@ __device__ __forceinline__ void warp_topk_insert(float& tv, int& ti, float v, in
 // copies of the rr-row block (rr = 32 or 64, one TMA box each, tmA's box is rr rows), so every
 // epilogue warp has rows: the warps reading copy cp take columns [cp 256 / rep, (cp + 1) 256 / rep)
 // of each tile and keep their own list (copy cp's list of CTA g is candidate list g rep + cp).
+//
+// Before any list is fed, every CTA publishes each row's largest logit of its first tile (pmax
+// [M][gpitch], slot g; NaN = not yet published, set by the launcher) and waits, at most
+// kLmTauWaitNs, for the other CTAs' maxima (arrive counts the publishing warps).  For a row, the
+// maxima in slots j, j + 32, ... (j = 0..31) form 32 disjoint groups of columns; the smallest of the
+// 32 group maxima is the 32nd largest of 32 distinct logits, so no logit below it can be among the
+// row's top 32.  The lists then only take logits at or above that bound (ties kept), and being
+// the top 32 under key_gt of those, they still merge to the exact top 32.  A CTA that stops
+// waiting uses what is published by then: a weaker bound, the same result.
 __global__ void __launch_bounds__(kGThreads, 1)
     lm_head_topk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* cand,
-                        int M, int N, int K, int rep, int* err) {
+                        float* pmax, int gpitch, unsigned* arrive, int M, int N, int K, int rep, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -674,7 +694,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
     uint64_t* tfree = tfull + 2;         // [2] the epilogue has read accumulator b
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* rows = reinterpret_cast<float*>(tmem_slot + 4);  // [128][33] chunk staging
+    float* rows = reinterpret_cast<float*>(tmem_slot + 4);  // [128 rows][kLmBufPitch] (value, index) buffers
+    float* pub = rows + 128 * kLmBufPitch * 2;              // [4 warps][32] first-tile maxima
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, g = blockIdx.x, m0 = blockIdx.y * kGBM;
     const int ntile = (N + kGBN - 1) / kGBN;
@@ -752,12 +773,14 @@ __global__ void __launch_bounds__(kGThreads, 1)
         __syncwarp();
     } else {
         // ---------------- epilogue: running top-32 of rows 32 warp + r, spread over the warp's lanes ----------------
-        // Each 32-column chunk (thread = row) is transposed through shared memory; then, row by row,
-        // every lane tests one column against the row's 32nd value and only the ballot's survivors
-        // are inserted (warp-uniform work: no lane idles through another lane's insertion).
+        // Thread r holds row r's logits of each 16-column half chunk (tcgen05.ld, thread = row) and
+        // appends those above its row's 32nd value to the row's buffer in shared memory.  A row
+        // whose buffer passes 16 entries (so the next half always fits) has it sorted (bitonic,
+        // four rows at a time) and merged into the list in one step, which refreshes the row's
+        // threshold; the buffers left at the end are merged the same way.  The list of a row is the
+        // top 32 under key_gt of every column it saw, the same as inserting them one by one.
         const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
-        float* stage = rows + warp * 32 * 33;  // [32 rows][33]
-        uint8_t* srcb = reinterpret_cast<uint8_t*>(rows + 128 * 33) + warp * 32 * 32;  // [32 rows][32]
+        float2* buf = reinterpret_cast<float2*>(rows) + warp * 32 * kLmBufPitch;  // [32 rows][pitch] (value, index)
         const int rr = kGBM / rep;                    // rows per copy of the A block
         const int cp = (32 * warp) / rr;              // the copy this warp's TMEM lanes hold
         const int rbase = (32 * warp) % rr;           // its first row within the copy
@@ -770,88 +793,149 @@ __global__ void __launch_bounds__(kGThreads, 1)
             lv[r] = -INFINITY;
             li[r] = -1;
         }
-        for (int i = 0; i < my_tiles; i++) {
-            const int b = i & 1, n0 = (g + i * G) * kGBN;
-            if (!tc::mbar_wait(&tfull[b], (uint32_t)(i >> 1) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
+        // ---- the rows' lower bounds from every CTA's first-tile maxima ----
+        float my_max = -INFINITY;  // row `lane`'s largest logit among this warp's columns of the first tile
+        if (tc::mbar_wait(&tfull[0], 0, err, ANELM_ERR_TIMEOUT, abort)) {
             tc::tc_fence_after();
+            const int n0 = g * kGBN;
 #pragma unroll 1
-            for (int c0 = cbeg; c0 < cend; c0 += 32) {
-                uint32_t x[32];
-                tc::tmem_ld32(trow + b * kGBN + c0, x);
+            for (int c = cbeg; c < cend; c += 16) {
+                uint32_t x[16];
+                tc::tmem_ld16(trow + c, x);
                 tc::tmem_ld_wait();
-                if (c0 == cend - 32) {  // this warp's last read of accumulator b: the MMAs may reuse it
+                const int lim = N - (n0 + c);
+#pragma unroll
+                for (int k = 0; k < 16; k++)
+                    if (k < lim) my_max = fmaxf(my_max, __uint_as_float(x[k]));
+            }
+        }
+        pub[warp * 32 + lane] = my_max;
+        tc::named_bar_sync(1, 128);
+        if (cp == 0) {  // the warps of copy 0 publish their rows' maxima over the rep copies
+#pragma unroll 1
+            for (int k = 1; k < rep; k++) my_max = fmaxf(my_max, pub[(warp + k * (rr / 32)) * 32 + lane]);
+            if (lane < nrow) pmax[(long long)(m0 + rbase + lane) * gpitch + g] = my_max;
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence();
+                atomicAdd(arrive, 1u);
+            }
+        }
+        if (lane == 0) {
+            const unsigned total = gridDim.x * gridDim.y * (4 / rep);
+            const unsigned long long t0 = globaltimer_ns();
+            while (ld_acquire_gpu(arrive) < total && globaltimer_ns() - t0 < kLmTauWaitNs) __nanosleep(128);
+        }
+        __syncwarp();
+        float my_tau = -INFINITY;  // row `lane`'s bound: min over groups j of max(pmax[row][j + 32 t])
+        if (lane < nrow) {
+            const float* prow = pmax + (long long)(m0 + rbase + lane) * gpitch;
+            float grp[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) grp[j] = -INFINITY;
+#pragma unroll 1
+            for (int t0 = 0; t0 < G; t0 += 32) {  // 32 slots (8 float4) a batch, slot t in group t % 32
+                float4 q[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    q[u] = t0 + 4 * u < G ? __ldcg(reinterpret_cast<const float4*>(prow + t0) + u)
+                                          : make_float4(NAN, NAN, NAN, NAN);
+#pragma unroll
+                for (int u = 0; u < 8; u++) {  // slots past G (padding of the row pitch) hold NaN
+                    grp[4 * u] = fmaxf(grp[4 * u], q[u].x);
+                    grp[4 * u + 1] = fmaxf(grp[4 * u + 1], q[u].y);
+                    grp[4 * u + 2] = fmaxf(grp[4 * u + 2], q[u].z);
+                    grp[4 * u + 3] = fmaxf(grp[4 * u + 3], q[u].w);
+                }
+            }
+            my_tau = grp[0];
+#pragma unroll
+            for (int j = 1; j < 32; j++) my_tau = fminf(my_tau, grp[j]);
+        }
+        // v >= tau as one strict compare: the float just below tau (-inf stays -inf)
+        const float tau_lo = my_tau > -INFINITY ? nextafterf(my_tau, -INFINITY) : -INFINITY;
+        float my_thr = lane < nrow ? tau_lo : INFINITY;  // row `lane`'s admission bound (+inf: no such row)
+        int my_cnt = 0;                                  // entries in row `lane`'s buffer
+        float2* my_buf = buf + lane * kLmBufPitch;
+        const float2 pad = make_float2(-INFINITY, __int_as_float(INT_MAX));
+        int i = 0, c0 = cbeg;  // the next tile and half chunk
+        for (;;) {
+            const bool last = i >= my_tiles;  // every tile read: merge what the buffers still hold
+            unsigned need;
+            if (!last) {
+                const int b = i & 1, n0 = (g + i * G) * kGBN;
+                if (c0 == cbeg) {
+                    if (!tc::mbar_wait(&tfull[b], (uint32_t)(i >> 1) & 1, err, ANELM_ERR_TIMEOUT, abort)) break;
+                    tc::tc_fence_after();
+                }
+                uint32_t x[16];
+                tc::tmem_ld16(trow + b * kGBN + c0, x);
+                tc::tmem_ld_wait();
+                if (c0 + 16 == cend) {  // this warp's last read of accumulator b: the MMAs may reuse it
                     tc::tc_fence_before();
                     tc::mbar_arrive(&tfree[b]);
                 }
+                const int lim = N - (n0 + c0);  // columns of this half inside the vocabulary
 #pragma unroll
-                for (int c = 0; c < 32; c++) stage[lane * 33 + c] = __uint_as_float(x[c]);
-                __syncwarp();
-                const int n = n0 + c0 + lane;  // the column this lane tests
-                // first every row's survivors (32 independent ballots, which pipeline); lane r keeps
-                // row r's mask, and bit g of `big` marks the four-row groups with more than
-                // kLmInsertMax survivors in some row
-                unsigned masks[32], my_mask = 0, big = 0;
-#pragma unroll
-                for (int r = 0; r < 32; r++) {
-                    const float thr = __shfl_sync(0xffffffffu, lv[r], 31);  // every lane shuffles (outside the &&)
-                    masks[r] = __ballot_sync(0xffffffffu, r < nrow && n < N && stage[r * 33 + lane] > thr);
-                    my_mask = lane == r ? masks[r] : my_mask;
-                }
-#pragma unroll
-                for (int r0 = 0; r0 < 32; r0 += 4) {
-                    const int mx = max(max(__popc(masks[r0]), __popc(masks[r0 + 1])),
-                                       max(__popc(masks[r0 + 2]), __popc(masks[r0 + 3])));
-                    big |= (mx > kLmInsertMax ? 1u : 0u) << (r0 >> 2);
-                }
-                // groups with many survivors: each row's survivors (the rest as -inf) sorted ascending
-                // in place in the staging row, their source lanes beside them (32: none)
-#pragma unroll 1
-                for (int gi = 0; gi < 8; gi++) {
-                    if (!((big >> gi) & 1u)) continue;
-                    float cv[4];
-                    int cs[4];
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const int r = 4 * gi + q;
-                        const bool s = (__shfl_sync(0xffffffffu, my_mask, r) >> lane) & 1u;
-                        cv[q] = s ? stage[r * 33 + lane] : -INFINITY;
-                        cs[q] = s ? lane : 32;
-                    }
-                    warp_sort4_asc(cv, cs, lane);
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        stage[(4 * gi + q) * 33 + lane] = cv[q];
-                        srcb[(4 * gi + q) * 32 + lane] = (uint8_t)cs[q];
+                for (int c = 0; c < 16; c++) {
+                    const float v = __uint_as_float(x[c]);
+                    if (c < lim && v > my_thr) {
+                        my_buf[my_cnt] = make_float2(v, __int_as_float(n0 + c0 + c));
+                        my_cnt++;
                     }
                 }
-                __syncwarp();
-                // those groups merge their sorted survivors into the lists; the others insert theirs
-                // one by one, four rows interleaved (branch-free, so their shuffle chains overlap)
-#pragma unroll
-                for (int r0 = 0; r0 < 32; r0 += 4) {
-                    if ((big >> (r0 >> 2)) & 1u) {
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            const int s = srcb[(r0 + q) * 32 + lane];
-                            warp_merge_sorted(lv[r0 + q], li[r0 + q], stage[(r0 + q) * 33 + lane],
-                                              s < 32 ? n0 + c0 + s : INT_MAX, lane);
-                        }
-                        continue;
-                    }
-                    unsigned mk[4] = {masks[r0], masks[r0 + 1], masks[r0 + 2], masks[r0 + 3]};
-                    while (mk[0] | mk[1] | mk[2] | mk[3]) {
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            const bool has = mk[q] != 0;
-                            const int src = has ? __ffs(mk[q]) - 1 : 0;
-                            mk[q] &= mk[q] - 1;
-                            warp_topk_insert_if(lv[r0 + q], li[r0 + q], has, stage[(r0 + q) * 33 + src],
-                                                n0 + c0 + src, lane);
-                        }
-                    }
+                need = __ballot_sync(0xffffffffu, my_cnt > 16);
+                c0 += 16;
+                if (c0 == cend) {
+                    c0 = cbeg;
+                    i++;
                 }
-                __syncwarp();  // the next chunk overwrites the staging rows
+            } else {
+                need = __ballot_sync(0xffffffffu, my_cnt > 0);
             }
+            if (need) {
+                __syncwarp();  // the rows' appends are visible to the whole warp
+                // sort each chosen row's buffer ascending (the unused slots as padding), four rows at
+                // a time, in place
+                unsigned pend = need;
+                while (pend) {
+                    int rs[4];
+                    float cv[4];
+                    int ci[4];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        rs[q] = pend ? __ffs(pend) - 1 : 32;
+                        pend &= pend - 1;
+                        const int cnt = __shfl_sync(0xffffffffu, my_cnt, rs[q] & 31);
+                        const float2 e = rs[q] < 32 && lane < cnt ? buf[rs[q] * kLmBufPitch + lane] : pad;
+                        cv[q] = e.x;
+                        ci[q] = __float_as_int(e.y);
+                    }
+                    warp_sort4_asc(cv, ci, lane);
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        if (rs[q] < 32) buf[rs[q] * kLmBufPitch + lane] = make_float2(cv[q], __int_as_float(ci[q]));
+                }
+                __syncwarp();
+                // merge them into the lists, four rows' shuffle chains together, and refresh the thresholds
+#pragma unroll
+                for (int r0 = 0; r0 < 32; r0 += 4) {
+                    if (!((need >> r0) & 0xFu)) continue;
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const float2 e = (need >> (r0 + q)) & 1u ? buf[(r0 + q) * kLmBufPitch + lane] : pad;
+                        warp_merge_sorted(lv[r0 + q], li[r0 + q], e.x, __float_as_int(e.y), lane);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const float t = __shfl_sync(0xffffffffu, lv[r0 + q], 31);
+                        my_thr = lane == r0 + q && ((need >> (r0 + q)) & 1u) ? fmaxf(t, tau_lo) : my_thr;
+                    }
+                }
+                my_cnt = (need >> lane) & 1u ? 0 : my_cnt;
+                __syncwarp();  // the merged buffers are read before they are refilled
+            }
+            if (last) break;
         }
 #pragma unroll
         for (int r = 0; r < 32; r++) {
@@ -1215,11 +1299,16 @@ static int lm_swap_groups(int vocab) {
     return std::max(1, std::min((vocab + kLsBM - 1) / kLsBM, sms));
 }
 
+// the tensor-core path's first-tile maxima [n][pitch] (pitch: CTAs over the vocabulary, rounded up to
+// whole 16-byte rows) and its arrival counter follow its candidate lists
+static int lm_max_pitch(int n, int vocab) { return (lm_groups(n, vocab) + 3) & ~3; }
+
 size_t lm_head_topk_workspace_bytes(int n, int vocab) {
     int g = lm_groups(n, vocab) * lm_rep(n);                      // tensor-core path
     if (n <= kLmGemvRows) g = std::max(g, lm_gemv_groups(vocab));  // CUDA-core path
     if (n <= kLsN) g = std::max(g, lm_swap_groups(vocab) * 4);      // swapped path
-    return (size_t)n * g * kTopK * 8;
+    const size_t tc_extra = (size_t)n * lm_max_pitch(n, vocab) * 4 + 16;
+    return (size_t)n * g * kTopK * 8 + tc_extra;
 }
 
 int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long ldw, int n, int vocab, int hidden, int k,
@@ -1262,10 +1351,15 @@ int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long l
         return ANELM_ERR_CUDA;
     constexpr int smem = kLmSmem;
     cudaFuncSetAttribute(lm_head_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    const int G = lm_groups(n, vocab);
+    const int G = lm_groups(n, vocab), gpitch = lm_max_pitch(n, vocab);
+    float* pmax = static_cast<float*>(workspace) + (size_t)n * G * rep * kTopK * 2;
+    unsigned* arrive = reinterpret_cast<unsigned*>(pmax + (size_t)n * gpitch);
+    if (cudaMemsetAsync(pmax, 0xFF, (size_t)n * gpitch * 4, stream) != cudaSuccess ||  // NaN: not published
+        cudaMemsetAsync(arrive, 0, 4, stream) != cudaSuccess)
+        return ANELM_ERR_CUDA;
     dim3 grid(G, (n + kGBM - 1) / kGBM);
-    lm_head_topk_kernel<<<grid, kGThreads, smem, stream>>>(mA, mB, static_cast<float*>(workspace), n, vocab, hidden,
-                                                           rep, err);
+    lm_head_topk_kernel<<<grid, kGThreads, smem, stream>>>(mA, mB, static_cast<float*>(workspace), pmax, gpitch, arrive,
+                                                           n, vocab, hidden, rep, err);
     lm_topk_merge_kernel<<<n, 32 * kMergeWarps, 0, stream>>>(static_cast<const float*>(workspace), n, G * rep, k,
                                                           top_vals, top_idx);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
