@@ -955,7 +955,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
 }
 
-// LM head for 2-16 rows with the roles swapped: D^T [128 vocabulary rows][16] = W_tile . h^T, so the
+// LM head for a few rows (up to 16; the launcher takes it for 2-8) with the roles swapped:
+// D^T [128 vocabulary rows][16] = W_tile . h^T, so the
 // streamed weights are the M = 128 operand (16 KB a k-step, kLsStages of them in flight) and the
 // rows of h the N = 16 operand, loaded once for the whole K and kept in shared memory.  TMEM lane =
 // vocabulary row, column = row of h: epilogue warp w reads its 32 vocabulary rows of a tile with
@@ -1286,10 +1287,13 @@ static int lm_gemv_groups(int vocab) {
     return std::max(1, std::min((vocab + rows_per_block - 1) / rows_per_block, sms * kGvBlocksPerSm));
 }
 
-// copies of the row block in the tensor-core path's A tile, so every epilogue warp has rows (measured:
-// 32 rows 650 -> 475 us, 64 rows 659 -> 557 us); up to 8 rows the insertions are few and the extra
-// candidate lists cost the merge more than the split saves (4 rows 286 -> 297 us with four copies)
-static int lm_rep(int n) { return n <= 8 ? 1 : n <= 32 ? 4 : n <= 64 ? 2 : 1; }
+// copies of the row block in the tensor-core path's A tile, so every epilogue warp has rows: with
+// 9-24 rows four copies (graph-timed, 16 rows 241 -> 228 us, 24 rows 241 -> 217 us); from 25 rows
+// one copy does as well or better (32 rows 220 -> 210 us), since the epilogue takes few logits
+static int lm_rep(int n) { return n > 8 && n <= 24 ? 4 : 1; }
+// rows up to which the swapped kernel is taken (16 rows: 240 us there against 228 in the tile kernel)
+constexpr int kLmSwapRows = 8;
+static_assert(kLmSwapRows <= kLsN, "the swapped kernel's N covers its rows");
 
 // CTAs of the swapped few-row path: one per SM, at most one per 128 vocabulary rows
 static int lm_swap_groups(int vocab) {
@@ -1306,7 +1310,7 @@ static int lm_max_pitch(int n, int vocab) { return (lm_groups(n, vocab) + 3) & ~
 size_t lm_head_topk_workspace_bytes(int n, int vocab) {
     int g = lm_groups(n, vocab) * lm_rep(n);                      // tensor-core path
     if (n <= kLmGemvRows) g = std::max(g, lm_gemv_groups(vocab));  // CUDA-core path
-    if (n <= kLsN) g = std::max(g, lm_swap_groups(vocab) * 4);      // swapped path
+    if (n <= kLmSwapRows) g = std::max(g, lm_swap_groups(vocab) * 4);  // swapped path
     const size_t tc_extra = (size_t)n * lm_max_pitch(n, vocab) * 4 + 16;
     return (size_t)n * g * kTopK * 8 + tc_extra;
 }
@@ -1329,8 +1333,8 @@ int launch_lm_head_topk(const void* h, long long ldh, const void* W, long long l
                                                               top_idx);
         return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
     }
-    if (n <= kLsN && lm_swap_smem(hidden) <= (size_t)kGSmemMax) {
-        // 2-16 rows: weights as the M operand, h resident in shared memory (see lm_head_swap_topk_kernel)
+    if (n <= kLmSwapRows && lm_swap_smem(hidden) <= (size_t)kGSmemMax) {
+        // 2-8 rows: weights as the M operand, h resident in shared memory (see lm_head_swap_topk_kernel)
         CUtensorMap mW, mH;
         if (!make_bf16_map(&mW, W, (uint64_t)vocab, (uint64_t)hidden, (uint64_t)ldw, kLsBM) ||
             !make_bf16_map(&mH, h, (uint64_t)n, (uint64_t)hidden, (uint64_t)ldh, kLsN))

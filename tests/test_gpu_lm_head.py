@@ -32,12 +32,13 @@ def _check(n, vocab, hidden, k, seed):
     assert all(len(set(r.tolist())) == k for r in idx)  # no index twice
 
 
-@pytest.mark.parametrize("n", [1, 4, 5, 16, 17, 33, 64, 65, 256])
+@pytest.mark.parametrize("n", [1, 4, 5, 8, 9, 16, 17, 24, 25, 33, 64, 65, 256])
 def test_lm_head_top32_qwen_vocab(n):
-    """One row takes the CUDA-core path (weights streamed, per-warp running top-32), more rows the
-    tensor-core path: 9-32 rows with four copies of the row block in the A tile (each epilogue warp
-    takes a quarter of every tile's columns), 33-64 with two (33: the second warp of each copy holds
-    one row), others with one."""
+    """One row takes the CUDA-core path (weights streamed, per-warp running top-32), 2-8 rows the
+    swapped-role kernel, more rows the tensor-core tile kernel: 9-24 rows with four copies of the row
+    block in the A tile (each epilogue warp takes a quarter of every tile's columns), others with one
+    (256: two row tiles).  The tile kernel's lists only take logits at or above the bound built from
+    every CTA's first-tile maxima."""
     _check(n, 248320, 2560, 32, seed=n)
 
 
@@ -49,7 +50,32 @@ def test_lm_head_ragged_vocab(n, k):
 
 @pytest.mark.parametrize("n", [2, 8, 16])
 def test_lm_head_wide_hidden_few_rows(n):
-    """2-16 rows take the swapped-role kernel only while the rows of h fit its shared memory (hidden up
+    """2-8 rows take the swapped-role kernel only while the rows of h fit its shared memory (hidden up
     to about 3,100); at hidden 4,096 they fall back to the tensor-core tile kernel with one copy of the
-    row block -- that path, against the same reference."""
+    row block (16 rows: four copies) -- that path, against the same reference."""
     _check(n, 32768, 4096, 32, seed=100 + n)
+
+
+@pytest.mark.parametrize("n", [16, 32, 128])
+def test_lm_head_ties_exact(n):
+    """Integer logits (h, W in {-1, 0, 1}, hidden 256: exact in fp32 whatever the summation order) with
+    about a dozen vocabulary rows per value near the top, so the 32nd value is tied across rows that
+    land in different CTAs' lists.  The tile kernel's lists and the merge order by (value descending,
+    index ascending) and keep logits equal to the first-tile bound, so the result is exactly the first
+    32 of that order: values and indices."""
+    import numpy as np
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7 + n)
+    vocab, hidden = 248320, 256
+    h = torch.randint(-1, 2, (n, hidden), generator=g, device="cuda").to(torch.bfloat16)
+    w = torch.randint(-1, 2, (vocab, hidden), generator=g, device="cuda").to(torch.bfloat16)
+    vals, idx = lm_head_topk(h, w, 32)
+    logits = (h.float() @ w.float().T).cpu().numpy()
+    cols = np.arange(vocab)
+    for r in range(n):
+        order = np.lexsort((cols, -logits[r]))[:32]
+        assert np.array_equal(idx[r].cpu().numpy(), order), r
+        assert np.array_equal(vals[r].cpu().numpy(), logits[r][order]), r
+    # the boundary is tied: the 32nd value also appears beyond the first 32
+    assert any((logits[r] == logits[r][np.lexsort((cols, -logits[r]))[31]]).sum() > 1 for r in range(n))
