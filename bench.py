@@ -70,9 +70,9 @@ L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 ENQUEUE_COVER_CYCLES = 200_000
 
 
-def flush_and_cover(torch, flush):
+def flush_and_cover(torch, flush, cycles=ENQUEUE_COVER_CYCLES):
     flush.zero_()
-    torch.cuda._sleep(ENQUEUE_COVER_CYCLES)
+    torch.cuda._sleep(cycles)
 
 
 def env_rank():
@@ -849,7 +849,9 @@ def run_proj(args, torch, device):
     clocks = ClockSampler(device.index or 0).start()
     times = []
     for _ in range(args.steps):
-        flush_and_cover(torch, flush)  # weights would otherwise stay in L2 between iterations
+        # weights would otherwise stay in L2 between iterations; the longer spin covers the calls'
+        # host work (tensor maps, workspace set-up, several launches)
+        flush_and_cover(torch, flush, 3 * ENQUEUE_COVER_CYCLES)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
         call()
