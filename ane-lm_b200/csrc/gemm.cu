@@ -668,10 +668,11 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 // for rows [128 mt, 128 mt + 128).  Warp 4: TMA ring (A rows, B vocabulary rows); warp 5: MMAs
 // of each tile into TMEM buffer (i & 1) once the epilogue released it; warps 0-3: per row, the
 // running top-32 over all its tiles (spread over a warp's lanes), then candidate lists
-// [M][G rep][32] (values, then indices).  With M <= 64 (one row tile) the A tile holds rep = 128 / rr
-// copies of the rr-row block (rr = 32 or 64, one TMA box each, tmA's box is rr rows), so every
-// epilogue warp has rows: the warps reading copy cp take columns [cp 256 / rep, (cp + 1) 256 / rep)
-// of each tile and keep their own list (copy cp's list of CTA g is candidate list g rep + cp).
+// [M][G rep][32] (values, then indices).  With rep > 1 (one row tile of at most 128 / rep rows; the
+// launcher takes rep = 4 for 9-24 rows) the A tile holds rep copies of the rr = 128 / rep row block
+// (one TMA box each, tmA's box is rr rows), so every epilogue warp has rows: the warps reading copy
+// cp take columns [cp 256 / rep, (cp + 1) 256 / rep) of each tile and keep their own list (copy cp's
+// list of CTA g is candidate list g rep + cp).
 //
 // Before any list is fed, every CTA publishes each row's largest logit of its first tile (pmax
 // [M][gpitch], slot g; NaN = not yet published, set by the launcher) and waits, at most

@@ -43,9 +43,19 @@ def test_lm_head_top32_qwen_vocab(n):
 
 
 @pytest.mark.parametrize("k", [1, 5, 32])
-@pytest.mark.parametrize("n", [1, 3])
+@pytest.mark.parametrize("n", [1, 3, 17, 40])
 def test_lm_head_ragged_vocab(n, k):
+    """A 1,000-row vocabulary (four 256-column tiles, the last one partial) at hidden 136 (a partial
+    64-wide k-step): the GEMV, swapped and tile kernels; the tile kernel runs four CTAs here, fewer
+    than the 32 groups its first-tile bound needs, so its lists take every logit."""
     _check(n, 1000, 136, k, seed=k + 10 * n)
+
+
+@pytest.mark.parametrize("n", [17, 40])
+def test_lm_head_ragged_vocab_with_bound(n):
+    """34 vocabulary tiles (8,548 rows, the last tile 100 columns): 34 CTAs, enough for the
+    first-tile bound, with a partial tile among them."""
+    _check(n, 33 * 256 + 100, 136, 32, seed=500 + n)
 
 
 @pytest.mark.parametrize("n", [2, 8, 16])
