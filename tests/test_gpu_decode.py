@@ -96,6 +96,35 @@ def test_full_attn_config1_ring(length, start):
     np.testing.assert_array_equal(v, ring.v)
 
 
+@pytest.mark.parametrize("Hq,Hkv,d,cap", [(8, 2, 256, 100), (8, 2, 256, 160), (8, 2, 256, 300),
+                                           (16, 4, 256, 500), (4, 4, 128, 900), (6, 2, 128, 2048),
+                                           (2, 2, 256, 1500)])
+def test_full_attn_one_row_cluster_merge(Hq, Hkv, d, cap):
+    """One-row plans merge their splits inside a thread-block cluster: each split pushes every owner
+    CTA its slice of the G * d / 4 output float4s and its (m, l).  Ring capacities giving 2, 3, 5, 8,
+    15 and 16 splits (the last owner's slice shorter than the others at most of them), G = 4, 1, 3 and
+    1 query heads per kv head, head_dim 256 and 128; full and partly filled rings, against the oracle."""
+    rng = np.random.default_rng(cap + Hq)
+    shape = fa_shape(Hq, Hkv, d, 64, 1e7)
+    T = 3
+    proj, qn, kn = fa_inputs(rng, shape, T)
+    length = cap if cap % 2 == 0 else cap - 7
+    ring = random_ring(rng, cap, Hkv, d, length, cap // 3)
+    rope = po.rope_table(4096, 64, 1e7)
+    with fa_ctx(shape, cap=cap) as ctx:
+        ctx.set_full_attn_weights(0, qn, kn)
+        ctx.kv_import(0, 0, ring.k, ring.v, ring.len, ring.start)
+        p = dev(proj, torch.float16)
+        got = torch.stack([ctx.full_attn_from_proj(0, 0, p[t].contiguous(), 900 + t) for t in range(T)])
+        got = got.cpu().numpy()
+        assert ctx.device_error() == 0
+        k, v, ln, st = ctx.kv_export(0, 0)
+    want = po.full_attn_tokens("oracle", shape, po.make_variant(kv_round_f16=1), qn, kn, ring, proj, 900, rope)
+    assert_close(got, want, what=f"one-row decode, {Hq}/{Hkv} heads, d {d}, ring {cap}")
+    assert (ln, st) == (ring.len, ring.start)
+    np.testing.assert_array_equal(v, ring.v)
+
+
 @pytest.mark.parametrize("Hk,Hv,T", [(16, 16, 64), (16, 32, 24)])
 def test_deltanet_successive_tokens(Hk, Hv, T):
     """Config-2 (16/16 heads) and the 4B GQA shape (32 value / 16 key heads):
