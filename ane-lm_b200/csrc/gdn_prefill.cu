@@ -21,10 +21,10 @@
 // independent, so the sequential part runs one chain per (sequence, value head, 32 state columns).
 //
 // Precision: every tensor-core operand is held as an fp16 hi + lo pair (x = hi + lo to ~2^-22
-// relative) and each product is three mma.sync m16n8k16 (hi*hi + lo*hi + hi*lo) with fp32
-// accumulation, so the products match fp32 arithmetic; plain fp16 operands would let the gated
-// RMSNorm amplify their 2^-12 rounding past the tolerance.  Operands live in memory as a hi
-// plane followed by a lo plane and reach the MMAs through ldmatrix.  When the bare core op gets
+// relative) and each product is three tcgen05 MMAs (hi*hi + lo*hi + hi*lo) with fp32 accumulation
+// in TMEM, so the products match fp32 arithmetic; plain fp16 operands would let the gated RMSNorm
+// amplify their 2^-12 rounding past the tolerance.  Operands live in memory as a hi plane followed
+// by a lo plane and reach shared memory by TMA.  When the bare core op gets
 // 16-bit q / k / v (bf16 values have 8 significant bits, so they are exact in fp16), their lo
 // planes are zero: they are neither written nor loaded, K K^T / Q K^T take one term, and the
 // products with K, Q or V on one side take two.
@@ -37,9 +37,10 @@
 //   gdn_pf_pack_kernel      (core op only) token-major q, k, v, log g, beta -> chunk layout
 //   gdn_pf_chunk_kernel     per (chunk, value head): K K^T, Q K^T, T by forward substitution,
 //                           W, U, M
-//   gdn_pf_chain_kernel     per (sequence, value head, 32 columns): the chunk recurrence over
-//                           the state block; each operand buffer is refilled with the next
-//                           chunk's data (cp.async) as soon as this chunk's last reader is done
+//   gdn_pf_chain_tc_kernel  per (sequence, value head, 32 columns): the chunk recurrence over
+//                           the state block on tcgen05, warp-specialised; each operand buffer is
+//                           refilled with the next chunk's data (TMA) as soon as this chunk's
+//                           last reader is done
 //   gdn_pf_out_kernel       gated RMSNorm of y with z (layer path)
 #include <math.h>
 
@@ -54,37 +55,14 @@ namespace {
 constexpr int kC = 64;     // chunk length
 constexpr int kDk = 128;   // key head dim of these kernels
 constexpr int kDv = 128;   // value head dim
-constexpr int kDvb = 32;   // state columns per chain CTA
+constexpr int kUBox = 32;  // fp32 columns of one U tile box (128 bytes)
 
-// ---------------------------------------------------------------- fragments (mma.sync m16n8k16)
+// ---------------------------------------------------------------- hi / lo operand planes
 
 __device__ __forceinline__ void split_store(__half* hi, __half* lo, float x) {
     const __half h = __float2half_rn(x);
     *hi = h;
     *lo = __float2half_rn(x - __half2float(h));
-}
-
-// B (16 x 8) fragments of two n-tiles n0, n0 + 8 at k0 (ldmatrix), with B[k][n] = T[n][k] (ldb2_sw)
-// or B[k][n] = T[k][n] (ldb2_t_sw) for a tile T in shared memory.
-// Tiles are in the TMA's 128B-swizzled layout of 64-column boxes: element (row, col) of a tile at shared
-// address `tile` lives in box col / 64, 8192 bytes per box of 64 rows.
-__device__ __forceinline__ uint32_t sw_addr(uint32_t tile, int row, int col) {
-    return tile + (uint32_t)((col >> 6) * 8192 + row * 128 + ((((col & 63) >> 3) ^ row) & 7) * 16 + (col & 7) * 2);
-}
-__device__ __forceinline__ void ldb2_sw(uint32_t (&b)[4], uint32_t tile, int n0, int k0, int lane) {
-    const int mat = lane >> 3, i = lane & 7;
-    ldmatrix_x4(sw_addr(tile, n0 + i + (mat >> 1) * 8, k0 + (mat & 1) * 8), b[0], b[1], b[2], b[3]);
-}
-__device__ __forceinline__ void ldb2_t_sw(uint32_t (&b)[4], uint32_t tile, int n0, int k0, int lane) {
-    const int mat = lane >> 3, i = lane & 7;
-    ldmatrix_x4_trans(sw_addr(tile, k0 + i + (mat & 1) * 8, n0 + (mat >> 1) * 8), b[0], b[1], b[2], b[3]);
-}
-// Named barrier over `count` threads (a multiple of 32) of this CTA: wait, or arrive without waiting.
-__device__ __forceinline__ void named_bar_sync_cta(uint32_t id, uint32_t count) {
-    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
-}
-__device__ __forceinline__ void named_bar_arrive_cta(uint32_t id, uint32_t count) {
-    asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---------------------------------------------------------------- snapshot
@@ -563,40 +541,7 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
     }
 }
 
-// ---------------------------------------------------------------- the recurrence over chunks
-
-// One chain CTA per (sequence, value head, 32 state columns j0 .. j0 + 32), eight warps.  State warp
-// w < 4, (jg, dh) = (w / 2, w % 2), keeps S^T rows j0 + 16 jg .. + 16 (state columns) times key dims
-// d in [64 dh, 64 dh + 64) in registers, in the accumulator layout of mma.m16n8k16, which is also
-// the A-operand layout: S^T feeds W S directly (as hi / lo pairs), and the state update
-// S^T += E^T K accumulates into the same registers.  The two state warps of a column group hold the
-// two halves of d, so their partial W S sums meet in shared memory.  Output warp 4 + w computes,
-// beside state warp w, Q S over the same d half from the state warp's S^T fragments (handed over
-// in shared memory) and then Y = e^lc Q S + M D for 32 rows t from the group's D fragments, so
-// only W S, D and the state update are on the recurrence's critical path.  Per chunk:
-//   state:  S^T fragments -> W S -> exchange -> D = U - W S -> D fragments -> S = e^{lc_C} S + K^T E
-//   output:                  Q S -> exchange ->                 e^lc Q S + M D -> Y
-constexpr int kChainThreads = 256;
-struct ChainSmem {
-    // operand tiles in the TMA's 128B-swizzled layout (1024-byte aligned): [plane][box][64 rows][128 B]
-    uint8_t w[2][2][8192];             // W[t][d], d in boxes of 64
-    uint8_t q[2][2][8192];             // Q[t][d]
-    uint8_t k[2][2][8192];             // K[t][d]
-    uint8_t m[2][8192];                // M[t][i]
-    uint8_t u[8192];                   // U[t][j0 .. j0 + 32] fp32, 128-byte rows
-    float lc[2][kC];                   // in-chunk cumulative log decay, by chunk parity
-    float eg[kC], ef[kC];              // e^{lc_t}, e^{lc_C - lc_t} of the current chunk
-    float xd[4][32][32];               // partial W S of each state warp, [warp][register][lane]
-    float xy[4][32][32];               // partial Q S of each output warp
-    uint32_t sa[4][4][8][32];          // S^T fragments of each state warp: [warp][k-step][hi 0-3, lo 0-3][lane]
-    uint32_t sdf[2][4][8][32];         // D fragments of each column group: [jg][k-step][8][lane]
-    uint64_t bar[3];                   // W+Q, U+lc, M+K of the chunk landed (one phase per chunk)
-    int abort;
-};
-// U[t][j] (fp32, j < 32) in its 128B-swizzled tile
-__device__ __forceinline__ float u_at(const ChainSmem& sm, int t, int j) {
-    return *reinterpret_cast<const float*>(&sm.u[t * 128 + ((((j >> 2) ^ t) & 7) << 4) + (j & 3) * 4]);
-}
+// ---------------------------------------------------------------- the recurrence on tcgen05
 
 __device__ __forceinline__ uint32_t h2u(const __half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
 // x0, x1 as an fp16 hi pair and the fp16 pair of the remainders
@@ -606,295 +551,421 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_
     hi = h2u(h);
     lo = h2u(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
 }
-// A fragments (hi / lo) of k-step ks from accumulator tiles acc[2 ks] (k 0-7) and acc[2 ks + 1]
-// (k 8-15), each column scaled by sc (sc[nt][0 / 1]: columns 8 nt + 2 c, + 1)
-template <int NT>
-__device__ __forceinline__ void afrag(const float (&acc)[NT][4], const float (&sc)[NT][2], int ks, uint32_t (&ah)[4],
-                                      uint32_t (&al)[4]) {
-    const int t0 = 2 * ks, t1 = 2 * ks + 1;
-    split2(acc[t0][0] * sc[t0][0], acc[t0][1] * sc[t0][1], ah[0], al[0]);
-    split2(acc[t0][2] * sc[t0][0], acc[t0][3] * sc[t0][1], ah[1], al[1]);
-    split2(acc[t1][0] * sc[t1][0], acc[t1][1] * sc[t1][1], ah[2], al[2]);
-    split2(acc[t1][2] * sc[t1][0], acc[t1][3] * sc[t1][1], ah[3], al[3]);
-}
-template <int NT>
-__device__ __forceinline__ void afrag(const float (&acc)[NT][4], int ks, uint32_t (&ah)[4], uint32_t (&al)[4]) {
-    const int t0 = 2 * ks, t1 = 2 * ks + 1;
-    split2(acc[t0][0], acc[t0][1], ah[0], al[0]);
-    split2(acc[t0][2], acc[t0][3], ah[1], al[1]);
-    split2(acc[t1][0], acc[t1][1], ah[2], al[2]);
-    split2(acc[t1][2], acc[t1][3], ah[3], al[3]);
-}
-// acc[2 np], acc[2 np + 1] += A B over NP n-tile pairs (fragments bh[np], bl[np]), issued term by
-// term across all 2 NP accumulators so dependent MMAs are 2 NP instructions apart
-template <int NP>
-__device__ __forceinline__ void mma3_tm(float (*acc)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
-                                        const uint32_t (&bh)[NP][4], const uint32_t (&bl)[NP][4], bool b_lo = true) {
-#pragma unroll
-    for (int np = 0; np < NP; np++) {
-        mma_16816(acc[2 * np], ah[0], ah[1], ah[2], ah[3], bh[np][0], bh[np][1]);
-        mma_16816(acc[2 * np + 1], ah[0], ah[1], ah[2], ah[3], bh[np][2], bh[np][3]);
-    }
-#pragma unroll
-    for (int np = 0; np < NP; np++) {
-        mma_16816(acc[2 * np], al[0], al[1], al[2], al[3], bh[np][0], bh[np][1]);
-        mma_16816(acc[2 * np + 1], al[0], al[1], al[2], al[3], bh[np][2], bh[np][3]);
-    }
-    if (!b_lo) return;  // B exact in fp16 (its lo plane is zero)
-#pragma unroll
-    for (int np = 0; np < NP; np++) {
-        mma_16816(acc[2 * np], ah[0], ah[1], ah[2], ah[3], bl[np][0], bl[np][1]);
-        mma_16816(acc[2 * np + 1], ah[0], ah[1], ah[2], ah[3], bl[np][2], bl[np][3]);
-    }
-}
-
-// A chunk's operand tiles are fetched by one thread as TMA tile copies (64 rows x 128 bytes, 128B
-// swizzle; the fragment loads undo the swizzle), completing on one mbarrier per group.
+// A chunk's operand tiles, fetched by TMA tile copies (64 rows x 128 bytes, 128B swizzle): W, Q, K
+// and M hi / lo planes, U (fp32, 32-column boxes)
 struct ChainMaps {
     CUtensorMap w, q, k, m, u;
 };
-// W and Q, hi and lo planes (read by W S and Q S)
-__device__ __forceinline__ void chain_load_wq(ChainSmem& sm, const ChainMaps& mp, long long krow, long long vrow,
-                                              bool exact) {
-    tc::mbar_arrive_expect_tx(&sm.bar[0], (exact ? 3 : 4) * 2 * 8192);  // exact: no Q lo plane
-    for (int pl = 0; pl < 2; pl++)
-        for (int bx = 0; bx < 2; bx++) {
-            tc::tma_load_3d(sm.w[pl][bx], &mp.w, &sm.bar[0], 64 * bx, (int)vrow, pl);
-            if (pl == 0 || !exact) tc::tma_load_3d(sm.q[pl][bx], &mp.q, &sm.bar[0], 64 * bx, (int)krow, pl);
-        }
+
+// One CTA per (sequence, value head, NB state columns); the three products of a chunk step run on
+// the tensor core with fp32 accumulators in TMEM (hi / lo operand planes, three MMAs per product as
+// above, two where one side is an exact 16-bit input):
+//   A:  [Q; W] S        M 128 (64 Q rows over 64 W rows), N NB, K 128   -> Q S and W S
+//   C:  K^T (Gamma D)   M 128 (key dims), N NB, K 64 (tokens)            -> the state update
+//   B:  M D             M 128 (64 M rows, 64 zero rows), N NB, K 64      -> the intra-chunk output
+// with D = U - W S and Gamma = diag(e^{lc_C - lc}).  Warp roles (a warp reads the TMEM lanes of its
+// index mod 4, 32 each):
+//   0-7         state: thread (lane quadrant q, half hf) holds S[32 q + lane][NB/2 hf .. + NB/2] in
+//               registers and, once C is done, applies S = e^{lc_C} S + K^T Gamma D and writes its
+//               part of the next S operand;
+//   10, 11, 14, 15  D = U - W S and Gamma D from the W S rows (lanes 64-127), NB/2 columns each;
+//   8, 9        Y = e^{lc} Q S + M D from lanes 0-63, stored to global;
+//   12          issues the MMAs; 13: issues the TMA loads of the next chunk as soon as the tensor
+//               core or the D warps are done with a buffer (both run converged and elect one lane
+//               for each tcgen05 / TMA instruction).
+// A step's critical path is A -> D -> C -> S; B is issued after C and runs while the state warps
+// work, and the outputs follow it (the A / B accumulators and D are double-buffered, so the output
+// warps may lag a step).  Every hand-over is an mbarrier (thread arrivals or tcgen05.commit), every
+// wait bounded.  A traced step spends about as long in the epilogues as in the MMAs
+// (~47 cycles per M=128 MMA issued, for N = 32 or 64), so narrow column blocks on many SMs pay:
+// NB 32 gives 4 x 32 x B CTAs.
+constexpr int kChainTcThreads = 512;
+template <int NB>
+struct ChainTcSmem {
+    static constexpr int kRowB = NB * 2;  // bytes of one fp16 row of an N = NB operand
+    uint8_t qw[2][32768];          // [Q; W] hi, lo: per key-dim box of 64 (16 KB) 64 Q rows, then 64 W rows
+    uint8_t m[2][16384];           // M hi, lo as a 128-row K-major A: rows 64-127 stay zero
+    uint8_t k[2][16384];           // K[t][d] hi, lo: two 8 KB key-dim boxes (MN-major A of the update)
+    uint8_t s[2][kDk * kRowB];     // S[d][j] hi, lo: swizzled rows of NB fp16 (MN-major B)
+    uint8_t d[2][2][kC * kRowB];   // D[t][j] hi, lo (MN-major B of M D), by chunk parity
+    uint8_t gd[2][kC * kRowB];     // (Gamma D)[t][j] hi, lo (MN-major B of the update)
+    uint8_t u[kC * NB * 4];        // U[t][j0 .. j0 + NB] fp32 in 32-column 128B-swizzled boxes
+    float lc[4][kC];               // in-chunk cumulative log decay, ring by chunk index
+    // one phase per chunk each: 0 S written (256 arrivals) and [Q; W] landed, 1 A done and U + lc
+    // landed, 2 D written (128 arrivals) and K landed, 3 C done, 4-5 B done (by accumulator buffer),
+    // 6-7 Y read (by buffer, 64 arrivals), 8 all MMAs done, 9 M landed
+    uint64_t bar[10];
+    uint32_t tmem_slot;
+    int abort;
+};
+
+// hi / lo fp16 planes of 8 consecutive values as two 16-byte words
+__device__ __forceinline__ void split8(const float (&v)[8], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) split2(v[2 * i], v[2 * i + 1], h[i], l[i]);
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
-// this block's U columns and lc (read by D = U - W S and the decay factors)
-__device__ __forceinline__ void chain_load_u(ChainSmem& sm, const ChainMaps& mp, const GdnPrefillParams& p,
-                                             long long vrow, int j0, int par) {
-    tc::mbar_arrive_expect_tx(&sm.bar[1], 8192 + kC * 4);
-    tc::tma_load_2d(sm.u, &mp.u, &sm.bar[1], j0, (int)vrow);
-    tc::bulk_load(sm.lc[par], p.lcb + vrow, kC * 4, &sm.bar[1]);
+// Operands with rows of NB fp16 (K index = row, N = column, N contiguous): 128-byte rows with the
+// 128-byte swizzle (NB 64: 16-byte word c of row r at ((c ^ r) & 7)) or 64-byte rows with the
+// 64-byte swizzle (NB 32: word c at ((c ^ (r >> 1)) & 3)); 8-row groups of 8 NB * 2 bytes.
+template <int NB>
+__device__ __forceinline__ uint32_t nb_word(int r, int c) {
+    if (NB == 64) return (uint32_t)(r * 128 + (((c ^ r) & 7) << 4));
+    return (uint32_t)(r * 64 + (((c ^ (r >> 1)) & 3) << 4));
 }
-// K and M, hi and lo planes (read by the state update and M D)
-__device__ __forceinline__ void chain_load_mk(ChainSmem& sm, const ChainMaps& mp, long long krow, long long vrow,
-                                              bool exact) {
-    tc::mbar_arrive_expect_tx(&sm.bar[2], (exact ? 1 : 2) * 2 * 8192 + 2 * 8192);  // exact: no K lo plane
-    for (int pl = 0; pl < 2; pl++) {
-        if (pl == 0 || !exact)
-            for (int bx = 0; bx < 2; bx++) tc::tma_load_3d(sm.k[pl][bx], &mp.k, &sm.bar[2], 64 * bx, (int)krow, pl);
-        tc::tma_load_3d(sm.m[pl], &mp.m, &sm.bar[2], 0, (int)vrow, pl);
+// MN-major operand descriptor of such a tile (one N atom, so the leading offset is unused)
+template <int NB>
+__device__ __forceinline__ uint64_t nb_desc(uint32_t smem_addr) {
+    uint64_t d = (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;                           // LBO (unused: one atom along N)
+    d |= (uint64_t)((8 * NB * 2) >> 4) << 32;         // SBO: 8 rows
+    d |= (uint64_t)1 << 46;                           // descriptor version (sm100)
+    d |= (uint64_t)(NB == 64 ? 2 : 4) << 61;          // SWIZZLE_128B / SWIZZLE_64B
+    return d;
+}
+// 16 consecutive fp32 columns of U[t][..] from its 32-column 128B-swizzled boxes
+__device__ __forceinline__ void u_row16(const uint8_t* u, int t, int j, float (&x)[16]) {
+    const uint8_t* row = u + (j >> 5) * 8192 + t * 128;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const float4 v = *reinterpret_cast<const float4*>(row + ((((((j & 31) >> 2) + q) ^ t) & 7) << 4));
+        x[4 * q] = v.x;
+        x[4 * q + 1] = v.y;
+        x[4 * q + 2] = v.z;
+        x[4 * q + 3] = v.w;
     }
 }
 
-__global__ void __launch_bounds__(kChainThreads, 1) gdn_pf_chain_kernel(const __grid_constant__ ChainMaps mp,
-                                                                        const GdnPrefillParams p) {
+template <int NB>
+__global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(const __grid_constant__ ChainMaps mp,
+                                                                             const GdnPrefillParams p) {
+    static_assert(NB == 32 || NB == 64, "operand rows of 64 or 128 bytes");
     extern __shared__ uint8_t smem_raw[];
-    ChainSmem& sm = *reinterpret_cast<ChainSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int nblk = kDv / kDvb;
-    const int h = blockIdx.x / nblk, j0 = (blockIdx.x % nblk) * kDvb, b = blockIdx.y;
+    using Smem = ChainTcSmem<NB>;
+    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int nblk = kDv / NB;
+    constexpr int kRowB = Smem::kRowB, kSPlane = kDk * kRowB, kDPlane = kC * kRowB;
+    constexpr int kHalf = NB / 2;               // columns per state / D thread
+    constexpr uint32_t kTmemCols = NB == 64 ? 512 : 256;
+    const int h = blockIdx.x / nblk, j0 = (blockIdx.x % nblk) * NB, b = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, c = lane & 3;
-    const bool state = warp < 4;
-    const int w4 = warp & 3, jg = w4 >> 1, dh = w4 & 1;
-    const int jr = 16 * jg;      // this warp's state columns j0 + jr .. + 16
-    const int dbase = 64 * dh;   // and key dims dbase .. + 64
     const int kh = h / (p.Hv / p.Hk);
     const int seq = p.seq_ids ? p.seq_ids[b] : b;
     float* S = p.state + ((long long)seq * p.Hv + h) * kDk * kDv;
-    // state warps: s[nt][e] = S[d][j0 + j], j = jr + g + 8 (e / 2), d = dbase + 8 nt + 2 c + (e % 2)
-    float s[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-        for (int e = 0; e < 4; e++)
-            s[nt][e] = state ? S[(long long)(dbase + 8 * nt + 2 * c + (e & 1)) * kDv + j0 + jr + g + 8 * (e >> 1)] : 0.f;
     const int nC = p.T_pad / kC;
-    const long long krow0 = ((long long)b * p.Hk + kh) * p.T_pad;
-    const long long vrow0 = ((long long)b * p.Hv + h) * p.T_pad;
-    // the loads of chunk ci complete phase ci of bar[0] (W, Q), bar[1] (U, lc), bar[2] (M, K); output
-    // warps 4, 5, 6 issue them once the previous chunk's readers are done
+    const int krow0 = (int)(((long long)b * p.Hk + kh) * p.T_pad);
+    const int vrow0 = (int)(((long long)b * p.Hv + h) * p.T_pad);
+    const bool exact = p.qkv_exact != 0;
+    uint64_t* bar = sm.bar;
+    volatile int* abort = &sm.abort;
     if (tid == 0) {
-        for (int i = 0; i < 3; i++) tc::mbar_init(&sm.bar[i], 1);
         sm.abort = 0;
+        const uint32_t count[10] = {257, 2, 129, 1, 1, 1, 64, 64, 1, 1};
+        for (int i = 0; i < 10; i++) tc::mbar_init(&bar[i], count[i]);
         tc::fence_barrier_init();
     }
-    __syncthreads();
-    volatile int* abort = &sm.abort;
-    const bool loader = tid == 4 * 32;  // lane 0 of output warp 4 issues every copy
-    const bool exact = p.qkv_exact != 0;  // Q and K exact in fp16: their lo planes are neither loaded nor used
-    if (loader) {
-        chain_load_wq(sm, mp, krow0, vrow0, exact);
-        chain_load_u(sm, mp, p, vrow0, j0, 0);
-        chain_load_mk(sm, mp, krow0, vrow0, exact);
+    {  // zero rows of the A tiles that no load fills: M rows 64-127 and, for exact inputs, the Q lo rows
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        for (int i = tid; i < 2 * 512; i += kChainTcThreads)
+            *reinterpret_cast<uint4*>(&sm.m[i >> 9][8192 + (i & 511) * 16]) = z;
+        if (exact)
+            for (int i = tid; i < 2 * 512; i += kChainTcThreads)
+                *reinterpret_cast<uint4*>(&sm.qw[1][(i >> 9) * 16384 + (i & 511) * 16]) = z;
     }
-    const uint32_t a_w = smem_u32(sm.w), a_q = smem_u32(sm.q), a_k = smem_u32(sm.k), a_m = smem_u32(sm.m);
-    // named barriers: 1 + jg state pair, 3 + jg output pair (64 threads); 5 + jg S^T fragments and
-    // 7 + jg D fragments, state warps arrive, output warps wait (128 threads)
-    for (int ci = 0; ci < nC; ci++) {
-        const int par = ci & 1;
-        const bool more = ci + 1 < nC;
-        tc::mbar_wait(&sm.bar[0], par, p.err, ANELM_ERR_TIMEOUT, abort);
-        __syncthreads();  // W and Q of this chunk are in shared memory
-        // ---- W S (state warps) and Q S (output warps) over this warp's half of d, all 64 rows t ----
-        float acc[8][4];
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) acc[nt][e] = 0.f;
-        {
-            const uint32_t bhi = state ? a_w : a_q, blo = bhi + 16384;
-            uint32_t fa[4][4], fl[4][4];
-            if (state) {
-#pragma unroll
-                for (int ks = 0; ks < 4; ks++) {
-                    afrag(s, ks, fa[ks], fl[ks]);
-#pragma unroll
-                    for (int r = 0; r < 4; r++) {
-                        sm.sa[w4][ks][r][lane] = fa[ks][r];
-                        sm.sa[w4][ks][4 + r][lane] = fl[ks][r];
+    if (warp == 12) {
+        tc::tmem_alloc(&sm.tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_proxy_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = sm.tmem_slot;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    // TMEM columns: A accumulators [0, 2 NB) by buffer, B accumulators [2 NB, 4 NB), C at 4 NB
+    constexpr uint32_t kColB = 2 * NB, kColC = 4 * NB;
+    static_assert(5 * NB <= kTmemCols, "TMEM columns");
+    auto wait = [&](int i, uint32_t parity) { return tc::mbar_wait(&bar[i], parity, p.err, ANELM_ERR_TIMEOUT, abort); };
+    // the same for a converged warp: lane 0 polls, every lane gets its answer
+    auto wait_w = [&](int i, uint32_t parity) {
+        int ok = 1;
+        if (lane == 0) ok = wait(i, parity);
+        return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    };
+
+    if (warp == 13) {
+        // ---------------------------------------------------------------- TMA loads
+        int loaded[4] = {0, 0, 0, 0};  // chunks whose loads are issued on bars 0-2 and 9 (one phase each)
+        auto load_qw = [&](int ci) {
+            if (tc::elect_one()) {
+                tc::mbar_arrive_expect_tx(&bar[0], (exact ? 3 : 4) * 2 * 8192);
+                for (int pl = 0; pl < 2; pl++)
+                    for (int kb = 0; kb < 2; kb++) {
+                        tc::tma_load_3d(&sm.qw[pl][kb * 16384 + 8192], &mp.w, &bar[0], 64 * kb, vrow0 + ci * kC, pl);
+                        if (pl == 0 || !exact)
+                            tc::tma_load_3d(&sm.qw[pl][kb * 16384], &mp.q, &bar[0], 64 * kb, krow0 + ci * kC, pl);
                     }
-                }
-                named_bar_arrive_cta(5 + jg, 128);
-            } else {
-                named_bar_sync_cta(5 + jg, 128);
+            }
+            loaded[0] = ci + 1;
+        };
+        auto load_u = [&](int ci) {
+            if (tc::elect_one()) {
+                tc::mbar_arrive_expect_tx(&bar[1], kC * NB * 4 + kC * 4);
+                for (int c32 = 0; c32 < NB / 32; c32++)
+                    tc::tma_load_2d(&sm.u[c32 * 8192], &mp.u, &bar[1], j0 + 32 * c32, vrow0 + ci * kC);
+                tc::bulk_load(sm.lc[ci & 3], p.lcb + vrow0 + (long long)ci * kC, kC * 4, &bar[1]);
+            }
+            loaded[1] = ci + 1;
+        };
+        auto load_k = [&](int ci) {
+            if (tc::elect_one()) {
+                tc::mbar_arrive_expect_tx(&bar[2], (exact ? 1 : 2) * 2 * 8192);
+                for (int pl = 0; pl < (exact ? 1 : 2); pl++)
+                    for (int kb = 0; kb < 2; kb++)
+                        tc::tma_load_3d(&sm.k[pl][kb * 8192], &mp.k, &bar[2], 64 * kb, krow0 + ci * kC, pl);
+            }
+            loaded[2] = ci + 1;
+        };
+        auto load_m = [&](int ci) {
+            if (tc::elect_one()) {
+                tc::mbar_arrive_expect_tx(&bar[9], 2 * 8192);
+                for (int pl = 0; pl < 2; pl++) tc::tma_load_3d(&sm.m[pl][0], &mp.m, &bar[9], 0, vrow0 + ci * kC, pl);
+            }
+            loaded[3] = ci + 1;
+        };
+        if (nC > 0) {
+            if (tc::elect_one()) {
+                tc::prefetch_tmap(&mp.w);
+                tc::prefetch_tmap(&mp.q);
+                tc::prefetch_tmap(&mp.k);
+                tc::prefetch_tmap(&mp.m);
+                tc::prefetch_tmap(&mp.u);
+            }
+            load_qw(0);
+            load_u(0);
+            load_k(0);
+            load_m(0);
+            // each buffer is refilled once its readers of chunk ci are done; none of these barriers can
+            // run a phase ahead of this warp, since their next phase needs the load issued here
+            for (int ci = 0; ci + 1 < nC; ci++) {
+                if (!wait_w(1, ci & 1)) break;  // A read [Q; W]
+                load_qw(ci + 1);
+                if (!wait_w(2, ci & 1)) break;  // the D warps read U and lc
+                load_u(ci + 1);
+                if (!wait_w(3, ci & 1)) break;  // C read K
+                load_k(ci + 1);
+                if (!wait_w(4 + (ci & 1), (ci >> 1) & 1)) break;  // B read M
+                load_m(ci + 1);
+            }
+            // nothing may still be in flight when the CTA leaves; a load is issued only once the
+            // previous phase of its barrier has completed, so waiting for the parity of the last one
+            // is exact (after an abort the phase may never complete: the wait is bounded)
+            if (lane == 0)
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    for (uint32_t n = 0; n < tc::kWaitPolls && !tc::mbar_try_wait(&bar[i < 3 ? i : 9], (loaded[i] - 1) & 1);
+                         n++) {
+                    }
+        }
+        __syncwarp();
+    } else if (warp == 12) {
+        // ---------------------------------------------------------------- MMAs
+        constexpr uint32_t idA = tc::idesc_f16_f32_bmn(128, NB);
+        constexpr uint32_t idC = tc::idesc_f16_f32_bmn(128, NB) | (1u << 15);  // A (K^T) MN-major too
+        // descriptors of the tiles' first bytes; later k-steps add their byte offset >> 4 to the
+        // start-address field (shared-memory addresses stay below 2^18, so it never carries out)
+        const uint64_t dqw = tc::desc_kmajor_sw128(smem_u32(sm.qw)), dm = tc::desc_kmajor_sw128(smem_u32(sm.m));
+        const uint64_t dk = tc::desc_sw128(smem_u32(sm.k), 8192, 1024);
+        const uint64_t ds = nb_desc<NB>(smem_u32(sm.s)), dd = nb_desc<NB>(smem_u32(sm.d));
+        const uint64_t dgd = nb_desc<NB>(smem_u32(sm.gd));
+        // B of chunk c: M D -> columns [2 NB + NB (c & 1), ...), D from its parity buffer
+        auto issue_b = [&](int c) {
+            const uint32_t cb = c & 1;
+            if (!wait_w(9, c & 1)) return false;  // M of chunk c landed
+            tc::tc_fence_after();
+#pragma unroll
+            for (int term = 0; term < 3; term++)
 #pragma unroll
                 for (int ks = 0; ks < 4; ks++)
+                    if (tc::elect_one())
+                        tc::mma_f16_ss(tmem + kColB + NB * cb, dm + (((term == 1 ? 16384 : 0) + ks * 32) >> 4),
+                                       dd + ((cb * 2 * kDPlane + (term == 2 ? kDPlane : 0) + ks * 16 * kRowB) >> 4), idA,
+                                       (term | ks) != 0);
+            if (tc::elect_one()) tc::mma_commit(&bar[4 + cb]);
+            return true;
+        };
+        for (int ci = 0; ci < nC; ci++) {
+            const uint32_t ph = ci & 1, bb = ci & 1;
+            if (!wait_w(0, ph)) break;  // S of this step written, [Q; W] landed
+            if (ci >= 2 && !wait_w(6 + bb, ((ci >> 1) + 1) & 1)) break;  // outputs of step ci - 2 read
+            tc::tc_fence_after();
+            // A: [Q; W] S -> columns [NB bb, NB bb + NB)
 #pragma unroll
-                    for (int r = 0; r < 4; r++) {
-                        fa[ks][r] = sm.sa[w4][ks][r][lane];
-                        fl[ks][r] = sm.sa[w4][ks][4 + r][lane];
+            for (int term = 0; term < 3; term++)
+#pragma unroll
+                for (int kb = 0; kb < 2; kb++)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ks++)
+                        if (tc::elect_one())
+                            tc::mma_f16_ss(tmem + NB * bb, dqw + (((term == 1 ? 32768 : 0) + kb * 16384 + ks * 32) >> 4),
+                                           ds + (((term == 2 ? kSPlane : 0) + (kb * 4 + ks) * 16 * kRowB) >> 4), idA,
+                                           (term | kb | ks) != 0);
+            if (tc::elect_one()) tc::mma_commit(&bar[1]);
+            if (!wait_w(2, ph)) break;  // D, Gamma D written; K landed
+            tc::tc_fence_after();
+            // C: K^T (Gamma D) -> columns [4 NB, 5 NB)
+#pragma unroll
+            for (int term = 0; term < 3; term++) {
+                if (term == 2 && exact) break;  // K exact: no K lo plane
+#pragma unroll
+                for (int ks = 0; ks < 4; ks++)
+                    if (tc::elect_one())
+                        tc::mma_f16_ss(tmem + kColC, dk + (((term == 2 ? 16384 : 0) + ks * 2048) >> 4),
+                                       dgd + (((term == 1 ? kDPlane : 0) + ks * 16 * kRowB) >> 4), idC, (term | ks) != 0);
+            }
+            if (tc::elect_one()) tc::mma_commit(&bar[3]);
+            if (!issue_b(ci)) break;  // overlaps the state warps' epilogue
+        }
+        // one commit tracks every MMA issued above: none may run once TMEM is released
+        if (tc::elect_one()) tc::mma_commit(&bar[8]);
+        if (lane == 0)
+            for (uint32_t n = 0; n < tc::kWaitPolls && !tc::mbar_try_wait(&bar[8], 0); n++) {
+            }
+        __syncwarp();
+    } else if (warp < 8) {
+        // ---------------------------------------------------------------- state: S[i][j0 + kHalf hf ..]
+        const int i = 32 * (warp & 3) + lane, hf = warp >> 2;
+        float s[kHalf];
+        const float4* src = reinterpret_cast<const float4*>(S + (long long)i * kDv + j0 + kHalf * hf);
+#pragma unroll
+        for (int c4 = 0; c4 < kHalf / 4; c4++) {
+            const float4 v = src[c4];
+            s[4 * c4] = v.x;
+            s[4 * c4 + 1] = v.y;
+            s[4 * c4 + 2] = v.z;
+            s[4 * c4 + 3] = v.w;
+        }
+        auto write_s = [&]() {  // row i, this thread's columns of the S operand, hi / lo
+#pragma unroll
+            for (int c = 0; c < kHalf / 8; c++) {
+                float v[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[e] = s[8 * c + e];
+                uint4 hi, lo;
+                split8(v, hi, lo);
+                const uint32_t o = nb_word<NB>(i, hf * (kHalf / 8) + c);
+                *reinterpret_cast<uint4*>(&sm.s[0][o]) = hi;
+                *reinterpret_cast<uint4*>(&sm.s[1][o]) = lo;
+            }
+            tc::fence_proxy_async_smem();
+            tc::mbar_arrive(&bar[0]);
+        };
+        if (nC > 0) write_s();
+        for (int ci = 0; ci < nC; ci++) {
+            if (!wait(3, ci & 1)) break;
+            tc::tc_fence_after();
+            const float gC = expf(sm.lc[ci & 3][kC - 1]);
+#pragma unroll
+            for (int q = 0; q < kHalf / 16; q++) {
+                uint32_t x[16];
+                tc::tmem_ld16(tmem + lane_base + kColC + kHalf * hf + 16 * q, x);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; j++) s[16 * q + j] = fmaf(gC, s[16 * q + j], __uint_as_float(x[j]));
+            }
+            tc::tc_fence_before();
+            if (ci + 1 < nC) write_s();
+        }
+        float4* dst = reinterpret_cast<float4*>(S + (long long)i * kDv + j0 + kHalf * hf);
+#pragma unroll
+        for (int c4 = 0; c4 < kHalf / 4; c4++)
+            dst[c4] = make_float4(s[4 * c4], s[4 * c4 + 1], s[4 * c4 + 2], s[4 * c4 + 3]);
+    } else if ((warp & 3) >= 2) {
+        // ---------------------------------------------------------------- D = U - W S, Gamma D
+        const int t = 32 * ((warp & 3) - 2) + lane;  // token row of the chunk; TMEM lane 64 + t
+        const int hf = warp >= 14;                    // columns kHalf hf .. + kHalf
+        for (int ci = 0; ci < nC; ci++) {
+            const uint32_t bb = ci & 1;
+            if (!wait(1, ci & 1)) break;  // A done, U and lc landed
+            tc::tc_fence_after();
+            const float* lc = sm.lc[ci & 3];
+            const float gam = expf(lc[kC - 1] - lc[t]);
+#pragma unroll
+            for (int q = 0; q < kHalf / 16; q++) {
+                uint32_t x[16];
+                tc::tmem_ld16(tmem + lane_base + NB * bb + kHalf * hf + 16 * q, x);
+                float u[16];
+                u_row16(sm.u, t, kHalf * hf + 16 * q, u);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    float v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] = u[8 * c + e] - __uint_as_float(x[8 * c + e]);
+                    uint4 hi, lo;
+                    split8(v, hi, lo);
+                    const uint32_t o = nb_word<NB>(t, (kHalf * hf + 16 * q) / 8 + c);
+                    *reinterpret_cast<uint4*>(&sm.d[bb][0][o]) = hi;
+                    *reinterpret_cast<uint4*>(&sm.d[bb][1][o]) = lo;
+#pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] *= gam;
+                    split8(v, hi, lo);
+                    *reinterpret_cast<uint4*>(&sm.gd[0][o]) = hi;
+                    *reinterpret_cast<uint4*>(&sm.gd[1][o]) = lo;
+                }
+            }
+            tc::fence_proxy_async_smem();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bar[2]);
+        }
+    } else {
+        // ---------------------------------------------------------------- Y = e^{lc} Q S + M D
+        const int t = 32 * (warp & 3) + lane;  // token row of the chunk; TMEM lane t
+        const bool vec = p.y_vec != 0;
+        for (int ci = 0; ci < nC; ci++) {
+            const uint32_t bb = ci & 1;
+            if (!wait(4 + bb, (ci >> 1) & 1)) break;
+            tc::tc_fence_after();
+            const float eg = expf(sm.lc[ci & 3][t]);
+            const int tok = ci * kC + t;
+            const long long o = ((long long)b * p.n + tok) * p.y_stride + (long long)h * kDv + j0;
+#pragma unroll
+            for (int q = 0; q < NB / 16; q++) {  // 16 columns at a time
+                uint32_t qs[16], md[16];
+                tc::tmem_ld16(tmem + lane_base + NB * bb + 16 * q, qs);
+                tc::tmem_ld16(tmem + lane_base + kColB + NB * bb + 16 * q, md);
+                tc::tmem_ld_wait();
+                if (tok >= p.n) continue;
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    float v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] = fmaf(eg, __uint_as_float(qs[8 * c + e]), __uint_as_float(md[8 * c + e]));
+                    const long long oc = o + 16 * q + 8 * c;
+                    if (!vec) {
+#pragma unroll
+                        for (int e = 0; e < 8; e++) store_from_float(p.y, p.y_dtype, oc + e, v[e]);
+                    } else if (p.y_dtype == ANELM_F32) {
+                        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + oc);
+                        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+                        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+                    } else {
+                        *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.y) + oc) = pack8(v, p.y_dtype == ANELM_BF16);
                     }
-            }
-#pragma unroll
-            for (int ks = 0; ks < 4; ks++) {
-                const int k0 = dbase + 16 * ks;
-#pragma unroll
-                for (int n2 = 0; n2 < 2; n2++) {
-                    uint32_t bh[2][4], bl[2][4];
-                    const bool b_lo = state || !exact;  // W always has a lo plane, Q only when not exact
-#pragma unroll
-                    for (int q = 0; q < 2; q++) {
-                        ldb2_sw(bh[q], bhi, 32 * n2 + 16 * q, k0, lane);
-                        if (b_lo) ldb2_sw(bl[q], blo, 32 * n2 + 16 * q, k0, lane);
-                    }
-                    mma3_tm<2>(&acc[4 * n2], fa[ks], fl[ks], bh, bl, b_lo);
                 }
             }
+            // the accumulators and this step's lc slot are read: release them
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bar[6 + bb]);
         }
-        __syncthreads();  // W, Q free
-        if (more && loader) chain_load_wq(sm, mp, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC, exact);
-        // ---- the two d halves of a column group meet ----
-        float (*xb)[32][32] = state ? sm.xd : sm.xy;
-#pragma unroll
-        for (int r = 0; r < 32; r++) xb[w4][r][lane] = acc[r >> 2][r & 3];
-        named_bar_sync_cta((state ? 1 : 3) + jg, 64);
-        float y[4][4];  // output warps: Q S for rows t in [32 dh, 32 dh + 32)
-        if (state) {
-#pragma unroll
-            for (int r = 0; r < 32; r++) acc[r >> 2][r & 3] += xb[w4 ^ 1][r][lane];
-        } else {
-#pragma unroll
-            for (int n4 = 0; n4 < 4; n4++)
-#pragma unroll
-                for (int e = 0; e < 4; e++)
-                    y[n4][e] = (dh ? acc[4 + n4][e] : acc[n4][e]) + xb[w4 ^ 1][4 * (4 * dh + n4) + e][lane];
-        }
-        tc::mbar_wait(&sm.bar[1], par, p.err, ANELM_ERR_TIMEOUT, abort);
-        __syncthreads();  // U and lc of this chunk are in shared memory
-        const float* lc = sm.lc[par];
-        const float lcC = lc[kC - 1];
-        if (tid < kC) {  // published by the barrier before M D
-            sm.eg[tid] = expf(lc[tid]);
-            sm.ef[tid] = expf(lcC - lc[tid]);
-        }
-        if (state) {
-            // D = U - W S (in place of acc); its fragments (k-steps 2 dh, 2 dh + 1) for the output warps
-#pragma unroll
-            for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-                for (int e = 0; e < 4; e++)
-                    acc[nt][e] = u_at(sm, 8 * nt + 2 * c + (e & 1), jr + g + 8 * (e >> 1)) - acc[nt][e];
-#pragma unroll
-            for (int k2 = 0; k2 < 2; k2++) {
-                uint32_t ah[4], al[4];
-                if (dh) afrag(acc, 2 + k2, ah, al);
-                else afrag(acc, k2, ah, al);
-#pragma unroll
-                for (int r = 0; r < 4; r++) {
-                    sm.sdf[jg][2 * dh + k2][r][lane] = ah[r];
-                    sm.sdf[jg][2 * dh + k2][4 + r][lane] = al[r];
-                }
-            }
-            named_bar_arrive_cta(7 + jg, 128);
-        }
-        tc::mbar_wait(&sm.bar[2], par, p.err, ANELM_ERR_TIMEOUT, abort);
-        __syncthreads();  // M and K of this chunk are in shared memory; U read; e^lc factors visible
-        if (more && loader) chain_load_u(sm, mp, p, vrow0 + (ci + 1) * kC, j0, par ^ 1);
-        if (!state) {
-            // ---- Y = e^lc Q S + M D for rows t in [32 dh, 32 dh + 32) ----
-            const int tt = 32 * dh;
-#pragma unroll
-            for (int n4 = 0; n4 < 4; n4++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) y[n4][e] *= sm.eg[tt + 8 * n4 + 2 * c + (e & 1)];
-            named_bar_sync_cta(7 + jg, 128);
-#pragma unroll
-            for (int ks = 0; ks < 4; ks++) {
-                if (16 * ks >= tt + 32) break;  // M[t][i] = 0 for i > t
-                uint32_t ah[4], al[4];
-#pragma unroll
-                for (int r = 0; r < 4; r++) {
-                    ah[r] = sm.sdf[jg][ks][r][lane];
-                    al[r] = sm.sdf[jg][ks][4 + r][lane];
-                }
-                uint32_t bh[2][4], bl[2][4];
-#pragma unroll
-                for (int np = 0; np < 2; np++) {
-                    ldb2_sw(bh[np], a_m, tt + 16 * np, 16 * ks, lane);
-                    ldb2_sw(bl[np], a_m + 8192, tt + 16 * np, 16 * ks, lane);
-                }
-                mma3_tm<2>(y, ah, al, bh, bl);
-            }
-#pragma unroll
-            for (int n4 = 0; n4 < 4; n4++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int t = ci * kC + tt + 8 * n4 + 2 * c + (e & 1);
-                    if (t < p.n)
-                        store_from_float(p.y, p.y_dtype,
-                                         ((long long)b * p.n + t) * p.y_stride + (long long)h * kDv + j0 + jr + g +
-                                             8 * (e >> 1),
-                                         y[n4][e]);
-                }
-        } else {
-            // ---- S = e^{lc_C} S + K^T diag(e^{lc_C - lc}) D over this warp's half of d ----
-            const float gC = expf(lcC);
-#pragma unroll
-            for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) s[nt][e] *= gC;
-            float fs[8][2];  // e^{lc_C - lc_t}, t = 8 nt + 2 c + e
-#pragma unroll
-            for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-                for (int e = 0; e < 2; e++) fs[nt][e] = sm.ef[8 * nt + 2 * c + e];
-#pragma unroll
-            for (int ks = 0; ks < 4; ks++) {
-                uint32_t ah[4], al[4];
-                afrag(acc, fs, ks, ah, al);
-                uint32_t bh[4][4], bl[4][4];
-#pragma unroll
-                for (int np = 0; np < 4; np++) {
-                    ldb2_t_sw(bh[np], a_k, dbase + 16 * np, 16 * ks, lane);
-                    if (!exact) ldb2_t_sw(bl[np], a_k + 16384, dbase + 16 * np, 16 * ks, lane);
-                }
-                mma3_tm<4>(s, ah, al, bh, bl, !exact);
-            }
-        }
-        __syncthreads();  // M, K free
-        if (more && loader) chain_load_mk(sm, mp, krow0 + (ci + 1) * kC, vrow0 + (ci + 1) * kC, exact);
     }
-    if (state) {
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-            for (int e = 0; e < 4; e++)
-                S[(long long)(dbase + 8 * nt + 2 * c + (e & 1)) * kDv + j0 + jr + g + 8 * (e >> 1)] = s[nt][e];
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 12) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kTmemCols);
     }
 }
 
@@ -996,7 +1067,7 @@ static bool make_plane_map(CUtensorMap* m, const __half* base, uint64_t rows, lo
 
 static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t stream) {
     const int nC = p.T_pad / kC;
-    const size_t chunk_smem = sizeof(ChunkSmem) + 1024, chain_smem = sizeof(ChainSmem) + 1024;
+    const size_t chunk_smem = sizeof(ChunkSmem) + 1024;
     const uint64_t krows = (uint64_t)p.B * p.Hk * p.T_pad, vrows = (uint64_t)p.B * p.Hv * p.T_pad;
     CUtensorMap mK, mQ, mV;
     ChainMaps cm;
@@ -1009,7 +1080,7 @@ static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t strea
         auto fn = tc::tmap_encode_fn();
         cuuint64_t dims[2] = {(cuuint64_t)kDv, vrows};
         cuuint64_t strides[1] = {(cuuint64_t)kDv * 4};
-        cuuint32_t box[2] = {(cuuint32_t)kDvb, (cuuint32_t)kC};
+        cuuint32_t box[2] = {(cuuint32_t)kUBox, (cuuint32_t)kC};
         cuuint32_t estr[2] = {1, 1};
         if (!make_plane_map(&cm.w, p.wh, vrows, p.v_plane) || !make_plane_map(&cm.m, p.mh, vrows, p.m_plane, kC) ||
             fn(&cm.u, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.Ub, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1018,9 +1089,11 @@ static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t strea
             return ANELM_ERR_CUDA;
     }
     cudaFuncSetAttribute(gdn_pf_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
-    cudaFuncSetAttribute(gdn_pf_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chain_smem);
     gdn_pf_chunk_kernel<<<dim3(nC, p.Hv, p.B), kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, p);
-    gdn_pf_chain_kernel<<<dim3(p.Hv * (kDv / kDvb), p.B), kChainThreads, chain_smem, stream>>>(cm, p);
+    constexpr int NB = 32;
+    const size_t chain_smem = sizeof(ChainTcSmem<NB>) + 1024;
+    cudaFuncSetAttribute(gdn_pf_chain_tc_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chain_smem);
+    gdn_pf_chain_tc_kernel<NB><<<dim3(p.Hv * (kDv / NB), p.B), kChainTcThreads, chain_smem, stream>>>(cm, p);
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 
@@ -1031,6 +1104,7 @@ int launch_gdn_prefill(GdnPrefillParams p, void* workspace, cudaStream_t stream)
     p.qkv_exact = 0;  // q, k, v come out of the conv / SiLU / L2 norm in fp32: both planes carry them
     p.y_dtype = ANELM_F32;
     p.y_stride = (long long)p.Hv * kDv;
+    p.y_vec = 1;      // workspace rows: 256-byte aligned base, 16-byte aligned rows
     gdn_pf_snapshot_kernel<<<dim3((p.C * 3 + 255) / 256, p.B), 256, 0, stream>>>(p);
     const size_t prep_smem = (size_t)p.C * sizeof(float);
     if (prep_smem > 48 * 1024)
@@ -1048,6 +1122,7 @@ int launch_gated_delta_chunked(GdnPrefillParams p, void* workspace, cudaStream_t
     p.in_vec = (uintptr_t)p.q_in % 16 == 0 && (uintptr_t)p.k_in % 16 == 0 && (uintptr_t)p.v_in % 16 == 0;
     // 16-bit inputs are exact in fp16 (bf16 normal values have 8 significant bits): lo planes are zero
     p.qkv_exact = p.in_dtype == ANELM_F16 || p.in_dtype == ANELM_BF16;
+    p.y_vec = (uintptr_t)p.y % 16 == 0 && p.y_stride % 8 == 0;  // 16-byte stores of 8 outputs
     gdn_pf_pack_kernel<<<dim3(p.T_pad, p.B), 256, 0, stream>>>(p);
     return launch_chunks_and_chain(p, stream);
 }

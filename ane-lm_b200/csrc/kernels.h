@@ -153,6 +153,7 @@ struct GdnPrefillParams {
     void* y;
     int y_dtype;
     long long y_stride;
+    int y_vec;             // set by the launcher: y and y_stride allow 16-byte stores of 8 outputs
     // workspace (carved by the launcher); tensor-core operands as an fp16 hi plane followed by a
     // lo plane (x = hi + lo)
     __half* qh;            // [B][Hk][T_pad][dk], lo plane at + q_plane
