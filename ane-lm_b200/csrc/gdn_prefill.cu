@@ -65,6 +65,23 @@ __device__ __forceinline__ void split_store(__half* hi, __half* lo, float x) {
     *lo = __float2half_rn(x - __half2float(h));
 }
 
+__device__ __forceinline__ uint32_t h2u(const __half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+// x0, x1 as an fp16 hi pair and the fp16 pair of the remainders
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    hi = h2u(h);
+    lo = h2u(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
+}
+// hi / lo fp16 planes of 8 consecutive values as two 16-byte words
+__device__ __forceinline__ void split8(const float (&v)[8], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) split2(v[2 * i], v[2 * i + 1], h[i], l[i]);
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 // ---------------------------------------------------------------- snapshot
 
 __global__ void gdn_pf_snapshot_kernel(const GdnPrefillParams p) {
@@ -258,6 +275,8 @@ __device__ __forceinline__ int sw128_off(int row, int col) {
 __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                       const __grid_constant__ CUtensorMap tmQ,
                                                                       const __grid_constant__ CUtensorMap tmV,
+                                                                      const __grid_constant__ CUtensorMap tmW,
+                                                                      const __grid_constant__ CUtensorMap tmU,
                                                                       const GdnPrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
     ChunkSmem& sm = *reinterpret_cast<ChunkSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -503,27 +522,45 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
         tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + col0, xx[0]);
         tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + col0 + 32, xx[1]);
         tc::tmem_ld_wait();
+        // staged in the operand buffers (free once GEMM 2 is done) in the tiles' TMA layouts and stored
+        // by eight tile copies: W hi / lo as four 64-column boxes (128-byte rows, 128B swizzle) in
+        // op[0], U as four 32-column fp32 boxes in op[1]
 #pragma unroll
         for (int h32 = 0; h32 < 2; h32++) {
             const uint32_t (&x)[32] = xx[h32];
-            const int d0 = 64 * hc + 32 * h32;
             if (is_w) {
-                __half* whi = p.wh + (vrow + t) * kDk + d0;
 #pragma unroll
                 for (int c8 = 0; c8 < 4; c8++) {
                     float v[8];
 #pragma unroll
                     for (int e = 0; e < 8; e++) v[e] = __uint_as_float(x[8 * c8 + e]);
-                    put_hl8(whi, p.v_plane, 8 * c8, v);
+                    uint4 whi, wlo;
+                    split8(v, whi, wlo);
+                    const int off = t * 128 + ((((4 * h32 + c8) ^ t) & 7) << 4);
+                    *reinterpret_cast<uint4*>(&sm.op[0][hc * 8192 + off]) = whi;
+                    *reinterpret_cast<uint4*>(&sm.op[0][16384 + hc * 8192 + off]) = wlo;
                 }
             } else {
-                float4* u = reinterpret_cast<float4*>(p.Ub + (vrow + t) * kDv + d0);
+                uint8_t* ub = &sm.op[1][(2 * hc + h32) * 8192 + t * 128];
 #pragma unroll
                 for (int c4 = 0; c4 < 8; c4++)
-                    u[c4] = make_float4(__uint_as_float(x[4 * c4]), __uint_as_float(x[4 * c4 + 1]),
-                                        __uint_as_float(x[4 * c4 + 2]), __uint_as_float(x[4 * c4 + 3]));
+                    *reinterpret_cast<float4*>(ub + (((c4 ^ t) & 7) << 4)) =
+                        make_float4(__uint_as_float(x[4 * c4]), __uint_as_float(x[4 * c4 + 1]),
+                                    __uint_as_float(x[4 * c4 + 2]), __uint_as_float(x[4 * c4 + 3]));
             }
         }
+        tc::fence_proxy_async_smem();
+    }
+    __syncthreads();
+    if (tid == 0 && !*abort) {
+#pragma unroll
+        for (int pl = 0; pl < 2; pl++)
+#pragma unroll
+            for (int kb = 0; kb < 2; kb++) tc::tma_store_3d(&tmW, &sm.op[0][pl * 16384 + kb * 8192], 64 * kb, (int)vrow, pl);
+#pragma unroll
+        for (int bx = 0; bx < 4; bx++) tc::tma_store_2d(&tmU, &sm.op[1][bx * 8192], 32 * bx, (int)vrow);
+        tc::bulk_commit_group();
+        tc::bulk_wait_group_read0();  // the shared-memory sources stay valid until the copies read them
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -543,14 +580,6 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
 
 // ---------------------------------------------------------------- the recurrence on tcgen05
 
-__device__ __forceinline__ uint32_t h2u(const __half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
-// x0, x1 as an fp16 hi pair and the fp16 pair of the remainders
-__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-    const __half2 h = __floats2half2_rn(x0, x1);
-    const float2 hf = __half22float2(h);
-    hi = h2u(h);
-    lo = h2u(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
-}
 // A chunk's operand tiles, fetched by TMA tile copies (64 rows x 128 bytes, 128B swizzle): W, Q, K
 // and M hi / lo planes, U (fp32, 32-column boxes)
 struct ChainMaps {
@@ -599,14 +628,6 @@ struct ChainTcSmem {
     int abort;
 };
 
-// hi / lo fp16 planes of 8 consecutive values as two 16-byte words
-__device__ __forceinline__ void split8(const float (&v)[8], uint4& hi, uint4& lo) {
-    uint32_t h[4], l[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) split2(v[2 * i], v[2 * i + 1], h[i], l[i]);
-    hi = make_uint4(h[0], h[1], h[2], h[3]);
-    lo = make_uint4(l[0], l[1], l[2], l[3]);
-}
 // Operands with rows of NB fp16 (K index = row, N = column, N contiguous): 128-byte rows with the
 // 128-byte swizzle (NB 64: 16-byte word c of row r at ((c ^ r) & 7)) or 64-byte rows with the
 // 64-byte swizzle (NB 32: word c at ((c ^ (r >> 1)) & 3)); 8-row groups of 8 NB * 2 bytes.
@@ -1097,7 +1118,7 @@ static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t strea
             return ANELM_ERR_CUDA;
     }
     cudaFuncSetAttribute(gdn_pf_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
-    gdn_pf_chunk_kernel<<<dim3(nC, p.Hv, p.B), kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, p);
+    gdn_pf_chunk_kernel<<<dim3(nC, p.Hv, p.B), kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, cm.w, cm.u, p);
     constexpr int NB = 32;
     const size_t chain_smem = sizeof(ChainTcSmem<NB>) + 1024;
     cudaFuncSetAttribute(gdn_pf_chain_tc_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chain_smem);
