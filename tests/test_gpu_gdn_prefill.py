@@ -170,3 +170,26 @@ def test_chunked_core_rejects_bad_arguments():
         gated_delta_chunked(q, q, q, torch.zeros(1, 8, 1, device="cuda"), torch.zeros(1, 8, 1, device="cuda"),
                             torch.zeros(1, 1, 128, 128, device="cuda"), workspace=small)
     assert e.value.status == ab.ERR_CAPACITY
+
+
+@pytest.mark.parametrize("y_dtype", [torch.bfloat16, torch.float32])
+def test_chunked_core_output_without_16_byte_alignment(y_dtype):
+    """An output buffer that does not start on a 16-byte boundary takes the per-element store path
+    of the recurrence kernel; its values must equal those of the aligned buffer bit for bit."""
+    rng = np.random.default_rng(77)
+    B, T, Hk, Hv = 1, 100, 2, 4
+    q, k, v, lg, beta, s0 = core_inputs(rng, B, T, Hk, Hv)
+    dev = lambda a, dt=torch.float32: torch.tensor(a, device="cuda").to(dt).contiguous()  # noqa: E731
+    st_a, st_b = dev(s0), dev(s0)
+    y_a = gated_delta_chunked(dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16), dev(lg),
+                              dev(beta), st_a, ab.DELTA_CPUOPS, y_dtype=y_dtype)
+    n = B * T * Hv * 128
+    buf = torch.zeros(n + 1, dtype=y_dtype, device="cuda")
+    y_b = buf[1:].view(B, T, Hv, 128)
+    assert y_b.data_ptr() % 16 != 0
+    gated_delta_chunked(dev(q, torch.bfloat16), dev(k, torch.bfloat16), dev(v, torch.bfloat16), dev(lg), dev(beta),
+                        st_b, ab.DELTA_CPUOPS, y=y_b)
+    torch.cuda.synchronize()
+    assert torch.equal(y_a, y_b)
+    assert torch.equal(st_a, st_b)
+    assert buf[0].item() == 0
