@@ -728,48 +728,59 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kWarpK || warp == kWarpV) {
         // ---------------- TMA producers: one warp streams Q then K (then the gate tile), one streams V ----------------
-        if (lane == 0 && nT > 0) {
+        // (each runs converged, polls its barriers with every lane and elects one lane per copy)
+        if (nT > 0) {
             const int krow0 = (b * p.Hkv + kvh) * p.n_tot + kt0 * kBN;
             if (warp == kWarpK) {
-                tc::prefetch_tmap(&tmQ);
-                tc::prefetch_tmap(&tmK);
                 const int qrow0 = (b * p.Hq + h) * p.n_pad + q0;
-                tc::mbar_arrive_expect_tx(&bars[Q_FULL], kQBytes);
-                for (int kb = 0; kb < 4; kb++) tc::tma_load_2d(sQ + kb * (kBM * 128), &tmQ, &bars[Q_FULL], kb * 64, qrow0);
+                if (tc::elect_one()) {
+                    tc::prefetch_tmap(&tmQ);
+                    tc::prefetch_tmap(&tmK);
+                    tc::mbar_arrive_expect_tx(&bars[Q_FULL], kQBytes);
+                    for (int kb = 0; kb < 4; kb++) tc::tma_load_2d(sQ + kb * (kBM * 128), &tmQ, &bars[Q_FULL], kb * 64, qrow0);
+                }
                 for (int j = 0; j < nT; j++) {
                     if (j >= 1) tc::mbar_wait(&bars[K_EMPTY], (j - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                    tc::mbar_arrive_expect_tx(&bars[K_FULL], kKBytes);
-                    for (int kb = 0; kb < 4; kb++)
-                        tc::tma_load_2d(sK + kb * (kBN * 128), &tmK, &bars[K_FULL], kb * 64, krow0 + j * kBN);
+                    if (tc::elect_one()) {
+                        tc::mbar_arrive_expect_tx(&bars[K_FULL], kKBytes);
+                        for (int kb = 0; kb < 4; kb++)
+                            tc::tma_load_2d(sK + kb * (kBN * 128), &tmK, &bars[K_FULL], kb * 64, krow0 + j * kBN);
+                    }
                 }
                 if (p.tma_epilogue && p.gate) {
                     // sigmoid(gate) of this tile's 128 rows into the K buffer once the last Q K^T has
                     // read it (rows past the sequence end are zero-filled), hidden behind the last tiles
-                    tc::prefetch_tmap(&tmG);
                     tc::mbar_wait(&bars[K_EMPTY], (nT - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                    tc::mbar_arrive_expect_tx(&bars[G_FULL], kBM * kD * 2);
-                    for (int kb = 0; kb < 4; kb++)
-                        tc::tma_load_3d(sK + kb * (kBM * 128), &tmG, &bars[G_FULL], h * kD + kb * 64, q0, b);
+                    if (tc::elect_one()) {
+                        tc::prefetch_tmap(&tmG);
+                        tc::mbar_arrive_expect_tx(&bars[G_FULL], kBM * kD * 2);
+                        for (int kb = 0; kb < 4; kb++)
+                            tc::tma_load_3d(sK + kb * (kBM * 128), &tmG, &bars[G_FULL], h * kD + kb * 64, q0, b);
+                    }
                 }
             } else {
-                tc::prefetch_tmap(&tmV);
+                if (tc::elect_one()) tc::prefetch_tmap(&tmV);
                 for (int j = 0; j < nT; j++) {
                     if (j >= 1) tc::mbar_wait(&bars[V_EMPTY], (j - 1) & 1, p.err, ANELM_ERR_TIMEOUT, abort);
-                    tc::mbar_arrive_expect_tx(&bars[V_FULL], kVBytes);
-                    for (int kb = 0; kb < 4; kb++)
-                        tc::tma_load_2d(sV + kb * (kBN * 128), &tmV, &bars[V_FULL], kb * 64, krow0 + j * kBN);
+                    if (tc::elect_one()) {
+                        tc::mbar_arrive_expect_tx(&bars[V_FULL], kVBytes);
+                        for (int kb = 0; kb < 4; kb++)
+                            tc::tma_load_2d(sV + kb * (kBN * 128), &tmV, &bars[V_FULL], kb * 64, krow0 + j * kBN);
+                    }
                 }
             }
         }
         __syncwarp();
     } else if (warp == kWarpMma) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0 && nT > 0) {
+        // ---------------- MMA issuer (converged warp, one elected lane per tcgen05 instruction) ----------------
+        if (nT > 0) {
             constexpr uint32_t id_qk = tc::idesc_f16_f32(kBM, kBN);
             constexpr uint32_t id_pv = tc::idesc_f16_f32_bmn(kBM, kD);  // V[key][d]: d contiguous
-            const uint32_t aQ = (uint32_t)__cvta_generic_to_shared(sQ);
-            const uint32_t aK = (uint32_t)__cvta_generic_to_shared(sK);
-            const uint32_t aV = (uint32_t)__cvta_generic_to_shared(sV);
+            // descriptors of the tiles' first bytes; a k-step adds its byte offset >> 4 to the start
+            // address field (shared-memory addresses stay below 2^18, so it never carries out)
+            const uint64_t dQ = tc::desc_kmajor_sw128((uint32_t)__cvta_generic_to_shared(sQ));
+            const uint64_t dK = tc::desc_kmajor_sw128((uint32_t)__cvta_generic_to_shared(sK));
+            const uint64_t dV = tc::desc_sw128((uint32_t)__cvta_generic_to_shared(sV), kBN * 128, 1024);
             tc::mbar_wait(&bars[Q_FULL], 0, p.err, ANELM_ERR_TIMEOUT, abort);
             auto qk = [&](int j) {
                 const int s = j & 1, u = j >> 1;
@@ -781,10 +792,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kb = 0; kb < 4; kb++)
 #pragma unroll
                     for (int ks = 0; ks < 4; ks++)
-                        tc::mma_f16_ss(tmem + s * kBN, tc::desc_kmajor_sw128(aQ + kb * (kBM * 128) + ks * 32),
-                                       tc::desc_kmajor_sw128(aK + kb * (kBN * 128) + ks * 32), id_qk, (kb | ks) != 0);
-                tc::mma_commit(&bars[S_FULL + s]);
-                tc::mma_commit(&bars[K_EMPTY]);
+                        if (tc::elect_one())
+                            tc::mma_f16_ss(tmem + s * kBN, dQ + ((kb * (kBM * 128) + ks * 32) >> 4),
+                                           dK + ((kb * (kBN * 128) + ks * 32) >> 4), id_qk, (kb | ks) != 0);
+                if (tc::elect_one()) {
+                    tc::mma_commit(&bars[S_FULL + s]);
+                    tc::mma_commit(&bars[K_EMPTY]);
+                }
             };
             auto pv = [&](int j) {
                 const int s = j & 1, u = j >> 1;
@@ -795,10 +809,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // four 64-d boxes (boxes kBN * 128 bytes apart, 8-row groups 1024 bytes apart)
 #pragma unroll
                 for (int ks = 0; ks < kBN / 16; ks++)
-                    tc::mma_f16_ts(tmem + kOCol, tmem + s * kBN + ks * 8,
-                                   tc::desc_sw128(aV + ks * 16 * 128, kBN * 128, 1024), id_pv, (j > 0) || (ks > 0));
-                tc::mma_commit(&bars[PV_DONE + s]);
-                tc::mma_commit(&bars[V_EMPTY]);
+                    if (tc::elect_one())
+                        tc::mma_f16_ts(tmem + kOCol, tmem + s * kBN + ks * 8, dV + ((ks * 16 * 128) >> 4), id_pv,
+                                       (j > 0) || (ks > 0));
+                if (tc::elect_one()) {
+                    tc::mma_commit(&bars[PV_DONE + s]);
+                    tc::mma_commit(&bars[V_EMPTY]);
+                }
             };
             qk(0);
             for (int j = 0; j < nT; j++) {
