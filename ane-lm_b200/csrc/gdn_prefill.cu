@@ -73,11 +73,23 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_
     hi = h2u(h);
     lo = h2u(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
 }
-// hi / lo fp16 planes of 8 consecutive values as two 16-byte words
+// the same split in bf16 (8 + 8 significant bits): the operands that meet bf16 inputs in an MMA
+__device__ __forceinline__ void split2_bf(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+// hi / lo planes (fp16, or bf16 with BF) of 8 consecutive values as two 16-byte words
+template <bool BF = false>
 __device__ __forceinline__ void split8(const float (&v)[8], uint4& hi, uint4& lo) {
     uint32_t h[4], l[4];
 #pragma unroll
-    for (int i = 0; i < 4; i++) split2(v[2 * i], v[2 * i + 1], h[i], l[i]);
+    for (int i = 0; i < 4; i++) {
+        if (BF) split2_bf(v[2 * i], v[2 * i + 1], h[i], l[i]);
+        else split2(v[2 * i], v[2 * i + 1], h[i], l[i]);
+    }
     hi = make_uint4(h[0], h[1], h[2], h[3]);
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
@@ -272,6 +284,7 @@ __device__ __forceinline__ int sw128_off(int row, int col) {
     return row * 128 + ((((col >> 3) ^ row) & 7) << 4) + (col & 7) * 2;
 }
 
+template <bool BF>
 __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                       const __grid_constant__ CUtensorMap tmQ,
                                                                       const __grid_constant__ CUtensorMap tmV,
@@ -313,12 +326,32 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
             if (pl == 0 || lo)
 #pragma unroll
                 for (int kb = 0; kb < 2; kb++) {
-                    tc::tma_load_3d(&sm.op[pl][kb * 16384], &tmK, &bar[0], kb * 64, (int)krow, pl);
-                    tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmQ, &bar[0], kb * 64, (int)krow, pl);
+                    if (p.direct) {  // the caller's token-major q / k: [b][token][head][d]
+                        tc::tma_load_4d(&sm.op[pl][kb * 16384], &tmK, &bar[0], kb * 64, kh, t0, b);
+                        tc::tma_load_4d(&sm.op[pl][kb * 16384 + 8192], &tmQ, &bar[0], kb * 64, kh, t0, b);
+                    } else {
+                        tc::tma_load_3d(&sm.op[pl][kb * 16384], &tmK, &bar[0], kb * 64, (int)krow, pl);
+                        tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmQ, &bar[0], kb * 64, (int)krow, pl);
+                    }
                 }
     }
     if (warp == 1) {  // inclusive prefix sum of log g over the chunk (two tokens per lane)
-        const float g0 = p.lg[vrow + 2 * lane], g1 = p.lg[vrow + 2 * lane + 1];
+        // log g and beta of tokens t0 + 2 lane, + 1 (direct: the caller's [b][token][head] arrays, zero
+        // past the prompt)
+        float g0, g1, b0, b1;
+        if (p.direct) {
+            const int ta = t0 + 2 * lane, tb = ta + 1;
+            const long long ia = ((long long)b * p.n + ta) * p.Hv + h, ib = ia + p.Hv;
+            g0 = ta < p.n ? p.lg_in[ia] : 0.f;
+            g1 = tb < p.n ? p.lg_in[ib] : 0.f;
+            b0 = ta < p.n ? p.beta_in[ia] : 0.f;
+            b1 = tb < p.n ? p.beta_in[ib] : 0.f;
+        } else {
+            g0 = p.lg[vrow + 2 * lane];
+            g1 = p.lg[vrow + 2 * lane + 1];
+            b0 = p.beta[vrow + 2 * lane];
+            b1 = p.beta[vrow + 2 * lane + 1];
+        }
         float s = g0 + g1;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -331,13 +364,13 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
         // lt = lc_{t-1} (Sk from the undecayed state) or lc_t (decay first)
         sm.lt[2 * lane] = p.delta_mode == ANELM_DELTA_CPUOPS ? excl : excl + g0;
         sm.lt[2 * lane + 1] = p.delta_mode == ANELM_DELTA_CPUOPS ? excl + g0 : s;
-        sm.bt[2 * lane] = p.beta[vrow + 2 * lane];
-        sm.bt[2 * lane + 1] = p.beta[vrow + 2 * lane + 1];
+        sm.bt[2 * lane] = b0;
+        sm.bt[2 * lane + 1] = b1;
     }
     if (tid == 0) {  // GEMM 1: [K; Q] K^T -> TMEM columns [0, 64)
         if (tc::mbar_wait(&bar[0], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {
             tc::tc_fence_after();
-            constexpr uint32_t id1 = tc::idesc_f16_f32(128, kC);
+            constexpr uint32_t id1 = BF ? tc::idesc_as_bf16(tc::idesc_f16_f32(128, kC)) : tc::idesc_f16_f32(128, kC);
             // exact inputs: K and Q are exact in fp16, so hi * hi is the whole product
             const bool lo_terms = !p.qkv_exact;
 #pragma unroll
@@ -367,7 +400,8 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
             if (pl == 0 || lo)
 #pragma unroll
                 for (int kb = 0; kb < 2; kb++)
-                    tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmV, &bar[2], kb * 64, (int)vrow, pl);
+                    if (p.direct) tc::tma_load_4d(&sm.op[pl][kb * 16384 + 8192], &tmV, &bar[2], kb * 64, h, t0, b);
+                    else tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmV, &bar[2], kb * 64, (int)vrow, pl);
     }
     {
         const int q = warp & 3, hc = warp >> 2;
@@ -484,10 +518,16 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
 #pragma unroll
             for (int half = 0; half < 2; half++) {
                 const float v = xs[m] * (half ? fu : fw);
-                const __half hv = __float2half_rn(v);
                 const int off = sw128_off(half * kC + t, j);
-                *reinterpret_cast<__half*>(&sm.t[0][off]) = hv;
-                *reinterpret_cast<__half*>(&sm.t[1][off]) = __float2half_rn(v - __half2float(hv));
+                if (BF) {  // hi / lo in bf16, the type of the K / V operands they meet
+                    const __nv_bfloat16 hv = __float2bfloat16_rn(v);
+                    *reinterpret_cast<__nv_bfloat16*>(&sm.t[0][off]) = hv;
+                    *reinterpret_cast<__nv_bfloat16*>(&sm.t[1][off]) = __float2bfloat16_rn(v - __bfloat162float(hv));
+                } else {
+                    const __half hv = __float2half_rn(v);
+                    *reinterpret_cast<__half*>(&sm.t[0][off]) = hv;
+                    *reinterpret_cast<__half*>(&sm.t[1][off]) = __float2half_rn(v - __half2float(hv));
+                }
             }
         }
     }
@@ -496,7 +536,8 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
     if (tid == 0 && ok1) {  // GEMM 2: [T'; T''] [K0 V0 K1 V1] -> TMEM columns [0, 256)
         if (tc::mbar_wait(&bar[2], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {
             tc::tc_fence_after();
-            constexpr uint32_t id2 = tc::idesc_f16_f32_bmn(128, 256);
+            constexpr uint32_t id2 =
+                BF ? tc::idesc_as_bf16(tc::idesc_f16_f32_bmn(128, 256)) : tc::idesc_f16_f32_bmn(128, 256);
             const bool b_lo = !p.qkv_exact;  // exact inputs: K and V have no lo plane (hi * lo vanishes)
 #pragma unroll
             for (int term = 0; term < 3; term++) {
@@ -535,7 +576,7 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
 #pragma unroll
                     for (int e = 0; e < 8; e++) v[e] = __uint_as_float(x[8 * c8 + e]);
                     uint4 whi, wlo;
-                    split8(v, whi, wlo);
+                    split8<BF>(v, whi, wlo);
                     const int off = t * 128 + ((((4 * h32 + c8) ^ t) & 7) << 4);
                     *reinterpret_cast<uint4*>(&sm.op[0][hc * 8192 + off]) = whi;
                     *reinterpret_cast<uint4*>(&sm.op[0][16384 + hc * 8192 + off]) = wlo;
@@ -659,7 +700,7 @@ __device__ __forceinline__ void u_row16(const uint8_t* u, int t, int j, float (&
     }
 }
 
-template <int NB>
+template <int NB, bool BF>
 __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(const __grid_constant__ ChainMaps mp,
                                                                              const GdnPrefillParams p) {
     static_assert(NB == 32 || NB == 64, "operand rows of 64 or 128 bytes");
@@ -733,7 +774,9 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
                 for (int pl = 0; pl < 2; pl++)
                     for (int kb = 0; kb < 2; kb++) {
                         tc::tma_load_3d(&sm.qw[pl][kb * 16384 + 8192], &mp.w, &bar[0], 64 * kb, vrow0 + ci * kC, pl);
-                        if (pl == 0 || !exact)
+                        if (p.direct && pl == 0)  // the caller's token-major q: [b][token][head][d]
+                            tc::tma_load_4d(&sm.qw[pl][kb * 16384], &mp.q, &bar[0], 64 * kb, kh, ci * kC, b);
+                        else if (pl == 0 || !exact)
                             tc::tma_load_3d(&sm.qw[pl][kb * 16384], &mp.q, &bar[0], 64 * kb, krow0 + ci * kC, pl);
                     }
             }
@@ -753,7 +796,8 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
                 tc::mbar_arrive_expect_tx(&bar[2], (exact ? 1 : 2) * 2 * 8192);
                 for (int pl = 0; pl < (exact ? 1 : 2); pl++)
                     for (int kb = 0; kb < 2; kb++)
-                        tc::tma_load_3d(&sm.k[pl][kb * 8192], &mp.k, &bar[2], 64 * kb, krow0 + ci * kC, pl);
+                        if (p.direct) tc::tma_load_4d(&sm.k[pl][kb * 8192], &mp.k, &bar[2], 64 * kb, kh, ci * kC, b);
+                        else tc::tma_load_3d(&sm.k[pl][kb * 8192], &mp.k, &bar[2], 64 * kb, krow0 + ci * kC, pl);
             }
             loaded[2] = ci + 1;
         };
@@ -801,8 +845,10 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
         __syncwarp();
     } else if (warp == 12) {
         // ---------------------------------------------------------------- MMAs
-        constexpr uint32_t idA = tc::idesc_f16_f32_bmn(128, NB);
-        constexpr uint32_t idC = tc::idesc_f16_f32_bmn(128, NB) | (1u << 15);  // A (K^T) MN-major too
+        // A and C meet q / k: their operands are bf16 when those are (BF); B (M D) stays fp16
+        constexpr uint32_t idB = tc::idesc_f16_f32_bmn(128, NB);
+        constexpr uint32_t idA = BF ? tc::idesc_as_bf16(idB) : idB;
+        constexpr uint32_t idC = idA | (1u << 15);  // A (K^T) MN-major too
         // descriptors of the tiles' first bytes; later k-steps add their byte offset >> 4 to the
         // start-address field (shared-memory addresses stay below 2^18, so it never carries out)
         const uint64_t dqw = tc::desc_kmajor_sw128(smem_u32(sm.qw)), dm = tc::desc_kmajor_sw128(smem_u32(sm.m));
@@ -820,7 +866,7 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
                 for (int ks = 0; ks < 4; ks++)
                     if (tc::elect_one())
                         tc::mma_f16_ss(tmem + kColB + NB * cb, dm + (((term == 1 ? 16384 : 0) + ks * 32) >> 4),
-                                       dd + ((cb * 2 * kDPlane + (term == 2 ? kDPlane : 0) + ks * 16 * kRowB) >> 4), idA,
+                                       dd + ((cb * 2 * kDPlane + (term == 2 ? kDPlane : 0) + ks * 16 * kRowB) >> 4), idB,
                                        (term | ks) != 0);
             if (tc::elect_one()) tc::mma_commit(&bar[4 + cb]);
             return true;
@@ -883,7 +929,7 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
 #pragma unroll
                 for (int e = 0; e < 8; e++) v[e] = s[8 * c + e];
                 uint4 hi, lo;
-                split8(v, hi, lo);
+                split8<BF>(v, hi, lo);  // S meets [Q; W] in A
                 const uint32_t o = nb_word<NB>(i, hf * (kHalf / 8) + c);
                 *reinterpret_cast<uint4*>(&sm.s[0][o]) = hi;
                 *reinterpret_cast<uint4*>(&sm.s[1][o]) = lo;
@@ -940,7 +986,7 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
                     *reinterpret_cast<uint4*>(&sm.d[bb][1][o]) = lo;
 #pragma unroll
                     for (int e = 0; e < 8; e++) v[e] *= gam;
-                    split8(v, hi, lo);
+                    split8<BF>(v, hi, lo);  // Gamma D meets K in C; D (for B) stays fp16
                     *reinterpret_cast<uint4*>(&sm.gd[0][o]) = hi;
                     *reinterpret_cast<uint4*>(&sm.gd[1][o]) = lo;
                 }
@@ -1094,15 +1140,36 @@ static bool make_plane_map(CUtensorMap* m, const __half* base, uint64_t rows, lo
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 4D map over the caller's token-major 16-bit [B][n][heads][128] q, k or v: box {64 d, 1 head, 64 tokens,
+// 1 sequence}, 128B swizzle (the same tile as a plane box); tokens past n read as zeros
+static bool make_direct_map(CUtensorMap* m, const void* base, int dtype, uint64_t heads, uint64_t n, uint64_t B) {
+    auto fn = tc::tmap_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {128, heads, n, B};
+    cuuint64_t strides[3] = {256, heads * 256, n * heads * 256};
+    cuuint32_t box[4] = {64, 1, (cuuint32_t)kC, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    return fn(m, dtype == ANELM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t stream) {
     const int nC = p.T_pad / kC;
     const size_t chunk_smem = sizeof(ChunkSmem) + 1024;
     const uint64_t krows = (uint64_t)p.B * p.Hk * p.T_pad, vrows = (uint64_t)p.B * p.Hv * p.T_pad;
     CUtensorMap mK, mQ, mV;
     ChainMaps cm;
-    if (!make_plane_map(&mK, p.kh, krows, p.q_plane) || !make_plane_map(&mQ, p.qh, krows, p.q_plane) ||
-        !make_plane_map(&mV, p.vh, vrows, p.v_plane))
+    if (p.direct) {
+        if (!make_direct_map(&mK, p.k_in, p.in_dtype, p.Hk, p.n, p.B) ||
+            !make_direct_map(&mQ, p.q_in, p.in_dtype, p.Hk, p.n, p.B) ||
+            !make_direct_map(&mV, p.v_in, p.in_dtype, p.Hv, p.n, p.B))
+            return ANELM_ERR_CUDA;
+    } else if (!make_plane_map(&mK, p.kh, krows, p.q_plane) || !make_plane_map(&mQ, p.qh, krows, p.q_plane) ||
+               !make_plane_map(&mV, p.vh, vrows, p.v_plane)) {
         return ANELM_ERR_CUDA;
+    }
     cm.k = mK;
     cm.q = mQ;
     {  // W (hi / lo like V), M (64 columns), U (fp32, 32-column boxes of this block's state columns)
@@ -1117,12 +1184,22 @@ static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t strea
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return ANELM_ERR_CUDA;
     }
-    cudaFuncSetAttribute(gdn_pf_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
-    gdn_pf_chunk_kernel<<<dim3(nC, p.Hv, p.B), kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, cm.w, cm.u, p);
     constexpr int NB = 32;
     const size_t chain_smem = sizeof(ChainTcSmem<NB>) + 1024;
-    cudaFuncSetAttribute(gdn_pf_chain_tc_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chain_smem);
-    gdn_pf_chain_tc_kernel<NB><<<dim3(p.Hv * (kDv / NB), p.B), kChainTcThreads, chain_smem, stream>>>(cm, p);
+    const dim3 chunk_grid(nC, p.Hv, p.B), chain_grid(p.Hv * (kDv / NB), p.B);
+    if (p.direct && p.op_bf16) {  // bf16 inputs read in place: the operands that meet them are bf16 too
+        cudaFuncSetAttribute(gdn_pf_chunk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
+        gdn_pf_chunk_kernel<true><<<chunk_grid, kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, cm.w, cm.u, p);
+        cudaFuncSetAttribute(gdn_pf_chain_tc_kernel<NB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)chain_smem);
+        gdn_pf_chain_tc_kernel<NB, true><<<chain_grid, kChainTcThreads, chain_smem, stream>>>(cm, p);
+    } else {
+        cudaFuncSetAttribute(gdn_pf_chunk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
+        gdn_pf_chunk_kernel<false><<<chunk_grid, kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, cm.w, cm.u, p);
+        cudaFuncSetAttribute(gdn_pf_chain_tc_kernel<NB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)chain_smem);
+        gdn_pf_chain_tc_kernel<NB, false><<<chain_grid, kChainTcThreads, chain_smem, stream>>>(cm, p);
+    }
     return cudaGetLastError() == cudaSuccess ? ANELM_OK : ANELM_ERR_CUDA;
 }
 
@@ -1131,6 +1208,8 @@ int launch_gdn_prefill(GdnPrefillParams p, void* workspace, cudaStream_t stream)
     p.T_pad = (p.n + kC - 1) / kC * kC;
     carve(p, workspace, true);
     p.qkv_exact = 0;  // q, k, v come out of the conv / SiLU / L2 norm in fp32: both planes carry them
+    p.direct = 0;
+    p.op_bf16 = 0;
     p.y_dtype = ANELM_F32;
     p.y_stride = (long long)p.Hv * kDv;
     p.y_vec = 1;      // workspace rows: 256-byte aligned base, 16-byte aligned rows
@@ -1152,7 +1231,11 @@ int launch_gated_delta_chunked(GdnPrefillParams p, void* workspace, cudaStream_t
     // 16-bit inputs are exact in fp16 (bf16 normal values have 8 significant bits): lo planes are zero
     p.qkv_exact = p.in_dtype == ANELM_F16 || p.in_dtype == ANELM_BF16;
     p.y_vec = (uintptr_t)p.y % 16 == 0 && p.y_stride % 8 == 0;  // 16-byte stores of 8 outputs
-    gdn_pf_pack_kernel<<<dim3(p.T_pad, p.B), 256, 0, stream>>>(p);
+    // 16-bit inputs on 16-byte boundaries are read in place by TMA (no pack); their products then use
+    // their own type (bf16 inputs: bf16 hi / lo partners, 16 significant bits)
+    p.direct = p.qkv_exact && p.in_vec;
+    p.op_bf16 = p.direct && p.in_dtype == ANELM_BF16;
+    if (!p.direct) gdn_pf_pack_kernel<<<dim3(p.T_pad, p.B), 256, 0, stream>>>(p);
     return launch_chunks_and_chain(p, stream);
 }
 

@@ -144,6 +144,9 @@ struct GdnPrefillParams {
     int in_vec;            // set by the launcher: q_in, k_in, v_in 16-byte aligned
     int qkv_exact;        // q, k, v arrive as 16-bit values: exact in fp16, their lo planes are zero and
                           // are neither written nor read; products against them take two of the three terms
+    int direct;           // set by the launcher: 16-bit q, k, v (and log g, beta) read in place by the chunk
+                          // and chain kernels (no pack), every product with them in their own type
+    int op_bf16;          // with direct: the inputs (and so the hi / lo operands meeting them) are bf16
     const float* lg_in;
     const float* beta_in;
     // state [seq][Hv][dk][dv], row b uses seq_ids[b] (or b)

@@ -108,6 +108,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+        "[%2];\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+        "l"((uint64_t)map), "r"((uint32_t)__cvta_generic_to_shared(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+
 // Shared -> global tile store; elements outside the tensor map's extent are not written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"((uint64_t)map),
@@ -303,6 +312,8 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
 }
 // The same with B MN-major (transpose-B bit): B[k][n] stored with n contiguous.
 __host__ __device__ constexpr uint32_t idesc_f16_f32_bmn(int M, int N) { return idesc_f16_f32(M, N) | (1u << 16); }
+// A and B as bf16 instead of fp16 (kind::f16 takes one type for both operands).
+__host__ __device__ constexpr uint32_t idesc_as_bf16(uint32_t idesc) { return idesc | (1u << 7) | (1u << 10); }
 
 }  // namespace tc
 }  // namespace anelm
