@@ -24,17 +24,19 @@
 // relative) and each product is three tcgen05 MMAs (hi*hi + lo*hi + hi*lo) with fp32 accumulation
 // in TMEM, so the products match fp32 arithmetic; plain fp16 operands would let the gated RMSNorm
 // amplify their 2^-12 rounding past the tolerance.  Operands live in memory as a hi plane followed
-// by a lo plane and reach shared memory by TMA.  When the bare core op gets
-// 16-bit q / k / v (bf16 values have 8 significant bits, so they are exact in fp16), their lo
-// planes are zero: they are neither written nor loaded, K K^T / Q K^T take one term, and the
-// products with K, Q or V on one side take two.
+// by a lo plane and reach shared memory by TMA.  When the bare core op gets 16-bit q / k / v they
+// are exact, so they need no lo plane: K K^T / Q K^T take one term and the products with K, Q or V
+// on one side take two.  On 16-byte boundaries they are read in place (4D tensor maps over the
+// caller's [B][n][heads][128] arrays, no pack), and with bf16 inputs the operands that meet them in
+// an MMA are bf16 hi / lo pairs (16 significant bits, ~1e-5 relative per product).
 //
 // Launches:
 //   gdn_pf_snapshot_kernel  copy of the conv rings / positions of the plan's sequences (the
 //                           prep kernel reads the old ring while the last tokens overwrite it)
 //   gdn_pf_prep_kernel      per token: conv + SiLU + L2 / scale, gates; q, k, v (hi / lo) in
 //                           chunk layout, log g and beta; the last 3 inputs into the ring
-//   gdn_pf_pack_kernel      (core op only) token-major q, k, v, log g, beta -> chunk layout
+//   gdn_pf_pack_kernel      (core op, 32-bit or unaligned inputs) token-major q, k, v, log g, beta ->
+//                           chunk layout
 //   gdn_pf_chunk_kernel     per (chunk, value head): K K^T, Q K^T, T by forward substitution,
 //                           W, U, M
 //   gdn_pf_chain_tc_kernel  per (sequence, value head, 32 columns): the chunk recurrence over
