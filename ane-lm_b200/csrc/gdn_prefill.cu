@@ -253,19 +253,22 @@ __global__ void __launch_bounds__(256) gdn_pf_pack_kernel(const GdnPrefillParams
 // TMEM, fp16 operands staged by TMA with the 128-byte swizzle, each product as three MMAs over the
 // hi / lo planes: hi*hi + lo*hi + hi*lo):
 //   GEMM 1  [K; Q] K^T  (M 128 = 64 K rows + 64 Q rows, N 64, K 128): K K^T -> A, Q K^T -> M;
-//   GEMM 2  [T'; T''] [K | V]  (M 128, N 256, K 64) with T' = T diag(beta e^{lt}), T'' = T diag(beta):
-//           its diagonal blocks are W = T' K and U = T'' V (the off-diagonal ones are not used).
+//   GEMM 2  [T'; T''] [K | V]  (M 128, K 64) with T' = T diag(beta e^{lt}), T'' = T diag(beta), in two
+//           N = 128 halves through the same 128 TMEM columns: [T'; T''] [K0 K1], whose rows 0-63 are
+//           W = T' K, then [T'; T''] [V0 V1], whose rows 64-127 are U = T'' V (the other rows unused).
 // The operand buffer of each plane is [K d0-63 | Q d0-63 | K d64-127 | Q d64-127] (8 KB boxes of
 // 64 rows x 128 bytes): read as the K-major A of GEMM 1 (two 16 KB boxes of 128 rows), as its
-// K-major B (the K rows), and, once V has replaced Q, as the MN-major B of GEMM 2 (N boxes K0, V0,
-// K1, V1, 8 KB apart).  T = (I + A)^{-1} by forward substitution on the CUDA cores in between.
+// K-major B (the K rows), and, once V has replaced Q, as the MN-major B of GEMM 2 (N boxes K0, K1 or
+// V0, V1, 16 KB apart).  T = (I + A)^{-1} by forward substitution on the CUDA cores in between.  With
+// exact inputs the lo plane is not allocated: 71 KB of shared memory and 128 TMEM columns admit three
+// CTAs per SM.
 constexpr int kChunkThreads = 256;
 constexpr int kOpPlane = 32768;            // bytes of one plane of the operand buffer
 constexpr int kTPlane = 16384;             // bytes of one plane of [T'; T''] (128 rows x 128 bytes)
 constexpr int kTs = kC + 4;                // fp32 pitch of A and T in the inversion
-constexpr uint32_t kChunkTmemCols = 256;
+constexpr uint32_t kChunkTmemCols = 128;
 struct ChunkSmem {
-    uint8_t op[2][kOpPlane];               // hi, lo planes (1024-byte aligned)
+    uint8_t op[kOpPlane];                  // hi plane of the operand buffer (1024-byte aligned)
     union {
         uint8_t t[2][kTPlane];             // [T'; T''] hi, lo (K-major, 128-byte swizzle)
         struct {
@@ -273,12 +276,16 @@ struct ChunkSmem {
             float tm[kC][kTs];             // T = (I + A)^{-1}
             float z[3][16][17];            // block products of one level
         } inv;
+        uint8_t ustage[4 * 8192];          // U staged for its tile stores once GEMM 2 is done
     };
     float lc[kC], lt[kC], bt[kC];
-    uint64_t bar[4];                       // K+Q loaded, GEMM 1 done, V loaded, GEMM 2 done
+    uint64_t bar[5];                       // K+Q loaded, GEMM 1 done, V loaded, GEMM 2 K half done, V half done
     uint32_t tmem_slot;
     int abort;
+    alignas(1024) uint8_t op_lo[kOpPlane];  // lo plane: allocated and read only for inputs that are not exact
 };
+// shared memory of a chunk-kernel CTA (with the slack that aligns its base to 1024 bytes)
+inline size_t chunk_smem_bytes(bool exact) { return (exact ? offsetof(ChunkSmem, op_lo) : sizeof(ChunkSmem)) + 1024; }
 
 
 // byte offset of element (row, col) (fp16, 64 columns per 128-byte row) in a 128B-swizzled tile
@@ -287,7 +294,7 @@ __device__ __forceinline__ int sw128_off(int row, int col) {
 }
 
 template <bool BF>
-__global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __grid_constant__ CUtensorMap tmK,
+__global__ void __launch_bounds__(kChunkThreads, 3) gdn_pf_chunk_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                       const __grid_constant__ CUtensorMap tmQ,
                                                                       const __grid_constant__ CUtensorMap tmV,
                                                                       const __grid_constant__ CUtensorMap tmW,
@@ -305,7 +312,7 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
     uint64_t* bar = sm.bar;
     if (tid == 0) {
         sm.abort = 0;
-        for (int i = 0; i < 4; i++) tc::mbar_init(&bar[i], 1);
+        for (int i = 0; i < 5; i++) tc::mbar_init(&bar[i], 1);
         tc::fence_barrier_init();
     }
     if (warp == 0) {
@@ -316,8 +323,10 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = sm.tmem_slot;
-    const uint32_t aop = (uint32_t)__cvta_generic_to_shared(&sm.op[0][0]);
+    const uint32_t aop = (uint32_t)__cvta_generic_to_shared(&sm.op[0]);
+    const uint32_t aop_lo = (uint32_t)__cvta_generic_to_shared(&sm.op_lo[0]);  // not inside the launch when exact
     const uint32_t at_ = (uint32_t)__cvta_generic_to_shared(&sm.t[0][0]);
+    auto opl = [&](int pl) { return pl ? sm.op_lo : sm.op; };  // a plane of the operand buffer
     if (tid == 0) {  // K and Q, both planes, into the operand buffers
         tc::prefetch_tmap(&tmK);
         tc::prefetch_tmap(&tmQ);
@@ -329,11 +338,11 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
 #pragma unroll
                 for (int kb = 0; kb < 2; kb++) {
                     if (p.direct) {  // the caller's token-major q / k: [b][token][head][d]
-                        tc::tma_load_4d(&sm.op[pl][kb * 16384], &tmK, &bar[0], kb * 64, kh, t0, b);
-                        tc::tma_load_4d(&sm.op[pl][kb * 16384 + 8192], &tmQ, &bar[0], kb * 64, kh, t0, b);
+                        tc::tma_load_4d(opl(pl) + kb * 16384, &tmK, &bar[0], kb * 64, kh, t0, b);
+                        tc::tma_load_4d(opl(pl) + kb * 16384 + 8192, &tmQ, &bar[0], kb * 64, kh, t0, b);
                     } else {
-                        tc::tma_load_3d(&sm.op[pl][kb * 16384], &tmK, &bar[0], kb * 64, (int)krow, pl);
-                        tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmQ, &bar[0], kb * 64, (int)krow, pl);
+                        tc::tma_load_3d(opl(pl) + kb * 16384, &tmK, &bar[0], kb * 64, (int)krow, pl);
+                        tc::tma_load_3d(opl(pl) + kb * 16384 + 8192, &tmQ, &bar[0], kb * 64, (int)krow, pl);
                     }
                 }
     }
@@ -377,7 +386,7 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
             const bool lo_terms = !p.qkv_exact;
 #pragma unroll
             for (int term = 0; term < 3; term++) {
-                const uint32_t pa = aop + (term == 1 ? kOpPlane : 0), pb = aop + (term == 2 ? kOpPlane : 0);
+                const uint32_t pa = term == 1 ? aop_lo : aop, pb = term == 2 ? aop_lo : aop;
                 if (term == 0 || lo_terms)
 #pragma unroll
                     for (int kb = 0; kb < 2; kb++)
@@ -402,8 +411,8 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
             if (pl == 0 || lo)
 #pragma unroll
                 for (int kb = 0; kb < 2; kb++)
-                    if (p.direct) tc::tma_load_4d(&sm.op[pl][kb * 16384 + 8192], &tmV, &bar[2], kb * 64, h, t0, b);
-                    else tc::tma_load_3d(&sm.op[pl][kb * 16384 + 8192], &tmV, &bar[2], kb * 64, (int)vrow, pl);
+                    if (p.direct) tc::tma_load_4d(opl(pl) + kb * 16384 + 8192, &tmV, &bar[2], kb * 64, h, t0, b);
+                    else tc::tma_load_3d(opl(pl) + kb * 16384 + 8192, &tmV, &bar[2], kb * 64, (int)vrow, pl);
     }
     {
         const int q = warp & 3, hc = warp >> 2;
@@ -535,39 +544,58 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
     }
     tc::fence_proxy_async_smem();
     __syncthreads();  // [T'; T''] visible to the tensor core
-    if (tid == 0 && ok1) {  // GEMM 2: [T'; T''] [K0 V0 K1 V1] -> TMEM columns [0, 256)
-        if (tc::mbar_wait(&bar[2], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {
+    // ---- GEMM 2 in two N = 128 halves through TMEM columns [0, 128): [T'; T''] [K0 K1] (rows 0-63 are W),
+    // then, once the W rows are read, [T'; T''] [V0 V1] (rows 64-127 are U) ----
+    constexpr uint32_t id2 = BF ? tc::idesc_as_bf16(tc::idesc_f16_f32_bmn(128, 128)) : tc::idesc_f16_f32_bmn(128, 128);
+    const bool b_lo = !p.qkv_exact;  // exact inputs: K and V have no lo plane (hi * lo vanishes)
+    auto gemm2 = [&](uint32_t boff) {  // B = the two 64-column boxes at boff, boff + 16 KB of each plane
+#pragma unroll
+        for (int term = 0; term < 3; term++) {
+            const uint32_t pa = at_ + (term == 1 ? kTPlane : 0), pb = (term == 2 ? aop_lo : aop) + boff;
+            if (term < 2 || b_lo)
+#pragma unroll
+                for (int ks = 0; ks < 4; ks++)
+                    tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(pa + ks * 32), tc::desc_sw128(pb + ks * 16 * 128, 16384, 1024),
+                                   id2, (term | ks) != 0);
+        }
+    };
+    if (tid == 0 && ok1) {
+        if (tc::mbar_wait(&bar[2], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {  // V landed too (read by the second half)
             tc::tc_fence_after();
-            constexpr uint32_t id2 =
-                BF ? tc::idesc_as_bf16(tc::idesc_f16_f32_bmn(128, 256)) : tc::idesc_f16_f32_bmn(128, 256);
-            const bool b_lo = !p.qkv_exact;  // exact inputs: K and V have no lo plane (hi * lo vanishes)
-#pragma unroll
-            for (int term = 0; term < 3; term++) {
-                const uint32_t pa = at_ + (term == 1 ? kTPlane : 0), pb = aop + (term == 2 ? kOpPlane : 0);
-                if (term < 2 || b_lo)
-#pragma unroll
-                    for (int ks = 0; ks < 4; ks++)
-                        tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(pa + ks * 32),
-                                       tc::desc_sw128(pb + ks * 16 * 128, 8192, 1024), id2, (term | ks) != 0);
-            }
+            gemm2(0);
             tc::mma_commit(&bar[3]);
         }
     }
-    // ---- epilogue 2: W = T' K (rows 0-63) hi / lo, U = T'' V (rows 64-127) fp32 ----
-    if (tc::mbar_wait(&bar[3], 0, p.err, ANELM_ERR_TIMEOUT, abort)) {
+    const int q = warp & 3, hc = warp >> 2;  // hc: key / value dims [64 hc, 64 hc + 64)
+    const int r = 32 * q + lane;
+    const bool is_w = r < kC;                // warps of TMEM lanes 0-63: W; 64-127: U
+    const int t = is_w ? r : r - kC;
+    uint32_t xx[2][32];  // this thread's 64 values of W or U, both 32-column loads in flight before one wait
+    const bool okw = tc::mbar_wait(&bar[3], 0, p.err, ANELM_ERR_TIMEOUT, abort);
+    if (okw && is_w) {
         tc::tc_fence_after();
-        const int q = warp & 3, hc = warp >> 2;  // hc: key / value dims [64 hc, 64 hc + 64)
-        const int r = 32 * q + lane;
-        const bool is_w = r < kC;
-        const int t = is_w ? r : r - kC;
-        const uint32_t col0 = (is_w ? 0 : 64) + 128 * hc;
-        uint32_t xx[2][32];  // both 32-column loads in flight before the one wait
-        tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + col0, xx[0]);
-        tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + col0 + 32, xx[1]);
+        tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 64 * hc, xx[0]);
+        tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 64 * hc + 32, xx[1]);
         tc::tmem_ld_wait();
-        // staged in the operand buffers (free once GEMM 2 is done) in the tiles' TMA layouts and stored
-        // by eight tile copies: W hi / lo as four 64-column boxes (128-byte rows, 128B swizzle) in
-        // op[0], U as four 32-column fp32 boxes in op[1]
+    }
+    tc::tc_fence_before();
+    __syncthreads();  // the W rows are read: the second half may overwrite the columns
+    if (tid == 0 && okw) {
+        tc::tc_fence_after();
+        gemm2(8192);
+        tc::mma_commit(&bar[4]);
+    }
+    const bool oku = okw && tc::mbar_wait(&bar[4], 0, p.err, ANELM_ERR_TIMEOUT, abort);
+    if (oku) {
+        tc::tc_fence_after();
+        if (!is_w) {
+            tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 64 * hc, xx[0]);
+            tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 64 * hc + 32, xx[1]);
+            tc::tmem_ld_wait();
+        }
+        // GEMM 2 is done with the operand buffer and [T'; T'']: W (hi / lo) is staged in the former as
+        // four 64-column boxes (128-byte rows, 128B swizzle), U (fp32) in the latter as four 32-column
+        // boxes, in the tiles' TMA layouts, and both are written by eight tile stores
 #pragma unroll
         for (int h32 = 0; h32 < 2; h32++) {
             const uint32_t (&x)[32] = xx[h32];
@@ -580,11 +608,11 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
                     uint4 whi, wlo;
                     split8<BF>(v, whi, wlo);
                     const int off = t * 128 + ((((4 * h32 + c8) ^ t) & 7) << 4);
-                    *reinterpret_cast<uint4*>(&sm.op[0][hc * 8192 + off]) = whi;
-                    *reinterpret_cast<uint4*>(&sm.op[0][16384 + hc * 8192 + off]) = wlo;
+                    *reinterpret_cast<uint4*>(&sm.op[hc * 8192 + off]) = whi;
+                    *reinterpret_cast<uint4*>(&sm.op[16384 + hc * 8192 + off]) = wlo;
                 }
             } else {
-                uint8_t* ub = &sm.op[1][(2 * hc + h32) * 8192 + t * 128];
+                uint8_t* ub = &sm.ustage[(2 * hc + h32) * 8192 + t * 128];
 #pragma unroll
                 for (int c4 = 0; c4 < 8; c4++)
                     *reinterpret_cast<float4*>(ub + (((c4 ^ t) & 7) << 4)) =
@@ -595,13 +623,13 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
         tc::fence_proxy_async_smem();
     }
     __syncthreads();
-    if (tid == 0 && !*abort) {
+    if (tid == 0 && oku && !*abort) {
 #pragma unroll
         for (int pl = 0; pl < 2; pl++)
 #pragma unroll
-            for (int kb = 0; kb < 2; kb++) tc::tma_store_3d(&tmW, &sm.op[0][pl * 16384 + kb * 8192], 64 * kb, (int)vrow, pl);
+            for (int kb = 0; kb < 2; kb++) tc::tma_store_3d(&tmW, &sm.op[pl * 16384 + kb * 8192], 64 * kb, (int)vrow, pl);
 #pragma unroll
-        for (int bx = 0; bx < 4; bx++) tc::tma_store_2d(&tmU, &sm.op[1][bx * 8192], 32 * bx, (int)vrow);
+        for (int bx = 0; bx < 4; bx++) tc::tma_store_2d(&tmU, &sm.ustage[bx * 8192], 32 * bx, (int)vrow);
         tc::bulk_commit_group();
         tc::bulk_wait_group_read0();  // the shared-memory sources stay valid until the copies read them
     }
@@ -609,10 +637,10 @@ __global__ void __launch_bounds__(kChunkThreads) gdn_pf_chunk_kernel(const __gri
     __syncthreads();
     if (warp == 0) {
         if (lane == 0) {  // nothing of this CTA's may still be in flight when its TMEM is released
-            for (int i = 0; i < 4; i++)
+            for (int i = 0; i < 5; i++)
                 for (uint32_t n = 0; n < tc::kWaitPolls && !tc::mbar_try_wait(&bar[i], 0); n++) {
                     if (i == 2 && !ok1) break;  // V was never requested
-                    if ((i == 1 || i == 3) && *abort) break;
+                    if ((i == 1 || i >= 3) && *abort) break;
                 }
         }
         __syncwarp();
@@ -1159,7 +1187,7 @@ static bool make_direct_map(CUtensorMap* m, const void* base, int dtype, uint64_
 
 static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t stream) {
     const int nC = p.T_pad / kC;
-    const size_t chunk_smem = sizeof(ChunkSmem) + 1024;
+    const size_t chunk_smem = chunk_smem_bytes(p.qkv_exact != 0);
     const uint64_t krows = (uint64_t)p.B * p.Hk * p.T_pad, vrows = (uint64_t)p.B * p.Hv * p.T_pad;
     CUtensorMap mK, mQ, mV;
     ChainMaps cm;
@@ -1190,13 +1218,15 @@ static int launch_chunks_and_chain(const GdnPrefillParams& p, cudaStream_t strea
     const size_t chain_smem = sizeof(ChainTcSmem<NB>) + 1024;
     const dim3 chunk_grid(nC, p.Hv, p.B), chain_grid(p.Hv * (kDv / NB), p.B);
     if (p.direct && p.op_bf16) {  // bf16 inputs read in place: the operands that meet them are bf16 too
-        cudaFuncSetAttribute(gdn_pf_chunk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
+        cudaFuncSetAttribute(gdn_pf_chunk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)chunk_smem_bytes(false));
         gdn_pf_chunk_kernel<true><<<chunk_grid, kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, cm.w, cm.u, p);
         cudaFuncSetAttribute(gdn_pf_chain_tc_kernel<NB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)chain_smem);
         gdn_pf_chain_tc_kernel<NB, true><<<chain_grid, kChainTcThreads, chain_smem, stream>>>(cm, p);
     } else {
-        cudaFuncSetAttribute(gdn_pf_chunk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk_smem);
+        cudaFuncSetAttribute(gdn_pf_chunk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)chunk_smem_bytes(false));
         gdn_pf_chunk_kernel<false><<<chunk_grid, kChunkThreads, chunk_smem, stream>>>(mK, mQ, mV, cm.w, cm.u, p);
         cudaFuncSetAttribute(gdn_pf_chain_tc_kernel<NB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)chain_smem);
