@@ -193,3 +193,18 @@ def test_chunked_core_output_without_16_byte_alignment(y_dtype):
     assert torch.equal(y_a, y_b)
     assert torch.equal(st_a, st_b)
     assert buf[0].item() == 0
+
+
+def test_chunked_core_fp32_inputs_through_the_pack():
+    """fp32 q / k / v are not exact in fp16: the pack splits them into hi / lo planes and every product
+    takes its three terms (the path 16-bit inputs skip by reading them in place)."""
+    rng = np.random.default_rng(91)
+    B, T, Hk, Hv = 2, 130, 2, 4
+    q, k, v, lg, beta, s0 = core_inputs(rng, B, T, Hk, Hv)
+    q = q + (1e-4 * rng.standard_normal(q.shape)).astype(np.float32)  # values fp16 cannot hold exactly
+    y, s = run_core(q, k, v, lg, beta, s0, ab.DELTA_CPUOPS, torch.float32)
+    for b in range(B):
+        st = s0[b].copy()
+        want = po.gated_delta_tokens("oracle", q[b], k[b], v[b], lg[b], beta[b], st, ab.DELTA_CPUOPS)
+        assert_close(y[b], want, what=f"y (b={b}, fp32 inputs)")
+        assert_close(s[b], st, what=f"final state (b={b}, fp32 inputs)")
