@@ -26,7 +26,8 @@
 // amplify their 2^-12 rounding past the tolerance.  Operands live in memory as a hi plane followed
 // by a lo plane and reach shared memory by TMA.  When the bare core op gets 16-bit q / k / v they
 // are exact, so they need no lo plane: K K^T / Q K^T take one term and the products with K, Q or V
-// on one side take two.  On 16-byte boundaries they are read in place (4D tensor maps over the
+// on one side take two; [Q; W] S takes two as well, W meeting S by its hi plane alone (the state
+// and U keep their pairs: their lo planes carry the accuracy).  On 16-byte boundaries they are read in place (4D tensor maps over the
 // caller's [B][n][heads][128] arrays, no pack), and with bf16 inputs the operands that meet them in
 // an MMA are bf16 hi / lo pairs (16 significant bits, ~1e-5 relative per product).
 //
@@ -625,7 +626,7 @@ __global__ void __launch_bounds__(kChunkThreads, 3) gdn_pf_chunk_kernel(const __
     __syncthreads();
     if (tid == 0 && oku && !*abort) {
 #pragma unroll
-        for (int pl = 0; pl < 2; pl++)
+        for (int pl = 0; pl < (p.qkv_exact ? 1 : 2); pl++)  // exact inputs: the chain reads W hi only
 #pragma unroll
             for (int kb = 0; kb < 2; kb++) tc::tma_store_3d(&tmW, &sm.op[pl * 16384 + kb * 8192], 64 * kb, (int)vrow, pl);
 #pragma unroll
@@ -758,13 +759,10 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
         for (int i = 0; i < 10; i++) tc::mbar_init(&bar[i], count[i]);
         tc::fence_barrier_init();
     }
-    {  // zero rows of the A tiles that no load fills: M rows 64-127 and, for exact inputs, the Q lo rows
+    {  // zero rows of the A tiles that no load fills: M rows 64-127
         const uint4 z = make_uint4(0u, 0u, 0u, 0u);
         for (int i = tid; i < 2 * 512; i += kChainTcThreads)
             *reinterpret_cast<uint4*>(&sm.m[i >> 9][8192 + (i & 511) * 16]) = z;
-        if (exact)
-            for (int i = tid; i < 2 * 512; i += kChainTcThreads)
-                *reinterpret_cast<uint4*>(&sm.qw[1][(i >> 9) * 16384 + (i & 511) * 16]) = z;
     }
     if (warp == 12) {
         tc::tmem_alloc(&sm.tmem_slot, kTmemCols);
@@ -800,13 +798,14 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
         int loaded[4] = {0, 0, 0, 0};  // chunks whose loads are issued on bars 0-2 and 9 (one phase each)
         auto load_qw = [&](int ci) {
             if (tc::elect_one()) {
-                tc::mbar_arrive_expect_tx(&bar[0], (exact ? 3 : 4) * 2 * 8192);
-                for (int pl = 0; pl < 2; pl++)
+                // exact inputs: the hi plane alone (A drops its [Q; W] lo term, below)
+                tc::mbar_arrive_expect_tx(&bar[0], (exact ? 2 : 4) * 2 * 8192);
+                for (int pl = 0; pl < (exact ? 1 : 2); pl++)
                     for (int kb = 0; kb < 2; kb++) {
                         tc::tma_load_3d(&sm.qw[pl][kb * 16384 + 8192], &mp.w, &bar[0], 64 * kb, vrow0 + ci * kC, pl);
-                        if (p.direct && pl == 0)  // the caller's token-major q: [b][token][head][d]
+                        if (p.direct)  // the caller's token-major q: [b][token][head][d]
                             tc::tma_load_4d(&sm.qw[pl][kb * 16384], &mp.q, &bar[0], 64 * kb, kh, ci * kC, b);
-                        else if (pl == 0 || !exact)
+                        else
                             tc::tma_load_3d(&sm.qw[pl][kb * 16384], &mp.q, &bar[0], 64 * kb, krow0 + ci * kC, pl);
                     }
             }
@@ -906,9 +905,12 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
             if (!wait_w(0, ph)) break;  // S of this step written, [Q; W] landed
             if (ci >= 2 && !wait_w(6 + bb, ((ci >> 1) + 1) & 1)) break;  // outputs of step ci - 2 read
             tc::tc_fence_after();
-            // A: [Q; W] S -> columns [NB bb, NB bb + NB)
+            // A: [Q; W] S -> columns [NB bb, NB bb + NB).  Exact inputs: Q has no lo plane, and W enters
+            // by its hi plane alone (16 MMAs instead of 24 on the step's critical path); over 128 chunk
+            // steps that moves y and the state by ~2e-6 (fp16) / ~2e-5 (bf16), 1 % of the tolerance
 #pragma unroll
-            for (int term = 0; term < 3; term++)
+            for (int term = 0; term < 3; term++) {
+                if (term == 1 && exact) continue;
 #pragma unroll
                 for (int kb = 0; kb < 2; kb++)
 #pragma unroll
@@ -917,6 +919,7 @@ __global__ void __launch_bounds__(kChainTcThreads, 1) gdn_pf_chain_tc_kernel(con
                             tc::mma_f16_ss(tmem + NB * bb, dqw + (((term == 1 ? 32768 : 0) + kb * 16384 + ks * 32) >> 4),
                                            ds + (((term == 2 ? kSPlane : 0) + (kb * 4 + ks) * 16 * kRowB) >> 4), idA,
                                            (term | kb | ks) != 0);
+            }
             if (tc::elect_one()) tc::mma_commit(&bar[1]);
             if (!wait_w(2, ph)) break;  // D, Gamma D written; K landed
             tc::tc_fence_after();

@@ -12,9 +12,10 @@ Tokens past the end are zero (k, v, q, beta, log g), which leaves the state unch
 
 The restatement runs twice: in float64 (the algebra alone, tight tolerance) and with every
 tensor-core operand rounded the way the kernels round it -- 16-bit inputs as one plane, computed
-operands as hi / lo pairs (fp16, or bf16 where an MMA meets bf16 inputs), each product as
-hi*hi + lo*hi + hi*lo in fp32, T by an fp32 solve, S and D in fp32 -- over BASELINE config 4's
-8192 tokens, within a hundredth of the GPU tests' tolerance.  CPU only; the GPU tests check the
+operands as hi / lo pairs (fp16, or bf16 where an MMA meets bf16 inputs) except W, which meets the
+state by its hi plane alone, each product as hi*hi + lo*hi + hi*lo in fp32, T by an fp32 solve,
+S and D in fp32 -- over BASELINE config 4's 8192 tokens, within a twentieth of the GPU tests'
+tolerance.  CPU only; the GPU tests check the
 kernels themselves."""
 import numpy as np
 import pytest
@@ -108,7 +109,7 @@ def chunk_form(q, k, v, lg, beta, s0, hf, inputs=None, pairs=True):
             # GEMM 2: [T'; T''] as hi / lo pairs against exact K | V
             W, U = mma(sp(Tp, comp), (K,)), mma(sp(Tpp, comp), (V,))
             Sp = sp(S, comp)
-            QS, WS = mma((Q,), Sp), mma(sp(W, comp), Sp)  # A = [Q; W] S
+            QS, WS = mma((Q,), Sp), mma(sp(W, comp)[:1], Sp)  # A = [Q; W] S, W by its hi plane
             D = U - WS
             MD = mma(sp(M, "f16"), sp(D, "f16"))  # B = M D stays fp16
             y[c0:c0 + CHUNK] = np.exp(lc)[:, None] * QS + MD
@@ -158,15 +159,16 @@ def test_chunk_algebra_equals_token_recurrence(hf, T):
 @pytest.mark.parametrize("hf", [0, 1])
 def test_kernel_operand_format_over_config4_length(hf, inputs):
     """8192 tokens (128 chunk steps) of one value head with the kernels' operand rounding: the
-    hi / lo products keep outputs and state within 2e-5 of the recurrence after 128 chunk steps
-    (a hundredth of the GPU tests' tolerance), where one 16-bit plane per computed operand drifts
-    past it (fp16: ~5e-5 in y, ~4e-4 in the state; bf16: ~3e-4 and ~2e-3)."""
+    hi / lo products keep outputs and state within 1e-4 + 1e-3 rel of the recurrence after 128
+    chunk steps (a twentieth of the GPU tests' tolerance; measured ~3e-6 with fp16 inputs, ~2e-5
+    with bf16), where one 16-bit plane per computed operand drifts past it (fp16: ~5e-5 in y,
+    ~4e-4 in the state; bf16: ~3e-4 and ~2e-3)."""
     rng = np.random.default_rng(40 + hf + 2 * (inputs == "bf16"))
     q, k, v, lg, beta, s0 = inputs_cfg4(rng, 8192, 1, 1, inputs)
     st = s0.copy()
     want = po.gated_delta_tokens("oracle", q, k, v, lg, beta, st, hf)
     y, s = run_chunks(q, k, v, lg, beta, s0, hf, inputs)
-    tight = dict(atol=2e-5, rtol=1e-4)
+    tight = dict(atol=1e-4, rtol=1e-3)
     assert_close(y, want, **tight, what=f"y, {inputs} operand pairs (hf={hf})")
     assert_close(s, st, **tight, what=f"state, {inputs} operand pairs (hf={hf})")
     y1, s1 = run_chunks(q, k, v, lg, beta, s0, hf, inputs, pairs=False)
