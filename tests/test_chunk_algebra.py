@@ -14,8 +14,8 @@ The restatement runs twice: in float64 (the algebra alone, tight tolerance) and 
 tensor-core operand rounded the way the kernels round it -- 16-bit inputs as one plane, computed
 operands as hi / lo pairs (fp16, or bf16 where an MMA meets bf16 inputs) except W, which meets the
 state by its hi plane alone, each product as hi*hi + lo*hi + hi*lo in fp32, T by an fp32 solve,
-S and D in fp32 -- over BASELINE config 4's 8192 tokens, within a twentieth of the GPU tests'
-tolerance.  CPU only; the GPU tests check the
+S and D in fp32 -- over BASELINE config 4's 8192 tokens, within 1e-4 abs + 1e-3 rel (the GPU
+tests allow 2e-3 + 1e-2).  CPU only; the GPU tests check the
 kernels themselves."""
 import numpy as np
 import pytest
@@ -160,7 +160,7 @@ def test_chunk_algebra_equals_token_recurrence(hf, T):
 def test_kernel_operand_format_over_config4_length(hf, inputs):
     """8192 tokens (128 chunk steps) of one value head with the kernels' operand rounding: the
     hi / lo products keep outputs and state within 1e-4 + 1e-3 rel of the recurrence after 128
-    chunk steps (a twentieth of the GPU tests' tolerance; measured ~3e-6 with fp16 inputs, ~2e-5
+    chunk steps (the GPU tests allow 2e-3 + 1e-2 rel; measured ~3e-6 with fp16 inputs, ~2e-5
     with bf16), where one 16-bit plane per computed operand drifts past it (fp16: ~5e-5 in y,
     ~4e-4 in the state; bf16: ~3e-4 and ~2e-3)."""
     rng = np.random.default_rng(40 + hf + 2 * (inputs == "bf16"))
